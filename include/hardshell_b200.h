@@ -1,0 +1,130 @@
+/* The C ABI of the B200 HardShell backend (libhardshell_b200.so).
+ *
+ * It replaces the CUDA engine of the reference, crates/hardshell-cuda, behind the interface that
+ * crates/taco uses for a GPU backend (the `Lanes` trait, crates/taco/src/lanes.rs:61-113). Every
+ * entry point names the reference function it replaces. Plain pointers and sizes only: the caller
+ * owns every host array, the library copies in and out and owns the device memory.
+ *
+ * Handles nest as in the reference: a device outlives its models, a model outlives its batches.
+ * A device handle is bound to the host thread that opened it (crates/hardshell-cuda/src/device.rs:9:
+ * "use it on one thread"); use one thread per GPU.
+ *
+ * Every function returns a status (HS_OK = 0) unless its comment says otherwise; on an error,
+ * hs_last_error() gives the message of the calling thread. After a failed run, no slot position
+ * changed (crates/hardshell-cuda/src/batch.rs:443-446).
+ */
+#ifndef HARDSHELL_B200_H
+#define HARDSHELL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes; they mirror crates/hardshell-cuda/src/error.rs:9-50 (enum Error). */
+enum hs_status {
+    HS_OK = 0,
+    HS_NO_DEVICE = 1,       /* Error::NoDevice: no driver or no such device */
+    HS_CUDA = 2,            /* Error::Cuda: a CUDA call or a kernel failed */
+    HS_UNSUPPORTED = 3,     /* Error::Unsupported: the device, model or request shape */
+    HS_MODEL = 4,           /* Error::Model: the model file is not valid */
+    HS_BAD_SLOT = 5,        /* Error::BadSlot */
+    HS_LENGTH_MISMATCH = 6, /* Error::LengthMismatch */
+    HS_TOKEN_RANGE = 7,     /* Error::Model(TokenOutOfRange) */
+    HS_INVALID_OVERLAP = 8, /* Error::Model(InvalidOverlap) */
+    HS_BAD_ARGUMENT = 9     /* a null pointer or a size out of range */
+};
+
+typedef struct hs_dev hs_dev;
+typedef struct hs_model hs_model;
+typedef struct hs_batch hs_batch;
+
+/* The answer of the coder op for one input: a symbol and its interval in the table of
+ * taco_coder::FreqTable::from_weights(weights, freq_bits) (crates/hardshell-cuda/src/batch.rs:47
+ * CoderInterval). is_last is 1 when the symbol is the last symbol of the table. 32 bytes. */
+typedef struct hs_interval {
+    uint32_t symbol;
+    uint32_t is_last;
+    uint64_t start;
+    uint64_t freq;
+    uint64_t reserved;
+} hs_interval;
+
+/* Model dimensions (crates/hardshell/src/gpt2/model.rs:87 Dims and the header constants). */
+typedef struct hs_model_info {
+    uint32_t n_layer, n_head, d_model, d_ff, vocab, n_ctx, eot_token, version;
+    uint64_t cache_bytes_per_slot; /* crates/hardshell-cuda/src/model.rs:395 */
+    uint64_t weight_bytes;         /* crates/hardshell-cuda/src/model.rs:389 */
+    uint8_t hash[32];              /* SHA-256 of the model file (model.rs:359) */
+} hs_model_info;
+
+/* CudaDevice::open (crates/hardshell-cuda/src/device.rs:29). HS_NO_DEVICE without a device,
+ * HS_UNSUPPORTED below compute capability 10.0 (the kernels are sm_100a). */
+int hs_open(int ordinal, hs_dev** out);
+void hs_dev_free(hs_dev* dev);
+/* CudaDevice::memory (device.rs:58): free and total bytes. */
+int hs_mem_info(hs_dev* dev, uint64_t* free_bytes, uint64_t* total_bytes);
+/* CudaDevice::name (device.rs:43): the device name, NUL-terminated, cut to `cap` bytes. */
+int hs_dev_name(hs_dev* dev, char* buf, size_t cap);
+
+/* CudaModel::load (crates/hardshell-cuda/src/model.rs:242): validates the .hsm bytes as
+ * hardshell::gpt2::Model::load does (crates/hardshell/src/gpt2/model.rs:292) and uploads the
+ * weights. The bytes are copied. HS_MODEL for an invalid file, HS_UNSUPPORTED for a valid model
+ * this backend does not run (see the message). */
+int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out);
+void hs_model_free(hs_model* model);
+int hs_model_get_info(hs_model* model, hs_model_info* out);
+
+/* CudaBatch::new (crates/hardshell-cuda/src/batch.rs:237): `slots` sessions with their KV
+ * caches and passes of at most `max_rows` rows (a max_rows of 1 becomes 2). */
+int hs_batch_new(hs_model* model, uint32_t slots, uint32_t max_rows, hs_batch** out);
+void hs_batch_free(hs_batch* batch);
+/* CudaBatch::set_overlap (batch.rs:354): the context overlap K <= n_ctx - 2 of every slot. */
+int hs_batch_set_overlap(hs_batch* batch, uint16_t k);
+/* CudaBatch::reset (batch.rs:397): empties the context of `slot`. */
+int hs_batch_reset(hs_batch* batch, uint32_t slot);
+/* CudaBatch::position (batch.rs:391): the tokens in the context of `slot` (0 if not valid). */
+uint32_t hs_batch_position(hs_batch* batch, uint32_t slot);
+/* CudaBatch::gpu_bytes (batch.rs:385). */
+uint64_t hs_batch_gpu_bytes(hs_batch* batch);
+
+/* CudaBatch::run_coded (batch.rs:463): runs the n inputs (slots[i], tokens[i]) and answers
+ * query i: kinds[i] = 0 (Encode) gives the interval of token values[i]; kinds[i] = 1 (Decode)
+ * gives the symbol whose interval holds target values[i] < 2^freq_bits. The rows of one slot run
+ * at consecutive positions (prefill); a full context starts again with the overlap. Only the
+ * intervals come back (32 bytes per input). */
+int hs_batch_run_coded(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds,
+                       const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out);
+
+/* CudaBatch::run_weights (batch.rs:447): the vocab weights of every input, n * vocab u64. */
+int hs_batch_run_weights(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
+                         uint64_t* out);
+
+/* The message of the last error of the calling thread (NUL-terminated, cut to `cap`). */
+int hs_last_error(char* buf, size_t cap);
+
+/* ---- op-level entry points: the kernels alone, for tests and measurements ----
+ * (the reference's op-level path, crates/hardshell-cuda/src/batch/record.rs, and its GEMM tests,
+ * crates/hardshell-cuda/tests/ops.rs). Host buffers in and out. */
+
+/* out[m][n] = clamp(rescale(A[m] . W[n] + bias[n], mult[n], shift), -127, 127) for int8
+ * A [M, K] and W [N, K], exact int32 accumulation (crates/hardshell/src/gpt2/ops.rs:434
+ * LinearOut::Act). path 0 = tensor cores (tcgen05), 1 = CUDA cores (dp4a).
+ * With raw32 != NULL the int32 accumulators are written there instead (out8 may be NULL). */
+int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, const int32_t* bias,
+                     const int32_t* mult, uint32_t shift, uint32_t M, uint32_t N, uint32_t K, int8_t* out8,
+                     int32_t* raw32);
+
+/* A device-resident GEMM benchmark: the same op on device buffers it allocates, with inputs
+ * from a seed, timed with CUDA events over `iters` launches after `warmup`. Fills the mean
+ * launch time in microseconds. For bench.py. */
+int hs_op_linear_bench(hs_dev* dev, int path, uint32_t M, uint32_t N, uint32_t K, uint64_t seed, int warmup,
+                       int iters, double* us_per_launch);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HARDSHELL_B200_H */

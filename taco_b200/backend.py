@@ -1,0 +1,269 @@
+"""The Python host side of the B200 HardShell backend: the API of the reference's CUDA engine
+(crates/hardshell-cuda: CudaDevice, CudaModel, CudaBatch) over the C ABI of
+libhardshell_b200.so (include/hardshell_b200.h).
+
+There is no CPU fallback: if the library or a GPU is missing, every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libhardshell_b200.so"
+
+HS_OK, HS_NO_DEVICE, HS_CUDA, HS_UNSUPPORTED, HS_MODEL = 0, 1, 2, 3, 4
+HS_BAD_SLOT, HS_LENGTH_MISMATCH, HS_TOKEN_RANGE, HS_INVALID_OVERLAP, HS_BAD_ARGUMENT = 5, 6, 7, 8, 9
+_NAMES = {
+    HS_NO_DEVICE: "NoDevice", HS_CUDA: "Cuda", HS_UNSUPPORTED: "Unsupported", HS_MODEL: "Model",
+    HS_BAD_SLOT: "BadSlot", HS_LENGTH_MISMATCH: "LengthMismatch", HS_TOKEN_RANGE: "TokenOutOfRange",
+    HS_INVALID_OVERLAP: "InvalidOverlap", HS_BAD_ARGUMENT: "BadArgument",
+}
+
+ENCODE, DECODE = 0, 1
+
+
+class HardShellError(RuntimeError):
+    """An error of the backend; `code` is the hs_status (crates/hardshell-cuda/src/error.rs)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{_NAMES.get(code, code)}: {message}")
+        self.code = code
+        self.kind = _NAMES.get(code, str(code))
+
+
+class Interval(ctypes.Structure):
+    _fields_ = [("symbol", ctypes.c_uint32), ("is_last", ctypes.c_uint32), ("start", ctypes.c_uint64),
+                ("freq", ctypes.c_uint64), ("reserved", ctypes.c_uint64)]
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [("n_layer", ctypes.c_uint32), ("n_head", ctypes.c_uint32), ("d_model", ctypes.c_uint32),
+                ("d_ff", ctypes.c_uint32), ("vocab", ctypes.c_uint32), ("n_ctx", ctypes.c_uint32),
+                ("eot_token", ctypes.c_uint32), ("version", ctypes.c_uint32),
+                ("cache_bytes_per_slot", ctypes.c_uint64), ("weight_bytes", ctypes.c_uint64),
+                ("hash", ctypes.c_uint8 * 32)]
+
+
+INTERVAL_DTYPE = np.dtype([("symbol", "<u4"), ("is_last", "<u4"), ("start", "<u8"), ("freq", "<u8"),
+                           ("reserved", "<u8")])
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The backend library. Raises if it is not built (no silent fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise HardShellError(HS_NO_DEVICE, f"{LIB_PATH.name} is not built: run python -m taco_b200.build")
+    L = ctypes.CDLL(str(LIB_PATH))
+    vp, u32, u64, i32 = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int
+    L.hs_open.argtypes = [i32, ctypes.POINTER(vp)]
+    L.hs_dev_free.argtypes = [vp]
+    L.hs_dev_free.restype = None
+    L.hs_mem_info.argtypes = [vp, ctypes.POINTER(u64), ctypes.POINTER(u64)]
+    L.hs_dev_name.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
+    L.hs_model_load.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(vp)]
+    L.hs_model_free.argtypes = [vp]
+    L.hs_model_free.restype = None
+    L.hs_model_get_info.argtypes = [vp, ctypes.POINTER(ModelInfo)]
+    L.hs_batch_new.argtypes = [vp, u32, u32, ctypes.POINTER(vp)]
+    L.hs_batch_free.argtypes = [vp]
+    L.hs_batch_free.restype = None
+    L.hs_batch_set_overlap.argtypes = [vp, ctypes.c_uint16]
+    L.hs_batch_reset.argtypes = [vp, u32]
+    L.hs_batch_position.argtypes = [vp, u32]
+    L.hs_batch_position.restype = u32
+    L.hs_batch_gpu_bytes.argtypes = [vp]
+    L.hs_batch_gpu_bytes.restype = u64
+    L.hs_batch_run_coded.argtypes = [vp, vp, vp, vp, vp, u32, u32, vp]
+    L.hs_batch_run_weights.argtypes = [vp, vp, vp, u32, vp]
+    L.hs_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
+    L.hs_op_linear_bench.argtypes = [vp, i32, u32, u32, u32, u64, i32, i32, ctypes.POINTER(ctypes.c_double)]
+    _lib = L
+    return L
+
+
+def _check(rc: int):
+    if rc != HS_OK:
+        buf = ctypes.create_string_buffer(1024)
+        lib().hs_last_error(buf, 1024)
+        raise HardShellError(rc, buf.value.decode(errors="replace"))
+
+
+def _p(a: np.ndarray) -> ctypes.c_void_p:
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class CudaDevice:
+    """crates/hardshell-cuda/src/device.rs CudaDevice: one GPU (use it on one thread)."""
+
+    def __init__(self, ordinal: int = 0):
+        h = ctypes.c_void_p()
+        _check(lib().hs_open(ordinal, ctypes.byref(h)))
+        self.h = h
+        self.ordinal = ordinal
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().hs_dev_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def name(self) -> str:
+        buf = ctypes.create_string_buffer(256)
+        _check(lib().hs_dev_name(self.h, buf, 256))
+        return buf.value.decode()
+
+    def memory(self) -> tuple[int, int]:
+        f, t = ctypes.c_uint64(), ctypes.c_uint64()
+        _check(lib().hs_mem_info(self.h, ctypes.byref(f), ctypes.byref(t)))
+        return f.value, t.value
+
+    def linear_act(self, A: np.ndarray, W: np.ndarray, bias: np.ndarray, mult: np.ndarray, shift: int,
+                   path: str = "tc") -> np.ndarray:
+        """The linear op alone: clamp(rescale(A . W^T + b, m, s), -127, 127) (tests)."""
+        A = np.ascontiguousarray(A, dtype=np.int8)
+        W = np.ascontiguousarray(W, dtype=np.int8)
+        b = np.ascontiguousarray(bias, dtype=np.int32)
+        m = np.ascontiguousarray(mult, dtype=np.int32)
+        M, K = A.shape
+        N = W.shape[0]
+        out = np.zeros((M, N), dtype=np.int8)
+        _check(lib().hs_op_linear_act(self.h, 0 if path == "tc" else 1, _p(A), _p(W), _p(b), _p(m), shift, M, N, K,
+                                      _p(out), None))
+        return out
+
+    def matmul_raw(self, A: np.ndarray, W: np.ndarray, path: str = "tc") -> np.ndarray:
+        """The exact int32 accumulators A . W^T (tests)."""
+        A = np.ascontiguousarray(A, dtype=np.int8)
+        W = np.ascontiguousarray(W, dtype=np.int8)
+        M, K = A.shape
+        N = W.shape[0]
+        out = np.zeros((M, N), dtype=np.int32)
+        _check(lib().hs_op_linear_act(self.h, 0 if path == "tc" else 1, _p(A), _p(W), None, None, 0, M, N, K, None,
+                                      _p(out)))
+        return out
+
+    def linear_bench(self, M: int, N: int, K: int, seed: int = 1, warmup: int = 3, iters: int = 20,
+                     path: str = "tc") -> float:
+        """Mean microseconds of one device-resident linear launch (bench.py)."""
+        us = ctypes.c_double()
+        _check(lib().hs_op_linear_bench(self.h, 0 if path == "tc" else 1, M, N, K, seed, warmup, iters,
+                                        ctypes.byref(us)))
+        return us.value
+
+
+@dataclass
+class Info:
+    n_layer: int
+    n_head: int
+    d_model: int
+    d_ff: int
+    vocab: int
+    n_ctx: int
+    eot_token: int
+    version: int
+    cache_bytes_per_slot: int
+    weight_bytes: int
+    hash: bytes
+
+
+class CudaModel:
+    """crates/hardshell-cuda/src/model.rs CudaModel: a validated .hsm model on one device."""
+
+    def __init__(self, device: CudaDevice, data: bytes):
+        self.device = device
+        h = ctypes.c_void_p()
+        _check(lib().hs_model_load(device.h, bytes(data), len(data), ctypes.byref(h)))
+        self.h = h
+        mi = ModelInfo()
+        _check(lib().hs_model_get_info(self.h, ctypes.byref(mi)))
+        self.info = Info(mi.n_layer, mi.n_head, mi.d_model, mi.d_ff, mi.vocab, mi.n_ctx, mi.eot_token, mi.version,
+                         mi.cache_bytes_per_slot, mi.weight_bytes, bytes(mi.hash))
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().hs_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def vocab_size(self) -> int:
+        return self.info.vocab
+
+    def n_ctx(self) -> int:
+        return self.info.n_ctx
+
+    def eot_token(self) -> int:
+        return self.info.eot_token
+
+    def hash(self) -> bytes:
+        return self.info.hash
+
+    def cache_bytes_per_slot(self) -> int:
+        return self.info.cache_bytes_per_slot
+
+
+class CudaBatch:
+    """crates/hardshell-cuda/src/batch.rs CudaBatch: `slots` sessions that run together."""
+
+    def __init__(self, model: CudaModel, slots: int, max_rows: int):
+        self.model = model
+        h = ctypes.c_void_p()
+        _check(lib().hs_batch_new(model.h, slots, max_rows, ctypes.byref(h)))
+        self.h = h
+        self.slots = slots
+        self.max_rows = max(2, max_rows)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().hs_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_overlap(self, k: int):
+        _check(lib().hs_batch_set_overlap(self.h, k))
+
+    def reset(self, slot: int):
+        _check(lib().hs_batch_reset(self.h, slot))
+
+    def position(self, slot: int) -> int:
+        return lib().hs_batch_position(self.h, slot)
+
+    def gpu_bytes(self) -> int:
+        return lib().hs_batch_gpu_bytes(self.h)
+
+    def run_coded(self, slots, tokens, kinds, values, freq_bits: int = 32) -> np.ndarray:
+        """The coder answers of the inputs: a structured array (symbol, is_last, start, freq)."""
+        s = np.ascontiguousarray(slots, dtype=np.uint32)
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        k = np.ascontiguousarray(kinds, dtype=np.uint32)
+        v = np.ascontiguousarray(values, dtype=np.uint64)
+        n = s.size
+        if not (t.size == k.size == v.size == n):
+            raise HardShellError(HS_LENGTH_MISMATCH, "the inputs and the queries differ in length")
+        out = np.zeros(n, dtype=INTERVAL_DTYPE)
+        _check(lib().hs_batch_run_coded(self.h, _p(s), _p(t), _p(k), _p(v), n, freq_bits, _p(out)))
+        return out
+
+    def run_weights(self, slots, tokens) -> np.ndarray:
+        s = np.ascontiguousarray(slots, dtype=np.uint32)
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        if s.size != t.size:
+            raise HardShellError(HS_LENGTH_MISMATCH, "slots and tokens differ in length")
+        out = np.zeros((s.size, self.model.info.vocab), dtype=np.uint64)
+        _check(lib().hs_batch_run_weights(self.h, _p(s), _p(t), s.size, _p(out)))
+        return out

@@ -1,0 +1,85 @@
+// The device-side layout of a loaded model and of the work buffers of one pass, shared by the
+// kernels and the host runtime of the B200 HardShell backend.
+#pragma once
+
+#include <cstdint>
+
+namespace hs {
+
+// Rows of the GEMM operand tiles and the padding of every K and N dimension.
+constexpr int TILE_M = 128;
+constexpr int TILE_N = 256;
+constexpr int TILE_K = 128;
+// Columns of one logits tile: the coder op reads the max of each tile (LOGIT_TILE columns).
+constexpr int LOGIT_TILE = 256;
+// The largest logit table the coder op keeps in shared memory (entries).
+constexpr int MAX_LOGIT_TABLE = 16384;
+// The largest context the attention kernels hold in shared memory (scores of one row).
+constexpr int MAX_ATTN_CTX = 8192;
+
+inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// One linear layer on the device: weights [Np, Kp] (K-major, zero padded), bias, multiplier.
+struct LinearDev {
+    const int8_t* w;
+    int N, K, Np, Kp;
+    const int32_t* b;
+    const int32_t* m;
+    int s;
+};
+
+struct LnDev {
+    const int16_t* g;
+    const int32_t* b;
+    int32_t m;
+    int s;
+    int beta_frac;
+};
+
+struct LayerDev {
+    LnDev ln1, ln2;
+    LinearDev qkv, proj, fc, mlp;
+    int32_t score_m;
+    int score_s;
+    int32_t out_m;
+    int out_s;
+    const int8_t* gelu;  // i8 outputs
+    int gelu_off;        // 2^(b-1): the input range is [-off, off - 1]
+};
+
+// One row of a pass: the slot, the input token, the position, and the coder query
+// (kind 0 = the interval of token `value`, 1 = the symbol that holds target `value`).
+struct RowInfo {
+    uint32_t slot, token, pos, kind;
+    uint64_t value;
+};
+
+// The epilogue of a GEMM tile: what happens to acc = W[n] . A[r] (exact s32).
+enum EpiMode : int {
+    EPI_ACT = 0,     // out8[r, n] = clamp(rescale(acc + b[n], m[n], s), -127, 127)
+    EPI_GELU = 1,    // out8[r, n] = gelu[clamp(rescale(acc + b[n], m[n], s), lo, hi) + off]
+    EPI_RESID = 2,   // x[r, n] = clamp(x[r, n] + rescale(acc + b[n], m[n], s), -R, R)
+    EPI_LOGITS = 3,  // l = clamp(rescale(acc, m[n], s), +-2^40); tile max and d16 = min(tmax - l, last)
+    EPI_RAW = 4,     // out32[r, n] = acc (the GEMM tests)
+};
+
+struct EpiArgs {
+    int R, N;
+    const int32_t* b;
+    const int32_t* m;
+    int s;
+    int8_t* out8;
+    int ldo;
+    const int8_t* gelu;
+    int gelu_off;
+    int32_t* x;
+    int ldx;
+    uint16_t* d16;
+    int ldd;
+    int64_t* tmax;
+    int ldt;
+    int last;
+    int32_t* out32;
+};
+
+}  // namespace hs

@@ -1,0 +1,486 @@
+// The CUDA-core kernels of the B200 HardShell backend: embeddings, LayerNorm, the dp4a GEMM
+// (reference and small passes), the KV-cache store, causal integer attention and the coder op.
+// Every value is exact integer arithmetic with the rules of crates/hardshell/src/int.rs.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "hs_common.cuh"
+#include "hs_kernels.cuh"
+
+namespace hs {
+
+namespace {
+
+__device__ __forceinline__ int64_t warp_max64(int64_t v) {
+    for (int o = 16; o > 0; o >>= 1) {
+        int64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}
+__device__ __forceinline__ uint64_t warp_sum64(uint64_t v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int64_t warp_sums64(int64_t v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Block reductions for up to 1024 threads (blockDim a multiple of 32). `sh` holds 32 slots.
+__device__ int64_t block_max64(int64_t v, int64_t* sh) {
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_max64(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    int64_t r = lane < nw ? sh[lane] : INT64_MIN;
+    r = warp_max64(r);
+    return r;
+}
+__device__ uint64_t block_sum64(uint64_t v, uint64_t* sh) {
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum64(v);
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    uint64_t r = lane < nw ? sh[lane] : 0;
+    return warp_sum64(r);
+}
+
+// ---- embeddings (crates/hardshell/src/gpt2/ops.rs:52 embed) ----
+
+__global__ void k_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const int32_t* em, int es,
+                        const int8_t* wpe, const int32_t* pm, int ps, int d, int32_t* x) {
+    int r = blockIdx.y;
+    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R || j >= d) return;
+    uint32_t tok = rows[r].token, pos = rows[r].pos;
+    int64_t a = rescale64(wte[(size_t)tok * ldw + j], em[tok], es);
+    int64_t b = rescale64(wpe[(size_t)pos * d + j], pm[pos], ps);
+    x[(size_t)r * d + j] = (int32_t)clamp64(a + b, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+}
+
+// ---- LayerNorm (crates/hardshell/src/layernorm.rs:201-256), one block per row ----
+
+__global__ void k_layernorm(const int32_t* x, int R, int d, LnDev ln, int ln_k, int ln_j, uint64_t eps, int8_t* out,
+                            int ldo) {
+    __shared__ int64_t sh[32];
+    __shared__ uint64_t shu[64];
+    int r = blockIdx.x;
+    if (r >= R) return;
+    const int32_t* xr = x + (size_t)r * d;
+    int64_t s = 0;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) s += xr[j];
+    s = warp_sums64(s);
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) sh[w] = s;
+    __syncthreads();
+    int64_t sum = 0;
+    for (int i = 0; i < nw; i++) sum += sh[i];
+    int64_t mean = floor_div64(sum, d);
+    u128 sq = 0;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        int64_t c = (int64_t)xr[j] - mean;
+        uint64_t a = c < 0 ? (uint64_t)(-c) : (uint64_t)c;
+        sq += (u128)a * a;
+    }
+    // Reduce the 128-bit sums with the two halves and a carry.
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t lo = (uint64_t)sq, hi = (uint64_t)(sq >> 64);
+        uint64_t lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
+        uint64_t hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
+        sq += ((u128)hi2 << 64) | lo2;
+    }
+    __syncthreads();
+    if (lane == 0) {
+        shu[2 * w] = (uint64_t)sq;
+        shu[2 * w + 1] = (uint64_t)(sq >> 64);
+    }
+    __syncthreads();
+    u128 sum_sq = 0;
+    for (int i = 0; i < nw; i++) sum_sq += ((u128)shu[2 * i + 1] << 64) | shu[2 * i];
+    u128 var = sum_sq / (u128)d;
+    u128 root = isqrt128((var << (2 * ln_j)) + (u128)eps);
+    if (root < 1) root = 1;
+    i128 inv = (i128)(((u128)1 << ln_k) / root);
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        i128 t = (i128)((int64_t)xr[j] - mean) * inv * (i128)ln.g[j];
+        i128 y;
+        if (ln.beta_frac == 0) {
+            y = shift_round128((i128)((u128)t * (u128)(i128)ln.m), ln.s, 126) + (i128)ln.b[j];
+        } else {
+            i128 c = (i128)ln.b[j] << (ln.s - ln.beta_frac);
+            y = shift_round128((i128)((u128)t * (u128)(i128)ln.m + (u128)c), ln.s, 126);
+        }
+        out[(size_t)r * ldo + j] = (int8_t)clamp128(y, -127, 127);
+    }
+}
+
+// ---- the GEMM epilogue for one element (shared by the dp4a GEMM) ----
+
+__device__ __forceinline__ void epi_store(int mode, const EpiArgs& e, int r, int n, int32_t acc) {
+    if (mode == EPI_RAW) {
+        e.out32[(size_t)r * e.ldo + n] = acc;
+        return;
+    }
+    int64_t v = (int64_t)acc + (int64_t)e.b[n];
+    int64_t y = rescale64(v, e.m[n], e.s);
+    if (mode == EPI_ACT) {
+        e.out8[(size_t)r * e.ldo + n] = (int8_t)clamp64(y, -127, 127);
+    } else if (mode == EPI_GELU) {
+        int64_t in = clamp64(y, -e.gelu_off, e.gelu_off - 1);
+        e.out8[(size_t)r * e.ldo + n] = e.gelu[in + e.gelu_off];
+    } else if (mode == EPI_RESID) {
+        int32_t* xp = &e.x[(size_t)r * e.ldx + n];
+        *xp = (int32_t)clamp64((int64_t)*xp + y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+    }
+}
+
+// ---- the dp4a GEMM: a block of 256 threads computes 8 rows x 256 columns ----
+
+constexpr int SG_ROWS = 8;
+
+__global__ void __launch_bounds__(256) k_gemm_simple(int mode, const int8_t* A, int lda, int R, LinearDev W,
+                                                     EpiArgs e) {
+    __shared__ int4 sa[SG_ROWS][8];  // 8 rows x 128 bytes of K
+    __shared__ int64_t red[SG_ROWS][8];
+    int n = blockIdx.x * 256 + threadIdx.x;
+    int r0 = blockIdx.y * SG_ROWS;
+    int32_t acc[SG_ROWS];
+#pragma unroll
+    for (int i = 0; i < SG_ROWS; i++) acc[i] = 0;
+    const int8_t* wrow = W.w + (size_t)(n < W.Np ? n : 0) * W.Kp;
+    for (int k0 = 0; k0 < W.Kp; k0 += 128) {
+        __syncthreads();
+        if (threadIdx.x < SG_ROWS * 8) {
+            int rr = threadIdx.x >> 3, c = threadIdx.x & 7;
+            int r = r0 + rr;
+            int4 v = make_int4(0, 0, 0, 0);
+            if (r < R) v = *reinterpret_cast<const int4*>(A + (size_t)r * lda + k0 + 16 * c);
+            sa[rr][c] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            int4 wv = *reinterpret_cast<const int4*>(wrow + k0 + 16 * c);
+#pragma unroll
+            for (int i = 0; i < SG_ROWS; i++) {
+                int4 av = sa[i][c];
+                acc[i] = __dp4a(wv.x, av.x, acc[i]);
+                acc[i] = __dp4a(wv.y, av.y, acc[i]);
+                acc[i] = __dp4a(wv.z, av.z, acc[i]);
+                acc[i] = __dp4a(wv.w, av.w, acc[i]);
+            }
+        }
+    }
+    if (mode != EPI_LOGITS) {
+        if (n < e.N)
+            for (int i = 0; i < SG_ROWS; i++)
+                if (r0 + i < R) epi_store(mode, e, r0 + i, n, acc[i]);
+        return;
+    }
+    // Logits: l = clamp(rescale(acc, m[n], s), +-2^40); per row the max over the 256 columns
+    // of the block (one logits tile), then d16 = min(tmax - l, last).
+    int64_t l[SG_ROWS];
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < SG_ROWS; i++) {
+        l[i] = n < e.N ? clamp64(rescale64(acc[i], e.m[n], e.s), -SCORE_LIMIT, SCORE_LIMIT) : INT64_MIN;
+        int64_t mx = warp_max64(l[i]);
+        if (lane == 0) red[i][w] = mx;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < SG_ROWS; i++) {
+        int64_t tm = red[i][0];
+        for (int q = 1; q < 8; q++) tm = red[i][q] > tm ? red[i][q] : tm;
+        int r = r0 + i;
+        if (r < R) {
+            if (n < e.N) {
+                int64_t dd = tm - l[i];
+                e.d16[(size_t)r * e.ldd + n] = (uint16_t)(dd < e.last ? dd : e.last);
+            }
+            if (threadIdx.x == 0) e.tmax[(size_t)r * e.ldt + blockIdx.x] = tm;
+        }
+    }
+}
+
+// ---- the KV cache: keys and values of each row at (slot, layer, head, pos) ----
+
+__global__ void k_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
+                           int layer, int n_ctx, int8_t* kc, int8_t* vc) {
+    int r = blockIdx.x;
+    if (r >= R) return;
+    uint32_t slot = rows[r].slot, pos = rows[r].pos;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        int h = j / hd, c = j - h * hd;
+        size_t at = ((((size_t)slot * L + layer) * H + h) * n_ctx + pos) * hd + c;
+        kc[at] = qkv[(size_t)r * ldq + d + j];
+        vc[at] = qkv[(size_t)r * ldq + 2 * d + j];
+    }
+}
+
+// ---- causal attention of one row and one head (crates/hardshell/src/gpt2/reference.rs:252-284) ----
+
+constexpr int ATT_THREADS = 128;
+
+__global__ void __launch_bounds__(ATT_THREADS) k_attention(const RowInfo* rows, int R, const int8_t* qkv, int ldq,
+                                                           const int8_t* kc, const int8_t* vc, int L, int layer,
+                                                           int H, int hd, int n_ctx, int d, int32_t sm, int ss,
+                                                           int32_t om, int os, const int32_t* table, int tlen,
+                                                           int P, int8_t* att, int lda) {
+    extern __shared__ int64_t s_sc[];  // n_ctx scores, then weights, then p
+    __shared__ int64_t red[32];
+    __shared__ uint64_t redu[32];
+    __shared__ int8_t q[1024];
+    __shared__ int64_t part[ATT_THREADS];
+    int h = blockIdx.x, r = blockIdx.y;
+    if (r >= R) return;
+    uint32_t slot = rows[r].slot;
+    int n = (int)rows[r].pos + 1;
+    for (int c = threadIdx.x; c < hd; c += ATT_THREADS) q[c] = qkv[(size_t)r * ldq + h * hd + c];
+    __syncthreads();
+    size_t head = (((size_t)slot * L + layer) * H + h) * n_ctx * (size_t)hd;
+    const int8_t* K = kc + head;
+    const int8_t* Vv = vc + head;
+    int64_t mx = INT64_MIN;
+    for (int j = threadIdx.x; j < n; j += ATT_THREADS) {
+        const int8_t* kr = K + (size_t)j * hd;
+        int32_t dot = 0;
+        for (int c = 0; c < hd; c++) dot += (int32_t)q[c] * (int32_t)kr[c];
+        int64_t sc = clamp64(rescale64(dot, sm, ss), -SCORE_LIMIT, SCORE_LIMIT);
+        s_sc[j] = sc;
+        mx = sc > mx ? sc : mx;
+    }
+    mx = block_max64(mx, red);
+    // softmax.rs:78: e = table[min(max - s, len - 1)], p = floor((e << P) / sum(e)).
+    uint64_t sum = 0;
+    int64_t last = tlen - 1;
+    for (int j = threadIdx.x; j < n; j += ATT_THREADS) {
+        int64_t dd = mx - s_sc[j];
+        int64_t e = table[dd < last ? dd : last];
+        s_sc[j] = e;
+        sum += (uint64_t)e;
+    }
+    sum = block_sum64(sum, redu);
+    if (sum == 0) sum = 1;
+    uint64_t rec = (~0ULL) / sum;
+    for (int j = threadIdx.x; j < n; j += ATT_THREADS) {
+        uint64_t x = (uint64_t)s_sc[j] << P;
+        uint64_t qv = __umul64hi(x, rec);
+        while ((qv + 1) * sum <= x) qv++;
+        s_sc[j] = (int64_t)qv;
+    }
+    __syncthreads();
+    // acc[c] = sum_j p_j v_j[c] in i64; groups of hd threads split the keys.
+    int groups = hd <= ATT_THREADS ? ATT_THREADS / hd : 1;
+    for (int c0 = 0; c0 < hd; c0 += ATT_THREADS) {
+        int c = c0 + (hd <= ATT_THREADS ? threadIdx.x % hd : threadIdx.x);
+        int g = hd <= ATT_THREADS ? threadIdx.x / hd : 0;
+        int64_t acc = 0;
+        if (c < hd && g < groups)
+            for (int j = g; j < n; j += groups) acc += s_sc[j] * (int64_t)Vv[(size_t)j * hd + c];
+        part[threadIdx.x] = acc;
+        __syncthreads();
+        if (threadIdx.x < (hd <= ATT_THREADS ? hd : ATT_THREADS) && c < hd) {
+            int64_t t = 0;
+            if (hd <= ATT_THREADS) {
+                for (int gg = 0; gg < groups; gg++) t += part[gg * hd + c];
+            } else {
+                t = part[threadIdx.x];
+            }
+            att[(size_t)r * lda + h * hd + c] = (int8_t)clamp128(rescale128(t, om, os), -127, 127);
+        }
+        __syncthreads();
+    }
+}
+
+// ---- the coder op (crates/taco-coder/src/freq.rs:103 from_weights, interval.rs:82-100) ----
+
+constexpr int CODER_THREADS = 512;
+constexpr int CODER_WARPS = CODER_THREADS / 32;
+
+__global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
+                                                         int R, int V, const uint64_t* table, int tlen, uint32_t bits,
+                                                         const RowInfo* rows, uint64_t* out) {
+    extern __shared__ uint32_t F[];  // tlen entries: 1 + floor(table[j] * spare / W)
+    __shared__ int64_t red[32];
+    __shared__ uint64_t redu[32];
+    __shared__ uint64_t wsum[CODER_WARPS];
+    __shared__ int s_largest;
+    int r = blockIdx.x;
+    if (r >= R) return;
+    const uint16_t* dr = d16 + (size_t)r * ldd;
+    const int64_t* tr = tmax + (size_t)r * ldt;
+    int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
+    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t last = tlen - 1;
+    // The row max.
+    int64_t mx = INT64_MIN;
+    for (int t = threadIdx.x; t < VT; t += CODER_THREADS) mx = tr[t] > mx ? tr[t] : mx;
+    mx = block_max64(mx, red);
+    // Pass 1: W = sum(w) and the largest weight (freq.rs:112-121).
+    uint64_t W = 0, wmax = 0;
+    for (int v = threadIdx.x; v < V; v += CODER_THREADS) {
+        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
+        uint64_t wv = table[dd < last ? dd : last];
+        W += wv;
+        wmax = wv > wmax ? wv : wmax;
+    }
+    W = block_sum64(W, redu);
+    wmax = (uint64_t)block_max64((int64_t)wmax, red);
+    // The lowest id with the largest weight.
+    if (threadIdx.x == 0) s_largest = V;
+    __syncthreads();
+    for (int v = threadIdx.x; v < V; v += CODER_THREADS) {
+        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
+        uint64_t wv = table[dd < last ? dd : last];
+        if (wv == wmax) {
+            atomicMin(&s_largest, v);
+            break;
+        }
+    }
+    __syncthreads();
+    bool all_zero = W == 0;
+    int largest = all_zero ? 0 : s_largest;
+    uint64_t total = 1ULL << bits;
+    uint64_t spare = total - (uint64_t)V;
+    uint32_t f_flat = (uint32_t)(1 + spare / (uint64_t)V);  // all-zero rule: every weight is 1
+    if (!all_zero)
+        for (int j = threadIdx.x; j < tlen; j += CODER_THREADS)
+            F[j] = (uint32_t)(1 + udiv128_small((u128)table[j] * spare, W));
+    __syncthreads();
+    // Pass 2: per warp, the sum of f over its contiguous range of symbols.
+    int per = (V + CODER_WARPS - 1) / CODER_WARPS;
+    int a = w * per, b = min(V, a + per);
+    uint64_t s = 0;
+    for (int v = a + lane; v < b; v += 32) {
+        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
+        s += all_zero ? f_flat : F[dd < last ? dd : last];
+    }
+    s = warp_sum64(s);
+    if (lane == 0) wsum[w] = s;
+    __syncthreads();
+    uint64_t before = 0, sum_f = 0;
+    for (int i = 0; i < CODER_WARPS; i++) {
+        if (i < w) before += wsum[i];
+        sum_f += wsum[i];
+    }
+    uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
+    RowInfo q = rows[r];
+    // A(v): the start of symbol v; A(a) of this warp and A(b) (A(V) = total).
+    uint64_t Aa = before + ((uint64_t)a > (uint64_t)largest ? rem : 0);
+    uint64_t Ab = b >= V ? total : before + wsum[w] + ((uint64_t)b > (uint64_t)largest ? rem : 0);
+    bool mine;
+    if (q.kind == 0) mine = (int64_t)q.value >= a && (int64_t)q.value < b;
+    else mine = a < b && q.value >= Aa && q.value < Ab;
+    if (!mine) return;
+    // This warp owns the answer: walk its range 32 symbols at a time.
+    uint64_t base = before;  // sum of f below the current step, without the remainder
+    for (int v0 = a; v0 < b; v0 += 32) {
+        int v = v0 + lane;
+        uint64_t f = 0;
+        if (v < b) {
+            int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
+            f = all_zero ? f_flat : F[dd < last ? dd : last];
+        }
+        uint64_t incl = f;
+        for (int o = 1; o < 32; o <<= 1) {
+            uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        uint64_t start = base + incl - f + ((uint64_t)v > (uint64_t)largest ? rem : 0);
+        uint64_t freq = f + (v == largest ? rem : 0);
+        bool hit;
+        if (q.kind == 0) hit = v < b && (uint64_t)v == q.value;
+        else hit = v < b && q.value >= start && q.value < start + freq;
+        unsigned m = __ballot_sync(0xffffffffu, hit);
+        if (m) {
+            if (lane == __ffs(m) - 1) {
+                out[3 * (size_t)r] = (uint64_t)v;
+                out[3 * (size_t)r + 1] = start;
+                out[3 * (size_t)r + 2] = freq;
+            }
+            return;
+        }
+        base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+}
+
+__global__ void k_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,
+                          const uint64_t* table, int tlen, uint64_t* wout) {
+    __shared__ int64_t red[32];
+    int r = blockIdx.x;
+    if (r >= R) return;
+    const uint16_t* dr = d16 + (size_t)r * ldd;
+    const int64_t* tr = tmax + (size_t)r * ldt;
+    int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
+    int64_t mx = INT64_MIN;
+    for (int t = threadIdx.x; t < VT; t += blockDim.x) mx = tr[t] > mx ? tr[t] : mx;
+    mx = block_max64(mx, red);
+    const int64_t last = tlen - 1;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
+        wout[(size_t)r * V + v] = table[dd < last ? dd : last];
+    }
+}
+
+}  // namespace
+
+cudaError_t configure_core_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_ATTN_CTX * 8);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_coder, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
+}
+
+void launch_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const int32_t* em, int es,
+                  const int8_t* wpe, const int32_t* pm, int ps, int d, int32_t* x, cudaStream_t st) {
+    if (R <= 0) return;
+    dim3 grid((d + 255) / 256, R);
+    k_embed<<<grid, 256, 0, st>>>(rows, R, wte, ldw, em, es, wpe, pm, ps, d, x);
+}
+
+void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k, int ln_j, uint64_t eps,
+                      int8_t* out, int ldo, cudaStream_t st) {
+    if (R <= 0) return;
+    k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo);
+}
+
+void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearDev& W, const EpiArgs& e,
+                        cudaStream_t st) {
+    if (R <= 0) return;
+    dim3 grid(W.Np / 256, (R + SG_ROWS - 1) / SG_ROWS);
+    k_gemm_simple<<<grid, 256, 0, st>>>(mode, A, lda, R, W, e);
+}
+
+void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
+                     int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st) {
+    if (R <= 0) return;
+    k_kv_store<<<R, 256, 0, st>>>(rows, R, qkv, ldq, d, H, hd, L, layer, n_ctx, kc, vc);
+}
+
+void launch_attention(const RowInfo* rows, int R, const int8_t* qkv, int ldq, const int8_t* kc, const int8_t* vc,
+                      int L, int layer, int H, int hd, int n_ctx, int d, int32_t sm, int ss, int32_t om, int os,
+                      const int32_t* table, int tlen, int P, int8_t* att, int lda, cudaStream_t st) {
+    if (R <= 0) return;
+    size_t smem = (size_t)n_ctx * sizeof(int64_t);
+    dim3 grid(H, R);
+    k_attention<<<grid, ATT_THREADS, smem, st>>>(rows, R, qkv, ldq, kc, vc, L, layer, H, hd, n_ctx, d, sm, ss, om,
+                                                  os, table, tlen, P, att, lda);
+}
+
+void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,
+                  int tlen, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st) {
+    if (R <= 0) return;
+    k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, R, V, table, tlen, bits, rows, out);
+}
+
+void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,
+                    const uint64_t* table, int tlen, uint64_t* w, cudaStream_t st) {
+    if (R <= 0) return;
+    k_weights<<<R, 256, 0, st>>>(d16, ldd, tmax, ldt, R, V, table, tlen, w);
+}
+
+}  // namespace hs

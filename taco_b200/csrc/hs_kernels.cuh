@@ -1,0 +1,57 @@
+// Launchers of the CUDA-core kernels of the B200 HardShell backend (hs_kernels.cu) and of the
+// tcgen05 GEMM (hs_gemm_tc.cu). Every launcher takes the stream of its batch.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "hs_device.hpp"
+
+namespace hs {
+
+// Set the shared-memory limits of the kernels for the current device (once per device).
+cudaError_t configure_core_kernels();
+cudaError_t configure_tc_kernels();
+
+struct ModelConsts {
+    int d, f, V, H, hd, L, n_ctx;
+    int Dp, Fp, QKVp, Vp, VT;
+    int ln_k, ln_j;
+    uint64_t ln_eps;
+    int softmax_p;
+};
+
+void launch_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const int32_t* em, int es,
+                  const int8_t* wpe, const int32_t* pm, int ps, int d, int32_t* x, cudaStream_t st);
+
+void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k, int ln_j, uint64_t eps,
+                      int8_t* out, int ldo, cudaStream_t st);
+
+// out = epilogue(W . A^T) on CUDA cores (dp4a); the reference kernel of the tensor-core GEMM and
+// the path for passes of a few rows.
+void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearDev& W, const EpiArgs& e,
+                        cudaStream_t st);
+
+// The same GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
+// `tmA` and `tmB` are CUtensorMap objects (128-byte aligned, 128 bytes each).
+void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, int Kp, const EpiArgs& e,
+                    int num_sms, int* err, cudaStream_t st);
+
+void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
+                     int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st);
+
+void launch_attention(const RowInfo* rows, int R, const int8_t* qkv, int ldq, const int8_t* kc, const int8_t* vc,
+                      int L, int layer, int H, int hd, int n_ctx, int d, int32_t sm, int ss, int32_t om, int os,
+                      const int32_t* table, int tlen, int P, int8_t* att, int lda, cudaStream_t st);
+
+// The coder op: from the d16/tmax output of the logits GEMM, the interval of each row's query
+// in the table of taco_coder::FreqTable::from_weights(weights, bits). out: 3 u64 per row.
+void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,
+                  int tlen, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st);
+
+// The full weights of each row (run_weights): w[r, v] = table[min(max - logit, last)].
+void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,
+                    const uint64_t* table, int tlen, uint64_t* w, cudaStream_t st);
+
+}  // namespace hs

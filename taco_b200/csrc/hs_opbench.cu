@@ -1,0 +1,128 @@
+// The device-resident GEMM benchmark of the C ABI (hs_op_linear_bench): the linear op of one
+// HardShell layer (int8 x int8 -> int32, per-channel requant to int8) on inputs from a seed,
+// timed with CUDA events on the launching stream.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/hardshell_b200.h"
+#include "hs_device.hpp"
+#include "hs_kernels.cuh"
+
+using namespace hs;
+
+namespace {
+
+__global__ void k_fill_i8(int8_t* p, size_t n, uint64_t seed) {
+    size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (; i < n; i += stride) {
+        uint64_t z = seed + 0x9E3779B97F4A7C15ULL * (i + 1);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+        z ^= z >> 31;
+        p[i] = (int8_t)((int)(z % 255) - 127);  // uniform in [-127, 127]
+    }
+}
+
+__global__ void k_fill_mult(int32_t* m, int n, uint64_t seed) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    uint64_t z = seed ^ (0xD1B54A32D192ED03ULL * (i + 7));
+    z = (z ^ (z >> 29)) * 0xBF58476D1CE4E5B9ULL;
+    m[i] = (int32_t)((1u << 30) + (uint32_t)(z % (1u << 30)));  // in [2^30, 2^31)
+}
+
+}  // namespace
+
+// Defined in hs_runtime.cu.
+extern "C" int hs_internal_tmap(hs_dev* dev, void* tm, const void* base, uint64_t rows, uint64_t cols,
+                                uint32_t box_rows);
+extern "C" int hs_internal_dev_info(hs_dev* dev, int* num_sms, int** d_err);
+extern "C" int hs_internal_fail(int code, const char* msg);
+
+extern "C" int hs_op_linear_bench(hs_dev* dev, int path, uint32_t M, uint32_t N, uint32_t K, uint64_t seed, int warmup,
+                                  int iters, double* us_per_launch) {
+    if (!dev || !us_per_launch || iters <= 0) return hs_internal_fail(HS_BAD_ARGUMENT, "bad argument");
+    int num_sms = 0;
+    int* d_err = nullptr;
+    int rc = hs_internal_dev_info(dev, &num_sms, &d_err);
+    if (rc) return rc;
+    int Mp = round_up((int)M, TILE_M), Np = round_up((int)N, TILE_N), Kp = round_up((int)K, TILE_K);
+    if (Kp != (int)K || N % 16 != 0) return hs_internal_fail(HS_UNSUPPORTED, "the benchmark needs K % 128 == 0");
+    int8_t *a = nullptr, *w = nullptr, *out = nullptr;
+    int32_t *b = nullptr, *m = nullptr;
+    auto cleanup = [&]() {
+        cudaFree(a);
+        cudaFree(w);
+        cudaFree(out);
+        cudaFree(b);
+        cudaFree(m);
+    };
+#define BK_CK(call)                                                                              \
+    do {                                                                                         \
+        cudaError_t e_ = (call);                                                                 \
+        if (e_ != cudaSuccess) {                                                                 \
+            cleanup();                                                                           \
+            return hs_internal_fail(HS_CUDA, (std::string(#call) + ": " + cudaGetErrorString(e_)).c_str()); \
+        }                                                                                        \
+    } while (0)
+    BK_CK(cudaMalloc(&a, (size_t)Mp * Kp));
+    BK_CK(cudaMalloc(&w, (size_t)Np * Kp));
+    BK_CK(cudaMalloc(&out, (size_t)M * N));
+    BK_CK(cudaMalloc(&b, sizeof(int32_t) * Np));
+    BK_CK(cudaMalloc(&m, sizeof(int32_t) * Np));
+    BK_CK(cudaMemset(a, 0, (size_t)Mp * Kp));
+    BK_CK(cudaMemset(w, 0, (size_t)Np * Kp));
+    BK_CK(cudaMemset(b, 0, sizeof(int32_t) * Np));
+    k_fill_i8<<<1184, 256>>>(a, (size_t)M * Kp, seed);
+    k_fill_i8<<<1184, 256>>>(w, (size_t)N * Kp, seed ^ 0xABCDEF);
+    k_fill_mult<<<(Np + 255) / 256, 256>>>(m, Np, seed);
+    BK_CK(cudaGetLastError());
+    alignas(128) CUtensorMap ta, tb;
+    if ((rc = hs_internal_tmap(dev, &ta, a, Mp, Kp, TILE_M)) || (rc = hs_internal_tmap(dev, &tb, w, Np, Kp, TILE_N))) {
+        cleanup();
+        return rc;
+    }
+    LinearDev L{w, (int)N, (int)K, Np, Kp, b, m, 38};
+    EpiArgs e{};
+    e.R = (int)M;
+    e.N = (int)N;
+    e.b = b;
+    e.m = m;
+    e.s = 38;
+    e.out8 = out;
+    e.ldo = (int)N;
+    cudaStream_t st;
+    BK_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    auto launch = [&]() {
+        if (path == 0) launch_gemm_tc(EPI_ACT, &ta, &tb, (int)M, Np, Kp, e, num_sms, d_err, st);
+        else launch_gemm_simple(EPI_ACT, a, Kp, (int)M, L, e, st);
+    };
+    for (int i = 0; i < warmup; i++) launch();
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaStreamSynchronize(st);
+    cudaEventRecord(e0, st);
+    for (int i = 0; i < iters; i++) launch();
+    cudaEventRecord(e1, st);
+    cudaError_t se = cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaStreamDestroy(st);
+    int herr = 0;
+    cudaMemcpy(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost);
+    cleanup();
+    if (se != cudaSuccess) return hs_internal_fail(HS_CUDA, cudaGetErrorString(se));
+    if (herr) {
+        cudaMemset(d_err, 0, sizeof(int));
+        return hs_internal_fail(HS_CUDA, "a kernel wait timed out");
+    }
+    *us_per_launch = 1000.0 * ms / iters;
+    return HS_OK;
+}

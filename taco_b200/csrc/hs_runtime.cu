@@ -1,0 +1,749 @@
+// The host runtime of the B200 HardShell backend and its C ABI (include/hardshell_b200.h).
+//
+// It restates the CUDA engine of the reference (crates/hardshell-cuda) B200-first:
+// - the device: one CUDA context per GPU, one stream per batch (device.rs);
+// - the model: the validated .hsm uploaded once, every weight matrix padded to the GEMM tiles
+//   (K to 128 bytes, N to 256 rows) with its TMA descriptor (model.rs);
+// - the batch: slots with their KV caches, the pass planner with the context restart and
+//   overlap (batch/plan.rs:60-120), one forward pass per plan pass, and the coder op, so that only
+//   32 bytes per input come back (batch.rs:463-570). Positions change only after every pass ran.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/hardshell_b200.h"
+#include "hs_device.hpp"
+#include "hs_kernels.cuh"
+#include "hsm_file.hpp"
+#include "sha256.hpp"
+
+using namespace hs;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+#define CK(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess)                                                                       \
+            return fail(HS_CUDA, std::string(#call) + " failed: " + cudaGetErrorString(e_));         \
+    } while (0)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The GEMM path: the tensor-core kernel, or the dp4a kernel (HS_GEMM=simple, for tests).
+bool use_tc_default() {
+    const char* v = getenv("HS_GEMM");
+    return !(v && strcmp(v, "simple") == 0);
+}
+
+}  // namespace
+
+struct hs_dev {
+    int ordinal = 0;
+    int num_sms = 0;
+    std::string name;
+    int* d_err = nullptr;
+    EncodeTiledFn encode = nullptr;
+};
+
+namespace {
+
+int set_device(hs_dev* d) {
+    CK(cudaSetDevice(d->ordinal));
+    return HS_OK;
+}
+
+// A 2D int8 tensor map over [rows, cols] (cols contiguous): box {128, box_rows}, 128-byte swizzle.
+int make_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    cuuint64_t gdim[2] = {cols, rows};
+    cuuint64_t gstride[1] = {cols};
+    cuuint32_t box[2] = {(cuuint32_t)TILE_K, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    if (((uintptr_t)base & 15) != 0 || (cols & 15) != 0)
+        return fail(HS_UNSUPPORTED, "a TMA tensor needs 16-byte aligned rows");
+    CUresult r = dev->encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(HS_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return HS_OK;
+}
+
+template <typename T>
+int dalloc(T** p, size_t count, std::vector<void*>& owned) {
+    void* q = nullptr;
+    size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    CK(cudaMalloc(&q, bytes));
+    CK(cudaMemset(q, 0, bytes));
+    owned.push_back(q);
+    *p = (T*)q;
+    return HS_OK;
+}
+
+template <typename T>
+int upload(T** p, const T* src, size_t count, std::vector<void*>& owned) {
+    int rc = dalloc(p, count, owned);
+    if (rc) return rc;
+    if (count) CK(cudaMemcpy(*p, src, count * sizeof(T), cudaMemcpyHostToDevice));
+    return HS_OK;
+}
+
+struct DevLinear {
+    LinearDev ld{};
+    alignas(128) CUtensorMap tm;
+};
+
+}  // namespace
+
+struct hs_model {
+    hs_dev* dev = nullptr;
+    std::vector<void*> owned;
+    ModelConsts c{};
+    uint32_t eot = 0, version = 1;
+    uint8_t hash[32] = {0};
+    uint64_t weight_bytes = 0;
+    bool use_tc = true;
+    int8_t* wte = nullptr;
+    int32_t* em = nullptr;
+    int es = 0;
+    int32_t* lm = nullptr;
+    int ls = 0;
+    int8_t* wpe = nullptr;
+    int32_t* pm = nullptr;
+    int ps = 0;
+    std::vector<LayerDev> layers;
+    std::vector<std::unique_ptr<DevLinear>> lins;  // 4 per layer (qkv, proj, fc, mlp), then the LM head
+    LnDev lnf{};
+    int32_t* attn_exp = nullptr;
+    int attn_len = 0;
+    uint64_t* logits_exp = nullptr;
+    int logits_len = 0;
+
+    ~hs_model() {
+        if (dev) cudaSetDevice(dev->ordinal);
+        for (void* p : owned) cudaFree(p);
+    }
+};
+
+struct hs_batch {
+    hs_model* model = nullptr;
+    int slots = 0, max_rows = 0, Rcap = 0;
+    uint16_t overlap = 0;
+    std::vector<int> pos;
+    std::vector<uint32_t> hist;  // [slots, n_ctx]
+    std::vector<void*> owned;
+    cudaStream_t stream = nullptr;
+    int8_t* kc = nullptr;
+    int8_t* vc = nullptr;
+    RowInfo* d_rows = nullptr;
+    int32_t* x = nullptr;
+    int8_t* a = nullptr;
+    int8_t* qkv = nullptr;
+    int8_t* att = nullptr;
+    int8_t* g = nullptr;
+    uint16_t* d16 = nullptr;
+    int64_t* tmax = nullptr;
+    uint64_t* intervals = nullptr;
+    uint64_t* weights = nullptr;
+    RowInfo* h_rows = nullptr;       // pinned
+    uint64_t* h_intervals = nullptr;  // pinned
+    uint64_t bytes = 0;
+    alignas(128) CUtensorMap tm_a;
+    alignas(128) CUtensorMap tm_att;
+    alignas(128) CUtensorMap tm_g;
+
+    ~hs_batch() {
+        if (model) cudaSetDevice(model->dev->ordinal);
+        if (stream) cudaStreamDestroy(stream);
+        for (void* p : owned) cudaFree(p);
+        if (h_rows) cudaFreeHost(h_rows);
+        if (h_intervals) cudaFreeHost(h_intervals);
+    }
+};
+
+namespace {
+
+int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D) {
+    int N = L.rows, K = L.cols;
+    int Np = round_up(N, TILE_N), Kp = round_up(K, TILE_K);
+    std::vector<int8_t> w((size_t)Np * Kp, 0);
+    for (int n = 0; n < N; n++) memcpy(&w[(size_t)n * Kp], &L.w[(size_t)n * K], K);
+    std::vector<int32_t> b(Np, 0), mm(Np, 0);
+    std::copy(L.b.begin(), L.b.end(), b.begin());
+    std::copy(L.rs.m.begin(), L.rs.m.end(), mm.begin());
+    int8_t* dw;
+    int32_t *db, *dm;
+    int rc = upload(&dw, w.data(), w.size(), m->owned);
+    if (!rc) rc = upload(&db, b.data(), b.size(), m->owned);
+    if (!rc) rc = upload(&dm, mm.data(), mm.size(), m->owned);
+    if (rc) return rc;
+    D.ld = LinearDev{dw, N, K, Np, Kp, db, dm, (int)L.rs.s};
+    m->weight_bytes += w.size() + 8 * (size_t)Np;
+    return make_tmap(m->dev, &D.tm, dw, Np, Kp, TILE_N);
+}
+
+int upload_ln(hs_model* m, const hsm::LayerNormP& L, LnDev& D) {
+    int16_t* g;
+    int32_t* b;
+    int rc = upload(&g, L.g.data(), L.g.size(), m->owned);
+    if (!rc) rc = upload(&b, L.b.data(), L.b.size(), m->owned);
+    if (rc) return rc;
+    D = LnDev{g, b, L.m, (int)L.s, (int)L.beta_frac};
+    return HS_OK;
+}
+
+// The forward pass of R rows (the rows are in b->d_rows): the layers, then the logits GEMM.
+int forward(hs_batch* b, int R) {
+    hs_model* m = b->model;
+    const ModelConsts& c = m->c;
+    cudaStream_t st = b->stream;
+    launch_embed(b->d_rows, R, m->wte, c.Dp, m->em, m->es, m->wpe, m->pm, m->ps, c.d, b->x, st);
+    auto gemm = [&](int mode, const int8_t* A, int lda, const CUtensorMap* tmA, const DevLinear& W, EpiArgs e) {
+        if (m->use_tc)
+            launch_gemm_tc(mode, tmA, &W.tm, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms, m->dev->d_err, st);
+        else
+            launch_gemm_simple(mode, A, lda, R, W.ld, e, st);
+    };
+    for (int l = 0; l < c.L; l++) {
+        const LayerDev& Ld = m->layers[l];
+        const DevLinear& qkv = *m->lins[4 * l];
+        const DevLinear& proj = *m->lins[4 * l + 1];
+        const DevLinear& fc = *m->lins[4 * l + 2];
+        const DevLinear& mlp = *m->lins[4 * l + 3];
+        launch_layernorm(b->x, R, c.d, Ld.ln1, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+        EpiArgs e{};
+        e.R = R;
+        e.N = 3 * c.d;
+        e.b = qkv.ld.b;
+        e.m = qkv.ld.m;
+        e.s = qkv.ld.s;
+        e.out8 = b->qkv;
+        e.ldo = c.QKVp;
+        gemm(EPI_ACT, b->a, c.Dp, &b->tm_a, qkv, e);
+        launch_kv_store(b->d_rows, R, b->qkv, c.QKVp, c.d, c.H, c.hd, c.L, l, c.n_ctx, b->kc, b->vc, st);
+        launch_attention(b->d_rows, R, b->qkv, c.QKVp, b->kc, b->vc, c.L, l, c.H, c.hd, c.n_ctx, c.d, Ld.score_m,
+                         Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p, b->att, c.Dp, st);
+        e = EpiArgs{};
+        e.R = R;
+        e.N = c.d;
+        e.b = proj.ld.b;
+        e.m = proj.ld.m;
+        e.s = proj.ld.s;
+        e.x = b->x;
+        e.ldx = c.d;
+        gemm(EPI_RESID, b->att, c.Dp, &b->tm_att, proj, e);
+        launch_layernorm(b->x, R, c.d, Ld.ln2, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+        e = EpiArgs{};
+        e.R = R;
+        e.N = c.f;
+        e.b = fc.ld.b;
+        e.m = fc.ld.m;
+        e.s = fc.ld.s;
+        e.out8 = b->g;
+        e.ldo = c.Fp;
+        e.gelu = Ld.gelu;
+        e.gelu_off = Ld.gelu_off;
+        gemm(EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e);
+        e = EpiArgs{};
+        e.R = R;
+        e.N = c.d;
+        e.b = mlp.ld.b;
+        e.m = mlp.ld.m;
+        e.s = mlp.ld.s;
+        e.x = b->x;
+        e.ldx = c.d;
+        gemm(EPI_RESID, b->g, c.Fp, &b->tm_g, mlp, e);
+    }
+    launch_layernorm(b->x, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+    const DevLinear& lmh = *m->lins[4 * c.L];
+    EpiArgs e{};
+    e.R = R;
+    e.N = c.V;
+    e.m = lmh.ld.m;
+    e.s = lmh.ld.s;
+    e.d16 = b->d16;
+    e.ldd = c.Vp;
+    e.tmax = b->tmax;
+    e.ldt = c.VT;
+    e.last = m->logits_len - 1;
+    gemm(EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e);
+    return HS_OK;
+}
+
+int check_device_error(hs_batch* b) {
+    hs_dev* dev = b->model->dev;
+    CK(cudaStreamSynchronize(b->stream));
+    CK(cudaGetLastError());
+    int herr = 0;
+    CK(cudaMemcpy(&herr, dev->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr != 0) {
+        cudaMemset(dev->d_err, 0, sizeof(int));
+        return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
+    }
+    return HS_OK;
+}
+
+struct PlanRow {
+    uint32_t slot, token, pos;
+    long input;  // -1: a restart row
+};
+
+// batch/plan.rs:60-120: the passes of a call, with the restart rows of a full context. The
+// positions and histories change in copies; the caller commits them after the passes ran.
+void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
+                 std::vector<std::vector<PlanRow>>& passes, std::vector<int>& pos, std::vector<uint32_t>& hist) {
+    const int n_ctx = b->model->c.n_ctx;
+    const int k = std::min<int>(b->overlap, n_ctx - 2);
+    const uint32_t eot = b->model->eot;
+    pos = b->pos;
+    hist = b->hist;
+    std::vector<char> in_pass(b->slots, 0);
+    std::vector<PlanRow> cur;
+    auto flush = [&]() {
+        if (!cur.empty()) passes.push_back(std::move(cur));
+        cur.clear();
+        std::fill(in_pass.begin(), in_pass.end(), 0);
+    };
+    auto push = [&](PlanRow r) {
+        if ((int)cur.size() >= b->max_rows) flush();
+        in_pass[r.slot] = 1;
+        cur.push_back(r);
+    };
+    for (uint32_t i = 0; i < n; i++) {
+        uint32_t s = slots[i];
+        uint32_t* h = &hist[(size_t)s * n_ctx];
+        int at = pos[s];
+        if (at >= n_ctx) {
+            if (in_pass[s]) flush();
+            memmove(h + 1, h + (n_ctx - k), sizeof(uint32_t) * k);
+            h[0] = eot;
+            for (int q = 0; q <= k; q++) push({s, h[q], (uint32_t)q, -1});
+            at = k + 1;
+        }
+        h[at] = tokens[i];
+        push({s, tokens[i], (uint32_t)at, (long)i});
+        pos[s] = at + 1;
+    }
+    flush();
+}
+
+// Runs the passes; with `out` the coder answers (3 u64 per input), else the weights.
+int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds, const uint64_t* values,
+        uint32_t n, uint32_t bits, hs_interval* out, uint64_t* wout) {
+    hs_model* m = b->model;
+    const ModelConsts& c = m->c;
+    for (uint32_t i = 0; i < n; i++) {
+        if (slots[i] >= (uint32_t)b->slots)
+            return fail(HS_BAD_SLOT, "slot " + std::to_string(slots[i]) + " is not valid in a batch of " +
+                                         std::to_string(b->slots) + " slots");
+        if (tokens[i] >= (uint32_t)c.V)
+            return fail(HS_TOKEN_RANGE, "token " + std::to_string(tokens[i]) + " is not in the vocabulary of " +
+                                            std::to_string(c.V) + " tokens");
+    }
+    if (out) {
+        if (bits == 0 || bits > 32 || (uint64_t)c.V > (1ULL << bits))
+            return fail(HS_UNSUPPORTED, "freq_bits must be in 1..=32 and 2^freq_bits >= vocab");
+        for (uint32_t i = 0; i < n; i++) {
+            bool ok = (kinds[i] == 0 && values[i] < (uint64_t)c.V) || (kinds[i] == 1 && values[i] < (1ULL << bits));
+            if (!ok) return fail(HS_UNSUPPORTED, "a coder token or target is out of range");
+        }
+    }
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    std::vector<std::vector<PlanRow>> passes;
+    std::vector<int> pos;
+    std::vector<uint32_t> hist;
+    plan_passes(b, slots, tokens, n, passes, pos, hist);
+    for (auto& pass : passes) {
+        int R = (int)pass.size();
+        for (int r = 0; r < R; r++) {
+            const PlanRow& p = pass[r];
+            RowInfo ri{p.slot, p.token, p.pos, 0, 0};
+            if (out && p.input >= 0) {
+                ri.kind = kinds[p.input];
+                ri.value = values[p.input];
+            }
+            b->h_rows[r] = ri;
+        }
+        CK(cudaMemcpyAsync(b->d_rows, b->h_rows, sizeof(RowInfo) * R, cudaMemcpyHostToDevice, b->stream));
+        rc = forward(b, R);
+        if (rc) return rc;
+        if (out) {
+            launch_coder(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, bits, b->d_rows,
+                         b->intervals, b->stream);
+            CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
+                               b->stream));
+        } else {
+            launch_weights(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, b->weights, b->stream);
+        }
+        rc = check_device_error(b);
+        if (rc) return rc;
+        if (out) {
+            for (int r = 0; r < R; r++) {
+                long in = pass[r].input;
+                if (in < 0) continue;
+                hs_interval& iv = out[in];
+                iv.symbol = (uint32_t)b->h_intervals[3 * r];
+                iv.start = b->h_intervals[3 * r + 1];
+                iv.freq = b->h_intervals[3 * r + 2];
+                iv.is_last = iv.symbol + 1 == (uint32_t)c.V;
+                iv.reserved = 0;
+            }
+        } else {
+            for (int r = 0; r < R; r++) {
+                long in = pass[r].input;
+                if (in < 0) continue;
+                CK(cudaMemcpy(wout + (size_t)in * c.V, b->weights + (size_t)r * c.V, sizeof(uint64_t) * c.V,
+                              cudaMemcpyDeviceToHost));
+            }
+        }
+    }
+    // Every pass ran: commit the positions and histories (batch/plan.rs:120 commit).
+    b->pos = pos;
+    b->hist = hist;
+    return HS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Helpers for the other translation units of the library (not in the public header).
+int hs_internal_tmap(hs_dev* dev, void* tm, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    return make_tmap(dev, (CUtensorMap*)tm, base, rows, cols, box_rows);
+}
+int hs_internal_dev_info(hs_dev* dev, int* num_sms, int** d_err) {
+    int rc = set_device(dev);
+    if (rc) return rc;
+    *num_sms = dev->num_sms;
+    *d_err = dev->d_err;
+    return HS_OK;
+}
+int hs_internal_fail(int code, const char* msg) { return fail(code, msg); }
+
+int hs_last_error(char* buf, size_t cap) {
+    if (!buf || cap == 0) return HS_BAD_ARGUMENT;
+    size_t n = std::min(cap - 1, g_err.size());
+    memcpy(buf, g_err.data(), n);
+    buf[n] = 0;
+    return HS_OK;
+}
+
+int hs_open(int ordinal, hs_dev** out) {
+    if (!out) return fail(HS_BAD_ARGUMENT, "null output");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0)
+        return fail(HS_NO_DEVICE, std::string("no CUDA device: ") + (e != cudaSuccess ? cudaGetErrorString(e) : "none"));
+    if (ordinal < 0 || ordinal >= count) return fail(HS_NO_DEVICE, "no CUDA device " + std::to_string(ordinal));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, ordinal));
+    if (prop.major < 10)
+        return fail(HS_UNSUPPORTED, "the kernels are sm_100a: the GPU needs compute capability 10.0");
+    CK(cudaSetDevice(ordinal));
+    auto d = std::make_unique<hs_dev>();
+    d->ordinal = ordinal;
+    d->num_sms = prop.multiProcessorCount;
+    d->name = prop.name;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess) return fail(HS_CUDA, "cuTensorMapEncodeTiled is not available");
+    d->encode = (EncodeTiledFn)fn;
+    CK(cudaMalloc(&d->d_err, sizeof(int)));
+    CK(cudaMemset(d->d_err, 0, sizeof(int)));
+    CK(configure_core_kernels());
+    CK(configure_tc_kernels());
+    *out = d.release();
+    return HS_OK;
+}
+
+void hs_dev_free(hs_dev* d) {
+    if (!d) return;
+    cudaSetDevice(d->ordinal);
+    if (d->d_err) cudaFree(d->d_err);
+    delete d;
+}
+
+int hs_mem_info(hs_dev* d, uint64_t* free_bytes, uint64_t* total_bytes) {
+    if (!d || !free_bytes || !total_bytes) return fail(HS_BAD_ARGUMENT, "null argument");
+    int rc = set_device(d);
+    if (rc) return rc;
+    size_t f = 0, t = 0;
+    CK(cudaMemGetInfo(&f, &t));
+    *free_bytes = f;
+    *total_bytes = t;
+    return HS_OK;
+}
+
+int hs_dev_name(hs_dev* d, char* buf, size_t cap) {
+    if (!d || !buf || cap == 0) return fail(HS_BAD_ARGUMENT, "null argument");
+    size_t n = std::min(cap - 1, d->name.size());
+    memcpy(buf, d->name.data(), n);
+    buf[n] = 0;
+    return HS_OK;
+}
+
+int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) {
+    if (!dev || !file || !out) return fail(HS_BAD_ARGUMENT, "null argument");
+    *out = nullptr;
+    hsm::Model M;
+    std::string err;
+    if (!hsm::load_model(file, len, M, err)) return fail(HS_MODEL, "the model file is not valid: " + err);
+    if (M.is_wide())
+        return fail(HS_UNSUPPORTED, "hsm format version 2 rules (i16 activations, ln_beta_frac) are not run by "
+                                    "this backend yet");
+    if (M.vocab < 2) return fail(HS_UNSUPPORTED, "the vocabulary needs at least 2 tokens");
+    if ((int)M.logits_exp.size() > MAX_LOGIT_TABLE)
+        return fail(HS_UNSUPPORTED, "the logit table is longer than 16384 entries");
+    if (M.n_ctx > MAX_ATTN_CTX) return fail(HS_UNSUPPORTED, "the context is longer than 8192 positions");
+    if (M.head_dim > 1024) return fail(HS_UNSUPPORTED, "the head width is more than 1024");
+    int rc = set_device(dev);
+    if (rc) return rc;
+    auto m = std::make_unique<hs_model>();
+    m->dev = dev;
+    m->use_tc = use_tc_default();
+    sha256(file, len, m->hash);
+    m->eot = M.eot;
+    m->version = M.version;
+    ModelConsts& c = m->c;
+    c.d = M.d_model;
+    c.f = M.d_ff;
+    c.V = M.vocab;
+    c.H = M.n_head;
+    c.hd = M.head_dim;
+    c.L = M.n_layer;
+    c.n_ctx = M.n_ctx;
+    c.Dp = round_up(c.d, TILE_K);
+    c.Fp = round_up(c.f, TILE_K);
+    c.QKVp = round_up(3 * c.d, 16);
+    c.Vp = round_up(c.V, TILE_N);
+    c.VT = (c.V + LOGIT_TILE - 1) / LOGIT_TILE;
+    c.ln_k = (int)M.ln_k;
+    c.ln_j = (int)M.ln_j;
+    c.ln_eps = M.ln_eps;
+    c.softmax_p = (int)M.softmax_p;
+    // The token embedding doubles as the LM head: [Vp, Dp], rows padded with zeros.
+    hsm::Linear lm;
+    lm.rows = c.V;
+    lm.cols = c.d;
+    lm.w = M.wte;
+    lm.b.assign(c.V, 0);
+    lm.rs = M.logit;
+    for (int l = 0; l < c.L; l++) {
+        const hsm::Block& B = M.blocks[l];
+        LayerDev Ld{};
+        for (const hsm::Linear* L : {&B.c_attn, &B.c_proj, &B.c_fc, &B.mlp_proj}) {
+            m->lins.emplace_back(new DevLinear());
+            rc = upload_linear(m.get(), *L, *m->lins.back());
+            if (rc) return rc;
+        }
+        Ld.qkv = m->lins[4 * l]->ld;
+        Ld.proj = m->lins[4 * l + 1]->ld;
+        Ld.fc = m->lins[4 * l + 2]->ld;
+        Ld.mlp = m->lins[4 * l + 3]->ld;
+        if ((rc = upload_ln(m.get(), B.ln_1, Ld.ln1)) || (rc = upload_ln(m.get(), B.ln_2, Ld.ln2))) return rc;
+        Ld.score_m = B.score_m;
+        Ld.score_s = (int)B.score_s;
+        Ld.out_m = B.out_m;
+        Ld.out_s = (int)B.out_s;
+        int8_t* gl;
+        if ((rc = upload(&gl, B.gelu8.data(), B.gelu8.size(), m->owned))) return rc;
+        Ld.gelu = gl;
+        Ld.gelu_off = (int)B.gelu_offset;
+        m->layers.push_back(Ld);
+    }
+    m->lins.emplace_back(new DevLinear());
+    if ((rc = upload_linear(m.get(), lm, *m->lins.back()))) return rc;
+    m->wte = const_cast<int8_t*>(m->lins.back()->ld.w);
+    m->es = (int)M.embed.s;
+    m->ls = (int)M.logit.s;
+    if ((rc = upload(&m->em, M.embed.m.data(), M.embed.m.size(), m->owned))) return rc;
+    m->lm = const_cast<int32_t*>(m->lins.back()->ld.m);
+    if ((rc = upload(&m->wpe, M.wpe.data(), M.wpe.size(), m->owned))) return rc;
+    if ((rc = upload(&m->pm, M.pos.m.data(), M.pos.m.size(), m->owned))) return rc;
+    m->ps = (int)M.pos.s;
+    if ((rc = upload_ln(m.get(), M.ln_f, m->lnf))) return rc;
+    if ((rc = upload(&m->attn_exp, M.attn_exp.data(), M.attn_exp.size(), m->owned))) return rc;
+    m->attn_len = (int)M.attn_exp.size();
+    if ((rc = upload(&m->logits_exp, M.logits_exp.data(), M.logits_exp.size(), m->owned))) return rc;
+    m->logits_len = (int)M.logits_exp.size();
+    m->weight_bytes += M.wpe.size() + 8 * M.logits_exp.size() + 4 * M.attn_exp.size();
+    CK(cudaDeviceSynchronize());
+    *out = m.release();
+    return HS_OK;
+}
+
+void hs_model_free(hs_model* m) { delete m; }
+
+int hs_model_get_info(hs_model* m, hs_model_info* out) {
+    if (!m || !out) return fail(HS_BAD_ARGUMENT, "null argument");
+    const ModelConsts& c = m->c;
+    out->n_layer = c.L;
+    out->n_head = c.H;
+    out->d_model = c.d;
+    out->d_ff = c.f;
+    out->vocab = c.V;
+    out->n_ctx = c.n_ctx;
+    out->eot_token = m->eot;
+    out->version = m->version;
+    out->cache_bytes_per_slot = 2ULL * c.L * c.n_ctx * c.d;
+    out->weight_bytes = m->weight_bytes;
+    memcpy(out->hash, m->hash, 32);
+    return HS_OK;
+}
+
+int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out) {
+    if (!m || !out) return fail(HS_BAD_ARGUMENT, "null argument");
+    *out = nullptr;
+    if (slots == 0 || max_rows == 0) return fail(HS_UNSUPPORTED, "a batch needs at least one slot and one row");
+    if (max_rows < 2) max_rows = 2;  // a restart needs two rows in one pass
+    if (max_rows > (1u << 20)) return fail(HS_UNSUPPORTED, "max_rows is more than 2^20");
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    auto b = std::make_unique<hs_batch>();
+    b->model = m;
+    b->slots = (int)slots;
+    b->max_rows = (int)max_rows;
+    b->Rcap = round_up((int)max_rows, TILE_M);
+    const ModelConsts& c = m->c;
+    b->pos.assign(slots, 0);
+    b->hist.assign((size_t)slots * c.n_ctx, 0);
+    CK(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
+    size_t cache = (size_t)slots * c.L * c.n_ctx * c.d;
+    size_t R = b->Rcap;
+    if ((rc = dalloc(&b->kc, cache, b->owned)) || (rc = dalloc(&b->vc, cache, b->owned)) ||
+        (rc = dalloc(&b->d_rows, R, b->owned)) || (rc = dalloc(&b->x, R * c.d, b->owned)) ||
+        (rc = dalloc(&b->a, R * c.Dp, b->owned)) || (rc = dalloc(&b->qkv, R * c.QKVp, b->owned)) ||
+        (rc = dalloc(&b->att, R * c.Dp, b->owned)) || (rc = dalloc(&b->g, R * c.Fp, b->owned)) ||
+        (rc = dalloc(&b->d16, R * c.Vp, b->owned)) || (rc = dalloc(&b->tmax, R * c.VT, b->owned)) ||
+        (rc = dalloc(&b->intervals, 3 * R, b->owned)) || (rc = dalloc(&b->weights, R * c.V, b->owned)))
+        return rc;
+    CK(cudaMallocHost(&b->h_rows, sizeof(RowInfo) * R));
+    CK(cudaMallocHost(&b->h_intervals, sizeof(uint64_t) * 3 * R));
+    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 4 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24 +
+                                8 * c.V);
+    if ((rc = make_tmap(m->dev, &b->tm_a, b->a, R, c.Dp, TILE_M)) ||
+        (rc = make_tmap(m->dev, &b->tm_att, b->att, R, c.Dp, TILE_M)) ||
+        (rc = make_tmap(m->dev, &b->tm_g, b->g, R, c.Fp, TILE_M)))
+        return rc;
+    *out = b.release();
+    return HS_OK;
+}
+
+void hs_batch_free(hs_batch* b) { delete b; }
+
+int hs_batch_set_overlap(hs_batch* b, uint16_t k) {
+    if (!b) return fail(HS_BAD_ARGUMENT, "null argument");
+    if ((int)k + 2 > b->model->c.n_ctx)
+        return fail(HS_INVALID_OVERLAP, "the overlap " + std::to_string(k) + " is more than n_ctx - 2");
+    b->overlap = k;
+    return HS_OK;
+}
+
+int hs_batch_reset(hs_batch* b, uint32_t slot) {
+    if (!b) return fail(HS_BAD_ARGUMENT, "null argument");
+    if (slot < (uint32_t)b->slots) b->pos[slot] = 0;
+    return HS_OK;
+}
+
+uint32_t hs_batch_position(hs_batch* b, uint32_t slot) {
+    if (!b || slot >= (uint32_t)b->slots) return 0;
+    return (uint32_t)b->pos[slot];
+}
+
+uint64_t hs_batch_gpu_bytes(hs_batch* b) { return b ? b->bytes : 0; }
+
+int hs_batch_run_coded(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds,
+                       const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out) {
+    if (!b || (n && (!slots || !tokens || !kinds || !values || !out))) return fail(HS_BAD_ARGUMENT, "null argument");
+    return run(b, slots, tokens, kinds, values, n, freq_bits, out, nullptr);
+}
+
+int hs_batch_run_weights(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, uint32_t n, uint64_t* out) {
+    if (!b || (n && (!slots || !tokens || !out))) return fail(HS_BAD_ARGUMENT, "null argument");
+    return run(b, slots, tokens, nullptr, nullptr, n, 32, nullptr, out);
+}
+
+// ---- op-level entry points ----
+
+int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, const int32_t* bias, const int32_t* mult,
+                     uint32_t shift, uint32_t M, uint32_t N, uint32_t K, int8_t* out8, int32_t* raw32) {
+    if (!dev || !A || !W || (!raw32 && (!bias || !mult || !out8))) return fail(HS_BAD_ARGUMENT, "null argument");
+    if (M == 0 || N == 0 || K == 0 || K > 65536) return fail(HS_UNSUPPORTED, "shape out of range");
+    int rc = set_device(dev);
+    if (rc) return rc;
+    std::vector<void*> owned;
+    struct Guard {
+        std::vector<void*>& o;
+        ~Guard() {
+            for (void* p : o) cudaFree(p);
+        }
+    } guard{owned};
+    int Mp = round_up((int)M, TILE_M), Np = round_up((int)N, TILE_N), Kp = round_up((int)K, TILE_K);
+    std::vector<int8_t> ha((size_t)Mp * Kp, 0), hw((size_t)Np * Kp, 0);
+    for (uint32_t r = 0; r < M; r++) memcpy(&ha[(size_t)r * Kp], A + (size_t)r * K, K);
+    for (uint32_t n = 0; n < N; n++) memcpy(&hw[(size_t)n * Kp], W + (size_t)n * K, K);
+    std::vector<int32_t> hb(Np, 0), hm(Np, 0);
+    if (!raw32) {
+        std::copy(bias, bias + N, hb.begin());
+        std::copy(mult, mult + N, hm.begin());
+    }
+    int8_t *da, *dw, *dout;
+    int32_t *db, *dm, *d32;
+    if ((rc = upload(&da, ha.data(), ha.size(), owned)) || (rc = upload(&dw, hw.data(), hw.size(), owned)) ||
+        (rc = upload(&db, hb.data(), hb.size(), owned)) || (rc = upload(&dm, hm.data(), hm.size(), owned)) ||
+        (rc = dalloc(&dout, (size_t)M * N, owned)) || (rc = dalloc(&d32, (size_t)M * N, owned)))
+        return rc;
+    LinearDev L{dw, (int)N, (int)K, Np, Kp, db, dm, (int)shift};
+    EpiArgs e{};
+    e.R = (int)M;
+    e.N = (int)N;
+    e.b = db;
+    e.m = dm;
+    e.s = (int)shift;
+    e.out8 = dout;
+    e.ldo = (int)N;
+    e.out32 = d32;
+    int mode = raw32 ? EPI_RAW : EPI_ACT;
+    cudaStream_t st = 0;
+    if (path == 0) {
+        if (N % 16 != 0) return fail(HS_UNSUPPORTED, "the tensor-core path needs N % 16 == 0 for aligned stores");
+        alignas(128) CUtensorMap ta, tb;
+        if ((rc = make_tmap(dev, &ta, da, Mp, Kp, TILE_M)) || (rc = make_tmap(dev, &tb, dw, Np, Kp, TILE_N)))
+            return rc;
+        launch_gemm_tc(mode, &ta, &tb, (int)M, Np, Kp, e, dev->num_sms, dev->d_err, st);
+    } else {
+        launch_gemm_simple(mode, da, Kp, (int)M, L, e, st);
+    }
+    CK(cudaGetLastError());
+    CK(cudaDeviceSynchronize());
+    int herr = 0;
+    CK(cudaMemcpy(&herr, dev->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) {
+        cudaMemset(dev->d_err, 0, sizeof(int));
+        return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
+    }
+    if (raw32) CK(cudaMemcpy(raw32, d32, sizeof(int32_t) * M * N, cudaMemcpyDeviceToHost));
+    else CK(cudaMemcpy(out8, dout, (size_t)M * N, cudaMemcpyDeviceToHost));
+    return HS_OK;
+}
+
+}  // extern "C"
