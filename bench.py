@@ -1,0 +1,390 @@
+"""Benchmark of the B200 HardShell backend: fold (prefill) throughput in input MB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload ("fold throughput"): the synthetic GPT-2 124M .hsm
+(taco_b200/synth.py), 512 independent 1024-token windows of seeded Zipf text per GPU, all
+positions of every window scored in one forward pass of its slot, each row answered by the coder
+op (the interval of the coded token in FreqTable::from_weights(weights, 32)). One step = one
+run_coded call over the 512 windows (passes of --max-rows rows). Windows are dealt to GPUs
+(weak scaling: 512 per GPU, no collective on the data path; torch.distributed only for the
+barrier and the max over ranks of the timings).
+
+value  = input bytes of all ranks / max over ranks of the device time of the K steps (CUDA
+         events around every pass on the batch stream, the token rows already on the device);
+e2e    = the same bytes / wall time of the K C-ABI calls with host buffers (row upload, planning,
+         interval read back inside);
+roofline = the tcgen05 GEMMs (the dominant kernel class): algorithmic int8 ops / their CUDA-event
+         time, against the int8 tensor peak measured in this run (torch._int_mm, cuBLASLt);
+cpu_baseline = the CPU oracle's fast path (a C++ restatement of the reference CPU engine) on a
+         bounded sample of the same windows, all host threads, rank 0 at N = 1.
+Extra fields: the GEMM microbench and the unfold decode step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fold/unfold input MB/s at 1/2/4/8 B200 (bit-exact); int8 GEMM % of peak"
+WINDOWS, WINDOW = 512, 1024
+NOMINAL_INT8_TOPS = 4500.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--windows", type=int, default=WINDOWS)
+    ap.add_argument("--max-rows", type=int, default=16384)
+    ap.add_argument("--no-extras", action="store_true", help="skip the GEMM microbench and the unfold step")
+    ap.add_argument("--cpu-threads", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    ap.add_argument("--no-peak", action="store_true", help="skip the int8 peak measurement (profiling runs)")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def window_rows(tokens: np.ndarray, eot: int, slot0: int = 0):
+    """The rows of whole windows (gpu_fold.rs:145 Window::rows for window 0 of a block): the
+    inputs [EOT, t0 .. t(n-2)], each row coding the next token."""
+    n_win, n = tokens.shape
+    slots = np.repeat(np.arange(n_win, dtype=np.uint32) + slot0, n)
+    inputs = np.concatenate([np.full((n_win, 1), eot, np.uint32), tokens[:, :-1]], axis=1).reshape(-1)
+    coded = tokens.reshape(-1).astype(np.uint64)
+    return slots, inputs, coded
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_int8_peak_tops(device: int) -> dict:
+    """The dense int8 tensor peak of this GPU: torch._int_mm (cuBLASLt) on 8192^3, best of 10."""
+    import torch
+
+    torch.cuda.set_device(device)
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    torch.cuda.empty_cache()
+    return {"tops": 2.0 * n ** 3 / (best * 1e-3) / 1e12, "how": "torch._int_mm int8 8192^3, best of 10, CUDA events"}
+
+
+def read_traffic() -> float | None:
+    """DRAM bytes per launch of the dominant GEMM from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "gemm_tc_fold.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+def cpu_baseline(model_bytes: bytes, windows: np.ndarray, eot: int, lens: np.ndarray, threads: int,
+                 n_tokens: int) -> dict:
+    """The CPU oracle's fast path on `threads` windows of `n_tokens` tokens (one window per thread)."""
+    from oracle import oracle as O
+
+    om = O.Model(model_bytes)
+    sample = windows[:threads, :n_tokens]
+    fb = O.FastBatch(om, sample.shape[0], 0)
+    slots, inputs, coded = window_rows(sample, eot)
+    t0 = time.perf_counter()
+    fb.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32, threads=threads)
+    dt = time.perf_counter() - t0
+    nbytes = int(lens[coded.astype(np.int64)].sum())
+    return {"value": nbytes / dt / 1e6, "unit": "MB/s", "cores": threads, "kind": "port",
+            "tokens_per_s": slots.size / dt,
+            "sample": f"{sample.shape[0]} windows x {n_tokens} tokens (positions 0..{n_tokens - 1}), "
+                      f"{nbytes} input bytes, {dt:.1f} s, one window per thread"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the CPU oracle port of the reference CPU engine, timed on the host cores."""
+    if rank != 0:
+        return 0
+    from taco_b200 import synth
+
+    model = synth.gpt2_hsm(124)
+    vocab = synth.vocabulary()
+    lens = synth.token_lengths(vocab)
+    threads = args.cpu_threads or os.cpu_count() or 1
+    n_tok = 256
+    wins = synth.zipf_windows(threads, n_tok, seed=1000)
+    from oracle import oracle as O
+
+    om = O.Model(model)
+    slots, inputs, coded = window_rows(wins, synth.VOCAB - 1)
+    nbytes = int(lens[coded.astype(np.int64)].sum())
+    for _ in range(args.warmup):
+        fb = O.FastBatch(om, threads, 0)
+        fb.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        fb = O.FastBatch(om, threads, 0)
+        t0 = time.perf_counter()
+        fb.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32, threads=threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = nbytes * args.steps / total / 1e6
+    sample = f"{threads} windows x {n_tok} tokens per step ({nbytes} input bytes), one window per thread"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "MB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32/int64",
+        "data": "synthetic", "config": {"workload": "fold throughput (configs[2]) sample on host cores",
+                                         "model": "GPT-2 124M synthetic .hsm", "window": n_tok},
+        "cpu_baseline": {"value": value, "unit": "MB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "MB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "tokens_per_s": slots.size * args.steps / total,
+        "note": "the reference is Rust (cargo absent, crates not vendored): its CPU engine runs as the C++ "
+                "oracle port (oracle/), a restatement of crates/hardshell with the same chunked prefill",
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+
+    pg = False
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        pg = True
+
+    from taco_b200 import backend as B
+    from taco_b200 import synth
+
+    model_bytes = synth.gpt2_hsm(124)
+    vocab = synth.vocabulary()
+    lens = synth.token_lengths(vocab)
+    eot = synth.VOCAB - 1
+    windows = synth.zipf_windows(args.windows, WINDOW, seed=1000 + rank)
+    slots, inputs, coded = window_rows(windows, eot)
+    kinds = np.zeros(slots.size, np.uint32)
+    step_bytes = int(lens[coded.astype(np.int64)].sum())
+
+    peak = measured_int8_peak_tops(local) if rank == 0 and not args.no_peak else None
+    dev = B.CudaDevice(local)
+    model = B.CudaModel(dev, model_bytes)
+    batch = B.CudaBatch(model, args.windows, args.max_rows)
+
+    def step():
+        for s in range(args.windows):
+            batch.reset(s)
+        return batch.run_coded(slots, inputs, kinds, coded, 32)
+
+    # Warm-up; the first answers are checked for their symbols (the coded tokens).
+    for i in range(args.warmup):
+        ans = step()
+    if not np.array_equal(ans["symbol"].astype(np.uint64), coded):
+        raise SystemExit("the coder op answered the wrong symbols")
+
+    def barrier():
+        torch.cuda.synchronize(local)
+        if pg:
+            torch.distributed.barrier()
+
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    batch.set_profiling(True)
+    launches0 = B.launch_count()
+    wall = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        wall.append(time.perf_counter() - t0)
+    launches = B.launch_count() - launches0
+    prof = batch.profile()
+    batch.set_profiling(False)
+    barrier()
+    clk = clocks.stop()
+
+    dev_s = prof["pass"]["ms"] / 1e3
+    wall_s = sum(wall)
+    times = torch.tensor([dev_s, wall_s], dtype=torch.float64, device=f"cuda:{local}")
+    if pg:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    dev_s, wall_s = float(times[0]), float(times[1])
+    total_bytes = step_bytes * args.steps * world
+    total_rows = slots.size * args.steps * world
+
+    gemm_ops = sum(prof[k]["ops"] for k in prof if k.startswith("gemm"))
+    gemm_ms = sum(prof[k]["ms"] for k in prof if k.startswith("gemm"))
+    gemm_launches = sum(prof[k]["launches"] for k in prof if k.startswith("gemm"))
+    achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else 0.0
+
+    result = None
+    if rank == 0:
+        kernels = {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
+                       "share": round(v["ms"] / prof["pass"]["ms"], 4) if prof["pass"]["ms"] else None}
+                   for k, v in prof.items() if k != "pass"}
+        for k in kernels:
+            if prof[k]["ops"] and prof[k]["ms"]:
+                kernels[k]["tops"] = round(prof[k]["ops"] / (prof[k]["ms"] * 1e-3) / 1e12, 1)
+        traffic = read_traffic()
+        result = {
+            "metric": METRIC, "value": total_bytes / dev_s / 1e6, "unit": "MB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dev_s / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": "fold throughput (BASELINE configs[2]): 512 windows x 1024 tokens per GPU, "
+                                   "all positions in one forward pass per window, coder interval per row",
+                       "model": "GPT-2 124M .hsm from seeded N(0,0.02) (taco_b200/synth.py)",
+                       "windows_per_gpu": args.windows, "window_tokens": WINDOW, "max_rows_per_pass": args.max_rows,
+                       "parallelism": f"windows dealt to {world} GPU(s), no collective",
+                       "l2": "inputs larger than L2: each step streams 124 MB of weights per pass and "
+                             "9.7 GB of KV cache"},
+            "tokens_per_s": total_rows / dev_s,
+            "e2e": {"value": total_bytes / wall_s / 1e6, "unit": "MB/s",
+                    "h2d_bytes_per_step": int(slots.size * 24), "d2h_bytes_per_step": int(slots.size * 24)},
+            "roofline": {"bound": "tensor", "kernel": "tcgen05 int8 GEMMs (qkv, proj, fc, mlp, logits)",
+                         "achieved": achieved, "peak": peak["tops"] if peak else None, "unit": "TOP/s",
+                         "frac": achieved / peak["tops"] if peak else None,
+                         "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
+                         "peak_source": peak["how"] if peak else None,
+                         "traffic": traffic,
+                         "ops_per_launch": gemm_ops / max(1, gemm_launches)},
+            "clocks": clk,
+            "gpu_launches": launches,
+            "kernels": kernels,
+        }
+
+    # Extras: the GEMM microbench and one unfold decode step.
+    if rank == 0 and not args.no_extras:
+        micro = {}
+        for (K, N) in [(768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 50257)]:
+            n16 = (N + 15) // 16 * 16
+            us = dev.linear_bench(8192, n16, K, seed=7, warmup=3, iters=20)
+            tops = 2.0 * 8192 * N * K / (us * 1e-6) / 1e12
+            micro[f"M8192_K{K}_N{N}"] = {"us": round(us, 2), "tops": round(tops, 1),
+                                        "frac": round(tops / peak["tops"], 3) if peak else None}
+        result["gemm_microbench"] = micro
+        result["unfold"] = unfold_step(B, model, lens, eot, clock_note=None)
+    if rank == 0:
+        if world == 1 and not args.no_cpu:
+            threads = args.cpu_threads or os.cpu_count() or 1
+            result["cpu_baseline"] = cpu_baseline(model_bytes, windows, eot, lens, threads, 1024)
+        print(json.dumps(result))
+    batch.close()
+    model.close()
+    dev.close()
+    if pg:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, context: int = 512, steps: int = 16) -> dict:
+    """1024 streams decoded token by token. The streams are filled to `context`
+    positions (prefill, not timed), then `steps` decode steps (one row per stream, the coder
+    op answering each row) are timed with the wall clock around the C-ABI calls."""
+    from taco_b200 import synth
+
+    toks = synth.zipf_windows(streams, context + steps, seed=77)
+    batch = B.CudaBatch(model, streams, 16384)
+    slots, inputs, coded = window_rows(toks[:, :context], eot)
+    batch.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32)
+    sl = np.arange(streams, dtype=np.uint32)
+    kinds = np.zeros(streams, np.uint32)
+    batch.set_profiling(True)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        batch.run_coded(sl, toks[:, context + i - 1], kinds, toks[:, context + i].astype(np.uint64), 32)
+    wall = time.perf_counter() - t0
+    prof = batch.profile()
+    batch.close()
+    dev_s = prof["pass"]["ms"] / 1e3
+    nbytes = int(lens[toks[:, context:context + steps].astype(np.int64)].sum())
+    kv_read = streams * steps * 2 * 12 * 768 * (context + steps / 2)
+    return {"streams": streams, "positions": f"{context}..{context + steps - 1}", "steps": steps,
+            "tokens_per_s": streams * steps / dev_s, "MB_per_s": nbytes / dev_s / 1e6,
+            "e2e_tokens_per_s": streams * steps / wall,
+            "kv_GB_per_s": kv_read / dev_s / 1e9,
+            "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3)}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

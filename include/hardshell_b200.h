@@ -105,6 +105,24 @@ int hs_batch_run_weights(hs_batch* batch, const uint32_t* slots, const uint32_t*
 /* The message of the last error of the calling thread (NUL-terminated, cut to `cap`). */
 int hs_last_error(char* buf, size_t cap);
 
+/* The per-op device time of the passes that ran since profiling was switched on, as
+ * CudaBatch::profile gives it (crates/hardshell-cuda/src/batch.rs:488-499): the reference marks
+ * each op with a %globaltimer stamp, this backend brackets each launch with CUDA events on the
+ * batch stream. `ops` is the algorithmic integer work of the op (2 per multiply-add). */
+typedef struct hs_op_profile {
+    char name[32];
+    double ms;
+    uint64_t launches;
+    uint64_t ops;
+} hs_op_profile;
+
+/* Switches the profile on (1) or off (0) and clears it (batch.rs:488 profile). */
+int hs_batch_set_profiling(hs_batch* batch, int on);
+/* Fills up to `cap` op entries; returns their number (0 when profiling is off), or < 0 on error. */
+int hs_batch_profile(hs_batch* batch, hs_op_profile* out, int cap);
+/* The number of kernel launches of this library in this process (for the benchmark). */
+uint64_t hs_launch_count(void);
+
 /* ---- op-level entry points: the kernels alone, for tests and measurements ----
  * (the reference's op-level path, crates/hardshell-cuda/src/batch/record.rs, and its GEMM tests,
  * crates/hardshell-cuda/tests/ops.rs). Host buffers in and out. */

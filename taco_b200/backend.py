@@ -48,6 +48,11 @@ class ModelInfo(ctypes.Structure):
                 ("hash", ctypes.c_uint8 * 32)]
 
 
+class OpProfile(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("ms", ctypes.c_double), ("launches", ctypes.c_uint64),
+                ("ops", ctypes.c_uint64)]
+
+
 INTERVAL_DTYPE = np.dtype([("symbol", "<u4"), ("is_last", "<u4"), ("start", "<u8"), ("freq", "<u8"),
                            ("reserved", "<u8")])
 
@@ -86,6 +91,10 @@ def lib() -> ctypes.CDLL:
     L.hs_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_bench.argtypes = [vp, i32, u32, u32, u32, u64, i32, i32, ctypes.POINTER(ctypes.c_double)]
+    L.hs_batch_set_profiling.argtypes = [vp, i32]
+    L.hs_batch_profile.argtypes = [vp, vp, i32]
+    L.hs_launch_count.argtypes = []
+    L.hs_launch_count.restype = u64
     _lib = L
     return L
 
@@ -99,6 +108,11 @@ def _check(rc: int):
 
 def _p(a: np.ndarray) -> ctypes.c_void_p:
     return ctypes.c_void_p(a.ctypes.data)
+
+
+def launch_count() -> int:
+    """Kernel launches of the library in this process."""
+    return int(lib().hs_launch_count())
 
 
 class CudaDevice:
@@ -245,6 +259,18 @@ class CudaBatch:
 
     def gpu_bytes(self) -> int:
         return lib().hs_batch_gpu_bytes(self.h)
+
+    def set_profiling(self, on: bool):
+        """CudaBatch::profile: per-op device time from CUDA events around each launch."""
+        _check(lib().hs_batch_set_profiling(self.h, int(on)))
+
+    def profile(self) -> dict[str, dict]:
+        arr = (OpProfile * 32)()
+        n = lib().hs_batch_profile(self.h, arr, 32)
+        if n < 0:
+            _check(n)
+        return {arr[i].name.decode(): {"ms": arr[i].ms, "launches": arr[i].launches, "ops": arr[i].ops}
+                for i in range(n)}
 
     def run_coded(self, slots, tokens, kinds, values, freq_bits: int = 32) -> np.ndarray:
         """The coder answers of the inputs: a structured array (symbol, is_last, start, freq)."""

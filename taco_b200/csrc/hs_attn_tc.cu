@@ -1,0 +1,400 @@
+// Prefill attention of the B200 HardShell backend on the tensor cores (tcgen05).
+//
+// One CTA per (group, head): a group is up to 128 rows of one slot at consecutive positions
+// pos0 .. pos0 + count - 1, attending causally to the keys 0 .. pos0 + count - 1 of its slot.
+// The integer softmax of crates/hardshell/src/softmax.rs:78 needs the exact row max before any
+// weight and the exact row sum before any probability, so the scores S = Q K^T are computed
+// three times per 128-key chunk on the tensor cores (cheap: K = 64):
+//   pass 1: S -> the max and min dot of each row (score() is monotone in the dot, so the max
+//           score is max(score(maxdot), score(mindot)), as in the reference GPU kernel);
+//   pass 2: S -> e = attn_exp[min(max - score, len - 1)] -> the row sum;
+//   pass 3: S -> p = floor(e * 2^P / sum) (a 64-bit reciprocal and one exact correction), split
+//           into four unsigned bytes p = p0 + 2^8 p1 + 2^16 p2 + 2^24 p3, written to shared
+//           memory as four u8 A operands; O_k += P_k V (u8 x s8) accumulates in TMEM.
+// Then acc = sum_k 2^(8k) O_k (exact: each O_k has at most n_ctx terms below 2^15) and
+// att = clamp(rescale(acc, out_m, out_s), -127, 127) (crates/hardshell/src/gpt2/reference.rs:252-284).
+//
+// Operands come in by TMA (no multicast): Q [128 x 64] and K chunks [128 x 64] with the 64-byte
+// swizzle, V^T chunks [64 x 128] with the 128-byte swizzle from the transposed values cache.
+// Warps 0..7 do the softmax (TMEM lane group warp % 4, key half warp / 4), warp 8 is the TMA
+// producer, warp 9 owns TMEM and issues the MMAs. Every wait is bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "hs_common.cuh"
+#include "hs_kernels.cuh"
+
+namespace hs {
+
+namespace {
+
+constexpr int GM = 128;        // rows of a group (TMEM lanes)
+constexpr int KC = 128;        // keys per chunk
+constexpr int HDIM = 64;       // head width of this kernel
+constexpr int EW = 8;          // epilogue warps
+constexpr int ETH = 32 * EW;   // epilogue threads
+constexpr int ATHREADS = ETH + 64;
+constexpr int Q_BYTES = GM * HDIM;        // 8 KB
+constexpr int K_BYTES = KC * HDIM;        // 8 KB
+constexpr int V_BYTES = HDIM * KC;        // 8 KB
+constexpr int P_BYTES = 4 * GM * KC;      // 64 KB (four planes)
+constexpr int TABLE_MAX = 8192;           // attn_exp entries kept in shared memory
+constexpr size_t ASMEM = (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + P_BYTES + 4 * TABLE_MAX + 4 * GM * 8 + 512 + 1024;
+
+struct __align__(8) ABars {
+    uint64_t q_full;
+    uint64_t k_full[2], k_empty[2];
+    uint64_t v_full[2], v_empty[2];
+    uint64_t s_full[2], s_empty[2];
+    uint64_t p_full, p_empty;
+    uint64_t o_full;
+    uint32_t tmem_base;
+};
+
+// The shared-memory descriptor of a K-major tile with the 64-byte swizzle (rows of 64 bytes,
+// 8-row groups 512 bytes apart), descriptor version 1, layout type 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;
+    return d;
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ int64_t score_of(int32_t dot, int32_t sm, int ss, bool fast, int64_t h) {
+    int64_t y = fast ? (((int64_t)dot * (int64_t)sm + h) >> ss) : rescale64(dot, sm, (uint32_t)ss);
+    return clamp64(y, -SCORE_LIMIT, SCORE_LIMIT);
+}
+
+__global__ void __launch_bounds__(ATHREADS, 1)
+    k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const AttnGroup* groups, int L, int layer, int H,
+                   int n_ctx, int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P,
+                   int8_t* att, int lda, int* err) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sQ = smem;
+    uint8_t* sK = sQ + Q_BYTES;                 // 2 x 8 KB
+    uint8_t* sV = sK + 2 * K_BYTES;             // 2 x 8 KB
+    uint8_t* sP = sV + 2 * V_BYTES;             // 4 planes x 16 KB
+    int32_t* sT = reinterpret_cast<int32_t*>(sP + P_BYTES);
+    int64_t* sX = reinterpret_cast<int64_t*>(sT + TABLE_MAX);  // [2][2][GM] row exchange
+    ABars* bars = reinterpret_cast<ABars*>(sX + 4 * GM);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const AttnGroup grp = groups[blockIdx.x];
+    const int h = blockIdx.y;
+    const int n_keys = (int)grp.pos0 + (int)grp.count;
+    const int nch = (n_keys + KC - 1) / KC;
+    const size_t head = ((size_t)grp.slot * L + layer) * H + h;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->q_full, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bars->k_full[i], 1);
+            mbar_init(&bars->k_empty[i], 1);
+            mbar_init(&bars->v_full[i], 1);
+            mbar_init(&bars->v_empty[i], 1);
+            mbar_init(&bars->s_full[i], 1);
+            mbar_init(&bars->s_empty[i], ETH);
+        }
+        mbar_init(&bars->p_full, ETH);
+        mbar_init(&bars->p_empty, 1);
+        mbar_init(&bars->o_full, 1);
+        fence_barrier_init();
+    }
+    if (warp == EW + 1) {
+        tmem_alloc(&bars->tmem_base, 512);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    const int tl = tlen < TABLE_MAX ? tlen : TABLE_MAX;
+    for (int i = threadIdx.x; i < tl; i += ATHREADS) sT[i] = table[i];
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == EW) {
+        // TMA producer: Q, then K chunks for the three passes, with the V^T chunks in pass 3.
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            mbar_arrive_expect_tx(&bars->q_full, Q_BYTES);
+            tma_load_2d(sQ, &tmQ, &bars->q_full, h * HDIM, (int)grp.first_row);
+            int ks = 0, vs = 0;
+            uint32_t kph = 0, vph = 0;
+            bool ok = true;
+            for (int it = 0; it < 3 * nch && ok; it++) {
+                int c = it % nch;
+                if (!mbar_wait(&bars->k_empty[ks], kph ^ 1, err, 11)) break;
+                mbar_arrive_expect_tx(&bars->k_full[ks], K_BYTES);
+                tma_load_2d(sK + ks * K_BYTES, &tmK, &bars->k_full[ks], 0, (int)(head * n_ctx) + c * KC);
+                if (++ks == 2) {
+                    ks = 0;
+                    kph ^= 1;
+                }
+                if (it >= 2 * nch) {
+                    if (!mbar_wait(&bars->v_empty[vs], vph ^ 1, err, 12)) break;
+                    mbar_arrive_expect_tx(&bars->v_full[vs], V_BYTES);
+                    tma_load_2d(sV + vs * V_BYTES, &tmV, &bars->v_full[vs], c * KC, (int)(head * HDIM));
+                    if (++vs == 2) {
+                        vs = 0;
+                        vph ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == EW + 1) {
+        // MMA issuer.
+        if (lane == 0) {
+            const uint32_t id_s = idesc_i8(GM, KC, true, true);
+            const uint32_t id_pv = idesc_i8(GM, HDIM, false, true);
+            bool ok = mbar_wait(&bars->q_full, 0, err, 13);
+            tc_fence_after();
+            const uint32_t qa = smem_u32(sQ);
+            int ks = 0, vs = 0;
+            uint32_t kph = 0, vph = 0, pph = 0;
+            for (int it = 0; it < 3 * nch && ok; it++) {
+                const int c = it % nch;
+                const int sb = it & 1;
+                const uint32_t sph = (it >> 1) & 1;
+                if (!mbar_wait(&bars->s_empty[sb], sph ^ 1, err, 14)) break;
+                if (!mbar_wait(&bars->k_full[ks], kph, err, 15)) break;
+                tc_fence_after();
+                const uint32_t kb = smem_u32(sK + ks * K_BYTES);
+                const uint32_t d = tmem + sb * KC;
+#pragma unroll
+                for (int k = 0; k < HDIM / 32; k++)
+                    mma_i8(d, sdesc_sw64(qa + 32 * k), sdesc_sw64(kb + 32 * k), id_s, k != 0 ? 1u : 0u);
+                mma_commit(&bars->k_empty[ks]);
+                mma_commit(&bars->s_full[sb]);
+                if (++ks == 2) {
+                    ks = 0;
+                    kph ^= 1;
+                }
+                if (it >= 2 * nch) {
+                    // P of this chunk from the softmax warps, then O_k += P_k V for the four planes.
+                    if (!mbar_wait(&bars->p_full, pph, err, 16)) break;
+                    if (!mbar_wait(&bars->v_full[vs], vph, err, 17)) break;
+                    tc_fence_after();
+                    const uint32_t vb = smem_u32(sV + vs * V_BYTES);
+#pragma unroll
+                    for (int pl = 0; pl < 4; pl++) {
+                        const uint32_t pa = smem_u32(sP + pl * (GM * KC));
+                        const uint32_t o = tmem + 2 * KC + pl * HDIM;
+#pragma unroll
+                        for (int k = 0; k < KC / 32; k++)
+                            mma_i8(o, sdesc_sw128(pa + 32 * k), sdesc_sw128(vb + 32 * k), id_pv,
+                                   (c > 0 || k > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&bars->v_empty[vs]);
+                    mma_commit(&bars->p_empty);
+                    if (++vs == 2) {
+                        vs = 0;
+                        vph ^= 1;
+                    }
+                    pph ^= 1;
+                }
+            }
+            mma_commit(&bars->o_full);
+        }
+    } else {
+        // Softmax warps: one row per thread, 64 keys of each chunk (half = warp / 4).
+        const int g = warp & 3, half = warp >> 2;
+        const int row = g * 32 + lane;
+        const int rpos = (int)grp.pos0 + row;  // rows past the group compute harmless values
+        const uint32_t tbase = tmem + ((uint32_t)(g * 32) << 16);
+        const bool fast = ss >= 0 && ss <= 62;
+        const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
+        const int64_t last = tl - 1;
+        int it = 0;
+        // Pass 1: the max and min dot over the row's causal keys.
+        int32_t maxd = INT32_MIN, mind = INT32_MAX;
+        for (int c = 0; c < nch; c++, it++) {
+            const int sb = it & 1;
+            mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 21);
+            __syncwarp();
+            tc_fence_after();
+#pragma unroll
+            for (int q2 = 0; q2 < 2; q2++) {
+                uint32_t v[32];
+                __syncwarp();
+                tmem_ld32(tbase + sb * KC + half * 64 + q2 * 32, v);
+                tmem_ld_wait();
+                const int j0 = c * KC + half * 64 + q2 * 32;
+#pragma unroll
+                for (int q = 0; q < 32; q++) {
+                    if (j0 + q <= rpos) {
+                        int32_t dv = (int32_t)v[q];
+                        maxd = dv > maxd ? dv : maxd;
+                        mind = dv < mind ? dv : mind;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->s_empty[sb]);
+        }
+        sX[(0 * 2 + half) * GM + row] = maxd;
+        sX[(1 * 2 + half) * GM + row] = mind;
+        named_bar(1, ETH);
+        {
+            int64_t a = sX[(0 * 2 + (half ^ 1)) * GM + row], b = sX[(1 * 2 + (half ^ 1)) * GM + row];
+            maxd = (int32_t)(a > maxd ? a : maxd);
+            mind = (int32_t)(b < mind ? b : mind);
+        }
+        int64_t M = INT64_MIN;
+        if (maxd >= mind) {
+            int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
+            M = s1 > s2 ? s1 : s2;
+        }
+        // Pass 2: the row sum of e.
+        uint64_t sum = 0;
+        for (int c = 0; c < nch; c++, it++) {
+            const int sb = it & 1;
+            mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 22);
+            __syncwarp();
+            tc_fence_after();
+#pragma unroll
+            for (int q2 = 0; q2 < 2; q2++) {
+                uint32_t v[32];
+                __syncwarp();
+                tmem_ld32(tbase + sb * KC + half * 64 + q2 * 32, v);
+                tmem_ld_wait();
+                const int j0 = c * KC + half * 64 + q2 * 32;
+#pragma unroll
+                for (int q = 0; q < 32; q++) {
+                    if (j0 + q <= rpos) {
+                        int64_t dd = M - score_of((int32_t)v[q], sm, ss, fast, hround);
+                        sum += (uint64_t)sT[dd < last ? dd : last];
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->s_empty[sb]);
+        }
+        named_bar(1, ETH);  // everyone has read sX (pass 1) before it is reused
+        sX[(0 * 2 + half) * GM + row] = (int64_t)sum;
+        named_bar(1, ETH);
+        sum += (uint64_t)sX[(0 * 2 + (half ^ 1)) * GM + row];
+        if (sum == 0) sum = 1;
+        const uint64_t rec = (~0ULL) / sum;
+        // Pass 3: p, its four byte planes into shared memory (128-byte swizzle, K-major), P V.
+        uint32_t pph = 0;
+        const uint32_t rsw = (uint32_t)(row & 7);
+        uint8_t* prow = sP + (row >> 3) * 1024 + (row & 7) * 128;
+        for (int c = 0; c < nch; c++, it++) {
+            const int sb = it & 1;
+            mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 23);
+            __syncwarp();
+            tc_fence_after();
+            uint32_t pw[4][16];  // [plane][4-key word] for this thread's 64 keys
+#pragma unroll
+            for (int q2 = 0; q2 < 2; q2++) {
+                uint32_t v[32];
+                __syncwarp();
+                tmem_ld32(tbase + sb * KC + half * 64 + q2 * 32, v);
+                tmem_ld_wait();
+                const int j0 = c * KC + half * 64 + q2 * 32;
+#pragma unroll
+                for (int q = 0; q < 32; q++) {
+                    uint32_t p = 0;
+                    if (j0 + q <= rpos) {
+                        int64_t dd = M - score_of((int32_t)v[q], sm, ss, fast, hround);
+                        uint64_t x = (uint64_t)(uint32_t)sT[dd < last ? dd : last] << P;
+                        uint64_t qv = __umul64hi(x, rec);
+                        while ((qv + 1) * sum <= x) qv++;
+                        p = (uint32_t)qv;
+                    }
+                    const int w = (q2 * 32 + q) >> 2, sh = 8 * (q & 3);
+#pragma unroll
+                    for (int pl = 0; pl < 4; pl++) {
+                        uint32_t byte = (p >> (8 * pl)) & 255u;
+                        if ((q & 3) == 0) pw[pl][w] = byte;
+                        else pw[pl][w] |= byte << sh;
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->s_empty[sb]);
+            // The previous chunk's P V must be done before the planes are overwritten.
+            mbar_wait(&bars->p_empty, pph ^ 1, err, 24);
+            __syncwarp();
+#pragma unroll
+            for (int pl = 0; pl < 4; pl++) {
+                uint8_t* base = prow + pl * (GM * KC);
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++) {
+                    const uint32_t chunk = (uint32_t)(half * 4 + cc);  // 16-byte chunk of the 128-byte row
+                    *reinterpret_cast<uint4*>(base + ((chunk ^ rsw) << 4)) =
+                        make_uint4(pw[pl][4 * cc], pw[pl][4 * cc + 1], pw[pl][4 * cc + 2], pw[pl][4 * cc + 3]);
+                }
+            }
+            fence_proxy_async();
+            mbar_arrive(&bars->p_full);
+            pph ^= 1;
+        }
+        // O: acc = sum_k 2^(8k) O_k, then the output rescale.
+        mbar_wait(&bars->o_full, 0, err, 25);
+        __syncwarp();
+        tc_fence_after();
+        const bool row_ok = row < (int)grp.count;
+        int32_t o[4][32];
+#pragma unroll
+        for (int pl = 0; pl < 4; pl++) {
+            __syncwarp();
+            tmem_ld32(tbase + 2 * KC + pl * HDIM + half * 32, reinterpret_cast<uint32_t(&)[32]>(o[pl]));
+        }
+        tmem_ld_wait();
+        if (row_ok) {
+            uint32_t packed[8];
+#pragma unroll
+            for (int q = 0; q < 32; q++) {
+                int64_t acc = ((((int64_t)o[3][q] * 256 + o[2][q]) * 256 + o[1][q]) * 256) + o[0][q];
+                int8_t y = (int8_t)clamp128(rescale128(acc, om, (uint32_t)os), -127, 127);
+                if ((q & 3) == 0) packed[q >> 2] = (uint8_t)y;
+                else packed[q >> 2] |= (uint32_t)(uint8_t)y << (8 * (q & 3));
+            }
+            uint4* dst = reinterpret_cast<uint4*>(att + (size_t)(grp.first_row + row) * lda + h * HDIM + half * 32);
+            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == EW + 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace
+
+cudaError_t configure_attn_tc() {
+    return cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+}
+
+bool attention_tc_supported(int hd, int n_ctx, int tlen) {
+    return hd == HDIM && n_ctx % 16 == 0 && n_ctx <= 8192 && tlen <= TABLE_MAX;
+}
+
+void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, const AttnGroup* groups, int n_groups,
+                         int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,
+                         const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st) {
+    if (n_groups <= 0) return;
+    dim3 grid(n_groups, H);
+    k_attention_tc<<<grid, ATHREADS, ASMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(tmQ),
+                                                  *reinterpret_cast<const CUtensorMap*>(tmK),
+                                                  *reinterpret_cast<const CUtensorMap*>(tmV), groups, L, layer, H,
+                                                  n_ctx, sm, ss, om, os, table, tlen, P, att, lda, err);
+}
+
+}  // namespace hs

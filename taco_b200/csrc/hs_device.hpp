@@ -54,6 +54,12 @@ struct RowInfo {
     uint64_t value;
 };
 
+// A run of up to 128 rows of one slot at consecutive positions pos0 .. pos0 + count - 1, whose
+// rows are first_row .. first_row + count - 1 of the pass (the prefill attention unit).
+struct AttnGroup {
+    uint32_t first_row, count, slot, pos0;
+};
+
 // The epilogue of a GEMM tile: what happens to acc = W[n] . A[r] (exact s32).
 enum EpiMode : int {
     EPI_ACT = 0,     // out8[r, n] = clamp(rescale(acc + b[n], m[n], s), -127, 127)
@@ -61,6 +67,9 @@ enum EpiMode : int {
     EPI_RESID = 2,   // x[r, n] = clamp(x[r, n] + rescale(acc + b[n], m[n], s), -R, R)
     EPI_LOGITS = 3,  // l = clamp(rescale(acc, m[n], s), +-2^40); tile max and d16 = min(tmax - l, last)
     EPI_RAW = 4,     // out32[r, n] = acc (the GEMM tests)
+    EPI_DELTA = 5,   // out32[r, n] = clamp(rescale(acc + b[n], m[n], s), i32); the residual add and its
+                     // clamp to [-R, R] happen in the next LayerNorm kernel: clamping the delta to the
+                     // i32 range first gives the same result, because |x| <= R < 2^30.
 };
 
 struct EpiArgs {

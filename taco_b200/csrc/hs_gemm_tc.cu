@@ -6,12 +6,15 @@
 // requantisation of HardShell (crates/hardshell/src/gpt2/ops.rs:107-169 linear, :213 logits)
 // before any value leaves the SM.
 //
-// Persistent kernel, one CTA per SM, 6 warps:
-//   warp 0      TMA producer (one thread): A and B tiles into a 4-stage ring;
+// Persistent kernel, one CTA per SM, 10 warps:
+//   warp 0      TMA producer (one thread): A and B tiles into a ring of 3 or 4 stages;
 //   warp 1      TMEM owner and MMA issuer (one thread);
-//   warps 2..5  epilogue: each thread owns one accumulator row (TMEM lane).
+//   warps 2..9  epilogue: TMEM lane group (warp % 4) and column half ((warp - 2) / 4), so each
+//               thread owns 128 of the 256 accumulator columns of one row.
 // The accumulator is double-buffered in TMEM (2 x 256 columns), so the epilogue of one tile runs
-// while the MMAs of the next tile fill the other buffer. Every wait is bounded.
+// while the MMAs of the next tile fill the other buffer. The per-column multiplier and the bias
+// folded with the rounding constant (c = b * m + 2^(s-1)) are staged in shared memory once per
+// tile, so an output costs one 32x32->64 multiply-add and one shift. Every wait is bounded.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -28,92 +31,50 @@ constexpr int BM = TILE_M;   // 128 rows (TMEM lanes)
 constexpr int BN = TILE_N;   // 256 columns (one MMA instruction N)
 constexpr int BK = TILE_K;   // 128 bytes of K per stage (one swizzle atom row)
 constexpr int UMMA_K = 32;   // K of one kind::i8 instruction
-constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int THREADS = 192;
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int EPI_WARPS = 8;
+constexpr int EPI_THREADS = 32 * EPI_WARPS;
+constexpr int THREADS = 64 + EPI_THREADS;
+constexpr int GELU_SMEM = 65536;
+
+template <int MODE>
+struct Cfg {
+    static constexpr int STAGES = MODE == EPI_GELU ? 3 : 4;
+    static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : 0;
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + EXTRA + 2 * BN * 12 + 2 * 2 * BM * 8 + 256 + 1024;
+};
 
 struct __align__(8) Bars {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[4];
+    uint64_t empty[4];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint32_t tmem_base;
 };
 
-__device__ __forceinline__ void epi_chunk(int mode, const EpiArgs& e, int row, int col, const uint32_t (&v)[16]) {
-    const bool row_ok = row < e.R;
-    if (!row_ok) return;
-    if (mode == EPI_RAW) {
-#pragma unroll
-        for (int i = 0; i < 16; i++)
-            if (col + i < e.N) e.out32[(size_t)row * e.ldo + col + i] = (int32_t)v[i];
-        return;
-    }
-    if (mode == EPI_ACT || mode == EPI_GELU) {
-        uint32_t packed[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-            int n = col + i < e.N ? col + i : e.N - 1;
-            int64_t y = rescale64((int64_t)(int32_t)v[i] + (int64_t)e.b[n], e.m[n], e.s);
-            int8_t o;
-            if (mode == EPI_ACT) {
-                o = (int8_t)clamp64(y, -127, 127);
-            } else {
-                int64_t in = clamp64(y, -e.gelu_off, e.gelu_off - 1);
-                o = e.gelu[in + e.gelu_off];
-            }
-            packed[i >> 2] |= (uint32_t)(uint8_t)o << (8 * (i & 3));
-        }
-        int8_t* dst = e.out8 + (size_t)row * e.ldo + col;
-        if (col + 16 <= e.N && (e.ldo & 15) == 0) {
-            *reinterpret_cast<uint4*>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; i++)
-                if (col + i < e.N) dst[i] = (int8_t)(packed[i >> 2] >> (8 * (i & 3)));
-        }
-        return;
-    }
-    if (mode == EPI_RESID) {
-        int32_t* xp = e.x + (size_t)row * e.ldx + col;
-        if (col + 16 <= e.N && (e.ldx & 3) == 0) {
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                int4 xv = reinterpret_cast<int4*>(xp)[q];
-                int32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    int n = col + 4 * q + i;
-                    int64_t y = rescale64((int64_t)(int32_t)v[4 * q + i] + (int64_t)e.b[n], e.m[n], e.s);
-                    xs[i] = (int32_t)clamp64((int64_t)xs[i] + y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-                }
-                reinterpret_cast<int4*>(xp)[q] = make_int4(xs[0], xs[1], xs[2], xs[3]);
-            }
-        } else {
-            for (int i = 0; i < 16; i++) {
-                int n = col + i;
-                if (n >= e.N) break;
-                int64_t y = rescale64((int64_t)(int32_t)v[i] + (int64_t)e.b[n], e.m[n], e.s);
-                xp[i] = (int32_t)clamp64((int64_t)xp[i] + y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-            }
-        }
-    }
+__device__ __forceinline__ int64_t rescale_fast(uint32_t acc, int32_t m, int64_t c, int s, bool fast) {
+    // fast (0 <= s <= 62): floor((acc * m + b * m + 2^(s-1)) / 2^s) with c = b * m + 2^(s-1);
+    // |acc * m| <= 2^61 and |c| < 2^62 + 2^61, so the sum fits in an i64 and the shift is the floor.
+    // Otherwise c holds b and the general rule runs (int.rs:63).
+    if (fast) return ((int64_t)(int32_t)acc * (int64_t)m + c) >> s;
+    return rescale64((int64_t)(int32_t)acc + c, m, (uint32_t)s);
 }
 
-__device__ __forceinline__ int64_t logit_of(const EpiArgs& e, int n, uint32_t acc) {
-    return clamp64(rescale64((int64_t)(int32_t)acc, e.m[n], e.s), -SCORE_LIMIT, SCORE_LIMIT);
-}
-
+template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int mode, int MT,
-              int NT, int KB, EpiArgs e, int* err) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int MT, int NT,
+              int KB, EpiArgs e, int* err) {
+    constexpr int STAGES = Cfg<MODE>::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    Bars* bars = reinterpret_cast<Bars*>(smem + (size_t)STAGES * STAGE_BYTES);
+    int8_t* s_gelu = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * STAGE_BYTES);
+    int64_t* s_c = reinterpret_cast<int64_t*>(smem + (size_t)STAGES * STAGE_BYTES + Cfg<MODE>::EXTRA);  // [2][BN]
+    int32_t* s_m = reinterpret_cast<int32_t*>(s_c + 2 * BN);                                            // [2][BN]
+    int64_t* s_tm = reinterpret_cast<int64_t*>(s_m + 2 * BN);                                           // [2][2][BM]
+    Bars* bars = reinterpret_cast<Bars*>(s_tm + 2 * 2 * BM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (warp == 0 && lane == 0) {
@@ -125,7 +86,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&bars->tfull[a], 1);
-            mbar_init(&bars->tempty[a], 128);
+            mbar_init(&bars->tempty[a], EPI_THREADS);
         }
         fence_barrier_init();
     }
@@ -133,6 +94,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_alloc(&bars->tmem_base, TMEM_COLS);
         tmem_relinquish();
         tc_fence_before();
+    }
+    if (MODE == EPI_GELU) {
+        // The GELU table (256 or 65536 i8 entries) in shared memory for the epilogue look-ups.
+        const int n = 2 * e.gelu_off;
+        for (int i = threadIdx.x * 16; i < n; i += THREADS * 16)
+            *reinterpret_cast<int4*>(s_gelu + i) = *reinterpret_cast<const int4*>(e.gelu + i);
     }
     __syncthreads();
     tc_fence_after();
@@ -198,77 +165,154 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        // Epilogue: TMEM lane group g = warp % 4 (the lanes a warp may read), one row per thread.
-        const int g = warp & 3;
+        const int et = threadIdx.x - 64;        // 0..255
+        const int g = warp & 3;                 // TMEM lane group this warp may read
+        const int half = (warp - 2) >> 2;       // which 128 columns of the tile
         const int row_in_tile = g * 32 + lane;
+        const int s = e.s;
+        const bool fast = s >= 0 && s <= 62;
+        const int64_t hround = (fast && s > 0) ? (1LL << (s - 1)) : 0;
         int i = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
-            int mt = t % MT, nt = t / MT;
-            int acc = i & 1;
-            uint32_t aphase = (i >> 1) & 1;
-            bool ready = mbar_wait(&bars->tfull[acc], aphase, err, 4);
+            const int mt = t % MT, nt = t / MT;
+            const int acc = i & 1;
+            const uint32_t aphase = (i >> 1) & 1;
+            const int col0 = nt * BN;
+            // Stage this tile's column parameters (double-buffered by the accumulator parity).
+            {
+                int n = col0 + et;
+                int32_t m = 0;
+                int64_t c = 0;
+                if (n < e.N) {
+                    m = e.m[n];
+                    int64_t b = (MODE == EPI_LOGITS || MODE == EPI_RAW) ? 0 : (int64_t)e.b[n];
+                    c = fast ? b * (int64_t)m + hround : b;
+                }
+                s_m[acc * BN + et] = m;
+                s_c[acc * BN + et] = c;
+            }
+            named_bar(1, EPI_THREADS);
+            // On a timeout the error word is set and every later wait returns at once; the warps keep
+            // taking part in the named barriers, so no thread can wait on a barrier forever.
+            mbar_wait(&bars->tfull[acc], aphase, err, 4);
             __syncwarp();
-            if (!__all_sync(0xffffffffu, ready)) break;
             tc_fence_after();
             const int row = mt * BM + row_in_tile;
+            const bool row_ok = row < e.R;
             const uint32_t taddr = tmem_base + ((uint32_t)(g * 32) << 16) + (uint32_t)(acc * BN);
-            const int col0 = nt * BN;
-            if (mode != EPI_LOGITS) {
-#pragma unroll 1
-                for (int c = 0; c < BN; c += 16) {
-                    uint32_t v[16];
-                    __syncwarp();
-                    tmem_ld16(taddr + c, v);
-                    tmem_ld_wait();
-                    if (col0 + c < e.N) epi_chunk(mode, e, row, col0 + c, v);
-                }
-            } else {
-                // Pass 1: the max of this row over the tile; pass 2: d16 = min(tmax - l, last).
+            const int32_t* pm = s_m + acc * BN;
+            const int64_t* pc = s_c + acc * BN;
+            if (MODE == EPI_LOGITS) {
                 int64_t tm = INT64_MIN;
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 16) {
-                    uint32_t v[16];
+                for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+                    uint32_t v[32];
                     __syncwarp();
-                    tmem_ld16(taddr + c, v);
+                    tmem_ld32(taddr + c0, v);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int q = 0; q < 16; q++) {
-                        int n = col0 + c + q;
-                        if (n < e.N) {
-                            int64_t l = logit_of(e, n, v[q]);
+                    for (int q = 0; q < 32; q++) {
+                        if (col0 + c0 + q < e.N) {
+                            int64_t l = clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), -SCORE_LIMIT,
+                                                SCORE_LIMIT);
                             tm = l > tm ? l : tm;
                         }
                     }
                 }
+                s_tm[(acc * 2 + half) * BM + row_in_tile] = tm;
+                named_bar(1, EPI_THREADS);
+                int64_t other = s_tm[(acc * 2 + (half ^ 1)) * BM + row_in_tile];
+                tm = other > tm ? other : tm;
 #pragma unroll 1
-                for (int c = 0; c < BN; c += 16) {
-                    uint32_t v[16];
+                for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+                    uint32_t v[32];
                     __syncwarp();
-                    tmem_ld16(taddr + c, v);
+                    tmem_ld32(taddr + c0, v);
                     tmem_ld_wait();
-                    if (row < e.R && col0 + c < e.N) {
-                        uint32_t packed[8];
+                    if (row_ok && col0 + c0 < e.N) {
+                        uint32_t packed[16];
 #pragma unroll
-                        for (int q = 0; q < 16; q += 2) {
-                            int n0 = col0 + c + q, n1 = n0 + 1;
+                        for (int q = 0; q < 32; q += 2) {
                             uint32_t a0 = 0, a1 = 0;
-                            if (n0 < e.N) {
-                                int64_t dd = tm - logit_of(e, n0, v[q]);
+                            if (col0 + c0 + q < e.N) {
+                                int64_t l = clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast),
+                                                    -SCORE_LIMIT, SCORE_LIMIT);
+                                int64_t dd = tm - l;
                                 a0 = (uint32_t)(dd < e.last ? dd : e.last);
                             }
-                            if (n1 < e.N) {
-                                int64_t dd = tm - logit_of(e, n1, v[q + 1]);
+                            if (col0 + c0 + q + 1 < e.N) {
+                                int64_t l = clamp64(rescale_fast(v[q + 1], pm[c0 + q + 1], pc[c0 + q + 1], s, fast),
+                                                    -SCORE_LIMIT, SCORE_LIMIT);
+                                int64_t dd = tm - l;
                                 a1 = (uint32_t)(dd < e.last ? dd : e.last);
                             }
                             packed[q >> 1] = a0 | (a1 << 16);
                         }
-                        uint16_t* dst = e.d16 + (size_t)row * e.ldd + col0 + c;
-                        // d16 rows are padded to a multiple of 256 columns, so 16 entries fit.
-                        reinterpret_cast<uint4*>(dst)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        reinterpret_cast<uint4*>(dst)[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                        uint4* dst = reinterpret_cast<uint4*>(e.d16 + (size_t)row * e.ldd + col0 + c0);
+#pragma unroll
+                        for (int q = 0; q < 4; q++)
+                            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
                     }
                 }
-                if (row < e.R) e.tmax[(size_t)row * e.ldt + nt] = tm;
+                if (row_ok && half == 0) e.tmax[(size_t)row * e.ldt + nt] = tm;
+            } else {
+#pragma unroll 1
+                for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+                    uint32_t v[32];
+                    __syncwarp();
+                    tmem_ld32(taddr + c0, v);
+                    tmem_ld_wait();
+                    const int colb = col0 + c0;
+                    if (!row_ok || colb >= e.N) continue;
+                    const bool full = colb + 32 <= e.N;
+                    if (MODE == EPI_ACT || MODE == EPI_GELU) {
+                        uint32_t packed[8];
+#pragma unroll
+                        for (int q = 0; q < 8; q++) packed[q] = 0;
+#pragma unroll
+                        for (int q = 0; q < 32; q++) {
+                            int64_t y = rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast);
+                            int8_t o;
+                            if (MODE == EPI_ACT) {
+                                o = (int8_t)clamp64(y, -127, 127);
+                            } else {
+                                int64_t in = clamp64(y, -e.gelu_off, e.gelu_off - 1);
+                                o = s_gelu[in + e.gelu_off];
+                            }
+                            packed[q >> 2] |= (uint32_t)(uint8_t)o << (8 * (q & 3));
+                        }
+                        int8_t* dst = e.out8 + (size_t)row * e.ldo + colb;
+                        if (full && (e.ldo & 15) == 0) {
+                            reinterpret_cast<uint4*>(dst)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                            reinterpret_cast<uint4*>(dst)[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 32; q++)
+                                if (colb + q < e.N) dst[q] = (int8_t)(packed[q >> 2] >> (8 * (q & 3)));
+                        }
+                    } else if (MODE == EPI_DELTA) {
+                        int32_t o[32];
+#pragma unroll
+                        for (int q = 0; q < 32; q++)
+                            o[q] = (int32_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), INT32_MIN,
+                                                    INT32_MAX);
+                        int32_t* dst = e.out32 + (size_t)row * e.ldo + colb;
+                        if (full && (e.ldo & 3) == 0) {
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                reinterpret_cast<int4*>(dst)[q] = make_int4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 32; q++)
+                                if (colb + q < e.N) dst[q] = o[q];
+                        }
+                    } else if (MODE == EPI_RAW) {
+                        int32_t* dst = e.out32 + (size_t)row * e.ldo + colb;
+#pragma unroll
+                        for (int q = 0; q < 32; q++)
+                            if (colb + q < e.N) dst[q] = (int32_t)v[q];
+                    }
+                }
             }
             tc_fence_before();
             mbar_arrive(&bars->tempty[acc]);
@@ -282,10 +326,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+template <int MODE>
+void launch_mode(const void* tmA, const void* tmB, int MT, int NT, int KB, const EpiArgs& e, int grid, int* err,
+                 cudaStream_t st) {
+    k_gemm_tc<MODE><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(tmA),
+                                                           *reinterpret_cast<const CUtensorMap*>(tmB), MT, NT, KB, e,
+                                                           err);
+}
+
+template <int MODE>
+cudaError_t configure_mode() {
+    return cudaFuncSetAttribute(k_gemm_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<MODE>::SMEM);
+}
+
 }  // namespace
 
 cudaError_t configure_tc_kernels() {
-    return cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    cudaError_t e;
+    if ((e = configure_mode<EPI_ACT>()) != cudaSuccess) return e;
+    if ((e = configure_mode<EPI_GELU>()) != cudaSuccess) return e;
+    if ((e = configure_mode<EPI_LOGITS>()) != cudaSuccess) return e;
+    if ((e = configure_mode<EPI_RAW>()) != cudaSuccess) return e;
+    return configure_mode<EPI_DELTA>();
 }
 
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, int Kp, const EpiArgs& e,
@@ -294,9 +356,14 @@ void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, i
     int MT = (R + BM - 1) / BM, NT = Np / BN, KB = Kp / BK;
     int tiles = MT * NT;
     int grid = tiles < num_sms ? tiles : num_sms;
-    k_gemm_tc<<<grid, THREADS, SMEM_BYTES, st>>>(*reinterpret_cast<const CUtensorMap*>(tmA),
-                                                 *reinterpret_cast<const CUtensorMap*>(tmB), mode, MT, NT, KB, e,
-                                                 err);
+    switch (mode) {
+        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        default: break;
+    }
 }
 
 }  // namespace hs

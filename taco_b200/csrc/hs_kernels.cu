@@ -118,6 +118,85 @@ __global__ void k_layernorm(const int32_t* x, int R, int d, LnDev ln, int ln_k, 
     }
 }
 
+// ---- residual add + LayerNorm, one warp per row ----
+//
+// x = clamp(x + delta, -R, R) (the residual step of reference.rs:224-231; the delta of the GEMM is
+// already clamped to i32, which gives the same value because |x| <= R), then the LayerNorm of
+// layernorm.rs:201-256 with t * m = (x - mean) * g * (inv * m): the per-row factor inv * m is one
+// 128-bit value, so an output costs one 64 x 128-bit product, a shift and a clamp. The row stays in
+// registers (RPL values per lane).
+template <int RPL>
+__global__ void __launch_bounds__(256) k_resid_ln(int32_t* x, const int32_t* delta, int R, int d, LnDev ln, int ln_k,
+                                                  int ln_j, uint64_t eps, int8_t* out, int ldo) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= R) return;
+    int32_t* xr = x + (size_t)r * d;
+    int32_t v[RPL];
+    int64_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < RPL; i++) {
+        int j = lane + 32 * i;
+        int32_t xv = 0;
+        if (j < d) {
+            xv = xr[j];
+            if (delta) {
+                xv = (int32_t)clamp64((int64_t)xv + delta[(size_t)r * d + j], -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+                xr[j] = xv;
+            }
+        }
+        v[i] = xv;
+        sum += xv;
+    }
+    sum = warp_sums64(sum);
+    const int64_t mean = floor_div64(sum, d);
+    uint64_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < RPL; i++) {
+        int j = lane + 32 * i;
+        if (j < d) {
+            int64_t c = (int64_t)v[i] - mean;
+            uint64_t a = c < 0 ? (uint64_t)(-c) : (uint64_t)c;
+            uint64_t sq = a * a;  // |c| < 2^32, so c^2 < 2^64
+            lo += sq;
+            hi += lo < sq ? 1 : 0;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
+        uint64_t hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
+        lo += lo2;
+        hi += hi2 + (lo < lo2 ? 1 : 0);
+    }
+    const u128 sum_sq = ((u128)hi << 64) | lo;
+    const u128 var = sum_sq / (u128)d;
+    u128 root = isqrt128((var << (2 * ln_j)) + (u128)eps);
+    if (root < 1) root = 1;
+    const i128 inv = (i128)(((u128)1 << ln_k) / root);
+    const i128 u = inv * (i128)ln.m;  // |u| < 2^80
+    const int s = ln.s;
+#pragma unroll
+    for (int i = 0; i < RPL; i++) {
+        int j = lane + 32 * i;
+        if (j >= d) continue;
+        int64_t cg = ((int64_t)v[i] - mean) * (int64_t)ln.g[j];  // |cg| < 2^47
+        i128 p = (i128)cg * u;                                     // t * m, |p| < 2^126
+        i128 y;
+        if (ln.beta_frac == 0) {
+            y = shift_round128(p, s, 126) + (i128)ln.b[j];
+        } else {
+            i128 cb = (i128)ln.b[j] << (s - ln.beta_frac);
+            y = shift_round128((i128)((u128)p + (u128)cb), s, 126);
+        }
+        out[(size_t)r * ldo + j] = (int8_t)clamp128(y, -127, 127);
+    }
+}
+
+__global__ void k_resid_add(int32_t* x, const int32_t* delta, size_t n) {
+    size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (i < n) x[i] = (int32_t)clamp64((int64_t)x[i] + delta[i], -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+}
+
 // ---- the GEMM epilogue for one element (shared by the dp4a GEMM) ----
 
 __device__ __forceinline__ void epi_store(int mode, const EpiArgs& e, int r, int n, int32_t acc) {
@@ -135,6 +214,8 @@ __device__ __forceinline__ void epi_store(int mode, const EpiArgs& e, int r, int
     } else if (mode == EPI_RESID) {
         int32_t* xp = &e.x[(size_t)r * e.ldx + n];
         *xp = (int32_t)clamp64((int64_t)*xp + y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+    } else if (mode == EPI_DELTA) {
+        e.out32[(size_t)r * e.ldo + n] = (int32_t)clamp64(y, INT32_MIN, INT32_MAX);
     }
 }
 
@@ -207,7 +288,9 @@ __global__ void __launch_bounds__(256) k_gemm_simple(int mode, const int8_t* A, 
     }
 }
 
-// ---- the KV cache: keys and values of each row at (slot, layer, head, pos) ----
+// ---- the KV cache: keys [slot, layer, head, pos, hd]; values transposed [slot, layer, head, hd, pos]
+// (the values layout of crates/hardshell/src/gpt2/attention.rs:48, so p.v is a dot product along
+// the positions of one channel) ----
 
 __global__ void k_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
                            int layer, int n_ctx, int8_t* kc, int8_t* vc) {
@@ -216,9 +299,9 @@ __global__ void k_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ld
     uint32_t slot = rows[r].slot, pos = rows[r].pos;
     for (int j = threadIdx.x; j < d; j += blockDim.x) {
         int h = j / hd, c = j - h * hd;
-        size_t at = ((((size_t)slot * L + layer) * H + h) * n_ctx + pos) * hd + c;
-        kc[at] = qkv[(size_t)r * ldq + d + j];
-        vc[at] = qkv[(size_t)r * ldq + 2 * d + j];
+        size_t head = ((size_t)slot * L + layer) * H + h;
+        kc[(head * n_ctx + pos) * hd + c] = qkv[(size_t)r * ldq + d + j];
+        vc[(head * hd + c) * n_ctx + pos] = qkv[(size_t)r * ldq + 2 * d + j];
     }
 }
 
@@ -226,17 +309,29 @@ __global__ void k_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ld
 
 constexpr int ATT_THREADS = 128;
 
+// attention.rs:36 digits: p = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3 with each d in -128..127.
+__device__ __forceinline__ void balanced_digits(int64_t p, int8_t* d) {
+    int64_t rest = p;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        int64_t digit = ((rest + 128) & 255) - 128;
+        d[k] = (int8_t)digit;
+        rest = (rest - digit) >> 8;
+    }
+}
+
+// The general kernel (any head width): scalar loops. The fast kernel below takes hd % 16 == 0.
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const RowInfo* rows, int R, const int8_t* qkv, int ldq,
                                                            const int8_t* kc, const int8_t* vc, int L, int layer,
                                                            int H, int hd, int n_ctx, int d, int32_t sm, int ss,
                                                            int32_t om, int os, const int32_t* table, int tlen,
-                                                           int P, int8_t* att, int lda) {
+                                                           int P, int8_t* att, int lda, const int* rowlist) {
     extern __shared__ int64_t s_sc[];  // n_ctx scores, then weights, then p
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
     __shared__ int8_t q[1024];
     __shared__ int64_t part[ATT_THREADS];
-    int h = blockIdx.x, r = blockIdx.y;
+    int h = blockIdx.x, r = rowlist ? rowlist[blockIdx.y] : (int)blockIdx.y;
     if (r >= R) return;
     uint32_t slot = rows[r].slot;
     int n = (int)rows[r].pos + 1;
@@ -244,7 +339,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const RowInfo* rows, 
     __syncthreads();
     size_t head = (((size_t)slot * L + layer) * H + h) * n_ctx * (size_t)hd;
     const int8_t* K = kc + head;
-    const int8_t* Vv = vc + head;
+    const int8_t* Vt = vc + head;
     int64_t mx = INT64_MIN;
     for (int j = threadIdx.x; j < n; j += ATT_THREADS) {
         const int8_t* kr = K + (size_t)j * hd;
@@ -281,7 +376,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const RowInfo* rows, 
         int g = hd <= ATT_THREADS ? threadIdx.x / hd : 0;
         int64_t acc = 0;
         if (c < hd && g < groups)
-            for (int j = g; j < n; j += groups) acc += s_sc[j] * (int64_t)Vv[(size_t)j * hd + c];
+            for (int j = g; j < n; j += groups) acc += s_sc[j] * (int64_t)Vt[(size_t)c * n_ctx + j];
         part[threadIdx.x] = acc;
         __syncthreads();
         if (threadIdx.x < (hd <= ATT_THREADS ? hd : ATT_THREADS) && c < hd) {
@@ -294,6 +389,107 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const RowInfo* rows, 
             att[(size_t)r * lda + h * hd + c] = (int8_t)clamp128(rescale128(t, om, os), -127, 127);
         }
         __syncthreads();
+    }
+}
+
+// The fast kernel for a head width HD (a multiple of 16) and n_ctx % 4 == 0: q.k with dp4a over
+// 16-byte key loads, and p.v as four dp4a dot products per channel over the balanced base-256
+// digits of p (attention.rs:36), four positions per instruction along the transposed values.
+// Exact: each digit dot has at most n_ctx terms of magnitude <= 2^14.
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS) k_attention_vec(const RowInfo* rows, int R, const int8_t* qkv,
+                                                               int ldq, const int8_t* kc, const int8_t* vc, int L,
+                                                               int layer, int H, int n_ctx, int32_t sm, int ss,
+                                                               int32_t om, int os, const int32_t* table, int tlen,
+                                                               int P, int8_t* att, int lda, const int* rowlist) {
+    extern __shared__ __align__(16) uint8_t smem_att[];
+    int64_t* s_sc = reinterpret_cast<int64_t*>(smem_att);             // n_ctx: scores, then e
+    int4* s_dig = reinterpret_cast<int4*>(smem_att + 8 * (size_t)n_ctx);  // n_ctx / 4 quads x 4 planes
+    __shared__ int64_t red[32];
+    __shared__ uint64_t redu[32];
+    const int h = blockIdx.x, r = rowlist ? rowlist[blockIdx.y] : (int)blockIdx.y;
+    if (r >= R) return;
+    const uint32_t slot = rows[r].slot;
+    const int n = (int)rows[r].pos + 1;
+    const int nq = (n + 3) >> 2;
+    int32_t qw[HD / 4];
+    {
+        const int4* qp = reinterpret_cast<const int4*>(qkv + (size_t)r * ldq + h * HD);
+#pragma unroll
+        for (int i = 0; i < HD / 16; i++) {
+            int4 v = qp[i];
+            qw[4 * i] = v.x;
+            qw[4 * i + 1] = v.y;
+            qw[4 * i + 2] = v.z;
+            qw[4 * i + 3] = v.w;
+        }
+    }
+    const size_t head = ((size_t)slot * L + layer) * H + h;
+    const int4* K = reinterpret_cast<const int4*>(kc + head * n_ctx * HD);
+    const int8_t* Vt = vc + head * HD * n_ctx;
+    int64_t mx = INT64_MIN;
+    for (int j = threadIdx.x; j < n; j += ATT_THREADS) {
+        int32_t dot = 0;
+#pragma unroll
+        for (int i = 0; i < HD / 16; i++) {
+            int4 k4 = K[(size_t)j * (HD / 16) + i];
+            dot = __dp4a(qw[4 * i], k4.x, dot);
+            dot = __dp4a(qw[4 * i + 1], k4.y, dot);
+            dot = __dp4a(qw[4 * i + 2], k4.z, dot);
+            dot = __dp4a(qw[4 * i + 3], k4.w, dot);
+        }
+        int64_t sc = clamp64(rescale64(dot, sm, ss), -SCORE_LIMIT, SCORE_LIMIT);
+        s_sc[j] = sc;
+        mx = sc > mx ? sc : mx;
+    }
+    mx = block_max64(mx, red);
+    uint64_t sum = 0;
+    const int64_t last = tlen - 1;
+    for (int j = threadIdx.x; j < n; j += ATT_THREADS) {
+        int64_t dd = mx - s_sc[j];
+        int64_t e = table[dd < last ? dd : last];
+        s_sc[j] = e;
+        sum += (uint64_t)e;
+    }
+    sum = block_sum64(sum, redu);
+    if (sum == 0) sum = 1;
+    const uint64_t rec = (~0ULL) / sum;
+    int8_t* dig = reinterpret_cast<int8_t*>(s_dig);
+    for (int j = threadIdx.x; j < 4 * nq; j += ATT_THREADS) {
+        int8_t dk[4] = {0, 0, 0, 0};
+        if (j < n) {
+            uint64_t x = (uint64_t)s_sc[j] << P;
+            uint64_t qv = __umul64hi(x, rec);
+            while ((qv + 1) * sum <= x) qv++;
+            balanced_digits((int64_t)qv, dk);
+        }
+        int qd = j >> 2, i = j & 3;
+#pragma unroll
+        for (int k = 0; k < 4; k++) dig[16 * (size_t)qd + 4 * k + i] = dk[k];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int c = warp; c < HD; c += ATT_THREADS / 32) {
+        const int32_t* vrow = reinterpret_cast<const int32_t*>(Vt + (size_t)c * n_ctx);
+        int32_t a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+        for (int qd = lane; qd < nq; qd += 32) {
+            int32_t v = vrow[qd];
+            int4 dg = s_dig[qd];
+            a0 = __dp4a(dg.x, v, a0);
+            a1 = __dp4a(dg.y, v, a1);
+            a2 = __dp4a(dg.z, v, a2);
+            a3 = __dp4a(dg.w, v, a3);
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+            a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+            a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+            a3 += __shfl_xor_sync(0xffffffffu, a3, o);
+        }
+        if (lane == 0) {
+            int64_t acc = ((((int64_t)a3 * 256 + a2) * 256 + a1) * 256) + a0;
+            att[(size_t)r * lda + h * HD + c] = (int8_t)clamp128(rescale128(acc, om, os), -127, 127);
+        }
     }
 }
 
@@ -432,6 +628,11 @@ __global__ void k_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int
 cudaError_t configure_core_kernels() {
     cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_ATTN_CTX * 8);
     if (e != cudaSuccess) return e;
+    const int vsmem = 8 * MAX_ATTN_CTX + 16 * (MAX_ATTN_CTX / 4 + 1);
+    e = cudaFuncSetAttribute(k_attention_vec<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsmem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_attention_vec<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsmem);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_coder, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
 }
 
@@ -448,6 +649,24 @@ void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k,
     k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo);
 }
 
+void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, const LnDev& ln, int ln_k, int ln_j,
+                            uint64_t eps, int8_t* out, int ldo, cudaStream_t st) {
+    if (R <= 0) return;
+    int blocks = (R + 7) / 8;
+    if (d <= 32 * 24) {
+        k_resid_ln<24><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo);
+    } else if (d <= 32 * 64) {
+        k_resid_ln<64><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo);
+    } else {
+        // Wide rows: the residual step as its own pass, then the block-per-row LayerNorm.
+        if (delta) {
+            size_t n = (size_t)R * d;
+            k_resid_add<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, delta, n);
+        }
+        k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo);
+    }
+}
+
 void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearDev& W, const EpiArgs& e,
                         cudaStream_t st) {
     if (R <= 0) return;
@@ -461,14 +680,28 @@ void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int
     k_kv_store<<<R, 256, 0, st>>>(rows, R, qkv, ldq, d, H, hd, L, layer, n_ctx, kc, vc);
 }
 
-void launch_attention(const RowInfo* rows, int R, const int8_t* qkv, int ldq, const int8_t* kc, const int8_t* vc,
-                      int L, int layer, int H, int hd, int n_ctx, int d, int32_t sm, int ss, int32_t om, int os,
-                      const int32_t* table, int tlen, int P, int8_t* att, int lda, cudaStream_t st) {
-    if (R <= 0) return;
+void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, const int8_t* qkv, int ldq,
+                      const int8_t* kc, const int8_t* vc, int L, int layer, int H, int hd, int n_ctx, int d,
+                      int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att,
+                      int lda, cudaStream_t st) {
+    if (R <= 0 || n <= 0) return;
+    dim3 grid(H, n);
+    // The vector kernel needs 16-byte aligned q rows and 4-byte aligned value rows.
+    bool vec_ok = (n_ctx % 4) == 0 && (ldq % 16) == 0;
+    size_t vsmem = 8 * (size_t)n_ctx + 16 * (size_t)(n_ctx / 4 + 1);
+    if (vec_ok && hd == 64) {
+        k_attention_vec<64><<<grid, ATT_THREADS, vsmem, st>>>(rows, R, qkv, ldq, kc, vc, L, layer, H, n_ctx, sm, ss,
+                                                               om, os, table, tlen, P, att, lda, rowlist);
+        return;
+    }
+    if (vec_ok && hd == 16) {
+        k_attention_vec<16><<<grid, ATT_THREADS, vsmem, st>>>(rows, R, qkv, ldq, kc, vc, L, layer, H, n_ctx, sm, ss,
+                                                               om, os, table, tlen, P, att, lda, rowlist);
+        return;
+    }
     size_t smem = (size_t)n_ctx * sizeof(int64_t);
-    dim3 grid(H, R);
     k_attention<<<grid, ATT_THREADS, smem, st>>>(rows, R, qkv, ldq, kc, vc, L, layer, H, hd, n_ctx, d, sm, ss, om,
-                                                  os, table, tlen, P, att, lda);
+                                                  os, table, tlen, P, att, lda, rowlist);
 }
 
 void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,

@@ -28,6 +28,10 @@ void launch_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const 
 void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k, int ln_j, uint64_t eps,
                       int8_t* out, int ldo, cudaStream_t st);
 
+// x = clamp(x + delta, -R, R) (delta may be null), then out = LayerNorm(x) (i8).
+void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, const LnDev& ln, int ln_k, int ln_j,
+                            uint64_t eps, int8_t* out, int ldo, cudaStream_t st);
+
 // out = epilogue(W . A^T) on CUDA cores (dp4a); the reference kernel of the tensor-core GEMM and
 // the path for passes of a few rows.
 void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearDev& W, const EpiArgs& e,
@@ -41,9 +45,21 @@ void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, i
 void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
                      int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st);
 
-void launch_attention(const RowInfo* rows, int R, const int8_t* qkv, int ldq, const int8_t* kc, const int8_t* vc,
-                      int L, int layer, int H, int hd, int n_ctx, int d, int32_t sm, int ss, int32_t om, int os,
-                      const int32_t* table, int tlen, int P, int8_t* att, int lda, cudaStream_t st);
+// Attention of the rows `rowlist[0..n)` (all R rows when rowlist is null) on CUDA cores: the
+// decode path and the rows that are not in a prefill group.
+void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, const int8_t* qkv, int ldq,
+                      const int8_t* kc, const int8_t* vc, int L, int layer, int H, int hd, int n_ctx, int d,
+                      int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att,
+                      int lda, cudaStream_t st);
+
+// Prefill attention of whole groups on the tensor cores (hs_attn_tc.cu). tmQ covers the qkv
+// buffer (box 64 x 128, 64-byte swizzle), tmK the keys cache (64 x 128, 64-byte swizzle), tmV the
+// transposed values cache (128 x 64, 128-byte swizzle).
+cudaError_t configure_attn_tc();
+bool attention_tc_supported(int hd, int n_ctx, int tlen);
+void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, const AttnGroup* groups, int n_groups,
+                         int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,
+                         const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st);
 
 // The coder op: from the d16/tmax output of the logits GEMM, the interval of each row's query
 // in the table of taco_coder::FreqTable::from_weights(weights, bits). out: 3 u64 per row.

@@ -53,6 +53,16 @@ bool use_tc_default() {
     return !(v && strcmp(v, "simple") == 0);
 }
 
+// The prefill attention path: tensor cores for groups of rows (default), or CUDA cores for every
+// row (HS_ATTN=vec, for tests).
+bool use_attn_tc_default() {
+    const char* v = getenv("HS_ATTN");
+    return !(v && strcmp(v, "vec") == 0);
+}
+
+// The smallest group of consecutive rows of one slot that takes the tensor-core attention.
+constexpr int ATTN_TC_MIN_ROWS = 16;
+
 }  // namespace
 
 struct hs_dev {
@@ -70,17 +80,20 @@ int set_device(hs_dev* d) {
     return HS_OK;
 }
 
-// A 2D int8 tensor map over [rows, cols] (cols contiguous): box {128, box_rows}, 128-byte swizzle.
-int make_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// A 2D int8 tensor map over [rows, cols] (cols contiguous): box {box_cols, box_rows} with the
+// 128-byte swizzle (box_cols = 128) or the 64-byte swizzle (box_cols = 64).
+int make_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+              uint32_t box_cols = TILE_K) {
     cuuint64_t gdim[2] = {cols, rows};
     cuuint64_t gstride[1] = {cols};
-    cuuint32_t box[2] = {(cuuint32_t)TILE_K, box_rows};
+    cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     if (((uintptr_t)base & 15) != 0 || (cols & 15) != 0)
         return fail(HS_UNSUPPORTED, "a TMA tensor needs 16-byte aligned rows");
+    CUtensorMapSwizzle sw = box_cols == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUresult r = dev->encode(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(HS_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     return HS_OK;
 }
@@ -119,6 +132,7 @@ struct hs_model {
     uint8_t hash[32] = {0};
     uint64_t weight_bytes = 0;
     bool use_tc = true;
+    bool attn_tc = false;
     int8_t* wte = nullptr;
     int32_t* em = nullptr;
     int es = 0;
@@ -157,27 +171,89 @@ struct hs_batch {
     int8_t* qkv = nullptr;
     int8_t* att = nullptr;
     int8_t* g = nullptr;
+    int32_t* dbuf = nullptr;  // the residual delta of the last proj/mlp GEMM
     uint16_t* d16 = nullptr;
     int64_t* tmax = nullptr;
     uint64_t* intervals = nullptr;
     uint64_t* weights = nullptr;
     RowInfo* h_rows = nullptr;       // pinned
     uint64_t* h_intervals = nullptr;  // pinned
+    AttnGroup* d_groups = nullptr;   // the prefill groups of the pass
+    int* d_rowlist = nullptr;        // the other rows of the pass
+    AttnGroup* h_groups = nullptr;   // pinned
+    int* h_rowlist = nullptr;        // pinned
+    int n_groups = 0, n_rowlist = 0;
     uint64_t bytes = 0;
+    // Per-op device time (CUDA events on the batch stream) when profiling is on.
+    bool profiling = false;
+    std::vector<cudaEvent_t> ev_pool;
+    std::vector<std::pair<int, int>> ev_pending;  // (op, index of the begin event; end = +1)
+    std::vector<double> op_ms;
+    std::vector<uint64_t> op_launches, op_flops;
     alignas(128) CUtensorMap tm_a;
     alignas(128) CUtensorMap tm_att;
     alignas(128) CUtensorMap tm_g;
+    alignas(128) CUtensorMap tm_q;   // qkv rows, 64-byte boxes (attention Q)
+    alignas(128) CUtensorMap tm_k;   // the keys cache
+    alignas(128) CUtensorMap tm_v;   // the transposed values cache
 
     ~hs_batch() {
         if (model) cudaSetDevice(model->dev->ordinal);
+        for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         if (stream) cudaStreamDestroy(stream);
         for (void* p : owned) cudaFree(p);
         if (h_rows) cudaFreeHost(h_rows);
         if (h_intervals) cudaFreeHost(h_intervals);
+        if (h_groups) cudaFreeHost(h_groups);
+        if (h_rowlist) cudaFreeHost(h_rowlist);
     }
 };
 
 namespace {
+
+// The ops of one pass, for the profile (the reference's CudaBatch::profile op names).
+// OP_PASS spans a whole pass (first kernel to the coder, gaps included); it is not a launch.
+enum Op { OP_EMBED, OP_LN, OP_GEMM_QKV, OP_KV, OP_ATTN, OP_GEMM_PROJ, OP_GEMM_FC, OP_GEMM_MLP, OP_GEMM_LOGITS,
+          OP_CODER, OP_PASS, OP_COUNT };
+const char* OP_NAMES[OP_COUNT] = {"embed", "layernorm", "gemm_qkv", "kv_store", "attention", "gemm_proj",
+                                  "gemm_fc", "gemm_mlp", "gemm_logits", "coder", "pass"};
+
+// Kernel launches of this process (the bench reports the launches of its timed region).
+unsigned long long g_launches = 0;
+
+struct ProfScope {
+    hs_batch* b;
+    int op;
+    int idx = -1;
+    ProfScope(hs_batch* b_, int op_, uint64_t flops) : b(b_), op(op_) {
+        if (op != OP_PASS) g_launches++;
+        if (!b->profiling) return;
+        b->op_launches[op]++;
+        b->op_flops[op] += flops;
+        size_t need = 2 * (b->ev_pending.size() + 1);
+        while (b->ev_pool.size() < need) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            b->ev_pool.push_back(e);
+        }
+        idx = (int)(2 * b->ev_pending.size());
+        b->ev_pending.push_back({op, idx});
+        cudaEventRecord(b->ev_pool[idx], b->stream);
+    }
+    ~ProfScope() {
+        if (idx >= 0) cudaEventRecord(b->ev_pool[idx + 1], b->stream);
+    }
+};
+
+// After a synchronised pass: add the elapsed time of every recorded op.
+void prof_collect(hs_batch* b) {
+    for (auto& p : b->ev_pending) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, b->ev_pool[p.second], b->ev_pool[p.second + 1]) == cudaSuccess)
+            b->op_ms[p.first] += ms;
+    }
+    b->ev_pending.clear();
+}
 
 int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D) {
     int N = L.rows, K = L.cols;
@@ -213,8 +289,16 @@ int forward(hs_batch* b, int R) {
     hs_model* m = b->model;
     const ModelConsts& c = m->c;
     cudaStream_t st = b->stream;
-    launch_embed(b->d_rows, R, m->wte, c.Dp, m->em, m->es, m->wpe, m->pm, m->ps, c.d, b->x, st);
-    auto gemm = [&](int mode, const int8_t* A, int lda, const CUtensorMap* tmA, const DevLinear& W, EpiArgs e) {
+    {
+        ProfScope p(b, OP_EMBED, 0);
+        launch_embed(b->d_rows, R, m->wte, c.Dp, m->em, m->es, m->wpe, m->pm, m->ps, c.d, b->x, st);
+    }
+    // The attention work of this pass: 2 * 2 * hd * (pos + 1) per row and head (q.k and p.v).
+    uint64_t attn_ops = 0;
+    for (int r = 0; r < R; r++) attn_ops += 4ULL * c.d * (b->h_rows[r].pos + 1);
+    auto gemm = [&](int op, int mode, const int8_t* A, int lda, const CUtensorMap* tmA, const DevLinear& W,
+                    EpiArgs e) {
+        ProfScope p(b, op, 2ULL * R * W.ld.N * W.ld.K);
         if (m->use_tc)
             launch_gemm_tc(mode, tmA, &W.tm, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms, m->dev->d_err, st);
         else
@@ -226,7 +310,12 @@ int forward(hs_batch* b, int R) {
         const DevLinear& proj = *m->lins[4 * l + 1];
         const DevLinear& fc = *m->lins[4 * l + 2];
         const DevLinear& mlp = *m->lins[4 * l + 3];
-        launch_layernorm(b->x, R, c.d, Ld.ln1, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+        {
+            // The residual of the previous layer's MLP joins x here (none before layer 0).
+            ProfScope p(b, OP_LN, 0);
+            launch_resid_layernorm(b->x, l == 0 ? nullptr : b->dbuf, R, c.d, Ld.ln1, c.ln_k, c.ln_j, c.ln_eps, b->a,
+                                   c.Dp, st);
+        }
         EpiArgs e{};
         e.R = R;
         e.N = 3 * c.d;
@@ -235,20 +324,33 @@ int forward(hs_batch* b, int R) {
         e.s = qkv.ld.s;
         e.out8 = b->qkv;
         e.ldo = c.QKVp;
-        gemm(EPI_ACT, b->a, c.Dp, &b->tm_a, qkv, e);
-        launch_kv_store(b->d_rows, R, b->qkv, c.QKVp, c.d, c.H, c.hd, c.L, l, c.n_ctx, b->kc, b->vc, st);
-        launch_attention(b->d_rows, R, b->qkv, c.QKVp, b->kc, b->vc, c.L, l, c.H, c.hd, c.n_ctx, c.d, Ld.score_m,
-                         Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p, b->att, c.Dp, st);
+        gemm(OP_GEMM_QKV, EPI_ACT, b->a, c.Dp, &b->tm_a, qkv, e);
+        {
+            ProfScope p(b, OP_KV, 0);
+            launch_kv_store(b->d_rows, R, b->qkv, c.QKVp, c.d, c.H, c.hd, c.L, l, c.n_ctx, b->kc, b->vc, st);
+        }
+        {
+            ProfScope p(b, OP_ATTN, attn_ops);
+            launch_attention_tc(&b->tm_q, &b->tm_k, &b->tm_v, b->d_groups, b->n_groups, c.L, l, c.H, c.n_ctx,
+                                Ld.score_m, Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p,
+                                b->att, c.Dp, m->dev->d_err, st);
+            launch_attention(b->d_rows, R, b->n_groups ? b->d_rowlist : nullptr, b->n_groups ? b->n_rowlist : R,
+                             b->qkv, c.QKVp, b->kc, b->vc, c.L, l, c.H, c.hd, c.n_ctx, c.d, Ld.score_m, Ld.score_s,
+                             Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p, b->att, c.Dp, st);
+        }
         e = EpiArgs{};
         e.R = R;
         e.N = c.d;
         e.b = proj.ld.b;
         e.m = proj.ld.m;
         e.s = proj.ld.s;
-        e.x = b->x;
-        e.ldx = c.d;
-        gemm(EPI_RESID, b->att, c.Dp, &b->tm_att, proj, e);
-        launch_layernorm(b->x, R, c.d, Ld.ln2, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+        e.out32 = b->dbuf;
+        e.ldo = c.d;
+        gemm(OP_GEMM_PROJ, EPI_DELTA, b->att, c.Dp, &b->tm_att, proj, e);
+        {
+            ProfScope p(b, OP_LN, 0);
+            launch_resid_layernorm(b->x, b->dbuf, R, c.d, Ld.ln2, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+        }
         e = EpiArgs{};
         e.R = R;
         e.N = c.f;
@@ -259,18 +361,21 @@ int forward(hs_batch* b, int R) {
         e.ldo = c.Fp;
         e.gelu = Ld.gelu;
         e.gelu_off = Ld.gelu_off;
-        gemm(EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e);
+        gemm(OP_GEMM_FC, EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e);
         e = EpiArgs{};
         e.R = R;
         e.N = c.d;
         e.b = mlp.ld.b;
         e.m = mlp.ld.m;
         e.s = mlp.ld.s;
-        e.x = b->x;
-        e.ldx = c.d;
-        gemm(EPI_RESID, b->g, c.Fp, &b->tm_g, mlp, e);
+        e.out32 = b->dbuf;
+        e.ldo = c.d;
+        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e);
     }
-    launch_layernorm(b->x, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+    {
+        ProfScope p(b, OP_LN, 0);
+        launch_resid_layernorm(b->x, b->dbuf, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+    }
     const DevLinear& lmh = *m->lins[4 * c.L];
     EpiArgs e{};
     e.R = R;
@@ -282,7 +387,7 @@ int forward(hs_batch* b, int R) {
     e.tmax = b->tmax;
     e.ldt = c.VT;
     e.last = m->logits_len - 1;
-    gemm(EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e);
+    gemm(OP_GEMM_LOGITS, EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e);
     return HS_OK;
 }
 
@@ -297,6 +402,27 @@ int check_device_error(hs_batch* b) {
         return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
     }
     return HS_OK;
+}
+
+// The prefill groups of a pass (the reference's attention row groups, batch.rs att_groups): runs
+// of rows of one slot at consecutive positions, cut at 128 rows. Runs of at least
+// ATTN_TC_MIN_ROWS rows go to the tensor-core kernel; the other rows to the CUDA-core kernel.
+void plan_groups(hs_batch* b, int R) {
+    b->n_groups = 0;
+    b->n_rowlist = 0;
+    if (!b->model->attn_tc) return;
+    int r = 0;
+    while (r < R) {
+        const RowInfo& f = b->h_rows[r];
+        int e = r + 1;
+        while (e < R && e - r < 128 && b->h_rows[e].slot == f.slot && b->h_rows[e].pos == f.pos + (uint32_t)(e - r)) e++;
+        if (e - r >= ATTN_TC_MIN_ROWS) {
+            b->h_groups[b->n_groups++] = AttnGroup{(uint32_t)r, (uint32_t)(e - r), f.slot, f.pos};
+        } else {
+            for (int q = r; q < e; q++) b->h_rowlist[b->n_rowlist++] = q;
+        }
+        r = e;
+    }
 }
 
 struct PlanRow {
@@ -366,6 +492,11 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     }
     int rc = set_device(m->dev);
     if (rc) return rc;
+    if (wout && !b->weights) {
+        // The weights buffer of run_weights: made on the first use (vocab u64 per row).
+        if ((rc = dalloc(&b->weights, (size_t)b->Rcap * c.V, b->owned))) return rc;
+        b->bytes += (uint64_t)b->Rcap * c.V * 8;
+    }
     std::vector<std::vector<PlanRow>> passes;
     std::vector<int> pos;
     std::vector<uint32_t> hist;
@@ -382,18 +513,37 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             b->h_rows[r] = ri;
         }
         CK(cudaMemcpyAsync(b->d_rows, b->h_rows, sizeof(RowInfo) * R, cudaMemcpyHostToDevice, b->stream));
+        plan_groups(b, R);
+        if (b->n_groups) {
+            CK(cudaMemcpyAsync(b->d_groups, b->h_groups, sizeof(AttnGroup) * b->n_groups, cudaMemcpyHostToDevice,
+                               b->stream));
+            if (b->n_rowlist)
+                CK(cudaMemcpyAsync(b->d_rowlist, b->h_rowlist, sizeof(int) * b->n_rowlist, cudaMemcpyHostToDevice,
+                                   b->stream));
+        }
+        std::unique_ptr<ProfScope> pass_scope(new ProfScope(b, OP_PASS, (uint64_t)R));
         rc = forward(b, R);
         if (rc) return rc;
         if (out) {
-            launch_coder(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, bits, b->d_rows,
-                         b->intervals, b->stream);
+            {
+                ProfScope p(b, OP_CODER, 0);
+                launch_coder(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, bits, b->d_rows,
+                             b->intervals, b->stream);
+            }
+            pass_scope.reset();
             CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
                                b->stream));
         } else {
-            launch_weights(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, b->weights, b->stream);
+            {
+                ProfScope p(b, OP_CODER, 0);
+                launch_weights(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, b->weights,
+                               b->stream);
+            }
+            pass_scope.reset();
         }
         rc = check_device_error(b);
         if (rc) return rc;
+        if (b->profiling) prof_collect(b);
         if (out) {
             for (int r = 0; r < R; r++) {
                 long in = pass[r].input;
@@ -471,6 +621,7 @@ int hs_open(int ordinal, hs_dev** out) {
     CK(cudaMemset(d->d_err, 0, sizeof(int)));
     CK(configure_core_kernels());
     CK(configure_tc_kernels());
+    CK(configure_attn_tc());
     *out = d.release();
     return HS_OK;
 }
@@ -520,6 +671,7 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
     auto m = std::make_unique<hs_model>();
     m->dev = dev;
     m->use_tc = use_tc_default();
+    m->attn_tc = use_attn_tc_default() && attention_tc_supported(M.head_dim, M.n_ctx, (int)M.attn_exp.size());
     sha256(file, len, m->hash);
     m->eot = M.eot;
     m->version = M.version;
@@ -633,17 +785,27 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         (rc = dalloc(&b->d_rows, R, b->owned)) || (rc = dalloc(&b->x, R * c.d, b->owned)) ||
         (rc = dalloc(&b->a, R * c.Dp, b->owned)) || (rc = dalloc(&b->qkv, R * c.QKVp, b->owned)) ||
         (rc = dalloc(&b->att, R * c.Dp, b->owned)) || (rc = dalloc(&b->g, R * c.Fp, b->owned)) ||
+        (rc = dalloc(&b->dbuf, R * c.d, b->owned)) ||
         (rc = dalloc(&b->d16, R * c.Vp, b->owned)) || (rc = dalloc(&b->tmax, R * c.VT, b->owned)) ||
-        (rc = dalloc(&b->intervals, 3 * R, b->owned)) || (rc = dalloc(&b->weights, R * c.V, b->owned)))
+        (rc = dalloc(&b->intervals, 3 * R, b->owned)))
         return rc;
+    if ((rc = dalloc(&b->d_groups, R, b->owned)) || (rc = dalloc(&b->d_rowlist, R, b->owned))) return rc;
+    CK(cudaMallocHost(&b->h_groups, sizeof(AttnGroup) * R));
+    CK(cudaMallocHost(&b->h_rowlist, sizeof(int) * R));
     CK(cudaMallocHost(&b->h_rows, sizeof(RowInfo) * R));
     CK(cudaMallocHost(&b->h_intervals, sizeof(uint64_t) * 3 * R));
-    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 4 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24 +
-                                8 * c.V);
+    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24);
     if ((rc = make_tmap(m->dev, &b->tm_a, b->a, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_att, b->att, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_g, b->g, R, c.Fp, TILE_M)))
         return rc;
+    if (m->attn_tc) {
+        uint64_t heads = (uint64_t)slots * c.L * c.H;
+        if ((rc = make_tmap(m->dev, &b->tm_q, b->qkv, R, c.QKVp, 128, 64)) ||
+            (rc = make_tmap(m->dev, &b->tm_k, b->kc, heads * c.n_ctx, c.hd, 128, 64)) ||
+            (rc = make_tmap(m->dev, &b->tm_v, b->vc, heads * c.hd, c.n_ctx, 64, 128)))
+            return rc;
+    }
     *out = b.release();
     return HS_OK;
 }
@@ -670,6 +832,33 @@ uint32_t hs_batch_position(hs_batch* b, uint32_t slot) {
 }
 
 uint64_t hs_batch_gpu_bytes(hs_batch* b) { return b ? b->bytes : 0; }
+
+int hs_batch_set_profiling(hs_batch* b, int on) {
+    if (!b) return fail(HS_BAD_ARGUMENT, "null argument");
+    b->profiling = on != 0;
+    b->op_ms.assign(OP_COUNT, 0.0);
+    b->op_launches.assign(OP_COUNT, 0);
+    b->op_flops.assign(OP_COUNT, 0);
+    b->ev_pending.clear();
+    return HS_OK;
+}
+
+int hs_batch_profile(hs_batch* b, hs_op_profile* out, int cap) {
+    if (!b || (cap > 0 && !out)) return fail(HS_BAD_ARGUMENT, "null argument");
+    if (!b->profiling) return 0;
+    int n = 0;
+    for (int op = 0; op < OP_COUNT && n < cap; op++) {
+        hs_op_profile& p = out[n++];
+        memset(&p, 0, sizeof(p));
+        strncpy(p.name, OP_NAMES[op], sizeof(p.name) - 1);
+        p.ms = b->op_ms[op];
+        p.launches = b->op_launches[op];
+        p.ops = b->op_flops[op];
+    }
+    return n;
+}
+
+uint64_t hs_launch_count(void) { return g_launches; }
 
 int hs_batch_run_coded(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds,
                        const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out) {

@@ -1,0 +1,337 @@
+"""Seeded synthetic workloads of the benchmark (no network, no published weights here).
+
+- `gpt2_hsm(seed)`: a GPT-2 124M-shaped model file (12 layers, d_model 768, 12 heads, FFN 3072,
+  vocab 50257, ctx 1024) with float weights from seeded N(0, 0.02), biases 0, LayerNorm gamma 1
+  and beta 0, converted to the HardShell .hsm integer format (version 1) with the rules of the
+  reference converter (tools/convert/build.py of the reference): per-row symmetric int8 weights,
+  activation scales from a float calibration pass, multipliers in [2^30, 2^31), the constants
+  K = 48, J = 8, P = 30, exponent tables of 8192 entries with a unit of 2^-8, and 16-bit-input
+  GELU tables. The reference converter needs the published GPT-2 files and exact rationals; this
+  stand-in uses float64 numpy for the same rules, so its bytes are its own (the HardShell engine
+  only needs a valid file).
+- `zipf_windows(...)`: token windows of seeded Zipf(s=1.1) text over a 5,000-word random
+  lowercase vocabulary, space and newline separated. The synthetic vocabulary has one token per
+  word (with its leading space or newline), so the text is exactly the bytes of its tokens.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+N_LAYER, N_HEAD, D_MODEL, D_FF, VOCAB, N_CTX = 12, 12, 768, 3072, 50257, 1024
+
+
+@dataclass(frozen=True)
+class Shape:
+    n_layer: int
+    n_head: int
+    d_model: int
+    d_ff: int
+    vocab: int
+    n_ctx: int
+
+
+GPT2 = Shape(N_LAYER, N_HEAD, D_MODEL, D_FF, VOCAB, N_CTX)
+# A small model with GPT-2's head width (64) for the tests of the tensor-core attention.
+MINI = Shape(2, 2, 128, 512, 1000, 512)
+LN_K, LN_J, SOFTMAX_P = 48, 8, 30
+TABLE_LEN, ATTN_EXP_E, LOGITS_EXP_E, DELTA = 8192, 30, 40, 2.0 ** -8
+I32_MAX = 2**31 - 1
+N_WORDS = 5000
+CACHE = Path(__file__).resolve().parent / "_cache"
+
+
+# ---- the synthetic vocabulary ----
+
+def vocabulary(seed: int = 0x7AC0, vocab: int = VOCAB) -> list[bytes]:
+    """256 single bytes, word tokens (for GPT-2's 50,257: 25,000 " w" and 25,000 "\\nw" tokens; for a
+    smaller vocabulary: " w" tokens only), and <|endoftext|> last."""
+    rng = np.random.default_rng(seed)
+    if vocab != VOCAB:
+        letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz", dtype=np.uint8)
+        words, seen = [], set()
+        while len(words) < vocab - 257:
+            w = letters[rng.integers(0, 26, int(rng.integers(2, 6)))].tobytes()
+            if w not in seen:
+                seen.add(w)
+                words.append(b" " + w)
+        return [bytes([b]) for b in range(256)] + words + [b"<|endoftext|>"]
+    letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz", dtype=np.uint8)
+    words: list[bytes] = []
+    seen = set()
+    while len(words) < 25_000:
+        n = int(rng.integers(2, 6))
+        w = letters[rng.integers(0, 26, n)].tobytes()
+        if w not in seen:
+            seen.add(w)
+            words.append(w)
+    toks = [bytes([b]) for b in range(256)]
+    toks += [b" " + w for w in words]
+    toks += [b"\n" + w for w in words]
+    toks.append(b"<|endoftext|>")
+    assert len(toks) == VOCAB
+    return toks
+
+
+def text_word_tokens() -> tuple[np.ndarray, np.ndarray]:
+    """The token ids of the 5,000 text words with a leading space and with a leading newline."""
+    space = 256 + np.arange(N_WORDS)
+    newline = 256 + 25_000 + np.arange(N_WORDS)
+    return space, newline
+
+
+def zipf_windows(n_windows: int, window: int, seed: int) -> np.ndarray:
+    """[n_windows, window] token ids of seeded Zipf(1.1) text; one line in ~12 words."""
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, N_WORDS + 1, dtype=np.float64)
+    p = ranks ** -1.1
+    p /= p.sum()
+    idx = rng.choice(N_WORDS, size=(n_windows, window), p=p)
+    space, newline = text_word_tokens()
+    nl = rng.random((n_windows, window)) < 1.0 / 12
+    return np.where(nl, newline[idx], space[idx]).astype(np.uint32)
+
+
+def token_lengths(vocab: list[bytes]) -> np.ndarray:
+    return np.array([len(t) for t in vocab], dtype=np.int64)
+
+
+# ---- the float model and its calibration ----
+
+def _gelu(x):
+    return 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3)))
+
+
+def _ln(x, g, b):
+    mu = x.mean(-1, keepdims=True)
+    var = ((x - mu) ** 2).mean(-1, keepdims=True)
+    return (x - mu) / np.sqrt(var + 1e-5) * g + b
+
+
+def float_model(seed: int, sh: Shape = GPT2) -> dict:
+    rng = np.random.default_rng(seed)
+    n = lambda *s: rng.normal(0.0, 0.02, s).astype(np.float32)  # noqa: E731
+    d, f = sh.d_model, sh.d_ff
+    m = {"wte": n(sh.vocab, d), "wpe": n(sh.n_ctx, d), "blocks": [], "shape": sh}
+    for _ in range(sh.n_layer):
+        m["blocks"].append({"attn_w": n(3 * d, d), "proj_w": n(d, d), "fc_w": n(f, d), "mlp_w": n(d, f)})
+    return m
+
+
+def calibrate(fm: dict, seed: int, seqs: int = 2, length: int = 256) -> dict:
+    """The largest |x| of each activation site, and the residual max and smallest row std."""
+    sh: Shape = fm["shape"]
+    rng = np.random.default_rng(seed ^ 0xCA1)
+    ranges: dict[str, float] = {}
+    res_max, row_std = 0.0, np.inf
+    hd = sh.d_model // sh.n_head
+    length = min(length, sh.n_ctx)
+    one = np.ones(sh.d_model, np.float32)
+    zero = np.zeros(sh.d_model, np.float32)
+
+    def see(k, v):
+        ranges[k] = max(ranges.get(k, 0.0), float(np.abs(v).max()))
+
+    for _ in range(seqs):
+        toks = rng.integers(0, sh.vocab - 1, length)
+        x = fm["wte"][toks] + fm["wpe"][:length]
+        for l, b in enumerate(fm["blocks"]):
+            res_max = max(res_max, float(np.abs(x).max()))
+            row_std = min(row_std, float(x.std(-1).min()))
+            a = _ln(x, one, zero)
+            see(f"h.{l}.ln_1", a)
+            qkv = a @ b["attn_w"].T
+            q, k, v = np.split(qkv, 3, axis=-1)
+            see(f"h.{l}.q", q)
+            see(f"h.{l}.k", k)
+            see(f"h.{l}.v", v)
+            att = np.zeros_like(q)
+            mask = np.triu(np.full((length, length), -np.inf, np.float32), 1)
+            for h in range(sh.n_head):
+                sl = slice(h * hd, (h + 1) * hd)
+                s = q[:, sl] @ k[:, sl].T / np.sqrt(hd) + mask
+                s = np.exp(s - s.max(-1, keepdims=True))
+                s /= s.sum(-1, keepdims=True)
+                att[:, sl] = s @ v[:, sl]
+            see(f"h.{l}.att", att)
+            x = x + att @ b["proj_w"].T
+            a = _ln(x, one, zero)
+            see(f"h.{l}.ln_2", a)
+            f = a @ b["fc_w"].T
+            see(f"h.{l}.fc", f)
+            g = _gelu(f)
+            see(f"h.{l}.gelu", g)
+            x = x + g @ b["mlp_w"].T
+        res_max = max(res_max, float(np.abs(x).max()))
+        row_std = min(row_std, float(x.std(-1).min()))
+        see("ln_f", _ln(x, one, zero))
+    ranges["res_max"] = res_max
+    ranges["row_std_min"] = row_std
+    return ranges
+
+
+# ---- the conversion rules (tools/convert/build.py and exact.py of the reference) ----
+
+def quantise_rows(w: np.ndarray, qmax: int = 127) -> tuple[np.ndarray, np.ndarray]:
+    w = np.asarray(w, np.float64)
+    mx = np.abs(w).max(axis=1)
+    scale = np.where(mx > 0, mx / qmax, 1.0)
+    q = np.clip(np.rint(w / scale[:, None]), -qmax, qmax).astype(np.int64)
+    return q, scale
+
+
+def quant_mult_rows(ratios) -> tuple[np.ndarray, int]:
+    r = np.asarray(ratios, np.float64)
+    mx = float(r.max())
+    assert 0 < mx < I32_MAX and r.min() >= 0
+    s = 0
+    while s < 126 and mx * 2.0 ** (s + 1) < I32_MAX:
+        s += 1
+    m = np.rint(r * 2.0 ** s)
+    assert m.max() <= I32_MAX
+    return m.astype(np.int32), s
+
+
+def quant_mult(ratio: float) -> tuple[int, int]:
+    m, s = quant_mult_rows([ratio])
+    return int(m[0]), s
+
+
+def exp_table(e: int) -> np.ndarray:
+    i = np.arange(TABLE_LEN, dtype=np.float64)
+    t = np.rint(2.0 ** e * np.exp(-i * DELTA))
+    t[0] = 2.0 ** e
+    return t
+
+
+def gelu_table(s_in: float, s_out: float) -> np.ndarray:
+    x = np.arange(-32768, 32768, dtype=np.float64) * s_in
+    return np.clip(np.rint(_gelu(x) / s_out), -127, 127).astype(np.int8)
+
+
+def build_tensors(fm: dict, rg: dict) -> list[tuple[str, str, np.ndarray, int | None]]:
+    """(name, dtype, values, shift) in the order of crates/hardshell/src/gpt2/mod.rs."""
+    out: list[tuple[str, str, np.ndarray, int | None]] = []
+    sh: Shape = fm["shape"]
+    D_MODEL, D_FF, N_HEAD = sh.d_model, sh.d_ff, sh.n_head  # noqa: N806
+    res = min(rg["res_max"] / 2 ** 24, rg["row_std_min"] / 2 ** 12.5)
+    site = lambda k, qmax=127: rg[k] / qmax  # noqa: E731
+    s_lnf = site("ln_f")
+    wq, ws = quantise_rows(fm["wte"])
+    out.append(("wte", "i8", wq.astype(np.int8), None))
+    m, s = quant_mult_rows(ws / res)
+    out.append(("wte.rescale_embed", "i32", m, s))
+    m, s = quant_mult_rows(ws * s_lnf / DELTA)
+    out.append(("wte.rescale_logits", "i32", m, s))
+    pq, ps = quantise_rows(fm["wpe"])
+    out.append(("wpe", "i8", pq.astype(np.int8), None))
+    m, s = quant_mult_rows(ps / res)
+    out.append(("wpe.rescale", "i32", m, s))
+
+    def layernorm(prefix, s_out):
+        gq, gs = quantise_rows(np.ones((1, D_MODEL)), 32767)
+        out.append((f"{prefix}.g", "i16", gq.reshape(-1).astype(np.int16), None))
+        out.append((f"{prefix}.b", "i32", np.zeros(D_MODEL, np.int32), None))
+        mm, ss = quant_mult(gs[0] / (2.0 ** (LN_K - LN_J) * s_out))
+        out.append((f"{prefix}.rescale", "i32", np.array([mm], np.int32), ss))
+
+    def linear(prefix, w, s_in, s_out):
+        q, ws_ = quantise_rows(w)
+        out.append((f"{prefix}.w", "i8", q.astype(np.int8), None))
+        out.append((f"{prefix}.b", "i32", np.zeros(w.shape[0], np.int32), None))
+        mm, ss = quant_mult_rows(s_in * ws_ / np.asarray(s_out))
+        out.append((f"{prefix}.rescale", "i32", mm, ss))
+
+    hd = D_MODEL // N_HEAD
+    for l, b in enumerate(fm["blocks"]):
+        p = f"h.{l}"
+        layernorm(f"{p}.ln_1", site(f"{p}.ln_1"))
+        sq, sk, sv = site(f"{p}.q"), site(f"{p}.k"), site(f"{p}.v")
+        qkv_out = np.concatenate([np.full(D_MODEL, sq), np.full(D_MODEL, sk), np.full(D_MODEL, sv)])
+        linear(f"{p}.attn.c_attn", b["attn_w"], site(f"{p}.ln_1"), qkv_out)
+        mm, ss = quant_mult(sq * sk / DELTA / np.sqrt(hd))
+        out.append((f"{p}.attn.score.rescale", "i32", np.array([mm], np.int32), ss))
+        mm, ss = quant_mult(sv / (2.0 ** SOFTMAX_P * site(f"{p}.att")))
+        out.append((f"{p}.attn.out.rescale", "i32", np.array([mm], np.int32), ss))
+        linear(f"{p}.attn.c_proj", b["proj_w"], site(f"{p}.att"), np.full(D_MODEL, res))
+        layernorm(f"{p}.ln_2", site(f"{p}.ln_2"))
+        s_fc = site(f"{p}.fc", 32767)
+        linear(f"{p}.mlp.c_fc", b["fc_w"], site(f"{p}.ln_2"), np.full(D_FF, s_fc))
+        out.append((f"{p}.mlp.gelu", "i8", gelu_table(s_fc, site(f"{p}.gelu")), None))
+        linear(f"{p}.mlp.c_proj", b["mlp_w"], site(f"{p}.gelu"), np.full(D_MODEL, res))
+    layernorm("ln_f", s_lnf)
+    out.append(("attn_exp", "i32", exp_table(ATTN_EXP_E).astype(np.int32), None))
+    out.append(("logits_exp", "u64", exp_table(LOGITS_EXP_E).astype(np.uint64), None))
+    return out, res
+
+
+def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2) -> bytes:
+    """The .hsm layout (crates/hardshell/src/hsm/mod.rs:1-120): preamble, compact JSON header,
+    vocabulary and tensors at 64-byte boundaries with zero padding."""
+    vocab_sec = b"".join(struct.pack("<H", len(t)) + t for t in vocab)
+    dt = {"i8": np.int8, "i16": np.int16, "i32": np.int32, "u64": np.uint64}
+    blobs = [(n, d, np.ascontiguousarray(v, dtype=dt[d]).astype(np.dtype(dt[d]).newbyteorder("<")), s)
+             for n, d, v, s in tensors]
+    align = lambda x: (x + 63) & ~63  # noqa: E731
+    hlen = 4096
+    while True:
+        cursor = align(16 + hlen)
+        voff = cursor
+        cursor = voff + len(vocab_sec)
+        entries = []
+        for n, d, v, s in blobs:
+            off = align(cursor)
+            e = {"name": n, "dtype": d, "shape": list(v.shape), "offset": off, "length": v.nbytes}
+            if s is not None:
+                e["shift"] = int(s)
+            entries.append(e)
+            cursor = off + v.nbytes
+        header = {
+            "model": {"architecture": "gpt2", "n_layer": sh.n_layer, "n_head": sh.n_head, "d_model": sh.d_model,
+                      "d_ff": sh.d_ff, "vocab_size": sh.vocab, "n_ctx": sh.n_ctx, "eot_token": sh.vocab - 1,
+                      "constants": {"ln_k": LN_K, "ln_j": LN_J, "ln_eps": eps, "softmax_p": SOFTMAX_P}},
+            "vocabulary": {"offset": voff, "length": len(vocab_sec)},
+            "tensors": entries,
+        }
+        text = json.dumps(header, separators=(",", ":")).encode()
+        if len(text) <= hlen:
+            text += b" " * (hlen - len(text))
+            break
+        hlen = len(text)
+    out = bytearray(b"HSHLMDL\0" + struct.pack("<II", 1, hlen) + text)
+    out += bytes(align(len(out)) - len(out))
+    out += vocab_sec
+    for (n, d, v, s), e in zip(blobs, entries):
+        out += bytes(e["offset"] - len(out))
+        out += v.tobytes()
+    return bytes(out)
+
+
+def gpt2_hsm(seed: int = 124, cache: bool = True, shape: Shape = GPT2) -> bytes:
+    """The synthetic GPT-2 model file for `seed` and `shape` (GPT-2 124M by default; cached under
+    taco_b200/_cache)."""
+    tag = "gpt2_124m" if shape == GPT2 else "gpt2_{}l{}h{}d{}f{}v{}c".format(*vars(shape).values())
+    path = CACHE / f"{tag}_seed{seed}.hsm"
+    if cache and path.exists():
+        return path.read_bytes()
+    fm = float_model(seed, shape)
+    rg = calibrate(fm, seed)
+    tensors, res = build_tensors(fm, rg)
+    eps = max(1, int(round(1e-5 / (res * res) * 2 ** (2 * LN_J))))
+    data = write_hsm(tensors, vocabulary(vocab=shape.vocab), eps, shape)
+    if cache:
+        CACHE.mkdir(exist_ok=True)
+        tmp = path.with_suffix(".tmp")
+        tmp.write_bytes(data)
+        tmp.replace(path)
+    return data
+
+
+def describe(data: bytes) -> str:
+    return f"{len(data)} bytes, sha256 {hashlib.sha256(data).hexdigest()[:16]}"
