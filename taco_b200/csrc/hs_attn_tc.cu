@@ -16,8 +16,10 @@
 //
 // Operands come in by TMA (no multicast): Q [128 x 64] and K chunks [128 x 64] with the 64-byte
 // swizzle, V^T chunks [64 x 128] with the 128-byte swizzle from the transposed values cache.
-// Warps 0..7 do the softmax (TMEM lane group warp % 4, key half warp / 4), warp 8 is the TMA
-// producer, warp 9 owns TMEM and issues the MMAs. Every wait is bounded.
+// Warps 0..15 do the softmax: TMEM lane group warp % 4 (32 rows) and key quarter warp / 4 (32
+// of the 128 keys of a chunk). Warp 16 is the TMA producer, warp 17 owns TMEM and issues the
+// MMAs: S of chunk i + 1 is issued before P V of chunk i, and P is double-buffered, so the
+// softmax warps always have work while the tensor core runs. Every wait is bounded.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -33,22 +35,23 @@ namespace {
 constexpr int GM = 128;        // rows of a group (TMEM lanes)
 constexpr int KC = 128;        // keys per chunk
 constexpr int HDIM = 64;       // head width of this kernel
-constexpr int EW = 8;          // epilogue warps
-constexpr int ETH = 32 * EW;   // epilogue threads
+constexpr int EW = 16;         // softmax warps
+constexpr int ETH = 32 * EW;   // softmax threads
 constexpr int ATHREADS = ETH + 64;
 constexpr int Q_BYTES = GM * HDIM;        // 8 KB
 constexpr int K_BYTES = KC * HDIM;        // 8 KB
 constexpr int V_BYTES = HDIM * KC;        // 8 KB
-constexpr int P_BYTES = 4 * GM * KC;      // 64 KB (four planes)
+constexpr int P_BYTES = 4 * GM * KC;      // 64 KB (four planes), double-buffered
 constexpr int TABLE_MAX = 8192;           // attn_exp entries kept in shared memory
-constexpr size_t ASMEM = (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + P_BYTES + 4 * TABLE_MAX + 4 * GM * 8 + 512 + 1024;
+constexpr size_t ASMEM =
+    (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 4 * TABLE_MAX + 8 * GM * 8 + 512 + 1024;
 
 struct __align__(8) ABars {
     uint64_t q_full;
     uint64_t k_full[2], k_empty[2];
     uint64_t v_full[2], v_empty[2];
     uint64_t s_full[2], s_empty[2];
-    uint64_t p_full, p_empty;
+    uint64_t p_full[2], p_empty[2];
     uint64_t o_full;
     uint32_t tmem_base;
 };
@@ -74,6 +77,21 @@ __device__ __forceinline__ int64_t score_of(int32_t dot, int32_t sm, int ss, boo
     return clamp64(y, -SCORE_LIMIT, SCORE_LIMIT);
 }
 
+// The table index min(max - score, last). NARROW (21 <= ss <= 62): |dot| <= 64 * 2^14 = 2^20 and
+// |sm| <= 2^31, so |score| < 2^30 (no clamp at 2^40) and the distance fits in 32 bits.
+template <bool NARROW>
+__device__ __forceinline__ int32_t dist_of(int64_t M, int32_t dot, int32_t sm, int ss, bool fast, int64_t h,
+                                           int32_t last) {
+    if (NARROW) {
+        int32_t dd = (int32_t)M - (int32_t)(((int64_t)dot * (int64_t)sm + h) >> ss);
+        return dd < last ? dd : last;
+    } else {
+        int64_t dd = M - score_of(dot, sm, ss, fast, h);
+        return (int32_t)(dd < (int64_t)last ? dd : (int64_t)last);
+    }
+}
+
+template <bool NARROW>
 __global__ void __launch_bounds__(ATHREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnGroup* groups, int L, int layer, int H,
@@ -84,10 +102,10 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + Q_BYTES;                 // 2 x 8 KB
     uint8_t* sV = sK + 2 * K_BYTES;             // 2 x 8 KB
-    uint8_t* sP = sV + 2 * V_BYTES;             // 4 planes x 16 KB
-    int32_t* sT = reinterpret_cast<int32_t*>(sP + P_BYTES);
-    int64_t* sX = reinterpret_cast<int64_t*>(sT + TABLE_MAX);  // [2][2][GM] row exchange
-    ABars* bars = reinterpret_cast<ABars*>(sX + 4 * GM);
+    uint8_t* sP = sV + 2 * V_BYTES;             // 2 x 4 planes x 16 KB
+    int32_t* sT = reinterpret_cast<int32_t*>(sP + 2 * P_BYTES);
+    int64_t* sX = reinterpret_cast<int64_t*>(sT + TABLE_MAX);  // [2][4][GM] row exchange
+    ABars* bars = reinterpret_cast<ABars*>(sX + 8 * GM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const AttnGroup grp = groups[blockIdx.x];
     const int h = blockIdx.y;
@@ -105,8 +123,10 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->s_empty[i], ETH);
         }
-        mbar_init(&bars->p_full, ETH);
-        mbar_init(&bars->p_empty, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&bars->p_full[i], ETH);
+            mbar_init(&bars->p_empty[i], 1);
+        }
         mbar_init(&bars->o_full, 1);
         fence_barrier_init();
     }
@@ -153,7 +173,8 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             }
         }
     } else if (warp == EW + 1) {
-        // MMA issuer.
+        // MMA issuer: S of chunk `it`, then (pass 3) the P V of the chunk before it, so the softmax
+        // warps always have the next S while the tensor core multiplies the previous P.
         if (lane == 0) {
             const uint32_t id_s = idesc_i8(GM, KC, true, true);
             const uint32_t id_pv = idesc_i8(GM, HDIM, false, true);
@@ -161,9 +182,30 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tc_fence_after();
             const uint32_t qa = smem_u32(sQ);
             int ks = 0, vs = 0;
-            uint32_t kph = 0, vph = 0, pph = 0;
+            uint32_t kph = 0, vph = 0;
+            auto do_pv = [&](int c) -> bool {
+                const int pb = c & 1;
+                if (!mbar_wait(&bars->p_full[pb], (c >> 1) & 1, err, 16)) return false;
+                if (!mbar_wait(&bars->v_full[vs], vph, err, 17)) return false;
+                tc_fence_after();
+                const uint32_t vb = smem_u32(sV + vs * V_BYTES);
+#pragma unroll
+                for (int pl = 0; pl < 4; pl++) {
+                    const uint32_t pa = smem_u32(sP + pb * P_BYTES + pl * (GM * KC));
+                    const uint32_t o = tmem + 2 * KC + pl * HDIM;
+#pragma unroll
+                    for (int k = 0; k < KC / 32; k++)
+                        mma_i8(o, sdesc_sw128(pa + 32 * k), sdesc_sw128(vb + 32 * k), id_pv, (c > 0 || k > 0) ? 1u : 0u);
+                }
+                mma_commit(&bars->v_empty[vs]);
+                mma_commit(&bars->p_empty[pb]);
+                if (++vs == 2) {
+                    vs = 0;
+                    vph ^= 1;
+                }
+                return true;
+            };
             for (int it = 0; it < 3 * nch && ok; it++) {
-                const int c = it % nch;
                 const int sb = it & 1;
                 const uint32_t sph = (it >> 1) & 1;
                 if (!mbar_wait(&bars->s_empty[sb], sph ^ 1, err, 14)) break;
@@ -180,41 +222,20 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     ks = 0;
                     kph ^= 1;
                 }
-                if (it >= 2 * nch) {
-                    // P of this chunk from the softmax warps, then O_k += P_k V for the four planes.
-                    if (!mbar_wait(&bars->p_full, pph, err, 16)) break;
-                    if (!mbar_wait(&bars->v_full[vs], vph, err, 17)) break;
-                    tc_fence_after();
-                    const uint32_t vb = smem_u32(sV + vs * V_BYTES);
-#pragma unroll
-                    for (int pl = 0; pl < 4; pl++) {
-                        const uint32_t pa = smem_u32(sP + pl * (GM * KC));
-                        const uint32_t o = tmem + 2 * KC + pl * HDIM;
-#pragma unroll
-                        for (int k = 0; k < KC / 32; k++)
-                            mma_i8(o, sdesc_sw128(pa + 32 * k), sdesc_sw128(vb + 32 * k), id_pv,
-                                   (c > 0 || k > 0) ? 1u : 0u);
-                    }
-                    mma_commit(&bars->v_empty[vs]);
-                    mma_commit(&bars->p_empty);
-                    if (++vs == 2) {
-                        vs = 0;
-                        vph ^= 1;
-                    }
-                    pph ^= 1;
-                }
+                if (it > 2 * nch && !do_pv(it - 2 * nch - 1)) ok = false;
             }
+            if (ok) do_pv(nch - 1);
             mma_commit(&bars->o_full);
         }
     } else {
-        // Softmax warps: one row per thread, 64 keys of each chunk (half = warp / 4).
-        const int g = warp & 3, half = warp >> 2;
+        // Softmax warps: one row per thread, 32 keys of each chunk (quarter qt = warp / 4).
+        const int g = warp & 3, qt = warp >> 2;
         const int row = g * 32 + lane;
         const int rpos = (int)grp.pos0 + row;  // rows past the group compute harmless values
-        const uint32_t tbase = tmem + ((uint32_t)(g * 32) << 16);
+        const uint32_t tbase = tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(qt * 32);
         const bool fast = ss >= 0 && ss <= 62;
         const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
-        const int64_t last = tl - 1;
+        const int32_t last = tl - 1;
         int it = 0;
         // Pass 1: the max and min dot over the row's causal keys.
         int32_t maxd = INT32_MIN, mind = INT32_MAX;
@@ -223,13 +244,20 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 21);
             __syncwarp();
             tc_fence_after();
+            uint32_t v[32];
+            tmem_ld32(tbase + sb * KC, v);
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(&bars->s_empty[sb]);
+            const int j0 = c * KC + qt * 32;
+            if (j0 + 31 <= rpos) {
 #pragma unroll
-            for (int q2 = 0; q2 < 2; q2++) {
-                uint32_t v[32];
-                __syncwarp();
-                tmem_ld32(tbase + sb * KC + half * 64 + q2 * 32, v);
-                tmem_ld_wait();
-                const int j0 = c * KC + half * 64 + q2 * 32;
+                for (int q = 0; q < 32; q++) {
+                    int32_t dv = (int32_t)v[q];
+                    maxd = dv > maxd ? dv : maxd;
+                    mind = dv < mind ? dv : mind;
+                }
+            } else {
 #pragma unroll
                 for (int q = 0; q < 32; q++) {
                     if (j0 + q <= rpos) {
@@ -239,14 +267,13 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     }
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&bars->s_empty[sb]);
         }
-        sX[(0 * 2 + half) * GM + row] = maxd;
-        sX[(1 * 2 + half) * GM + row] = mind;
+        sX[(0 * 4 + qt) * GM + row] = maxd;
+        sX[(1 * 4 + qt) * GM + row] = mind;
         named_bar(1, ETH);
-        {
-            int64_t a = sX[(0 * 2 + (half ^ 1)) * GM + row], b = sX[(1 * 2 + (half ^ 1)) * GM + row];
+#pragma unroll
+        for (int o = 0; o < 4; o++) {
+            int64_t a = sX[(0 * 4 + o) * GM + row], b = sX[(1 * 4 + o) * GM + row];
             maxd = (int32_t)(a > maxd ? a : maxd);
             mind = (int32_t)(b < mind ? b : mind);
         }
@@ -262,109 +289,103 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 22);
             __syncwarp();
             tc_fence_after();
-#pragma unroll
-            for (int q2 = 0; q2 < 2; q2++) {
-                uint32_t v[32];
-                __syncwarp();
-                tmem_ld32(tbase + sb * KC + half * 64 + q2 * 32, v);
-                tmem_ld_wait();
-                const int j0 = c * KC + half * 64 + q2 * 32;
-#pragma unroll
-                for (int q = 0; q < 32; q++) {
-                    if (j0 + q <= rpos) {
-                        int64_t dd = M - score_of((int32_t)v[q], sm, ss, fast, hround);
-                        sum += (uint64_t)sT[dd < last ? dd : last];
-                    }
-                }
-            }
+            uint32_t v[32];
+            tmem_ld32(tbase + sb * KC, v);
+            tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
+            const int j0 = c * KC + qt * 32;
+            if (j0 + 31 <= rpos) {
+#pragma unroll
+                for (int q = 0; q < 32; q++)
+                    sum += (uint32_t)sT[dist_of<NARROW>(M, (int32_t)v[q], sm, ss, fast, hround, last)];
+            } else {
+#pragma unroll
+                for (int q = 0; q < 32; q++)
+                    if (j0 + q <= rpos)
+                        sum += (uint32_t)sT[dist_of<NARROW>(M, (int32_t)v[q], sm, ss, fast, hround, last)];
+            }
         }
         named_bar(1, ETH);  // everyone has read sX (pass 1) before it is reused
-        sX[(0 * 2 + half) * GM + row] = (int64_t)sum;
+        sX[qt * GM + row] = (int64_t)sum;
         named_bar(1, ETH);
-        sum += (uint64_t)sX[(0 * 2 + (half ^ 1)) * GM + row];
+        sum = 0;
+#pragma unroll
+        for (int o = 0; o < 4; o++) sum += (uint64_t)sX[o * GM + row];
         if (sum == 0) sum = 1;
         const uint64_t rec = (~0ULL) / sum;
         // Pass 3: p, its four byte planes into shared memory (128-byte swizzle, K-major), P V.
-        uint32_t pph = 0;
         const uint32_t rsw = (uint32_t)(row & 7);
-        uint8_t* prow = sP + (row >> 3) * 1024 + (row & 7) * 128;
         for (int c = 0; c < nch; c++, it++) {
             const int sb = it & 1;
             mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 23);
             __syncwarp();
             tc_fence_after();
-            uint32_t pw[4][16];  // [plane][4-key word] for this thread's 64 keys
-#pragma unroll
-            for (int q2 = 0; q2 < 2; q2++) {
-                uint32_t v[32];
-                __syncwarp();
-                tmem_ld32(tbase + sb * KC + half * 64 + q2 * 32, v);
-                tmem_ld_wait();
-                const int j0 = c * KC + half * 64 + q2 * 32;
-#pragma unroll
-                for (int q = 0; q < 32; q++) {
-                    uint32_t p = 0;
-                    if (j0 + q <= rpos) {
-                        int64_t dd = M - score_of((int32_t)v[q], sm, ss, fast, hround);
-                        uint64_t x = (uint64_t)(uint32_t)sT[dd < last ? dd : last] << P;
-                        uint64_t qv = __umul64hi(x, rec);
-                        while ((qv + 1) * sum <= x) qv++;
-                        p = (uint32_t)qv;
-                    }
-                    const int w = (q2 * 32 + q) >> 2, sh = 8 * (q & 3);
-#pragma unroll
-                    for (int pl = 0; pl < 4; pl++) {
-                        uint32_t byte = (p >> (8 * pl)) & 255u;
-                        if ((q & 3) == 0) pw[pl][w] = byte;
-                        else pw[pl][w] |= byte << sh;
-                    }
-                }
-            }
+            uint32_t v[32];
+            tmem_ld32(tbase + sb * KC, v);
+            tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
-            // The previous chunk's P V must be done before the planes are overwritten.
-            mbar_wait(&bars->p_empty, pph ^ 1, err, 24);
+            const int j0 = c * KC + qt * 32;
+            uint32_t pw[4][8];  // [plane][4-key word] of this thread's 32 keys
+#pragma unroll
+            for (int q = 0; q < 32; q++) {
+                uint32_t p = 0;
+                if (j0 + q <= rpos) {
+                    uint64_t x = (uint64_t)(uint32_t)sT[dist_of<NARROW>(M, (int32_t)v[q], sm, ss, fast, hround, last)]
+                                 << P;
+                    uint64_t qv = __umul64hi(x, rec);  // floor(x / sum) - qv is 0, 1 or 2
+                    if ((qv + 1) * sum <= x) qv++;
+                    if ((qv + 1) * sum <= x) qv++;
+                    p = (uint32_t)qv;
+                }
+#pragma unroll
+                for (int pl = 0; pl < 4; pl++) {
+                    uint32_t byte = (p >> (8 * pl)) & 255u;
+                    if ((q & 3) == 0) pw[pl][q >> 2] = byte;
+                    else pw[pl][q >> 2] |= byte << (8 * (q & 3));
+                }
+            }
+            // The P V of chunk c - 2 (the same buffer) must be done before its planes are overwritten.
+            const int pb = c & 1;
+            mbar_wait(&bars->p_empty[pb], ((c >> 1) & 1) ^ 1, err, 24);
             __syncwarp();
+            uint8_t* prow = sP + pb * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
             for (int pl = 0; pl < 4; pl++) {
                 uint8_t* base = prow + pl * (GM * KC);
 #pragma unroll
-                for (int cc = 0; cc < 4; cc++) {
-                    const uint32_t chunk = (uint32_t)(half * 4 + cc);  // 16-byte chunk of the 128-byte row
+                for (int cc = 0; cc < 2; cc++) {
+                    const uint32_t chunk = (uint32_t)(qt * 2 + cc);  // 16-byte chunk of the 128-byte row
                     *reinterpret_cast<uint4*>(base + ((chunk ^ rsw) << 4)) =
                         make_uint4(pw[pl][4 * cc], pw[pl][4 * cc + 1], pw[pl][4 * cc + 2], pw[pl][4 * cc + 3]);
                 }
             }
             fence_proxy_async();
-            mbar_arrive(&bars->p_full);
-            pph ^= 1;
+            mbar_arrive(&bars->p_full[pb]);
         }
-        // O: acc = sum_k 2^(8k) O_k, then the output rescale.
+        // O: acc = sum_k 2^(8k) O_k for this thread's 16 channels, then the output rescale.
         mbar_wait(&bars->o_full, 0, err, 25);
         __syncwarp();
         tc_fence_after();
         const bool row_ok = row < (int)grp.count;
-        int32_t o[4][32];
+        uint32_t o[4][16];
 #pragma unroll
-        for (int pl = 0; pl < 4; pl++) {
-            __syncwarp();
-            tmem_ld32(tbase + 2 * KC + pl * HDIM + half * 32, reinterpret_cast<uint32_t(&)[32]>(o[pl]));
-        }
+        for (int pl = 0; pl < 4; pl++)
+            tmem_ld16(tmem + ((uint32_t)(g * 32) << 16) + 2 * KC + pl * HDIM + qt * 16, o[pl]);
         tmem_ld_wait();
         if (row_ok) {
-            uint32_t packed[8];
+            uint32_t packed[4];
 #pragma unroll
-            for (int q = 0; q < 32; q++) {
-                int64_t acc = ((((int64_t)o[3][q] * 256 + o[2][q]) * 256 + o[1][q]) * 256) + o[0][q];
+            for (int q = 0; q < 16; q++) {
+                int64_t acc = ((((int64_t)(int32_t)o[3][q] * 256 + (int32_t)o[2][q]) * 256 + (int32_t)o[1][q]) * 256) +
+                              (int32_t)o[0][q];
                 int8_t y = (int8_t)clamp128(rescale128(acc, om, (uint32_t)os), -127, 127);
                 if ((q & 3) == 0) packed[q >> 2] = (uint8_t)y;
                 else packed[q >> 2] |= (uint32_t)(uint8_t)y << (8 * (q & 3));
             }
-            uint4* dst = reinterpret_cast<uint4*>(att + (size_t)(grp.first_row + row) * lda + h * HDIM + half * 32);
-            dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-            dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            *reinterpret_cast<uint4*>(att + (size_t)(grp.first_row + row) * lda + h * HDIM + qt * 16) =
+                make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
         tc_fence_before();
     }
@@ -379,7 +400,9 @@ __global__ void __launch_bounds__(ATHREADS, 1)
 }  // namespace
 
 cudaError_t configure_attn_tc() {
-    return cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_attention_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_attention_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
 }
 
 bool attention_tc_supported(int hd, int n_ctx, int tlen) {
@@ -391,10 +414,15 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
                          const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st) {
     if (n_groups <= 0) return;
     dim3 grid(n_groups, H);
-    k_attention_tc<<<grid, ATHREADS, ASMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(tmQ),
-                                                  *reinterpret_cast<const CUtensorMap*>(tmK),
-                                                  *reinterpret_cast<const CUtensorMap*>(tmV), groups, L, layer, H,
-                                                  n_ctx, sm, ss, om, os, table, tlen, P, att, lda, err);
+    const CUtensorMap& q = *reinterpret_cast<const CUtensorMap*>(tmQ);
+    const CUtensorMap& k = *reinterpret_cast<const CUtensorMap*>(tmK);
+    const CUtensorMap& v = *reinterpret_cast<const CUtensorMap*>(tmV);
+    if (ss >= 21 && ss <= 62)
+        k_attention_tc<true><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os, table,
+                                                           tlen, P, att, lda, err);
+    else
+        k_attention_tc<false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os, table,
+                                                            tlen, P, att, lda, err);
 }
 
 }  // namespace hs

@@ -72,10 +72,14 @@ HS_HD u128 isqrt128(u128 x) {
     return res;
 }
 
+__device__ __forceinline__ double u128_to_double(u128 x) {
+    return (double)(uint64_t)(x >> 64) * 18446744073709551616.0 + (double)(uint64_t)x;
+}
+
 // floor(x / d) for a 128-bit x whose quotient fits in 64 bits, d >= 1: a double estimate and an
 // exact integer correction (the estimate is within a few units; each correction is exact).
 __device__ __forceinline__ uint64_t udiv128_small(u128 x, uint64_t d) {
-    double qd = (double)x / (double)d;
+    double qd = u128_to_double(x) / (double)d;
     uint64_t q = qd >= 18446744073709551615.0 ? ~0ULL : (uint64_t)qd;
     u128 qw = (u128)q * d;
     while (qw > x) {
@@ -87,6 +91,28 @@ __device__ __forceinline__ uint64_t udiv128_small(u128 x, uint64_t d) {
         qw += d;
     }
     return q;
+}
+
+// floor(x / d) for a 128-bit x and a 32-bit d >= 1, with three 64-bit divisions.
+__device__ __forceinline__ u128 udiv128_u32(u128 x, uint32_t d) {
+    uint64_t hi = (uint64_t)(x >> 64), lo = (uint64_t)x;
+    if (hi == 0) return lo / d;
+    uint64_t qh = hi / d, r = hi % d;
+    uint64_t t1 = (r << 32) | (lo >> 32);
+    uint64_t q1 = t1 / d;
+    r = t1 % d;
+    uint64_t t0 = (r << 32) | (lo & 0xFFFFFFFFull);
+    uint64_t q0 = t0 / d;
+    return ((u128)qh << 64) | ((u128)q1 << 32) | q0;
+}
+
+// floor(sqrt(x)) for x < 2^100: the double square root as an estimate, then exact integer
+// corrections (int.rs:213 isqrt_u128 defines the value).
+__device__ __forceinline__ uint64_t isqrt_u128_fast(u128 x) {
+    uint64_t r = (uint64_t)sqrt(u128_to_double(x));
+    while ((u128)r * r > x) r--;
+    while ((u128)(r + 1) * (r + 1) <= x) r++;
+    return r;
 }
 
 // ---- sm_100a PTX wrappers ----

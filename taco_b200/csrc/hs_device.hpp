@@ -14,6 +14,8 @@ constexpr int TILE_K = 128;
 constexpr int LOGIT_TILE = 256;
 // The largest logit table the coder op keeps in shared memory (entries).
 constexpr int MAX_LOGIT_TABLE = 16384;
+// The largest vocabulary of the coder op (8 warps x 32 steps x 256 symbols).
+constexpr int MAX_CODER_VOCAB = 65536;
 // The largest context the attention kernels hold in shared memory (scores of one row).
 constexpr int MAX_ATTN_CTX = 8192;
 
@@ -70,6 +72,8 @@ enum EpiMode : int {
     EPI_DELTA = 5,   // out32[r, n] = clamp(rescale(acc + b[n], m[n], s), i32); the residual add and its
                      // clamp to [-R, R] happen in the next LayerNorm kernel: clamping the delta to the
                      // i32 range first gives the same result, because |x| <= R < 2^30.
+    EPI_QKV = 6,     // as EPI_ACT; q (columns < d) to out8, k to the keys cache and v to the
+                     // transposed values cache at the row's (slot, pos) (reference.rs:241-246)
 };
 
 struct EpiArgs {
@@ -89,6 +93,11 @@ struct EpiArgs {
     int ldt;
     int last;
     int32_t* out32;
+    // EPI_QKV: the rows of the pass and the caches of this layer.
+    const RowInfo* rows;
+    int8_t* kc;
+    int8_t* vc;
+    int L, layer, H, hd, n_ctx, d;
 };
 
 }  // namespace hs

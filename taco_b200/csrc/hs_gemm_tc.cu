@@ -63,6 +63,19 @@ __device__ __forceinline__ int64_t rescale_fast(uint32_t acc, int32_t m, int64_t
     return rescale64((int64_t)(int32_t)acc + c, m, (uint32_t)s);
 }
 
+// EPI_QKV: one value at column n of a row of (slot, pos): q to out8, k and v to the caches.
+__device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowInfo& ri, int n, int8_t o) {
+    if (n < e.d) {
+        e.out8[(size_t)row * e.ldo + n] = o;
+        return;
+    }
+    const int j = n < 2 * e.d ? n - e.d : n - 2 * e.d;
+    const int h = j / e.hd, c = j - h * e.hd;
+    const size_t head = ((size_t)ri.slot * e.L + e.layer) * e.H + h;
+    if (n < 2 * e.d) e.kc[(head * e.n_ctx + ri.pos) * e.hd + c] = o;
+    else e.vc[(head * e.hd + c) * e.n_ctx + ri.pos] = o;
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int MT, int NT,
@@ -265,7 +278,39 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int colb = col0 + c0;
                     if (!row_ok || colb >= e.N) continue;
                     const bool full = colb + 32 <= e.N;
-                    if (MODE == EPI_ACT || MODE == EPI_GELU) {
+                    if (MODE == EPI_QKV) {
+                        const RowInfo ri = e.rows[row];
+                        int8_t o[32];
+#pragma unroll
+                        for (int q = 0; q < 32; q++) o[q] = (int8_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), -127, 127);
+                        if (full && colb + 32 <= e.d && (e.ldo & 15) == 0) {
+                            // A whole 32-byte run of q.
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                pk[q] = (uint32_t)(uint8_t)o[4 * q] | (uint32_t)(uint8_t)o[4 * q + 1] << 8 |
+                                        (uint32_t)(uint8_t)o[4 * q + 2] << 16 | (uint32_t)(uint8_t)o[4 * q + 3] << 24;
+                            uint4* dst = reinterpret_cast<uint4*>(e.out8 + (size_t)row * e.ldo + colb);
+                            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        } else if (full && (e.hd & 31) == 0 && (e.d & 31) == 0 && colb >= e.d && colb < 2 * e.d) {
+                            // A whole 32-byte run of one key row.
+                            const int j = colb - e.d, h = j / e.hd, c = j - h * e.hd;
+                            const size_t head = ((size_t)ri.slot * e.L + e.layer) * e.H + h;
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                pk[q] = (uint32_t)(uint8_t)o[4 * q] | (uint32_t)(uint8_t)o[4 * q + 1] << 8 |
+                                        (uint32_t)(uint8_t)o[4 * q + 2] << 16 | (uint32_t)(uint8_t)o[4 * q + 3] << 24;
+                            uint4* dst = reinterpret_cast<uint4*>(e.kc + (head * e.n_ctx + ri.pos) * e.hd + c);
+                            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 32; q++)
+                                if (colb + q < e.N) qkv_store(e, row, ri, colb + q, o[q]);
+                        }
+                    } else if (MODE == EPI_ACT || MODE == EPI_GELU) {
                         uint32_t packed[8];
 #pragma unroll
                         for (int q = 0; q < 8; q++) packed[q] = 0;
@@ -347,6 +392,7 @@ cudaError_t configure_tc_kernels() {
     if ((e = configure_mode<EPI_GELU>()) != cudaSuccess) return e;
     if ((e = configure_mode<EPI_LOGITS>()) != cudaSuccess) return e;
     if ((e = configure_mode<EPI_RAW>()) != cudaSuccess) return e;
+    if ((e = configure_mode<EPI_QKV>()) != cudaSuccess) return e;
     return configure_mode<EPI_DELTA>();
 }
 
@@ -362,6 +408,7 @@ void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, i
         case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
         case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
         case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
         default: break;
     }
 }

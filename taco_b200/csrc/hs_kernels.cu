@@ -169,10 +169,11 @@ __global__ void __launch_bounds__(256) k_resid_ln(int32_t* x, const int32_t* del
         hi += hi2 + (lo < lo2 ? 1 : 0);
     }
     const u128 sum_sq = ((u128)hi << 64) | lo;
-    const u128 var = sum_sq / (u128)d;
-    u128 root = isqrt128((var << (2 * ln_j)) + (u128)eps);
+    const u128 var = udiv128_u32(sum_sq, (uint32_t)d);  // var < 2^64 (layernorm.rs bounds)
+    const u128 sq_arg = (var << (2 * ln_j)) + (u128)eps;  // < 2^97
+    uint64_t root = isqrt_u128_fast(sq_arg);
     if (root < 1) root = 1;
-    const i128 inv = (i128)(((u128)1 << ln_k) / root);
+    const i128 inv = (i128)((1ULL << ln_k) / root);     // 2^K <= 2^48
     const i128 u = inv * (i128)ln.m;  // |u| < 2^80
     const int s = ln.s;
 #pragma unroll
@@ -216,6 +217,18 @@ __device__ __forceinline__ void epi_store(int mode, const EpiArgs& e, int r, int
         *xp = (int32_t)clamp64((int64_t)*xp + y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
     } else if (mode == EPI_DELTA) {
         e.out32[(size_t)r * e.ldo + n] = (int32_t)clamp64(y, INT32_MIN, INT32_MAX);
+    } else if (mode == EPI_QKV) {
+        int8_t o = (int8_t)clamp64(y, -127, 127);
+        const RowInfo ri = e.rows[r];
+        if (n < e.d) {
+            e.out8[(size_t)r * e.ldo + n] = o;
+        } else {
+            const int j = n < 2 * e.d ? n - e.d : n - 2 * e.d;
+            const int h = j / e.hd, c = j - h * e.hd;
+            const size_t head = ((size_t)ri.slot * e.L + e.layer) * e.H + h;
+            if (n < 2 * e.d) e.kc[(head * e.n_ctx + ri.pos) * e.hd + c] = o;
+            else e.vc[(head * e.hd + c) * e.n_ctx + ri.pos] = o;
+        }
     }
 }
 
@@ -495,113 +508,195 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention_vec(const RowInfo* ro
 
 // ---- the coder op (crates/taco-coder/src/freq.rs:103 from_weights, interval.rs:82-100) ----
 
-constexpr int CODER_THREADS = 512;
+constexpr int CODER_THREADS = 256;
 constexpr int CODER_WARPS = CODER_THREADS / 32;
+constexpr int CODER_MAX_STEPS = 32;  // steps of 256 symbols per warp: V <= 8 * 32 * 256 = 65536
 
+// One block per row. d16 is read as groups of 8 symbols (one 16-byte load); warp w owns the
+// groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step). The
+// coder answer walks warp -> step -> lane -> symbol, each level a parallel scan.
 __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
                                                          int R, int V, const uint64_t* table, int tlen, uint32_t bits,
                                                          const RowInfo* rows, uint64_t* out) {
-    extern __shared__ uint32_t F[];  // tlen entries: 1 + floor(table[j] * spare / W)
+    extern __shared__ __align__(16) uint32_t F[];  // 1 + floor(table[j] * spare / W), j <= dmax
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
     __shared__ uint64_t wsum[CODER_WARPS];
+    __shared__ uint64_t steps[CODER_WARPS][CODER_MAX_STEPS];
     __shared__ int s_largest;
-    int r = blockIdx.x;
+    const int r = blockIdx.x;
     if (r >= R) return;
     const uint16_t* dr = d16 + (size_t)r * ldd;
     const int64_t* tr = tmax + (size_t)r * ldt;
-    int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
-    int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t last = tlen - 1;
+    const uint64_t total = 1ULL << bits;
+    const uint64_t spare = total - (uint64_t)V;
+    const int ng = (V + 7) / 8;
     // The row max.
     int64_t mx = INT64_MIN;
     for (int t = threadIdx.x; t < VT; t += CODER_THREADS) mx = tr[t] > mx ? tr[t] : mx;
     mx = block_max64(mx, red);
-    // Pass 1: W = sum(w) and the largest weight (freq.rs:112-121).
+    // Pass 1: W = sum(w), the largest weight and the largest distance (freq.rs:112-121).
     uint64_t W = 0, wmax = 0;
-    for (int v = threadIdx.x; v < V; v += CODER_THREADS) {
-        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
-        uint64_t wv = table[dd < last ? dd : last];
-        W += wv;
-        wmax = wv > wmax ? wv : wmax;
+    int64_t dmax = 0;
+    for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
+        const int v0 = 8 * gi;
+        const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+        const int64_t off = mx - tr[v0 / LOGIT_TILE];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            if (v0 + i < V) {
+                int64_t dd = off + (int64_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
+                dd = dd < last ? dd : last;
+                uint64_t wv = table[dd];
+                W += wv;
+                wmax = wv > wmax ? wv : wmax;
+                dmax = dd > dmax ? dd : dmax;
+            }
+        }
     }
     W = block_sum64(W, redu);
     wmax = (uint64_t)block_max64((int64_t)wmax, red);
+    dmax = block_max64(dmax, red);
     // The lowest id with the largest weight.
     if (threadIdx.x == 0) s_largest = V;
     __syncthreads();
-    for (int v = threadIdx.x; v < V; v += CODER_THREADS) {
-        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
-        uint64_t wv = table[dd < last ? dd : last];
-        if (wv == wmax) {
-            atomicMin(&s_largest, v);
+    for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
+        const int v0 = 8 * gi;
+        const int64_t off = mx - tr[v0 / LOGIT_TILE];
+        int found = -1;
+        for (int i = 0; i < 8 && v0 + i < V; i++) {
+            int64_t dd = off + (int64_t)dr[v0 + i];
+            if (table[dd < last ? dd : last] == wmax) {
+                found = v0 + i;
+                break;
+            }
+        }
+        if (found >= 0) {
+            atomicMin(&s_largest, found);
             break;
         }
     }
     __syncthreads();
-    bool all_zero = W == 0;
-    int largest = all_zero ? 0 : s_largest;
-    uint64_t total = 1ULL << bits;
-    uint64_t spare = total - (uint64_t)V;
-    uint32_t f_flat = (uint32_t)(1 + spare / (uint64_t)V);  // all-zero rule: every weight is 1
+    const bool all_zero = W == 0;
+    const int largest = all_zero ? 0 : s_largest;
+    const uint32_t f_flat = (uint32_t)(1 + spare / (uint64_t)V);  // all-zero rule: every weight is 1
+    // F for the distances that occur in this row (every table entry is <= wmax <= W, so the quotient
+    // is below 2^32).
     if (!all_zero)
-        for (int j = threadIdx.x; j < tlen; j += CODER_THREADS)
-            F[j] = (uint32_t)(1 + udiv128_small((u128)table[j] * spare, W));
+        for (int j = threadIdx.x; j <= dmax; j += CODER_THREADS) F[j] = (uint32_t)(1 + udiv128_small((u128)table[j] * spare, W));
     __syncthreads();
-    // Pass 2: per warp, the sum of f over its contiguous range of symbols.
-    int per = (V + CODER_WARPS - 1) / CODER_WARPS;
-    int a = w * per, b = min(V, a + per);
-    uint64_t s = 0;
-    for (int v = a + lane; v < b; v += 32) {
-        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
-        s += all_zero ? f_flat : F[dd < last ? dd : last];
+    // f of one group of 8 symbols (0 past V).
+    auto group_f = [&](int gi, uint32_t (&f)[8]) {
+        const int v0 = 8 * gi;
+        const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+        const int64_t off = mx - tr[v0 / LOGIT_TILE];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            f[i] = 0;
+            if (v0 + i < V) {
+                int64_t dd = off + (int64_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
+                f[i] = all_zero ? f_flat : F[dd < last ? dd : last];
+            }
+        }
+    };
+    // Pass 2: per warp and step (32 groups), the sum of f.
+    const int gpw = (ng + CODER_WARPS - 1) / CODER_WARPS;
+    const int ga = min(ng, w * gpw), gb = min(ng, ga + gpw);
+    const int nsteps = (gb - ga + 31) / 32;
+    uint64_t wtotal = 0;
+    for (int k = 0; k < nsteps; k++) {
+        const int gi = ga + 32 * k + lane;
+        uint64_t s = 0;
+        if (gi < gb) {
+            uint32_t f[8];
+            group_f(gi, f);
+#pragma unroll
+            for (int i = 0; i < 8; i++) s += f[i];
+        }
+        s = warp_sum64(s);
+        if (lane == 0) steps[w][k] = s;
+        wtotal += s;
     }
-    s = warp_sum64(s);
-    if (lane == 0) wsum[w] = s;
+    if (lane == 0) wsum[w] = wtotal;
     __syncthreads();
     uint64_t before = 0, sum_f = 0;
     for (int i = 0; i < CODER_WARPS; i++) {
         if (i < w) before += wsum[i];
         sum_f += wsum[i];
     }
-    uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
-    RowInfo q = rows[r];
-    // A(v): the start of symbol v; A(a) of this warp and A(b) (A(V) = total).
-    uint64_t Aa = before + ((uint64_t)a > (uint64_t)largest ? rem : 0);
-    uint64_t Ab = b >= V ? total : before + wsum[w] + ((uint64_t)b > (uint64_t)largest ? rem : 0);
+    const uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
+    const RowInfo q = rows[r];
+    const int a = 8 * ga, b = min(V, 8 * gb);
+    // A(v) = sum of f below v + (rem if v > largest): the start of symbol v.
+    auto adj = [&](int v) -> uint64_t { return (uint64_t)v > (uint64_t)largest ? rem : 0; };
+    const uint64_t Aa = before + adj(a);
+    const uint64_t Ab = b >= V ? total : before + wtotal + adj(b);
     bool mine;
     if (q.kind == 0) mine = (int64_t)q.value >= a && (int64_t)q.value < b;
     else mine = a < b && q.value >= Aa && q.value < Ab;
     if (!mine) return;
-    // This warp owns the answer: walk its range 32 symbols at a time.
-    uint64_t base = before;  // sum of f below the current step, without the remainder
-    for (int v0 = a; v0 < b; v0 += 32) {
-        int v = v0 + lane;
-        uint64_t f = 0;
-        if (v < b) {
-            int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
-            f = all_zero ? f_flat : F[dd < last ? dd : last];
-        }
-        uint64_t incl = f;
-        for (int o = 1; o < 32; o <<= 1) {
-            uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
-        }
-        uint64_t start = base + incl - f + ((uint64_t)v > (uint64_t)largest ? rem : 0);
-        uint64_t freq = f + (v == largest ? rem : 0);
-        bool hit;
-        if (q.kind == 0) hit = v < b && (uint64_t)v == q.value;
-        else hit = v < b && q.value >= start && q.value < start + freq;
-        unsigned m = __ballot_sync(0xffffffffu, hit);
-        if (m) {
-            if (lane == __ffs(m) - 1) {
-                out[3 * (size_t)r] = (uint64_t)v;
-                out[3 * (size_t)r + 1] = start;
-                out[3 * (size_t)r + 2] = freq;
-            }
+    // Level 1: the step. Lane k holds the exclusive prefix of the step sums.
+    uint64_t st = lane < nsteps ? steps[w][lane] : 0;
+    uint64_t incl = st;
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint64_t excl = incl - st;
+    int kstep;
+    if (q.kind == 0) {
+        kstep = ((int)q.value / 8 - ga) / 32;
+    } else {
+        // The last step whose start is <= target (starts include rem past the largest symbol).
+        const int v0 = 8 * (ga + 32 * lane);
+        const bool ok = lane < nsteps && before + excl + adj(v0) <= q.value;
+        const unsigned m = __ballot_sync(0xffffffffu, ok);
+        kstep = 31 - __clz(m);
+    }
+    const uint64_t step_base = before + __shfl_sync(0xffffffffu, excl, kstep);
+    // Level 2: the lane (group of 8) within the step.
+    const int gi = ga + 32 * kstep + lane;
+    uint32_t f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (gi < gb) group_f(gi, f);
+    uint64_t gs = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) gs += f[i];
+    uint64_t ginc = gs;
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t t = __shfl_up_sync(0xffffffffu, ginc, o);
+        if (lane >= o) ginc += t;
+    }
+    const uint64_t gstart = step_base + ginc - gs;  // sum of f below this group (no rem)
+    int owner;
+    if (q.kind == 0) {
+        owner = ((int)q.value / 8 - ga) % 32;
+    } else {
+        const bool ok = gi < gb && gstart + adj(8 * gi) <= q.value;
+        const unsigned m = __ballot_sync(0xffffffffu, ok);
+        owner = 31 - __clz(m);
+    }
+    if (lane != owner) return;
+    // Level 3: the symbol within the group (this lane).
+    uint64_t acc = gstart;
+#pragma unroll 1
+    for (int i = 0; i < 8; i++) {
+        const int v = 8 * gi + i;
+        if (v >= V) break;
+        const uint64_t start = acc + adj(v);
+        const uint64_t freq = f[i] + (v == largest ? rem : 0);
+        const bool hit = q.kind == 0 ? (uint64_t)v == q.value : (q.value >= start && q.value < start + freq);
+        if (hit) {
+            out[3 * (size_t)r] = (uint64_t)v;
+            out[3 * (size_t)r + 1] = start;
+            out[3 * (size_t)r + 2] = freq;
             return;
         }
-        base += __shfl_sync(0xffffffffu, incl, 31);
+        acc += f[i];
     }
 }
 

@@ -324,11 +324,17 @@ int forward(hs_batch* b, int R) {
         e.s = qkv.ld.s;
         e.out8 = b->qkv;
         e.ldo = c.QKVp;
-        gemm(OP_GEMM_QKV, EPI_ACT, b->a, c.Dp, &b->tm_a, qkv, e);
-        {
-            ProfScope p(b, OP_KV, 0);
-            launch_kv_store(b->d_rows, R, b->qkv, c.QKVp, c.d, c.H, c.hd, c.L, l, c.n_ctx, b->kc, b->vc, st);
-        }
+        // q to the qkv buffer, k and v straight into the caches of this layer (no separate store).
+        e.rows = b->d_rows;
+        e.kc = b->kc;
+        e.vc = b->vc;
+        e.L = c.L;
+        e.layer = l;
+        e.H = c.H;
+        e.hd = c.hd;
+        e.n_ctx = c.n_ctx;
+        e.d = c.d;
+        gemm(OP_GEMM_QKV, EPI_QKV, b->a, c.Dp, &b->tm_a, qkv, e);
         {
             ProfScope p(b, OP_ATTN, attn_ops);
             launch_attention_tc(&b->tm_q, &b->tm_k, &b->tm_v, b->d_groups, b->n_groups, c.L, l, c.H, c.n_ctx,
@@ -662,6 +668,8 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
         return fail(HS_UNSUPPORTED, "hsm format version 2 rules (i16 activations, ln_beta_frac) are not run by "
                                     "this backend yet");
     if (M.vocab < 2) return fail(HS_UNSUPPORTED, "the vocabulary needs at least 2 tokens");
+    if (M.vocab > MAX_CODER_VOCAB)
+        return fail(HS_UNSUPPORTED, "the coder op of this backend takes at most 65536 tokens");
     if ((int)M.logits_exp.size() > MAX_LOGIT_TABLE)
         return fail(HS_UNSUPPORTED, "the logit table is longer than 16384 entries");
     if (M.n_ctx > MAX_ATTN_CTX) return fail(HS_UNSUPPORTED, "the context is longer than 8192 positions");
