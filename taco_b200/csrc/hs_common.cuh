@@ -76,6 +76,15 @@ __device__ __forceinline__ double u128_to_double(u128 x) {
     return (double)(uint64_t)(x >> 64) * 18446744073709551616.0 + (double)(uint64_t)x;
 }
 
+__device__ __forceinline__ double u128_to_double_signed(i128 x) {
+    return x < 0 ? -u128_to_double((u128)(-x)) : u128_to_double((u128)x);
+}
+
+// 2^-s as a double (exact for 0 <= s <= 1022).
+__device__ __forceinline__ double exp2_neg(int s) {
+    return __longlong_as_double((long long)(1023 - s) << 52);
+}
+
 // floor(x / d) for a 128-bit x whose quotient fits in 64 bits, d >= 1: a double estimate and an
 // exact integer correction (the estimate is within a few units; each correction is exact).
 __device__ __forceinline__ uint64_t udiv128_small(u128 x, uint64_t d) {

@@ -40,10 +40,13 @@ constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int GELU_SMEM = 65536;
 
+constexpr int VT_STRIDE = 36;                  // bytes per row of a warp's 32 x 32 transpose tile
+constexpr int VT_TILE = 32 * VT_STRIDE;
+
 template <int MODE>
 struct Cfg {
     static constexpr int STAGES = MODE == EPI_GELU ? 3 : 4;
-    static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : 0;
+    static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : (MODE == EPI_QKV ? EPI_WARPS * VT_TILE : 0);
     static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + EXTRA + 2 * BN * 12 + 2 * 2 * BM * 8 + 256 + 1024;
 };
 
@@ -212,6 +215,21 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_after();
             const int row = mt * BM + row_in_tile;
             const bool row_ok = row < e.R;
+            // EPI_QKV: are this warp's 32 rows 32 consecutive positions of one slot, starting at a
+            // multiple of 16 (the transposed v store)? Warp-uniform.
+            bool vt_ok = false;
+            uint32_t vt_slot = 0, vt_pos0 = 0;
+            if (MODE == EPI_QKV) {
+                const int r0 = mt * BM + g * 32;
+                if (r0 + 31 < e.R && (e.n_ctx & 15) == 0) {
+                    const RowInfo a0 = e.rows[r0], a1 = e.rows[r0 + 31];
+                    const RowInfo me = e.rows[row];
+                    const bool mine_ok = me.slot == a0.slot && me.pos == a0.pos + (uint32_t)lane;
+                    vt_ok = __all_sync(0xffffffffu, mine_ok) && a1.slot == a0.slot && (a0.pos & 15) == 0;
+                    vt_slot = a0.slot;
+                    vt_pos0 = a0.pos;
+                }
+            }
             const uint32_t taddr = tmem_base + ((uint32_t)(g * 32) << 16) + (uint32_t)(acc * BN);
             const int32_t* pm = s_m + acc * BN;
             const int64_t* pc = s_c + acc * BN;
@@ -303,6 +321,30 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 pk[q] = (uint32_t)(uint8_t)o[4 * q] | (uint32_t)(uint8_t)o[4 * q + 1] << 8 |
                                         (uint32_t)(uint8_t)o[4 * q + 2] << 16 | (uint32_t)(uint8_t)o[4 * q + 3] << 24;
                             uint4* dst = reinterpret_cast<uint4*>(e.kc + (head * e.n_ctx + ri.pos) * e.hd + c);
+                            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        } else if (full && vt_ok && colb >= 2 * e.d) {
+                            // 32 channels of v for 32 consecutive positions: transpose the 32 x 32
+                            // bytes through shared memory, then each lane writes one channel's 32
+                            // positions (two 16-byte stores into the transposed values cache).
+                            uint8_t* tile = reinterpret_cast<uint8_t*>(s_gelu) + (warp - 2) * VT_TILE;
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                *reinterpret_cast<uint32_t*>(tile + lane * VT_STRIDE + 4 * q) =
+                                    (uint32_t)(uint8_t)o[4 * q] | (uint32_t)(uint8_t)o[4 * q + 1] << 8 |
+                                    (uint32_t)(uint8_t)o[4 * q + 2] << 16 | (uint32_t)(uint8_t)o[4 * q + 3] << 24;
+                            __syncwarp();
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                pk[q] = (uint32_t)tile[(4 * q) * VT_STRIDE + lane] |
+                                        (uint32_t)tile[(4 * q + 1) * VT_STRIDE + lane] << 8 |
+                                        (uint32_t)tile[(4 * q + 2) * VT_STRIDE + lane] << 16 |
+                                        (uint32_t)tile[(4 * q + 3) * VT_STRIDE + lane] << 24;
+                            __syncwarp();
+                            const int j = colb - 2 * e.d + lane, h = j / e.hd, c = j - h * e.hd;
+                            const size_t head = ((size_t)vt_slot * e.L + e.layer) * e.H + h;
+                            uint4* dst = reinterpret_cast<uint4*>(e.vc + (head * e.hd + c) * e.n_ctx + vt_pos0);
                             dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                             dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                         } else {

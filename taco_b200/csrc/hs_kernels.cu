@@ -176,20 +176,42 @@ __global__ void __launch_bounds__(256) k_resid_ln(int32_t* x, const int32_t* del
     const i128 inv = (i128)((1ULL << ln_k) / root);     // 2^K <= 2^48
     const i128 u = inv * (i128)ln.m;  // |u| < 2^80
     const int s = ln.s;
+    // The estimate t ~ cg * u / 2^s in double: cg is exact (|cg| < 2^47) and ud has a relative
+    // error of at most 2^-53, so for |t| < 2^20 the estimate of t + 1/2 is within 2^-31 of the
+    // exact value and its floor is exact unless the fraction is within 2^-30 of an integer. Those
+    // values, |t| >= 2^20, and the beta_frac form take the exact 128-bit rule below.
+    const bool est_ok = ln.beta_frac == 0 && s <= 126;
+    const double ud = u128_to_double_signed(u) * exp2_neg(s);
 #pragma unroll
     for (int i = 0; i < RPL; i++) {
         int j = lane + 32 * i;
         if (j >= d) continue;
         int64_t cg = ((int64_t)v[i] - mean) * (int64_t)ln.g[j];  // |cg| < 2^47
-        i128 p = (i128)cg * u;                                     // t * m, |p| < 2^126
-        i128 y;
-        if (ln.beta_frac == 0) {
-            y = shift_round128(p, s, 126) + (i128)ln.b[j];
-        } else {
-            i128 cb = (i128)ln.b[j] << (s - ln.beta_frac);
-            y = shift_round128((i128)((u128)p + (u128)cb), s, 126);
+        int64_t yv;
+        bool done = false;
+        if (est_ok) {
+            const double z = fma((double)cg, ud, 0.5);
+            if (fabs(z) < 1048576.0) {
+                const double fl = floor(z);
+                const double fr = z - fl;
+                if (fr > 9.313225746154785e-10 && fr < 1.0 - 9.313225746154785e-10) {
+                    yv = (int64_t)fl + (int64_t)ln.b[j];
+                    done = true;
+                }
+            }
         }
-        out[(size_t)r * ldo + j] = (int8_t)clamp128(y, -127, 127);
+        if (!done) {
+            i128 p = (i128)cg * u;  // t * m, |p| < 2^126
+            i128 y;
+            if (ln.beta_frac == 0) {
+                y = shift_round128(p, s, 126) + (i128)ln.b[j];
+            } else {
+                i128 cb = (i128)ln.b[j] << (s - ln.beta_frac);
+                y = shift_round128((i128)((u128)p + (u128)cb), s, 126);
+            }
+            yv = clamp128(y, -127, 127);
+        }
+        out[(size_t)r * ldo + j] = (int8_t)clamp64(yv, -127, 127);
     }
 }
 
