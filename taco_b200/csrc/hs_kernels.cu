@@ -126,7 +126,7 @@ __global__ void k_layernorm(const int32_t* x, int R, int d, LnDev ln, int ln_k, 
 // 128-bit value, so an output costs one 64 x 128-bit product, a shift and a clamp. The row stays in
 // registers (RPL values per lane).
 template <int RPL>
-__global__ void __launch_bounds__(256) k_resid_ln(int32_t* x, const int32_t* delta, int R, int d, LnDev ln, int ln_k,
+__global__ void __launch_bounds__(256, RPL <= 32 ? 4 : 1) k_resid_ln(int32_t* x, const int32_t* delta, int R, int d, LnDev ln, int ln_k,
                                                   int ln_j, uint64_t eps, int8_t* out, int ldo) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
@@ -561,8 +561,11 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     for (int t = threadIdx.x; t < VT; t += CODER_THREADS) mx = tr[t] > mx ? tr[t] : mx;
     mx = block_max64(mx, red);
     // Pass 1: W = sum(w), the largest weight and the largest distance (freq.rs:112-121).
+    // Each thread visits its symbols in increasing order, so its first symbol with its largest
+    // weight is its lowest such id; the block reduces (max weight, then min id).
     uint64_t W = 0, wmax = 0;
     int64_t dmax = 0;
+    int best = V;
     for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
         const int v0 = 8 * gi;
         const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
@@ -575,33 +578,22 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
                 dd = dd < last ? dd : last;
                 uint64_t wv = table[dd];
                 W += wv;
-                wmax = wv > wmax ? wv : wmax;
+                if (wv > wmax || best == V) {
+                    wmax = wv;
+                    best = v0 + i;
+                }
                 dmax = dd > dmax ? dd : dmax;
             }
         }
     }
     W = block_sum64(W, redu);
-    wmax = (uint64_t)block_max64((int64_t)wmax, red);
+    const uint64_t my_w = best < V ? wmax : 0;
+    wmax = (uint64_t)block_max64((int64_t)my_w, red);
     dmax = block_max64(dmax, red);
     // The lowest id with the largest weight.
     if (threadIdx.x == 0) s_largest = V;
     __syncthreads();
-    for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
-        const int v0 = 8 * gi;
-        const int64_t off = mx - tr[v0 / LOGIT_TILE];
-        int found = -1;
-        for (int i = 0; i < 8 && v0 + i < V; i++) {
-            int64_t dd = off + (int64_t)dr[v0 + i];
-            if (table[dd < last ? dd : last] == wmax) {
-                found = v0 + i;
-                break;
-            }
-        }
-        if (found >= 0) {
-            atomicMin(&s_largest, found);
-            break;
-        }
-    }
+    if (best < V && my_w == wmax) atomicMin(&s_largest, best);
     __syncthreads();
     const bool all_zero = W == 0;
     const int largest = all_zero ? 0 : s_largest;
