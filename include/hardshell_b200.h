@@ -135,6 +135,19 @@ int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, co
                      const int32_t* mult, uint32_t shift, uint32_t M, uint32_t N, uint32_t K, int8_t* out8,
                      int32_t* raw32);
 
+/* No counterpart in the reference: hs_op_linear_act for callers that cannot allocate device
+ * memory at call time (another allocator owns the rest of HBM, or cudaFree's device-wide
+ * synchronisation would stall their other streams). Same arguments, results and errors, but the
+ * padded operands, parameters and result are staged in one static __device__ array of
+ * HS_STATIC_SCRATCH_BYTES per GPU (held until exit); shapes that need more are refused with
+ * HS_UNSUPPORTED. It calls no cudaMalloc or cudaFree. The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress): make it before any stream capture. Calls share the
+ * array, so calls that overlap on one GPU race: serialise them. */
+#define HS_STATIC_SCRATCH_BYTES (32u << 20)
+int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, const int8_t* W, const int32_t* bias,
+                             const int32_t* mult, uint32_t shift, uint32_t M, uint32_t N, uint32_t K, int8_t* out8,
+                             int32_t* raw32);
+
 /* A device-resident GEMM benchmark: the same op on device buffers it allocates, with inputs
  * from a seed, timed with CUDA events over `iters` launches after `warmup`. Fills the mean
  * launch time in microseconds. For bench.py. */

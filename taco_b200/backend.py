@@ -90,6 +90,7 @@ def lib() -> ctypes.CDLL:
     L.hs_batch_run_weights.argtypes = [vp, vp, vp, u32, vp]
     L.hs_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
+    L.hs_op_linear_act_noalloc.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_bench.argtypes = [vp, i32, u32, u32, u32, u64, i32, i32, ctypes.POINTER(ctypes.c_double)]
     L.hs_batch_set_profiling.argtypes = [vp, i32]
     L.hs_batch_profile.argtypes = [vp, vp, i32]
@@ -166,6 +167,26 @@ class CudaDevice:
         out = np.zeros((M, N), dtype=np.int32)
         _check(lib().hs_op_linear_act(self.h, 0 if path == "tc" else 1, _p(A), _p(W), None, None, 0, M, N, K, None,
                                       _p(out)))
+        return out
+
+    def linear_act_noalloc(self, A: np.ndarray, W: np.ndarray, bias: np.ndarray | None, mult: np.ndarray | None,
+                           shift: int, path: str = "tc", raw: bool = False) -> np.ndarray:
+        """linear_act (or matmul_raw with raw=True) through the entry point that stages everything in
+        the library's static device array instead of allocating (HS_STATIC_SCRATCH_BYTES)."""
+        A = np.ascontiguousarray(A, dtype=np.int8)
+        W = np.ascontiguousarray(W, dtype=np.int8)
+        M, K = A.shape
+        N = W.shape[0]
+        if raw:
+            out = np.zeros((M, N), dtype=np.int32)
+            _check(lib().hs_op_linear_act_noalloc(self.h, 0 if path == "tc" else 1, _p(A), _p(W), None, None, 0,
+                                                  M, N, K, None, _p(out)))
+            return out
+        b = np.ascontiguousarray(bias, dtype=np.int32)
+        m = np.ascontiguousarray(mult, dtype=np.int32)
+        out = np.zeros((M, N), dtype=np.int8)
+        _check(lib().hs_op_linear_act_noalloc(self.h, 0 if path == "tc" else 1, _p(A), _p(W), _p(b), _p(m), shift,
+                                              M, N, K, _p(out), None))
         return out
 
     def linear_bench(self, M: int, N: int, K: int, seed: int = 1, warmup: int = 3, iters: int = 20,
