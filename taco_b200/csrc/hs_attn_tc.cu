@@ -313,7 +313,16 @@ __global__ void __launch_bounds__(ATHREADS, 1)
 #pragma unroll
         for (int o = 0; o < 4; o++) sum += (uint64_t)sX[o * GM + row];
         if (sum == 0) sum = 1;
-        const uint64_t rec = (~0ULL) / sum;
+        // p = floor(e * 2^P / sum) for every e < 2^31 as floor(e * mg / 2^(31 + l)): the numerators
+        // e * 2^P have N = 31 + P <= 61 bits, 2^l >= sum and mg = ceil(2^(N + l) / sum) <= 2^(N + 1),
+        // so the quotient is exact (Granlund and Montgomery, "Division by invariant integers using
+        // multiplication", 1994, Theorem 4.2). With mg = mh 2^32 + ml and u = e mh + (e ml >> 32),
+        // p = u >> (l - 1): two 32x32 multiplies per key.
+        int l = 64 - __clzll((long long)(sum - 1));
+        if (l < 1) l = 1;
+        const uint64_t mg = (uint64_t)((((u128)1 << (31 + P + l)) + (sum - 1)) / sum);
+        const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
+        const int psh = l - 1;
         // Pass 3: p, its four byte planes into shared memory (128-byte swizzle, K-major), P V.
         const uint32_t rsw = (uint32_t)(row & 7);
         for (int c = 0; c < nch; c++, it++) {
@@ -327,24 +336,32 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
             const int j0 = c * KC + qt * 32;
+            auto prob = [&](int32_t dot) -> uint32_t {
+                const uint32_t e = (uint32_t)sT[dist_of<NARROW>(M, dot, sm, ss, fast, hround, last)];
+                const uint64_t t = (uint64_t)e * ml;
+                const uint64_t u = (uint64_t)e * mh + (t >> 32);
+                return (uint32_t)(u >> psh);
+            };
+            uint32_t pv[32];
+            if (j0 + 31 <= rpos) {
+#pragma unroll
+                for (int q = 0; q < 32; q++) pv[q] = prob((int32_t)v[q]);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 32; q++) pv[q] = j0 + q <= rpos ? prob((int32_t)v[q]) : 0u;
+            }
+            // The four byte planes of each 4-key word: a 4x4 byte transpose with byte permutes.
             uint32_t pw[4][8];  // [plane][4-key word] of this thread's 32 keys
 #pragma unroll
-            for (int q = 0; q < 32; q++) {
-                uint32_t p = 0;
-                if (j0 + q <= rpos) {
-                    uint64_t x = (uint64_t)(uint32_t)sT[dist_of<NARROW>(M, (int32_t)v[q], sm, ss, fast, hround, last)]
-                                 << P;
-                    uint64_t qv = __umul64hi(x, rec);  // floor(x / sum) - qv is 0, 1 or 2
-                    if ((qv + 1) * sum <= x) qv++;
-                    if ((qv + 1) * sum <= x) qv++;
-                    p = (uint32_t)qv;
-                }
-#pragma unroll
-                for (int pl = 0; pl < 4; pl++) {
-                    uint32_t byte = (p >> (8 * pl)) & 255u;
-                    if ((q & 3) == 0) pw[pl][q >> 2] = byte;
-                    else pw[pl][q >> 2] |= byte << (8 * (q & 3));
-                }
+            for (int w = 0; w < 8; w++) {
+                const uint32_t a = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x5140);
+                const uint32_t b2 = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x7362);
+                const uint32_t c2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x5140);
+                const uint32_t d2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x7362);
+                pw[0][w] = __byte_perm(a, c2, 0x5410);
+                pw[1][w] = __byte_perm(a, c2, 0x7632);
+                pw[2][w] = __byte_perm(b2, d2, 0x5410);
+                pw[3][w] = __byte_perm(b2, d2, 0x7632);
             }
             // The P V of chunk c - 2 (the same buffer) must be done before its planes are overwritten.
             const int pb = c & 1;

@@ -215,6 +215,123 @@ __global__ void __launch_bounds__(256, RPL <= 32 ? 4 : 1) k_resid_ln(int32_t* x,
     }
 }
 
+// The exact LayerNorm output rule for one value (layernorm.rs:201-256): kept out of line, as the
+// vector kernel below takes it only for values whose double estimate is too close to call.
+__device__ __noinline__ int64_t ln_exact(int64_t cg, i128 u, int s, int32_t b, int beta_frac) {
+    i128 p = (i128)cg * u;
+    i128 y;
+    if (beta_frac == 0) {
+        y = shift_round128(p, s, 126) + (i128)b;
+    } else {
+        i128 cb = (i128)b << (s - beta_frac);
+        y = shift_round128((i128)((u128)p + (u128)cb), s, 126);
+    }
+    return (int64_t)clamp128(y, -127, 127);
+}
+
+// The same fused step for rows of exactly 128 * NV values (GPT-2: NV = 6): each lane holds NV
+// groups of four consecutive values, so every load and store is a 16-byte vector (the output a
+// 4-byte word), and the row width is a compile-time constant, so the divisions by it become
+// multiplications.
+template <int NV>
+__global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t* delta, int R, LnDev ln, int ln_k,
+                                                       int ln_j, uint64_t eps, int8_t* out, int ldo) {
+    constexpr int D = 128 * NV;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= R) return;
+    int4* xr = reinterpret_cast<int4*>(x + (size_t)r * D) + lane;
+    int4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) v[i] = xr[32 * i];
+    if (delta) {
+        const int4* dr = reinterpret_cast<const int4*>(delta + (size_t)r * D) + lane;
+        int4 dv[NV];
+#pragma unroll
+        for (int i = 0; i < NV; i++) dv[i] = __ldcs(dr + 32 * i);
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            v[i].x = (int32_t)clamp64((int64_t)v[i].x + dv[i].x, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+            v[i].y = (int32_t)clamp64((int64_t)v[i].y + dv[i].y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+            v[i].z = (int32_t)clamp64((int64_t)v[i].z + dv[i].z, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+            v[i].w = (int32_t)clamp64((int64_t)v[i].w + dv[i].w, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+            xr[32 * i] = v[i];
+        }
+    }
+    int64_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < NV; i++) sum += (int64_t)v[i].x + v[i].y + v[i].z + v[i].w;
+    sum = warp_sums64(sum);
+    const int64_t mean = floor_div64(sum, D);
+    uint64_t lo = 0, hi = 0;
+    auto acc_sq = [&](int32_t xv) {
+        const int64_t c = (int64_t)xv - mean;
+        const uint64_t a = c < 0 ? (uint64_t)(-c) : (uint64_t)c;
+        const uint64_t sq = a * a;  // |c| < 2^31, so c^2 < 2^62
+        lo += sq;
+        hi += lo < sq ? 1 : 0;
+    };
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        acc_sq(v[i].x);
+        acc_sq(v[i].y);
+        acc_sq(v[i].z);
+        acc_sq(v[i].w);
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
+        uint64_t hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
+        lo += lo2;
+        hi += hi2 + (lo < lo2 ? 1 : 0);
+    }
+    const u128 sum_sq = ((u128)hi << 64) | lo;
+    const u128 var = udiv128_u32(sum_sq, (uint32_t)D);
+    const u128 sq_arg = (var << (2 * ln_j)) + (u128)eps;
+    uint64_t root = isqrt_u128_fast(sq_arg);
+    if (root < 1) root = 1;
+    // floor(2^K / root) (K <= 48): the correctly rounded double quotient, then exact corrections.
+    const uint64_t num = 1ULL << ln_k;
+    uint64_t q = (uint64_t)((double)num / (double)root);
+    while (q * root > num) q--;
+    while ((q + 1) * root <= num) q++;
+    const i128 u = (i128)q * (i128)ln.m;  // |u| < 2^80
+    const int s = ln.s;
+    const bool est_ok = ln.beta_frac == 0 && s <= 126;
+    const double ud = u128_to_double_signed(u) * exp2_neg(s);
+    uint32_t* orow = reinterpret_cast<uint32_t*>(out + (size_t)r * ldo) + lane;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        const int j0 = 128 * i + 4 * lane;
+        const uint2 graw = *reinterpret_cast<const uint2*>(ln.g + j0);
+        const int4 bv = *reinterpret_cast<const int4*>(ln.b + j0);
+        const int32_t xs[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        const int32_t gs[4] = {(int16_t)(graw.x & 0xFFFF), (int16_t)(graw.x >> 16), (int16_t)(graw.y & 0xFFFF),
+                               (int16_t)(graw.y >> 16)};
+        const int32_t bs[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t cg = ((int64_t)xs[k] - mean) * (int64_t)gs[k];  // |cg| < 2^47
+            int64_t yv;
+            bool done = false;
+            if (est_ok) {
+                const double z = fma((double)cg, ud, 0.5);
+                if (fabs(z) < 1048576.0) {
+                    const double fl = floor(z);
+                    const double fr = z - fl;
+                    if (fr > 9.313225746154785e-10 && fr < 1.0 - 9.313225746154785e-10) {
+                        yv = (int64_t)fl + (int64_t)bs[k];
+                        done = true;
+                    }
+                }
+            }
+            if (!done) yv = ln_exact(cg, u, s, bs[k], ln.beta_frac);
+            word |= (uint32_t)(uint8_t)(int8_t)clamp64(yv, -127, 127) << (8 * k);
+        }
+        orow[32 * i] = word;
+    }
+}
+
 __global__ void k_resid_add(int32_t* x, const int32_t* delta, size_t n) {
     size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
     if (i < n) x[i] = (int32_t)clamp64((int64_t)x[i] + delta[i], -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
@@ -762,7 +879,9 @@ void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, cons
                             uint64_t eps, int8_t* out, int ldo, cudaStream_t st) {
     if (R <= 0) return;
     int blocks = (R + 7) / 8;
-    if (d <= 32 * 24) {
+    if (d == 768 && ldo % 4 == 0) {
+        k_resid_ln_v<6><<<blocks, 256, 0, st>>>(x, delta, R, ln, ln_k, ln_j, eps, out, ldo);
+    } else if (d <= 32 * 24) {
         k_resid_ln<24><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo);
     } else if (d <= 32 * 64) {
         k_resid_ln<64><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo);

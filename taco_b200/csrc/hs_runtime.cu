@@ -429,6 +429,10 @@ void plan_groups(hs_batch* b, int R) {
         }
         r = e;
     }
+    // Longest first: a group's work grows with its last key, and the CTAs start in launch order.
+    std::stable_sort(b->h_groups, b->h_groups + b->n_groups, [](const AttnGroup& x, const AttnGroup& y) {
+        return x.pos0 + x.count > y.pos0 + y.count;
+    });
 }
 
 struct PlanRow {
