@@ -11,7 +11,7 @@ constexpr int TILE_M = 128;
 constexpr int TILE_N = 256;
 constexpr int TILE_K = 128;
 // Columns of one logits tile: the coder op reads the max of each tile (LOGIT_TILE columns).
-constexpr int LOGIT_TILE = 256;
+constexpr int LOGIT_TILE = 128;
 // The largest logit table the coder op keeps in shared memory (entries).
 constexpr int MAX_LOGIT_TABLE = 16384;
 // The largest vocabulary of the coder op (8 warps x 32 steps x 256 symbols).

@@ -234,58 +234,61 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int32_t* pm = s_m + acc * BN;
             const int64_t* pc = s_c + acc * BN;
             if (MODE == EPI_LOGITS) {
-                int64_t tm = INT64_MIN;
-#pragma unroll 1
-                for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
-                    uint32_t v[32];
-                    __syncwarp();
-                    tmem_ld32(taddr + c0, v);
-                    tmem_ld_wait();
+                // One TMEM pass over this thread's 128 columns (one logits tile). Per 16-column chunk:
+                // the running max M_c after the chunk and the distances min(M_c - l, last) as packed
+                // u16 pairs in registers. Then every chunk moves to the tile max M with saturating
+                // packed adds: min(d' + min(M - M_c, last), last) = min(M - l, last), because d' and
+                // the shift are each clamped at last only when the true value is at least last.
+                const uint32_t lastv = (uint32_t)e.last;
+                const uint32_t last2 = lastv | (lastv << 16);
+                uint32_t pk[64];
+                int64_t mc[8];
+                int64_t run = -SCORE_LIMIT;
 #pragma unroll
-                    for (int q = 0; q < 32; q++) {
-                        if (col0 + c0 + q < e.N) {
-                            int64_t l = clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), -SCORE_LIMIT,
-                                                SCORE_LIMIT);
-                            tm = l > tm ? l : tm;
-                        }
+                for (int ch = 0; ch < 8; ch++) {
+                    const int c0 = half * 128 + ch * 16;
+                    uint32_t v[16];
+                    __syncwarp();
+                    tmem_ld16(taddr + c0, v);
+                    tmem_ld_wait();
+                    int64_t l[16];
+#pragma unroll
+                    for (int q = 0; q < 16; q++) {
+                        l[q] = col0 + c0 + q < e.N
+                                   ? clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), -SCORE_LIMIT,
+                                             SCORE_LIMIT)
+                                   : -SCORE_LIMIT;
+                        run = l[q] > run ? l[q] : run;
+                    }
+                    mc[ch] = run;
+#pragma unroll
+                    for (int q = 0; q < 16; q += 2) {
+                        const int64_t d0 = run - l[q], d1 = run - l[q + 1];
+                        const uint32_t a0 = d0 < (int64_t)lastv ? (uint32_t)d0 : lastv;
+                        const uint32_t a1 = d1 < (int64_t)lastv ? (uint32_t)d1 : lastv;
+                        pk[ch * 8 + (q >> 1)] = a0 | (a1 << 16);
                     }
                 }
-                s_tm[(acc * 2 + half) * BM + row_in_tile] = tm;
-                named_bar(1, EPI_THREADS);
-                int64_t other = s_tm[(acc * 2 + (half ^ 1)) * BM + row_in_tile];
-                tm = other > tm ? other : tm;
-#pragma unroll 1
-                for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
-                    uint32_t v[32];
-                    __syncwarp();
-                    tmem_ld32(taddr + c0, v);
-                    tmem_ld_wait();
-                    if (row_ok && col0 + c0 < e.N) {
-                        uint32_t packed[16];
+                // The accumulator is read: hand it back to the MMA warp before the stores.
+                tc_fence_before();
+                mbar_arrive(&bars->tempty[acc]);
+                const int tile = nt * 2 + half;
+                if (row_ok && col0 + half * 128 < e.N) {
 #pragma unroll
-                        for (int q = 0; q < 32; q += 2) {
-                            uint32_t a0 = 0, a1 = 0;
-                            if (col0 + c0 + q < e.N) {
-                                int64_t l = clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast),
-                                                    -SCORE_LIMIT, SCORE_LIMIT);
-                                int64_t dd = tm - l;
-                                a0 = (uint32_t)(dd < e.last ? dd : e.last);
-                            }
-                            if (col0 + c0 + q + 1 < e.N) {
-                                int64_t l = clamp64(rescale_fast(v[q + 1], pm[c0 + q + 1], pc[c0 + q + 1], s, fast),
-                                                    -SCORE_LIMIT, SCORE_LIMIT);
-                                int64_t dd = tm - l;
-                                a1 = (uint32_t)(dd < e.last ? dd : e.last);
-                            }
-                            packed[q >> 1] = a0 | (a1 << 16);
-                        }
-                        uint4* dst = reinterpret_cast<uint4*>(e.d16 + (size_t)row * e.ldd + col0 + c0);
+                    for (int ch = 0; ch < 8; ch++) {
+                        const int64_t sh = run - mc[ch];
+                        const uint32_t a = sh < (int64_t)lastv ? (uint32_t)sh : lastv;
+                        const uint32_t a2 = a | (a << 16);
 #pragma unroll
-                        for (int q = 0; q < 4; q++)
-                            dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+                        for (int w = 0; w < 8; w++) pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
                     }
+                    uint4* dst = reinterpret_cast<uint4*>(e.d16 + (size_t)row * e.ldd + col0 + half * 128);
+#pragma unroll
+                    for (int q = 0; q < 16; q++)
+                        dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                    if (tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run;
                 }
-                if (row_ok && half == 0) e.tmax[(size_t)row * e.ldt + nt] = tm;
+                continue;
             } else {
 #pragma unroll 1
                 for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {

@@ -414,28 +414,30 @@ __global__ void __launch_bounds__(256) k_gemm_simple(int mode, const int8_t* A, 
                 if (r0 + i < R) epi_store(mode, e, r0 + i, n, acc[i]);
         return;
     }
-    // Logits: l = clamp(rescale(acc, m[n], s), +-2^40); per row the max over the 256 columns
-    // of the block (one logits tile), then d16 = min(tmax - l, last).
+    // Logits: l = clamp(rescale(acc, m[n], s), +-2^40); per row the max over each 128 columns
+    // of the block (one logits tile: warps 0-3 and warps 4-7), then d16 = min(tmax - l, last).
     int64_t l[SG_ROWS];
     int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
     for (int i = 0; i < SG_ROWS; i++) {
-        l[i] = n < e.N ? clamp64(rescale64(acc[i], e.m[n], e.s), -SCORE_LIMIT, SCORE_LIMIT) : INT64_MIN;
+        l[i] = n < e.N ? clamp64(rescale64(acc[i], e.m[n], e.s), -SCORE_LIMIT, SCORE_LIMIT) : -SCORE_LIMIT;
         int64_t mx = warp_max64(l[i]);
         if (lane == 0) red[i][w] = mx;
     }
     __syncthreads();
+    const int hq = w >> 2;  // which 128 columns
+    const int tile = blockIdx.x * 2 + hq;
 #pragma unroll
     for (int i = 0; i < SG_ROWS; i++) {
-        int64_t tm = red[i][0];
-        for (int q = 1; q < 8; q++) tm = red[i][q] > tm ? red[i][q] : tm;
+        int64_t tm = red[i][4 * hq];
+        for (int q = 1; q < 4; q++) tm = red[i][4 * hq + q] > tm ? red[i][4 * hq + q] : tm;
         int r = r0 + i;
         if (r < R) {
             if (n < e.N) {
                 int64_t dd = tm - l[i];
                 e.d16[(size_t)r * e.ldd + n] = (uint16_t)(dd < e.last ? dd : e.last);
             }
-            if (threadIdx.x == 0) e.tmax[(size_t)r * e.ldt + blockIdx.x] = tm;
+            if ((threadIdx.x & 127) == 0 && tile < e.ldt) e.tmax[(size_t)r * e.ldt + tile] = tm;
         }
     }
 }
@@ -651,89 +653,151 @@ constexpr int CODER_THREADS = 256;
 constexpr int CODER_WARPS = CODER_THREADS / 32;
 constexpr int CODER_MAX_STEPS = 32;  // steps of 256 symbols per warp: V <= 8 * 32 * 256 = 65536
 
-// One block per row. d16 is read as groups of 8 symbols (one 16-byte load); warp w owns the
-// groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step). The
-// coder answer walks warp -> step -> lane -> symbol, each level a parallel scan.
+// One block per row. d16 is read as groups of 8 symbols (one 16-byte load). Every weight is a
+// table entry, table[min(d, last)] for the symbol's distance d from the row max, so pass 1 only
+// counts the symbols at each distance (shared-memory atomics; the clamped tail has its own
+// register count) and W = sum over d of count[d] * table[d]. The table is not increasing and its
+// first entry is its largest, and the row max has distance 0, so the largest weight is table[0]:
+// the largest symbol (freq.rs:107-117, lowest id on a tie) is the lowest id whose distance is at
+// most `head`, the last index with table[head] == table[0]. F[d] = 1 + floor(table[d] * spare / W)
+// replaces the counts in place, and sum(f) = sum over d of count[d] * F[d].
+// An encode query (kind 0) then sums f over the symbols below its token: one block reduction. A
+// decode query walks warp -> step -> lane -> symbol, each level a parallel scan: warp w owns the
+// groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step).
 __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
-                                                         int R, int V, const uint64_t* table, int tlen, uint32_t bits,
-                                                         const RowInfo* rows, uint64_t* out) {
-    extern __shared__ __align__(16) uint32_t F[];  // 1 + floor(table[j] * spare / W), j <= dmax
+                                                         int R, int V, const uint64_t* table, int tlen, int head,
+                                                         uint32_t bits, const RowInfo* rows, uint64_t* out) {
+    extern __shared__ __align__(16) uint32_t F[];  // counts, then 1 + floor(table[j] * spare / W), j <= dmax
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
     __shared__ uint64_t wsum[CODER_WARPS];
     __shared__ uint64_t steps[CODER_WARPS][CODER_MAX_STEPS];
-    __shared__ int s_largest;
     const int r = blockIdx.x;
     if (r >= R) return;
     const uint16_t* dr = d16 + (size_t)r * ldd;
     const int64_t* tr = tmax + (size_t)r * ldt;
     const int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t last = tlen - 1;
+    const int32_t last = tlen - 1;
     const uint64_t total = 1ULL << bits;
     const uint64_t spare = total - (uint64_t)V;
-    const int ng = (V + 7) / 8;
+    const int ng = (V + 7) / 8, ng_full = V / 8;
+    for (int j = threadIdx.x; j < tlen; j += CODER_THREADS) F[j] = 0;
     // The row max.
     int64_t mx = INT64_MIN;
     for (int t = threadIdx.x; t < VT; t += CODER_THREADS) mx = tr[t] > mx ? tr[t] : mx;
-    mx = block_max64(mx, red);
-    // Pass 1: W = sum(w), the largest weight and the largest distance (freq.rs:112-121).
-    // Each thread visits its symbols in increasing order, so its first symbol with its largest
-    // weight is its lowest such id; the block reduces (max weight, then min id).
-    uint64_t W = 0, wmax = 0;
-    int64_t dmax = 0;
+    mx = block_max64(mx, red);  // (its barriers also order the clearing of F)
+    // The distance offset of the tile of symbol v0, clamped to last (then every distance is last).
+    auto tile_off = [&](int v0) -> int32_t {
+        const int64_t o = mx - tr[v0 / LOGIT_TILE];
+        return o < (int64_t)last ? (int32_t)o : last;
+    };
+    // Pass 1: the distance counts, the largest distance and the largest symbol.
+    uint32_t nlast = 0;
+    int32_t dmax = 0;
     int best = V;
-    for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
+    for (int gi = threadIdx.x; gi < ng_full; gi += CODER_THREADS) {
         const int v0 = 8 * gi;
         const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+        const int32_t off = tile_off(v0);
+        if (off == last) {
+            nlast += 8;
+            dmax = last;
+            continue;
+        }
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-        const int64_t off = mx - tr[v0 / LOGIT_TILE];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            if (v0 + i < V) {
-                int64_t dd = off + (int64_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
-                dd = dd < last ? dd : last;
-                uint64_t wv = table[dd];
-                W += wv;
-                if (wv > wmax || best == V) {
-                    wmax = wv;
-                    best = v0 + i;
-                }
-                dmax = dd > dmax ? dd : dmax;
-            }
+            int32_t dd = off + (int32_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
+            dd = dd < last ? dd : last;
+            if (dd < last) atomicAdd(&F[dd], 1u);
+            else nlast++;
+            dmax = dd > dmax ? dd : dmax;
+            best = dd <= head && v0 + i < best ? v0 + i : best;
         }
     }
+    if (ng_full < ng && threadIdx.x == ng_full % CODER_THREADS) {
+        const int v0 = 8 * ng_full;
+        const int32_t off = tile_off(v0);
+        for (int v = v0; v < V; v++) {
+            int32_t dd = off + (int32_t)dr[v];
+            dd = dd < last ? dd : last;
+            if (dd < last) atomicAdd(&F[dd], 1u);
+            else nlast++;
+            dmax = dd > dmax ? dd : dmax;
+            best = dd <= head && v < best ? v : best;
+        }
+    }
+    const uint64_t n_last = block_sum64(nlast, redu);
+    dmax = (int32_t)block_max64(dmax, red);
+    const int largest_found = (int)-block_max64(-(int64_t)best, red);
+    // W = sum over the distances of count * table (< 2^16 * 2^40: fits in 64 bits).
+    uint64_t W = 0;
+    for (int j = threadIdx.x; j <= dmax; j += CODER_THREADS)
+        W += (uint64_t)(j == last ? (uint32_t)n_last : F[j]) * table[j];
     W = block_sum64(W, redu);
-    const uint64_t my_w = best < V ? wmax : 0;
-    wmax = (uint64_t)block_max64((int64_t)my_w, red);
-    dmax = block_max64(dmax, red);
-    // The lowest id with the largest weight.
-    if (threadIdx.x == 0) s_largest = V;
-    __syncthreads();
-    if (best < V && my_w == wmax) atomicMin(&s_largest, best);
-    __syncthreads();
     const bool all_zero = W == 0;
-    const int largest = all_zero ? 0 : s_largest;
+    const int largest = all_zero ? 0 : largest_found;
     const uint32_t f_flat = (uint32_t)(1 + spare / (uint64_t)V);  // all-zero rule: every weight is 1
-    // F for the distances that occur in this row (every table entry is <= wmax <= W, so the quotient
-    // is below 2^32).
-    if (!all_zero)
-        for (int j = threadIdx.x; j <= dmax; j += CODER_THREADS) F[j] = (uint32_t)(1 + udiv128_small((u128)table[j] * spare, W));
-    __syncthreads();
-    // f of one group of 8 symbols (0 past V).
+    // F for the distances that occur (every table entry is <= table[0] <= W, so the quotient is
+    // below 2^32), and sum(f).
+    uint64_t sum_f = 0;
+    if (all_zero) {
+        sum_f = (uint64_t)V * f_flat;
+    } else {
+        for (int j = threadIdx.x; j <= dmax; j += CODER_THREADS) {
+            const uint32_t c = j == last ? (uint32_t)n_last : F[j];
+            if (c) {
+                const uint32_t f = (uint32_t)(1 + udiv128_small((u128)table[j] * spare, W));
+                F[j] = f;
+                sum_f += (uint64_t)c * f;
+            }
+        }
+        sum_f = block_sum64(sum_f, redu);  // (its barriers also publish F)
+    }
+    const uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
+    const RowInfo q = rows[r];
+    auto f_of = [&](int32_t off, uint32_t d) -> uint32_t {
+        int32_t dd = off + (int32_t)d;
+        return all_zero ? f_flat : F[dd < last ? dd : last];
+    };
+    if (q.kind == 0) {
+        // Encode: start = sum of f below the token (+ rem past the largest symbol).
+        const int s = (int)q.value;
+        const int gs = s / 8;
+        uint64_t pre = 0;
+        for (int gi = threadIdx.x; gi < gs; gi += CODER_THREADS) {
+            const int v0 = 8 * gi;
+            const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+            const int32_t off = tile_off(v0);
+            const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+            uint32_t gsum = 0;  // 8 frequencies: at most total - (V - 8) < 2^32 for V > 8
+#pragma unroll
+            for (int i = 0; i < 8; i++) gsum += f_of(off, (u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
+            pre += gsum;
+        }
+        if (threadIdx.x == CODER_THREADS - 1) {
+            const int32_t off = tile_off(8 * gs);
+            for (int v = 8 * gs; v < s; v++) pre += f_of(off, dr[v]);
+        }
+        pre = block_sum64(pre, redu);
+        if (threadIdx.x == 0) {
+            const uint64_t start = pre + ((uint64_t)s > (uint64_t)largest ? rem : 0);
+            const uint64_t freq = f_of(tile_off(s), dr[s]) + (s == largest ? rem : 0);
+            out[3 * (size_t)r] = (uint64_t)s;
+            out[3 * (size_t)r + 1] = start;
+            out[3 * (size_t)r + 2] = freq;
+        }
+        return;
+    }
+    // Decode. f of one group of 8 symbols (0 past V).
     auto group_f = [&](int gi, uint32_t (&f)[8]) {
         const int v0 = 8 * gi;
         const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-        const int64_t off = mx - tr[v0 / LOGIT_TILE];
+        const int32_t off = tile_off(v0);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            f[i] = 0;
-            if (v0 + i < V) {
-                int64_t dd = off + (int64_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
-                f[i] = all_zero ? f_flat : F[dd < last ? dd : last];
-            }
-        }
+        for (int i = 0; i < 8; i++) f[i] = v0 + i < V ? f_of(off, (u[i >> 1] >> (16 * (i & 1))) & 0xFFFF) : 0u;
     };
     // Pass 2: per warp and step (32 groups), the sum of f.
     const int gpw = (ng + CODER_WARPS - 1) / CODER_WARPS;
@@ -755,21 +819,14 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     }
     if (lane == 0) wsum[w] = wtotal;
     __syncthreads();
-    uint64_t before = 0, sum_f = 0;
-    for (int i = 0; i < CODER_WARPS; i++) {
-        if (i < w) before += wsum[i];
-        sum_f += wsum[i];
-    }
-    const uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
-    const RowInfo q = rows[r];
+    uint64_t before = 0;
+    for (int i = 0; i < w; i++) before += wsum[i];
     const int a = 8 * ga, b = min(V, 8 * gb);
     // A(v) = sum of f below v + (rem if v > largest): the start of symbol v.
     auto adj = [&](int v) -> uint64_t { return (uint64_t)v > (uint64_t)largest ? rem : 0; };
     const uint64_t Aa = before + adj(a);
     const uint64_t Ab = b >= V ? total : before + wtotal + adj(b);
-    bool mine;
-    if (q.kind == 0) mine = (int64_t)q.value >= a && (int64_t)q.value < b;
-    else mine = a < b && q.value >= Aa && q.value < Ab;
+    const bool mine = a < b && q.value >= Aa && q.value < Ab;
     if (!mine) return;
     // Level 1: the step. Lane k holds the exclusive prefix of the step sums.
     uint64_t st = lane < nsteps ? steps[w][lane] : 0;
@@ -779,11 +836,9 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         if (lane >= o) incl += t;
     }
     const uint64_t excl = incl - st;
+    // The last step whose start is <= target (starts include rem past the largest symbol).
     int kstep;
-    if (q.kind == 0) {
-        kstep = ((int)q.value / 8 - ga) / 32;
-    } else {
-        // The last step whose start is <= target (starts include rem past the largest symbol).
+    {
         const int v0 = 8 * (ga + 32 * lane);
         const bool ok = lane < nsteps && before + excl + adj(v0) <= q.value;
         const unsigned m = __ballot_sync(0xffffffffu, ok);
@@ -804,9 +859,7 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     }
     const uint64_t gstart = step_base + ginc - gs;  // sum of f below this group (no rem)
     int owner;
-    if (q.kind == 0) {
-        owner = ((int)q.value / 8 - ga) % 32;
-    } else {
+    {
         const bool ok = gi < gb && gstart + adj(8 * gi) <= q.value;
         const unsigned m = __ballot_sync(0xffffffffu, ok);
         owner = 31 - __clz(m);
@@ -820,7 +873,7 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         if (v >= V) break;
         const uint64_t start = acc + adj(v);
         const uint64_t freq = f[i] + (v == largest ? rem : 0);
-        const bool hit = q.kind == 0 ? (uint64_t)v == q.value : (q.value >= start && q.value < start + freq);
+        const bool hit = q.value >= start && q.value < start + freq;
         if (hit) {
             out[3 * (size_t)r] = (uint64_t)v;
             out[3 * (size_t)r + 1] = start;
@@ -933,9 +986,10 @@ void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, con
 }
 
 void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,
-                  int tlen, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st) {
+                  int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st) {
     if (R <= 0) return;
-    k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, R, V, table, tlen, bits, rows, out);
+    k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, R, V, table, tlen, head, bits, rows,
+                                                         out);
 }
 
 void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,

@@ -62,9 +62,10 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
                          const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st);
 
 // The coder op: from the d16/tmax output of the logits GEMM, the interval of each row's query
-// in the table of taco_coder::FreqTable::from_weights(weights, bits). out: 3 u64 per row.
+// in the table of taco_coder::FreqTable::from_weights(weights, bits). out: 3 u64 per row. `head`
+// is the last index j with table[j] == table[0] (the table is not increasing).
 void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,
-                  int tlen, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st);
+                  int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st);
 
 // The full weights of each row (run_weights): w[r, v] = table[min(max - logit, last)].
 void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,

@@ -148,6 +148,7 @@ struct hs_model {
     int attn_len = 0;
     uint64_t* logits_exp = nullptr;
     int logits_len = 0;
+    int logits_head = 0;  // the last index j with logits_exp[j] == logits_exp[0]
 
     ~hs_model() {
         if (dev) cudaSetDevice(dev->ordinal);
@@ -537,7 +538,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         if (out) {
             {
                 ProfScope p(b, OP_CODER, 0);
-                launch_coder(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, bits, b->d_rows,
+                launch_coder(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, m->logits_head, bits, b->d_rows,
                              b->intervals, b->stream);
             }
             pass_scope.reset();
@@ -749,6 +750,7 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
     m->attn_len = (int)M.attn_exp.size();
     if ((rc = upload(&m->logits_exp, M.logits_exp.data(), M.logits_exp.size(), m->owned))) return rc;
     m->logits_len = (int)M.logits_exp.size();
+    while (m->logits_head + 1 < m->logits_len && M.logits_exp[m->logits_head + 1] == M.logits_exp[0]) m->logits_head++;
     m->weight_bytes += M.wpe.size() + 8 * M.logits_exp.size() + 4 * M.attn_exp.size();
     CK(cudaDeviceSynchronize());
     *out = m.release();
