@@ -92,6 +92,7 @@ struct EpiArgs {
     int64_t* tmax;
     int ldt;
     int last;
+    int small;  // EPI_LOGITS: every logit is below 2^30 in magnitude (host bound), 32-bit arithmetic
     int32_t* out32;
     // EPI_QKV: the rows of the pass and the caches of this layer.
     const RowInfo* rows;

@@ -66,6 +66,19 @@ __device__ __forceinline__ int64_t rescale_fast(uint32_t acc, int32_t m, int64_t
     return rescale64((int64_t)(int32_t)acc + c, m, (uint32_t)s);
 }
 
+// S32: the host has bounded every output of this linear below 2^30 in magnitude (and the shift is
+// in 0..=62), so the rescaled value is the low word of the 64-bit shift and the clamps are 32-bit.
+template <bool S32>
+__device__ __forceinline__ auto rescale_e(uint32_t acc, int32_t m, int64_t c, int s, bool fast) {
+    if constexpr (S32) return (int32_t)(((int64_t)(int32_t)acc * (int64_t)m + c) >> s);
+    else return rescale_fast(acc, m, c, s, fast);
+}
+template <class T>
+__device__ __forceinline__ T clamp_e(T y, int64_t lo, int64_t hi) {
+    if constexpr (sizeof(T) == 4) return min(max(y, (T)lo), (T)hi);
+    else return clamp64(y, lo, hi);
+}
+
 // EPI_QKV: one value at column n of a row of (slot, pos): q to out8, k and v to the caches.
 __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowInfo& ri, int n, int8_t o) {
     if (n < e.d) {
@@ -79,7 +92,7 @@ __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowIn
     else e.vc[(head * e.hd + c) * e.n_ctx + ri.pos] = o;
 }
 
-template <int MODE>
+template <int MODE, bool S32>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int MT, int NT,
               int KB, EpiArgs e, int* err) {
@@ -242,6 +255,52 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t lastv = (uint32_t)e.last;
                 const uint32_t last2 = lastv | (lastv << 16);
                 uint32_t pk[64];
+                const int tile = nt * 2 + half;
+                if (S32 && col0 + BN <= e.N) {
+                    // Every logit is below 2^30 in magnitude (the host's bound), so the clamp at
+                    // 2^40 is the identity and the max and the distances fit in 32 bits.
+                    int32_t mc32[8];
+                    int32_t run32 = INT32_MIN;
+#pragma unroll
+                    for (int ch = 0; ch < 8; ch++) {
+                        const int c0 = half * 128 + ch * 16;
+                        uint32_t v[16];
+                        __syncwarp();
+                        tmem_ld16(taddr + c0, v);
+                        tmem_ld_wait();
+                        int32_t l[16];
+#pragma unroll
+                        for (int q = 0; q < 16; q++) {
+                            l[q] = (int32_t)(((int64_t)(int32_t)v[q] * (int64_t)pm[c0 + q] + pc[c0 + q]) >> s);
+                            run32 = l[q] > run32 ? l[q] : run32;
+                        }
+                        mc32[ch] = run32;
+#pragma unroll
+                        for (int q = 0; q < 16; q += 2) {
+                            const uint32_t a0 = min((uint32_t)(run32 - l[q]), lastv);
+                            const uint32_t a1 = min((uint32_t)(run32 - l[q + 1]), lastv);
+                            pk[ch * 8 + (q >> 1)] = a0 | (a1 << 16);
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&bars->tempty[acc]);
+                    if (row_ok) {
+#pragma unroll
+                        for (int ch = 0; ch < 8; ch++) {
+                            const uint32_t a = min((uint32_t)(run32 - mc32[ch]), lastv);
+                            const uint32_t a2 = a | (a << 16);
+#pragma unroll
+                            for (int w = 0; w < 8; w++)
+                                pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(e.d16 + (size_t)row * e.ldd + col0 + half * 128);
+#pragma unroll
+                        for (int q = 0; q < 16; q++)
+                            dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                        if (tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run32;
+                    }
+                    continue;
+                }
                 int64_t mc[8];
                 int64_t run = -SCORE_LIMIT;
 #pragma unroll
@@ -272,7 +331,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // The accumulator is read: hand it back to the MMA warp before the stores.
                 tc_fence_before();
                 mbar_arrive(&bars->tempty[acc]);
-                const int tile = nt * 2 + half;
                 if (row_ok && col0 + half * 128 < e.N) {
 #pragma unroll
                     for (int ch = 0; ch < 8; ch++) {
@@ -303,7 +361,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const RowInfo ri = e.rows[row];
                         int8_t o[32];
 #pragma unroll
-                        for (int q = 0; q < 32; q++) o[q] = (int8_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), -127, 127);
+                        for (int q = 0; q < 32; q++)
+                            o[q] = (int8_t)clamp_e(rescale_e<S32>(v[q], pm[c0 + q], pc[c0 + q], s, fast), -127, 127);
                         if (full && colb + 32 <= e.d && (e.ldo & 15) == 0) {
                             // A whole 32-byte run of q.
                             uint32_t pk[8];
@@ -361,12 +420,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int q = 0; q < 8; q++) packed[q] = 0;
 #pragma unroll
                         for (int q = 0; q < 32; q++) {
-                            int64_t y = rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast);
+                            const auto y = rescale_e<S32>(v[q], pm[c0 + q], pc[c0 + q], s, fast);
                             int8_t o;
                             if (MODE == EPI_ACT) {
-                                o = (int8_t)clamp64(y, -127, 127);
+                                o = (int8_t)clamp_e(y, -127, 127);
                             } else {
-                                int64_t in = clamp64(y, -e.gelu_off, e.gelu_off - 1);
+                                const auto in = clamp_e(y, -e.gelu_off, e.gelu_off - 1);
                                 o = s_gelu[in + e.gelu_off];
                             }
                             packed[q >> 2] |= (uint32_t)(uint8_t)o << (8 * (q & 3));
@@ -383,9 +442,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     } else if (MODE == EPI_DELTA) {
                         int32_t o[32];
 #pragma unroll
-                        for (int q = 0; q < 32; q++)
-                            o[q] = (int32_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), INT32_MIN,
-                                                    INT32_MAX);
+                        for (int q = 0; q < 32; q++) {
+                            if constexpr (S32) o[q] = rescale_e<true>(v[q], pm[c0 + q], pc[c0 + q], s, fast);
+                            else o[q] = (int32_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), INT32_MIN,
+                                                         INT32_MAX);
+                        }
                         int32_t* dst = e.out32 + (size_t)row * e.ldo + colb;
                         if (full && (e.ldo & 3) == 0) {
 #pragma unroll
@@ -419,14 +480,21 @@ __global__ void __launch_bounds__(THREADS, 1)
 template <int MODE>
 void launch_mode(const void* tmA, const void* tmB, int MT, int NT, int KB, const EpiArgs& e, int grid, int* err,
                  cudaStream_t st) {
-    k_gemm_tc<MODE><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(tmA),
-                                                           *reinterpret_cast<const CUtensorMap*>(tmB), MT, NT, KB, e,
-                                                           err);
+    const CUtensorMap& a = *reinterpret_cast<const CUtensorMap*>(tmA);
+    const CUtensorMap& b = *reinterpret_cast<const CUtensorMap*>(tmB);
+    if (MODE != EPI_RAW && e.small && e.s >= 0 && e.s <= 62)
+        k_gemm_tc<MODE, true><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, MT, NT, KB, e, err);
+    else
+        k_gemm_tc<MODE, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, MT, NT, KB, e, err);
 }
 
 template <int MODE>
 cudaError_t configure_mode() {
-    return cudaFuncSetAttribute(k_gemm_tc<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<MODE>::SMEM);
+    cudaError_t r = cudaFuncSetAttribute(k_gemm_tc<MODE, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Cfg<MODE>::SMEM);
+    if (r != cudaSuccess) return r;
+    return cudaFuncSetAttribute(k_gemm_tc<MODE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)Cfg<MODE>::SMEM);
 }
 
 }  // namespace

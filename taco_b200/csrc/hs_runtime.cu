@@ -119,6 +119,7 @@ int upload(T** p, const T* src, size_t count, std::vector<void*>& owned) {
 
 struct DevLinear {
     LinearDev ld{};
+    bool small = false;  // every rescaled output is below 2^30 in magnitude (32-bit epilogue)
     alignas(128) CUtensorMap tm;
 };
 
@@ -271,6 +272,21 @@ int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D) {
     if (!rc) rc = upload(&dm, mm.data(), mm.size(), m->owned);
     if (rc) return rc;
     D.ld = LinearDev{dw, N, K, Np, Kp, db, dm, (int)L.rs.s};
+    // |acc| <= K * 128 * 128 for i8 operands, so an output is at most
+    // (K * 2^14 * |m| + |b * m| + 2^(s-1)) / 2^s + 1 in magnitude.
+    D.small = false;
+    const int s = (int)L.rs.s;
+    if (s >= 0 && s <= 62) {
+        unsigned __int128 worst = 0;
+        for (int n = 0; n < N; n++) {
+            const uint64_t am = (uint64_t)std::abs((int64_t)L.rs.m[n]);
+            const uint64_t ab = (uint64_t)std::abs((int64_t)L.b[n]);
+            const unsigned __int128 t = (unsigned __int128)K * 16384 * am + (unsigned __int128)ab * am;
+            worst = t > worst ? t : worst;
+        }
+        worst += s > 0 ? (unsigned __int128)1 << (s - 1) : 0;
+        D.small = (worst >> s) + 1 < ((unsigned __int128)1 << 30);
+    }
     m->weight_bytes += w.size() + 8 * (size_t)Np;
     return make_tmap(m->dev, &D.tm, dw, Np, Kp, TILE_N);
 }
@@ -300,6 +316,7 @@ int forward(hs_batch* b, int R) {
     auto gemm = [&](int op, int mode, const int8_t* A, int lda, const CUtensorMap* tmA, const DevLinear& W,
                     EpiArgs e) {
         ProfScope p(b, op, 2ULL * R * W.ld.N * W.ld.K);
+        e.small = W.small ? 1 : 0;
         if (m->use_tc)
             launch_gemm_tc(mode, tmA, &W.tm, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms, m->dev->d_err, st);
         else
