@@ -43,11 +43,18 @@ constexpr int GELU_SMEM = 65536;
 constexpr int VT_STRIDE = 36;                  // bytes per row of a warp's 32 x 32 transpose tile
 constexpr int VT_TILE = 32 * VT_STRIDE;
 
+// The epilogue of EPI_DELTA, EPI_GELU and EPI_LOGITS stores through TMA: each epilogue warp
+// stages pieces of 32 rows x 32 bytes (the 32-byte swizzle) in shared memory, two buffers for
+// DELTA and LOGITS, one for GELU (whose 64 KB table fills the rest), so the stores leave as whole
+// row segments instead of 32 scattered 16-byte pieces per instruction.
 template <int MODE>
 struct Cfg {
     static constexpr int STAGES = MODE == EPI_GELU ? 3 : 4;
     static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : (MODE == EPI_QKV ? EPI_WARPS * VT_TILE : 0);
-    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + EXTRA + 2 * BN * 12 + 2 * 2 * BM * 8 + 256 + 1024;
+    static constexpr int STORE_BUFS = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 2 : (MODE == EPI_GELU ? 1 : 0);
+    static constexpr int STORE_WARP = 1024 * STORE_BUFS;
+    static constexpr size_t SMEM =
+        (size_t)STAGES * STAGE_BYTES + EXTRA + EPI_WARPS * STORE_WARP + 2 * BN * 12 + 256 + 1024;
 };
 
 struct __align__(8) Bars {
@@ -94,16 +101,17 @@ __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowIn
 
 template <int MODE, bool S32>
 __global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int MT, int NT,
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const __grid_constant__ CUtensorMap tmC, int MT, int NT,
               int KB, EpiArgs e, int* err) {
     constexpr int STAGES = Cfg<MODE>::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     int8_t* s_gelu = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * STAGE_BYTES);
-    int64_t* s_c = reinterpret_cast<int64_t*>(smem + (size_t)STAGES * STAGE_BYTES + Cfg<MODE>::EXTRA);  // [2][BN]
-    int32_t* s_m = reinterpret_cast<int32_t*>(s_c + 2 * BN);                                            // [2][BN]
-    int64_t* s_tm = reinterpret_cast<int64_t*>(s_m + 2 * BN);                                           // [2][2][BM]
-    Bars* bars = reinterpret_cast<Bars*>(s_tm + 2 * 2 * BM);
+    uint8_t* s_store = smem + (size_t)STAGES * STAGE_BYTES + Cfg<MODE>::EXTRA;  // [EPI_WARPS][STORE_WARP]
+    int64_t* s_c = reinterpret_cast<int64_t*>(s_store + EPI_WARPS * Cfg<MODE>::STORE_WARP);  // [2][BN]
+    int32_t* s_m = reinterpret_cast<int32_t*>(s_c + 2 * BN);                                 // [2][BN]
+    Bars* bars = reinterpret_cast<Bars*>(s_m + 2 * BN);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (warp == 0 && lane == 0) {
@@ -201,6 +209,28 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int s = e.s;
         const bool fast = s >= 0 && s <= 62;
         const int64_t hround = (fast && s > 0) ? (1LL << (s - 1)) : 0;
+        // One 32-row x 32-byte piece (this lane's row: lo, hi) to the output through TMA at
+        // element column x and row y. Warp-collective.
+        uint8_t* my_store = s_store + (warp - 2) * Cfg<MODE>::STORE_WARP;
+        uint32_t pieces = 0;
+        auto store_piece = [&](uint4 lo, uint4 hi, int x, int y) {
+            uint8_t* buf = my_store + (Cfg<MODE>::STORE_BUFS == 2 ? (pieces & 1) * 1024 : 0);
+            if (lane == 0) {
+                if (Cfg<MODE>::STORE_BUFS == 2) bulk_wait_read1();
+                else bulk_wait_read();
+            }
+            __syncwarp();
+            const uint32_t sw = (uint32_t)((lane >> 2) & 1);
+            *reinterpret_cast<uint4*>(buf + lane * 32 + (sw << 4)) = lo;
+            *reinterpret_cast<uint4*>(buf + lane * 32 + ((sw ^ 1) << 4)) = hi;
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&tmC, buf, x, y);
+                bulk_commit();
+            }
+            pieces++;
+        };
         int i = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
             const int mt = t % MT, nt = t / MT;
@@ -284,21 +314,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     tc_fence_before();
                     mbar_arrive(&bars->tempty[acc]);
-                    if (row_ok) {
 #pragma unroll
-                        for (int ch = 0; ch < 8; ch++) {
-                            const uint32_t a = min((uint32_t)(run32 - mc32[ch]), lastv);
-                            const uint32_t a2 = a | (a << 16);
+                    for (int ch = 0; ch < 8; ch++) {
+                        const uint32_t a = min((uint32_t)(run32 - mc32[ch]), lastv);
+                        const uint32_t a2 = a | (a << 16);
 #pragma unroll
-                            for (int w = 0; w < 8; w++)
-                                pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
-                        }
-                        uint4* dst = reinterpret_cast<uint4*>(e.d16 + (size_t)row * e.ldd + col0 + half * 128);
-#pragma unroll
-                        for (int q = 0; q < 16; q++)
-                            dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-                        if (tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run32;
+                        for (int w = 0; w < 8; w++) pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
+                        // Rows past R land in the padding rows of d16 (never read).
+                        store_piece(make_uint4(pk[ch * 8], pk[ch * 8 + 1], pk[ch * 8 + 2], pk[ch * 8 + 3]),
+                                    make_uint4(pk[ch * 8 + 4], pk[ch * 8 + 5], pk[ch * 8 + 6], pk[ch * 8 + 7]),
+                                    col0 + half * 128 + ch * 16, mt * BM + g * 32);
                     }
+                    if (row_ok && tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run32;
                     continue;
                 }
                 int64_t mc[8];
@@ -331,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 // The accumulator is read: hand it back to the MMA warp before the stores.
                 tc_fence_before();
                 mbar_arrive(&bars->tempty[acc]);
-                if (row_ok && col0 + half * 128 < e.N) {
+                if (col0 + half * 128 < e.N) {
 #pragma unroll
                     for (int ch = 0; ch < 8; ch++) {
                         const int64_t sh = run - mc[ch];
@@ -339,12 +366,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t a2 = a | (a << 16);
 #pragma unroll
                         for (int w = 0; w < 8; w++) pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
+                        // Columns past N are clipped by the tensor map; pieces wholly past N are skipped.
+                        if (col0 + half * 128 + ch * 16 < e.N)
+                            store_piece(make_uint4(pk[ch * 8], pk[ch * 8 + 1], pk[ch * 8 + 2], pk[ch * 8 + 3]),
+                                        make_uint4(pk[ch * 8 + 4], pk[ch * 8 + 5], pk[ch * 8 + 6], pk[ch * 8 + 7]),
+                                        col0 + half * 128 + ch * 16, mt * BM + g * 32);
                     }
-                    uint4* dst = reinterpret_cast<uint4*>(e.d16 + (size_t)row * e.ldd + col0 + half * 128);
-#pragma unroll
-                    for (int q = 0; q < 16; q++)
-                        dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-                    if (tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run;
+                    if (row_ok && tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run;
                 }
                 continue;
             } else {
@@ -355,7 +383,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tmem_ld32(taddr + c0, v);
                     tmem_ld_wait();
                     const int colb = col0 + c0;
-                    if (!row_ok || colb >= e.N) continue;
+                    if (colb >= e.N) continue;
+                    // GELU and DELTA store through TMA (warp-collective): rows past R land in the
+                    // padding rows of the output, which nothing reads.
+                    if (MODE != EPI_GELU && MODE != EPI_DELTA && !row_ok) continue;
                     const bool full = colb + 32 <= e.N;
                     if (MODE == EPI_QKV) {
                         const RowInfo ri = e.rows[row];
@@ -431,7 +462,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                             packed[q >> 2] |= (uint32_t)(uint8_t)o << (8 * (q & 3));
                         }
                         int8_t* dst = e.out8 + (size_t)row * e.ldo + colb;
-                        if (full && (e.ldo & 15) == 0) {
+                        if (MODE == EPI_GELU) {
+                            store_piece(make_uint4(packed[0], packed[1], packed[2], packed[3]),
+                                        make_uint4(packed[4], packed[5], packed[6], packed[7]), colb, mt * BM + g * 32);
+                        } else if (full && (e.ldo & 15) == 0) {
                             reinterpret_cast<uint4*>(dst)[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
                             reinterpret_cast<uint4*>(dst)[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
                         } else {
@@ -447,16 +481,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                             else o[q] = (int32_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), INT32_MIN,
                                                          INT32_MAX);
                         }
-                        int32_t* dst = e.out32 + (size_t)row * e.ldo + colb;
-                        if (full && (e.ldo & 3) == 0) {
 #pragma unroll
-                            for (int q = 0; q < 8; q++)
-                                reinterpret_cast<int4*>(dst)[q] = make_int4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-                        } else {
-#pragma unroll
-                            for (int q = 0; q < 32; q++)
-                                if (colb + q < e.N) dst[q] = o[q];
-                        }
+                        for (int p = 0; p < 4; p++)
+                            if (colb + 8 * p < e.N)
+                                store_piece(make_uint4(o[8 * p], o[8 * p + 1], o[8 * p + 2], o[8 * p + 3]),
+                                        make_uint4(o[8 * p + 4], o[8 * p + 5], o[8 * p + 6], o[8 * p + 7]),
+                                        colb + 8 * p, mt * BM + g * 32);
                     } else if (MODE == EPI_RAW) {
                         int32_t* dst = e.out32 + (size_t)row * e.ldo + colb;
 #pragma unroll
@@ -468,6 +498,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->tempty[acc]);
         }
+        // The TMA stores of this warp are complete before the CTA (and its shared memory) ends.
+        if (Cfg<MODE>::STORE_BUFS > 0 && lane == 0) bulk_wait_all();
     }
     __syncthreads();
     if (warp == 1) {
@@ -478,14 +510,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int MODE>
-void launch_mode(const void* tmA, const void* tmB, int MT, int NT, int KB, const EpiArgs& e, int grid, int* err,
-                 cudaStream_t st) {
+void launch_mode(const void* tmA, const void* tmB, const void* tmC, int MT, int NT, int KB, const EpiArgs& e, int grid,
+                 int* err, cudaStream_t st) {
     const CUtensorMap& a = *reinterpret_cast<const CUtensorMap*>(tmA);
     const CUtensorMap& b = *reinterpret_cast<const CUtensorMap*>(tmB);
+    const CUtensorMap& c = *reinterpret_cast<const CUtensorMap*>(tmC ? tmC : tmB);
     if (MODE != EPI_RAW && e.small && e.s >= 0 && e.s <= 62)
-        k_gemm_tc<MODE, true><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, true><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, c, MT, NT, KB, e, err);
     else
-        k_gemm_tc<MODE, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, c, MT, NT, KB, e, err);
 }
 
 template <int MODE>
@@ -509,19 +542,19 @@ cudaError_t configure_tc_kernels() {
     return configure_mode<EPI_DELTA>();
 }
 
-void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, int Kp, const EpiArgs& e,
-                    int num_sms, int* err, cudaStream_t st) {
+void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
+                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st) {
     if (R <= 0) return;
     int MT = (R + BM - 1) / BM, NT = Np / BN, KB = Kp / BK;
     int tiles = MT * NT;
     int grid = tiles < num_sms ? tiles : num_sms;
     switch (mode) {
-        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
-        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
-        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
-        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
-        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
-        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmB, MT, NT, KB, e, grid, err, st); break;
+        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
         default: break;
     }
 }

@@ -38,9 +38,11 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
                         cudaStream_t st);
 
 // The same GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
-// `tmA` and `tmB` are CUtensorMap objects (128-byte aligned, 128 bytes each).
-void launch_gemm_tc(int mode, const void* tmA, const void* tmB, int R, int Np, int Kp, const EpiArgs& e,
-                    int num_sms, int* err, cudaStream_t st);
+// `tmA` and `tmB` are CUtensorMap objects (128-byte aligned, 128 bytes each). EPI_DELTA, EPI_GELU
+// and EPI_LOGITS store their output through `tmC` (32-row x 32-byte boxes, 32-byte swizzle, over
+// all the rows of the output buffer); the other modes take nullptr.
+void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
+                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st);
 
 void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
                      int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st);

@@ -129,7 +129,7 @@ extern "C" int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, 
         alignas(128) CUtensorMap ta, tb;
         if ((rc = hs_internal_tmap(dev, &ta, da, Mp, Kp, TILE_M)) || (rc = hs_internal_tmap(dev, &tb, dw, Np, Kp, TILE_N)))
             return rc;
-        launch_gemm_tc(mode, &ta, &tb, (int)M, (int)Np, (int)Kp, e, num_sms, d_err, st);
+        launch_gemm_tc(mode, &ta, &tb, nullptr, (int)M, (int)Np, (int)Kp, e, num_sms, d_err, st);
     } else {
         launch_gemm_simple(mode, da, (int)Kp, (int)M, L, e, st);
     }

@@ -98,7 +98,7 @@ extern "C" int hs_op_linear_bench(hs_dev* dev, int path, uint32_t M, uint32_t N,
     cudaStream_t st;
     BK_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     auto launch = [&]() {
-        if (path == 0) launch_gemm_tc(EPI_ACT, &ta, &tb, (int)M, Np, Kp, e, num_sms, d_err, st);
+        if (path == 0) launch_gemm_tc(EPI_ACT, &ta, &tb, nullptr, (int)M, Np, Kp, e, num_sms, d_err, st);
         else launch_gemm_simple(EPI_ACT, a, Kp, (int)M, L, e, st);
     };
     for (int i = 0; i < warmup; i++) launch();

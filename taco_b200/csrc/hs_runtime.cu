@@ -98,6 +98,23 @@ int make_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, uint64_t rows, uin
     return HS_OK;
 }
 
+// The store tensor map of a GEMM epilogue: [rows, cols] elements of `esize` bytes with a row pitch
+// of `ld` elements, boxes of 32 rows x 32 bytes with the 32-byte swizzle.
+int make_store_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, CUtensorMapDataType type, int esize,
+                    uint64_t rows, uint64_t cols, uint64_t ld) {
+    cuuint64_t gdim[2] = {cols, rows};
+    cuuint64_t gstride[1] = {ld * (uint64_t)esize};
+    cuuint32_t box[2] = {(cuuint32_t)(32 / esize), 32};
+    cuuint32_t estr[2] = {1, 1};
+    if (((uintptr_t)base & 15) != 0 || (gstride[0] & 15) != 0)
+        return fail(HS_UNSUPPORTED, "a TMA tensor needs 16-byte aligned rows");
+    CUresult r = dev->encode(tm, type, 2, const_cast<void*>(base), gdim, gstride, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(HS_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return HS_OK;
+}
+
 template <typename T>
 int dalloc(T** p, size_t count, std::vector<void*>& owned) {
     void* q = nullptr;
@@ -198,6 +215,9 @@ struct hs_batch {
     alignas(128) CUtensorMap tm_q;   // qkv rows, 64-byte boxes (attention Q)
     alignas(128) CUtensorMap tm_k;   // the keys cache
     alignas(128) CUtensorMap tm_v;   // the transposed values cache
+    alignas(128) CUtensorMap ts_delta;  // epilogue stores: the residual delta (i32)
+    alignas(128) CUtensorMap ts_g;      // the GELU output (i8)
+    alignas(128) CUtensorMap ts_d16;    // the logit distances (u16)
 
     ~hs_batch() {
         if (model) cudaSetDevice(model->dev->ordinal);
@@ -272,16 +292,18 @@ int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D) {
     if (!rc) rc = upload(&dm, mm.data(), mm.size(), m->owned);
     if (rc) return rc;
     D.ld = LinearDev{dw, N, K, Np, Kp, db, dm, (int)L.rs.s};
-    // |acc| <= K * 128 * 128 for i8 operands, so an output is at most
-    // (K * 2^14 * |m| + |b * m| + 2^(s-1)) / 2^s + 1 in magnitude.
+    // An i8 activation is at most 128 in magnitude, so |acc_n| <= 128 * sum_k |W[n][k]| and an
+    // output is at most (|acc_n| * |m_n| + |b_n * m_n| + 2^(s-1)) / 2^s + 1 in magnitude.
     D.small = false;
     const int s = (int)L.rs.s;
     if (s >= 0 && s <= 62) {
         unsigned __int128 worst = 0;
         for (int n = 0; n < N; n++) {
+            uint64_t l1 = 0;
+            for (int k = 0; k < K; k++) l1 += (uint64_t)std::abs((int)L.w[(size_t)n * K + k]);
             const uint64_t am = (uint64_t)std::abs((int64_t)L.rs.m[n]);
             const uint64_t ab = (uint64_t)std::abs((int64_t)L.b[n]);
-            const unsigned __int128 t = (unsigned __int128)K * 16384 * am + (unsigned __int128)ab * am;
+            const unsigned __int128 t = (unsigned __int128)128 * l1 * am + (unsigned __int128)ab * am;
             worst = t > worst ? t : worst;
         }
         worst += s > 0 ? (unsigned __int128)1 << (s - 1) : 0;
@@ -314,11 +336,11 @@ int forward(hs_batch* b, int R) {
     uint64_t attn_ops = 0;
     for (int r = 0; r < R; r++) attn_ops += 4ULL * c.d * (b->h_rows[r].pos + 1);
     auto gemm = [&](int op, int mode, const int8_t* A, int lda, const CUtensorMap* tmA, const DevLinear& W,
-                    EpiArgs e) {
+                    EpiArgs e, const CUtensorMap* tmC) {
         ProfScope p(b, op, 2ULL * R * W.ld.N * W.ld.K);
         e.small = W.small ? 1 : 0;
         if (m->use_tc)
-            launch_gemm_tc(mode, tmA, &W.tm, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms, m->dev->d_err, st);
+            launch_gemm_tc(mode, tmA, &W.tm, tmC, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms, m->dev->d_err, st);
         else
             launch_gemm_simple(mode, A, lda, R, W.ld, e, st);
     };
@@ -352,7 +374,7 @@ int forward(hs_batch* b, int R) {
         e.hd = c.hd;
         e.n_ctx = c.n_ctx;
         e.d = c.d;
-        gemm(OP_GEMM_QKV, EPI_QKV, b->a, c.Dp, &b->tm_a, qkv, e);
+        gemm(OP_GEMM_QKV, EPI_QKV, b->a, c.Dp, &b->tm_a, qkv, e, nullptr);
         {
             ProfScope p(b, OP_ATTN, attn_ops);
             launch_attention_tc(&b->tm_q, &b->tm_k, &b->tm_v, b->d_groups, b->n_groups, c.L, l, c.H, c.n_ctx,
@@ -370,7 +392,7 @@ int forward(hs_batch* b, int R) {
         e.s = proj.ld.s;
         e.out32 = b->dbuf;
         e.ldo = c.d;
-        gemm(OP_GEMM_PROJ, EPI_DELTA, b->att, c.Dp, &b->tm_att, proj, e);
+        gemm(OP_GEMM_PROJ, EPI_DELTA, b->att, c.Dp, &b->tm_att, proj, e, &b->ts_delta);
         {
             ProfScope p(b, OP_LN, 0);
             launch_resid_layernorm(b->x, b->dbuf, R, c.d, Ld.ln2, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
@@ -385,7 +407,7 @@ int forward(hs_batch* b, int R) {
         e.ldo = c.Fp;
         e.gelu = Ld.gelu;
         e.gelu_off = Ld.gelu_off;
-        gemm(OP_GEMM_FC, EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e);
+        gemm(OP_GEMM_FC, EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e, &b->ts_g);
         e = EpiArgs{};
         e.R = R;
         e.N = c.d;
@@ -394,7 +416,7 @@ int forward(hs_batch* b, int R) {
         e.s = mlp.ld.s;
         e.out32 = b->dbuf;
         e.ldo = c.d;
-        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e);
+        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e, &b->ts_delta);
     }
     {
         ProfScope p(b, OP_LN, 0);
@@ -411,7 +433,7 @@ int forward(hs_batch* b, int R) {
     e.tmax = b->tmax;
     e.ldt = c.VT;
     e.last = m->logits_len - 1;
-    gemm(OP_GEMM_LOGITS, EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e);
+    gemm(OP_GEMM_LOGITS, EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e, &b->ts_d16);
     return HS_OK;
 }
 
@@ -826,6 +848,10 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
     CK(cudaMallocHost(&b->h_rows, sizeof(RowInfo) * R));
     CK(cudaMallocHost(&b->h_intervals, sizeof(uint64_t) * 3 * R));
     b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24);
+    if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d)) ||
+        (rc = make_store_tmap(m->dev, &b->ts_g, b->g, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, c.f, c.Fp)) ||
+        (rc = make_store_tmap(m->dev, &b->ts_d16, b->d16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, R, c.V, c.Vp)))
+        return rc;
     if ((rc = make_tmap(m->dev, &b->tm_a, b->a, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_att, b->att, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_g, b->g, R, c.Fp, TILE_M)))
@@ -949,7 +975,7 @@ int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, co
         alignas(128) CUtensorMap ta, tb;
         if ((rc = make_tmap(dev, &ta, da, Mp, Kp, TILE_M)) || (rc = make_tmap(dev, &tb, dw, Np, Kp, TILE_N)))
             return rc;
-        launch_gemm_tc(mode, &ta, &tb, (int)M, Np, Kp, e, dev->num_sms, dev->d_err, st);
+        launch_gemm_tc(mode, &ta, &tb, nullptr, (int)M, Np, Kp, e, dev->num_sms, dev->d_err, st);
     } else {
         launch_gemm_simple(mode, da, Kp, (int)M, L, e, st);
     }
