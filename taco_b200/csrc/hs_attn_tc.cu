@@ -53,6 +53,7 @@ struct __align__(8) ABars {
     uint64_t s_full[2], s_empty[2];
     uint64_t p_full[2], p_empty[2];
     uint64_t o_full;
+    uint64_t t_full;  // the exp table in shared memory
     uint32_t tmem_base;
 };
 
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             mbar_init(&bars->p_empty[i], 1);
         }
         mbar_init(&bars->o_full, 1);
+        mbar_init(&bars->t_full, 1);
         fence_barrier_init();
     }
     if (warp == EW + 1) {
@@ -136,7 +138,6 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         tc_fence_before();
     }
     const int tl = tlen < TABLE_MAX ? tlen : TABLE_MAX;
-    for (int i = threadIdx.x; i < tl; i += ATHREADS) sT[i] = table[i];
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
@@ -147,6 +148,10 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
+            // The exp table (its buffer is padded to 16 bytes), needed from pass 2 on.
+            const uint32_t tbytes = (uint32_t)((tl * 4 + 15) & ~15);
+            mbar_arrive_expect_tx(&bars->t_full, tbytes);
+            bulk_load(sT, table, tbytes, &bars->t_full);
             mbar_arrive_expect_tx(&bars->q_full, Q_BYTES);
             tma_load_2d(sQ, &tmQ, &bars->q_full, h * HDIM, (int)grp.first_row);
             int ks = 0, vs = 0;
@@ -283,6 +288,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             M = s1 > s2 ? s1 : s2;
         }
         // Pass 2: the row sum of e.
+        mbar_wait(&bars->t_full, 0, err, 26);
         uint64_t sum = 0;
         for (int c = 0; c < nch; c++, it++) {
             const int sb = it & 1;

@@ -785,7 +785,12 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
     if ((rc = upload(&m->pm, M.pos.m.data(), M.pos.m.size(), m->owned))) return rc;
     m->ps = (int)M.pos.s;
     if ((rc = upload_ln(m.get(), M.ln_f, m->lnf))) return rc;
-    if ((rc = upload(&m->attn_exp, M.attn_exp.data(), M.attn_exp.size(), m->owned))) return rc;
+    {
+        // Padded to a multiple of 4 entries: the attention kernel copies it in 16-byte units.
+        std::vector<int32_t> t(M.attn_exp);
+        t.resize((t.size() + 3) & ~(size_t)3, 0);
+        if ((rc = upload(&m->attn_exp, t.data(), t.size(), m->owned))) return rc;
+    }
     m->attn_len = (int)M.attn_exp.size();
     if ((rc = upload(&m->logits_exp, M.logits_exp.data(), M.logits_exp.size(), m->owned))) return rc;
     m->logits_len = (int)M.logits_exp.size();
