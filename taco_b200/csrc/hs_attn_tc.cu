@@ -92,7 +92,7 @@ __device__ __forceinline__ int32_t dist_of(int64_t M, int32_t dot, int32_t sm, i
     }
 }
 
-template <bool NARROW>
+template <bool NARROW, bool SSHI>
 __global__ void __launch_bounds__(ATHREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnGroup* groups, int L, int layer, int H,
@@ -241,6 +241,22 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         const bool fast = ss >= 0 && ss <= 62;
         const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
         const int32_t last = tl - 1;
+        // The last position of this warp's 32 rows: a key slice past it is masked for every lane.
+        const int wlast = (int)grp.pos0 + g * 32 + 31;
+        // The table index min(M - score(dot), last); NARROW: the score is the low word of the
+        // 64-bit shift (one shift of the high word when ss >= 32, a funnel shift below).
+        auto dist = [&](int64_t M, int32_t dot) -> int32_t {
+            if constexpr (NARROW) {
+                const int64_t t = (int64_t)dot * (int64_t)sm + hround;
+                int32_t score;
+                if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
+                else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+                const int32_t dd = (int32_t)M - score;
+                return dd < last ? dd : last;
+            } else {
+                return dist_of<false>(M, dot, sm, ss, fast, hround, last);
+            }
+        };
         int it = 0;
         // Pass 1: the max and min dot over the row's causal keys.
         int32_t maxd = INT32_MIN, mind = INT32_MAX;
@@ -255,7 +271,9 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
             const int j0 = c * KC + qt * 32;
-            if (j0 + 31 <= rpos) {
+            if (j0 > wlast) {
+                // every key of this slice is masked for this warp's rows
+            } else if (j0 + 31 <= rpos) {
 #pragma unroll
                 for (int q = 0; q < 32; q++) {
                     int32_t dv = (int32_t)v[q];
@@ -301,15 +319,15 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
             const int j0 = c * KC + qt * 32;
-            if (j0 + 31 <= rpos) {
+            if (j0 > wlast) {
+                // masked for every lane
+            } else if (j0 + 31 <= rpos) {
 #pragma unroll
-                for (int q = 0; q < 32; q++)
-                    sum += (uint32_t)sT[dist_of<NARROW>(M, (int32_t)v[q], sm, ss, fast, hround, last)];
+                for (int q = 0; q < 32; q++) sum += (uint32_t)sT[dist(M, (int32_t)v[q])];
             } else {
 #pragma unroll
                 for (int q = 0; q < 32; q++)
-                    if (j0 + q <= rpos)
-                        sum += (uint32_t)sT[dist_of<NARROW>(M, (int32_t)v[q], sm, ss, fast, hround, last)];
+                    if (j0 + q <= rpos) sum += (uint32_t)sT[dist(M, (int32_t)v[q])];
             }
         }
         named_bar(1, ETH);  // everyone has read sX (pass 1) before it is reused
@@ -343,13 +361,16 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             mbar_arrive(&bars->s_empty[sb]);
             const int j0 = c * KC + qt * 32;
             auto prob = [&](int32_t dot) -> uint32_t {
-                const uint32_t e = (uint32_t)sT[dist_of<NARROW>(M, dot, sm, ss, fast, hround, last)];
+                const uint32_t e = (uint32_t)sT[dist(M, dot)];
                 const uint64_t t = (uint64_t)e * ml;
                 const uint64_t u = (uint64_t)e * mh + (t >> 32);
                 return (uint32_t)(u >> psh);
             };
             uint32_t pv[32];
-            if (j0 + 31 <= rpos) {
+            if (j0 > wlast) {
+#pragma unroll
+                for (int q = 0; q < 32; q++) pv[q] = 0u;
+            } else if (j0 + 31 <= rpos) {
 #pragma unroll
                 for (int q = 0; q < 32; q++) pv[q] = prob((int32_t)v[q]);
             } else {
@@ -423,9 +444,13 @@ __global__ void __launch_bounds__(ATHREADS, 1)
 }  // namespace
 
 cudaError_t configure_attn_tc() {
-    cudaError_t e = cudaFuncSetAttribute(k_attention_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_attention_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+    const void* fns[3] = {(const void*)k_attention_tc<true, true>, (const void*)k_attention_tc<true, false>,
+                          (const void*)k_attention_tc<false, false>};
+    for (const void* f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 bool attention_tc_supported(int hd, int n_ctx, int tlen) {
@@ -440,12 +465,15 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
     const CUtensorMap& q = *reinterpret_cast<const CUtensorMap*>(tmQ);
     const CUtensorMap& k = *reinterpret_cast<const CUtensorMap*>(tmK);
     const CUtensorMap& v = *reinterpret_cast<const CUtensorMap*>(tmV);
-    if (ss >= 21 && ss <= 62)
-        k_attention_tc<true><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os, table,
-                                                           tlen, P, att, lda, err);
+    if (ss >= 32 && ss <= 62)
+        k_attention_tc<true, true><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os,
+                                                                 table, tlen, P, att, lda, err);
+    else if (ss >= 21 && ss < 32)
+        k_attention_tc<true, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os,
+                                                                  table, tlen, P, att, lda, err);
     else
-        k_attention_tc<false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os, table,
-                                                            tlen, P, att, lda, err);
+        k_attention_tc<false, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om,
+                                                                   os, table, tlen, P, att, lda, err);
 }
 
 }  // namespace hs
