@@ -14,8 +14,10 @@ value  = input bytes of all ranks / max over ranks of the device time of the K s
          events around every pass on the batch stream, the token rows already on the device);
 e2e    = the same bytes / wall time of the K C-ABI calls with host buffers (row upload, planning,
          interval read back inside);
-roofline = the tcgen05 GEMMs (the dominant kernel class): algorithmic int8 ops / their CUDA-event
-         time, against the int8 tensor peak measured in this run (torch._int_mm, cuBLASLt);
+roofline = the kernel with the largest share of the pass time: algorithmic int8 ops (tensor-bound
+         kernels) or algorithmic bytes (HBM-bound kernels) per launch / its mean CUDA-event launch
+         time, against the int8 tensor peak measured in this run (torch._int_mm, cuBLASLt) or the
+         measured HBM copy bandwidth (MEASURED_PEAKS.json); `rooflines` has every kernel class;
 cpu_baseline = the CPU oracle's fast path (a C++ restatement of the reference CPU engine) on a
          bounded sample of the same windows, all host threads, rank 0 at N = 1.
 Extra fields: the GEMM microbench and the unfold decode step.
@@ -144,13 +146,58 @@ def measured_int8_peak_tops(device: int) -> dict:
     return {"tops": 2.0 * n ** 3 / (best * 1e-3) / 1e12, "how": "torch._int_mm int8 8192^3, best of 10, CUDA events"}
 
 
-def read_traffic() -> float | None:
-    """DRAM bytes per launch of the dominant GEMM from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "gemm_tc_fold.md"
+def read_traffic() -> dict:
+    """DRAM bytes (read + write) per launch of each kernel class, from the committed ncu summary of
+    one 16384-row fold pass (the same pass shape as every pass of this benchmark)."""
+    p = ROOT / "profiles" / "fold_pass_traffic.md"
     if not p.exists():
+        return {}
+    return {m.group(1): float(m.group(2))
+            for m in re.finditer(r"traffic_bytes_per_launch\[(\w+)\]:\s*([0-9.eE+]+)", p.read_text())}
+
+
+def measured_hbm_gbs() -> float | None:
+    """The HBM copy bandwidth of MEASURED_PEAKS.json (driver-written), if present."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"])
+    except (OSError, ValueError, KeyError):
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", p.read_text())
-    return float(m.group(1)) if m else None
+
+
+def rooflines(prof: dict, info, peak_tops: float | None, hbm_gbs: float | None, traffic: dict) -> dict:
+    """Achieved work per launch / mean launch time for each kernel class of the fold pass."""
+    d, V, L = info.d_model, info.vocab, info.n_layer
+    vt = (V + 127) // 128
+    rows = prof["pass"]["ops"]  # the rows of the timed passes
+    out = {}
+
+    def add(name, keys, bound, work, unit):
+        ms = sum(prof[k]["ms"] for k in keys if k in prof)
+        launches = sum(prof[k]["launches"] for k in keys if k in prof)
+        if not ms or not launches:
+            return
+        per_launch = work / launches
+        achieved = per_launch / (ms * 1e-3 / launches) / (1e12 if bound == "tensor" else 1e9)
+        peak = peak_tops if bound == "tensor" else hbm_gbs
+        out[name] = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak if peak else None,
+                     "traffic": traffic.get(name), "work_per_launch": per_launch,
+                     "share": ms / prof["pass"]["ms"], "launches": launches,
+                     "mean_launch_us": 1000 * ms / launches}
+
+    gemm_keys = [k for k in prof if k.startswith("gemm")]
+    add("gemm", gemm_keys, "tensor", sum(prof[k]["ops"] for k in gemm_keys), "TOP/s")
+    add("attention", ["attention"], "tensor", prof["attention"]["ops"], "TOP/s")
+    # LayerNorm: layer 0's first one reads x and writes a (5d bytes per row); the other 2L ones
+    # also read the residual delta and write x back (13d bytes per row).
+    add("layernorm", ["layernorm"], "hbm", rows * d * (5 + 13 * 2 * L), "GB/s")
+    # The coder op: the row's logit distances (2V bytes) and tile maxima (8 per 128 symbols) in,
+    # one interval (24 bytes) out.
+    add("coder", ["coder"], "hbm", rows * (2 * V + 8 * vt + 24), "GB/s")
+    # The embedding: two int8 rows in, the i32 residual row out.
+    add("embed", ["embed"], "hbm", rows * (2 * d + 4 * d), "GB/s")
+    return out
 
 
 def cpu_baseline(model_bytes: bytes, windows: np.ndarray, eot: int, lens: np.ndarray, threads: int,
@@ -235,13 +282,17 @@ def main():
         pg = True
 
     from taco_b200 import backend as B
-    from taco_b200 import synth
+    from taco_b200 import shard, synth
 
     model_bytes = synth.gpt2_hsm(124)
     vocab = synth.vocabulary()
     lens = synth.token_lengths(vocab)
     eot = synth.VOCAB - 1
-    windows = synth.zipf_windows(args.windows, WINDOW, seed=1000 + rank)
+    # The job: windows x world windows of seeded text, dealt round-robin to the GPUs (weak scaling:
+    # each GPU gets `windows`); no collective touches them.
+    n_total = args.windows * world
+    all_windows = synth.zipf_windows(n_total, WINDOW, seed=1000)
+    windows = all_windows[shard.deal(n_total, world, rank)]
     slots, inputs, coded = window_rows(windows, eot)
     kinds = np.zeros(slots.size, np.uint32)
     step_bytes = int(lens[coded.astype(np.int64)].sum())
@@ -283,12 +334,7 @@ def main():
     barrier()
     clk = clocks.stop()
 
-    dev_s = prof["pass"]["ms"] / 1e3
-    wall_s = sum(wall)
-    times = torch.tensor([dev_s, wall_s], dtype=torch.float64, device=f"cuda:{local}")
-    if pg:
-        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
-    dev_s, wall_s = float(times[0]), float(times[1])
+    dev_s, wall_s = shard.max_over_ranks([prof["pass"]["ms"] / 1e3, sum(wall)], device=f"cuda:{local}")
     total_bytes = step_bytes * args.steps * world
     total_rows = slots.size * args.steps * world
 
@@ -305,7 +351,11 @@ def main():
         for k in kernels:
             if prof[k]["ops"] and prof[k]["ms"]:
                 kernels[k]["tops"] = round(prof[k]["ops"] / (prof[k]["ms"] * 1e-3) / 1e12, 1)
-        traffic = read_traffic()
+        roofs = rooflines(prof, model.info, peak["tops"] if peak else None, measured_hbm_gbs(), read_traffic())
+        dominant = max(roofs, key=lambda k: roofs[k]["share"])
+        roof = dict(roofs[dominant], kernel=dominant)
+        roof["peak_source"] = ((peak["how"] if peak else None) if roof["bound"] == "tensor"
+                               else "MEASURED_PEAKS.json hbm_gbs (STREAM-style copy)")
         result = {
             "metric": METRIC, "value": total_bytes / dev_s / 1e6, "unit": "MB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dev_s / args.steps,
@@ -315,19 +365,15 @@ def main():
                                    "all positions in one forward pass per window, coder interval per row",
                        "model": "GPT-2 124M .hsm from seeded N(0,0.02) (taco_b200/synth.py)",
                        "windows_per_gpu": args.windows, "window_tokens": WINDOW, "max_rows_per_pass": args.max_rows,
-                       "parallelism": f"windows dealt to {world} GPU(s), no collective",
+                       "parallelism": f"{n_total} windows dealt round-robin to {world} GPU(s), no collective",
                        "l2": "inputs larger than L2: each step streams 124 MB of weights per pass and "
                              "9.7 GB of KV cache"},
             "tokens_per_s": total_rows / dev_s,
             "e2e": {"value": total_bytes / wall_s / 1e6, "unit": "MB/s",
                     "h2d_bytes_per_step": int(slots.size * 24), "d2h_bytes_per_step": int(slots.size * 24)},
-            "roofline": {"bound": "tensor", "kernel": "tcgen05 int8 GEMMs (qkv, proj, fc, mlp, logits)",
-                         "achieved": achieved, "peak": peak["tops"] if peak else None, "unit": "TOP/s",
-                         "frac": achieved / peak["tops"] if peak else None,
-                         "frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
-                         "peak_source": peak["how"] if peak else None,
-                         "traffic": traffic,
-                         "ops_per_launch": gemm_ops / max(1, gemm_launches)},
+            "roofline": roof,
+            "rooflines": roofs,
+            "gemm_frac_of_nominal_4500": achieved / NOMINAL_INT8_TOPS,
             "clocks": clk,
             "gpu_launches": launches,
             "kernels": kernels,

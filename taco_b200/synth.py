@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import hashlib
 import json
+import os
 import struct
 from dataclasses import dataclass
 from pathlib import Path
@@ -327,7 +328,7 @@ def gpt2_hsm(seed: int = 124, cache: bool = True, shape: Shape = GPT2) -> bytes:
     data = write_hsm(tensors, vocabulary(vocab=shape.vocab), eps, shape)
     if cache:
         CACHE.mkdir(exist_ok=True)
-        tmp = path.with_suffix(".tmp")
+        tmp = path.with_suffix(f".{os.getpid()}.tmp")  # one per process: ranks may build it at once
         tmp.write_bytes(data)
         tmp.replace(path)
     return data
