@@ -10,8 +10,10 @@ namespace hs {
 constexpr int TILE_M = 128;
 constexpr int TILE_N = 256;
 constexpr int TILE_K = 128;
-// Columns of one logits tile: the coder op reads the max of each tile (LOGIT_TILE columns).
+// Columns of one logits tile: the coder op reads the max of each tile (LOGIT_TILE columns; a
+// model with a 16-bit ln_f uses tiles of LOGIT_TILE_WIDE columns).
 constexpr int LOGIT_TILE = 128;
+constexpr int LOGIT_TILE_WIDE = 64;
 // The largest logit table the coder op keeps in shared memory (entries).
 constexpr int MAX_LOGIT_TABLE = 16384;
 // The largest vocabulary of the coder op (8 warps x 32 steps x 256 symbols).
@@ -45,8 +47,9 @@ struct LayerDev {
     int score_s;
     int32_t out_m;
     int out_s;
-    const int8_t* gelu;  // i8 outputs
-    int gelu_off;        // 2^(b-1): the input range is [-off, off - 1]
+    const int8_t* gelu;      // i8 outputs
+    const int16_t* gelu16;   // i16 outputs (version 2), or null
+    int gelu_off;            // 2^(b-1): the input range is [-off, off - 1]
 };
 
 // One row of a pass: the slot, the input token, the position, and the coder query
@@ -74,6 +77,8 @@ enum EpiMode : int {
                      // i32 range first gives the same result, because |x| <= R < 2^30.
     EPI_QKV = 6,     // as EPI_ACT; q (columns < d) to out8, k to the keys cache and v to the
                      // transposed values cache at the row's (slot, pos) (reference.rs:241-246)
+    EPI_GELU16 = 7,  // as EPI_GELU with an i16 table (version 2 models): the output as two i8 planes,
+                     // hi = floor(v / 256) to out8 and lo = (v mod 256) - 128 to out8_lo
 };
 
 struct EpiArgs {
@@ -92,7 +97,13 @@ struct EpiArgs {
     int64_t* tmax;
     int ldt;
     int last;
-    int small;  // EPI_LOGITS: every logit is below 2^30 in magnitude (host bound), 32-bit arithmetic
+    int small;  // every rescaled output is below 2^30 in magnitude (host bound): 32-bit arithmetic
+    // Version 2 (i16 activations as two i8 planes, v = 256 hi + lo + 128): the i16 GELU table and
+    // the lo plane of EPI_GELU16, and for a GEMM over such planes the row sums of the weights
+    // (the 128 * sum_k W[n][k] term of the recombination).
+    const int16_t* gelu16;
+    int8_t* out8_lo;
+    const int64_t* wsum;
     int32_t* out32;
     // EPI_QKV: the rows of the pass and the caches of this layer.
     const RowInfo* rows;

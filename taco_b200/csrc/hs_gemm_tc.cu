@@ -53,8 +53,9 @@ struct Cfg {
     static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : (MODE == EPI_QKV ? EPI_WARPS * VT_TILE : 0);
     static constexpr int STORE_BUFS = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 2 : (MODE == EPI_GELU ? 1 : 0);
     static constexpr int STORE_WARP = 1024 * STORE_BUFS;
+    static constexpr int WSUM = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 2 * BN * 8 : 0;  // s_w (WIDE)
     static constexpr size_t SMEM =
-        (size_t)STAGES * STAGE_BYTES + EXTRA + EPI_WARPS * STORE_WARP + 2 * BN * 12 + 256 + 1024;
+        (size_t)STAGES * STAGE_BYTES + EXTRA + EPI_WARPS * STORE_WARP + 2 * BN * 12 + WSUM + 256 + 1024;
 };
 
 struct __align__(8) Bars {
@@ -99,23 +100,30 @@ __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowIn
     else e.vc[(head * e.hd + c) * e.n_ctx + ri.pos] = o;
 }
 
-template <int MODE, bool S32>
+// WIDE (version 2 models): the activations are i16, as two i8 planes (tmA: hi, tmA2: lo). Tiles
+// are 128 x 128; each stage holds both A planes and a 128-row B tile (the same 48 KB), the MMA warp
+// accumulates hi and lo into two TMEM accumulators of 128 columns, and the epilogue recombines
+// v = 256 acc_hi + acc_lo + 128 sum_k W[n][k] exactly in i64 (hardshell.cu:798-830 wide_dot).
+template <int MODE, bool S32, bool WIDE>
 __global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              const __grid_constant__ CUtensorMap tmC, int MT, int NT,
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+              const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC, int MT, int NT,
               int KB, EpiArgs e, int* err) {
     constexpr int STAGES = Cfg<MODE>::STAGES;
+    constexpr int TN = WIDE ? 128 : BN;  // columns of one tile
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     int8_t* s_gelu = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * STAGE_BYTES);
     uint8_t* s_store = smem + (size_t)STAGES * STAGE_BYTES + Cfg<MODE>::EXTRA;  // [EPI_WARPS][STORE_WARP]
     int64_t* s_c = reinterpret_cast<int64_t*>(s_store + EPI_WARPS * Cfg<MODE>::STORE_WARP);  // [2][BN]
     int32_t* s_m = reinterpret_cast<int32_t*>(s_c + 2 * BN);                                 // [2][BN]
-    Bars* bars = reinterpret_cast<Bars*>(s_m + 2 * BN);
+    int64_t* s_w = reinterpret_cast<int64_t*>(s_m + 2 * BN);                                 // [2][BN] (WIDE)
+    Bars* bars = reinterpret_cast<Bars*>(s_w + (WIDE ? 2 * BN : 0));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
+        if (WIDE) prefetch_tmap(&tmA2);
         prefetch_tmap(&tmB);
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&bars->full[s], 1);
@@ -158,7 +166,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
                     mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
                     tma_load_2d(sa, &tmA, &bars->full[stage], kb * BK, mt * BM);
-                    tma_load_2d(sa + A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * BN);
+                    if (WIDE) {
+                        // [A hi | A lo | B (128 rows)]: 16 + 16 + 16 KB.
+                        tma_load_2d(sa + A_BYTES, &tmA2, &bars->full[stage], kb * BK, mt * BM);
+                        tma_load_2d(sa + 2 * A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * TN);
+                    } else {
+                        tma_load_2d(sa + A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * BN);
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
@@ -168,7 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = idesc_i8(BM, BN, true, true);
+            const uint32_t idesc = idesc_i8(BM, TN, true, true);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -186,11 +200,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     tc_fence_after();
                     uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
-                    uint32_t sb = sa + A_BYTES;
+                    if (WIDE) {
+                        // hi plane into columns [0, 128), lo plane into [128, 256) of this buffer.
+                        const uint32_t sl = sa + A_BYTES, sb = sa + 2 * A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / UMMA_K; k++) {
-                        mma_i8(d, sdesc_sw128(sa + k * UMMA_K), sdesc_sw128(sb + k * UMMA_K), idesc,
-                               (kb | k) != 0 ? 1u : 0u);
+                        for (int k = 0; k < BK / UMMA_K; k++) {
+                            mma_i8(d, sdesc_sw128(sa + k * UMMA_K), sdesc_sw128(sb + k * UMMA_K), idesc,
+                                   (kb | k) != 0 ? 1u : 0u);
+                            mma_i8(d + TN, sdesc_sw128(sl + k * UMMA_K), sdesc_sw128(sb + k * UMMA_K), idesc,
+                                   (kb | k) != 0 ? 1u : 0u);
+                        }
+                    } else {
+                        uint32_t sb = sa + A_BYTES;
+#pragma unroll
+                        for (int k = 0; k < BK / UMMA_K; k++) {
+                            mma_i8(d, sdesc_sw128(sa + k * UMMA_K), sdesc_sw128(sb + k * UMMA_K), idesc,
+                                   (kb | k) != 0 ? 1u : 0u);
+                        }
                     }
                     mma_commit(&bars->empty[stage]);
                     if (++stage == STAGES) {
@@ -236,19 +262,22 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int mt = t % MT, nt = t / MT;
             const int acc = i & 1;
             const uint32_t aphase = (i >> 1) & 1;
-            const int col0 = nt * BN;
+            const int col0 = nt * TN;
             // Stage this tile's column parameters (double-buffered by the accumulator parity).
-            {
+            // WIDE: the raw bias (the epilogue rescales in 128 bits) and the weight row sums.
+            if (et < TN) {
                 int n = col0 + et;
                 int32_t m = 0;
-                int64_t c = 0;
+                int64_t c = 0, w = 0;
                 if (n < e.N) {
                     m = e.m[n];
                     int64_t b = (MODE == EPI_LOGITS || MODE == EPI_RAW) ? 0 : (int64_t)e.b[n];
-                    c = fast ? b * (int64_t)m + hround : b;
+                    c = (fast && !WIDE) ? b * (int64_t)m + hround : b;
+                    if (WIDE) w = e.wsum[n];
                 }
                 s_m[acc * BN + et] = m;
                 s_c[acc * BN + et] = c;
+                if (WIDE) s_w[acc * BN + et] = w;
             }
             named_bar(1, EPI_THREADS);
             // On a timeout the error word is set and every later wait returns at once; the warps keep
@@ -276,6 +305,95 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t taddr = tmem_base + ((uint32_t)(g * 32) << 16) + (uint32_t)(acc * BN);
             const int32_t* pm = s_m + acc * BN;
             const int64_t* pc = s_c + acc * BN;
+            if constexpr (WIDE) {
+                // This thread: row `row`, columns half * 64 .. + 63 of the 128-column tile; hi at
+                // TMEM columns [0, 128), lo at [128, 256).
+                const int64_t* pw = s_w + acc * BN;
+                auto value = [&](uint32_t hi, uint32_t lo, int n) -> int64_t {
+                    return 256 * (int64_t)(int32_t)hi + (int64_t)(int32_t)lo + 128 * pw[n];
+                };
+                if constexpr (MODE == EPI_LOGITS) {
+                    // One logits tile of LOGIT_TILE_WIDE = 64 columns per thread: the running max per
+                    // 16-column chunk and the packed distance fix-up of the 8-bit path.
+                    const uint32_t lastv = (uint32_t)e.last;
+                    const uint32_t last2 = lastv | (lastv << 16);
+                    uint32_t pk[32];
+                    int64_t mc[4];
+                    int64_t run = -SCORE_LIMIT;
+#pragma unroll
+                    for (int ch = 0; ch < 4; ch++) {
+                        const int c0 = half * 64 + ch * 16;
+                        uint32_t vh[16], vl[16];
+                        __syncwarp();
+                        tmem_ld16(taddr + c0, vh);
+                        tmem_ld16(taddr + TN + c0, vl);
+                        tmem_ld_wait();
+                        int64_t l[16];
+#pragma unroll
+                        for (int q = 0; q < 16; q++) {
+                            l[q] = col0 + c0 + q < e.N
+                                       ? (int64_t)clamp128(rescale128(value(vh[q], vl[q], c0 + q), pm[c0 + q], (uint32_t)s),
+                                                           -SCORE_LIMIT, SCORE_LIMIT)
+                                       : -SCORE_LIMIT;
+                            run = l[q] > run ? l[q] : run;
+                        }
+                        mc[ch] = run;
+#pragma unroll
+                        for (int q = 0; q < 16; q += 2) {
+                            const int64_t d0 = run - l[q], d1 = run - l[q + 1];
+                            const uint32_t a0 = d0 < (int64_t)lastv ? (uint32_t)d0 : lastv;
+                            const uint32_t a1 = d1 < (int64_t)lastv ? (uint32_t)d1 : lastv;
+                            pk[ch * 8 + (q >> 1)] = a0 | (a1 << 16);
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&bars->tempty[acc]);
+                    if (col0 + half * 64 < e.N) {
+#pragma unroll
+                        for (int ch = 0; ch < 4; ch++) {
+                            const int64_t sh = run - mc[ch];
+                            const uint32_t a = sh < (int64_t)lastv ? (uint32_t)sh : lastv;
+                            const uint32_t a2 = a | (a << 16);
+#pragma unroll
+                            for (int w = 0; w < 8; w++)
+                                pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
+                            if (col0 + half * 64 + ch * 16 < e.N)
+                                store_piece(make_uint4(pk[ch * 8], pk[ch * 8 + 1], pk[ch * 8 + 2], pk[ch * 8 + 3]),
+                                            make_uint4(pk[ch * 8 + 4], pk[ch * 8 + 5], pk[ch * 8 + 6], pk[ch * 8 + 7]),
+                                            col0 + half * 64 + ch * 16, mt * BM + g * 32);
+                        }
+                        const int tile = nt * 2 + half;
+                        if (row_ok && tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run;
+                    }
+                    continue;
+                } else if constexpr (MODE == EPI_DELTA) {
+#pragma unroll 1
+                    for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+                        uint32_t vh[32], vl[32];
+                        __syncwarp();
+                        tmem_ld32(taddr + c0, vh);
+                        tmem_ld32(taddr + TN + c0, vl);
+                        tmem_ld_wait();
+                        const int colb = col0 + c0;
+                        if (colb >= e.N) continue;
+                        int32_t o[32];
+#pragma unroll
+                        for (int q = 0; q < 32; q++)
+                            o[q] = (int32_t)clamp128(rescale128(value(vh[q], vl[q], c0 + q) + pc[c0 + q], pm[c0 + q],
+                                                                (uint32_t)s),
+                                                     INT32_MIN, INT32_MAX);
+#pragma unroll
+                        for (int p = 0; p < 4; p++)
+                            if (colb + 8 * p < e.N)
+                                store_piece(make_uint4(o[8 * p], o[8 * p + 1], o[8 * p + 2], o[8 * p + 3]),
+                                            make_uint4(o[8 * p + 4], o[8 * p + 5], o[8 * p + 6], o[8 * p + 7]),
+                                            colb + 8 * p, mt * BM + g * 32);
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&bars->tempty[acc]);
+                    continue;
+                }
+            }
             if (MODE == EPI_LOGITS) {
                 // One TMEM pass over this thread's 128 columns (one logits tile). Per 16-column chunk:
                 // the running max M_c after the chunk and the distances min(M_c - l, last) as packed
@@ -473,6 +591,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                             for (int q = 0; q < 32; q++)
                                 if (colb + q < e.N) dst[q] = (int8_t)(packed[q >> 2] >> (8 * (q & 3)));
                         }
+                    } else if (MODE == EPI_GELU16) {
+                        // i16 GELU outputs as two i8 planes (hi, lo): v = 256 hi + lo + 128.
+                        uint32_t ph[8], pl[8];
+#pragma unroll
+                        for (int q = 0; q < 8; q++) ph[q] = pl[q] = 0;
+#pragma unroll
+                        for (int q = 0; q < 32; q++) {
+                            const auto y = rescale_e<S32>(v[q], pm[c0 + q], pc[c0 + q], s, fast);
+                            const auto in = clamp_e(y, -e.gelu_off, e.gelu_off - 1);
+                            const int32_t g16 = __ldg(e.gelu16 + (int64_t)in + e.gelu_off);
+                            ph[q >> 2] |= (uint32_t)(uint8_t)(int8_t)(g16 >> 8) << (8 * (q & 3));
+                            pl[q >> 2] |= (uint32_t)(uint8_t)(int8_t)((g16 & 255) - 128) << (8 * (q & 3));
+                        }
+                        int8_t* dh = e.out8 + (size_t)row * e.ldo + colb;
+                        int8_t* dl = e.out8_lo + (size_t)row * e.ldo + colb;
+                        if (full && (e.ldo & 15) == 0) {
+                            reinterpret_cast<uint4*>(dh)[0] = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                            reinterpret_cast<uint4*>(dh)[1] = make_uint4(ph[4], ph[5], ph[6], ph[7]);
+                            reinterpret_cast<uint4*>(dl)[0] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+                            reinterpret_cast<uint4*>(dl)[1] = make_uint4(pl[4], pl[5], pl[6], pl[7]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 32; q++)
+                                if (colb + q < e.N) {
+                                    dh[q] = (int8_t)(ph[q >> 2] >> (8 * (q & 3)));
+                                    dl[q] = (int8_t)(pl[q >> 2] >> (8 * (q & 3)));
+                                }
+                        }
                     } else if (MODE == EPI_DELTA) {
                         int32_t o[32];
 #pragma unroll
@@ -510,24 +656,36 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 template <int MODE>
-void launch_mode(const void* tmA, const void* tmB, const void* tmC, int MT, int NT, int KB, const EpiArgs& e, int grid,
-                 int* err, cudaStream_t st) {
+void launch_mode(const void* tmA, const void* tmA2, const void* tmB, const void* tmC, int MT, int NT, int KB,
+                 const EpiArgs& e, int grid, int* err, cudaStream_t st) {
     const CUtensorMap& a = *reinterpret_cast<const CUtensorMap*>(tmA);
     const CUtensorMap& b = *reinterpret_cast<const CUtensorMap*>(tmB);
     const CUtensorMap& c = *reinterpret_cast<const CUtensorMap*>(tmC ? tmC : tmB);
+    if constexpr (MODE == EPI_DELTA || MODE == EPI_LOGITS) {
+        if (tmA2) {
+            const CUtensorMap& a2 = *reinterpret_cast<const CUtensorMap*>(tmA2);
+            k_gemm_tc<MODE, false, true><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, a2, b, c, MT, NT, KB, e, err);
+            return;
+        }
+    }
     if (MODE != EPI_RAW && e.small && e.s >= 0 && e.s <= 62)
-        k_gemm_tc<MODE, true><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, c, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, true, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
     else
-        k_gemm_tc<MODE, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, b, c, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, false, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
 }
 
 template <int MODE>
 cudaError_t configure_mode() {
-    cudaError_t r = cudaFuncSetAttribute(k_gemm_tc<MODE, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t r = cudaFuncSetAttribute(k_gemm_tc<MODE, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)Cfg<MODE>::SMEM);
     if (r != cudaSuccess) return r;
-    return cudaFuncSetAttribute(k_gemm_tc<MODE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)Cfg<MODE>::SMEM);
+    r = cudaFuncSetAttribute(k_gemm_tc<MODE, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Cfg<MODE>::SMEM);
+    if (r != cudaSuccess) return r;
+    if constexpr (MODE == EPI_DELTA || MODE == EPI_LOGITS)
+        r = cudaFuncSetAttribute(k_gemm_tc<MODE, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)Cfg<MODE>::SMEM);
+    return r;
 }
 
 }  // namespace
@@ -539,22 +697,24 @@ cudaError_t configure_tc_kernels() {
     if ((e = configure_mode<EPI_LOGITS>()) != cudaSuccess) return e;
     if ((e = configure_mode<EPI_RAW>()) != cudaSuccess) return e;
     if ((e = configure_mode<EPI_QKV>()) != cudaSuccess) return e;
+    if ((e = configure_mode<EPI_GELU16>()) != cudaSuccess) return e;
     return configure_mode<EPI_DELTA>();
 }
 
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
-                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st) {
+                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2) {
     if (R <= 0) return;
-    int MT = (R + BM - 1) / BM, NT = Np / BN, KB = Kp / BK;
+    int MT = (R + BM - 1) / BM, NT = Np / (tmA2 ? 128 : BN), KB = Kp / BK;
     int tiles = MT * NT;
     int grid = tiles < num_sms ? tiles : num_sms;
     switch (mode) {
-        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_GELU16: launch_mode<EPI_GELU16>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
         default: break;
     }
 }

@@ -64,8 +64,21 @@ __global__ void k_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, 
 
 // ---- LayerNorm (crates/hardshell/src/layernorm.rs:201-256), one block per row ----
 
+// A LayerNorm output: i8 (out_lo == nullptr), or an i16 value (ln_f_bits = 16) stored as two i8
+// planes, hi = floor(v / 256) in `out` and lo = (v mod 256) - 128 in `out_lo`, so that
+// v = 256 hi + lo + 128 (the limb split of crates/hardshell-cuda/kernels/hardshell.cu:549-556).
+__device__ __forceinline__ void ln_put(int64_t y, int8_t* out, int8_t* out_lo, size_t idx) {
+    if (!out_lo) {
+        out[idx] = (int8_t)clamp64(y, -127, 127);
+        return;
+    }
+    const int32_t v = (int32_t)clamp64(y, -32767, 32767);
+    out[idx] = (int8_t)(v >> 8);
+    out_lo[idx] = (int8_t)((v & 255) - 128);
+}
+
 __global__ void k_layernorm(const int32_t* x, int R, int d, LnDev ln, int ln_k, int ln_j, uint64_t eps, int8_t* out,
-                            int ldo) {
+                            int ldo, int8_t* out_lo) {
     __shared__ int64_t sh[32];
     __shared__ uint64_t shu[64];
     int r = blockIdx.x;
@@ -114,7 +127,7 @@ __global__ void k_layernorm(const int32_t* x, int R, int d, LnDev ln, int ln_k, 
             i128 c = (i128)ln.b[j] << (ln.s - ln.beta_frac);
             y = shift_round128((i128)((u128)t * (u128)(i128)ln.m + (u128)c), ln.s, 126);
         }
-        out[(size_t)r * ldo + j] = (int8_t)clamp128(y, -127, 127);
+        ln_put((int64_t)clamp128(y, -32767, 32767), out, out_lo, (size_t)r * ldo + j);
     }
 }
 
@@ -127,7 +140,7 @@ __global__ void k_layernorm(const int32_t* x, int R, int d, LnDev ln, int ln_k, 
 // registers (RPL values per lane).
 template <int RPL>
 __global__ void __launch_bounds__(256, RPL <= 32 ? 4 : 1) k_resid_ln(int32_t* x, const int32_t* delta, int R, int d, LnDev ln, int ln_k,
-                                                  int ln_j, uint64_t eps, int8_t* out, int ldo) {
+                                                  int ln_j, uint64_t eps, int8_t* out, int ldo, int8_t* out_lo) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
     if (r >= R) return;
@@ -209,9 +222,9 @@ __global__ void __launch_bounds__(256, RPL <= 32 ? 4 : 1) k_resid_ln(int32_t* x,
                 i128 cb = (i128)ln.b[j] << (s - ln.beta_frac);
                 y = shift_round128((i128)((u128)p + (u128)cb), s, 126);
             }
-            yv = clamp128(y, -127, 127);
+            yv = clamp128(y, -32767, 32767);
         }
-        out[(size_t)r * ldo + j] = (int8_t)clamp64(yv, -127, 127);
+        ln_put(yv, out, out_lo, (size_t)r * ldo + j);
     }
 }
 
@@ -226,7 +239,7 @@ __device__ __noinline__ int64_t ln_exact(int64_t cg, i128 u, int s, int32_t b, i
         i128 cb = (i128)b << (s - beta_frac);
         y = shift_round128((i128)((u128)p + (u128)cb), s, 126);
     }
-    return (int64_t)clamp128(y, -127, 127);
+    return (int64_t)clamp128(y, -32767, 32767);
 }
 
 // The same fused step for rows of exactly 128 * NV values (GPT-2: NV = 6): each lane holds NV
@@ -235,7 +248,7 @@ __device__ __noinline__ int64_t ln_exact(int64_t cg, i128 u, int s, int32_t b, i
 // multiplications.
 template <int NV>
 __global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t* delta, int R, LnDev ln, int ln_k,
-                                                       int ln_j, uint64_t eps, int8_t* out, int ldo) {
+                                                       int ln_j, uint64_t eps, int8_t* out, int ldo, int8_t* out_lo) {
     constexpr int D = 128 * NV;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.x * 8 + warp;
@@ -299,6 +312,7 @@ __global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t
     const bool est_ok = ln.beta_frac == 0 && s <= 126;
     const double ud = u128_to_double_signed(u) * exp2_neg(s);
     uint32_t* orow = reinterpret_cast<uint32_t*>(out + (size_t)r * ldo) + lane;
+    uint32_t* lrow = out_lo ? reinterpret_cast<uint32_t*>(out_lo + (size_t)r * ldo) + lane : nullptr;
 #pragma unroll
     for (int i = 0; i < NV; i++) {
         const int j0 = 128 * i + 4 * lane;
@@ -308,7 +322,7 @@ __global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t
         const int32_t gs[4] = {(int16_t)(graw.x & 0xFFFF), (int16_t)(graw.x >> 16), (int16_t)(graw.y & 0xFFFF),
                                (int16_t)(graw.y >> 16)};
         const int32_t bs[4] = {bv.x, bv.y, bv.z, bv.w};
-        uint32_t word = 0;
+        uint32_t word = 0, lword = 0;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int64_t cg = ((int64_t)xs[k] - mean) * (int64_t)gs[k];  // |cg| < 2^47
@@ -326,9 +340,17 @@ __global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t
                 }
             }
             if (!done) yv = ln_exact(cg, u, s, bs[k], ln.beta_frac);
-            word |= (uint32_t)(uint8_t)(int8_t)clamp64(yv, -127, 127) << (8 * k);
+            if (!lrow) {
+                word |= (uint32_t)(uint8_t)(int8_t)clamp64(yv, -127, 127) << (8 * k);
+            } else {
+                // An i16 output as two planes (ln_put).
+                const int32_t v = (int32_t)clamp64(yv, -32767, 32767);
+                word |= (uint32_t)(uint8_t)(int8_t)(v >> 8) << (8 * k);
+                lword |= (uint32_t)(uint8_t)(int8_t)((v & 255) - 128) << (8 * k);
+            }
         }
         orow[32 * i] = word;
+        if (lrow) lrow[32 * i] = lword;
     }
 }
 
@@ -665,8 +687,8 @@ constexpr int CODER_MAX_STEPS = 32;  // steps of 256 symbols per warp: V <= 8 * 
 // decode query walks warp -> step -> lane -> symbol, each level a parallel scan: warp w owns the
 // groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step).
 __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
-                                                         int R, int V, const uint64_t* table, int tlen, int head,
-                                                         uint32_t bits, const RowInfo* rows, uint64_t* out) {
+                                                         int tsh, int R, int V, const uint64_t* table, int tlen,
+                                                         int head, uint32_t bits, const RowInfo* rows, uint64_t* out) {
     extern __shared__ __align__(16) uint32_t F[];  // counts, then 1 + floor(table[j] * spare / W), j <= dmax
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
@@ -676,7 +698,7 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     if (r >= R) return;
     const uint16_t* dr = d16 + (size_t)r * ldd;
     const int64_t* tr = tmax + (size_t)r * ldt;
-    const int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
+    const int VT = (V + (1 << tsh) - 1) >> tsh;  // logits tiles of 2^tsh columns
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int32_t last = tlen - 1;
     const uint64_t total = 1ULL << bits;
@@ -689,7 +711,7 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     mx = block_max64(mx, red);  // (its barriers also order the clearing of F)
     // The distance offset of the tile of symbol v0, clamped to last (then every distance is last).
     auto tile_off = [&](int v0) -> int32_t {
-        const int64_t o = mx - tr[v0 / LOGIT_TILE];
+        const int64_t o = mx - tr[v0 >> tsh];
         return o < (int64_t)last ? (int32_t)o : last;
     };
     // Pass 1: the distance counts, the largest distance and the largest symbol.
@@ -884,20 +906,20 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     }
 }
 
-__global__ void k_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,
+__global__ void k_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                           const uint64_t* table, int tlen, uint64_t* wout) {
     __shared__ int64_t red[32];
     int r = blockIdx.x;
     if (r >= R) return;
     const uint16_t* dr = d16 + (size_t)r * ldd;
     const int64_t* tr = tmax + (size_t)r * ldt;
-    int VT = (V + LOGIT_TILE - 1) / LOGIT_TILE;
+    int VT = (V + (1 << tsh) - 1) >> tsh;
     int64_t mx = INT64_MIN;
     for (int t = threadIdx.x; t < VT; t += blockDim.x) mx = tr[t] > mx ? tr[t] : mx;
     mx = block_max64(mx, red);
     const int64_t last = tlen - 1;
     for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        int64_t dd = mx - tr[v / LOGIT_TILE] + (int64_t)dr[v];
+        int64_t dd = mx - tr[v >> tsh] + (int64_t)dr[v];
         wout[(size_t)r * V + v] = table[dd < last ? dd : last];
     }
 }
@@ -923,28 +945,28 @@ void launch_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const 
 }
 
 void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k, int ln_j, uint64_t eps,
-                      int8_t* out, int ldo, cudaStream_t st) {
+                      int8_t* out, int ldo, cudaStream_t st, int8_t* out_lo) {
     if (R <= 0) return;
-    k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo);
+    k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo, out_lo);
 }
 
 void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, const LnDev& ln, int ln_k, int ln_j,
-                            uint64_t eps, int8_t* out, int ldo, cudaStream_t st) {
+                            uint64_t eps, int8_t* out, int ldo, cudaStream_t st, int8_t* out_lo) {
     if (R <= 0) return;
     int blocks = (R + 7) / 8;
     if (d == 768 && ldo % 4 == 0) {
-        k_resid_ln_v<6><<<blocks, 256, 0, st>>>(x, delta, R, ln, ln_k, ln_j, eps, out, ldo);
+        k_resid_ln_v<6><<<blocks, 256, 0, st>>>(x, delta, R, ln, ln_k, ln_j, eps, out, ldo, out_lo);
     } else if (d <= 32 * 24) {
-        k_resid_ln<24><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo);
+        k_resid_ln<24><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo, out_lo);
     } else if (d <= 32 * 64) {
-        k_resid_ln<64><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo);
+        k_resid_ln<64><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo, out_lo);
     } else {
         // Wide rows: the residual step as its own pass, then the block-per-row LayerNorm.
         if (delta) {
             size_t n = (size_t)R * d;
             k_resid_add<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, delta, n);
         }
-        k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo);
+        k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo, out_lo);
     }
 }
 
@@ -985,17 +1007,18 @@ void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, con
                                                   os, table, tlen, P, att, lda, rowlist);
 }
 
-void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,
-                  int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st) {
+void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
+                  const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
+                  cudaStream_t st) {
     if (R <= 0) return;
-    k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, R, V, table, tlen, head, bits, rows,
-                                                         out);
+    k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, tsh, R, V, table, tlen, head, bits,
+                                                         rows, out);
 }
 
-void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,
+void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                     const uint64_t* table, int tlen, uint64_t* w, cudaStream_t st) {
     if (R <= 0) return;
-    k_weights<<<R, 256, 0, st>>>(d16, ldd, tmax, ldt, R, V, table, tlen, w);
+    k_weights<<<R, 256, 0, st>>>(d16, ldd, tmax, ldt, tsh, R, V, table, tlen, w);
 }
 
 }  // namespace hs

@@ -17,6 +17,8 @@ cudaError_t configure_tc_kernels();
 struct ModelConsts {
     int d, f, V, H, hd, L, n_ctx;
     int Dp, Fp, QKVp, Vp, VT;
+    int tsh;        // log2 of the logits tile width: 7 (128 columns), 6 for a 16-bit ln_f
+    bool lnf_wide;  // ln_f_bits = 16: the final LayerNorm output is i16 (two i8 planes)
     int ln_k, ln_j;
     uint64_t ln_eps;
     int softmax_p;
@@ -25,12 +27,14 @@ struct ModelConsts {
 void launch_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const int32_t* em, int es,
                   const int8_t* wpe, const int32_t* pm, int ps, int d, int32_t* x, cudaStream_t st);
 
+// out_lo != nullptr: 16-bit outputs (ln_f_bits = 16) as two i8 planes, hi in `out` and lo in
+// `out_lo` (v = 256 hi + lo + 128).
 void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k, int ln_j, uint64_t eps,
-                      int8_t* out, int ldo, cudaStream_t st);
+                      int8_t* out, int ldo, cudaStream_t st, int8_t* out_lo = nullptr);
 
 // x = clamp(x + delta, -R, R) (delta may be null), then out = LayerNorm(x) (i8).
 void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, const LnDev& ln, int ln_k, int ln_j,
-                            uint64_t eps, int8_t* out, int ldo, cudaStream_t st);
+                            uint64_t eps, int8_t* out, int ldo, cudaStream_t st, int8_t* out_lo = nullptr);
 
 // out = epilogue(W . A^T) on CUDA cores (dp4a); the reference kernel of the tensor-core GEMM and
 // the path for passes of a few rows.
@@ -41,8 +45,10 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
 // `tmA` and `tmB` are CUtensorMap objects (128-byte aligned, 128 bytes each). EPI_DELTA, EPI_GELU
 // and EPI_LOGITS store their output through `tmC` (32-row x 32-byte boxes, 32-byte swizzle, over
 // all the rows of the output buffer); the other modes take nullptr.
+// tmA2 != nullptr (EPI_DELTA and EPI_LOGITS of version 2 models): tmA and tmA2 are the hi and lo
+// planes of i16 activations, tmB has 128-row boxes and the tiles are 128 x 128.
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
-                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st);
+                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2 = nullptr);
 
 void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
                      int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st);
@@ -66,11 +72,12 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
 // The coder op: from the d16/tmax output of the logits GEMM, the interval of each row's query
 // in the table of taco_coder::FreqTable::from_weights(weights, bits). out: 3 u64 per row. `head`
 // is the last index j with table[j] == table[0] (the table is not increasing).
-void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V, const uint64_t* table,
-                  int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out, cudaStream_t st);
+void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
+                  const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
+                  cudaStream_t st);
 
 // The full weights of each row (run_weights): w[r, v] = table[min(max - logit, last)].
-void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int R, int V,
+void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                     const uint64_t* table, int tlen, uint64_t* w, cudaStream_t st);
 
 }  // namespace hs

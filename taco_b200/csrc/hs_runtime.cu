@@ -137,7 +137,11 @@ int upload(T** p, const T* src, size_t count, std::vector<void*>& owned) {
 struct DevLinear {
     LinearDev ld{};
     bool small = false;  // every rescaled output is below 2^30 in magnitude (32-bit epilogue)
+    // A linear over i16 activations (version 2): the row sums sum_k W[n][k] and a tensor map with
+    // 128-row boxes (the 128 x 128 tiles of the two-plane GEMM).
+    int64_t* wsum = nullptr;
     alignas(128) CUtensorMap tm;
+    alignas(128) CUtensorMap tm128;
 };
 
 }  // namespace
@@ -190,6 +194,9 @@ struct hs_batch {
     int8_t* qkv = nullptr;
     int8_t* att = nullptr;
     int8_t* g = nullptr;
+    // Version 2: the lo planes of the i16 ln_f output and of the i16 GELU outputs.
+    int8_t* a_lo = nullptr;
+    int8_t* g_lo = nullptr;
     int32_t* dbuf = nullptr;  // the residual delta of the last proj/mlp GEMM
     uint16_t* d16 = nullptr;
     int64_t* tmax = nullptr;
@@ -218,6 +225,8 @@ struct hs_batch {
     alignas(128) CUtensorMap ts_delta;  // epilogue stores: the residual delta (i32)
     alignas(128) CUtensorMap ts_g;      // the GELU output (i8)
     alignas(128) CUtensorMap ts_d16;    // the logit distances (u16)
+    alignas(128) CUtensorMap tm_a_lo;   // version 2: the lo plane of the ln_f output
+    alignas(128) CUtensorMap tm_g_lo;   // version 2: the lo plane of the GELU output
 
     ~hs_batch() {
         if (model) cudaSetDevice(model->dev->ordinal);
@@ -277,7 +286,7 @@ void prof_collect(hs_batch* b) {
     b->ev_pending.clear();
 }
 
-int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D) {
+int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D, bool wide_in = false) {
     int N = L.rows, K = L.cols;
     int Np = round_up(N, TILE_N), Kp = round_up(K, TILE_K);
     std::vector<int8_t> w((size_t)Np * Kp, 0);
@@ -310,6 +319,13 @@ int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D) {
         D.small = (worst >> s) + 1 < ((unsigned __int128)1 << 30);
     }
     m->weight_bytes += w.size() + 8 * (size_t)Np;
+    if (wide_in) {
+        std::vector<int64_t> ws(Np, 0);
+        for (int n = 0; n < N; n++)
+            for (int k = 0; k < K; k++) ws[n] += L.w[(size_t)n * K + k];
+        if ((rc = upload(&D.wsum, ws.data(), ws.size(), m->owned))) return rc;
+        if ((rc = make_tmap(m->dev, &D.tm128, dw, Np, Kp, 128))) return rc;
+    }
     return make_tmap(m->dev, &D.tm, dw, Np, Kp, TILE_N);
 }
 
@@ -335,12 +351,15 @@ int forward(hs_batch* b, int R) {
     // The attention work of this pass: 2 * 2 * hd * (pos + 1) per row and head (q.k and p.v).
     uint64_t attn_ops = 0;
     for (int r = 0; r < R; r++) attn_ops += 4ULL * c.d * (b->h_rows[r].pos + 1);
+    // tmA2: the lo plane of i16 activations (version 2); then the tiles are 128 x 128.
     auto gemm = [&](int op, int mode, const int8_t* A, int lda, const CUtensorMap* tmA, const DevLinear& W,
-                    EpiArgs e, const CUtensorMap* tmC) {
+                    EpiArgs e, const CUtensorMap* tmC, const CUtensorMap* tmA2 = nullptr) {
         ProfScope p(b, op, 2ULL * R * W.ld.N * W.ld.K);
         e.small = W.small ? 1 : 0;
+        e.wsum = W.wsum;
         if (m->use_tc)
-            launch_gemm_tc(mode, tmA, &W.tm, tmC, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms, m->dev->d_err, st);
+            launch_gemm_tc(mode, tmA, tmA2 ? &W.tm128 : &W.tm, tmC, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms,
+                           m->dev->d_err, st, tmA2);
         else
             launch_gemm_simple(mode, A, lda, R, W.ld, e, st);
     };
@@ -407,7 +426,14 @@ int forward(hs_batch* b, int R) {
         e.ldo = c.Fp;
         e.gelu = Ld.gelu;
         e.gelu_off = Ld.gelu_off;
-        gemm(OP_GEMM_FC, EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e, &b->ts_g);
+        const bool gwide = Ld.gelu16 != nullptr;
+        if (gwide) {
+            e.gelu16 = Ld.gelu16;
+            e.out8_lo = b->g_lo;
+            gemm(OP_GEMM_FC, EPI_GELU16, b->a, c.Dp, &b->tm_a, fc, e, nullptr);
+        } else {
+            gemm(OP_GEMM_FC, EPI_GELU, b->a, c.Dp, &b->tm_a, fc, e, &b->ts_g);
+        }
         e = EpiArgs{};
         e.R = R;
         e.N = c.d;
@@ -416,11 +442,12 @@ int forward(hs_batch* b, int R) {
         e.s = mlp.ld.s;
         e.out32 = b->dbuf;
         e.ldo = c.d;
-        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e, &b->ts_delta);
+        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e, &b->ts_delta, gwide ? &b->tm_g_lo : nullptr);
     }
     {
         ProfScope p(b, OP_LN, 0);
-        launch_resid_layernorm(b->x, b->dbuf, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+        launch_resid_layernorm(b->x, b->dbuf, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st,
+                               c.lnf_wide ? b->a_lo : nullptr);
     }
     const DevLinear& lmh = *m->lins[4 * c.L];
     EpiArgs e{};
@@ -433,7 +460,7 @@ int forward(hs_batch* b, int R) {
     e.tmax = b->tmax;
     e.ldt = c.VT;
     e.last = m->logits_len - 1;
-    gemm(OP_GEMM_LOGITS, EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e, &b->ts_d16);
+    gemm(OP_GEMM_LOGITS, EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e, &b->ts_d16, c.lnf_wide ? &b->tm_a_lo : nullptr);
     return HS_OK;
 }
 
@@ -577,7 +604,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         if (out) {
             {
                 ProfScope p(b, OP_CODER, 0);
-                launch_coder(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, m->logits_head, bits, b->d_rows,
+                launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len, m->logits_head, bits, b->d_rows,
                              b->intervals, b->stream);
             }
             pass_scope.reset();
@@ -586,7 +613,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         } else {
             {
                 ProfScope p(b, OP_CODER, 0);
-                launch_weights(b->d16, c.Vp, b->tmax, c.VT, R, c.V, m->logits_exp, m->logits_len, b->weights,
+                launch_weights(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len, b->weights,
                                b->stream);
             }
             pass_scope.reset();
@@ -708,9 +735,9 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
     hsm::Model M;
     std::string err;
     if (!hsm::load_model(file, len, M, err)) return fail(HS_MODEL, "the model file is not valid: " + err);
-    if (M.is_wide())
-        return fail(HS_UNSUPPORTED, "hsm format version 2 rules (i16 activations, ln_beta_frac) are not run by "
-                                    "this backend yet");
+    if (M.is_wide() && !use_tc_default())
+        return fail(HS_UNSUPPORTED, "the CUDA-core GEMM path (HS_GEMM=simple) does not run the i16 activations "
+                                    "of hsm format version 2");
     if (M.vocab < 2) return fail(HS_UNSUPPORTED, "the vocabulary needs at least 2 tokens");
     if (M.vocab > MAX_CODER_VOCAB)
         return fail(HS_UNSUPPORTED, "the coder op of this backend takes at most 65536 tokens");
@@ -739,7 +766,9 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
     c.Fp = round_up(c.f, TILE_K);
     c.QKVp = round_up(3 * c.d, 16);
     c.Vp = round_up(c.V, TILE_N);
-    c.VT = (c.V + LOGIT_TILE - 1) / LOGIT_TILE;
+    c.lnf_wide = M.ln_f_bits == 16;
+    c.tsh = c.lnf_wide ? 6 : 7;  // LOGIT_TILE_WIDE or LOGIT_TILE columns per logits tile
+    c.VT = (c.V + (1 << c.tsh) - 1) >> c.tsh;
     c.ln_k = (int)M.ln_k;
     c.ln_j = (int)M.ln_j;
     c.ln_eps = M.ln_eps;
@@ -756,7 +785,8 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
         LayerDev Ld{};
         for (const hsm::Linear* L : {&B.c_attn, &B.c_proj, &B.c_fc, &B.mlp_proj}) {
             m->lins.emplace_back(new DevLinear());
-            rc = upload_linear(m.get(), *L, *m->lins.back());
+            // mlp_proj reads the i16 GELU output of a version 2 layer (two planes).
+            rc = upload_linear(m.get(), *L, *m->lins.back(), L == &B.mlp_proj && B.gelu_wide);
             if (rc) return rc;
         }
         Ld.qkv = m->lins[4 * l]->ld;
@@ -771,11 +801,17 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
         int8_t* gl;
         if ((rc = upload(&gl, B.gelu8.data(), B.gelu8.size(), m->owned))) return rc;
         Ld.gelu = gl;
+        Ld.gelu16 = nullptr;
+        if (B.gelu_wide) {
+            int16_t* g16;
+            if ((rc = upload(&g16, B.gelu16.data(), B.gelu16.size(), m->owned))) return rc;
+            Ld.gelu16 = g16;
+        }
         Ld.gelu_off = (int)B.gelu_offset;
         m->layers.push_back(Ld);
     }
     m->lins.emplace_back(new DevLinear());
-    if ((rc = upload_linear(m.get(), lm, *m->lins.back()))) return rc;
+    if ((rc = upload_linear(m.get(), lm, *m->lins.back(), c.lnf_wide))) return rc;
     m->wte = const_cast<int8_t*>(m->lins.back()->ld.w);
     m->es = (int)M.embed.s;
     m->ls = (int)M.logit.s;
@@ -848,11 +884,22 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         (rc = dalloc(&b->intervals, 3 * R, b->owned)))
         return rc;
     if ((rc = dalloc(&b->d_groups, R, b->owned)) || (rc = dalloc(&b->d_rowlist, R, b->owned))) return rc;
+    bool gelu_wide = false;
+    for (const LayerDev& Ld : m->layers) gelu_wide |= Ld.gelu16 != nullptr;
+    if (c.lnf_wide) {
+        if ((rc = dalloc(&b->a_lo, R * c.Dp, b->owned))) return rc;
+        if ((rc = make_tmap(m->dev, &b->tm_a_lo, b->a_lo, R, c.Dp, TILE_M))) return rc;
+    }
+    if (gelu_wide) {
+        if ((rc = dalloc(&b->g_lo, R * c.Fp, b->owned))) return rc;
+        if ((rc = make_tmap(m->dev, &b->tm_g_lo, b->g_lo, R, c.Fp, TILE_M))) return rc;
+    }
     CK(cudaMallocHost(&b->h_groups, sizeof(AttnGroup) * R));
     CK(cudaMallocHost(&b->h_rowlist, sizeof(int) * R));
     CK(cudaMallocHost(&b->h_rows, sizeof(RowInfo) * R));
     CK(cudaMallocHost(&b->h_intervals, sizeof(uint64_t) * 3 * R));
-    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24);
+    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24 +
+                                (c.lnf_wide ? c.Dp : 0) + (gelu_wide ? c.Fp : 0));
     if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d)) ||
         (rc = make_store_tmap(m->dev, &b->ts_g, b->g, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, c.f, c.Fp)) ||
         (rc = make_store_tmap(m->dev, &b->ts_d16, b->d16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, R, c.V, c.Vp)))

@@ -216,14 +216,28 @@ def gelu_table(s_in: float, s_out: float) -> np.ndarray:
     return np.clip(np.rint(_gelu(x) / s_out), -127, 127).astype(np.int8)
 
 
-def build_tensors(fm: dict, rg: dict) -> list[tuple[str, str, np.ndarray, int | None]]:
-    """(name, dtype, values, shift) in the order of crates/hardshell/src/gpt2/mod.rs."""
+def gelu_table16(s_in: float, s_out: float) -> np.ndarray:
+    """The i16-output GELU table of a version 2 model (crates/hardshell/src/gelu.rs)."""
+    x = np.arange(-32768, 32768, dtype=np.float64) * s_in
+    return np.clip(np.rint(_gelu(x) / s_out), -32767, 32767).astype(np.int16)
+
+
+# A version 2 ("wide") synthetic model: a 16-bit final LayerNorm (ln_f_bits = 16), LayerNorm
+# betas with BETA_FRAC fractional bits, and 16-bit GELU outputs in the even layers.
+BETA_FRAC = 4
+
+
+def build_tensors(fm: dict, rg: dict, wide: bool = False) -> list[tuple[str, str, np.ndarray, int | None]]:
+    """(name, dtype, values, shift) in the order of crates/hardshell/src/gpt2/mod.rs. `wide`: the
+    version 2 rules (16-bit ln_f, 16-bit GELU in the even layers, betas with BETA_FRAC
+    fractional bits)."""
     out: list[tuple[str, str, np.ndarray, int | None]] = []
+    brng = np.random.default_rng(fm.get("seed", 0) + 99)
     sh: Shape = fm["shape"]
     D_MODEL, D_FF, N_HEAD = sh.d_model, sh.d_ff, sh.n_head  # noqa: N806
     res = min(rg["res_max"] / 2 ** 24, rg["row_std_min"] / 2 ** 12.5)
     site = lambda k, qmax=127: rg[k] / qmax  # noqa: E731
-    s_lnf = site("ln_f")
+    s_lnf = site("ln_f") / (256 if wide else 1)
     wq, ws = quantise_rows(fm["wte"])
     out.append(("wte", "i8", wq.astype(np.int8), None))
     m, s = quant_mult_rows(ws / res)
@@ -238,7 +252,12 @@ def build_tensors(fm: dict, rg: dict) -> list[tuple[str, str, np.ndarray, int | 
     def layernorm(prefix, s_out):
         gq, gs = quantise_rows(np.ones((1, D_MODEL)), 32767)
         out.append((f"{prefix}.g", "i16", gq.reshape(-1).astype(np.int16), None))
-        out.append((f"{prefix}.b", "i32", np.zeros(D_MODEL, np.int32), None))
+        if wide:
+            # Betas of about 0.05 of the output scale, in units of 2^-BETA_FRAC of an output step.
+            beta = np.rint(brng.normal(0.0, 0.05 / s_out, D_MODEL) * 2 ** BETA_FRAC)
+            out.append((f"{prefix}.b", "i32", beta.astype(np.int32), None))
+        else:
+            out.append((f"{prefix}.b", "i32", np.zeros(D_MODEL, np.int32), None))
         mm, ss = quant_mult(gs[0] / (2.0 ** (LN_K - LN_J) * s_out))
         out.append((f"{prefix}.rescale", "i32", np.array([mm], np.int32), ss))
 
@@ -264,15 +283,20 @@ def build_tensors(fm: dict, rg: dict) -> list[tuple[str, str, np.ndarray, int | 
         layernorm(f"{p}.ln_2", site(f"{p}.ln_2"))
         s_fc = site(f"{p}.fc", 32767)
         linear(f"{p}.mlp.c_fc", b["fc_w"], site(f"{p}.ln_2"), np.full(D_FF, s_fc))
-        out.append((f"{p}.mlp.gelu", "i8", gelu_table(s_fc, site(f"{p}.gelu")), None))
-        linear(f"{p}.mlp.c_proj", b["mlp_w"], site(f"{p}.gelu"), np.full(D_MODEL, res))
+        if wide and l % 2 == 0:
+            s_g = site(f"{p}.gelu") / 256
+            out.append((f"{p}.mlp.gelu", "i16", gelu_table16(s_fc, s_g), None))
+        else:
+            s_g = site(f"{p}.gelu")
+            out.append((f"{p}.mlp.gelu", "i8", gelu_table(s_fc, s_g), None))
+        linear(f"{p}.mlp.c_proj", b["mlp_w"], s_g, np.full(D_MODEL, res))
     layernorm("ln_f", s_lnf)
     out.append(("attn_exp", "i32", exp_table(ATTN_EXP_E).astype(np.int32), None))
     out.append(("logits_exp", "u64", exp_table(LOGITS_EXP_E).astype(np.uint64), None))
     return out, res
 
 
-def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2) -> bytes:
+def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2, wide: bool = False) -> bytes:
     """The .hsm layout (crates/hardshell/src/hsm/mod.rs:1-120): preamble, compact JSON header,
     vocabulary and tensors at 64-byte boundaries with zero padding."""
     vocab_sec = b"".join(struct.pack("<H", len(t)) + t for t in vocab)
@@ -296,7 +320,8 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2) -> bytes:
         header = {
             "model": {"architecture": "gpt2", "n_layer": sh.n_layer, "n_head": sh.n_head, "d_model": sh.d_model,
                       "d_ff": sh.d_ff, "vocab_size": sh.vocab, "n_ctx": sh.n_ctx, "eot_token": sh.vocab - 1,
-                      "constants": {"ln_k": LN_K, "ln_j": LN_J, "ln_eps": eps, "softmax_p": SOFTMAX_P}},
+                      "constants": dict({"ln_k": LN_K, "ln_j": LN_J, "ln_eps": eps, "softmax_p": SOFTMAX_P},
+                                        **({"ln_f_bits": 16, "ln_beta_frac": BETA_FRAC} if wide else {}))},
             "vocabulary": {"offset": voff, "length": len(vocab_sec)},
             "tensors": entries,
         }
@@ -305,7 +330,7 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2) -> bytes:
             text += b" " * (hlen - len(text))
             break
         hlen = len(text)
-    out = bytearray(b"HSHLMDL\0" + struct.pack("<II", 1, hlen) + text)
+    out = bytearray(b"HSHLMDL\0" + struct.pack("<II", 2 if wide else 1, hlen) + text)
     out += bytes(align(len(out)) - len(out))
     out += vocab_sec
     for (n, d, v, s), e in zip(blobs, entries):
@@ -314,18 +339,19 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2) -> bytes:
     return bytes(out)
 
 
-def gpt2_hsm(seed: int = 124, cache: bool = True, shape: Shape = GPT2) -> bytes:
+def gpt2_hsm(seed: int = 124, cache: bool = True, shape: Shape = GPT2, wide: bool = False) -> bytes:
     """The synthetic GPT-2 model file for `seed` and `shape` (GPT-2 124M by default; cached under
-    taco_b200/_cache)."""
+    taco_b200/_cache). `wide`: a version 2 file (16-bit ln_f and GELU, fractional betas)."""
     tag = "gpt2_124m" if shape == GPT2 else "gpt2_{}l{}h{}d{}f{}v{}c".format(*vars(shape).values())
+    tag += "_v2" if wide else ""
     path = CACHE / f"{tag}_seed{seed}.hsm"
     if cache and path.exists():
         return path.read_bytes()
     fm = float_model(seed, shape)
     rg = calibrate(fm, seed)
-    tensors, res = build_tensors(fm, rg)
+    tensors, res = build_tensors(fm, rg, wide)
     eps = max(1, int(round(1e-5 / (res * res) * 2 ** (2 * LN_J))))
-    data = write_hsm(tensors, vocabulary(vocab=shape.vocab), eps, shape)
+    data = write_hsm(tensors, vocabulary(vocab=shape.vocab), eps, shape, wide)
     if cache:
         CACHE.mkdir(exist_ok=True)
         tmp = path.with_suffix(f".{os.getpid()}.tmp")  # one per process: ranks may build it at once

@@ -221,3 +221,19 @@ def test_fast_path_equals_the_reference_session():
             for i, (s, t) in enumerate(seq):
                 want = refs[s].step(t)
                 assert np.array_equal(w[i], want), (overlap, call, i)
+
+
+def test_fast_path_equals_the_reference_session_on_a_version_2_model():
+    """The same on the synthetic version 2 model (16-bit ln_f, fractional betas, a 16-bit GELU
+    layer): hs_fast's i8 x i16 products and 16-bit LayerNorm equal the reference session."""
+    from taco_b200 import synth
+
+    model = O.Model(synth.gpt2_hsm(7, shape=synth.MINI, wide=True))
+    rng = np.random.default_rng(3)
+    fast = O.FastBatch(model, 2, 0)
+    refs = [O.Session(model, 0) for _ in range(2)]
+    seq = [(0, int(t)) for t in rng.integers(0, model.vocab - 1, 40)]
+    seq += [(1, int(t)) for t in rng.integers(0, model.vocab - 1, 33)]
+    w = fast.run_weights([s for s, _ in seq], [t for _, t in seq])
+    for i, (s, t) in enumerate(seq):
+        assert np.array_equal(w[i], refs[s].step(t)), i
