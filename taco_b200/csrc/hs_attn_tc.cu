@@ -274,12 +274,20 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             if (j0 > wlast) {
                 // every key of this slice is masked for this warp's rows
             } else if (j0 + 31 <= rpos) {
+                // A max/min tree instead of one dependent chain of 32 steps.
+                int32_t mx[8], mn[8];
 #pragma unroll
-                for (int q = 0; q < 32; q++) {
-                    int32_t dv = (int32_t)v[q];
-                    maxd = dv > maxd ? dv : maxd;
-                    mind = dv < mind ? dv : mind;
+                for (int q = 0; q < 8; q++) {
+                    mx[q] = max(max((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), max((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
+                    mn[q] = min(min((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), min((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
                 }
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    mx[q] = max(mx[q], mx[q + 4]);
+                    mn[q] = min(mn[q], mn[q + 4]);
+                }
+                maxd = max(maxd, max(max(mx[0], mx[1]), max(mx[2], mx[3])));
+                mind = min(mind, min(min(mn[0], mn[1]), min(mn[2], mn[3])));
             } else {
 #pragma unroll
                 for (int q = 0; q < 32; q++) {
@@ -322,8 +330,11 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             if (j0 > wlast) {
                 // masked for every lane
             } else if (j0 + 31 <= rpos) {
+                // Four partial sums: independent chains for the look-ups and adds.
+                uint64_t ps[4] = {0, 0, 0, 0};
 #pragma unroll
-                for (int q = 0; q < 32; q++) sum += (uint32_t)sT[dist(M, (int32_t)v[q])];
+                for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[dist(M, (int32_t)v[q])];
+                sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             } else {
 #pragma unroll
                 for (int q = 0; q < 32; q++)

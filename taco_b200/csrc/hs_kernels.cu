@@ -718,14 +718,14 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     uint32_t nlast = 0;
     int32_t dmax = 0;
     int best = V;
-    for (int gi = threadIdx.x; gi < ng_full; gi += CODER_THREADS) {
-        const int v0 = 8 * gi;
-        const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+    // Groups of 8 symbols, CODER_UNROLL groups per thread and round so that several 16-byte loads
+    // are in flight before the counting.
+    auto count_group = [&](int v0, uint4 raw) {
         const int32_t off = tile_off(v0);
         if (off == last) {
             nlast += 8;
             dmax = last;
-            continue;
+            return;
         }
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
@@ -737,6 +737,19 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
             dmax = dd > dmax ? dd : dmax;
             best = dd <= head && v0 + i < best ? v0 + i : best;
         }
+    };
+    constexpr int CODER_UNROLL = 4;
+    {
+        int g0 = threadIdx.x;
+        for (; g0 + (CODER_UNROLL - 1) * CODER_THREADS < ng_full; g0 += CODER_UNROLL * CODER_THREADS) {
+            uint4 raw[CODER_UNROLL];
+#pragma unroll
+            for (int k = 0; k < CODER_UNROLL; k++)
+                raw[k] = *reinterpret_cast<const uint4*>(dr + 8 * (g0 + k * CODER_THREADS));
+#pragma unroll
+            for (int k = 0; k < CODER_UNROLL; k++) count_group(8 * (g0 + k * CODER_THREADS), raw[k]);
+        }
+        for (; g0 < ng_full; g0 += CODER_THREADS) count_group(8 * g0, *reinterpret_cast<const uint4*>(dr + 8 * g0));
     }
     if (ng_full < ng && threadIdx.x == ng_full % CODER_THREADS) {
         const int v0 = 8 * ng_full;
@@ -788,16 +801,24 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         const int s = (int)q.value;
         const int gs = s / 8;
         uint64_t pre = 0;
-        for (int gi = threadIdx.x; gi < gs; gi += CODER_THREADS) {
-            const int v0 = 8 * gi;
-            const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+        auto group_sum = [&](int v0, uint4 raw) {
             const int32_t off = tile_off(v0);
             const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
             uint32_t gsum = 0;  // 8 frequencies: at most total - (V - 8) < 2^32 for V > 8
 #pragma unroll
             for (int i = 0; i < 8; i++) gsum += f_of(off, (u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
             pre += gsum;
+        };
+        int gj = threadIdx.x;
+        for (; gj + (CODER_UNROLL - 1) * CODER_THREADS < gs; gj += CODER_UNROLL * CODER_THREADS) {
+            uint4 raw[CODER_UNROLL];
+#pragma unroll
+            for (int k = 0; k < CODER_UNROLL; k++)
+                raw[k] = *reinterpret_cast<const uint4*>(dr + 8 * (gj + k * CODER_THREADS));
+#pragma unroll
+            for (int k = 0; k < CODER_UNROLL; k++) group_sum(8 * (gj + k * CODER_THREADS), raw[k]);
         }
+        for (; gj < gs; gj += CODER_THREADS) group_sum(8 * gj, *reinterpret_cast<const uint4*>(dr + 8 * gj));
         if (threadIdx.x == CODER_THREADS - 1) {
             const int32_t off = tile_off(8 * gs);
             for (int v = 8 * gs; v < s; v++) pre += f_of(off, dr[v]);
