@@ -43,16 +43,16 @@ constexpr int GELU_SMEM = 65536;
 constexpr int VT_STRIDE = 36;                  // bytes per row of a warp's 32 x 32 transpose tile
 constexpr int VT_TILE = 32 * VT_STRIDE;
 
-// The epilogue of EPI_DELTA, EPI_GELU and EPI_LOGITS stores through TMA: each epilogue warp
-// stages pieces of 32 rows x 32 bytes (the 32-byte swizzle) in shared memory, two buffers for
-// DELTA and LOGITS, one for GELU (whose 64 KB table fills the rest), so the stores leave as whole
-// row segments instead of 32 scattered 16-byte pieces per instruction.
+// The epilogue of EPI_DELTA, EPI_GELU and EPI_LOGITS stores through TMA, so the stores leave as
+// whole row segments instead of 32 scattered 16-byte pieces per instruction. DELTA and LOGITS:
+// each epilogue warp stages blocks of 32 rows x 128 bytes (the 128-byte swizzle) in two 4 KB
+// buffers, one TMA store per block; they run with 3 stages to make room. GELU, whose 64 KB table
+// fills shared memory: one buffer of 32 rows x 32 bytes (the 32-byte swizzle).
 template <int MODE>
 struct Cfg {
-    static constexpr int STAGES = MODE == EPI_GELU ? 3 : 4;
+    static constexpr int STAGES = (MODE == EPI_GELU || MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 3 : 4;
     static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : (MODE == EPI_QKV ? EPI_WARPS * VT_TILE : 0);
-    static constexpr int STORE_BUFS = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 2 : (MODE == EPI_GELU ? 1 : 0);
-    static constexpr int STORE_WARP = 1024 * STORE_BUFS;
+    static constexpr int STORE_WARP = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 8192 : (MODE == EPI_GELU ? 1024 : 0);
     static constexpr int WSUM = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 2 * BN * 8 : 0;  // s_w (WIDE)
     static constexpr size_t SMEM =
         (size_t)STAGES * STAGE_BYTES + EXTRA + EPI_WARPS * STORE_WARP + 2 * BN * 12 + WSUM + 256 + 1024;
@@ -85,6 +85,33 @@ template <class T>
 __device__ __forceinline__ T clamp_e(T y, int64_t lo, int64_t hi) {
     if constexpr (sizeof(T) == 4) return min(max(y, (T)lo), (T)hi);
     else return clamp64(y, lo, hi);
+}
+
+// The 32 rescaled values of one chunk on the S32 path: one 32x32->64 multiply-add and one shift
+// each (SHI: s >= 32, so the result is the high word shifted; else a funnel shift), with the
+// column parameters read as 16-byte vectors.
+template <bool SHI>
+__device__ __forceinline__ void rescale_chunk32(const uint32_t (&v)[32], const int32_t* pm, const int64_t* pc, int s,
+                                                int32_t (&y)[32]) {
+#pragma unroll
+    for (int q = 0; q < 32; q += 4) {
+        const int4 m4 = *reinterpret_cast<const int4*>(pm + q);
+        const longlong2 c01 = *reinterpret_cast<const longlong2*>(pc + q);
+        const longlong2 c23 = *reinterpret_cast<const longlong2*>(pc + q + 2);
+        const int32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
+        const int64_t cc[4] = {c01.x, c01.y, c23.x, c23.y};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t t = (int64_t)(int32_t)v[q + k] * (int64_t)mm[k] + cc[k];
+            if constexpr (SHI) y[q + k] = (int32_t)(t >> 32) >> (s - 32);
+            else y[q + k] = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), s);
+        }
+    }
+}
+
+// Four values already in [-128, 127] as the bytes of one word (byte permutes).
+__device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, int32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // EPI_QKV: one value at column n of a row of (slot, pos): q to out8, k and v to the caches.
@@ -238,24 +265,35 @@ __global__ void __launch_bounds__(THREADS, 1)
         // One 32-row x 32-byte piece (this lane's row: lo, hi) to the output through TMA at
         // element column x and row y. Warp-collective.
         uint8_t* my_store = s_store + (warp - 2) * Cfg<MODE>::STORE_WARP;
-        uint32_t pieces = 0;
         auto store_piece = [&](uint4 lo, uint4 hi, int x, int y) {
-            uint8_t* buf = my_store + (Cfg<MODE>::STORE_BUFS == 2 ? (pieces & 1) * 1024 : 0);
-            if (lane == 0) {
-                if (Cfg<MODE>::STORE_BUFS == 2) bulk_wait_read1();
-                else bulk_wait_read();
-            }
+            if (lane == 0) bulk_wait_read();
             __syncwarp();
             const uint32_t sw = (uint32_t)((lane >> 2) & 1);
-            *reinterpret_cast<uint4*>(buf + lane * 32 + (sw << 4)) = lo;
-            *reinterpret_cast<uint4*>(buf + lane * 32 + ((sw ^ 1) << 4)) = hi;
+            *reinterpret_cast<uint4*>(my_store + lane * 32 + (sw << 4)) = lo;
+            *reinterpret_cast<uint4*>(my_store + lane * 32 + ((sw ^ 1) << 4)) = hi;
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&tmC, my_store, x, y);
+                bulk_commit();
+            }
+        };
+        // One 32-row x 128-byte block (this lane's row: 8 x 16 bytes) through TMA at element column
+        // x and row y (the 128-byte swizzle), alternating between two buffers. Warp-collective.
+        uint32_t blocks = 0;
+        auto store_block = [&](const uint4 (&b)[8], int x, int y) {
+            uint8_t* buf = my_store + (blocks & 1) * 4096;
+            if (lane == 0) bulk_wait_read1();  // the store that last used this buffer has read it
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; j++) *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = b[j];
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
                 tma_store_2d(&tmC, buf, x, y);
                 bulk_commit();
             }
-            pieces++;
+            blocks++;
         };
         int i = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
@@ -357,11 +395,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                             for (int w = 0; w < 8; w++)
                                 pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
-                            if (col0 + half * 64 + ch * 16 < e.N)
-                                store_piece(make_uint4(pk[ch * 8], pk[ch * 8 + 1], pk[ch * 8 + 2], pk[ch * 8 + 3]),
-                                            make_uint4(pk[ch * 8 + 4], pk[ch * 8 + 5], pk[ch * 8 + 6], pk[ch * 8 + 7]),
-                                            col0 + half * 64 + ch * 16, mt * BM + g * 32);
                         }
+                        // 64 columns of u16 = one 128-byte block; columns past N are clipped.
+                        uint4 blk[8];
+#pragma unroll
+                        for (int j = 0; j < 8; j++) blk[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                        store_block(blk, col0 + half * 64, mt * BM + g * 32);
                         const int tile = nt * 2 + half;
                         if (row_ok && tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run;
                     }
@@ -382,12 +421,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                             o[q] = (int32_t)clamp128(rescale128(value(vh[q], vl[q], c0 + q) + pc[c0 + q], pm[c0 + q],
                                                                 (uint32_t)s),
                                                      INT32_MIN, INT32_MAX);
+                        uint4 blk[8];
 #pragma unroll
-                        for (int p = 0; p < 4; p++)
-                            if (colb + 8 * p < e.N)
-                                store_piece(make_uint4(o[8 * p], o[8 * p + 1], o[8 * p + 2], o[8 * p + 3]),
-                                            make_uint4(o[8 * p + 4], o[8 * p + 5], o[8 * p + 6], o[8 * p + 7]),
-                                            colb + 8 * p, mt * BM + g * 32);
+                        for (int j = 0; j < 8; j++) blk[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                        store_block(blk, colb, mt * BM + g * 32);
                     }
                     tc_fence_before();
                     mbar_arrive(&bars->tempty[acc]);
@@ -438,10 +475,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t a2 = a | (a << 16);
 #pragma unroll
                         for (int w = 0; w < 8; w++) pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
-                        // Rows past R land in the padding rows of d16 (never read).
-                        store_piece(make_uint4(pk[ch * 8], pk[ch * 8 + 1], pk[ch * 8 + 2], pk[ch * 8 + 3]),
-                                    make_uint4(pk[ch * 8 + 4], pk[ch * 8 + 5], pk[ch * 8 + 6], pk[ch * 8 + 7]),
-                                    col0 + half * 128 + ch * 16, mt * BM + g * 32);
+                    }
+                    // Two 128-byte blocks of 64 u16 columns. Rows past R land in the padding rows of
+                    // d16 (never read).
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        uint4 blk[8];
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            blk[j] = make_uint4(pk[32 * h2 + 4 * j], pk[32 * h2 + 4 * j + 1], pk[32 * h2 + 4 * j + 2],
+                                                pk[32 * h2 + 4 * j + 3]);
+                        store_block(blk, col0 + half * 128 + 64 * h2, mt * BM + g * 32);
                     }
                     if (row_ok && tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run32;
                     continue;
@@ -484,11 +528,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t a2 = a | (a << 16);
 #pragma unroll
                         for (int w = 0; w < 8; w++) pk[ch * 8 + w] = __vminu2(__vadd2(pk[ch * 8 + w], a2), last2);
-                        // Columns past N are clipped by the tensor map; pieces wholly past N are skipped.
-                        if (col0 + half * 128 + ch * 16 < e.N)
-                            store_piece(make_uint4(pk[ch * 8], pk[ch * 8 + 1], pk[ch * 8 + 2], pk[ch * 8 + 3]),
-                                        make_uint4(pk[ch * 8 + 4], pk[ch * 8 + 5], pk[ch * 8 + 6], pk[ch * 8 + 7]),
-                                        col0 + half * 128 + ch * 16, mt * BM + g * 32);
+                    }
+                    // Columns past N are clipped by the tensor map; blocks wholly past N are skipped.
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; h2++) {
+                        if (col0 + half * 128 + 64 * h2 >= e.N) continue;
+                        uint4 blk[8];
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            blk[j] = make_uint4(pk[32 * h2 + 4 * j], pk[32 * h2 + 4 * j + 1], pk[32 * h2 + 4 * j + 2],
+                                                pk[32 * h2 + 4 * j + 3]);
+                        store_block(blk, col0 + half * 128 + 64 * h2, mt * BM + g * 32);
                     }
                     if (row_ok && tile < e.ldt) e.tmax[(size_t)row * e.ldt + tile] = run;
                 }
@@ -506,12 +556,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // padding rows of the output, which nothing reads.
                     if (MODE != EPI_GELU && MODE != EPI_DELTA && !row_ok) continue;
                     const bool full = colb + 32 <= e.N;
+                    // The rescaled values: 32-bit on the S32 path, computed for the whole chunk.
+                    int32_t y32[32];
+                    if constexpr (S32) {
+                        if (s >= 32) rescale_chunk32<true>(v, pm + c0, pc + c0, s, y32);
+                        else rescale_chunk32<false>(v, pm + c0, pc + c0, s, y32);
+                    }
+                    auto Y = [&](int q) {
+                        if constexpr (S32) return y32[q];
+                        else return rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast);
+                    };
                     if (MODE == EPI_QKV) {
                         const RowInfo ri = e.rows[row];
                         int8_t o[32];
 #pragma unroll
                         for (int q = 0; q < 32; q++)
-                            o[q] = (int8_t)clamp_e(rescale_e<S32>(v[q], pm[c0 + q], pc[c0 + q], s, fast), -127, 127);
+                            o[q] = (int8_t)clamp_e(Y(q), -127, 127);
                         if (full && colb + 32 <= e.d && (e.ldo & 15) == 0) {
                             // A whole 32-byte run of q.
                             uint32_t pk[8];
@@ -566,18 +626,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                     } else if (MODE == EPI_ACT || MODE == EPI_GELU) {
                         uint32_t packed[8];
 #pragma unroll
-                        for (int q = 0; q < 8; q++) packed[q] = 0;
+                        for (int w = 0; w < 8; w++) {
+                            int32_t o4[4];
 #pragma unroll
-                        for (int q = 0; q < 32; q++) {
-                            const auto y = rescale_e<S32>(v[q], pm[c0 + q], pc[c0 + q], s, fast);
-                            int8_t o;
-                            if (MODE == EPI_ACT) {
-                                o = (int8_t)clamp_e(y, -127, 127);
-                            } else {
-                                const auto in = clamp_e(y, -e.gelu_off, e.gelu_off - 1);
-                                o = s_gelu[in + e.gelu_off];
+                            for (int k = 0; k < 4; k++) {
+                                const auto y = Y(4 * w + k);
+                                if (MODE == EPI_ACT) {
+                                    o4[k] = (int32_t)clamp_e(y, -127, 127);
+                                } else {
+                                    const auto in = clamp_e(y, -e.gelu_off, e.gelu_off - 1);
+                                    o4[k] = s_gelu[in + e.gelu_off];
+                                }
                             }
-                            packed[q >> 2] |= (uint32_t)(uint8_t)o << (8 * (q & 3));
+                            packed[w] = pack4_i8(o4[0], o4[1], o4[2], o4[3]);
                         }
                         int8_t* dst = e.out8 + (size_t)row * e.ldo + colb;
                         if (MODE == EPI_GELU) {
@@ -598,7 +659,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int q = 0; q < 8; q++) ph[q] = pl[q] = 0;
 #pragma unroll
                         for (int q = 0; q < 32; q++) {
-                            const auto y = rescale_e<S32>(v[q], pm[c0 + q], pc[c0 + q], s, fast);
+                            const auto y = Y(q);
                             const auto in = clamp_e(y, -e.gelu_off, e.gelu_off - 1);
                             const int32_t g16 = __ldg(e.gelu16 + (int64_t)in + e.gelu_off);
                             ph[q >> 2] |= (uint32_t)(uint8_t)(int8_t)(g16 >> 8) << (8 * (q & 3));
@@ -623,16 +684,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                         int32_t o[32];
 #pragma unroll
                         for (int q = 0; q < 32; q++) {
-                            if constexpr (S32) o[q] = rescale_e<true>(v[q], pm[c0 + q], pc[c0 + q], s, fast);
-                            else o[q] = (int32_t)clamp64(rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast), INT32_MIN,
-                                                         INT32_MAX);
+                            if constexpr (S32) o[q] = y32[q];
+                            else o[q] = (int32_t)clamp64(Y(q), INT32_MIN, INT32_MAX);
                         }
+                        uint4 blk[8];
 #pragma unroll
-                        for (int p = 0; p < 4; p++)
-                            if (colb + 8 * p < e.N)
-                                store_piece(make_uint4(o[8 * p], o[8 * p + 1], o[8 * p + 2], o[8 * p + 3]),
-                                        make_uint4(o[8 * p + 4], o[8 * p + 5], o[8 * p + 6], o[8 * p + 7]),
-                                        colb + 8 * p, mt * BM + g * 32);
+                        for (int j = 0; j < 8; j++) blk[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                        store_block(blk, colb, mt * BM + g * 32);
                     } else if (MODE == EPI_RAW) {
                         int32_t* dst = e.out32 + (size_t)row * e.ldo + colb;
 #pragma unroll
@@ -645,7 +703,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_arrive(&bars->tempty[acc]);
         }
         // The TMA stores of this warp are complete before the CTA (and its shared memory) ends.
-        if (Cfg<MODE>::STORE_BUFS > 0 && lane == 0) bulk_wait_all();
+        if (Cfg<MODE>::STORE_WARP > 0 && lane == 0) bulk_wait_all();
     }
     __syncthreads();
     if (warp == 1) {

@@ -42,9 +42,10 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
                         cudaStream_t st);
 
 // The same GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
-// `tmA` and `tmB` are CUtensorMap objects (128-byte aligned, 128 bytes each). EPI_DELTA, EPI_GELU
-// and EPI_LOGITS store their output through `tmC` (32-row x 32-byte boxes, 32-byte swizzle, over
-// all the rows of the output buffer); the other modes take nullptr.
+// `tmA` and `tmB` are CUtensorMap objects (128-byte aligned, 128 bytes each). EPI_DELTA and
+// EPI_LOGITS store their output through `tmC` with 32-row x 128-byte boxes (128-byte swizzle),
+// EPI_GELU with 32-row x 32-byte boxes (32-byte swizzle), over all the rows of the output buffer;
+// the other modes take nullptr.
 // tmA2 != nullptr (EPI_DELTA and EPI_LOGITS of version 2 models): tmA and tmA2 are the hi and lo
 // planes of i16 activations, tmB has 128-row boxes and the tiles are 128 x 128.
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,

@@ -95,6 +95,9 @@ extern "C" int hs_op_linear_bench(hs_dev* dev, int path, uint32_t M, uint32_t N,
     e.s = 38;
     e.out8 = out;
     e.ldo = (int)N;
+    // |acc| <= K * 127^2 <= 2^30 and m < 2^31, so every output is below 2^23 in magnitude at s = 38:
+    // the 32-bit epilogue of the forward pass applies.
+    e.small = 1;
     cudaStream_t st;
     BK_CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     auto launch = [&]() {

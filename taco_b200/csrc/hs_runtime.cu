@@ -99,17 +99,18 @@ int make_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, uint64_t rows, uin
 }
 
 // The store tensor map of a GEMM epilogue: [rows, cols] elements of `esize` bytes with a row pitch
-// of `ld` elements, boxes of 32 rows x 32 bytes with the 32-byte swizzle.
+// of `ld` elements, boxes of 32 rows x box_bytes (32 or 128) with the swizzle of that width.
 int make_store_tmap(hs_dev* dev, CUtensorMap* tm, const void* base, CUtensorMapDataType type, int esize,
-                    uint64_t rows, uint64_t cols, uint64_t ld) {
+                    uint64_t rows, uint64_t cols, uint64_t ld, int box_bytes) {
     cuuint64_t gdim[2] = {cols, rows};
     cuuint64_t gstride[1] = {ld * (uint64_t)esize};
-    cuuint32_t box[2] = {(cuuint32_t)(32 / esize), 32};
+    cuuint32_t box[2] = {(cuuint32_t)(box_bytes / esize), 32};
     cuuint32_t estr[2] = {1, 1};
     if (((uintptr_t)base & 15) != 0 || (gstride[0] & 15) != 0)
         return fail(HS_UNSUPPORTED, "a TMA tensor needs 16-byte aligned rows");
     CUresult r = dev->encode(tm, type, 2, const_cast<void*>(base), gdim, gstride, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(HS_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     return HS_OK;
@@ -900,9 +901,9 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
     CK(cudaMallocHost(&b->h_intervals, sizeof(uint64_t) * 3 * R));
     b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24 +
                                 (c.lnf_wide ? c.Dp : 0) + (gelu_wide ? c.Fp : 0));
-    if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d)) ||
-        (rc = make_store_tmap(m->dev, &b->ts_g, b->g, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, c.f, c.Fp)) ||
-        (rc = make_store_tmap(m->dev, &b->ts_d16, b->d16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, R, c.V, c.Vp)))
+    if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d, 128)) ||
+        (rc = make_store_tmap(m->dev, &b->ts_g, b->g, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, c.f, c.Fp, 32)) ||
+        (rc = make_store_tmap(m->dev, &b->ts_d16, b->d16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, R, c.V, c.Vp, 128)))
         return rc;
     if ((rc = make_tmap(m->dev, &b->tm_a, b->a, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_att, b->att, R, c.Dp, TILE_M)) ||
