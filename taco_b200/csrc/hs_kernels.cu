@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <type_traits>
 
 #include "hs_common.cuh"
 #include "hs_kernels.cuh"
@@ -714,17 +715,17 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         const int64_t o = mx - tr[v0 >> tsh];
         return o < (int64_t)last ? (int32_t)o : last;
     };
-    // Pass 1: the distance counts, the largest distance and the largest symbol.
+    // Pass 1: the distance counts (and, for a decode query, the largest symbol: an encode query
+    // finds out where it lies in its prefix pass instead).
+    const RowInfo q = rows[r];
     uint32_t nlast = 0;
-    int32_t dmax = 0;
     int best = V;
     // Groups of 8 symbols, CODER_UNROLL groups per thread and round so that several 16-byte loads
     // are in flight before the counting.
-    auto count_group = [&](int v0, uint4 raw) {
+    auto count_group = [&](int v0, uint4 raw, auto track) {
         const int32_t off = tile_off(v0);
         if (off == last) {
             nlast += 8;
-            dmax = last;
             return;
         }
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -734,12 +735,11 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
             dd = dd < last ? dd : last;
             if (dd < last) atomicAdd(&F[dd], 1u);
             else nlast++;
-            dmax = dd > dmax ? dd : dmax;
-            best = dd <= head && v0 + i < best ? v0 + i : best;
+            if constexpr (decltype(track)::value) best = dd <= head && v0 + i < best ? v0 + i : best;
         }
     };
     constexpr int CODER_UNROLL = 4;
-    {
+    auto pass1 = [&](auto track) {
         int g0 = threadIdx.x;
         for (; g0 + (CODER_UNROLL - 1) * CODER_THREADS < ng_full; g0 += CODER_UNROLL * CODER_THREADS) {
             uint4 raw[CODER_UNROLL];
@@ -747,10 +747,13 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
             for (int k = 0; k < CODER_UNROLL; k++)
                 raw[k] = *reinterpret_cast<const uint4*>(dr + 8 * (g0 + k * CODER_THREADS));
 #pragma unroll
-            for (int k = 0; k < CODER_UNROLL; k++) count_group(8 * (g0 + k * CODER_THREADS), raw[k]);
+            for (int k = 0; k < CODER_UNROLL; k++) count_group(8 * (g0 + k * CODER_THREADS), raw[k], track);
         }
-        for (; g0 < ng_full; g0 += CODER_THREADS) count_group(8 * g0, *reinterpret_cast<const uint4*>(dr + 8 * g0));
-    }
+        for (; g0 < ng_full; g0 += CODER_THREADS)
+            count_group(8 * g0, *reinterpret_cast<const uint4*>(dr + 8 * g0), track);
+    };
+    if (q.kind == 0) pass1(std::false_type{});
+    else pass1(std::true_type{});
     if (ng_full < ng && threadIdx.x == ng_full % CODER_THREADS) {
         const int v0 = 8 * ng_full;
         const int32_t off = tile_off(v0);
@@ -759,11 +762,14 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
             dd = dd < last ? dd : last;
             if (dd < last) atomicAdd(&F[dd], 1u);
             else nlast++;
-            dmax = dd > dmax ? dd : dmax;
             best = dd <= head && v < best ? v : best;
         }
     }
-    const uint64_t n_last = block_sum64(nlast, redu);
+    const uint64_t n_last = block_sum64(nlast, redu);  // (its barriers also publish the counts)
+    // The largest distance that occurs: the highest counted bin.
+    int32_t dmax = n_last ? last : 0;
+    for (int j = threadIdx.x; j < last; j += CODER_THREADS)
+        if (F[j]) dmax = j > dmax ? j : dmax;
     dmax = (int32_t)block_max64(dmax, red);
     const int largest_found = (int)-block_max64(-(int64_t)best, red);
     // W = sum over the distances of count * table (< 2^16 * 2^40: fits in 64 bits).
@@ -791,23 +797,32 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         sum_f = block_sum64(sum_f, redu);  // (its barriers also publish F)
     }
     const uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
-    const RowInfo q = rows[r];
     auto f_of = [&](int32_t off, uint32_t d) -> uint32_t {
         int32_t dd = off + (int32_t)d;
         return all_zero ? f_flat : F[dd < last ? dd : last];
     };
     if (q.kind == 0) {
-        // Encode: start = sum of f below the token (+ rem past the largest symbol).
+        // Encode: start = sum of f below the token (+ rem if the largest symbol is below it). The
+        // largest symbol is the lowest id at a distance <= head, so it lies below the token if any
+        // symbol below does, and is the token if none does and the token does.
         const int s = (int)q.value;
         const int gs = s / 8;
         uint64_t pre = 0;
+        bool below = false;
         auto group_sum = [&](int v0, uint4 raw) {
             const int32_t off = tile_off(v0);
             const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
             uint32_t gsum = 0;  // 8 frequencies: at most total - (V - 8) < 2^32 for V > 8
+            int32_t dmin = last;
 #pragma unroll
-            for (int i = 0; i < 8; i++) gsum += f_of(off, (u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
+            for (int i = 0; i < 8; i++) {
+                int32_t dd = off + (int32_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
+                dd = dd < last ? dd : last;
+                dmin = dd < dmin ? dd : dmin;
+                gsum += all_zero ? f_flat : F[dd];
+            }
             pre += gsum;
+            below |= dmin <= head;
         };
         int gj = threadIdx.x;
         for (; gj + (CODER_UNROLL - 1) * CODER_THREADS < gs; gj += CODER_UNROLL * CODER_THREADS) {
@@ -821,12 +836,23 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         for (; gj < gs; gj += CODER_THREADS) group_sum(8 * gj, *reinterpret_cast<const uint4*>(dr + 8 * gj));
         if (threadIdx.x == CODER_THREADS - 1) {
             const int32_t off = tile_off(8 * gs);
-            for (int v = 8 * gs; v < s; v++) pre += f_of(off, dr[v]);
+            for (int v = 8 * gs; v < s; v++) {
+                int32_t dd = off + (int32_t)dr[v];
+                dd = dd < last ? dd : last;
+                below |= dd <= head;
+                pre += f_of(off, dr[v]);
+            }
         }
         pre = block_sum64(pre, redu);
+        below = __syncthreads_or(below) != 0;
         if (threadIdx.x == 0) {
-            const uint64_t start = pre + ((uint64_t)s > (uint64_t)largest ? rem : 0);
-            const uint64_t freq = f_of(tile_off(s), dr[s]) + (s == largest ? rem : 0);
+            int32_t ds = tile_off(s) + (int32_t)dr[s];
+            ds = ds < last ? ds : last;
+            // all_zero: every weight is 1 and symbol 0 is the largest.
+            const bool lt = all_zero ? s > 0 : below;
+            const bool eq = all_zero ? s == 0 : (!below && ds <= head);
+            const uint64_t start = pre + (lt ? rem : 0);
+            const uint64_t freq = f_of(tile_off(s), dr[s]) + (eq ? rem : 0);
             out[3 * (size_t)r] = (uint64_t)s;
             out[3 * (size_t)r + 1] = start;
             out[3 * (size_t)r + 2] = freq;
