@@ -263,34 +263,54 @@ __global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t
         int4 dv[NV];
 #pragma unroll
         for (int i = 0; i < NV; i++) dv[i] = __ldcs(dr + 32 * i);
+        // clamp(x + delta, -R, R): |x| <= R < 2^31, so the saturating 32-bit sum clamped to
+        // [-R, R] is exact.
+        auto radd = [](int32_t a, int32_t b) {
+            int32_t t;
+            asm("add.sat.s32 %0, %1, %2;" : "=r"(t) : "r"(a), "r"(b));
+            return min(max(t, -RESIDUAL_LIMIT), RESIDUAL_LIMIT);
+        };
 #pragma unroll
         for (int i = 0; i < NV; i++) {
-            v[i].x = (int32_t)clamp64((int64_t)v[i].x + dv[i].x, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-            v[i].y = (int32_t)clamp64((int64_t)v[i].y + dv[i].y, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-            v[i].z = (int32_t)clamp64((int64_t)v[i].z + dv[i].z, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-            v[i].w = (int32_t)clamp64((int64_t)v[i].w + dv[i].w, -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
+            v[i].x = radd(v[i].x, dv[i].x);
+            v[i].y = radd(v[i].y, dv[i].y);
+            v[i].z = radd(v[i].z, dv[i].z);
+            v[i].w = radd(v[i].w, dv[i].w);
             xr[32 * i] = v[i];
         }
     }
+    // Pairs of values (|x| <= R < 2^30) add in 32 bits without overflow.
     int64_t sum = 0;
 #pragma unroll
-    for (int i = 0; i < NV; i++) sum += (int64_t)v[i].x + v[i].y + v[i].z + v[i].w;
+    for (int i = 0; i < NV; i++) sum += (int64_t)(v[i].x + v[i].y) + (int64_t)(v[i].z + v[i].w);
     sum = warp_sums64(sum);
     const int64_t mean = floor_div64(sum, D);
+    // |x - mean| < 2^31, so (x - mean)^2 < 2^62 is one 32x32 -> 64 multiply, and three of them add in
+    // 64 bits without overflow; the 128-bit total carries between the groups of three.
+    const int32_t mean32 = (int32_t)mean;
     uint64_t lo = 0, hi = 0;
-    auto acc_sq = [&](int32_t xv) {
-        const int64_t c = (int64_t)xv - mean;
-        const uint64_t a = c < 0 ? (uint64_t)(-c) : (uint64_t)c;
-        const uint64_t sq = a * a;  // |c| < 2^31, so c^2 < 2^62
-        lo += sq;
-        hi += lo < sq ? 1 : 0;
+    auto sq = [&](int32_t xv) {
+        const int32_t c = xv - mean32;
+        return (uint64_t)((int64_t)c * (int64_t)c);
     };
+    auto acc3 = [&](uint64_t t) {
+        lo += t;
+        hi += lo < t ? 1 : 0;
+    };
+    int32_t xs_all[4 * NV];
 #pragma unroll
     for (int i = 0; i < NV; i++) {
-        acc_sq(v[i].x);
-        acc_sq(v[i].y);
-        acc_sq(v[i].z);
-        acc_sq(v[i].w);
+        xs_all[4 * i] = v[i].x;
+        xs_all[4 * i + 1] = v[i].y;
+        xs_all[4 * i + 2] = v[i].z;
+        xs_all[4 * i + 3] = v[i].w;
+    }
+#pragma unroll
+    for (int k = 0; k < 4 * NV; k += 3) {
+        uint64_t t = sq(xs_all[k]);
+        if (k + 1 < 4 * NV) t += sq(xs_all[k + 1]);
+        if (k + 2 < 4 * NV) t += sq(xs_all[k + 2]);
+        acc3(t);
     }
     for (int o = 16; o > 0; o >>= 1) {
         uint64_t lo2 = __shfl_xor_sync(0xffffffffu, lo, o);
@@ -326,7 +346,7 @@ __global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t
         uint32_t word = 0, lword = 0;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const int64_t cg = ((int64_t)xs[k] - mean) * (int64_t)gs[k];  // |cg| < 2^47
+            const int64_t cg = (int64_t)(xs[k] - mean32) * (int64_t)gs[k];  // |cg| < 2^47
             int64_t yv;
             bool done = false;
             if (est_ok) {
