@@ -430,14 +430,16 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tmem_ld16(tmem + ((uint32_t)(g * 32) << 16) + 2 * KC + pl * HDIM + qt * 16, o[pl]);
         tmem_ld_wait();
         if (row_ok) {
+            // att = clamp(rescale(acc, om, os), -127, 127), |acc| <= 2^30 * 128.
+            const double omsc = (double)om * exp2_neg(os);
             uint32_t packed[4];
 #pragma unroll
             for (int q = 0; q < 16; q++) {
                 int64_t acc = ((((int64_t)(int32_t)o[3][q] * 256 + (int32_t)o[2][q]) * 256 + (int32_t)o[1][q]) * 256) +
                               (int32_t)o[0][q];
-                int8_t y = (int8_t)clamp128(rescale128(acc, om, (uint32_t)os), -127, 127);
-                if ((q & 3) == 0) packed[q >> 2] = (uint8_t)y;
-                else packed[q >> 2] |= (uint32_t)(uint8_t)y << (8 * (q & 3));
+                const int32_t y = rescale_clamp127(acc, om, os, omsc);
+                if ((q & 3) == 0) packed[q >> 2] = (uint8_t)(int8_t)y;
+                else packed[q >> 2] |= (uint32_t)(uint8_t)(int8_t)y << (8 * (q & 3));
             }
             *reinterpret_cast<uint4*>(att + (size_t)(grp.first_row + row) * lda + h * HDIM + qt * 16) =
                 make_uint4(packed[0], packed[1], packed[2], packed[3]);

@@ -85,6 +85,21 @@ __device__ __forceinline__ double exp2_neg(int s) {
     return __longlong_as_double((long long)(1023 - s) << 52);
 }
 
+// clamp(rescale(acc, m, s), -127, 127) (int.rs:63 with the attention output clamp) for
+// |acc| < 2^53, with msc = m * 2^-s (exact). The double z = acc * msc + 1/2 has one rounding, so
+// for |z| < 1024 it is within 2^-43 of the exact value and its floor is the result unless the
+// fraction is within 2^-40 of an integer; those values, and s > 95, take the exact 128-bit rule.
+__device__ __forceinline__ int32_t rescale_clamp127(int64_t acc, int32_t m, int s, double msc) {
+    const double z = fma((double)acc, msc, 0.5);
+    const double fl = floor(z);
+    const double fr = z - fl;
+    if (s <= 95) {
+        if (fabs(z) >= 1024.0) return z > 0 ? 127 : -127;
+        if (fr > 9.094947017729282e-13 && fr < 1.0 - 9.094947017729282e-13) return min(max((int32_t)fl, -127), 127);
+    }
+    return (int32_t)clamp128(rescale128(acc, m, (uint32_t)s), -127, 127);
+}
+
 // floor(x / d) for a 128-bit x whose quotient fits in 64 bits, d >= 1: a double estimate and an
 // exact integer correction (the estimate is within a few units; each correction is exact).
 __device__ __forceinline__ uint64_t udiv128_small(u128 x, uint64_t d) {

@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention_vec(const RowInfo* ro
         }
         if (lane == 0) {
             int64_t acc = ((((int64_t)a3 * 256 + a2) * 256 + a1) * 256) + a0;
-            att[(size_t)r * lda + h * HD + c] = (int8_t)clamp128(rescale128(acc, om, os), -127, 127);
+            att[(size_t)r * lda + h * HD + c] = (int8_t)rescale_clamp127(acc, om, (int)os, (double)om * exp2_neg((int)os));
         }
     }
 }
