@@ -430,17 +430,35 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tmem_ld16(tmem + ((uint32_t)(g * 32) << 16) + 2 * KC + pl * HDIM + qt * 16, o[pl]);
         tmem_ld_wait();
         if (row_ok) {
-            // att = clamp(rescale(acc, om, os), -127, 127), |acc| <= 2^30 * 128.
+            // att = clamp(rescale(acc, om, os), -127, 127), |acc| <= 2^30 * 128 (rescale_clamp127): the
+            // double estimates of all 16 values first, branch-free, so their latencies overlap; the
+            // values too close to a rounding boundary take the exact rule afterwards.
             const double omsc = (double)om * exp2_neg(os);
-            uint32_t packed[4];
+            int64_t accs[16];
+            int32_t ys[16];
+            uint32_t slow = os > 95 ? 0xFFFFu : 0u;
 #pragma unroll
             for (int q = 0; q < 16; q++) {
-                int64_t acc = ((((int64_t)(int32_t)o[3][q] * 256 + (int32_t)o[2][q]) * 256 + (int32_t)o[1][q]) * 256) +
-                              (int32_t)o[0][q];
-                const int32_t y = rescale_clamp127(acc, om, os, omsc);
-                if ((q & 3) == 0) packed[q >> 2] = (uint8_t)(int8_t)y;
-                else packed[q >> 2] |= (uint32_t)(uint8_t)(int8_t)y << (8 * (q & 3));
+                accs[q] = ((((int64_t)(int32_t)o[3][q] * 256 + (int32_t)o[2][q]) * 256 + (int32_t)o[1][q]) * 256) +
+                          (int32_t)o[0][q];
+                const double z = fma((double)accs[q], omsc, 0.5);
+                const double zc = fmin(fmax(z, -1024.0), 1024.0);
+                const double fl = floor(zc);
+                const double fr = zc - fl;
+                ys[q] = min(max((int32_t)fl, -127), 127);
+                const bool near = fabs(z) < 1024.0 && !(fr > 9.094947017729282e-13 && fr < 1.0 - 9.094947017729282e-13);
+                slow |= (uint32_t)near << q;
             }
+            if (slow) {
+#pragma unroll
+                for (int q = 0; q < 16; q++)
+                    if ((slow >> q) & 1) ys[q] = (int32_t)clamp128(rescale128(accs[q], om, (uint32_t)os), -127, 127);
+            }
+            uint32_t packed[4];
+#pragma unroll
+            for (int w = 0; w < 4; w++)
+                packed[w] = __byte_perm(__byte_perm(ys[4 * w], ys[4 * w + 1], 0x0040),
+                                        __byte_perm(ys[4 * w + 2], ys[4 * w + 3], 0x0040), 0x5410);
             *reinterpret_cast<uint4*>(att + (size_t)(grp.first_row + row) * lda + h * HDIM + qt * 16) =
                 make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
