@@ -406,7 +406,9 @@ def main():
 def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, context: int = 512, steps: int = 16) -> dict:
     """1024 streams decoded token by token. The streams are filled to `context`
     positions (prefill, not timed), then `steps` decode steps (one row per stream, the coder
-    op answering each row) are timed with the wall clock around the C-ABI calls."""
+    op answering a decode query for each row: the symbol whose interval holds a seeded 32-bit
+    target) are timed on the device and with the wall clock around the C-ABI calls. The next
+    input of a stream is the text's own next token, so the rows are those of a real unfold."""
     from taco_b200 import synth
 
     toks = synth.zipf_windows(streams, context + steps, seed=77)
@@ -414,11 +416,12 @@ def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, conte
     slots, inputs, coded = window_rows(toks[:, :context], eot)
     batch.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32)
     sl = np.arange(streams, dtype=np.uint32)
-    kinds = np.zeros(streams, np.uint32)
+    kinds = np.ones(streams, np.uint32)
+    targets = np.random.default_rng(78).integers(0, 1 << 32, (steps, streams), dtype=np.uint64)
     batch.set_profiling(True)
     t0 = time.perf_counter()
     for i in range(steps):
-        batch.run_coded(sl, toks[:, context + i - 1], kinds, toks[:, context + i].astype(np.uint64), 32)
+        batch.run_coded(sl, toks[:, context + i - 1], kinds, targets[i], 32)
     wall = time.perf_counter() - t0
     prof = batch.profile()
     batch.close()
@@ -429,7 +432,8 @@ def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, conte
             "tokens_per_s": streams * steps / dev_s, "MB_per_s": nbytes / dev_s / 1e6,
             "e2e_tokens_per_s": streams * steps / wall,
             "kv_GB_per_s": kv_read / dev_s / 1e9,
-            "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3)}
+            "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3),
+            "kernels_ms_per_step": {k: round(v["ms"] / steps, 3) for k, v in prof.items() if v["launches"]}}
 
 
 if __name__ == "__main__":

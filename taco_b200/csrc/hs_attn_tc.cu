@@ -472,6 +472,191 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     }
 }
 
+// ---- decode attention: one warp per (row, head) ----
+//
+// The rows of a pass that are not in a prefill group (batched decode: one row per stream). Each
+// warp reads the row's K [n x 64] and V^T [64 x n] of one head once, which is all the DRAM traffic
+// there is: the dots (dp4a) into shared memory with the max and min dot, then e and the sum, then
+// p (the exact multiply-shift of the prefill kernel) as four unsigned byte planes in place, then
+// P V with u8 x s8 dp4a over 16 channels at a time. Each lane accumulates its keys' part of the
+// 16 channels x 4 planes; a butterfly reduce-scatter leaves lane l with values 2l and 2l + 1, and
+// one more exchange joins the four planes of a channel. No block-wide synchronisation.
+constexpr int DEC_WARPS = 4;
+
+__device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+template <bool NARROW, bool SSHI>
+__global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo* rows, const int* rowlist, int nrows,
+                                                                   const int8_t* qkv, int ldq, const int8_t* kc,
+                                                                   const int8_t* vc, int L, int layer, int H,
+                                                                   int n_ctx, int32_t sm, int ss, int32_t om, int os,
+                                                                   const int32_t* table, int tlen, int P, int8_t* att,
+                                                                   int lda) {
+    extern __shared__ __align__(16) uint32_t s_dec[];  // [DEC_WARPS][n_ctx]: dots, then e, then p planes
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int item = blockIdx.x * DEC_WARPS + warp;
+    if (item >= nrows * H) return;
+    const int h = item % H;
+    const int r = rowlist ? rowlist[item / H] : item / H;
+    const RowInfo ri = rows[r];
+    const int n = (int)ri.pos + 1;
+    uint32_t* sb = s_dec + (size_t)warp * n_ctx;
+    const size_t head = ((size_t)ri.slot * L + layer) * H + h;
+    const int4* K = reinterpret_cast<const int4*>(kc + head * n_ctx * HDIM);
+    const int8_t* Vt = vc + head * HDIM * n_ctx;
+    int32_t qw[16];
+    {
+        const int4* qp = reinterpret_cast<const int4*>(qkv + (size_t)r * ldq + h * HDIM);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int4 v = qp[i];
+            qw[4 * i] = v.x;
+            qw[4 * i + 1] = v.y;
+            qw[4 * i + 2] = v.z;
+            qw[4 * i + 3] = v.w;
+        }
+    }
+    // Pass 1: the dots (4 keys per lane in flight).
+    int32_t maxd = INT32_MIN, mind = INT32_MAX;
+    for (int j0 = 0; j0 < n; j0 += 128) {
+        int4 kv[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int j = j0 + 32 * u + lane;
+            if (j < n) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) kv[u][i] = K[(size_t)j * 4 + i];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int j = j0 + 32 * u + lane;
+            if (j < n) {
+                int32_t dot = 0;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    dot = __dp4a(qw[4 * i], kv[u][i].x, dot);
+                    dot = __dp4a(qw[4 * i + 1], kv[u][i].y, dot);
+                    dot = __dp4a(qw[4 * i + 2], kv[u][i].z, dot);
+                    dot = __dp4a(qw[4 * i + 3], kv[u][i].w, dot);
+                }
+                sb[j] = (uint32_t)dot;
+                maxd = max(maxd, dot);
+                mind = min(mind, dot);
+            }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        maxd = max(maxd, __shfl_xor_sync(0xffffffffu, maxd, o));
+        mind = min(mind, __shfl_xor_sync(0xffffffffu, mind, o));
+    }
+    const bool fast = ss >= 0 && ss <= 62;
+    const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
+    const int32_t last = (tlen < TABLE_MAX ? tlen : TABLE_MAX) - 1;
+    const int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
+    const int64_t M = s1 > s2 ? s1 : s2;
+    auto dist = [&](int32_t dot) -> int32_t {
+        if constexpr (NARROW) {
+            const int64_t t = (int64_t)dot * (int64_t)sm + hround;
+            int32_t score;
+            if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
+            else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+            const int32_t dd = (int32_t)M - score;
+            return dd < last ? dd : last;
+        } else {
+            return dist_of<false>(M, dot, sm, ss, fast, hround, last);
+        }
+    };
+    __syncwarp();
+    // Pass 2: e in place and the sum.
+    uint64_t sum = 0;
+    for (int j = lane; j < n; j += 32) {
+        const uint32_t e = (uint32_t)__ldg(table + dist((int32_t)sb[j]));
+        sb[j] = e;
+        sum += e;
+    }
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (sum == 0) sum = 1;
+    int l = 64 - __clzll((long long)(sum - 1));
+    if (l < 1) l = 1;
+    const uint64_t mg = (uint64_t)((((u128)1 << (31 + P + l)) + (sum - 1)) / sum);
+    const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
+    const int psh = l - 1;
+    __syncwarp();
+    // Pass 3: p as four byte planes of each quad of keys, in place (keys past n give 0).
+    const int nq = (n + 15) >> 4 << 2;  // whole 16-key groups (n_ctx % 16 == 0), zeros past n
+    for (int qd = lane; qd < nq; qd += 32) {
+        uint32_t pv[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int j = 4 * qd + k;
+            uint32_t p = 0;
+            if (j < n) {
+                const uint32_t e = sb[j];
+                const uint64_t t = (uint64_t)e * ml;
+                const uint64_t u = (uint64_t)e * mh + (t >> 32);
+                p = (uint32_t)(u >> psh);
+            }
+            pv[k] = p;
+        }
+        const uint32_t a = __byte_perm(pv[0], pv[1], 0x5140), b2 = __byte_perm(pv[0], pv[1], 0x7362);
+        const uint32_t c2 = __byte_perm(pv[2], pv[3], 0x5140), d2 = __byte_perm(pv[2], pv[3], 0x7362);
+        *reinterpret_cast<uint4*>(sb + 4 * qd) = make_uint4(__byte_perm(a, c2, 0x5410), __byte_perm(a, c2, 0x7632),
+                                                            __byte_perm(b2, d2, 0x5410), __byte_perm(b2, d2, 0x7632));
+    }
+    __syncwarp();
+    // P V, 16 channels at a time.
+    const double omsc = (double)om * exp2_neg(os);
+#pragma unroll 1
+    for (int c0 = 0; c0 < HDIM; c0 += 16) {
+        int32_t acc[64];  // [channel][plane]
+#pragma unroll
+        for (int i = 0; i < 64; i++) acc[i] = 0;
+        // Each lane takes 16 keys (4 quads) per step: one 16-byte load per channel row.
+        for (int qg = lane; 4 * qg < nq; qg += 32) {
+            uint4 vv[16];
+#pragma unroll
+            for (int c = 0; c < 16; c++)
+                vv[c] = __ldg(reinterpret_cast<const uint4*>(Vt + (size_t)(c0 + c) * n_ctx) + qg);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint4 pw = *reinterpret_cast<const uint4*>(sb + 16 * qg + 4 * k);
+#pragma unroll
+                for (int c = 0; c < 16; c++) {
+                    const uint32_t v = k == 0 ? vv[c].x : k == 1 ? vv[c].y : k == 2 ? vv[c].z : vv[c].w;
+                    acc[4 * c] = dp4a_us(pw.x, v, acc[4 * c]);
+                    acc[4 * c + 1] = dp4a_us(pw.y, v, acc[4 * c + 1]);
+                    acc[4 * c + 2] = dp4a_us(pw.z, v, acc[4 * c + 2]);
+                    acc[4 * c + 3] = dp4a_us(pw.w, v, acc[4 * c + 3]);
+                }
+            }
+        }
+        // Butterfly reduce-scatter: lane l ends with the warp sums of values 2l and 2l + 1.
+#pragma unroll
+        for (int o = 16, half = 32; o > 0; o >>= 1, half >>= 1) {
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int k = 0; k < half; k++) {
+                const int32_t send = up ? acc[k] : acc[k + half];
+                const int32_t keep = up ? acc[k + half] : acc[k];
+                acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        // Lane l holds channel c0 + l / 2, planes 0 and 1 (l even) or 2 and 3 (l odd).
+        const int32_t o2 = __shfl_xor_sync(0xffffffffu, acc[0], 1);
+        const int32_t o3 = __shfl_xor_sync(0xffffffffu, acc[1], 1);
+        if ((lane & 1) == 0) {
+            // Each plane sum is at most n * 255 * 128 < 2^31 in magnitude.
+            const int64_t a = ((((int64_t)o3 * 256 + o2) * 256 + acc[1]) * 256) + acc[0];
+            att[(size_t)r * lda + h * HDIM + c0 + (lane >> 1)] = (int8_t)rescale_clamp127(a, om, os, omsc);
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t configure_attn_tc() {
@@ -481,7 +666,39 @@ cudaError_t configure_attn_tc() {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
         if (e != cudaSuccess) return e;
     }
+    const void* dfns[3] = {(const void*)k_attention_dec<true, true>, (const void*)k_attention_dec<true, false>,
+                           (const void*)k_attention_dec<false, false>};
+    for (const void* f : dfns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             DEC_WARPS * 4 * MAX_ATTN_CTX);
+        if (e != cudaSuccess) return e;
+    }
     return cudaSuccess;
+}
+
+bool attention_dec_supported(int hd, int n_ctx, int ldq, int tlen) {
+    return hd == HDIM && n_ctx % 16 == 0 && ldq % 16 == 0 && tlen <= TABLE_MAX;
+}
+
+void launch_attention_dec(const RowInfo* rows, const int* rowlist, int nrows, const int8_t* qkv, int ldq,
+                          const int8_t* kc, const int8_t* vc, int L, int layer, int H, int n_ctx, int32_t sm, int ss,
+                          int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att, int lda,
+                          cudaStream_t st) {
+    if (nrows <= 0) return;
+    const int grid = (nrows * H + DEC_WARPS - 1) / DEC_WARPS;
+    const size_t smem = (size_t)DEC_WARPS * n_ctx * 4;
+    if (ss >= 32 && ss <= 62)
+        k_attention_dec<true, true><<<grid, 32 * DEC_WARPS, smem, st>>>(rows, rowlist, nrows, qkv, ldq, kc, vc, L,
+                                                                       layer, H, n_ctx, sm, ss, om, os, table, tlen,
+                                                                       P, att, lda);
+    else if (ss >= 21 && ss < 32)
+        k_attention_dec<true, false><<<grid, 32 * DEC_WARPS, smem, st>>>(rows, rowlist, nrows, qkv, ldq, kc, vc, L,
+                                                                        layer, H, n_ctx, sm, ss, om, os, table, tlen,
+                                                                        P, att, lda);
+    else
+        k_attention_dec<false, false><<<grid, 32 * DEC_WARPS, smem, st>>>(rows, rowlist, nrows, qkv, ldq, kc, vc, L,
+                                                                         layer, H, n_ctx, sm, ss, om, os, table,
+                                                                         tlen, P, att, lda);
 }
 
 bool attention_tc_supported(int hd, int n_ctx, int tlen) {

@@ -66,6 +66,14 @@ void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, con
 // transposed values cache (128 x 64, 128-byte swizzle).
 cudaError_t configure_attn_tc();
 bool attention_tc_supported(int hd, int n_ctx, int tlen);
+// The rows of a pass outside the prefill groups (batched decode) with one warp per (row, head):
+// head width 64, n_ctx % 16 == 0, 16-byte aligned q rows.
+bool attention_dec_supported(int hd, int n_ctx, int ldq, int tlen);
+void launch_attention_dec(const RowInfo* rows, const int* rowlist, int nrows, const int8_t* qkv, int ldq,
+                          const int8_t* kc, const int8_t* vc, int L, int layer, int H, int n_ctx, int32_t sm, int ss,
+                          int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att, int lda,
+                          cudaStream_t st);
+
 void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, const AttnGroup* groups, int n_groups,
                          int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,
                          const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st);

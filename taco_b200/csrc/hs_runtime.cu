@@ -156,6 +156,7 @@ struct hs_model {
     uint64_t weight_bytes = 0;
     bool use_tc = true;
     bool attn_tc = false;
+    bool attn_dec = false;  // the warp-per-(row, head) decode attention for rows outside the groups
     int8_t* wte = nullptr;
     int32_t* em = nullptr;
     int es = 0;
@@ -400,9 +401,16 @@ int forward(hs_batch* b, int R) {
             launch_attention_tc(&b->tm_q, &b->tm_k, &b->tm_v, b->d_groups, b->n_groups, c.L, l, c.H, c.n_ctx,
                                 Ld.score_m, Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p,
                                 b->att, c.Dp, m->dev->d_err, st);
-            launch_attention(b->d_rows, R, b->n_groups ? b->d_rowlist : nullptr, b->n_groups ? b->n_rowlist : R,
-                             b->qkv, c.QKVp, b->kc, b->vc, c.L, l, c.H, c.hd, c.n_ctx, c.d, Ld.score_m, Ld.score_s,
-                             Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p, b->att, c.Dp, st);
+            const int* rl = b->n_groups ? b->d_rowlist : nullptr;
+            const int nr = b->n_groups ? b->n_rowlist : R;
+            if (m->attn_dec)
+                launch_attention_dec(b->d_rows, rl, nr, b->qkv, c.QKVp, b->kc, b->vc, c.L, l, c.H, c.n_ctx, Ld.score_m,
+                                     Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p, b->att,
+                                     c.Dp, st);
+            else
+                launch_attention(b->d_rows, R, rl, nr, b->qkv, c.QKVp, b->kc, b->vc, c.L, l, c.H, c.hd, c.n_ctx, c.d,
+                                 Ld.score_m, Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p,
+                                 b->att, c.Dp, st);
         }
         e = EpiArgs{};
         e.R = R;
@@ -752,6 +760,8 @@ int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) 
     m->dev = dev;
     m->use_tc = use_tc_default();
     m->attn_tc = use_attn_tc_default() && attention_tc_supported(M.head_dim, M.n_ctx, (int)M.attn_exp.size());
+    m->attn_dec = use_attn_tc_default() &&
+                  attention_dec_supported(M.head_dim, M.n_ctx, round_up(3 * M.d_model, 16), (int)M.attn_exp.size());
     sha256(file, len, m->hash);
     m->eot = M.eot;
     m->version = M.version;
