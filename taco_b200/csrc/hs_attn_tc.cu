@@ -478,9 +478,11 @@ __global__ void __launch_bounds__(ATHREADS, 1)
 // warp reads the row's K [n x 64] and V^T [64 x n] of one head once, which is all the DRAM traffic
 // there is: the dots (dp4a) into shared memory with the max and min dot, then e and the sum, then
 // p (the exact multiply-shift of the prefill kernel) as four unsigned byte planes in place, then
-// P V with u8 x s8 dp4a over 16 channels at a time. Each lane accumulates its keys' part of the
-// 16 channels x 4 planes; a butterfly reduce-scatter leaves lane l with values 2l and 2l + 1, and
-// one more exchange joins the four planes of a channel. No block-wide synchronisation.
+// P V with u8 x s8 dp4a over 8 channels at a time: each lane takes 16 keys per step, one 16-byte
+// load per channel row (a warp reads 512 contiguous bytes of a row), and accumulates its keys'
+// part of the 8 channels x 4 planes; a butterfly reduce-scatter leaves lane l with value l, and
+// lane 4c gathers the four planes of channel c. The dots pass keeps 2 keys per lane in flight,
+// so that 5 blocks fit on an SM. No block-wide synchronisation.
 constexpr int DEC_WARPS = 4;
 
 __device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
@@ -490,7 +492,7 @@ __device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
 }
 
 template <bool NARROW, bool SSHI>
-__global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo* rows, const int* rowlist, int nrows,
+__global__ void __launch_bounds__(32 * DEC_WARPS, 5) k_attention_dec(const RowInfo* rows, const int* rowlist, int nrows,
                                                                    const int8_t* qkv, int ldq, const int8_t* kc,
                                                                    const int8_t* vc, int L, int layer, int H,
                                                                    int n_ctx, int32_t sm, int ss, int32_t om, int os,
@@ -520,12 +522,12 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo*
             qw[4 * i + 3] = v.w;
         }
     }
-    // Pass 1: the dots (4 keys per lane in flight).
+    // Pass 1: the dots (2 keys per lane in flight).
     int32_t maxd = INT32_MIN, mind = INT32_MAX;
-    for (int j0 = 0; j0 < n; j0 += 128) {
-        int4 kv[4][4];
+    for (int j0 = 0; j0 < n; j0 += 64) {
+        int4 kv[2][4];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < 2; u++) {
             const int j = j0 + 32 * u + lane;
             if (j < n) {
 #pragma unroll
@@ -533,7 +535,7 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo*
             }
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < 2; u++) {
             const int j = j0 + 32 * u + lane;
             if (j < n) {
                 int32_t dot = 0;
@@ -609,24 +611,24 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo*
                                                             __byte_perm(b2, d2, 0x5410), __byte_perm(b2, d2, 0x7632));
     }
     __syncwarp();
-    // P V, 16 channels at a time.
+    // P V, 8 channels at a time.
     const double omsc = (double)om * exp2_neg(os);
 #pragma unroll 1
-    for (int c0 = 0; c0 < HDIM; c0 += 16) {
-        int32_t acc[64];  // [channel][plane]
+    for (int c0 = 0; c0 < HDIM; c0 += 8) {
+        int32_t acc[32];  // [channel][plane]
 #pragma unroll
-        for (int i = 0; i < 64; i++) acc[i] = 0;
+        for (int i = 0; i < 32; i++) acc[i] = 0;
         // Each lane takes 16 keys (4 quads) per step: one 16-byte load per channel row.
         for (int qg = lane; 4 * qg < nq; qg += 32) {
-            uint4 vv[16];
+            uint4 vv[8];
 #pragma unroll
-            for (int c = 0; c < 16; c++)
+            for (int c = 0; c < 8; c++)
                 vv[c] = __ldg(reinterpret_cast<const uint4*>(Vt + (size_t)(c0 + c) * n_ctx) + qg);
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const uint4 pw = *reinterpret_cast<const uint4*>(sb + 16 * qg + 4 * k);
 #pragma unroll
-                for (int c = 0; c < 16; c++) {
+                for (int c = 0; c < 8; c++) {
                     const uint32_t v = k == 0 ? vv[c].x : k == 1 ? vv[c].y : k == 2 ? vv[c].z : vv[c].w;
                     acc[4 * c] = dp4a_us(pw.x, v, acc[4 * c]);
                     acc[4 * c + 1] = dp4a_us(pw.y, v, acc[4 * c + 1]);
@@ -635,9 +637,10 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo*
                 }
             }
         }
-        // Butterfly reduce-scatter: lane l ends with the warp sums of values 2l and 2l + 1.
+        // Butterfly reduce-scatter over the 32 values: after offset o the lane keeps the half of
+        // its values picked by its bit o, summed with its partner's; lane l ends with value l.
 #pragma unroll
-        for (int o = 16, half = 32; o > 0; o >>= 1, half >>= 1) {
+        for (int o = 16, half = 16; o > 0; o >>= 1, half >>= 1) {
             const bool up = (lane & o) != 0;
 #pragma unroll
             for (int k = 0; k < half; k++) {
@@ -646,13 +649,14 @@ __global__ void __launch_bounds__(32 * DEC_WARPS) k_attention_dec(const RowInfo*
                 acc[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
             }
         }
-        // Lane l holds channel c0 + l / 2, planes 0 and 1 (l even) or 2 and 3 (l odd).
-        const int32_t o2 = __shfl_xor_sync(0xffffffffu, acc[0], 1);
-        const int32_t o3 = __shfl_xor_sync(0xffffffffu, acc[1], 1);
-        if ((lane & 1) == 0) {
+        // Value l = 4 c + plane: lane 4 c gathers channel c's four planes.
+        const int32_t p1 = __shfl_down_sync(0xffffffffu, acc[0], 1);
+        const int32_t p2 = __shfl_down_sync(0xffffffffu, acc[0], 2);
+        const int32_t p3 = __shfl_down_sync(0xffffffffu, acc[0], 3);
+        if ((lane & 3) == 0) {
             // Each plane sum is at most n * 255 * 128 < 2^31 in magnitude.
-            const int64_t a = ((((int64_t)o3 * 256 + o2) * 256 + acc[1]) * 256) + acc[0];
-            att[(size_t)r * lda + h * HDIM + c0 + (lane >> 1)] = (int8_t)rescale_clamp127(a, om, os, omsc);
+            const int64_t a = ((((int64_t)p3 * 256 + p2) * 256 + p1) * 256) + acc[0];
+            att[(size_t)r * lda + h * HDIM + c0 + (lane >> 2)] = (int8_t)rescale_clamp127(a, om, os, omsc);
         }
     }
 }

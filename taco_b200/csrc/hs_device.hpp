@@ -110,6 +110,23 @@ struct EpiArgs {
     int8_t* kc;
     int8_t* vc;
     int L, layer, H, hd, n_ctx, d;
+    // EPI_QKV on tensor cores: the v of the rows whose 32-row group is not a transposed run
+    // (vt_run) goes here, row-major with stride ldv, for launch_v_scatter to place in vc.
+    int8_t* vstage;
+    int ldv;
 };
+
+// The 32 rows r0 .. r0 + 31 of a pass are one slot at 32 consecutive positions starting at a
+// multiple of 16: their v is stored into the transposed values cache as 32-byte runs. The
+// host form decides whether a pass needs launch_v_scatter; the device forms (the QKV epilogue
+// and the scatter kernel) decide per group, with the same rule.
+inline bool vt_run_host(const RowInfo* rows, int r0, int R, int n_ctx) {
+    if (r0 + 31 >= R || (n_ctx & 15) != 0) return false;
+    const RowInfo& a0 = rows[r0];
+    if ((a0.pos & 15) != 0) return false;
+    for (int i = 1; i < 32; i++)
+        if (rows[r0 + i].slot != a0.slot || rows[r0 + i].pos != a0.pos + (uint32_t)i) return false;
+    return true;
+}
 
 }  // namespace hs

@@ -114,10 +114,15 @@ __device__ __forceinline__ uint32_t pack4_i8(int32_t a, int32_t b, int32_t c, in
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// EPI_QKV: one value at column n of a row of (slot, pos): q to out8, k and v to the caches.
-__device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowInfo& ri, int n, int8_t o) {
+// EPI_QKV: one value at column n of a row of (slot, pos): q to out8, k and v to the caches (v
+// to the staging rows instead when `stage`).
+__device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowInfo& ri, int n, int8_t o, bool stage) {
     if (n < e.d) {
         e.out8[(size_t)row * e.ldo + n] = o;
+        return;
+    }
+    if (stage && n >= 2 * e.d) {
+        e.vstage[(size_t)row * e.ldv + (n - 2 * e.d)] = o;
         return;
     }
     const int j = n < 2 * e.d ? n - e.d : n - 2 * e.d;
@@ -327,18 +332,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             const bool row_ok = row < e.R;
             // EPI_QKV: are this warp's 32 rows 32 consecutive positions of one slot, starting at a
             // multiple of 16 (the transposed v store)? Warp-uniform.
-            bool vt_ok = false;
+            bool vt_ok = false, vt_stage = false;
             uint32_t vt_slot = 0, vt_pos0 = 0;
             if (MODE == EPI_QKV) {
                 const int r0 = mt * BM + g * 32;
-                if (r0 + 31 < e.R && (e.n_ctx & 15) == 0) {
-                    const RowInfo a0 = e.rows[r0], a1 = e.rows[r0 + 31];
-                    const RowInfo me = e.rows[row];
-                    const bool mine_ok = me.slot == a0.slot && me.pos == a0.pos + (uint32_t)lane;
-                    vt_ok = __all_sync(0xffffffffu, mine_ok) && a1.slot == a0.slot && (a0.pos & 15) == 0;
+                vt_ok = vt_run_warp(e.rows, r0, e.R, e.n_ctx, lane);
+                if (vt_ok) {
+                    const RowInfo a0 = e.rows[r0];
                     vt_slot = a0.slot;
                     vt_pos0 = a0.pos;
                 }
+                vt_stage = !vt_ok && e.vstage != nullptr;
             }
             const uint32_t taddr = tmem_base + ((uint32_t)(g * 32) << 16) + (uint32_t)(acc * BN);
             const int32_t* pm = s_m + acc * BN;
@@ -594,6 +598,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                             uint4* dst = reinterpret_cast<uint4*>(e.kc + (head * e.n_ctx + ri.pos) * e.hd + c);
                             dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                             dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        } else if (full && vt_stage && colb >= 2 * e.d && (e.ldv & 15) == 0 &&
+                                   colb + 32 <= 3 * e.d) {
+                            // A whole 32-byte run of v of one row, to the staging rows.
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                pk[q] = (uint32_t)(uint8_t)o[4 * q] | (uint32_t)(uint8_t)o[4 * q + 1] << 8 |
+                                        (uint32_t)(uint8_t)o[4 * q + 2] << 16 | (uint32_t)(uint8_t)o[4 * q + 3] << 24;
+                            uint4* dst = reinterpret_cast<uint4*>(e.vstage + (size_t)row * e.ldv + (colb - 2 * e.d));
+                            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                         } else if (full && vt_ok && colb >= 2 * e.d) {
                             // 32 channels of v for 32 consecutive positions: transpose the 32 x 32
                             // bytes through shared memory, then each lane writes one channel's 32
@@ -621,7 +636,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         } else {
 #pragma unroll
                             for (int q = 0; q < 32; q++)
-                                if (colb + q < e.N) qkv_store(e, row, ri, colb + q, o[q]);
+                                if (colb + q < e.N) qkv_store(e, row, ri, colb + q, o[q], vt_stage);
                         }
                     } else if (MODE == EPI_ACT || MODE == EPI_GELU) {
                         uint32_t packed[8];

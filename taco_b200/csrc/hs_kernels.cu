@@ -489,16 +489,27 @@ __global__ void __launch_bounds__(256) k_gemm_simple(int mode, const int8_t* A, 
 // (the values layout of crates/hardshell/src/gpt2/attention.rs:48, so p.v is a dot product along
 // the positions of one channel) ----
 
-__global__ void k_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
-                           int layer, int n_ctx, int8_t* kc, int8_t* vc) {
-    int r = blockIdx.x;
+// One block per (32-row group, 64 channels): 8 threads per row, 8 channels each. Every byte
+// lands in its own 32-byte sector of vc (one position of a channel row), so the stores are
+// spread over all SMs instead of the few CTAs of the QKV GEMM that hold the v columns.
+constexpr int VS_CH = 64;
+__global__ void __launch_bounds__(256) k_v_scatter(const RowInfo* rows, int R, const int8_t* vstage, int ldv, int d,
+                                                   int H, int hd, int L, int layer, int n_ctx, int8_t* vc) {
+    const int r0 = blockIdx.x * 32, lane = threadIdx.x & 31;
+    // Every warp reads the group's rows itself (no block barrier needed).
+    if (vt_run_warp(rows, r0, R, n_ctx, lane)) return;
+    const int r = r0 + (threadIdx.x >> 3);
     if (r >= R) return;
-    uint32_t slot = rows[r].slot, pos = rows[r].pos;
-    for (int j = threadIdx.x; j < d; j += blockDim.x) {
-        int h = j / hd, c = j - h * hd;
-        size_t head = ((size_t)slot * L + layer) * H + h;
-        kc[(head * n_ctx + pos) * hd + c] = qkv[(size_t)r * ldq + d + j];
-        vc[(head * hd + c) * n_ctx + pos] = qkv[(size_t)r * ldq + 2 * d + j];
+    const RowInfo ri = rows[r];
+    const int c0 = blockIdx.y * VS_CH + (threadIdx.x & 7) * 8;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        const int j = c0 + k;
+        if (j < d) {
+            const int h = j / hd, c = j - h * hd;
+            const size_t head = ((size_t)ri.slot * L + layer) * H + h;
+            vc[(head * hd + c) * n_ctx + ri.pos] = vstage[(size_t)r * ldv + j];
+        }
     }
 }
 
@@ -1044,10 +1055,11 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
     k_gemm_simple<<<grid, 256, 0, st>>>(mode, A, lda, R, W, e);
 }
 
-void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
-                     int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st) {
+void launch_v_scatter(const RowInfo* rows, int R, const int8_t* vstage, int ldv, int d, int H, int hd, int L,
+                      int layer, int n_ctx, int8_t* vc, cudaStream_t st) {
     if (R <= 0) return;
-    k_kv_store<<<R, 256, 0, st>>>(rows, R, qkv, ldq, d, H, hd, L, layer, n_ctx, kc, vc);
+    dim3 grid((R + 31) / 32, (d + VS_CH - 1) / VS_CH);
+    k_v_scatter<<<grid, 256, 0, st>>>(rows, R, vstage, ldv, d, H, hd, L, layer, n_ctx, vc);
 }
 
 void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, const int8_t* qkv, int ldq,

@@ -51,8 +51,20 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
                     const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2 = nullptr);
 
-void launch_kv_store(const RowInfo* rows, int R, const int8_t* qkv, int ldq, int d, int H, int hd, int L,
-                     int layer, int n_ctx, int8_t* kc, int8_t* vc, cudaStream_t st);
+#ifdef __CUDACC__
+// vt_run_host for the warp whose lane l holds row r0 + l (warp-uniform result).
+__device__ __forceinline__ bool vt_run_warp(const RowInfo* rows, int r0, int R, int n_ctx, int lane) {
+    if (r0 + 31 >= R || (n_ctx & 15) != 0) return false;
+    const RowInfo a0 = rows[r0], me = rows[r0 + lane];
+    const bool mine = me.slot == a0.slot && me.pos == a0.pos + (uint32_t)lane;
+    return __all_sync(0xffffffffu, mine) && (a0.pos & 15) == 0;
+}
+#endif
+
+// The v of the rows in 32-row groups that are not vt_run, from the QKV epilogue's row-major
+// staging (stride ldv) into the transposed values cache of one layer.
+void launch_v_scatter(const RowInfo* rows, int R, const int8_t* vstage, int ldv, int d, int H, int hd, int L,
+                      int layer, int n_ctx, int8_t* vc, cudaStream_t st);
 
 // Attention of the rows `rowlist[0..n)` (all R rows when rowlist is null) on CUDA cores: the
 // decode path and the rows that are not in a prefill group.

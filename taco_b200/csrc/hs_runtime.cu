@@ -211,6 +211,7 @@ struct hs_batch {
     AttnGroup* h_groups = nullptr;   // pinned
     int* h_rowlist = nullptr;        // pinned
     int n_groups = 0, n_rowlist = 0;
+    bool v_scatter = false;  // some 32-row group of the pass is not a transposed v run
     uint64_t bytes = 0;
     // Per-op device time (CUDA events on the batch stream) when profiling is on.
     bool profiling = false;
@@ -395,7 +396,18 @@ int forward(hs_batch* b, int R) {
         e.hd = c.hd;
         e.n_ctx = c.n_ctx;
         e.d = c.d;
+        // On tensor cores the v of rows outside transposed runs (decode rows, ragged groups) is
+        // staged row-major in the attention output buffer, free until attention writes it, and
+        // placed by the scatter kernel over all SMs.
+        if (m->use_tc) {
+            e.vstage = b->att;
+            e.ldv = c.Dp;
+        }
         gemm(OP_GEMM_QKV, EPI_QKV, b->a, c.Dp, &b->tm_a, qkv, e, nullptr);
+        if (m->use_tc && b->v_scatter) {
+            ProfScope p(b, OP_KV, 0);
+            launch_v_scatter(b->d_rows, R, b->att, c.Dp, c.d, c.H, c.hd, c.L, l, c.n_ctx, b->vc, st);
+        }
         {
             ProfScope p(b, OP_ATTN, attn_ops);
             launch_attention_tc(&b->tm_q, &b->tm_k, &b->tm_v, b->d_groups, b->n_groups, c.L, l, c.H, c.n_ctx,
@@ -600,6 +612,9 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         }
         CK(cudaMemcpyAsync(b->d_rows, b->h_rows, sizeof(RowInfo) * R, cudaMemcpyHostToDevice, b->stream));
         plan_groups(b, R);
+        b->v_scatter = false;
+        for (int r0 = 0; r0 < R && !b->v_scatter; r0 += 32)
+            b->v_scatter = !vt_run_host(b->h_rows, r0, R, b->model->c.n_ctx);
         if (b->n_groups) {
             CK(cudaMemcpyAsync(b->d_groups, b->h_groups, sizeof(AttnGroup) * b->n_groups, cudaMemcpyHostToDevice,
                                b->stream));
