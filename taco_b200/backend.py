@@ -8,6 +8,7 @@ There is no CPU fallback: if the library or a GPU is missing, every call raises.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -124,9 +125,14 @@ class CudaDevice:
         _check(lib().hs_open(ordinal, ctypes.byref(h)))
         self.h = h
         self.ordinal = ordinal
+        self._children = weakref.WeakSet()  # the models loaded on this device
 
     def close(self):
+        """Frees the device after its models (and their batches), the order in which the
+        reference's borrows end (a model borrows its device, a batch its model)."""
         if getattr(self, "h", None):
+            for c in list(self._children):
+                c.close()
             lib().hs_dev_free(self.h)
             self.h = None
 
@@ -217,10 +223,14 @@ class CudaModel:
     """crates/hardshell-cuda/src/model.rs CudaModel: a validated .hsm model on one device."""
 
     def __init__(self, device: CudaDevice, data: bytes):
+        if not device.h:
+            raise HardShellError(HS_BAD_ARGUMENT, "the device is closed")
         self.device = device
         h = ctypes.c_void_p()
         _check(lib().hs_model_load(device.h, bytes(data), len(data), ctypes.byref(h)))
         self.h = h
+        self._children = weakref.WeakSet()  # the batches of this model
+        device._children.add(self)
         mi = ModelInfo()
         _check(lib().hs_model_get_info(self.h, ctypes.byref(mi)))
         self.info = Info(mi.n_layer, mi.n_head, mi.d_model, mi.d_ff, mi.vocab, mi.n_ctx, mi.eot_token, mi.version,
@@ -228,6 +238,8 @@ class CudaModel:
 
     def close(self):
         if getattr(self, "h", None):
+            for c in list(self._children):
+                c.close()
             lib().hs_model_free(self.h)
             self.h = None
 
@@ -254,10 +266,13 @@ class CudaBatch:
     """crates/hardshell-cuda/src/batch.rs CudaBatch: `slots` sessions that run together."""
 
     def __init__(self, model: CudaModel, slots: int, max_rows: int):
+        if not model.h:
+            raise HardShellError(HS_BAD_ARGUMENT, "the model is closed")
         self.model = model
         h = ctypes.c_void_p()
         _check(lib().hs_batch_new(model.h, slots, max_rows, ctypes.byref(h)))
         self.h = h
+        model._children.add(self)
         self.slots = slots
         self.max_rows = max(2, max_rows)
 

@@ -175,7 +175,7 @@ struct hs_model {
     int logits_head = 0;  // the last index j with logits_exp[j] == logits_exp[0]
 
     ~hs_model() {
-        if (dev) cudaSetDevice(dev->ordinal);
+        if (dev && cudaSetDevice(dev->ordinal) != cudaSuccess) cudaGetLastError();
         for (void* p : owned) cudaFree(p);
     }
 };
@@ -232,7 +232,7 @@ struct hs_batch {
     alignas(128) CUtensorMap tm_g_lo;   // version 2: the lo plane of the GELU output
 
     ~hs_batch() {
-        if (model) cudaSetDevice(model->dev->ordinal);
+        if (model && cudaSetDevice(model->dev->ordinal) != cudaSuccess) cudaGetLastError();
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         if (stream) cudaStreamDestroy(stream);
         for (void* p : owned) cudaFree(p);
@@ -590,6 +590,10 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     }
     int rc = set_device(m->dev);
     if (rc) return rc;
+    // An earlier failed API call of this thread (already reported to its caller) leaves its code
+    // behind; clear it, so that the launch checks below report only this call's own errors. A
+    // device fault is sticky and still shows.
+    cudaGetLastError();
     if (wout && !b->weights) {
         // The weights buffer of run_weights: made on the first use (vocab u64 per row).
         if ((rc = dalloc(&b->weights, (size_t)b->Rcap * c.V, b->owned))) return rc;
@@ -729,7 +733,7 @@ int hs_open(int ordinal, hs_dev** out) {
 
 void hs_dev_free(hs_dev* d) {
     if (!d) return;
-    cudaSetDevice(d->ordinal);
+    if (cudaSetDevice(d->ordinal) != cudaSuccess) cudaGetLastError();
     if (d->d_err) cudaFree(d->d_err);
     delete d;
 }
