@@ -79,16 +79,18 @@ __device__ __forceinline__ int64_t score_of(int32_t dot, int32_t sm, int ss, boo
 }
 
 // The table index min(max - score, last). NARROW (21 <= ss <= 62): |dot| <= 64 * 2^14 = 2^20 and
-// |sm| <= 2^31, so |score| < 2^30 (no clamp at 2^40) and the distance fits in 32 bits.
+// |sm| <= 2^31, so |score| < 2^30 (no clamp at 2^40) and the distance fits in 32 bits. The
+// distance is never negative (max is the row's largest score); the unsigned comparison keeps the
+// index inside the table for any input all the same, at no cost.
 template <bool NARROW>
 __device__ __forceinline__ int32_t dist_of(int64_t M, int32_t dot, int32_t sm, int ss, bool fast, int64_t h,
                                            int32_t last) {
     if (NARROW) {
         int32_t dd = (int32_t)M - (int32_t)(((int64_t)dot * (int64_t)sm + h) >> ss);
-        return dd < last ? dd : last;
+        return (uint32_t)dd < (uint32_t)last ? dd : last;
     } else {
         int64_t dd = M - score_of(dot, sm, ss, fast, h);
-        return (int32_t)(dd < (int64_t)last ? dd : (int64_t)last);
+        return (int32_t)((uint64_t)dd < (uint64_t)last ? dd : (int64_t)last);
     }
 }
 
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                 if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
                 else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
                 const int32_t dd = (int32_t)M - score;
-                return dd < last ? dd : last;
+                return (uint32_t)dd < (uint32_t)last ? dd : last;
             } else {
                 return dist_of<false>(M, dot, sm, ss, fast, hround, last);
             }
@@ -568,7 +570,7 @@ __global__ void __launch_bounds__(32 * DEC_WARPS, 5) k_attention_dec(const RowIn
             if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
             else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
             const int32_t dd = (int32_t)M - score;
-            return dd < last ? dd : last;
+            return (uint32_t)dd < (uint32_t)last ? dd : last;
         } else {
             return dist_of<false>(M, dot, sm, ss, fast, hround, last);
         }

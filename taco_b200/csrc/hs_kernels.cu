@@ -817,10 +817,29 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     if (all_zero) {
         sum_f = (uint64_t)V * f_flat;
     } else {
+        // floor(t * spare / W) for a table entry t <= table[0] <= W (so the quotient is at most
+        // spare < 2^32): t * (spare / W) in double, the reciprocal ratio taken once per row, is
+        // within 2^-19 of the quotient, so its floor is q or q - 1; the remainder t * spare - q W
+        // computed mod 2^64 is exact because |t * spare - q W| < 2 W <= 2^57 (t <= 2^40, V <= 2^16),
+        // and at most a few exact steps put q right.
+        const double ratio = (double)spare / (double)W;
+        auto fdiv = [&](uint64_t t) -> uint64_t {
+            uint64_t q = (uint64_t)((double)t * ratio);
+            int64_t rm = (int64_t)(t * spare - q * W);
+            for (int k = 0; k < 4 && rm < 0; k++) {
+                q -= 1;
+                rm += (int64_t)W;
+            }
+            for (int k = 0; k < 4 && rm >= (int64_t)W; k++) {
+                q += 1;
+                rm -= (int64_t)W;
+            }
+            return q;
+        };
         for (int j = threadIdx.x; j <= dmax; j += CODER_THREADS) {
             const uint32_t c = j == last ? (uint32_t)n_last : F[j];
             if (c) {
-                const uint32_t f = (uint32_t)(1 + udiv128_small((u128)table[j] * spare, W));
+                const uint32_t f = (uint32_t)(1 + fdiv(table[j]));
                 F[j] = f;
                 sum_f += (uint64_t)c * f;
             }
