@@ -300,29 +300,41 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             blocks++;
         };
+        // The column parameters of a tile, staged in shared memory (double-buffered by the
+        // accumulator parity). Each thread's loads for the next tile are issued before the
+        // current tile's work and written to its buffer at the top of the next iteration, so the
+        // global load latency is not paid between tiles. WIDE: the raw bias (the epilogue
+        // rescales in 128 bits) and the weight row sums.
+        int32_t pf_m = 0, pf_b = 0;
+        int64_t pf_w = 0;
+        auto fetch_params = [&](int t) {
+            const int n = (t / MT) * TN + et;
+            pf_m = 0;
+            pf_b = 0;
+            pf_w = 0;
+            if (et < TN && t < tiles && n < e.N) {
+                pf_m = e.m[n];
+                if (MODE != EPI_LOGITS && MODE != EPI_RAW) pf_b = e.b[n];
+                if (WIDE) pf_w = e.wsum[n];
+            }
+        };
+        fetch_params(blockIdx.x);
         int i = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
             const int mt = t % MT, nt = t / MT;
             const int acc = i & 1;
             const uint32_t aphase = (i >> 1) & 1;
             const int col0 = nt * TN;
-            // Stage this tile's column parameters (double-buffered by the accumulator parity).
-            // WIDE: the raw bias (the epilogue rescales in 128 bits) and the weight row sums.
+            // Buffer `acc` was last read for tile i - 2, which every epilogue warp finished before
+            // the barrier of tile i - 1.
             if (et < TN) {
-                int n = col0 + et;
-                int32_t m = 0;
-                int64_t c = 0, w = 0;
-                if (n < e.N) {
-                    m = e.m[n];
-                    int64_t b = (MODE == EPI_LOGITS || MODE == EPI_RAW) ? 0 : (int64_t)e.b[n];
-                    c = (fast && !WIDE) ? b * (int64_t)m + hround : b;
-                    if (WIDE) w = e.wsum[n];
-                }
-                s_m[acc * BN + et] = m;
-                s_c[acc * BN + et] = c;
-                if (WIDE) s_w[acc * BN + et] = w;
+                const int64_t b = pf_b;
+                s_m[acc * BN + et] = pf_m;
+                s_c[acc * BN + et] = (fast && !WIDE) ? b * (int64_t)pf_m + hround : b;
+                if (WIDE) s_w[acc * BN + et] = pf_w;
             }
             named_bar(1, EPI_THREADS);
+            fetch_params(t + gridDim.x);
             // On a timeout the error word is set and every later wait returns at once; the warps keep
             // taking part in the named barriers, so no thread can wait on a barrier forever.
             mbar_wait(&bars->tfull[acc], aphase, err, 4);
