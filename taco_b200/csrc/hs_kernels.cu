@@ -747,26 +747,42 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         return o < (int64_t)last ? (int32_t)o : last;
     };
     // Pass 1: the distance counts (and, for a decode query, the largest symbol: an encode query
-    // finds out where it lies in its prefix pass instead).
+    // finds out where it lies in its prefix pass instead). Two distances at a time in the
+    // halfwords of a word: min(off + d, last) is a saturating halfword add, which stops at
+    // 65535 > last, then a halfword min, both exact. The clamped ones count in F[last].
     const RowInfo q = rows[r];
-    uint32_t nlast = 0;
     int best = V;
+    const uint32_t last2 = (uint32_t)last * 0x10001u;
+    const uint32_t head2 = (uint32_t)(head < last ? head : last) * 0x10001u;
     // Groups of 8 symbols, CODER_UNROLL groups per thread and round so that several 16-byte loads
     // are in flight before the counting.
     auto count_group = [&](int v0, uint4 raw, auto track) {
         const int32_t off = tile_off(v0);
         if (off == last) {
-            nlast += 8;
+            atomicAdd(&F[last], 8u);
+            if constexpr (decltype(track)::value) best = head >= last && v0 < best ? v0 : best;
             return;
         }
+        const uint32_t off2 = (uint32_t)off * 0x10001u;
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t near[4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            int32_t dd = off + (int32_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
-            dd = dd < last ? dd : last;
-            if (dd < last) atomicAdd(&F[dd], 1u);
-            else nlast++;
-            if constexpr (decltype(track)::value) best = dd <= head && v0 + i < best ? v0 + i : best;
+        for (int k = 0; k < 4; k++) {
+            const uint32_t p = __vminu2(__vaddus2(u[k], off2), last2);
+            atomicAdd(&F[p & 0xFFFFu], 1u);
+            atomicAdd(&F[p >> 16], 1u);
+            if constexpr (decltype(track)::value) near[k] = __vcmpleu2(p, head2);
+        }
+        if constexpr (decltype(track)::value) {
+            if ((near[0] | near[1] | near[2] | near[3]) != 0) {
+                int first = 8;
+#pragma unroll
+                for (int k = 3; k >= 0; k--) {
+                    if (near[k] >> 16) first = 2 * k + 1;
+                    if (near[k] & 0xFFFFu) first = 2 * k;
+                }
+                best = v0 + first < best ? v0 + first : best;
+            }
         }
     };
     constexpr int CODER_UNROLL = 4;
@@ -791,12 +807,12 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         for (int v = v0; v < V; v++) {
             int32_t dd = off + (int32_t)dr[v];
             dd = dd < last ? dd : last;
-            if (dd < last) atomicAdd(&F[dd], 1u);
-            else nlast++;
+            atomicAdd(&F[dd], 1u);
             best = dd <= head && v < best ? v : best;
         }
     }
-    const uint64_t n_last = block_sum64(nlast, redu);  // (its barriers also publish the counts)
+    __syncthreads();  // the counts are complete
+    const uint64_t n_last = F[last];
     // The largest distance that occurs: the highest counted bin.
     int32_t dmax = n_last ? last : 0;
     for (int j = threadIdx.x; j < last; j += CODER_THREADS)
@@ -860,19 +876,19 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
         uint64_t pre = 0;
         bool below = false;
         auto group_sum = [&](int v0, uint4 raw) {
-            const int32_t off = tile_off(v0);
+            const uint32_t off2 = (uint32_t)tile_off(v0) * 0x10001u;
             const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
             uint32_t gsum = 0;  // 8 frequencies: at most total - (V - 8) < 2^32 for V > 8
-            int32_t dmin = last;
+            uint32_t dm = last2;
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                int32_t dd = off + (int32_t)((u[i >> 1] >> (16 * (i & 1))) & 0xFFFF);
-                dd = dd < last ? dd : last;
-                dmin = dd < dmin ? dd : dmin;
-                gsum += all_zero ? f_flat : F[dd];
+            for (int k = 0; k < 4; k++) {
+                const uint32_t p = __vminu2(__vaddus2(u[k], off2), last2);  // as in pass 1
+                dm = __vminu2(dm, p);
+                gsum += F[p & 0xFFFFu] + F[p >> 16];
             }
-            pre += gsum;
-            below |= dmin <= head;
+            pre += all_zero ? 8ull * f_flat : gsum;
+            const uint32_t dmin = min(dm & 0xFFFFu, dm >> 16);
+            below |= dmin <= (uint32_t)head;
         };
         int gj = threadIdx.x;
         for (; gj + (CODER_UNROLL - 1) * CODER_THREADS < gs; gj += CODER_UNROLL * CODER_THREADS) {
