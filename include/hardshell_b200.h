@@ -102,6 +102,24 @@ int hs_batch_run_coded(hs_batch* batch, const uint32_t* slots, const uint32_t* t
 int hs_batch_run_weights(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
                          uint64_t* out);
 
+/* The unfold of n coded blocks with the range decoder on the device. It replaces the host loop
+ * of crates/taco/src/gpu_unfold.rs:100-160 (codec.rs BlockDecoder over run_coded with Decode
+ * queries, one host round trip per token) for the coded blocks of a job. Block i is reset into
+ * slot slots[i] (distinct slots), takes EOT as its first input and each decoded symbol as its
+ * next one, and decodes counts[i] tokens from its range-coded bytes
+ * payload[offsets[i] .. offsets[i] + lengths[i]) (the bytes after the block's varint count),
+ * each with the coder op at freq_bits (taco-coder decoder.rs target / decode_interval).
+ * tokens_out[token_offsets[i] + j] receives its j-th symbol (the caller maps tokens to bytes
+ * and checks the block's length, as BlockDecoder::finish does). status[i] (may be NULL) is 0, or
+ * 1 if an interval did not hold its target (the reference's TargetNotInInterval: the block is
+ * corrupt; its tokens mean nothing). At most max_rows blocks per call. No counterpart call in the
+ * reference: it is the GPU range coder of its "next" list. On an error the positions of the
+ * call's slots are unspecified: reset them before reuse. */
+int hs_batch_decode_blocks(hs_batch* batch, uint32_t n, const uint32_t* slots, const uint8_t* payload,
+                           uint64_t payload_len, const uint64_t* offsets, const uint64_t* lengths,
+                           const uint32_t* counts, uint32_t freq_bits, uint32_t* tokens_out, uint64_t tokens_cap,
+                           const uint64_t* token_offsets, uint32_t* status);
+
 /* The message of the last error of the calling thread (NUL-terminated, cut to `cap`). */
 int hs_last_error(char* buf, size_t cap);
 

@@ -89,6 +89,7 @@ def lib() -> ctypes.CDLL:
     L.hs_batch_gpu_bytes.restype = u64
     L.hs_batch_run_coded.argtypes = [vp, vp, vp, vp, vp, u32, u32, vp]
     L.hs_batch_run_weights.argtypes = [vp, vp, vp, u32, vp]
+    L.hs_batch_decode_blocks.argtypes = [vp, u32, vp, vp, ctypes.c_uint64, vp, vp, vp, u32, vp, ctypes.c_uint64, vp, vp]
     L.hs_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_act_noalloc.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
@@ -329,3 +330,28 @@ class CudaBatch:
         out = np.zeros((s.size, self.model.info.vocab), dtype=np.uint64)
         _check(lib().hs_batch_run_weights(self.h, _p(s), _p(t), s.size, _p(out)))
         return out
+
+    def decode_blocks(self, slots, payloads, counts, freq_bits: int = 32):
+        """hs_batch_decode_blocks: block i (the range-coded bytes payloads[i], counts[i] tokens) is
+        decoded in slot slots[i] with the decoder on the device. Returns (tokens per block, status
+        per block: 0, or 1 if an interval did not hold its target)."""
+        s = np.ascontiguousarray(slots, dtype=np.uint32)
+        cnt = np.ascontiguousarray(counts, dtype=np.uint32)
+        n = s.size
+        if len(payloads) != n or cnt.size != n:
+            raise HardShellError(HS_LENGTH_MISMATCH, "slots, payloads and counts differ in length")
+        lens = np.array([len(p) for p in payloads], dtype=np.uint64)
+        offs = np.zeros(n, dtype=np.uint64)
+        if n:
+            offs[1:] = np.cumsum(lens)[:-1]
+        buf = np.frombuffer(b"".join(bytes(p) for p in payloads) or b"\0", dtype=np.uint8).copy()
+        toff = np.zeros(n, dtype=np.uint64)
+        if n:
+            toff[1:] = np.cumsum(cnt.astype(np.uint64))[:-1]
+        total = int(cnt.astype(np.uint64).sum())
+        out = np.zeros(max(total, 1), dtype=np.uint32)
+        status = np.zeros(max(n, 1), dtype=np.uint32)
+        _check(lib().hs_batch_decode_blocks(self.h, n, _p(s), _p(buf), int(lens.sum()), _p(offs), _p(lens), _p(cnt),
+                                            freq_bits, _p(out), total, _p(toff), _p(status)))
+        toks = [out[int(toff[i]):int(toff[i]) + int(cnt[i])].copy() for i in range(n)]
+        return toks, status[:n].copy()

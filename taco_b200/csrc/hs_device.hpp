@@ -59,6 +59,14 @@ struct RowInfo {
     uint64_t value;
 };
 
+// The range decoder state of one coded block on the device (crates/taco-coder/src/decoder.rs
+// Decoder: code, range, the next byte `pos` of its input payload[base .. base + len)), and
+// whether an interval failed to hold its target.
+struct DecState {
+    uint64_t code, range, base, len, pos;
+    uint32_t failed, pad;
+};
+
 // A run of up to 128 rows of one slot at consecutive positions pos0 .. pos0 + count - 1, whose
 // rows are first_row .. first_row + count - 1 of the pass (the prefill attention unit).
 struct AttnGroup {

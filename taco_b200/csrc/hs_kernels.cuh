@@ -61,6 +61,20 @@ __device__ __forceinline__ bool vt_run_warp(const RowInfo* rows, int r0, int R, 
 }
 #endif
 
+// The range decoder of the batched unfold (hs_decode.cu): the states of n blocks, one step's rows
+// (the live blocks are the first R), the consumption of one step's intervals, the targets of a
+// host-run step, and the failed flags.
+void launch_dec_init(DecState* st, const uint8_t* payload, const uint64_t* offsets, const uint64_t* lengths,
+                     uint32_t* prev, uint32_t eot, int n, cudaStream_t s);
+void launch_dec_begin(const DecState* st, int R, const uint32_t* slot_of, const uint32_t* pos_of,
+                      uint32_t steps_since, const uint32_t* prev, uint32_t bits, RowInfo* rows, cudaStream_t s);
+void launch_dec_end(DecState* st, int R, const uint64_t* intervals, uint32_t bits, uint32_t V, const uint8_t* payload,
+                    uint32_t* prev, uint32_t* out, const uint64_t* out_off, uint32_t step, cudaStream_t s);
+void launch_dec_targets(const DecState* st, int R, uint32_t bits, uint64_t* targets, cudaStream_t s);
+void launch_dec_gather(const uint32_t* out, const uint64_t* out_off, const uint32_t* counts, int L, uint32_t s0,
+                       uint32_t s1, uint32_t* dst, cudaStream_t s);
+void launch_dec_status(const DecState* st, int n, uint32_t* status, cudaStream_t s);
+
 // The v of the rows in 32-row groups that are not vt_run, from the QKV epilogue's row-major
 // staging (stride ldv) into the transposed values cache of one layer.
 void launch_v_scatter(const RowInfo* rows, int R, const int8_t* vstage, int ldv, int d, int H, int hd, int L,

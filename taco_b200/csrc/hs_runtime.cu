@@ -248,9 +248,9 @@ namespace {
 // The ops of one pass, for the profile (the reference's CudaBatch::profile op names).
 // OP_PASS spans a whole pass (first kernel to the coder, gaps included); it is not a launch.
 enum Op { OP_EMBED, OP_LN, OP_GEMM_QKV, OP_KV, OP_ATTN, OP_GEMM_PROJ, OP_GEMM_FC, OP_GEMM_MLP, OP_GEMM_LOGITS,
-          OP_CODER, OP_PASS, OP_COUNT };
+          OP_CODER, OP_DECODER, OP_PASS, OP_COUNT };
 const char* OP_NAMES[OP_COUNT] = {"embed", "layernorm", "gemm_qkv", "kv_store", "attention", "gemm_proj",
-                                  "gemm_fc", "gemm_mlp", "gemm_logits", "coder", "pass"};
+                                  "gemm_fc", "gemm_mlp", "gemm_logits", "coder", "decoder", "pass"};
 
 // Kernel launches of this process (the bench reports the launches of its timed region).
 unsigned long long g_launches = 0;
@@ -675,6 +675,197 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     return HS_OK;
 }
 
+// hs_batch_decode_blocks: n coded blocks unfolded at once, the decoder of each on the device
+// (hs_decode.cu). Block i runs in slot slots[i] from position 0, takes EOT as its first input
+// and every decoded symbol as the next one (crates/taco/src/gpu_unfold.rs:100-160). The blocks
+// are ordered by token count, longest first, so the blocks still running at a step are a prefix
+// of that order. A step where no running block needs a context restart is enqueued without a
+// host wait: the rows come from the decoder states (k_dec_begin), then the forward pass, the
+// coder op and the interval check (k_dec_end). A step with a restart takes the host path of
+// run_coded with the targets read back, after the histories of the slots are brought up to date.
+int decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t* payload, uint64_t payload_len,
+                  const uint64_t* offsets, const uint64_t* lengths, const uint32_t* counts, uint32_t bits,
+                  uint32_t* tokens_out, uint64_t tokens_cap, const uint64_t* token_offsets, uint32_t* status) {
+    hs_model* m = b->model;
+    const ModelConsts& c = m->c;
+    if (n == 0) return HS_OK;
+    if (bits == 0 || bits > 32 || (uint64_t)c.V > (1ULL << bits))
+        return fail(HS_UNSUPPORTED, "freq_bits must be in 1..=32 and 2^freq_bits >= vocab");
+    if (n > (uint32_t)b->max_rows) return fail(HS_UNSUPPORTED, "more blocks than the batch's max_rows");
+    std::vector<char> seen(b->slots, 0);
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        if (slots[i] >= (uint32_t)b->slots)
+            return fail(HS_BAD_SLOT, "slot " + std::to_string(slots[i]) + " is not valid in a batch of " +
+                                         std::to_string(b->slots) + " slots");
+        if (seen[slots[i]]) return fail(HS_BAD_ARGUMENT, "two blocks in one slot");
+        seen[slots[i]] = 1;
+        if (offsets[i] > payload_len || lengths[i] > payload_len - offsets[i])
+            return fail(HS_LENGTH_MISMATCH, "a block lies outside the payload");
+        if (token_offsets[i] > tokens_cap || counts[i] > tokens_cap - token_offsets[i])
+            return fail(HS_LENGTH_MISMATCH, "a block's tokens lie outside the output");
+        total += counts[i];
+    }
+    int rc = set_device(m->dev);
+    if (rc) return rc;
+    cudaGetLastError();
+    cudaStream_t st = b->stream;
+    const int n_ctx = c.n_ctx;
+    std::vector<uint32_t> order(n);
+    for (uint32_t i = 0; i < n; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t x, uint32_t y) { return counts[x] > counts[y]; });
+    // Per-call device buffers, in block order (`order`).
+    std::vector<void*> owned;
+    struct Guard {
+        std::vector<void*>& o;
+        ~Guard() {
+            for (void* p : o) cudaFree(p);
+        }
+    } guard{owned};
+    std::vector<uint64_t> h_off(n), h_len(n), h_oo(n);
+    std::vector<uint32_t> h_cnt(n), h_slot(n), h_pos(n, 0);
+    uint64_t acc = 0;
+    for (uint32_t k = 0; k < n; k++) {
+        const uint32_t i = order[k];
+        h_off[k] = offsets[i];
+        h_len[k] = lengths[i];
+        h_cnt[k] = counts[i];
+        h_slot[k] = slots[i];
+        h_oo[k] = acc;
+        acc += counts[i];
+    }
+    uint8_t* d_payload = nullptr;
+    uint64_t *d_off = nullptr, *d_len = nullptr, *d_oo = nullptr, *d_tg = nullptr, *d_iv = nullptr;
+    uint32_t *d_cnt = nullptr, *d_slot = nullptr, *d_pos = nullptr, *d_prev = nullptr, *d_out = nullptr,
+             *d_gather = nullptr, *d_status = nullptr;
+    DecState* d_st = nullptr;
+    if ((rc = upload(&d_payload, payload, payload_len, owned)) || (rc = upload(&d_off, h_off.data(), n, owned)) ||
+        (rc = upload(&d_len, h_len.data(), n, owned)) || (rc = upload(&d_oo, h_oo.data(), n, owned)) ||
+        (rc = upload(&d_cnt, h_cnt.data(), n, owned)) || (rc = upload(&d_slot, h_slot.data(), n, owned)) ||
+        (rc = dalloc(&d_pos, n, owned)) || (rc = dalloc(&d_prev, n, owned)) || (rc = dalloc(&d_out, total, owned)) ||
+        (rc = dalloc(&d_tg, n, owned)) || (rc = dalloc(&d_iv, 3 * (size_t)n, owned)) ||
+        (rc = dalloc(&d_status, n, owned)) || (rc = dalloc(&d_st, n, owned)))
+        return rc;
+    launch_dec_init(d_st, d_payload, d_off, d_len, d_prev, m->eot, (int)n, st);
+    for (uint32_t k = 0; k < n; k++) {
+        b->pos[h_slot[k]] = 0;
+        std::fill(b->hist.begin() + (size_t)h_slot[k] * n_ctx, b->hist.begin() + (size_t)(h_slot[k] + 1) * n_ctx, 0u);
+    }
+    // The steps since the last host sync run at positions h_pos[k] + (step - s_sync); sync_hist
+    // reads their symbols back and writes the inputs of those rows into the histories.
+    uint32_t s_sync = 0;
+    std::vector<uint32_t> last_sym(n, m->eot);  // the input of the block's next row
+    std::vector<uint32_t> h_gather;
+    auto live_at = [&](uint32_t step) {
+        uint32_t L = 0;
+        while (L < n && h_cnt[L] > step) L++;
+        return L;
+    };
+    auto sync_hist = [&](uint32_t step) -> int {
+        if (step <= s_sync) return HS_OK;
+        const uint32_t L = live_at(s_sync), w = step - s_sync;
+        if (L == 0) return HS_OK;
+        if (!d_gather || h_gather.size() < (size_t)L * w) {
+            h_gather.assign((size_t)L * w, 0);
+            int r2 = dalloc(&d_gather, (size_t)L * w, owned);
+            if (r2) return r2;
+        }
+        launch_dec_gather(d_out, d_oo, d_cnt, (int)L, s_sync, step, d_gather, st);
+        CK(cudaMemcpyAsync(h_gather.data(), d_gather, sizeof(uint32_t) * L * w, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        for (uint32_t k = 0; k < L; k++) {
+            uint32_t* h = &b->hist[(size_t)h_slot[k] * n_ctx];
+            const uint32_t e = std::min(step, h_cnt[k]);
+            for (uint32_t s2 = s_sync; s2 < e; s2++) {
+                h[h_pos[k] + (s2 - s_sync)] = last_sym[k];
+                last_sym[k] = h_gather[(size_t)k * w + (s2 - s_sync)];
+            }
+            b->pos[h_slot[k]] = (int)(h_pos[k] + (e - s_sync));
+            h_pos[k] = (uint32_t)b->pos[h_slot[k]];
+        }
+        s_sync = step;
+        return HS_OK;
+    };
+    const uint32_t S = h_cnt[0];
+    bool upload_pos = true;
+    for (uint32_t step = 0; step < S; step++) {
+        const uint32_t L = live_at(step);
+        bool restart = false;
+        for (uint32_t k = 0; k < L && !restart; k++) restart = h_pos[k] + (step - s_sync) >= (uint32_t)n_ctx;
+        if (!restart) {
+            if (upload_pos) {
+                CK(cudaMemcpyAsync(d_pos, h_pos.data(), sizeof(uint32_t) * n, cudaMemcpyHostToDevice, st));
+                upload_pos = false;
+            }
+            {
+                ProfScope p(b, OP_DECODER, 0);
+                launch_dec_begin(d_st, (int)L, d_slot, d_pos, step - s_sync, d_prev, bits, b->d_rows, st);
+            }
+            b->n_groups = 0;
+            b->n_rowlist = 0;
+            b->v_scatter = true;
+            for (uint32_t k = 0; k < L; k++) b->h_rows[k].pos = h_pos[k] + (step - s_sync);  // host statistics only
+            {
+                std::unique_ptr<ProfScope> pass_scope(new ProfScope(b, OP_PASS, (uint64_t)L));
+                rc = forward(b, (int)L);
+                if (rc) return rc;
+                ProfScope p(b, OP_CODER, 0);
+                launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, (int)L, c.V, m->logits_exp, m->logits_len,
+                             m->logits_head, bits, b->d_rows, b->intervals, st);
+            }
+            {
+                ProfScope p(b, OP_DECODER, 0);
+                launch_dec_end(d_st, (int)L, b->intervals, bits, (uint32_t)c.V, d_payload, d_prev, d_out, d_oo, step, st);
+            }
+            if (b->profiling) {
+                // Keep the event pool bounded: collect the profile of the enqueued steps now and then.
+                if ((step & 63) == 63) {
+                    if ((rc = check_device_error(b))) return rc;
+                    prof_collect(b);
+                }
+            }
+            continue;
+        }
+        // A restart step: bring the histories up to date, then run it through run_coded.
+        if ((rc = check_device_error(b)) || (rc = sync_hist(step))) return rc;
+        launch_dec_targets(d_st, (int)L, bits, d_tg, st);
+        std::vector<uint64_t> tg(L);
+        CK(cudaMemcpyAsync(tg.data(), d_tg, sizeof(uint64_t) * L, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        std::vector<uint32_t> in_slot(h_slot.begin(), h_slot.begin() + L), in_tok(last_sym.begin(), last_sym.begin() + L),
+            kinds(L, 1);
+        std::vector<hs_interval> ivs(L);
+        if ((rc = run(b, in_slot.data(), in_tok.data(), kinds.data(), tg.data(), L, bits, ivs.data(), nullptr)))
+            return rc;
+        std::vector<uint64_t> h_iv(3 * (size_t)L);
+        for (uint32_t k = 0; k < L; k++) {
+            h_iv[3 * k] = ivs[k].symbol;
+            h_iv[3 * k + 1] = ivs[k].start;
+            h_iv[3 * k + 2] = ivs[k].freq;
+            last_sym[k] = ivs[k].symbol;
+            h_pos[k] = (uint32_t)b->pos[h_slot[k]];
+        }
+        CK(cudaMemcpyAsync(d_iv, h_iv.data(), sizeof(uint64_t) * 3 * L, cudaMemcpyHostToDevice, st));
+        launch_dec_end(d_st, (int)L, d_iv, bits, (uint32_t)c.V, d_payload, d_prev, d_out, d_oo, step, st);
+        CK(cudaStreamSynchronize(st));  // the host copies of h_iv and h_pos stay valid until here
+        s_sync = step + 1;
+        upload_pos = true;
+    }
+    if ((rc = check_device_error(b)) || (rc = sync_hist(S))) return rc;
+    if (b->profiling) prof_collect(b);
+    std::vector<uint32_t> all(total), fl(n);
+    launch_dec_status(d_st, (int)n, d_status, st);
+    if (total) CK(cudaMemcpyAsync(all.data(), d_out, sizeof(uint32_t) * total, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(fl.data(), d_status, sizeof(uint32_t) * n, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    for (uint32_t k = 0; k < n; k++) {
+        const uint32_t i = order[k];
+        memcpy(tokens_out + token_offsets[i], all.data() + h_oo[k], sizeof(uint32_t) * counts[i]);
+        if (status) status[i] = fl[k];
+    }
+    return HS_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1003,6 +1194,17 @@ int hs_batch_run_coded(hs_batch* b, const uint32_t* slots, const uint32_t* token
                        const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out) {
     if (!b || (n && (!slots || !tokens || !kinds || !values || !out))) return fail(HS_BAD_ARGUMENT, "null argument");
     return run(b, slots, tokens, kinds, values, n, freq_bits, out, nullptr);
+}
+
+int hs_batch_decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t* payload,
+                           uint64_t payload_len, const uint64_t* offsets, const uint64_t* lengths,
+                           const uint32_t* counts, uint32_t freq_bits, uint32_t* tokens_out, uint64_t tokens_cap,
+                           const uint64_t* token_offsets, uint32_t* status) {
+    if (!b || (n && (!slots || !offsets || !lengths || !counts || !token_offsets || (!payload && payload_len) ||
+                     (!tokens_out && tokens_cap))))
+        return fail(HS_BAD_ARGUMENT, "null argument");
+    return decode_blocks(b, n, slots, payload, payload_len, offsets, lengths, counts, freq_bits, tokens_out, tokens_cap,
+                         token_offsets, status);
 }
 
 int hs_batch_run_weights(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, uint32_t n, uint64_t* out) {
