@@ -390,6 +390,7 @@ def main():
                                         "frac": round(tops / peak["tops"], 3) if peak else None}
         result["gemm_microbench"] = micro
         result["unfold"] = unfold_step(B, model, lens, eot, clock_note=None)
+        result["unfold_blocks"] = unfold_blocks(B, model)
     if rank == 0:
         if world == 1 and not args.no_cpu:
             threads = args.cpu_threads or os.cpu_count() or 1
@@ -434,6 +435,51 @@ def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, conte
             "kv_GB_per_s": kv_read / dev_s / 1e9,
             "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3),
             "kernels_ms_per_step": {k: round(v["ms"] / steps, 3) for k, v in prof.items() if v["launches"]}}
+
+
+def unfold_blocks(B, model, streams: int = 1024, tokens: int = 256) -> dict:
+    """configs[3] with the range decoder on the device: `streams` coded blocks of `tokens` tokens,
+    unfolded from position 0 by one hs_batch_decode_blocks call (no host round trip per token),
+    against the same rows driven step by step through run_coded with decode queries (one host
+    round trip per step, the structure of the reference's unfold loop; its targets here are
+    seeded, as a host decoder's would be). The payloads are seeded random bytes: the decoder turns
+    any input into symbols, and the work of a step does not depend on the bytes. Both arms are
+    timed by the wall clock around the C-ABI calls, the better of two runs each; the device time
+    of the decoder arm comes from a third, profiled call."""
+    rng = np.random.default_rng(79)
+    payloads = [rng.integers(0, 256, 4 * tokens, dtype=np.uint8).tobytes() for _ in range(streams)]
+    sl = np.arange(streams, dtype=np.uint32)
+    batch = B.CudaBatch(model, streams, 4096)
+    batch.decode_blocks(sl[:8], payloads[:8], [4] * 8, 32)  # warm-up
+    wall = float("inf")
+    for _ in range(2):  # the better of two calls, for each arm
+        t0 = time.perf_counter()
+        toks, status = batch.decode_blocks(sl, payloads, [tokens] * streams, 32)
+        wall = min(wall, time.perf_counter() - t0)
+    batch.set_profiling(True)
+    batch.decode_blocks(sl, payloads, [tokens] * streams, 32)
+    prof = batch.profile()
+    batch.set_profiling(False)
+    dev_ms = prof["pass"]["ms"] + prof.get("decoder", {"ms": 0.0})["ms"]
+    # The host loop over run_coded, from position 0 as well.
+    targets = rng.integers(0, 1 << 32, (tokens, streams), dtype=np.uint64)
+    kinds = np.ones(streams, np.uint32)
+    wall_host = float("inf")
+    for _ in range(2):
+        for s in range(streams):
+            batch.reset(s)
+        inp = np.full(streams, model.eot_token(), np.uint32)
+        t0 = time.perf_counter()
+        for j in range(tokens):
+            iv = batch.run_coded(sl, inp, kinds, targets[j], 32)
+            inp = iv["symbol"].astype(np.uint32)
+        wall_host = min(wall_host, time.perf_counter() - t0)
+    batch.close()
+    n = streams * tokens
+    return {"streams": streams, "tokens_per_block": tokens, "positions": f"0..{tokens - 1}",
+            "e2e_tokens_per_s": n / wall, "device_tokens_per_s": n / (dev_ms / 1e3),
+            "host_loop_e2e_tokens_per_s": n / wall_host, "failed_blocks": int(status.sum()),
+            "decoder_ms": round(prof.get("decoder", {"ms": 0.0})["ms"], 3)}
 
 
 if __name__ == "__main__":
