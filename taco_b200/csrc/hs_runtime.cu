@@ -204,12 +204,20 @@ struct hs_batch {
     int64_t* tmax = nullptr;
     uint64_t* intervals = nullptr;
     uint64_t* weights = nullptr;
-    RowInfo* h_rows = nullptr;       // pinned
-    uint64_t* h_intervals = nullptr;  // pinned
+    // The host copies of a pass (pinned, two halves: run() prepares the next pass in one half
+    // while the GPU works on the pass it uploaded from the other); the pointers below are the
+    // current half.
+    RowInfo* h_rows_base = nullptr;
+    uint64_t* h_intervals_base = nullptr;
+    AttnGroup* h_groups_base = nullptr;
+    int* h_rowlist_base = nullptr;
+    RowInfo* h_rows = nullptr;
+    uint64_t* h_intervals = nullptr;
+    AttnGroup* h_groups = nullptr;
+    int* h_rowlist = nullptr;
+    cudaEvent_t pass_done[2] = {nullptr, nullptr};  // recorded after a pass's read back, per half
     AttnGroup* d_groups = nullptr;   // the prefill groups of the pass
     int* d_rowlist = nullptr;        // the other rows of the pass
-    AttnGroup* h_groups = nullptr;   // pinned
-    int* h_rowlist = nullptr;        // pinned
     int n_groups = 0, n_rowlist = 0;
     bool v_scatter = false;  // some 32-row group of the pass is not a transposed v run
     uint64_t bytes = 0;
@@ -236,10 +244,12 @@ struct hs_batch {
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         if (stream) cudaStreamDestroy(stream);
         for (void* p : owned) cudaFree(p);
-        if (h_rows) cudaFreeHost(h_rows);
-        if (h_intervals) cudaFreeHost(h_intervals);
-        if (h_groups) cudaFreeHost(h_groups);
-        if (h_rowlist) cudaFreeHost(h_rowlist);
+        for (cudaEvent_t e : pass_done)
+            if (e) cudaEventDestroy(e);
+        if (h_rows_base) cudaFreeHost(h_rows_base);
+        if (h_intervals_base) cudaFreeHost(h_intervals_base);
+        if (h_groups_base) cudaFreeHost(h_groups_base);
+        if (h_rowlist_base) cudaFreeHost(h_rowlist_base);
     }
 };
 
@@ -603,7 +613,36 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     std::vector<int> pos;
     std::vector<uint32_t> hist;
     plan_passes(b, slots, tokens, n, passes, pos, hist);
-    for (auto& pass : passes) {
+    // Coder answers: pass k uses half k & 1 of the host buffers, and the host prepares pass k + 1
+    // while the GPU runs pass k. Before a half is filled again (pass k + 2), the answers of the
+    // pass that used it are copied out. The device buffers are reused in stream order.
+    auto use_half = [&](size_t k) {
+        const size_t h = k & 1, Rc = (size_t)b->Rcap;
+        b->h_rows = b->h_rows_base + h * Rc;
+        b->h_groups = b->h_groups_base + h * Rc;
+        b->h_rowlist = b->h_rowlist_base + h * Rc;
+        b->h_intervals = b->h_intervals_base + h * 3 * Rc;
+    };
+    auto answers_out = [&](size_t k) -> int {
+        CK(cudaEventSynchronize(b->pass_done[k & 1]));
+        const uint64_t* hi = b->h_intervals_base + (k & 1) * 3 * (size_t)b->Rcap;
+        const auto& pass = passes[k];
+        for (size_t r = 0; r < pass.size(); r++) {
+            long in = pass[r].input;
+            if (in < 0) continue;
+            hs_interval& iv = out[in];
+            iv.symbol = (uint32_t)hi[3 * r];
+            iv.start = hi[3 * r + 1];
+            iv.freq = hi[3 * r + 2];
+            iv.is_last = iv.symbol + 1 == (uint32_t)c.V;
+            iv.reserved = 0;
+        }
+        return HS_OK;
+    };
+    for (size_t k = 0; k < passes.size(); k++) {
+        const auto& pass = passes[k];
+        if (out && k >= 2 && (rc = answers_out(k - 2))) return rc;
+        use_half(k);
         int R = (int)pass.size();
         for (int r = 0; r < R; r++) {
             const PlanRow& p = pass[r];
@@ -638,6 +677,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             pass_scope.reset();
             CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
                                b->stream));
+            CK(cudaEventRecord(b->pass_done[k & 1], b->stream));
         } else {
             {
                 ProfScope p(b, OP_CODER, 0);
@@ -645,22 +685,9 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
                                b->stream);
             }
             pass_scope.reset();
-        }
-        rc = check_device_error(b);
-        if (rc) return rc;
-        if (b->profiling) prof_collect(b);
-        if (out) {
-            for (int r = 0; r < R; r++) {
-                long in = pass[r].input;
-                if (in < 0) continue;
-                hs_interval& iv = out[in];
-                iv.symbol = (uint32_t)b->h_intervals[3 * r];
-                iv.start = b->h_intervals[3 * r + 1];
-                iv.freq = b->h_intervals[3 * r + 2];
-                iv.is_last = iv.symbol + 1 == (uint32_t)c.V;
-                iv.reserved = 0;
-            }
-        } else {
+            // The weights of this pass leave before the next pass overwrites them.
+            rc = check_device_error(b);
+            if (rc) return rc;
             for (int r = 0; r < R; r++) {
                 long in = pass[r].input;
                 if (in < 0) continue;
@@ -668,6 +695,13 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
                               cudaMemcpyDeviceToHost));
             }
         }
+    }
+    rc = check_device_error(b);
+    if (rc) return rc;
+    if (b->profiling) prof_collect(b);
+    if (out) {
+        for (size_t k = passes.size() >= 2 ? passes.size() - 2 : 0; k < passes.size(); k++)
+            if ((rc = answers_out(k))) return rc;
     }
     // Every pass ran: commit the positions and histories (batch/plan.rs:120 commit).
     b->pos = pos;
@@ -1115,10 +1149,15 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         if ((rc = dalloc(&b->g_lo, R * c.Fp, b->owned))) return rc;
         if ((rc = make_tmap(m->dev, &b->tm_g_lo, b->g_lo, R, c.Fp, TILE_M))) return rc;
     }
-    CK(cudaMallocHost(&b->h_groups, sizeof(AttnGroup) * R));
-    CK(cudaMallocHost(&b->h_rowlist, sizeof(int) * R));
-    CK(cudaMallocHost(&b->h_rows, sizeof(RowInfo) * R));
-    CK(cudaMallocHost(&b->h_intervals, sizeof(uint64_t) * 3 * R));
+    CK(cudaMallocHost(&b->h_groups_base, sizeof(AttnGroup) * 2 * R));
+    CK(cudaMallocHost(&b->h_rowlist_base, sizeof(int) * 2 * R));
+    CK(cudaMallocHost(&b->h_rows_base, sizeof(RowInfo) * 2 * R));
+    CK(cudaMallocHost(&b->h_intervals_base, sizeof(uint64_t) * 3 * 2 * R));
+    for (cudaEvent_t& e : b->pass_done) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    b->h_groups = b->h_groups_base;
+    b->h_rowlist = b->h_rowlist_base;
+    b->h_rows = b->h_rows_base;
+    b->h_intervals = b->h_intervals_base;
     b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24 +
                                 (c.lnf_wide ? c.Dp : 0) + (gelu_wide ? c.Fp : 0));
     if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d, 128)) ||
