@@ -12,8 +12,8 @@ barrier and the max over ranks of the timings).
 
 value  = input bytes of all ranks / max over ranks of the device time of the K steps (CUDA
          events around every pass on the batch stream, the token rows already on the device);
-e2e    = the same bytes / wall time of the K C-ABI calls with host buffers (row upload, planning,
-         interval read back inside);
+e2e    = the same bytes / wall time of K more C-ABI calls with host buffers, without the
+         profiling events (row upload, planning, interval read back inside);
 roofline = the kernel with the largest share of the pass time: algorithmic int8 ops (tensor-bound
          kernels) or algorithmic bytes (HBM-bound kernels) per launch / its mean CUDA-event launch
          time, against the int8 tensor peak measured in this run (torch._int_mm, cuBLASLt) or the
@@ -321,16 +321,21 @@ def main():
     barrier()
     clocks = ClockSampler(local)
     clocks.start()
+    # The device time: K steps with per-op CUDA events on the batch stream.
     batch.set_profiling(True)
     launches0 = B.launch_count()
+    for _ in range(args.steps):
+        step()
+    launches = B.launch_count() - launches0
+    prof = batch.profile()
+    batch.set_profiling(False)
+    # End to end: K more steps through the C-ABI with host buffers, timed by the wall clock
+    # without the profiling events.
     wall = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
         step()
         wall.append(time.perf_counter() - t0)
-    launches = B.launch_count() - launches0
-    prof = batch.profile()
-    batch.set_profiling(False)
     barrier()
     clk = clocks.stop()
 
@@ -408,28 +413,32 @@ def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, conte
     """1024 streams decoded token by token. The streams are filled to `context`
     positions (prefill, not timed), then `steps` decode steps (one row per stream, the coder
     op answering a decode query for each row: the symbol whose interval holds a seeded 32-bit
-    target) are timed on the device and with the wall clock around the C-ABI calls. The next
-    input of a stream is the text's own next token, so the rows are those of a real unfold."""
+    target) are timed with the wall clock around the C-ABI calls (end to end, no profiling), and
+    the next `steps` steps on the device (per-op CUDA events). The next input of a stream is the
+    text's own next token, so the rows are those of a real unfold."""
     from taco_b200 import synth
 
-    toks = synth.zipf_windows(streams, context + steps, seed=77)
+    toks = synth.zipf_windows(streams, context + 2 * steps, seed=77)
     batch = B.CudaBatch(model, streams, 16384)
     slots, inputs, coded = window_rows(toks[:, :context], eot)
     batch.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32)
     sl = np.arange(streams, dtype=np.uint32)
     kinds = np.ones(streams, np.uint32)
-    targets = np.random.default_rng(78).integers(0, 1 << 32, (steps, streams), dtype=np.uint64)
-    batch.set_profiling(True)
+    targets = np.random.default_rng(78).integers(0, 1 << 32, (2 * steps, streams), dtype=np.uint64)
     t0 = time.perf_counter()
     for i in range(steps):
         batch.run_coded(sl, toks[:, context + i - 1], kinds, targets[i], 32)
     wall = time.perf_counter() - t0
+    batch.set_profiling(True)
+    for i in range(steps, 2 * steps):
+        batch.run_coded(sl, toks[:, context + i - 1], kinds, targets[i], 32)
     prof = batch.profile()
     batch.close()
     dev_s = prof["pass"]["ms"] / 1e3
-    nbytes = int(lens[toks[:, context:context + steps].astype(np.int64)].sum())
-    kv_read = streams * steps * 2 * 12 * 768 * (context + steps / 2)
-    return {"streams": streams, "positions": f"{context}..{context + steps - 1}", "steps": steps,
+    nbytes = int(lens[toks[:, context + steps:context + 2 * steps].astype(np.int64)].sum())
+    kv_read = streams * steps * 2 * 12 * 768 * (context + 1.5 * steps)
+    return {"streams": streams, "positions": f"{context}..{context + steps - 1} (end to end), "
+            f"{context + steps}..{context + 2 * steps - 1} (device)", "steps": steps,
             "tokens_per_s": streams * steps / dev_s, "MB_per_s": nbytes / dev_s / 1e6,
             "e2e_tokens_per_s": streams * steps / wall,
             "kv_GB_per_s": kv_read / dev_s / 1e9,
