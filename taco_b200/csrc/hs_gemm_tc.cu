@@ -35,9 +35,6 @@ constexpr int A_BYTES = BM * BK;
 constexpr int B_BYTES = BN * BK;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int EPI_WARPS = 8;
-constexpr int EPI_THREADS = 32 * EPI_WARPS;
-constexpr int THREADS = 64 + EPI_THREADS;
 constexpr int GELU_SMEM = 65536;
 
 constexpr int VT_STRIDE = 36;                  // bytes per row of a warp's 32 x 32 transpose tile
@@ -48,8 +45,16 @@ constexpr int VT_TILE = 32 * VT_STRIDE;
 // each epilogue warp stages blocks of 32 rows x 128 bytes (the 128-byte swizzle) in two 4 KB
 // buffers, one TMA store per block; they run with 3 stages to make room. GELU, whose 64 KB table
 // fills shared memory: one buffer of 32 rows x 32 bytes (the 32-byte swizzle).
+//
+// Epilogue warps: 8 (two per TMEM lane group), or 12 for QKV (three per lane group),
+// whose epilogue bounds its K = 768 GEMM: 14 warps still leave 128 registers per thread (at
+// most 4 warps per SM sub-partition), and a warp's share of a tile drops from 4 to 3 or 2 of the
+// 8 chunks of 32 columns, in contiguous ranges.
 template <int MODE>
 struct Cfg {
+    static constexpr int EPI_WARPS = MODE == EPI_QKV ? 12 : 8;
+    static constexpr int EPI_THREADS = 32 * EPI_WARPS;
+    static constexpr int THREADS = 64 + EPI_THREADS;
     static constexpr int STAGES = (MODE == EPI_GELU || MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 3 : 4;
     static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : (MODE == EPI_QKV ? EPI_WARPS * VT_TILE : 0);
     static constexpr int STORE_WARP = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 8192 : (MODE == EPI_GELU ? 1024 : 0);
@@ -137,12 +142,18 @@ __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowIn
 // accumulates hi and lo into two TMEM accumulators of 128 columns, and the epilogue recombines
 // v = 256 acc_hi + acc_lo + 128 sum_k W[n][k] exactly in i64 (hardshell.cu:798-830 wide_dot).
 template <int MODE, bool S32, bool WIDE>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC, int MT, int NT,
               int KB, EpiArgs e, int* err) {
     constexpr int STAGES = Cfg<MODE>::STAGES;
+    constexpr int EPI_WARPS = Cfg<MODE>::EPI_WARPS;
+    constexpr int EPI_THREADS = Cfg<MODE>::EPI_THREADS;
+    constexpr int THREADS = Cfg<MODE>::THREADS;
+    constexpr int NPART = EPI_WARPS / 4;  // epilogue warps per TMEM lane group
     constexpr int TN = WIDE ? 128 : BN;  // columns of one tile
+    static_assert(!WIDE || EPI_WARPS == 8, "the version 2 epilogues take 8 warps");
+    static_assert(MODE != EPI_LOGITS || EPI_WARPS == 8, "the logits epilogue takes 8 warps");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     int8_t* s_gelu = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * STAGE_BYTES);
@@ -260,9 +271,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else {
-        const int et = threadIdx.x - 64;        // 0..255
+        const int et = threadIdx.x - 64;        // 0 .. EPI_THREADS - 1
         const int g = warp & 3;                 // TMEM lane group this warp may read
-        const int half = (warp - 2) >> 2;       // which 128 columns of the tile
+        const int part = (warp - 2) >> 2;       // 0 .. NPART - 1 within the lane group
+        const int half = part;                  // (the 8-warp epilogues: which 128 columns)
         const int row_in_tile = g * 32 + lane;
         const int s = e.s;
         const bool fast = s >= 0 && s <= 62;
@@ -561,7 +573,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 continue;
             } else {
 #pragma unroll 1
-                for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 32) {
+                // This warp's chunks of 32 columns: a contiguous range (4 of the 8 with 8 warps;
+                // 3, 3 and 2 with 12).
+                constexpr int CPP = (TN / 32 + NPART - 1) / NPART;
+                const int c_end = min(TN, 32 * CPP * (part + 1));
+                for (int c0 = 32 * CPP * part; c0 < c_end; c0 += 32) {
                     uint32_t v[32];
                     __syncwarp();
                     tmem_ld32(taddr + c0, v);
@@ -749,14 +765,14 @@ void launch_mode(const void* tmA, const void* tmA2, const void* tmB, const void*
     if constexpr (MODE == EPI_DELTA || MODE == EPI_LOGITS) {
         if (tmA2) {
             const CUtensorMap& a2 = *reinterpret_cast<const CUtensorMap*>(tmA2);
-            k_gemm_tc<MODE, false, true><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, a2, b, c, MT, NT, KB, e, err);
+            k_gemm_tc<MODE, false, true><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a2, b, c, MT, NT, KB, e, err);
             return;
         }
     }
     if (MODE != EPI_RAW && e.small && e.s >= 0 && e.s <= 62)
-        k_gemm_tc<MODE, true, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, true, false><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
     else
-        k_gemm_tc<MODE, false, false><<<grid, THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, false, false><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
 }
 
 template <int MODE>
