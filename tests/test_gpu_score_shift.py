@@ -6,7 +6,8 @@ shift of both words for 21 <= s <= 31, and the general 64-bit rule otherwise. Th
 have s near 40, so this test rewrites each layer's (m, s) to a target shift with about the same
 ratio (m >> k, s - k) and checks the weights of prefill groups and decode rows against the
 oracle's fast path, for the tensor-core prefill kernel with the decode kernel (HS_ATTN=tc) and
-the CUDA-core kernel (HS_ATTN=vec).
+the CUDA-core kernel (HS_ATTN=vec). The output rescale (attn.out.rescale) is checked the same way
+at other shifts.
 """
 
 import os
@@ -39,11 +40,11 @@ def parts():
     return tensors, eps
 
 
-def _with_score_shift(parts, target: int) -> bytes:
+def _with_score_shift(parts, target: int, suffix: str = "attn.score.rescale") -> bytes:
     tensors, eps = parts
     out = []
     for name, dt, v, s in tensors:
-        if name.endswith("attn.score.rescale"):
+        if name.endswith(suffix):
             k = s - target
             assert k > 0
             m = np.array([int(v[0]) >> k], np.int32)
@@ -82,5 +83,29 @@ def test_attention_at_each_score_shift_range(dev, parts, attn, shift):
         want = fast.run_weights(sl, tk)
         bad = np.nonzero(~np.all(got == want, axis=1))[0]
         assert bad.size == 0, (attn, shift, bad[:10], len(seq))
+    batch.close()
+    model.close()
+
+
+@pytest.mark.parametrize("shift", [31, 32, 47])
+def test_attention_at_each_output_shift_range(dev, parts, shift):
+    """The output rescale of the attention kernels (a double estimate with an exact 128-bit
+    fallback near ties) at output shifts other than the model's own 60."""
+    data = _with_score_shift(parts, shift, "attn.out.rescale")
+    om = O.Model(data)
+    model = _model(dev, data, "tc")
+    batch = B.CudaBatch(model, 3, 1024)
+    fast = O.FastBatch(om, 3, 0)
+    rng = np.random.default_rng(100 + shift)
+    for spec in ([(0, 200), (1, 130), (2, 33)], [(0, 1), (1, 1), (2, 20), (0, 1)]):
+        seq = []
+        for s, n in spec:
+            seq += [(s, int(t)) for t in rng.integers(0, om.vocab - 1, n)]
+        sl = [s for s, _ in seq]
+        tk = [t for _, t in seq]
+        got = batch.run_weights(sl, tk)
+        want = fast.run_weights(sl, tk)
+        bad = np.nonzero(~np.all(got == want, axis=1))[0]
+        assert bad.size == 0, (shift, bad[:10], len(seq))
     batch.close()
     model.close()
