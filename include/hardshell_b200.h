@@ -102,6 +102,22 @@ int hs_batch_run_coded(hs_batch* batch, const uint32_t* slots, const uint32_t* t
 int hs_batch_run_weights(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
                          uint64_t* out);
 
+/* CudaBatch::stream_len (batch/stream.rs:17-21): the inputs of `slot` since its last reset (the
+ * EOT row of a block start is one input; the rows of a context restart are not). */
+int hs_batch_stream_len(hs_batch* batch, uint32_t slot, uint64_t* len);
+/* CudaBatch::room (batch/stream.rs:23-33, StreamState::room): the inputs `slot` can take before
+ * its next context restart; a draft of at most this many rows never needs a rebuild at a
+ * truncation. */
+int hs_batch_room(hs_batch* batch, uint32_t slot, uint64_t* room);
+/* CudaBatch::truncate (batch/stream.rs:35-77), the engine side of speculative decoding: the
+ * slot keeps its first `len` inputs and then gives the weights of a slot that ran only those,
+ * bit for bit (crates/hardshell/src/gpt2/stream.rs rules). Inside the current context only the
+ * position moves back; before the last context restart the slot takes back the old context and
+ * runs the rows that the new context overwrote again (no read back). Errors: HS_BAD_SLOT;
+ * HS_MODEL (BadTruncate) if len is more than the stream length or before the restart before
+ * the last one. The slot does not change on an error. */
+int hs_batch_truncate(hs_batch* batch, uint32_t slot, uint64_t len);
+
 /* The unfold of n coded blocks with the range decoder on the device. It replaces the host loop
  * of crates/taco/src/gpu_unfold.rs:100-160 (codec.rs BlockDecoder over run_coded with Decode
  * queries, one host round trip per token) for the coded blocks of a job. Block i is reset into

@@ -89,6 +89,9 @@ def lib() -> ctypes.CDLL:
     L.hs_batch_gpu_bytes.restype = u64
     L.hs_batch_run_coded.argtypes = [vp, vp, vp, vp, vp, u32, u32, vp]
     L.hs_batch_run_weights.argtypes = [vp, vp, vp, u32, vp]
+    L.hs_batch_stream_len.argtypes = [vp, u32, ctypes.POINTER(ctypes.c_uint64)]
+    L.hs_batch_room.argtypes = [vp, u32, ctypes.POINTER(ctypes.c_uint64)]
+    L.hs_batch_truncate.argtypes = [vp, u32, ctypes.c_uint64]
     L.hs_batch_decode_blocks.argtypes = [vp, u32, vp, vp, ctypes.c_uint64, vp, vp, vp, u32, vp, ctypes.c_uint64, vp, vp]
     L.hs_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
@@ -330,6 +333,22 @@ class CudaBatch:
         out = np.zeros((s.size, self.model.info.vocab), dtype=np.uint64)
         _check(lib().hs_batch_run_weights(self.h, _p(s), _p(t), s.size, _p(out)))
         return out
+
+    def stream_len(self, slot: int) -> int:
+        """CudaBatch::stream_len: the inputs of `slot` since its last reset."""
+        v = ctypes.c_uint64()
+        _check(lib().hs_batch_stream_len(self.h, slot, ctypes.byref(v)))
+        return v.value
+
+    def room(self, slot: int) -> int:
+        """CudaBatch::room: the inputs `slot` can take before its next context restart."""
+        v = ctypes.c_uint64()
+        _check(lib().hs_batch_room(self.h, slot, ctypes.byref(v)))
+        return v.value
+
+    def truncate(self, slot: int, length: int):
+        """CudaBatch::truncate: keep the first `length` inputs of `slot`."""
+        _check(lib().hs_batch_truncate(self.h, slot, length))
 
     def decode_blocks(self, slots, payloads, counts, freq_bits: int = 32):
         """hs_batch_decode_blocks: block i (the range-coded bytes payloads[i], counts[i] tokens) is

@@ -180,12 +180,23 @@ struct hs_model {
     }
 };
 
+// The bookkeeping of one slot's inputs for a truncation (crates/hardshell/src/gpt2/stream.rs
+// StreamState): the inputs since the last reset, the first input position of the current
+// context (0, or K + 1 after a restart), one more than the highest position the current context
+// wrote, and `first` of the context before the last restart (-1: none).
+struct StreamSt {
+    uint32_t len = 0, first = 0, written = 0;
+    int32_t prev_first = -1;
+};
+
 struct hs_batch {
     hs_model* model = nullptr;
     int slots = 0, max_rows = 0, Rcap = 0;
     uint16_t overlap = 0;
     std::vector<int> pos;
     std::vector<uint32_t> hist;  // [slots, n_ctx]
+    std::vector<StreamSt> streams;              // per slot
+    std::vector<std::vector<uint32_t>> prev;    // per slot: the full context before the last restart
     std::vector<void*> owned;
     cudaStream_t stream = nullptr;
     int8_t* kc = nullptr;
@@ -540,8 +551,16 @@ struct PlanRow {
 
 // batch/plan.rs:60-120: the passes of a call, with the restart rows of a full context. The
 // positions and histories change in copies; the caller commits them after the passes ran.
+// The stream states and kept contexts of the slots that a call touches, committed with the
+// positions (batch/plan.rs:68-116).
+struct StreamPlan {
+    std::unordered_map<uint32_t, StreamSt> st;
+    std::unordered_map<uint32_t, std::vector<uint32_t>> prev;
+};
+
 void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
-                 std::vector<std::vector<PlanRow>>& passes, std::vector<int>& pos, std::vector<uint32_t>& hist) {
+                 std::vector<std::vector<PlanRow>>& passes, std::vector<int>& pos, std::vector<uint32_t>& hist,
+                 StreamPlan& sp) {
     const int n_ctx = b->model->c.n_ctx;
     const int k = std::min<int>(b->overlap, n_ctx - 2);
     const uint32_t eot = b->model->eot;
@@ -563,8 +582,14 @@ void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* token
         uint32_t s = slots[i];
         uint32_t* h = &hist[(size_t)s * n_ctx];
         int at = pos[s];
+        StreamSt& ss = sp.st.try_emplace(s, b->streams[s]).first->second;
         if (at >= n_ctx) {
             if (in_pass[s]) flush();
+            // The full context before the restart, for a truncation (stream.rs restart).
+            sp.prev[s].assign(h, h + n_ctx);
+            ss.prev_first = (int32_t)ss.first;
+            ss.first = (uint32_t)k + 1;
+            ss.written = (uint32_t)k + 1;
             memmove(h + 1, h + (n_ctx - k), sizeof(uint32_t) * k);
             h[0] = eot;
             for (int q = 0; q <= k; q++) push({s, h[q], (uint32_t)q, -1});
@@ -573,6 +598,8 @@ void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* token
         h[at] = tokens[i];
         push({s, tokens[i], (uint32_t)at, (long)i});
         pos[s] = at + 1;
+        ss.len++;
+        ss.written = std::max(ss.written, (uint32_t)at + 1);
     }
     flush();
 }
@@ -612,7 +639,8 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     std::vector<std::vector<PlanRow>> passes;
     std::vector<int> pos;
     std::vector<uint32_t> hist;
-    plan_passes(b, slots, tokens, n, passes, pos, hist);
+    StreamPlan sp;
+    plan_passes(b, slots, tokens, n, passes, pos, hist, sp);
     // Coder answers: pass k uses half k & 1 of the host buffers, and the host prepares pass k + 1
     // while the GPU runs pass k. Before a half is filled again (pass k + 2), the answers of the
     // pass that used it are copied out. The device buffers are reused in stream order.
@@ -706,6 +734,8 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     // Every pass ran: commit the positions and histories (batch/plan.rs:120 commit).
     b->pos = pos;
     b->hist = hist;
+    for (auto& kv : sp.st) b->streams[kv.first] = kv.second;
+    for (auto& kv : sp.prev) b->prev[kv.first] = std::move(kv.second);
     return HS_OK;
 }
 
@@ -783,6 +813,7 @@ int decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t*
     launch_dec_init(d_st, d_payload, d_off, d_len, d_prev, m->eot, (int)n, st);
     for (uint32_t k = 0; k < n; k++) {
         b->pos[h_slot[k]] = 0;
+        b->streams[h_slot[k]] = StreamSt{};
         std::fill(b->hist.begin() + (size_t)h_slot[k] * n_ctx, b->hist.begin() + (size_t)(h_slot[k] + 1) * n_ctx, 0u);
     }
     // The steps since the last host sync run at positions h_pos[k] + (step - s_sync); sync_hist
@@ -810,9 +841,13 @@ int decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t*
         for (uint32_t k = 0; k < L; k++) {
             uint32_t* h = &b->hist[(size_t)h_slot[k] * n_ctx];
             const uint32_t e = std::min(step, h_cnt[k]);
+            StreamSt& ss = b->streams[h_slot[k]];
             for (uint32_t s2 = s_sync; s2 < e; s2++) {
-                h[h_pos[k] + (s2 - s_sync)] = last_sym[k];
+                const uint32_t p2 = h_pos[k] + (s2 - s_sync);
+                h[p2] = last_sym[k];
                 last_sym[k] = h_gather[(size_t)k * w + (s2 - s_sync)];
+                ss.len++;
+                ss.written = std::max(ss.written, p2 + 1);
             }
             b->pos[h_slot[k]] = (int)(h_pos[k] + (e - s_sync));
             h_pos[k] = (uint32_t)b->pos[h_slot[k]];
@@ -897,6 +932,79 @@ int decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t*
         memcpy(tokens_out + token_offsets[i], all.data() + h_oo[k], sizeof(uint32_t) * counts[i]);
         if (status) status[i] = fl[k];
     }
+    return HS_OK;
+}
+
+// Rows with no coder answer (the rebuild rows of a truncation): passes of at most max_rows rows,
+// each synchronised before the host buffers are filled again.
+int run_rows(hs_batch* b, const std::vector<PlanRow>& rows) {
+    for (size_t r0 = 0; r0 < rows.size(); r0 += (size_t)b->max_rows) {
+        const int R = (int)std::min(rows.size() - r0, (size_t)b->max_rows);
+        for (int r = 0; r < R; r++) {
+            const PlanRow& p = rows[r0 + r];
+            b->h_rows[r] = RowInfo{p.slot, p.token, p.pos, 0, 0};
+        }
+        CK(cudaMemcpyAsync(b->d_rows, b->h_rows, sizeof(RowInfo) * R, cudaMemcpyHostToDevice, b->stream));
+        plan_groups(b, R);
+        b->v_scatter = false;
+        for (int q0 = 0; q0 < R && !b->v_scatter; q0 += 32) b->v_scatter = !vt_run_host(b->h_rows, q0, R, b->model->c.n_ctx);
+        if (b->n_groups) {
+            CK(cudaMemcpyAsync(b->d_groups, b->h_groups, sizeof(AttnGroup) * b->n_groups, cudaMemcpyHostToDevice,
+                               b->stream));
+            if (b->n_rowlist)
+                CK(cudaMemcpyAsync(b->d_rowlist, b->h_rowlist, sizeof(int) * b->n_rowlist, cudaMemcpyHostToDevice,
+                                   b->stream));
+        }
+        int rc = forward(b, R);
+        if (rc || (rc = check_device_error(b))) return rc;
+    }
+    return HS_OK;
+}
+
+// CudaBatch::truncate (crates/hardshell-cuda/src/batch/stream.rs:46-77) with the rules of
+// StreamState::plan_truncate / commit_truncate (crates/hardshell/src/gpt2/stream.rs:118-160):
+// inside the current context only the position moves back; before the last restart the slot
+// takes the kept history of the old context and runs its rows again at the positions that the
+// new context wrote (the rebuilt cache entries are the old ones, bit for bit); before the restart
+// before the last one it is an error. The slot does not change on an error.
+int truncate_slot(hs_batch* b, uint32_t slot, uint64_t len) {
+    if (slot >= (uint32_t)b->slots)
+        return fail(HS_BAD_SLOT, "slot " + std::to_string(slot) + " is not valid in a batch of " +
+                                     std::to_string(b->slots) + " slots");
+    const int n_ctx = b->model->c.n_ctx;
+    StreamSt ss = b->streams[slot];
+    const uint64_t pos = (uint64_t)b->pos[slot];
+    auto bad = [&]() {
+        return fail(HS_MODEL, "BadTruncate: length " + std::to_string(len) + " for a stream of " +
+                                  std::to_string(ss.len) + " inputs");
+    };
+    if (len > ss.len) return bad();
+    const uint64_t drop = ss.len - len;
+    const uint64_t here = pos > ss.first ? pos - ss.first : 0;
+    if (drop <= here) {
+        b->streams[slot].len = (uint32_t)len;
+        b->pos[slot] = (int)(pos - drop);
+        return HS_OK;
+    }
+    if (ss.prev_first < 0) return bad();
+    const uint64_t before = drop - here;
+    if (before > (uint64_t)(n_ctx - ss.prev_first)) return bad();
+    const uint32_t target = (uint32_t)(n_ctx - before);
+    const std::vector<uint32_t>& old = b->prev[slot];
+    if (old.size() != (size_t)n_ctx) return bad();
+    int rc = set_device(b->model->dev);
+    if (rc) return rc;
+    cudaGetLastError();
+    std::vector<PlanRow> rows;
+    for (uint32_t p = 0; p < std::min(target, ss.written); p++) rows.push_back({slot, old[p], p, -1});
+    if ((rc = run_rows(b, rows))) return rc;
+    std::copy(old.begin(), old.end(), b->hist.begin() + (size_t)slot * n_ctx);
+    StreamSt& st = b->streams[slot];
+    st.len = (uint32_t)len;
+    st.first = (uint32_t)ss.prev_first;
+    st.prev_first = -1;
+    st.written = (uint32_t)n_ctx;
+    b->pos[slot] = (int)target;
     return HS_OK;
 }
 
@@ -1127,6 +1235,8 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
     const ModelConsts& c = m->c;
     b->pos.assign(slots, 0);
     b->hist.assign((size_t)slots * c.n_ctx, 0);
+    b->streams.assign(slots, StreamSt{});
+    b->prev.assign(slots, {});
     CK(cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking));
     size_t cache = (size_t)slots * c.L * c.n_ctx * c.d;
     size_t R = b->Rcap;
@@ -1191,7 +1301,10 @@ int hs_batch_set_overlap(hs_batch* b, uint16_t k) {
 
 int hs_batch_reset(hs_batch* b, uint32_t slot) {
     if (!b) return fail(HS_BAD_ARGUMENT, "null argument");
-    if (slot < (uint32_t)b->slots) b->pos[slot] = 0;
+    if (slot < (uint32_t)b->slots) {
+        b->pos[slot] = 0;
+        b->streams[slot] = StreamSt{};
+    }
     return HS_OK;
 }
 
@@ -1233,6 +1346,30 @@ int hs_batch_run_coded(hs_batch* b, const uint32_t* slots, const uint32_t* token
                        const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out) {
     if (!b || (n && (!slots || !tokens || !kinds || !values || !out))) return fail(HS_BAD_ARGUMENT, "null argument");
     return run(b, slots, tokens, kinds, values, n, freq_bits, out, nullptr);
+}
+
+int hs_batch_stream_len(hs_batch* b, uint32_t slot, uint64_t* len) {
+    if (!b || !len) return fail(HS_BAD_ARGUMENT, "null argument");
+    if (slot >= (uint32_t)b->slots)
+        return fail(HS_BAD_SLOT, "slot " + std::to_string(slot) + " is not valid in a batch of " +
+                                     std::to_string(b->slots) + " slots");
+    *len = b->streams[slot].len;
+    return HS_OK;
+}
+
+int hs_batch_room(hs_batch* b, uint32_t slot, uint64_t* room) {
+    if (!b || !room) return fail(HS_BAD_ARGUMENT, "null argument");
+    if (slot >= (uint32_t)b->slots)
+        return fail(HS_BAD_SLOT, "slot " + std::to_string(slot) + " is not valid in a batch of " +
+                                     std::to_string(b->slots) + " slots");
+    const int n_ctx = b->model->c.n_ctx, k = std::min<int>(b->overlap, n_ctx - 2), p = b->pos[slot];
+    *room = p >= n_ctx ? (uint64_t)std::max(0, n_ctx - k - 1) : (uint64_t)(n_ctx - p);
+    return HS_OK;
+}
+
+int hs_batch_truncate(hs_batch* b, uint32_t slot, uint64_t len) {
+    if (!b) return fail(HS_BAD_ARGUMENT, "null argument");
+    return truncate_slot(b, slot, len);
 }
 
 int hs_batch_decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t* payload,
