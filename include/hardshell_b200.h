@@ -102,6 +102,48 @@ int hs_batch_run_coded(hs_batch* batch, const uint32_t* slots, const uint32_t* t
 int hs_batch_run_weights(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
                          uint64_t* out);
 
+/* The mixed coder op of the profile `logs` (crates/hardshell-cuda/src/mixed.rs, batch/mixed.rs).
+ * The table word of an input: a predicted token (the table of the mixed weights of
+ * taco_match::Mixer::mix, mixer.rs:491-516), HS_MIX_NONE (a mixed table without a prediction:
+ * the weights max(1, w)) or HS_MIX_PLAIN (the table of GPT-2 alone, as hs_batch_run_coded). */
+#define HS_MIX_NONE 0xFFFFFFFFu
+#define HS_MIX_PLAIN 0xFFFFFFFEu
+
+/* What the host mixer needs from the GPT-2 weights w of one input (mixed.rs:36-47 MixStats):
+ * total = sum(w), predicted = w[p], top = the token with the largest weight (the lowest id on a
+ * tie, 0 if every weight is 0). 24 bytes. */
+typedef struct hs_mix_stats {
+    uint64_t total;
+    uint64_t predicted;
+    uint32_t top;
+    uint32_t reserved;
+} hs_mix_stats;
+
+/* The host mixer: gives q, the probability of the predicted token in units of 2^-16 (1..=65535),
+ * for input `input` from its statistics (rules 2 to 4 of the mixer: W = total, w[p] = predicted,
+ * agreement = top == p). Called in input order, once for each input with a predicted token, so
+ * the caller can update its mixer state between calls. A q outside 1..=65535 fails the call. */
+typedef uint32_t (*hs_mixer_fn)(void* user, uint32_t input, const hs_mix_stats* stats);
+
+/* CudaBatch::run_coded_mixed (batch/mixed.rs:71-109): runs the inputs as hs_batch_run_coded, but
+ * answers query i in the table that tables[i] names. For each pass: the forward pass, the
+ * statistics of every row (one more kernel and a read back of 24 bytes per row), the mixer calls,
+ * the mix records (32 bytes per row up), and the mixed coder kernel. Errors: those of
+ * hs_batch_run_coded; HS_UNSUPPORTED if a table word is not a token, HS_MIX_NONE or HS_MIX_PLAIN,
+ * or if `mixer` gives a q outside 1..=65535. After an error no position changed, but `mixer` can
+ * have been called: the caller must drop its mixer state. */
+int hs_batch_run_coded_mixed(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds,
+                             const uint64_t* values, const uint32_t* tables, uint32_t n, uint32_t freq_bits,
+                             hs_mixer_fn mixer, void* user, hs_interval* out);
+
+/* CudaBatch::run_coded_dual (batch/mixed.rs:109-135): the two intervals of coded[i] for the
+ * encoder of the profile `logs`, in the table of GPT-2 alone (plain_out[i]) and in the mixed
+ * table of predictions[i] (mixed_out[i]; a token or HS_MIX_NONE). `mixer` is called as for
+ * hs_batch_run_coded_mixed. */
+int hs_batch_run_coded_dual(hs_batch* batch, const uint32_t* slots, const uint32_t* tokens, const uint32_t* coded,
+                            const uint32_t* predictions, uint32_t n, uint32_t freq_bits, hs_mixer_fn mixer,
+                            void* user, hs_interval* plain_out, hs_interval* mixed_out);
+
 /* CudaBatch::stream_len (batch/stream.rs:17-21): the inputs of `slot` since its last reset (the
  * EOT row of a block start is one input; the rows of a context restart are not). */
 int hs_batch_stream_len(hs_batch* batch, uint32_t slot, uint64_t* len);

@@ -116,6 +116,18 @@ int hso_from_weights(const uint64_t* w, size_t n, uint32_t bits, uint32_t* start
     return from_weights(w, n, bits, starts);
 }
 
+// out = {W, w[p], top} (mixer.rs:276-287).
+int hso_mix_stats(const uint64_t* w, size_t n, uint32_t p, uint64_t* out) {
+    uint32_t top = 0;
+    int rc = mix_stats(w, n, p, &out[0], &out[1], &top);
+    out[2] = top;
+    return rc;
+}
+
+int hso_mix_weights(const uint64_t* w, size_t n, uint32_t p, uint32_t q, uint64_t* out) {
+    return mix_weights(w, n, p, q, out);
+}
+
 // The answer of the coder op for one weight vector (lanes.rs:20 Query, batch.rs:463 run_coded):
 // kind 0 = the interval of token `value`, kind 1 = the symbol whose interval holds `value`.
 // out = {symbol, start, freq}. Returns 0, or the error code of from_weights, or 4 (bad query).

@@ -402,4 +402,56 @@ void Decoder::renormalise() {
     }
 }
 
+// ---- mixer.rs ----
+
+int mix_stats(const uint64_t* w, size_t n, uint32_t p, uint64_t* total, uint64_t* wp, uint32_t* top) {
+    if ((size_t)p >= n) return 1;
+    u128 sum = 0;
+    size_t t = 0;
+    uint64_t tw = 0;
+    for (size_t i = 0; i < n; i++) {
+        sum += w[i];
+        if (w[i] > tw) {  // the first largest weight; token 0 if every weight is 0
+            t = i;
+            tw = w[i];
+        }
+    }
+    if (sum >> 64) return 2;
+    *total = (uint64_t)sum;
+    *wp = w[p];
+    *top = (uint32_t)t;
+    return 0;
+}
+
+int mix_weights(const uint64_t* w, size_t n, uint32_t p, uint32_t q, uint64_t* out) {
+    if (p == MIX_PLAIN) {
+        for (size_t i = 0; i < n; i++) out[i] = w[i];
+        return 0;
+    }
+    if (p == MIX_NONE) {
+        for (size_t i = 0; i < n; i++) out[i] = w[i] > 1 ? w[i] : 1;
+        return 0;
+    }
+    if (q == 0 || q >= 65536) return 3;
+    uint64_t total, wp;
+    uint32_t top;
+    int rc = mix_stats(w, n, p, &total, &wp, &top);
+    if (rc) return rc;
+    // apply (mixer.rs:491-516): R = max(W - w[p], 1), m = 2^16 - q, k = max(0, bitlen(R) + 16 - 62),
+    // w'[i] = max(1, (w[i] * m) >> k), then w'[p] = max(1, (R * q) >> k). In u128 throughout: the
+    // reference's u64 loop for weights below 2^48 gives the same values.
+    const u128 r = total - wp > 0 ? (u128)(total - wp) : (u128)1;
+    const u128 m = 65536u - q;
+    int bits = 0;
+    while (bits < 128 && (r >> bits) != 0) bits++;
+    const int k = bits + 16 > 62 ? bits + 16 - 62 : 0;
+    for (size_t i = 0; i < n; i++) {
+        u128 x = ((u128)w[i] * m) >> k;
+        out[i] = x > 1 ? (uint64_t)x : 1;  // below 2^62: w[i] <= R for i != p
+    }
+    u128 x = (r * q) >> k;
+    out[p] = x > 1 ? (uint64_t)x : 1;
+    return 0;
+}
+
 }  // namespace hso

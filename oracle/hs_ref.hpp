@@ -75,6 +75,25 @@ inline Interval table_interval(const uint32_t* starts, size_t n, uint32_t bits, 
 // freq.rs:229 FreqTable::find: the largest i with starts[i] <= target.
 size_t table_find(const uint32_t* starts, size_t n, uint64_t target);
 
+// ---- the weight step of the logs-profile mixer (crates/taco-match/src/mixer.rs) ----
+
+// The table word of an input without a prediction and of a plain input
+// (crates/hardshell-cuda/src/mixed.rs:31,104).
+constexpr uint32_t MIX_NONE = 0xFFFFFFFFu;
+constexpr uint32_t MIX_PLAIN = 0xFFFFFFFEu;
+
+// Pass 1 of Mixer::mix (mixer.rs:276-287): W = sum(w) (a u128 there; below 2^64 for GPT-2
+// weights, and the caller checks), w[p], and the top token (the first largest weight, 0 if every
+// weight is 0). Returns 0, or 1 if p >= n, or 2 if the sum is 2^64 or more.
+int mix_stats(const uint64_t* w, size_t n, uint32_t p, uint64_t* total, uint64_t* wp, uint32_t* top);
+
+// The weights of Mixer::mix for the prediction p and the mixer probability q (units of 2^-16):
+// p = MIX_NONE gives max(1, w) (mixer.rs:265-269, rule 1), p = MIX_PLAIN the weights unchanged
+// (the table of GPT-2 alone), a token p the weights of apply (mixer.rs:491-516). Returns 0, or
+// 1 if p is neither a token nor a table word, 2 if the sum is 2^64 or more, 3 if q is not in
+// 1..=65535 (the reference's mix_record check, crates/hardshell-cuda/src/mixed.rs:71-73).
+int mix_weights(const uint64_t* w, size_t n, uint32_t p, uint32_t q, uint64_t* out);
+
 // encoder.rs:13 Encoder: the LZMA-style range encoder with a 64-bit window.
 struct Encoder {
     unsigned __int128 low = 0;

@@ -52,6 +52,8 @@ def lib() -> ctypes.CDLL:
     L.hso_from_weights.argtypes = [ctypes.c_void_p, sz, ctypes.c_uint32, ctypes.c_void_p]
     L.hso_answer.argtypes = [ctypes.c_void_p, sz, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64,
                              ctypes.c_void_p]
+    L.hso_mix_stats.argtypes = [ctypes.c_void_p, sz, ctypes.c_uint32, ctypes.c_void_p]
+    L.hso_mix_weights.argtypes = [ctypes.c_void_p, sz, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_void_p]
     L.hso_encode_block.argtypes = [vp, ctypes.c_uint16, ctypes.c_void_p, sz, ctypes.c_void_p, sz,
                                    ctypes.POINTER(sz)]
     L.hso_decode_block.argtypes = [vp, ctypes.c_uint16, ctypes.c_char_p, sz, ctypes.c_uint32, ctypes.c_void_p,
@@ -199,6 +201,31 @@ def answer(w: np.ndarray, bits: int, kind: int, value: int) -> tuple[int, int, i
     if rc:
         raise OracleError(f"answer failed: {rc}")
     return int(out[0]), int(out[1]), int(out[2])
+
+
+MIX_NONE = 0xFFFFFFFF  # crates/hardshell-cuda/src/mixed.rs:31: an input without a prediction
+MIX_PLAIN = 0xFFFFFFFE  # mixed.rs:104: the table of GPT-2 alone
+
+
+def mix_stats(w: np.ndarray, p: int) -> tuple[int, int, int]:
+    """taco-match mixer.rs:276-287, pass 1 of Mixer::mix: (W, w[p], top)."""
+    w = np.ascontiguousarray(w, dtype=np.uint64)
+    out = np.zeros(3, dtype=np.uint64)
+    rc = lib().hso_mix_stats(_ptr(w), w.size, p, _ptr(out))
+    if rc:
+        raise OracleError(f"mix_stats failed: {rc}")
+    return int(out[0]), int(out[1]), int(out[2])
+
+
+def mix_weights(w: np.ndarray, p: int, q: int = 0) -> np.ndarray:
+    """The weights of Mixer::mix (mixer.rs:265-269 rule 1, :491-516 apply) for the table word p
+    (a token, MIX_NONE or MIX_PLAIN) and the mixer probability q in 1..=65535."""
+    w = np.ascontiguousarray(w, dtype=np.uint64)
+    out = np.zeros(w.size, dtype=np.uint64)
+    rc = lib().hso_mix_weights(_ptr(w), w.size, p, q, _ptr(out))
+    if rc:
+        raise OracleError(f"mix_weights failed: {rc}")
+    return out
 
 
 def encode_block(model: Model, tokens, overlap: int = 0) -> bytes:

@@ -54,6 +54,16 @@ class OpProfile(ctypes.Structure):
                 ("ops", ctypes.c_uint64)]
 
 
+class MixStats(ctypes.Structure):
+    """hs_mix_stats (crates/hardshell-cuda/src/mixed.rs:36-47 MixStats)."""
+    _fields_ = [("total", ctypes.c_uint64), ("predicted", ctypes.c_uint64), ("top", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
+
+
+MIXER_FN = ctypes.CFUNCTYPE(ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(MixStats))
+MIX_NONE = 0xFFFFFFFF   # a mixed table without a prediction: the weights max(1, w)
+MIX_PLAIN = 0xFFFFFFFE  # the table of GPT-2 alone
+
 INTERVAL_DTYPE = np.dtype([("symbol", "<u4"), ("is_last", "<u4"), ("start", "<u8"), ("freq", "<u8"),
                            ("reserved", "<u8")])
 
@@ -89,6 +99,8 @@ def lib() -> ctypes.CDLL:
     L.hs_batch_gpu_bytes.restype = u64
     L.hs_batch_run_coded.argtypes = [vp, vp, vp, vp, vp, u32, u32, vp]
     L.hs_batch_run_weights.argtypes = [vp, vp, vp, u32, vp]
+    L.hs_batch_run_coded_mixed.argtypes = [vp, vp, vp, vp, vp, vp, u32, u32, MIXER_FN, vp, vp]
+    L.hs_batch_run_coded_dual.argtypes = [vp, vp, vp, vp, vp, u32, u32, MIXER_FN, vp, vp, vp]
     L.hs_batch_stream_len.argtypes = [vp, u32, ctypes.POINTER(ctypes.c_uint64)]
     L.hs_batch_room.argtypes = [vp, u32, ctypes.POINTER(ctypes.c_uint64)]
     L.hs_batch_truncate.argtypes = [vp, u32, ctypes.c_uint64]
@@ -324,6 +336,63 @@ class CudaBatch:
         out = np.zeros(n, dtype=INTERVAL_DTYPE)
         _check(lib().hs_batch_run_coded(self.h, _p(s), _p(t), _p(k), _p(v), n, freq_bits, _p(out)))
         return out
+
+    @staticmethod
+    def _mixer(mixer, caught: list):
+        """The C callback of a Python mixer(input, total, predicted, top) -> q. An exception in the
+        mixer gives q = 0, which fails the call; the caller raises it again."""
+
+        def fn(_user, i, st):
+            try:
+                return int(mixer(int(i), int(st[0].total), int(st[0].predicted), int(st[0].top)))
+            except BaseException as e:  # noqa: BLE001 - re-raised by the caller
+                caught.append(e)
+                return 0
+
+        return MIXER_FN(fn)
+
+    def run_coded_mixed(self, slots, tokens, kinds, values, tables, freq_bits: int, mixer) -> np.ndarray:
+        """CudaBatch::run_coded_mixed: the answers in the table that tables[i] names (a predicted
+        token, MIX_NONE or MIX_PLAIN). mixer(input, total, predicted, top) gives q for each input
+        with a predicted token, in input order."""
+        s = np.ascontiguousarray(slots, dtype=np.uint32)
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        k = np.ascontiguousarray(kinds, dtype=np.uint32)
+        v = np.ascontiguousarray(values, dtype=np.uint64)
+        tb = np.ascontiguousarray(tables, dtype=np.uint32)
+        n = s.size
+        if not (t.size == k.size == v.size == tb.size == n):
+            raise HardShellError(HS_LENGTH_MISMATCH, "the inputs, queries and tables differ in length")
+        out = np.zeros(n, dtype=INTERVAL_DTYPE)
+        caught: list = []
+        cb = self._mixer(mixer, caught)
+        rc = lib().hs_batch_run_coded_mixed(self.h, _p(s), _p(t), _p(k), _p(v), _p(tb), n, freq_bits, cb, None,
+                                            _p(out))
+        if caught:
+            raise caught[0]
+        _check(rc)
+        return out
+
+    def run_coded_dual(self, slots, tokens, coded, predictions, freq_bits: int, mixer):
+        """CudaBatch::run_coded_dual: (intervals of coded[i] in the table of GPT-2 alone, in the mixed
+        table of predictions[i]); a prediction is a token or MIX_NONE."""
+        s = np.ascontiguousarray(slots, dtype=np.uint32)
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        c = np.ascontiguousarray(coded, dtype=np.uint32)
+        pr = np.ascontiguousarray(predictions, dtype=np.uint32)
+        n = s.size
+        if not (t.size == c.size == pr.size == n):
+            raise HardShellError(HS_LENGTH_MISMATCH, "the inputs, tokens and predictions differ in length")
+        plain = np.zeros(n, dtype=INTERVAL_DTYPE)
+        mixed = np.zeros(n, dtype=INTERVAL_DTYPE)
+        caught: list = []
+        cb = self._mixer(mixer, caught)
+        rc = lib().hs_batch_run_coded_dual(self.h, _p(s), _p(t), _p(c), _p(pr), n, freq_bits, cb, None, _p(plain),
+                                           _p(mixed))
+        if caught:
+            raise caught[0]
+        _check(rc)
+        return plain, mixed
 
     def run_weights(self, slots, tokens) -> np.ndarray:
         s = np.ascontiguousarray(slots, dtype=np.uint32)

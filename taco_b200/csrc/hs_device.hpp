@@ -59,6 +59,20 @@ struct RowInfo {
     uint64_t value;
 };
 
+// The table words of the mixed coder op (crates/hardshell-cuda/src/mixed.rs:31,104): a row
+// without a prediction (weights max(1, w)) and a plain row (the weights of GPT-2 alone).
+constexpr uint32_t MIX_NONE = 0xFFFFFFFFu;
+constexpr uint32_t MIX_PLAIN = 0xFFFFFFFEu;
+
+// The mix record of one row (mixed.rs:60-90 mix_record): the table word p (a predicted token,
+// MIX_NONE or MIX_PLAIN); for a token, the shift k, the factor m = 2^16 - q and the mixed
+// weight wp = max(1, (R * q) >> k) of p. The weight of every other symbol is
+// max(1, (w * m) >> k).
+struct MixRow {
+    uint32_t p, k, m, pad;
+    uint64_t wp, pad2;
+};
+
 // The range decoder state of one coded block on the device (crates/taco-coder/src/decoder.rs
 // Decoder: code, range, the next byte `pos` of its input payload[base .. base + len)), and
 // whether an interval failed to hold its target.

@@ -1037,6 +1037,353 @@ __global__ void k_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int
     }
 }
 
+// ---- the mixed coder op of the profile logs (crates/hardshell-cuda/src/mixed.rs:1-20) ----
+
+// floor(t * spare / W) for 0 < t <= W (so the quotient is at most spare < 2^32): the double
+// estimate is within one or two of it, and exact 128-bit products put it right.
+__device__ __forceinline__ uint64_t mix_fdiv(uint64_t t, uint64_t spare, uint64_t W, double ratio) {
+    uint64_t q = (uint64_t)((double)t * ratio);
+    q = q < spare ? q : spare;
+    const u128 x = (u128)t * spare;
+    for (int k = 0; k < 8 && (u128)q * W > x; k++) q--;
+    for (int k = 0; k < 8 && (u128)(q + 1) * W <= x; k++) q++;
+    return q;
+}
+
+// One block per row, on the d16/tmax output of the logits GEMM as k_coder. Every GPT-2 weight
+// is table[min(d, last)] for the symbol's distance d from the row max, and so is every mixed
+// weight of a symbol other than the prediction p: g(d) = max(1, (table[d] * m) >> k) with the
+// row's mix record (taco-match mixer.rs:491-516 apply), max(1, table[d]) without a prediction
+// (mixer.rs:265-269), table[d] for a plain row. g does not increase with d, because the table
+// does not. Pass 1 counts the symbols at each distance.
+//
+// Phase 0, the statistics of the GPT-2 weights (mixed.rs step 1): out = {W, w[p] (0 for a table
+// word), top}, top the lowest id at a distance <= head (the first largest weight, table[0]).
+// Phase 1: p leaves its bin; W' = sum over d of count[d] g(d) + w'[p], F[d] = 1 + floor(g(d)
+// spare / W') and f_p = 1 + floor(w'[p] spare / W') (freq.rs:103-157 from_weights). The largest
+// mixed weight is max(g(dmin), w'[p]), dmin the nearest distance of the other symbols. The
+// largest symbol (the lowest id on a tie) is p if w'[p] is the largest weight, or the lowest
+// other symbol at a distance <= gh (the last distance with g(d) == g(dmin)) if g(dmin) is and
+// that symbol is lower. An encode or decode query is then answered as in k_coder.
+__global__ void __launch_bounds__(CODER_THREADS) k_coder_mix(const uint16_t* d16, int ldd, const int64_t* tmax,
+                                                             int ldt, int tsh, int R, int V, const uint64_t* table,
+                                                             int tlen, int head, uint32_t bits, const RowInfo* rows,
+                                                             const MixRow* mix, int phase, uint64_t* out) {
+    extern __shared__ __align__(16) uint32_t F[];  // counts, then F[d] of the distances that occur
+    __shared__ int64_t red[32];
+    __shared__ uint64_t redu[32];
+    __shared__ uint64_t wsum[CODER_WARPS];
+    __shared__ uint64_t steps[CODER_WARPS][CODER_MAX_STEPS];
+    const int r = blockIdx.x;
+    if (r >= R) return;
+    const uint16_t* dr = d16 + (size_t)r * ldd;
+    const int64_t* tr = tmax + (size_t)r * ldt;
+    const int VT = (V + (1 << tsh) - 1) >> tsh;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int32_t last = tlen - 1;
+    const uint64_t total = 1ULL << bits;
+    const uint64_t spare = total - (uint64_t)V;
+    const int ng = (V + 7) / 8;
+    const MixRow mr = mix[r];
+    const bool has_p = mr.p < (uint32_t)V;
+    const int p = has_p ? (int)mr.p : -1;
+    for (int j = threadIdx.x; j < tlen; j += CODER_THREADS) F[j] = 0;
+    int64_t mx = INT64_MIN;
+    for (int t = threadIdx.x; t < VT; t += CODER_THREADS) mx = tr[t] > mx ? tr[t] : mx;
+    mx = block_max64(mx, red);  // (its barriers also order the clearing of F)
+    auto tile_off = [&](int v0) -> int32_t {
+        const int64_t o = mx - tr[v0 >> tsh];
+        return o < (int64_t)last ? (int32_t)o : last;
+    };
+    // The distances of the 8 symbols of group gi, two per word: min(off + d, last) as a
+    // saturating halfword add and a halfword min (as k_coder). The row stride is a multiple of 8,
+    // so the last group loads whole; its halfwords past V are not symbols.
+    const uint32_t last2 = (uint32_t)last * 0x10001u;
+    auto group_dist = [&](int gi, uint32_t (&pd)[4]) {
+        const int v0 = 8 * gi;
+        const uint4 raw = *reinterpret_cast<const uint4*>(dr + v0);
+        const uint32_t off2 = (uint32_t)tile_off(v0) * 0x10001u;
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int k = 0; k < 4; k++) pd[k] = __vminu2(__vaddus2(u[k], off2), last2);
+    };
+    // Bit i: symbol 8 gi + i is at a distance <= lim (lim2 = lim in both halfwords).
+    auto near_mask = [&](const uint32_t (&pd)[4], uint32_t lim2) -> uint32_t {
+        uint32_t nm = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t c = __vcmpleu2(pd[k], lim2);
+            nm |= ((c & 1u) << (2 * k)) | (((c >> 16) & 1u) << (2 * k + 1));
+        }
+        return nm;
+    };
+    // Pass 1: the counts, and in phase 0 the lowest symbol at a distance <= head.
+    const int32_t hd = head < last ? head : last;
+    const uint32_t head2 = (uint32_t)hd * 0x10001u;
+    int best = V;
+    for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
+        uint32_t pd[4];
+        group_dist(gi, pd);
+        const int v0 = 8 * gi;
+        const uint32_t valid = V - v0 >= 8 ? 0xFFu : (1u << (V - v0)) - 1;
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+            if (valid >> i & 1u) atomicAdd(&F[(pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu], 1u);
+        if (phase == 0 && best == V) {
+            const uint32_t nm = near_mask(pd, head2) & valid;
+            if (nm) best = v0 + __ffs(nm) - 1;
+        }
+    }
+    int32_t d_p = 0;
+    if (has_p) {
+        const int32_t dd = tile_off(p) + (int32_t)dr[p];
+        d_p = dd < last ? dd : last;
+    }
+    if (phase == 1 && has_p && threadIdx.x == 0) atomicSub(&F[d_p], 1u);
+    __syncthreads();  // the counts are complete
+    if (phase == 0) {
+        uint64_t W = 0;  // < 2^16 * 2^40
+        for (int j = threadIdx.x; j < tlen; j += CODER_THREADS) W += (uint64_t)F[j] * table[j];
+        W = block_sum64(W, redu);
+        const int top = (int)-block_max64(-(int64_t)best, red);
+        if (threadIdx.x == 0) {
+            out[3 * (size_t)r] = W;
+            out[3 * (size_t)r + 1] = has_p ? table[d_p] : 0;
+            out[3 * (size_t)r + 2] = W == 0 ? 0 : (uint64_t)top;
+        }
+        return;
+    }
+    const bool plain = mr.p == MIX_PLAIN;
+    const uint64_t mm = has_p ? (uint64_t)mr.m : 1;
+    const uint32_t kk = has_p ? mr.k : 0;
+    auto g = [&](int32_t d) -> uint64_t {
+        const uint64_t t = table[d];
+        if (plain) return t;
+        const uint64_t x = (uint64_t)(((u128)t * mm) >> kk);  // < 2^62 for t <= R (mixed.rs:17-19)
+        return x > 1 ? x : 1;
+    };
+    // The nearest and the farthest distance of the other symbols.
+    int32_t lo = INT32_MAX, hi = -1;
+    for (int j = threadIdx.x; j < tlen; j += CODER_THREADS)
+        if (F[j]) {
+            lo = j < lo ? j : lo;
+            hi = j > hi ? j : hi;
+        }
+    lo = (int32_t)-block_max64(-(int64_t)lo, red);
+    hi = (int32_t)block_max64(hi, red);
+    const bool has_o = hi >= 0;
+    const uint64_t wpm = has_p ? mr.wp : 0;
+    uint64_t W = 0;  // W' < 2^63 (mixed.rs:17-19)
+    if (has_o)
+        for (int j = lo + threadIdx.x; j <= hi; j += CODER_THREADS)
+            if (F[j]) W += (uint64_t)F[j] * g(j);
+    W = block_sum64(W, redu) + wpm;
+    const bool all_zero = W == 0;  // a plain row whose weights are all 0: every weight counts 1
+    const uint64_t Wo = has_o ? g(lo) : 0;
+    int32_t gh = -1;
+    if (has_o)
+        for (int j = lo + threadIdx.x; j <= last; j += CODER_THREADS)
+            if (g(j) == Wo) gh = j > gh ? j : gh;
+    gh = (int32_t)block_max64(gh, red);
+    const uint64_t Wmax = Wo > wpm ? Wo : wpm;
+    const bool cand_p = has_p && wpm == Wmax;
+    const bool cand_o = has_o && Wo == Wmax;
+    const uint32_t f_flat = (uint32_t)(1 + spare / (uint64_t)V);
+    uint64_t f_p = 0, sum_f;
+    if (all_zero) {
+        sum_f = (uint64_t)V * f_flat;
+    } else {
+        const double ratio = (double)spare / (double)W;
+        sum_f = 0;
+        if (has_o)
+            for (int j = lo + threadIdx.x; j <= hi; j += CODER_THREADS) {
+                const uint32_t c = F[j];
+                if (c) {
+                    const uint32_t f = (uint32_t)(1 + mix_fdiv(g(j), spare, W, ratio));
+                    F[j] = f;
+                    sum_f += (uint64_t)c * f;
+                }
+            }
+        sum_f = block_sum64(sum_f, redu);  // (its barriers also publish F)
+        if (has_p) {
+            f_p = 1 + mix_fdiv(wpm, spare, W, ratio);
+            sum_f += f_p;
+        }
+    }
+    const uint64_t rem = total - sum_f;  // the remainder goes to the largest symbol (freq.rs:150)
+    // f of a symbol at distance d other than p (a bin that p alone occupied holds 0).
+    auto fd = [&](uint32_t d) -> uint64_t { return all_zero ? f_flat : F[d]; };
+    const RowInfo q = rows[r];
+    if (q.kind == 0) {
+        // Encode: start = sum of f below the token (+ rem if the largest symbol is below it).
+        // The sum takes every symbol below s from its bin, then puts p right; nb counts the
+        // symbols below s at a distance <= gh (p among them, if it is one).
+        const int s = (int)q.value;
+        const int gs = s / 8;
+        uint64_t pre = 0, nb = 0;
+        const uint32_t gh2 = (uint32_t)(gh < 0 ? 0 : gh) * 0x10001u;
+        for (int gi = threadIdx.x; gi < gs; gi += CODER_THREADS) {
+            uint32_t pd[4];
+            group_dist(gi, pd);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                pre += fd(pd[k] & 0xFFFFu) + fd(pd[k] >> 16);
+                nb += __popc(__vcmpleu2(pd[k], gh2)) >> 4;
+            }
+        }
+        if (threadIdx.x == CODER_THREADS - 1 && 8 * gs < s) {
+            uint32_t pd[4];
+            group_dist(gs, pd);
+            const uint32_t nm = near_mask(pd, gh2);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (8 * gs + i < s) {
+                    pre += fd((pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
+                    nb += nm >> i & 1u;
+                }
+        }
+        pre = block_sum64(pre, redu);
+        nb = block_sum64(nb, redu);
+        if (threadIdx.x == 0) {
+            uint64_t start, freq;
+            if (all_zero) {  // every weight is 1 and symbol 0 is the largest
+                start = (uint64_t)s * f_flat + (s > 0 ? rem : 0);
+                freq = f_flat + (s == 0 ? rem : 0);
+            } else {
+                if (has_p && p < s) {
+                    pre = pre - F[d_p] + f_p;
+                    if (d_p <= gh) nb--;
+                }
+                const bool s_is_p = has_p && s == p;
+                const int32_t ds0 = tile_off(s) + (int32_t)dr[s];
+                const int32_t ds = ds0 < last ? ds0 : last;
+                const bool lt = (cand_p && p < s) || (cand_o && nb > 0);
+                const bool cs = s_is_p ? cand_p : (cand_o && ds <= gh);
+                start = pre + (lt ? rem : 0);
+                freq = (s_is_p ? f_p : (uint64_t)F[ds]) + (!lt && cs ? rem : 0);
+            }
+            out[3 * (size_t)r] = (uint64_t)s;
+            out[3 * (size_t)r + 1] = start;
+            out[3 * (size_t)r + 2] = freq;
+        }
+        return;
+    }
+    // Decode. The largest symbol first: the lowest other symbol at a distance <= gh (each thread
+    // scans its groups in order, so its first hit is its lowest), or p.
+    int largest = 0;
+    if (!all_zero) {
+        int lo_o = V;
+        if (cand_o) {
+            const uint32_t gh2 = (uint32_t)gh * 0x10001u;
+            for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
+                uint32_t pd[4];
+                group_dist(gi, pd);
+                const int v0 = 8 * gi;
+                uint32_t nm = near_mask(pd, gh2) & (V - v0 >= 8 ? 0xFFu : (1u << (V - v0)) - 1);
+                if (p >= v0 && p < v0 + 8) nm &= ~(1u << (p - v0));
+                if (nm) {
+                    lo_o = v0 + __ffs(nm) - 1;
+                    break;
+                }
+            }
+            lo_o = (int)-block_max64(-(int64_t)lo_o, red);
+        }
+        largest = cand_p && p < lo_o ? p : lo_o;
+    }
+    // f of one group of 8 symbols (0 past V).
+    auto group_f = [&](int gi, uint32_t (&f)[8]) {
+        uint32_t pd[4];
+        group_dist(gi, pd);
+        const int v0 = 8 * gi;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int v = v0 + i;
+            const uint32_t d = (pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+            f[i] = v >= V ? 0u : (uint32_t)(v == p ? f_p : fd(d));
+        }
+    };
+    // The walk of k_coder: warp -> step -> lane -> symbol. Pass 2: per warp and step (32
+    // groups), the sum of f.
+    const int gpw = (ng + CODER_WARPS - 1) / CODER_WARPS;
+    const int ga = min(ng, w * gpw), gb = min(ng, ga + gpw);
+    const int nsteps = (gb - ga + 31) / 32;
+    uint64_t wtotal = 0;
+    for (int k = 0; k < nsteps; k++) {
+        const int gi = ga + 32 * k + lane;
+        uint64_t s = 0;
+        if (gi < gb) {
+            uint32_t f[8];
+            group_f(gi, f);
+#pragma unroll
+            for (int i = 0; i < 8; i++) s += f[i];
+        }
+        s = warp_sum64(s);
+        if (lane == 0) steps[w][k] = s;
+        wtotal += s;
+    }
+    if (lane == 0) wsum[w] = wtotal;
+    __syncthreads();
+    uint64_t before = 0;
+    for (int i = 0; i < w; i++) before += wsum[i];
+    const int a = 8 * ga, b = min(V, 8 * gb);
+    // A(v) = sum of f below v + (rem if v > largest): the start of symbol v.
+    auto adj = [&](int v) -> uint64_t { return (uint64_t)v > (uint64_t)largest ? rem : 0; };
+    const uint64_t Aa = before + adj(a);
+    const uint64_t Ab = b >= V ? total : before + wtotal + adj(b);
+    const bool mine = a < b && q.value >= Aa && q.value < Ab;
+    if (!mine) return;
+    // Level 1: the step. Lane k holds the exclusive prefix of the step sums.
+    uint64_t st = lane < nsteps ? steps[w][lane] : 0;
+    uint64_t incl = st;
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint64_t excl = incl - st;
+    int kstep;
+    {
+        const int v0 = 8 * (ga + 32 * lane);
+        const bool ok = lane < nsteps && before + excl + adj(v0) <= q.value;
+        kstep = 31 - __clz(__ballot_sync(0xffffffffu, ok));
+    }
+    const uint64_t step_base = before + __shfl_sync(0xffffffffu, excl, kstep);
+    // Level 2: the lane (group of 8) within the step.
+    const int gi = ga + 32 * kstep + lane;
+    uint32_t f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (gi < gb) group_f(gi, f);
+    uint64_t gsum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) gsum += f[i];
+    uint64_t ginc = gsum;
+    for (int o = 1; o < 32; o <<= 1) {
+        uint64_t t = __shfl_up_sync(0xffffffffu, ginc, o);
+        if (lane >= o) ginc += t;
+    }
+    const uint64_t gstart = step_base + ginc - gsum;
+    int owner;
+    {
+        const bool ok = gi < gb && gstart + adj(8 * gi) <= q.value;
+        owner = 31 - __clz(__ballot_sync(0xffffffffu, ok));
+    }
+    if (lane != owner) return;
+    // Level 3: the symbol within the group (this lane).
+    uint64_t acc = gstart;
+#pragma unroll 1
+    for (int i = 0; i < 8; i++) {
+        const int v = 8 * gi + i;
+        if (v >= V) break;
+        const uint64_t start = acc + adj(v);
+        const uint64_t freq = f[i] + (v == largest ? rem : 0);
+        if (q.value >= start && q.value < start + freq) {
+            out[3 * (size_t)r] = (uint64_t)v;
+            out[3 * (size_t)r + 1] = start;
+            out[3 * (size_t)r + 2] = freq;
+            return;
+        }
+        acc += f[i];
+    }
+}
+
 }  // namespace
 
 cudaError_t configure_core_kernels() {
@@ -1046,6 +1393,8 @@ cudaError_t configure_core_kernels() {
     e = cudaFuncSetAttribute(k_attention_vec<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsmem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_attention_vec<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsmem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_coder_mix, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_coder, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
 }
@@ -1127,6 +1476,14 @@ void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, in
     if (R <= 0) return;
     k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, tsh, R, V, table, tlen, head, bits,
                                                          rows, out);
+}
+
+void launch_coder_mix(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
+                      const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows,
+                      const MixRow* mix, int phase, uint64_t* out, cudaStream_t st) {
+    if (R <= 0) return;
+    k_coder_mix<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, tsh, R, V, table, tlen, head, bits,
+                                                             rows, mix, phase, out);
 }
 
 void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,

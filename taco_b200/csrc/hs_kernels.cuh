@@ -111,6 +111,14 @@ void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, in
                   const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
                   cudaStream_t st);
 
+// The mixed coder op of the profile logs, in two phases around a host step. Phase 0 (the stats
+// kernel): out = {W, w[p], top} of the GPT-2 weights of each row, p = mix[r].p. Phase 1: the
+// interval of each row's query in the table from_weights(w', bits) of the mixed weights w' that
+// mix[r] describes. One block per row, as launch_coder.
+void launch_coder_mix(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
+                      const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows,
+                      const MixRow* mix, int phase, uint64_t* out, cudaStream_t st);
+
 // The full weights of each row (run_weights): w[r, v] = table[min(max - logit, last)].
 void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                     const uint64_t* table, int tlen, uint64_t* w, cudaStream_t st);

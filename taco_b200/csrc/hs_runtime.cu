@@ -231,6 +231,14 @@ struct hs_batch {
     int* d_rowlist = nullptr;        // the other rows of the pass
     int n_groups = 0, n_rowlist = 0;
     bool v_scatter = false;  // some 32-row group of the pass is not a transposed v run
+    // The mixed coder op (made on its first use): the mix records of a pass, the statistics of
+    // its rows and the intervals of GPT-2 alone (run_coded_dual), with pinned host copies.
+    MixRow* d_mix = nullptr;
+    uint64_t* d_stats = nullptr;
+    uint64_t* d_plain = nullptr;
+    MixRow* h_mix = nullptr;
+    uint64_t* h_stats = nullptr;
+    uint64_t* h_plain = nullptr;
     uint64_t bytes = 0;
     // Per-op device time (CUDA events on the batch stream) when profiling is on.
     bool profiling = false;
@@ -261,6 +269,9 @@ struct hs_batch {
         if (h_intervals_base) cudaFreeHost(h_intervals_base);
         if (h_groups_base) cudaFreeHost(h_groups_base);
         if (h_rowlist_base) cudaFreeHost(h_rowlist_base);
+        if (h_mix) cudaFreeHost(h_mix);
+        if (h_stats) cudaFreeHost(h_stats);
+        if (h_plain) cudaFreeHost(h_plain);
     }
 };
 
@@ -604,9 +615,34 @@ void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* token
     flush();
 }
 
-// Runs the passes; with `out` the coder answers (3 u64 per input), else the weights.
+// The host side of a mixed call (crates/hardshell-cuda/src/batch/mixed.rs:25-35 Mixing): the
+// table word of each input, the host mixer, and for run_coded_dual the intervals of GPT-2 alone.
+struct MixCall {
+    const uint32_t* tables;
+    hs_mixer_fn fn;
+    void* user;
+    hs_interval* plain;
+};
+
+// The mix record of a row with a predicted token p (crates/hardshell-cuda/src/mixed.rs:60-90
+// mix_record, the rule 5 values of taco_match::Mixer apply): R = max(W - w[p], 1), m = 2^16 - q,
+// k = max(0, bitlen(R) + 16 - 62), and w'[p] = max(1, (R * q) >> k) (below 2^62).
+int mix_record(const hs_mix_stats& st, uint32_t p, uint32_t q, MixRow* out) {
+    if (q == 0 || q >= (1u << 16)) return fail(HS_UNSUPPORTED, "the mixer probability q must be in 1..=65535");
+    if (st.predicted > st.total) return fail(HS_UNSUPPORTED, "the weight of the prediction is above the sum");
+    const uint64_t r = std::max<uint64_t>(st.total - st.predicted, 1);
+    const int bitlen = 64 - __builtin_clzll(r);
+    const uint32_t k = bitlen + 16 > 62 ? (uint32_t)(bitlen + 16 - 62) : 0;
+    const unsigned __int128 x = ((unsigned __int128)r * q) >> k;
+    *out = MixRow{p, k, (1u << 16) - q, 0, std::max<uint64_t>((uint64_t)x, 1), 0};
+    return HS_OK;
+}
+
+// Runs the passes; with `out` the coder answers (3 u64 per input), else the weights. With `mix`
+// the answers are those of the mixed coder op, pass by pass with the host mixer between the
+// statistics and the mixed table.
 int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds, const uint64_t* values,
-        uint32_t n, uint32_t bits, hs_interval* out, uint64_t* wout) {
+        uint32_t n, uint32_t bits, hs_interval* out, uint64_t* wout, const MixCall* mix = nullptr) {
     hs_model* m = b->model;
     const ModelConsts& c = m->c;
     for (uint32_t i = 0; i < n; i++) {
@@ -625,12 +661,30 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             if (!ok) return fail(HS_UNSUPPORTED, "a coder token or target is out of range");
         }
     }
+    if (mix) {
+        for (uint32_t i = 0; i < n; i++) {
+            const uint32_t t = mix->tables[i];
+            if (t >= (uint32_t)c.V && t != MIX_NONE && t != MIX_PLAIN)
+                return fail(HS_UNSUPPORTED, "a predicted token is out of range");
+        }
+    }
     int rc = set_device(m->dev);
     if (rc) return rc;
     // An earlier failed API call of this thread (already reported to its caller) leaves its code
     // behind; clear it, so that the launch checks below report only this call's own errors. A
     // device fault is sticky and still shows.
     cudaGetLastError();
+    if (mix && !b->d_mix) {
+        // The buffers of the mixed coder op: made on the first mixed call.
+        const size_t Rc = (size_t)b->Rcap;
+        if ((rc = dalloc(&b->d_mix, Rc, b->owned)) || (rc = dalloc(&b->d_stats, 3 * Rc, b->owned)) ||
+            (rc = dalloc(&b->d_plain, 3 * Rc, b->owned)))
+            return rc;
+        b->bytes += Rc * (sizeof(MixRow) + 48);
+        CK(cudaMallocHost(&b->h_mix, sizeof(MixRow) * Rc));
+        CK(cudaMallocHost(&b->h_stats, sizeof(uint64_t) * 3 * Rc));
+        CK(cudaMallocHost(&b->h_plain, sizeof(uint64_t) * 3 * Rc));
+    }
     if (wout && !b->weights) {
         // The weights buffer of run_weights: made on the first use (vocab u64 per row).
         if ((rc = dalloc(&b->weights, (size_t)b->Rcap * c.V, b->owned))) return rc;
@@ -669,7 +723,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     };
     for (size_t k = 0; k < passes.size(); k++) {
         const auto& pass = passes[k];
-        if (out && k >= 2 && (rc = answers_out(k - 2))) return rc;
+        if (out && !mix && k >= 2 && (rc = answers_out(k - 2))) return rc;
         use_half(k);
         int R = (int)pass.size();
         for (int r = 0; r < R; r++) {
@@ -696,7 +750,58 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         std::unique_ptr<ProfScope> pass_scope(new ProfScope(b, OP_PASS, (uint64_t)R));
         rc = forward(b, R);
         if (rc) return rc;
-        if (out) {
+        if (out && mix) {
+            // The mixed coder op (batch/mixed.rs:145-180 mix_pass): the statistics of the rows,
+            // read back; the host mixer for each input with a predicted token, in input order; the
+            // mix records up; then the coder of GPT-2 alone (run_coded_dual) and the mixed coder.
+            for (int r = 0; r < R; r++) {
+                const long in = pass[r].input;
+                b->h_mix[r] = MixRow{in >= 0 ? mix->tables[in] : MIX_NONE, 0, 0, 0, 0, 0};
+            }
+            CK(cudaMemcpyAsync(b->d_mix, b->h_mix, sizeof(MixRow) * R, cudaMemcpyHostToDevice, b->stream));
+            {
+                ProfScope p(b, OP_CODER, 0);
+                launch_coder_mix(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
+                                 m->logits_head, bits, b->d_rows, b->d_mix, 0, b->d_stats, b->stream);
+            }
+            CK(cudaMemcpyAsync(b->h_stats, b->d_stats, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost, b->stream));
+            if ((rc = check_device_error(b))) return rc;
+            for (int r = 0; r < R; r++) {
+                const long in = pass[r].input;
+                const uint32_t t = b->h_mix[r].p;
+                if (in < 0 || t >= (uint32_t)c.V) continue;
+                const hs_mix_stats st{b->h_stats[3 * r], b->h_stats[3 * r + 1], (uint32_t)b->h_stats[3 * r + 2], 0};
+                const uint32_t q = mix->fn(mix->user, (uint32_t)in, &st);
+                if ((rc = mix_record(st, t, q, &b->h_mix[r]))) return rc;
+            }
+            CK(cudaMemcpyAsync(b->d_mix, b->h_mix, sizeof(MixRow) * R, cudaMemcpyHostToDevice, b->stream));
+            {
+                ProfScope p(b, OP_CODER, 0);
+                if (mix->plain)
+                    launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
+                                 m->logits_head, bits, b->d_rows, b->d_plain, b->stream);
+                launch_coder_mix(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
+                                 m->logits_head, bits, b->d_rows, b->d_mix, 1, b->intervals, b->stream);
+            }
+            pass_scope.reset();
+            if (mix->plain)
+                CK(cudaMemcpyAsync(b->h_plain, b->d_plain, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
+                                   b->stream));
+            CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
+                               b->stream));
+            CK(cudaEventRecord(b->pass_done[k & 1], b->stream));
+            if ((rc = answers_out(k))) return rc;
+            for (int r = 0; mix->plain && r < R; r++) {
+                const long in = pass[r].input;
+                if (in < 0) continue;
+                hs_interval& iv = mix->plain[in];
+                iv.symbol = (uint32_t)b->h_plain[3 * r];
+                iv.start = b->h_plain[3 * r + 1];
+                iv.freq = b->h_plain[3 * r + 2];
+                iv.is_last = iv.symbol + 1 == (uint32_t)c.V;
+                iv.reserved = 0;
+            }
+        } else if (out) {
             {
                 ProfScope p(b, OP_CODER, 0);
                 launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len, m->logits_head, bits, b->d_rows,
@@ -727,7 +832,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     rc = check_device_error(b);
     if (rc) return rc;
     if (b->profiling) prof_collect(b);
-    if (out) {
+    if (out && !mix) {
         for (size_t k = passes.size() >= 2 ? passes.size() - 2 : 0; k < passes.size(); k++)
             if ((rc = answers_out(k))) return rc;
     }
@@ -1346,6 +1451,29 @@ int hs_batch_run_coded(hs_batch* b, const uint32_t* slots, const uint32_t* token
                        const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out) {
     if (!b || (n && (!slots || !tokens || !kinds || !values || !out))) return fail(HS_BAD_ARGUMENT, "null argument");
     return run(b, slots, tokens, kinds, values, n, freq_bits, out, nullptr);
+}
+
+int hs_batch_run_coded_mixed(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds,
+                             const uint64_t* values, const uint32_t* tables, uint32_t n, uint32_t freq_bits,
+                             hs_mixer_fn mixer, void* user, hs_interval* out) {
+    if (!b || !mixer || (n && (!slots || !tokens || !kinds || !values || !tables || !out)))
+        return fail(HS_BAD_ARGUMENT, "null argument");
+    const MixCall mc{tables, mixer, user, nullptr};
+    return run(b, slots, tokens, kinds, values, n, freq_bits, out, nullptr, &mc);
+}
+
+int hs_batch_run_coded_dual(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* coded,
+                            const uint32_t* predictions, uint32_t n, uint32_t freq_bits, hs_mixer_fn mixer,
+                            void* user, hs_interval* plain_out, hs_interval* mixed_out) {
+    if (!b || !mixer || (n && (!slots || !tokens || !coded || !predictions || !plain_out || !mixed_out)))
+        return fail(HS_BAD_ARGUMENT, "null argument");
+    // batch/mixed.rs prediction_words: a token or none (no plain word).
+    for (uint32_t i = 0; i < n; i++)
+        if (predictions[i] == MIX_PLAIN) return fail(HS_UNSUPPORTED, "a predicted token is out of range");
+    const std::vector<uint32_t> kinds(n, 0);
+    const std::vector<uint64_t> values(coded, coded + n);
+    const MixCall mc{predictions, mixer, user, plain_out};
+    return run(b, slots, tokens, kinds.data(), values.data(), n, freq_bits, mixed_out, nullptr, &mc);
 }
 
 int hs_batch_stream_len(hs_batch* b, uint32_t slot, uint64_t* len) {
