@@ -20,7 +20,9 @@ roofline = the kernel with the largest share of the pass time: algorithmic int8 
          measured HBM copy bandwidth (MEASURED_PEAKS.json); `rooflines` has every kernel class;
 cpu_baseline = the CPU oracle's fast path (a C++ restatement of the reference CPU engine) on a
          bounded sample of the same windows, all host threads, rank 0 at N = 1.
-Extra fields: the GEMM microbench and the unfold decode step.
+Extra fields: the GEMM microbench, the unfold decode step, the unfold of
+coded blocks with the range decoder on the device, and the encoder op of the profile logs
+(run_coded_dual). `--only fold_dual` runs the last alone on --windows windows (a profiling case).
 """
 
 from __future__ import annotations
@@ -59,6 +61,7 @@ def parse_args():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-peak", action="store_true", help="skip the int8 peak measurement (profiling runs)")
+    ap.add_argument("--only", default="", choices=["", "fold_dual"], help="run one extra alone (profiling runs)")
     return ap.parse_args()
 
 
@@ -296,6 +299,13 @@ def main():
     slots, inputs, coded = window_rows(windows, eot)
     kinds = np.zeros(slots.size, np.uint32)
     step_bytes = int(lens[coded.astype(np.int64)].sum())
+    if args.only == "fold_dual":
+        dev = B.CudaDevice(local)
+        model = B.CudaModel(dev, model_bytes)
+        print(json.dumps({"fold_dual": fold_dual(B, model, windows, lens, eot, sample=args.windows)}))
+        model.close()
+        dev.close()
+        return 0
 
     peak = measured_int8_peak_tops(local) if rank == 0 and not args.no_peak else None
     dev = B.CudaDevice(local)
@@ -396,6 +406,7 @@ def main():
         result["gemm_microbench"] = micro
         result["unfold"] = unfold_step(B, model, lens, eot, clock_note=None)
         result["unfold_blocks"] = unfold_blocks(B, model)
+        result["fold_dual"] = fold_dual(B, model, windows, lens, eot)
     if rank == 0:
         if world == 1 and not args.no_cpu:
             threads = args.cpu_threads or os.cpu_count() or 1
@@ -489,6 +500,63 @@ def unfold_blocks(B, model, streams: int = 1024, tokens: int = 256) -> dict:
             "e2e_tokens_per_s": n / wall, "device_tokens_per_s": n / (dev_ms / 1e3),
             "host_loop_e2e_tokens_per_s": n / wall_host, "failed_blocks": int(status.sum()),
             "decoder_ms": round(prof.get("decoder", {"ms": 0.0})["ms"], 3)}
+
+
+def fold_dual(B, model, windows, lens, eot, sample: int = 64) -> dict:
+    """The encoder op of the profile logs (run_coded_dual: the interval of each coded token in the
+    table of GPT-2 alone and in the mixed table of a prediction) on `sample` fold windows, against
+    run_coded on the same rows. The predictions are those of a stand-in match model (the token
+    that followed the last earlier occurrence of the input token in the window); the host mixer is
+    a Python callback (q from the agreement bit), called once per predicted row as the reference's
+    is. Timed by the wall clock around the C-ABI calls (the better of two), with the per-op device
+    time from a third, profiled call; a mixed pass includes its host step (the statistics read
+    back, the mixer calls and the records upload) inside the pass time."""
+    w = windows[:sample]
+    slots, inputs, coded = window_rows(w, eot)
+    preds = np.full(slots.size, B.MIX_NONE, np.uint32)
+    for r in range(w.shape[0]):
+        seen = {}
+        base = r * w.shape[1]
+        for j in range(w.shape[1]):
+            i = base + j
+            p = seen.get(int(inputs[i]))
+            if p is not None:
+                preds[i] = p
+            seen[int(inputs[i])] = int(coded[i])
+    kinds = np.zeros(slots.size, np.uint32)
+    nbytes = int(lens[coded.astype(np.int64)].sum())
+
+    def mixer(i, total, predicted, top):
+        return 52000 if top == preds[i] else 13000
+
+    batch = B.CudaBatch(model, sample, 16384)
+
+    def run(dual: bool):
+        for s in range(sample):
+            batch.reset(s)
+        if dual:
+            return batch.run_coded_dual(slots, inputs, coded, preds, 32, mixer)
+        return batch.run_coded(slots, inputs, kinds, coded, 32)
+
+    plain, mixed = run(True)
+    if not (np.array_equal(plain["symbol"], coded) and np.array_equal(mixed["symbol"], coded)):
+        raise SystemExit("the dual coder op answered the wrong symbols")
+    out = {"windows": sample, "rows": int(slots.size), "predicted_rows": int((preds != B.MIX_NONE).sum())}
+    for name, dual in (("dual", True), ("plain", False)):
+        wall = float("inf")
+        for _ in range(2):
+            t0 = time.perf_counter()
+            run(dual)
+            wall = min(wall, time.perf_counter() - t0)
+        batch.set_profiling(True)
+        run(dual)
+        prof = batch.profile()
+        batch.set_profiling(False)
+        out[name] = {"e2e_MB_per_s": nbytes / wall / 1e6, "device_MB_per_s": nbytes / (prof["pass"]["ms"] / 1e3) / 1e6,
+                     "pass_ms": round(prof["pass"]["ms"], 3), "coder_ms": round(prof["coder"]["ms"], 3),
+                     "coder_launches": prof["coder"]["launches"]}
+    batch.close()
+    return out
 
 
 if __name__ == "__main__":

@@ -1117,22 +1117,62 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder_mix(const uint16_t* d16
         }
         return nm;
     };
-    // Pass 1: the counts, and in phase 0 the lowest symbol at a distance <= head.
+    // Pass 1: the counts, and in phase 0 the lowest symbol at a distance <= head. Whole groups
+    // as k_coder's pass 1 (several 16-byte loads in flight, a group whose tile is clamped counted
+    // at once); the last, partial group by one thread.
     const int32_t hd = head < last ? head : last;
     const uint32_t head2 = (uint32_t)hd * 0x10001u;
+    const int ng_full = V / 8;
     int best = V;
-    for (int gi = threadIdx.x; gi < ng; gi += CODER_THREADS) {
+    auto count_group = [&](int v0, uint4 raw, auto track) {
+        const int32_t off = tile_off(v0);
+        if (off == last) {
+            atomicAdd(&F[last], 8u);
+            if constexpr (decltype(track)::value) best = hd >= last && v0 < best ? v0 : best;
+            return;
+        }
+        const uint32_t off2 = (uint32_t)off * 0x10001u;
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
         uint32_t pd[4];
-        group_dist(gi, pd);
-        const int v0 = 8 * gi;
-        const uint32_t valid = V - v0 >= 8 ? 0xFFu : (1u << (V - v0)) - 1;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            pd[k] = __vminu2(__vaddus2(u[k], off2), last2);
+            atomicAdd(&F[pd[k] & 0xFFFFu], 1u);
+            atomicAdd(&F[pd[k] >> 16], 1u);
+        }
+        if constexpr (decltype(track)::value) {
+            if (v0 < best) {
+                const uint32_t nm = near_mask(pd, head2);
+                if (nm) best = v0 + __ffs(nm) - 1;
+            }
+        }
+    };
+    constexpr int UNROLL = 4;
+    auto pass1 = [&](auto track) {
+        int g0 = threadIdx.x;
+        for (; g0 + (UNROLL - 1) * CODER_THREADS < ng_full; g0 += UNROLL * CODER_THREADS) {
+            uint4 raw[UNROLL];
+#pragma unroll
+            for (int k = 0; k < UNROLL; k++) raw[k] = *reinterpret_cast<const uint4*>(dr + 8 * (g0 + k * CODER_THREADS));
+#pragma unroll
+            for (int k = 0; k < UNROLL; k++) count_group(8 * (g0 + k * CODER_THREADS), raw[k], track);
+        }
+        for (; g0 < ng_full; g0 += CODER_THREADS)
+            count_group(8 * g0, *reinterpret_cast<const uint4*>(dr + 8 * g0), track);
+    };
+    if (phase == 0) pass1(std::true_type{});
+    else pass1(std::false_type{});
+    if (ng_full < ng && threadIdx.x == ng_full % CODER_THREADS) {
+        uint32_t pd[4];
+        group_dist(ng_full, pd);
+        const int v0 = 8 * ng_full;
 #pragma unroll
         for (int i = 0; i < 8; i++)
-            if (valid >> i & 1u) atomicAdd(&F[(pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu], 1u);
-        if (phase == 0 && best == V) {
-            const uint32_t nm = near_mask(pd, head2) & valid;
-            if (nm) best = v0 + __ffs(nm) - 1;
-        }
+            if (v0 + i < V) {
+                const uint32_t d = (pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+                atomicAdd(&F[d], 1u);
+                if (phase == 0 && d <= (uint32_t)hd && v0 + i < best) best = v0 + i;
+            }
     }
     int32_t d_p = 0;
     if (has_p) {
@@ -1215,49 +1255,77 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder_mix(const uint16_t* d16
     auto fd = [&](uint32_t d) -> uint64_t { return all_zero ? f_flat : F[d]; };
     const RowInfo q = rows[r];
     if (q.kind == 0) {
-        // Encode: start = sum of f below the token (+ rem if the largest symbol is below it).
-        // The sum takes every symbol below s from its bin, then puts p right; nb counts the
-        // symbols below s at a distance <= gh (p among them, if it is one).
+        // Encode: start = sum of f below the token (+ rem if the largest symbol is below it), as
+        // k_coder: 8 frequencies per group summed in 32 bits. In p's group, p's slot takes f_p in
+        // place of its bin's F, in 32-bit modular arithmetic: the true sum of 8 distinct symbols is
+        // below 2^32 (every other symbol has f >= 1, and V > 8). `below`: some symbol other than p
+        // below s is at a distance <= gh.
         const int s = (int)q.value;
         const int gs = s / 8;
-        uint64_t pre = 0, nb = 0;
+        const int gp = has_p ? p / 8 : -1;
+        uint64_t pre = 0;
+        bool below = false;
         const uint32_t gh2 = (uint32_t)(gh < 0 ? 0 : gh) * 0x10001u;
-        for (int gi = threadIdx.x; gi < gs; gi += CODER_THREADS) {
-            uint32_t pd[4];
-            group_dist(gi, pd);
+        if (!all_zero) {
+            auto group_sum = [&](int gi, uint4 raw) {
+                const int v0 = 8 * gi;
+                const uint32_t off2 = (uint32_t)tile_off(v0) * 0x10001u;
+                const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+                uint32_t pd[4], gsum = 0, dm = last2;
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                pre += fd(pd[k] & 0xFFFFu) + fd(pd[k] >> 16);
-                nb += __popc(__vcmpleu2(pd[k], gh2)) >> 4;
+                for (int k = 0; k < 4; k++) {
+                    pd[k] = __vminu2(__vaddus2(u[k], off2), last2);
+                    dm = __vminu2(dm, pd[k]);
+                    gsum += F[pd[k] & 0xFFFFu] + F[pd[k] >> 16];
+                }
+                if (gi == gp) {
+                    gsum += (uint32_t)f_p - F[d_p];
+                    below |= (near_mask(pd, gh2) & ~(1u << (p - v0))) != 0;
+                } else {
+                    below |= (int32_t)min(dm & 0xFFFFu, dm >> 16) <= gh;
+                }
+                pre += gsum;
+            };
+            constexpr int UNROLL = 4;
+            int gj = threadIdx.x;
+            for (; gj + (UNROLL - 1) * CODER_THREADS < gs; gj += UNROLL * CODER_THREADS) {
+                uint4 raw[UNROLL];
+#pragma unroll
+                for (int k = 0; k < UNROLL; k++) raw[k] = *reinterpret_cast<const uint4*>(dr + 8 * (gj + k * CODER_THREADS));
+#pragma unroll
+                for (int k = 0; k < UNROLL; k++) group_sum(gj + k * CODER_THREADS, raw[k]);
+            }
+            for (; gj < gs; gj += CODER_THREADS) group_sum(gj, *reinterpret_cast<const uint4*>(dr + 8 * gj));
+            if (threadIdx.x == CODER_THREADS - 1 && 8 * gs < s) {
+                uint32_t pd[4];
+                group_dist(gs, pd);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int v = 8 * gs + i;
+                    if (v < s) {
+                        const uint32_t d = (pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;
+                        if (v == p) {
+                            pre += f_p;
+                        } else {
+                            pre += F[d];
+                            below |= (int32_t)d <= gh;
+                        }
+                    }
+                }
             }
         }
-        if (threadIdx.x == CODER_THREADS - 1 && 8 * gs < s) {
-            uint32_t pd[4];
-            group_dist(gs, pd);
-            const uint32_t nm = near_mask(pd, gh2);
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-                if (8 * gs + i < s) {
-                    pre += fd((pd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
-                    nb += nm >> i & 1u;
-                }
-        }
         pre = block_sum64(pre, redu);
-        nb = block_sum64(nb, redu);
+        below = __syncthreads_or(below) != 0;
         if (threadIdx.x == 0) {
             uint64_t start, freq;
             if (all_zero) {  // every weight is 1 and symbol 0 is the largest
                 start = (uint64_t)s * f_flat + (s > 0 ? rem : 0);
                 freq = f_flat + (s == 0 ? rem : 0);
             } else {
-                if (has_p && p < s) {
-                    pre = pre - F[d_p] + f_p;
-                    if (d_p <= gh) nb--;
-                }
                 const bool s_is_p = has_p && s == p;
                 const int32_t ds0 = tile_off(s) + (int32_t)dr[s];
                 const int32_t ds = ds0 < last ? ds0 : last;
-                const bool lt = (cand_p && p < s) || (cand_o && nb > 0);
+                const bool lt = (cand_p && p < s) || (cand_o && below);
                 const bool cs = s_is_p ? cand_p : (cand_o && ds <= gh);
                 start = pre + (lt ? rem : 0);
                 freq = (s_is_p ? f_p : (uint64_t)F[ds]) + (!lt && cs ? rem : 0);

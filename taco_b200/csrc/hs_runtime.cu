@@ -233,12 +233,22 @@ struct hs_batch {
     bool v_scatter = false;  // some 32-row group of the pass is not a transposed v run
     // The mixed coder op (made on its first use): the mix records of a pass, the statistics of
     // its rows and the intervals of GPT-2 alone (run_coded_dual), with pinned host copies.
+    // Mixed passes run two deep (the host mixer of pass k beside the forward pass of pass k + 1),
+    // so pass k uses half k & 1 of the row table and of the logits (d16, tmax and the store map
+    // of d16); half 0 is the batch's own, half 1 is made with the mixed buffers. The pinned host
+    // buffers have a half per pass parity too: h_mix holds the table words [2][Rcap] of the
+    // statistics kernel, then the mix records [2][Rcap].
     MixRow* d_mix = nullptr;
     uint64_t* d_stats = nullptr;
     uint64_t* d_plain = nullptr;
     MixRow* h_mix = nullptr;
-    uint64_t* h_stats = nullptr;
-    uint64_t* h_plain = nullptr;
+    uint64_t* h_stats = nullptr;  // [2][3 Rcap]
+    uint64_t* h_plain = nullptr;  // [2][3 Rcap]
+    cudaEvent_t stats_done[2] = {nullptr, nullptr};
+    RowInfo* mx_rows[2] = {nullptr, nullptr};
+    uint16_t* mx_d16[2] = {nullptr, nullptr};
+    int64_t* mx_tmax[2] = {nullptr, nullptr};
+    alignas(128) CUtensorMap mx_ts_d16[2];
     uint64_t bytes = 0;
     // Per-op device time (CUDA events on the batch stream) when profiling is on.
     bool profiling = false;
@@ -269,6 +279,8 @@ struct hs_batch {
         if (h_intervals_base) cudaFreeHost(h_intervals_base);
         if (h_groups_base) cudaFreeHost(h_groups_base);
         if (h_rowlist_base) cudaFreeHost(h_rowlist_base);
+        for (cudaEvent_t e : stats_done)
+            if (e) cudaEventDestroy(e);
         if (h_mix) cudaFreeHost(h_mix);
         if (h_stats) cudaFreeHost(h_stats);
         if (h_plain) cudaFreeHost(h_plain);
@@ -675,16 +687,44 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     // device fault is sticky and still shows.
     cudaGetLastError();
     if (mix && !b->d_mix) {
-        // The buffers of the mixed coder op: made on the first mixed call.
+        // The buffers of the mixed coder op, made on the first mixed call: the second half of the
+        // row table and of the logits (with its store map), the mix records, the statistics.
         const size_t Rc = (size_t)b->Rcap;
-        if ((rc = dalloc(&b->d_mix, Rc, b->owned)) || (rc = dalloc(&b->d_stats, 3 * Rc, b->owned)) ||
+        b->mx_rows[0] = b->d_rows;
+        b->mx_d16[0] = b->d16;
+        b->mx_tmax[0] = b->tmax;
+        b->mx_ts_d16[0] = b->ts_d16;
+        if ((rc = dalloc(&b->mx_rows[1], Rc, b->owned)) || (rc = dalloc(&b->mx_d16[1], Rc * c.Vp, b->owned)) ||
+            (rc = dalloc(&b->mx_tmax[1], Rc * c.VT, b->owned)) ||
+            (rc = make_store_tmap(m->dev, &b->mx_ts_d16[1], b->mx_d16[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2,
+                                  (int)Rc, c.V, c.Vp, 128)) ||
+            (rc = dalloc(&b->d_mix, Rc, b->owned)) || (rc = dalloc(&b->d_stats, 3 * Rc, b->owned)) ||
             (rc = dalloc(&b->d_plain, 3 * Rc, b->owned)))
             return rc;
-        b->bytes += Rc * (sizeof(MixRow) + 48);
-        CK(cudaMallocHost(&b->h_mix, sizeof(MixRow) * Rc));
-        CK(cudaMallocHost(&b->h_stats, sizeof(uint64_t) * 3 * Rc));
-        CK(cudaMallocHost(&b->h_plain, sizeof(uint64_t) * 3 * Rc));
+        b->bytes += Rc * (sizeof(RowInfo) + 2 * (size_t)c.Vp + 8 * (size_t)c.VT + sizeof(MixRow) + 48);
+        CK(cudaMallocHost(&b->h_mix, sizeof(MixRow) * 4 * Rc));
+        CK(cudaMallocHost(&b->h_stats, sizeof(uint64_t) * 6 * Rc));
+        CK(cudaMallocHost(&b->h_plain, sizeof(uint64_t) * 6 * Rc));
+        for (cudaEvent_t& e : b->stats_done) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
+    // The batch's own buffers are current again when the call ends, however it ends.
+    struct MixHalfRestore {
+        hs_batch* b;
+        ~MixHalfRestore() {
+            if (!b->mx_rows[0]) return;
+            b->d_rows = b->mx_rows[0];
+            b->d16 = b->mx_d16[0];
+            b->tmax = b->mx_tmax[0];
+            b->ts_d16 = b->mx_ts_d16[0];
+        }
+    } mix_restore{b};
+    auto use_mix_half = [&](size_t k) {
+        const int h = (int)(k & 1);
+        b->d_rows = b->mx_rows[h];
+        b->d16 = b->mx_d16[h];
+        b->tmax = b->mx_tmax[h];
+        b->ts_d16 = b->mx_ts_d16[h];
+    };
     if (wout && !b->weights) {
         // The weights buffer of run_weights: made on the first use (vocab u64 per row).
         if ((rc = dalloc(&b->weights, (size_t)b->Rcap * c.V, b->owned))) return rc;
@@ -721,10 +761,69 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         }
         return HS_OK;
     };
+    auto plain_out = [&](size_t k) {
+        const uint64_t* hp = b->h_plain + (k & 1) * 3 * (size_t)b->Rcap;
+        const auto& pass = passes[k];
+        for (size_t r = 0; r < pass.size(); r++) {
+            long in = pass[r].input;
+            if (in < 0) continue;
+            hs_interval& iv = mix->plain[in];
+            iv.symbol = (uint32_t)hp[3 * r];
+            iv.start = hp[3 * r + 1];
+            iv.freq = hp[3 * r + 2];
+            iv.is_last = iv.symbol + 1 == (uint32_t)c.V;
+            iv.reserved = 0;
+        }
+    };
+    // The second half of mixed pass j (batch/mixed.rs:145-180 mix_pass), after the forward pass of
+    // pass j + 1 is in the stream: the host mixer for each input of pass j with a predicted token,
+    // in input order, on the statistics read back; the mix records up; the coder of GPT-2 alone
+    // (run_coded_dual) and the mixed coder on the logits of pass j (half j & 1).
+    auto finish = [&](size_t j) -> int {
+        const auto& pass = passes[j];
+        const int R = (int)pass.size();
+        const size_t h = j & 1, Rc = (size_t)b->Rcap;
+        CK(cudaEventSynchronize(b->stats_done[h]));
+        const uint64_t* st = b->h_stats + h * 3 * Rc;
+        MixRow* rec = b->h_mix + (2 + h) * Rc;
+        for (int r = 0; r < R; r++) {
+            const long in = pass[r].input;
+            const uint32_t t = in >= 0 ? mix->tables[in] : MIX_NONE;
+            rec[r] = MixRow{t, 0, 0, 0, 0, 0};
+            if (in < 0 || t >= (uint32_t)c.V) continue;
+            const hs_mix_stats ms{st[3 * r], st[3 * r + 1], (uint32_t)st[3 * r + 2], 0};
+            const uint32_t q = mix->fn(mix->user, (uint32_t)in, &ms);
+            if ((rc = mix_record(ms, t, q, &rec[r]))) return rc;
+        }
+        // The answers of pass j - 2 left before this pass's read back reuses their half (their
+        // copy is ahead of the statistics of pass j in the stream, so this does not wait).
+        if (j >= 2) {
+            if ((rc = answers_out(j - 2))) return rc;
+            if (mix->plain) plain_out(j - 2);
+        }
+        ProfScope pass_scope(b, OP_PASS, 0);
+        CK(cudaMemcpyAsync(b->d_mix, rec, sizeof(MixRow) * R, cudaMemcpyHostToDevice, b->stream));
+        {
+            ProfScope p(b, OP_CODER, 0);
+            if (mix->plain)
+                launch_coder(b->mx_d16[h], c.Vp, b->mx_tmax[h], c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
+                             m->logits_head, bits, b->mx_rows[h], b->d_plain, b->stream);
+            launch_coder_mix(b->mx_d16[h], c.Vp, b->mx_tmax[h], c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
+                             m->logits_head, bits, b->mx_rows[h], b->d_mix, 1, b->intervals, b->stream);
+        }
+        if (mix->plain)
+            CK(cudaMemcpyAsync(b->h_plain + h * 3 * Rc, b->d_plain, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
+                               b->stream));
+        CK(cudaMemcpyAsync(b->h_intervals_base + h * 3 * Rc, b->intervals, sizeof(uint64_t) * 3 * R,
+                           cudaMemcpyDeviceToHost, b->stream));
+        CK(cudaEventRecord(b->pass_done[h], b->stream));
+        return HS_OK;
+    };
     for (size_t k = 0; k < passes.size(); k++) {
         const auto& pass = passes[k];
         if (out && !mix && k >= 2 && (rc = answers_out(k - 2))) return rc;
         use_half(k);
+        if (mix) use_mix_half(k);
         int R = (int)pass.size();
         for (int r = 0; r < R; r++) {
             const PlanRow& p = pass[r];
@@ -751,56 +850,24 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         rc = forward(b, R);
         if (rc) return rc;
         if (out && mix) {
-            // The mixed coder op (batch/mixed.rs:145-180 mix_pass): the statistics of the rows,
-            // read back; the host mixer for each input with a predicted token, in input order; the
-            // mix records up; then the coder of GPT-2 alone (run_coded_dual) and the mixed coder.
+            // The first half of a mixed pass: the statistics of its rows, read back into half k & 1;
+            // then the second half of the previous pass.
+            MixRow* pw = b->h_mix + (k & 1) * (size_t)b->Rcap;
             for (int r = 0; r < R; r++) {
                 const long in = pass[r].input;
-                b->h_mix[r] = MixRow{in >= 0 ? mix->tables[in] : MIX_NONE, 0, 0, 0, 0, 0};
+                pw[r] = MixRow{in >= 0 ? mix->tables[in] : MIX_NONE, 0, 0, 0, 0, 0};
             }
-            CK(cudaMemcpyAsync(b->d_mix, b->h_mix, sizeof(MixRow) * R, cudaMemcpyHostToDevice, b->stream));
+            CK(cudaMemcpyAsync(b->d_mix, pw, sizeof(MixRow) * R, cudaMemcpyHostToDevice, b->stream));
             {
                 ProfScope p(b, OP_CODER, 0);
                 launch_coder_mix(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
                                  m->logits_head, bits, b->d_rows, b->d_mix, 0, b->d_stats, b->stream);
             }
-            CK(cudaMemcpyAsync(b->h_stats, b->d_stats, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost, b->stream));
-            if ((rc = check_device_error(b))) return rc;
-            for (int r = 0; r < R; r++) {
-                const long in = pass[r].input;
-                const uint32_t t = b->h_mix[r].p;
-                if (in < 0 || t >= (uint32_t)c.V) continue;
-                const hs_mix_stats st{b->h_stats[3 * r], b->h_stats[3 * r + 1], (uint32_t)b->h_stats[3 * r + 2], 0};
-                const uint32_t q = mix->fn(mix->user, (uint32_t)in, &st);
-                if ((rc = mix_record(st, t, q, &b->h_mix[r]))) return rc;
-            }
-            CK(cudaMemcpyAsync(b->d_mix, b->h_mix, sizeof(MixRow) * R, cudaMemcpyHostToDevice, b->stream));
-            {
-                ProfScope p(b, OP_CODER, 0);
-                if (mix->plain)
-                    launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
-                                 m->logits_head, bits, b->d_rows, b->d_plain, b->stream);
-                launch_coder_mix(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
-                                 m->logits_head, bits, b->d_rows, b->d_mix, 1, b->intervals, b->stream);
-            }
             pass_scope.reset();
-            if (mix->plain)
-                CK(cudaMemcpyAsync(b->h_plain, b->d_plain, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
-                                   b->stream));
-            CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
-                               b->stream));
-            CK(cudaEventRecord(b->pass_done[k & 1], b->stream));
-            if ((rc = answers_out(k))) return rc;
-            for (int r = 0; mix->plain && r < R; r++) {
-                const long in = pass[r].input;
-                if (in < 0) continue;
-                hs_interval& iv = mix->plain[in];
-                iv.symbol = (uint32_t)b->h_plain[3 * r];
-                iv.start = b->h_plain[3 * r + 1];
-                iv.freq = b->h_plain[3 * r + 2];
-                iv.is_last = iv.symbol + 1 == (uint32_t)c.V;
-                iv.reserved = 0;
-            }
+            CK(cudaMemcpyAsync(b->h_stats + (k & 1) * 3 * (size_t)b->Rcap, b->d_stats, sizeof(uint64_t) * 3 * R,
+                               cudaMemcpyDeviceToHost, b->stream));
+            CK(cudaEventRecord(b->stats_done[k & 1], b->stream));
+            if (k >= 1 && (rc = finish(k - 1))) return rc;
         } else if (out) {
             {
                 ProfScope p(b, OP_CODER, 0);
@@ -829,12 +896,15 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             }
         }
     }
+    if (out && mix && !passes.empty() && (rc = finish(passes.size() - 1))) return rc;
     rc = check_device_error(b);
     if (rc) return rc;
     if (b->profiling) prof_collect(b);
-    if (out && !mix) {
-        for (size_t k = passes.size() >= 2 ? passes.size() - 2 : 0; k < passes.size(); k++)
+    if (out) {
+        for (size_t k = passes.size() >= 2 ? passes.size() - 2 : 0; k < passes.size(); k++) {
             if ((rc = answers_out(k))) return rc;
+            if (mix && mix->plain) plain_out(k);
+        }
     }
     // Every pass ran: commit the positions and histories (batch/plan.rs:120 commit).
     b->pos = pos;
