@@ -178,6 +178,24 @@ int hs_batch_decode_blocks(hs_batch* batch, uint32_t n, const uint32_t* slots, c
                            const uint32_t* counts, uint32_t freq_bits, uint32_t* tokens_out, uint64_t tokens_cap,
                            const uint64_t* token_offsets, uint32_t* status);
 
+/* ---- the host glue of the fold: no GPU needed ---- */
+
+/* The tokenizer of a model (crates/taco/src/tokenizer/mod.rs Tokenizer::for_vocabulary): GPT-2
+ * byte-level BPE over the vocabulary and the merges of the .hsm file. Any byte string tokenizes,
+ * and the bytes of the tokens join to the input. HS_MODEL if the file is not valid, a byte has no
+ * single token, or a merge is refused (the MergeFault cases of mod.rs:33-47). */
+typedef struct hs_tokenizer hs_tokenizer;
+int hs_tokenizer_new(const uint8_t* file, size_t len, hs_tokenizer** out);
+void hs_tokenizer_free(hs_tokenizer* tokenizer);
+/* Tokenizer::encode (mod.rs:180-200): the tokens of data[0 .. len) into out (at most len
+ * tokens); *n = the token count. HS_BAD_ARGUMENT (with *n set) if cap is too small. */
+int hs_tokenize(const hs_tokenizer* tokenizer, const uint8_t* data, size_t len, uint32_t* out, size_t cap,
+                size_t* n);
+/* The pieces of the pre-tokenizer (tokenizer/pretokenize.rs Pieces, and the single bytes outside
+ * the well-formed UTF-8 runs): the end offset of each piece, in order. */
+int hs_tokenizer_pieces(const hs_tokenizer* tokenizer, const uint8_t* data, size_t len, uint64_t* ends,
+                        size_t cap, size_t* n);
+
 /* The message of the last error of the calling thread (NUL-terminated, cut to `cap`). */
 int hs_last_error(char* buf, size_t cap);
 

@@ -106,6 +106,13 @@ def lib() -> ctypes.CDLL:
     L.hs_batch_truncate.argtypes = [vp, u32, ctypes.c_uint64]
     L.hs_batch_decode_blocks.argtypes = [vp, u32, vp, vp, ctypes.c_uint64, vp, vp, vp, u32, vp, ctypes.c_uint64, vp, vp]
     L.hs_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+    L.hs_tokenizer_new.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(vp)]
+    L.hs_tokenizer_free.argtypes = [vp]
+    L.hs_tokenizer_free.restype = None
+    L.hs_tokenize.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t,
+                              ctypes.POINTER(ctypes.c_size_t)]
+    L.hs_tokenizer_pieces.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t,
+                                      ctypes.POINTER(ctypes.c_size_t)]
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_act_noalloc.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_bench.argtypes = [vp, i32, u32, u32, u32, u64, i32, i32, ctypes.POINTER(ctypes.c_double)]
@@ -131,6 +138,40 @@ def _p(a: np.ndarray) -> ctypes.c_void_p:
 def launch_count() -> int:
     """Kernel launches of the library in this process."""
     return int(lib().hs_launch_count())
+
+
+class Tokenizer:
+    """crates/taco/src/tokenizer Tokenizer: GPT-2 byte-level BPE of a .hsm model (host code, no GPU)."""
+
+    def __init__(self, model_file: bytes):
+        h = ctypes.c_void_p()
+        _check(lib().hs_tokenizer_new(model_file, len(model_file), ctypes.byref(h)))
+        self.h = h
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().hs_tokenizer_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def encode(self, data: bytes) -> np.ndarray:
+        out = np.zeros(max(len(data), 1), dtype=np.uint32)
+        n = ctypes.c_size_t()
+        _check(lib().hs_tokenize(self.h, data, len(data), _p(out), out.size, ctypes.byref(n)))
+        return out[:n.value].copy()
+
+    def pieces(self, data: bytes) -> list[bytes]:
+        """The pre-tokenizer's pieces of `data` (and the single bytes outside UTF-8 runs)."""
+        ends = np.zeros(max(len(data), 1), dtype=np.uint64)
+        n = ctypes.c_size_t()
+        _check(lib().hs_tokenizer_pieces(self.h, data, len(data), _p(ends), ends.size, ctypes.byref(n)))
+        out, a = [], 0
+        for e in ends[:n.value].tolist():
+            out.append(data[a:e])
+            a = e
+        return out
 
 
 class CudaDevice:

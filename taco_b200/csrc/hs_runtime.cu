@@ -22,6 +22,7 @@
 #include "../../include/hardshell_b200.h"
 #include "hs_device.hpp"
 #include "hs_kernels.cuh"
+#include "hs_host.hpp"
 #include "hsm_file.hpp"
 #include "sha256.hpp"
 
@@ -35,6 +36,12 @@ int fail(int code, const std::string& msg) {
     g_err = msg;
     return code;
 }
+
+}  // namespace
+
+int hs::host_fail(int code, const std::string& msg) { return fail(code, msg); }
+
+namespace {
 
 #define CK(call)                                                                                     \
     do {                                                                                             \
