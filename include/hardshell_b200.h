@@ -196,6 +196,43 @@ int hs_tokenize(const hs_tokenizer* tokenizer, const uint8_t* data, size_t len, 
 int hs_tokenizer_pieces(const hs_tokenizer* tokenizer, const uint8_t* data, size_t len, uint64_t* ends,
                         size_t cap, size_t* n);
 
+/* The options of a fold (crates/taco/src/fold.rs FoldOptions, profile text). block_size 0 is
+ * the default 16 KiB (lib.rs:101); with `spread` and no block size, the power of two that gives
+ * about 64 blocks, within 4 KiB .. 16 KiB (fold.rs:159-170). overlap is the context overlap K
+ * (the text profile's default is 0). threads: host threads for the tokenizer, zstd and the range
+ * encoder (0 = all). */
+typedef struct hs_fold_options {
+    uint32_t block_size;
+    uint32_t overlap;
+    uint32_t spread;
+    uint32_t threads;
+} hs_fold_options;
+
+/* FoldStats (fold.rs): the counts of one fold. */
+typedef struct hs_fold_stats {
+    uint64_t original_len, container_len, blocks, coded_blocks, zstd_blocks, tokens;
+    uint32_t block_size, reserved;
+} hs_fold_stats;
+
+/* The largest container of a fold of `len` bytes with this block size (0 = the default). */
+uint64_t hs_fold_bound(uint64_t len, uint32_t block_size);
+
+/* taco::fold_with on the CUDA engine (fold.rs:334-360), profile text: the .taco container
+ * (version 2) of input[0 .. len) with the model of `batch`. Each block is stored raw, as a zstd
+ * frame or coded by the model, whichever is smallest (writer.rs:89). The coder intervals come from
+ * hs_batch_run_coded (the slots of the batch take the blocks in rounds; their contexts are reset);
+ * the tokenizer, zstd and the range encoder run on host threads. zstd comes from the system
+ * library (libzstd.so.1, hs_zstd_version); the reference pins zstd 1.5.7, and a zstd frame of
+ * another version can differ in its bytes (it decodes to the same block). *out_len = the container
+ * length; HS_BAD_ARGUMENT if it is more than cap (see hs_fold_bound). The slots of the batch are
+ * left with the last blocks' contexts. */
+int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input, size_t len,
+            const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats);
+
+/* The version of the zstd library that hs_fold uses (major * 10000 + minor * 100 + patch), or 0
+ * if it is not available. */
+uint32_t hs_zstd_version(void);
+
 /* The message of the last error of the calling thread (NUL-terminated, cut to `cap`). */
 int hs_last_error(char* buf, size_t cap);
 

@@ -60,6 +60,17 @@ class MixStats(ctypes.Structure):
                 ("reserved", ctypes.c_uint32)]
 
 
+class FoldOptions(ctypes.Structure):
+    _fields_ = [("block_size", ctypes.c_uint32), ("overlap", ctypes.c_uint32), ("spread", ctypes.c_uint32),
+                ("threads", ctypes.c_uint32)]
+
+
+class FoldStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in ("original_len", "container_len", "blocks", "coded_blocks",
+                                               "zstd_blocks", "tokens")] + \
+               [("block_size", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
 MIXER_FN = ctypes.CFUNCTYPE(ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(MixStats))
 MIX_NONE = 0xFFFFFFFF   # a mixed table without a prediction: the weights max(1, w)
 MIX_PLAIN = 0xFFFFFFFE  # the table of GPT-2 alone
@@ -113,6 +124,12 @@ def lib() -> ctypes.CDLL:
                               ctypes.POINTER(ctypes.c_size_t)]
     L.hs_tokenizer_pieces.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_size_t)]
+    L.hs_fold_bound.argtypes = [u64, u32]
+    L.hs_fold_bound.restype = u64
+    L.hs_fold.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(FoldOptions), vp, ctypes.c_size_t,
+                          ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(FoldStats)]
+    L.hs_zstd_version.argtypes = []
+    L.hs_zstd_version.restype = u32
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_act_noalloc.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
     L.hs_op_linear_bench.argtypes = [vp, i32, u32, u32, u32, u64, i32, i32, ctypes.POINTER(ctypes.c_double)]
@@ -172,6 +189,24 @@ class Tokenizer:
             out.append(data[a:e])
             a = e
         return out
+
+
+def fold(batch, tokenizer, data: bytes, block_size: int = 0, overlap: int = 0, spread: bool = False,
+         threads: int = 0):
+    """taco::fold_with on the CUDA engine, profile text (hs_fold): (container bytes, stats dict)."""
+    opt = FoldOptions(block_size, overlap, int(spread), threads)
+    cap = int(lib().hs_fold_bound(len(data), block_size))
+    out = np.zeros(max(cap, 1), dtype=np.uint8)
+    n = ctypes.c_size_t()
+    st = FoldStats()
+    _check(lib().hs_fold(batch.h, tokenizer.h, data, len(data), ctypes.byref(opt), _p(out), out.size,
+                         ctypes.byref(n), ctypes.byref(st)))
+    stats = {name: getattr(st, name) for name, _ in FoldStats._fields_ if name != "reserved"}
+    return out[:n.value].tobytes(), stats
+
+
+def zstd_version() -> int:
+    return int(lib().hs_zstd_version())
 
 
 class CudaDevice:

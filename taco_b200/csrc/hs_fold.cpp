@@ -1,0 +1,378 @@
+// The fold of the profile text above the C ABI: bytes in, a .taco container out
+// (crates/taco/src/fold.rs fold_with and code_segment, codec.rs BlockEncoder, and the container
+// writer of crates/taco-format/src/writer.rs). The model's part is hs_batch_run_coded on the GPU;
+// the rest is host code: the tokenizer, the zstd frame, the range encoder with the stop rule, the
+// choice of the smallest stored form, and the container.
+//
+// The steps of one fold:
+// 1. The input divides into blocks of the block size (the last one shorter).
+// 2. On host threads, each block is tokenized (its tokens must join to its bytes) and compressed
+//    into one zstd frame (level 19, content size, no checksum, no dictionary id; zstd_block.rs).
+// 3. On the GPU, the blocks run in rounds of up to `slots` blocks, one slot each from a fresh
+//    context: the inputs EOT, t0 .. t(n-2) with the encode queries t0 .. t(n-1), the context
+//    restarting with the overlap K (codec.rs:1-24, the order of the encoder's calls).
+// 4. On host threads, each block's intervals go through the range encoder until the payload (the
+//    varint token count, then the coder bytes) is sure to reach the bound min(block length, zstd
+//    frame length): then the block has no coded form (codec.rs:70-131, the stop rule).
+// 5. Each block is stored in its smallest form: raw, then zstd, then coded, ties to the earlier
+//    (writer.rs:89 choose_smallest), and the container is written (header version 2).
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "hardshell_b200.h"
+#include "hs_host.hpp"
+#include "sha256.hpp"
+
+namespace {
+
+constexpr uint32_t DEFAULT_BLOCK_SIZE = 16 * 1024;  // crates/taco/src/lib.rs:101
+constexpr uint32_t SPREAD_BLOCKS = 64;              // lib.rs:138
+constexpr uint32_t SPREAD_MIN_BLOCK = 4 * 1024;     // lib.rs:145
+constexpr uint32_t MAX_BLOCK_SIZE = 64u << 20;      // crates/taco-format: the largest block size
+constexpr size_t HEADER_LEN = 104;                  // version 2 header
+constexpr uint32_t FREQ_BITS = 32;                  // codec.rs:35
+constexpr int ZSTD_LEVEL = 19;                      // crates/taco-format/src/zstd_block.rs:23
+constexpr uint8_t KIND_RAW = 0, KIND_CODED = 1, KIND_ZSTD = 2;
+
+// ---- zstd, from the system library (opened once) ----
+
+struct Zstd {
+    void* lib = nullptr;
+    void* (*create)() = nullptr;
+    size_t (*free_ctx)(void*) = nullptr;
+    size_t (*set_param)(void*, int, int) = nullptr;
+    size_t (*compress2)(void*, void*, size_t, const void*, size_t) = nullptr;
+    size_t (*bound)(size_t) = nullptr;
+    unsigned (*is_error)(size_t) = nullptr;
+    unsigned (*version)() = nullptr;
+    bool ok = false;
+
+    Zstd() {
+        lib = dlopen("libzstd.so.1", RTLD_NOW | RTLD_LOCAL);
+        if (!lib) return;
+        create = (void* (*)())dlsym(lib, "ZSTD_createCCtx");
+        free_ctx = (size_t(*)(void*))dlsym(lib, "ZSTD_freeCCtx");
+        set_param = (size_t(*)(void*, int, int))dlsym(lib, "ZSTD_CCtx_setParameter");
+        compress2 = (size_t(*)(void*, void*, size_t, const void*, size_t))dlsym(lib, "ZSTD_compress2");
+        bound = (size_t(*)(size_t))dlsym(lib, "ZSTD_compressBound");
+        is_error = (unsigned (*)(size_t))dlsym(lib, "ZSTD_isError");
+        version = (unsigned (*)())dlsym(lib, "ZSTD_versionNumber");
+        ok = create && free_ctx && set_param && compress2 && bound && is_error && version;
+    }
+};
+
+const Zstd& zstd() {
+    static const Zstd z;
+    return z;
+}
+
+// compress_zstd (zstd_block.rs:64-79): one frame at level 19 with the content size, no
+// checksum and no dictionary id. The parameter ids are those of zstd.h (ZSTD_c_compressionLevel
+// 100, ZSTD_c_contentSizeFlag 200, ZSTD_c_checksumFlag 201, ZSTD_c_dictIDFlag 202).
+bool compress_zstd(const uint8_t* data, size_t len, std::vector<uint8_t>& out) {
+    const Zstd& z = zstd();
+    void* cctx = z.create();
+    if (!cctx) return false;
+    bool ok = true;
+    const int params[4][2] = {{100, ZSTD_LEVEL}, {200, 1}, {201, 0}, {202, 0}};
+    for (const auto& p : params) ok = ok && !z.is_error(z.set_param(cctx, p[0], p[1]));
+    if (ok) {
+        out.resize(z.bound(len));
+        const size_t n = z.compress2(cctx, out.data(), out.size(), data, len);
+        ok = !z.is_error(n);
+        out.resize(ok ? n : 0);
+    }
+    z.free_ctx(cctx);
+    return ok;
+}
+
+// ---- the range encoder (crates/taco-coder/src/encoder.rs) ----
+
+// A 64-bit window over a 128-bit low with a carry, bytes out with the pending run of 0xFF, and
+// the length of the output up to its last non-zero byte (the smallest final length).
+struct RangeEncoder {
+    unsigned __int128 low = 0;
+    uint64_t range = ~0ULL;  // INITIAL_RANGE
+    uint8_t cache = 0;
+    size_t pending = 0;
+    std::vector<uint8_t> out;
+    size_t nonzero_len = 0;
+    static constexpr uint64_t TOP = 1ULL << 56;
+
+    void shift_low() {
+        const uint8_t carry = (uint8_t)((low >> 64) & 1);
+        const uint64_t window = (uint64_t)low;
+        if (pending == 0 || window < 0xFF00000000000000ULL || carry != 0) {
+            if (pending > 0) {
+                const uint8_t first = (uint8_t)(cache + carry);
+                out.push_back(first);
+                if (first != 0) nonzero_len = out.size();
+                const uint8_t fill = (uint8_t)(0xFF + carry);
+                out.insert(out.end(), pending - 1, fill);
+                if (fill != 0 && pending > 1) nonzero_len = out.size();
+            }
+            cache = (uint8_t)(window >> 56);
+            pending = 0;
+        }
+        pending++;
+        low = (unsigned __int128)(window << 8);
+    }
+
+    void encode(uint64_t start, uint64_t freq, bool is_last, uint32_t bits) {
+        const uint64_t r = range >> bits;
+        const uint64_t offset = r * start;
+        low += offset;
+        range = is_last ? range - offset : r * freq;
+        while (range < TOP) {
+            range <<= 8;
+            shift_low();
+        }
+    }
+
+    // The shortest tail that keeps the code inside [low, low + range): low rounded up to a
+    // multiple of 2^64, or else of 2^56; two more bytes out; trailing zero bytes dropped.
+    std::vector<uint8_t> finish() {
+        const unsigned __int128 end = low + range;
+        for (int k : {64, 56}) {
+            const unsigned __int128 mask = ((unsigned __int128)1 << k) - 1;
+            const unsigned __int128 v = (low + mask) & ~mask;
+            if (v < end) {
+                low = v;
+                break;
+            }
+        }
+        shift_low();
+        shift_low();
+        while (!out.empty() && out.back() == 0) out.pop_back();
+        return std::move(out);
+    }
+};
+
+void write_varint(uint64_t v, std::vector<uint8_t>& out) {  // payload.rs:20: LEB128
+    while (v >= 0x80) {
+        out.push_back((uint8_t)(v | 0x80));
+        v >>= 7;
+    }
+    out.push_back((uint8_t)v);
+}
+
+size_t varint_len(uint64_t v) {
+    size_t n = 1;
+    while (v >= 0x80) {
+        v >>= 7;
+        n++;
+    }
+    return n;
+}
+
+struct FoldBlock {
+    size_t off = 0, len = 0;
+    std::vector<uint32_t> tokens;
+    std::vector<uint8_t> zstd;
+    bool zstd_ok = false;
+    std::vector<hs_interval> intervals;
+    uint8_t kind = KIND_RAW;
+    std::vector<uint8_t> stored;  // the stored bytes of a zstd or coded block
+};
+
+// Runs f(i) for i in [0, n) on up to `threads` host threads.
+template <typename F>
+void parallel_for(size_t n, unsigned threads, F&& f) {
+    threads = std::max(1u, std::min<unsigned>(threads, (unsigned)std::max<size_t>(n, 1)));
+    std::atomic<size_t> next{0};
+    auto work = [&]() {
+        for (size_t i; (i = next.fetch_add(1)) < n;) f(i);
+    };
+    std::vector<std::thread> pool;
+    for (unsigned t = 1; t < threads; t++) pool.emplace_back(work);
+    work();
+    for (auto& t : pool) t.join();
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t hs_fold_bound(uint64_t len, uint32_t block_size) {
+    const uint64_t bs = block_size ? block_size : DEFAULT_BLOCK_SIZE;
+    return HEADER_LEN + 5 * ((len + bs - 1) / bs) + len;
+}
+
+int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt,
+            uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
+    if (!batch || !tok || !opt || !out_len || (len && !input)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    if (!zstd().ok) return hs::host_fail(HS_UNSUPPORTED, "the zstd library (libzstd.so.1) is not available");
+    hs_model* model = hs::batch_model(batch);
+    hs_model_info info;
+    int rc = hs_model_get_info(model, &info);
+    if (rc) return rc;
+    // FoldOptions::block_size_for (fold.rs:159-170): a set size, or 16 KiB; with `spread`, the
+    // power of two that makes about 64 blocks, within 4 KiB .. 16 KiB.
+    uint64_t bs = opt->block_size ? opt->block_size : DEFAULT_BLOCK_SIZE;
+    if (opt->spread && !opt->block_size) {
+        uint64_t per = (len + SPREAD_BLOCKS - 1) / SPREAD_BLOCKS, p2 = 1;
+        while (p2 < per) p2 <<= 1;
+        bs = std::min<uint64_t>(std::max<uint64_t>(p2, SPREAD_MIN_BLOCK), DEFAULT_BLOCK_SIZE);
+    }
+    if (bs == 0 || bs > MAX_BLOCK_SIZE) return hs::host_fail(HS_UNSUPPORTED, "the block size is out of range");
+    if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
+    if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
+    const size_t nblocks = (size_t)((len + bs - 1) / bs);
+    const uint64_t need = HEADER_LEN + 5 * (uint64_t)nblocks + len;
+    const unsigned threads = opt->threads ? opt->threads : std::max(1u, std::thread::hardware_concurrency());
+    std::vector<FoldBlock> blocks(nblocks);
+    for (size_t i = 0; i < nblocks; i++) {
+        blocks[i].off = i * bs;
+        blocks[i].len = std::min<size_t>(bs, len - i * bs);
+    }
+    // 2. Tokens and zstd frames on the host threads.
+    std::atomic<int> bad_tokens{-1}, bad_zstd{-1};
+    parallel_for(nblocks, threads, [&](size_t i) {
+        FoldBlock& b = blocks[i];
+        hs::tokenize(tok, input + b.off, b.len, b.tokens);
+        if (!hs::tokens_restore(tok, b.tokens.data(), b.tokens.size(), input + b.off, b.len)) bad_tokens = (int)i;
+        b.zstd_ok = compress_zstd(input + b.off, b.len, b.zstd);
+        if (!b.zstd_ok) bad_zstd = (int)i;
+    });
+    if (bad_tokens >= 0)
+        return hs::host_fail(HS_MODEL, "the tokens of block " + std::to_string(bad_tokens.load()) +
+                                           " do not give its bytes back (TokenizerRoundTrip)");
+    if (bad_zstd >= 0) return hs::host_fail(HS_CUDA, "zstd failed on block " + std::to_string(bad_zstd.load()));
+    // 3. The intervals on the GPU: rounds of up to `slots` blocks, slot-major rows. A block whose
+    // payload prefix already reaches its bound needs none.
+    const uint32_t slots = hs::batch_slots(batch);
+    auto stop_of = [&](const FoldBlock& b) { return std::min(b.len, b.zstd.size()); };
+    std::vector<uint32_t> s_slot, s_tok, s_kind;
+    std::vector<uint64_t> s_val;
+    std::vector<hs_interval> ivs;
+    for (size_t r0 = 0; r0 < nblocks; r0 += slots) {
+        const size_t r1 = std::min(nblocks, r0 + slots);
+        s_slot.clear();
+        s_tok.clear();
+        s_val.clear();
+        std::vector<size_t> first(r1 - r0);
+        for (size_t i = r0; i < r1; i++) {
+            const FoldBlock& b = blocks[i];
+            const uint32_t s = (uint32_t)(i - r0);
+            first[i - r0] = s_slot.size();
+            if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
+            if ((rc = hs_batch_reset(batch, s))) return rc;
+            for (size_t j = 0; j < b.tokens.size(); j++) {
+                s_slot.push_back(s);
+                s_tok.push_back(j ? b.tokens[j - 1] : info.eot_token);
+                s_val.push_back(b.tokens[j]);
+            }
+        }
+        s_kind.assign(s_slot.size(), 0);
+        ivs.resize(s_slot.size());
+        if (!s_slot.empty() &&
+            (rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
+                                     (uint32_t)s_slot.size(), FREQ_BITS, ivs.data())))
+            return rc;
+        for (size_t i = r0; i < r1; i++) {
+            FoldBlock& b = blocks[i];
+            if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
+            b.intervals.assign(ivs.begin() + first[i - r0], ivs.begin() + first[i - r0] + b.tokens.size());
+        }
+    }
+    // 4.-5. The range encoder with the stop rule, then the smallest form.
+    parallel_for(nblocks, threads, [&](size_t i) {
+        FoldBlock& b = blocks[i];
+        const size_t stop = stop_of(b), prefix = varint_len(b.tokens.size());
+        std::vector<uint8_t> coded;
+        bool live = prefix < stop;
+        if (live) {
+            RangeEncoder enc;
+            for (const hs_interval& iv : b.intervals) {
+                enc.encode(iv.start, iv.freq, iv.is_last != 0, FREQ_BITS);
+                if (prefix + enc.nonzero_len >= stop) {
+                    live = false;
+                    break;
+                }
+            }
+            if (live) {
+                write_varint(b.tokens.size(), coded);
+                const std::vector<uint8_t> tail = enc.finish();
+                coded.insert(coded.end(), tail.begin(), tail.end());
+            }
+        }
+        size_t best = b.len;
+        if (b.zstd.size() < best) {
+            best = b.zstd.size();
+            b.kind = KIND_ZSTD;
+            b.stored = std::move(b.zstd);
+        }
+        if (live && coded.size() < best) {
+            b.kind = KIND_CODED;
+            b.stored = std::move(coded);
+        }
+        b.intervals.clear();
+        b.intervals.shrink_to_fit();
+    });
+    // The container (writer.rs:245-300; the header of header.rs, version 2, profile text).
+    uint64_t total = HEADER_LEN + 5 * (uint64_t)nblocks;
+    for (const FoldBlock& b : blocks) total += b.kind == KIND_RAW ? b.len : b.stored.size();
+    *out_len = (size_t)total;
+    if (stats) {
+        memset(stats, 0, sizeof(*stats));
+        stats->original_len = len;
+        stats->container_len = total;
+        stats->blocks = nblocks;
+        stats->block_size = (uint32_t)bs;
+        for (const FoldBlock& b : blocks) {
+            stats->tokens += b.tokens.size();
+            stats->coded_blocks += b.kind == KIND_CODED;
+            stats->zstd_blocks += b.kind == KIND_ZSTD;
+        }
+    }
+    if (cap < total || !out)
+        return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
+                                                  std::to_string(total) + " needed (hs_fold_bound: " +
+                                                  std::to_string(need) + ")");
+    uint8_t* p = out;
+    auto put = [&](const void* src, size_t n) {
+        memcpy(p, src, n);
+        p += n;
+    };
+    auto put16 = [&](uint16_t v) { put(&v, 2); };
+    auto put32 = [&](uint32_t v) { put(&v, 4); };
+    auto put64 = [&](uint64_t v) { put(&v, 8); };
+    put("TACO", 4);
+    put16(2);  // version
+    put16(0);  // flags
+    put(info.hash, 32);
+    put64(len);
+    uint8_t sum[32];
+    hs::sha256(input, len, sum);
+    put(sum, 32);
+    put32((uint32_t)bs);
+    put32((uint32_t)nblocks);
+    const uint16_t k = (uint16_t)opt->overlap;
+    const uint8_t profile = 0, reserved = 0;
+    put(&profile, 1);
+    put(&reserved, 1);
+    put16(k ? 2 : 0);  // coding parts: bit 1 = the overlap
+    uint8_t params[12] = {0};
+    memcpy(params + 2, &k, 2);
+    put(params, 12);
+    for (const FoldBlock& b : blocks) {
+        put(&b.kind, 1);
+        put32((uint32_t)(b.kind == KIND_RAW ? b.len : b.stored.size()));
+    }
+    for (const FoldBlock& b : blocks) {
+        if (b.kind == KIND_RAW) put(input + b.off, b.len);
+        else put(b.stored.data(), b.stored.size());
+    }
+    return HS_OK;
+}
+
+uint32_t hs_zstd_version(void) { return zstd().ok ? zstd().version() : 0; }
+
+}  // extern "C"

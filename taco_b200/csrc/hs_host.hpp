@@ -9,3 +9,24 @@ namespace hs {
 int host_fail(int code, const std::string& msg);
 
 }  // namespace hs
+
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+struct hs_model;
+struct hs_batch;
+struct hs_tokenizer;
+
+namespace hs {
+
+// The model of a batch, and its slot count.
+hs_model* batch_model(hs_batch* b);
+uint32_t batch_slots(const hs_batch* b);
+
+// Tokenizer::encode, and the check of crates/taco/src/codec.rs:55 tokens_restore: the bytes of
+// `tokens` (none of them EOT or empty) join to data[0 .. len).
+void tokenize(const hs_tokenizer* t, const uint8_t* data, size_t len, std::vector<uint32_t>& out);
+bool tokens_restore(const hs_tokenizer* t, const uint32_t* tokens, size_t n, const uint8_t* data, size_t len);
+
+}  // namespace hs

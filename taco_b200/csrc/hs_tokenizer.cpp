@@ -297,6 +297,18 @@ void tokenize(const hs_tokenizer* t, const uint8_t* data, size_t len, std::vecto
     t->encode(data, len, out);
 }
 
+bool tokens_restore(const hs_tokenizer* t, const uint32_t* tokens, size_t n, const uint8_t* data, size_t len) {
+    size_t at = 0;
+    for (size_t i = 0; i < n; i++) {
+        const uint32_t id = tokens[i];
+        if (id >= t->vocab || id == t->eot) return false;
+        const size_t a = id ? t->ends[id - 1] : 0, e = t->ends[id];
+        if (e == a || e - a > len - at || memcmp(t->bytes.data() + a, data + at, e - a) != 0) return false;
+        at += e - a;
+    }
+    return at == len;
+}
+
 }  // namespace hs
 
 extern "C" {

@@ -1,0 +1,101 @@
+"""The fold of the profile text (hs_fold: tokenizer, zstd, the coder op on the GPU, the range
+encoder with its stop rule, the container writer) on a B200, against the published containers.
+
+Every text-profile conformance input folds with the vector's block size and overlap
+(vectors.tsv) and the tiny model. The container must equal the published bytes, except where the
+zstd library of this image (1.5.5) writes another frame than the reference's pinned 1.5.7: such
+a block must be the only difference, must decode to its bytes, and the header and every other
+block must be equal. The vectors whose zstd frames agree (and those without zstd blocks) must be
+equal byte for byte. A larger input of mixed text and binary folds and every block decodes.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from taco_b200 import backend as B
+from taco_b200 import container as C
+
+from .common import GOLDEN, tiny_bytes
+
+TEXT_VECTORS = ["empty", "one_byte", "random_raw", "text_k0", "text_k20", "text_kinds",
+                "predicted_text_k0", "predicted_text_k32", "all_kinds_text"]
+EXACT = {"empty", "one_byte", "random_raw", "text_k0", "text_k20", "predicted_text_k0", "predicted_text_k32"}
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def setup():
+    dev = B.CudaDevice(0)
+    model = B.CudaModel(dev, tiny_bytes())
+    batch = B.CudaBatch(model, 8, 4096)
+    tok = B.Tokenizer(tiny_bytes())
+    yield batch, tok
+    tok.close()
+    batch.close()
+    model.close()
+    dev.close()
+
+
+def _vector(name):
+    for line in (GOLDEN / "vectors.tsv").read_text().splitlines():
+        f = line.split("\t")
+        if f[0] == name:
+            return (0 if f[2] == "default" else int(f[2])), (0 if f[3] == "default" else int(f[3]))
+    raise KeyError(name)
+
+
+def _decode(om, c, b):
+    if b.kind == C.KIND_RAW:
+        return b.stored
+    if b.kind == C.KIND_ZSTD:
+        return C.decode_zstd(b.stored, b.original_len)
+    data, _ = O.decode_block(om, b.stored, b.original_len, c.overlap)
+    return data
+
+
+@pytest.mark.parametrize("name", TEXT_VECTORS)
+def test_fold_gives_the_published_container(setup, name):
+    batch, tok = setup
+    om = O.Model(tiny_bytes())
+    bs, k = _vector(name)
+    data = (GOLDEN / (name + ".in")).read_bytes()
+    want = (GOLDEN / (name + ".taco")).read_bytes()
+    got, stats = B.fold(batch, tok, data, bs, k)
+    assert stats["original_len"] == len(data) and stats["container_len"] == len(got)
+    if name in EXACT:
+        assert got == want
+        return
+    if got == want:
+        return
+    g, w = C.parse(got), C.parse(want)
+    for f in ("version", "model_hash", "original_len", "checksum", "block_size", "profile", "overlap"):
+        assert getattr(g, f) == getattr(w, f), f
+    off = 0
+    for gb, wb in zip(g.blocks, w.blocks, strict=True):
+        orig = data[off:off + gb.original_len]
+        off += gb.original_len
+        if (gb.kind, gb.stored) != (wb.kind, wb.stored):
+            assert C.KIND_ZSTD in (gb.kind, wb.kind), gb.index  # a zstd frame of another version
+        assert _decode(om, g, gb) == orig
+
+
+def test_a_larger_input_folds_and_every_block_decodes(setup):
+    batch, tok = setup
+    om = O.Model(tiny_bytes())
+    rng = np.random.default_rng(11)
+    # Model-predicted text (coded blocks win there), binary bytes, mixed text, ill-formed UTF-8.
+    pred = (GOLDEN / "predicted_text_k0.in").read_bytes()
+    data = pred + rng.integers(0, 256, 700, dtype=np.uint8).tobytes() + \
+        (GOLDEN / "all_kinds_text.in").read_bytes() + pred + "ünï ✓".encode() + b"\xff\xfe"
+    for bs, k, coded in [(300, 0, True), (300, 16, True), (777, 12, False), (0, 0, False)]:
+        got, stats = B.fold(batch, tok, data, bs, k, threads=4)
+        c = C.parse(got)
+        assert c.original_len == len(data) and c.overlap == k
+        assert stats["blocks"] == len(c.blocks)
+        assert stats["coded_blocks"] == sum(b.kind == C.KIND_CODED for b in c.blocks)
+        if coded:
+            assert stats["coded_blocks"] > 0
+        out = b"".join(_decode(om, c, b) for b in c.blocks)
+        assert out == data
