@@ -34,7 +34,10 @@ enum hs_status {
     HS_LENGTH_MISMATCH = 6, /* Error::LengthMismatch */
     HS_TOKEN_RANGE = 7,     /* Error::Model(TokenOutOfRange) */
     HS_INVALID_OVERLAP = 8, /* Error::Model(InvalidOverlap) */
-    HS_BAD_ARGUMENT = 9     /* a null pointer or a size out of range */
+    HS_BAD_ARGUMENT = 9,    /* a null pointer or a size out of range */
+    HS_FORMAT = 10,         /* TacoError::Format: the container breaks a rule of the format */
+    HS_CORRUPT = 11,        /* TacoError::CorruptBlock / ChecksumMismatch: a block or the output is wrong */
+    HS_MODEL_MISMATCH = 12  /* TacoError::ModelHashMismatch: the container names another model */
 };
 
 typedef struct hs_dev hs_dev;
@@ -228,6 +231,19 @@ uint64_t hs_fold_bound(uint64_t len, uint32_t block_size);
  * left with the last blocks' contexts. */
 int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input, size_t len,
             const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats);
+
+/* taco::unfold on the CUDA engine (crates/taco/src/unfold.rs, profile text): the original bytes of
+ * a .taco container (version 1 or 2) into out[0 .. *out_len). The header and the block table are
+ * checked as crates/taco-format/src/reader.rs checks them (HS_FORMAT); a container that names a
+ * model must name the model of `batch` (HS_MODEL_MISMATCH). Raw blocks are copied, zstd blocks
+ * decoded (one frame, content size = the block length, window <= 8 MiB), coded blocks decoded on
+ * the GPU by hs_batch_decode_blocks in rounds of min(slots, max_rows) blocks and turned into
+ * bytes with the tokenizer's vocabulary; a block whose decoding fails or whose tokens do not give
+ * its length, or output whose SHA-256 is not the header's, is HS_CORRUPT. Mixed blocks (profile
+ * logs) are HS_UNSUPPORTED: their unfold needs the caller's match model and mixer. *out_len = the
+ * original length; HS_BAD_ARGUMENT if it is more than cap. */
+int hs_unfold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* container, size_t len, uint8_t* out,
+              size_t cap, size_t* out_len);
 
 /* The version of the zstd library that hs_fold uses (major * 10000 + minor * 100 + patch), or 0
  * if it is not available. */

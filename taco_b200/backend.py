@@ -18,10 +18,12 @@ LIB_PATH = Path(__file__).resolve().parent / "libhardshell_b200.so"
 
 HS_OK, HS_NO_DEVICE, HS_CUDA, HS_UNSUPPORTED, HS_MODEL = 0, 1, 2, 3, 4
 HS_BAD_SLOT, HS_LENGTH_MISMATCH, HS_TOKEN_RANGE, HS_INVALID_OVERLAP, HS_BAD_ARGUMENT = 5, 6, 7, 8, 9
+HS_FORMAT, HS_CORRUPT, HS_MODEL_MISMATCH = 10, 11, 12
 _NAMES = {
     HS_NO_DEVICE: "NoDevice", HS_CUDA: "Cuda", HS_UNSUPPORTED: "Unsupported", HS_MODEL: "Model",
     HS_BAD_SLOT: "BadSlot", HS_LENGTH_MISMATCH: "LengthMismatch", HS_TOKEN_RANGE: "TokenOutOfRange",
-    HS_INVALID_OVERLAP: "InvalidOverlap", HS_BAD_ARGUMENT: "BadArgument",
+    HS_INVALID_OVERLAP: "InvalidOverlap", HS_BAD_ARGUMENT: "BadArgument", HS_FORMAT: "Format",
+    HS_CORRUPT: "CorruptBlock", HS_MODEL_MISMATCH: "ModelHashMismatch",
 }
 
 ENCODE, DECODE = 0, 1
@@ -128,6 +130,8 @@ def lib() -> ctypes.CDLL:
     L.hs_fold_bound.restype = u64
     L.hs_fold.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(FoldOptions), vp, ctypes.c_size_t,
                           ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(FoldStats)]
+    L.hs_unfold.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t,
+                            ctypes.POINTER(ctypes.c_size_t)]
     L.hs_zstd_version.argtypes = []
     L.hs_zstd_version.restype = u32
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
@@ -203,6 +207,16 @@ def fold(batch, tokenizer, data: bytes, block_size: int = 0, overlap: int = 0, s
                          ctypes.byref(n), ctypes.byref(st)))
     stats = {name: getattr(st, name) for name, _ in FoldStats._fields_ if name != "reserved"}
     return out[:n.value].tobytes(), stats
+
+
+def unfold(batch, tokenizer, container: bytes, original_len: int | None = None) -> bytes:
+    """taco::unfold on the CUDA engine (hs_unfold): the original bytes of a .taco container."""
+    if original_len is None:
+        original_len = int.from_bytes(container[40:48], "little") if len(container) >= 48 else 0
+    out = np.zeros(max(original_len, 1), dtype=np.uint8)
+    n = ctypes.c_size_t()
+    _check(lib().hs_unfold(batch.h, tokenizer.h, container, len(container), _p(out), out.size, ctypes.byref(n)))
+    return out[:n.value].tobytes()
 
 
 def zstd_version() -> int:

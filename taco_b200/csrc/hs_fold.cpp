@@ -52,6 +52,12 @@ struct Zstd {
     size_t (*bound)(size_t) = nullptr;
     unsigned (*is_error)(size_t) = nullptr;
     unsigned (*version)() = nullptr;
+    void* (*dcreate)() = nullptr;
+    size_t (*dfree)(void*) = nullptr;
+    size_t (*dset_param)(void*, int, int) = nullptr;
+    size_t (*decompress)(void*, void*, size_t, const void*, size_t) = nullptr;
+    unsigned long long (*content_size)(const void*, size_t) = nullptr;
+    size_t (*frame_size)(const void*, size_t) = nullptr;
     bool ok = false;
 
     Zstd() {
@@ -64,7 +70,14 @@ struct Zstd {
         bound = (size_t(*)(size_t))dlsym(lib, "ZSTD_compressBound");
         is_error = (unsigned (*)(size_t))dlsym(lib, "ZSTD_isError");
         version = (unsigned (*)())dlsym(lib, "ZSTD_versionNumber");
-        ok = create && free_ctx && set_param && compress2 && bound && is_error && version;
+        dcreate = (void* (*)())dlsym(lib, "ZSTD_createDCtx");
+        dfree = (size_t(*)(void*))dlsym(lib, "ZSTD_freeDCtx");
+        dset_param = (size_t(*)(void*, int, int))dlsym(lib, "ZSTD_DCtx_setParameter");
+        decompress = (size_t(*)(void*, void*, size_t, const void*, size_t))dlsym(lib, "ZSTD_decompressDCtx");
+        content_size = (unsigned long long (*)(const void*, size_t))dlsym(lib, "ZSTD_getFrameContentSize");
+        frame_size = (size_t(*)(const void*, size_t))dlsym(lib, "ZSTD_findFrameCompressedSize");
+        ok = create && free_ctx && set_param && compress2 && bound && is_error && version && dcreate && dfree &&
+             dset_param && decompress && content_size && frame_size;
     }
 };
 
@@ -90,6 +103,27 @@ bool compress_zstd(const uint8_t* data, size_t len, std::vector<uint8_t>& out) {
         out.resize(ok ? n : 0);
     }
     z.free_ctx(cctx);
+    return ok;
+}
+
+// The bounded decoder of a zstd block (zstd_block.rs): exactly one frame, whose header gives
+// the content size, equal to the block's original length; a window of at most 2^23 bytes
+// (ZSTD_d_windowLogMax, id 100); the output written into the block's own bytes only.
+bool decompress_zstd(const uint8_t* frame, size_t n, uint8_t* out, size_t original_len) {
+    const Zstd& z = zstd();
+    static const uint8_t magic[4] = {0x28, 0xB5, 0x2F, 0xFD};
+    if (n < 4 || memcmp(frame, magic, 4) != 0) return false;
+    if (z.content_size(frame, n) != (unsigned long long)original_len) return false;
+    const size_t fs = z.frame_size(frame, n);
+    if (z.is_error(fs) || fs != n) return false;
+    void* dctx = z.dcreate();
+    if (!dctx) return false;
+    bool ok = !z.is_error(z.dset_param(dctx, 100, 23));
+    if (ok) {
+        const size_t got = z.decompress(dctx, out, original_len, frame, n);
+        ok = !z.is_error(got) && got == original_len;
+    }
+    z.dfree(dctx);
     return ok;
 }
 
@@ -374,5 +408,182 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
 }
 
 uint32_t hs_zstd_version(void) { return zstd().ok ? zstd().version() : 0; }
+
+// The header and the block table of a container (crates/taco-format/src/header.rs:220-330 and
+// reader.rs), checked: versions 1 and 2, the layout rules, and the lengths.
+struct Parsed {
+    uint16_t version = 0;
+    uint8_t model_hash[32];
+    uint64_t original_len = 0;
+    uint8_t checksum[32];
+    uint32_t block_size = 0, count = 0;
+    uint8_t profile = 0, mixer_rule = 0;
+    uint16_t overlap = 0;
+    std::vector<uint8_t> kinds;
+    std::vector<uint32_t> stored;
+    std::vector<size_t> at;  // offset of each block's stored bytes
+};
+
+static int parse_container(const uint8_t* d, size_t n, Parsed& c) {
+    auto bad = [](const std::string& why) { return hs::host_fail(HS_FORMAT, "the container is not valid: " + why); };
+    auto rd16 = [&](size_t o) { uint16_t v; memcpy(&v, d + o, 2); return v; };
+    auto rd32 = [&](size_t o) { uint32_t v; memcpy(&v, d + o, 4); return v; };
+    auto rd64 = [&](size_t o) { uint64_t v; memcpy(&v, d + o, 8); return v; };
+    if (n < 6) return bad("truncated header");
+    if (memcmp(d, "TACO", 4) != 0) return bad("bad magic");
+    c.version = rd16(4);
+    if (c.version != 1 && c.version != 2) return bad("unsupported version " + std::to_string(c.version));
+    const size_t hlen = c.version == 1 ? 88 : HEADER_LEN;
+    if (n < hlen) return bad("truncated header");
+    if (rd16(6) != 0) return bad("unknown flags");
+    memcpy(c.model_hash, d + 8, 32);
+    c.original_len = rd64(40);
+    memcpy(c.checksum, d + 48, 32);
+    c.block_size = rd32(80);
+    c.count = rd32(84);
+    if (c.block_size == 0 || c.block_size > MAX_BLOCK_SIZE) return bad("block size out of range");
+    if ((uint64_t)c.count != (c.original_len + c.block_size - 1) / c.block_size) return bad("wrong block count");
+    if (c.version == 2) {
+        c.profile = d[88];
+        const uint8_t reserved = d[89];
+        const uint16_t bits = rd16(90);
+        const uint8_t* params = d + 92;
+        if (c.profile > 1 || reserved != 0 || (bits & ~3u)) return bad("bad version 2 fields");
+        if (c.profile == 0 && (bits & 1)) return bad("the text profile has no mixer");
+        if (bits & 1) {
+            if (params[0] != 1 && params[0] != 2) return bad("unknown mixer rule");
+            c.mixer_rule = params[0];
+        } else if (params[0] != 0) {
+            return bad("mixer rule without the mixer bit");
+        }
+        uint16_t k;
+        memcpy(&k, params + 2, 2);
+        if ((bits & 2) && k == 0) return bad("overlap bit with K = 0");
+        if (!(bits & 2) && k != 0) return bad("overlap without the overlap bit");
+        c.overlap = k;
+        if (params[1] != 0) return bad("non-zero coding parameters");
+        for (int i = 4; i < 12; i++)
+            if (params[i] != 0) return bad("non-zero coding parameters");
+    }
+    const bool needs_model = std::any_of(c.model_hash, c.model_hash + 32, [](uint8_t b) { return b != 0; });
+    const uint64_t table_end = hlen + 5 * (uint64_t)c.count;
+    if (n < table_end) return bad("truncated block table");
+    uint64_t off = table_end, remaining = c.original_len;
+    c.kinds.resize(c.count);
+    c.stored.resize(c.count);
+    c.at.resize(c.count);
+    for (uint32_t i = 0; i < c.count; i++) {
+        const uint8_t kind = d[hlen + 5 * (size_t)i];
+        const uint32_t sl = rd32(hlen + 5 * (size_t)i + 1);
+        const uint64_t olen = std::min<uint64_t>(c.block_size, remaining);
+        remaining -= olen;
+        if (kind > 3 || (c.version == 1 && kind > 1)) return bad("unknown block kind");
+        if (kind == KIND_RAW && sl != olen) return bad("a raw block stores its original bytes");
+        if (kind != KIND_RAW && sl >= olen) return bad("a coded, mixed or zstd block is not smaller than its bytes");
+        if ((kind == KIND_CODED || kind == 3) && !needs_model) return bad("a coded block needs a model");
+        if (kind == 3 && c.mixer_rule == 0) return bad("a mixed block needs the mixer bit");
+        if (off + sl > n) return bad("truncated block");
+        c.kinds[i] = kind;
+        c.stored[i] = sl;
+        c.at[i] = (size_t)off;
+        off += sl;
+    }
+    if (off != n) return bad("extra bytes after the last block");
+    return HS_OK;
+}
+
+int hs_unfold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* container, size_t len, uint8_t* out,
+              size_t cap, size_t* out_len) {
+    if (!batch || !tok || !out_len || (len && !container)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    Parsed c;
+    int rc = parse_container(container, len, c);
+    if (rc) return rc;
+    *out_len = (size_t)c.original_len;
+    if (cap < c.original_len || (!out && c.original_len))
+        return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
+                                                  std::to_string(c.original_len) + " needed");
+    hs_model_info info;
+    if ((rc = hs_model_get_info(hs::batch_model(batch), &info))) return rc;
+    // unfold.rs:157-180 checked_model: a container that names a model needs that model.
+    if (std::any_of(c.model_hash, c.model_hash + 32, [](uint8_t b) { return b != 0; }) &&
+        memcmp(c.model_hash, info.hash, 32) != 0)
+        return hs::host_fail(HS_MODEL_MISMATCH, "the container was folded with another model");
+    for (uint32_t i = 0; i < c.count; i++)
+        if (c.kinds[i] == 3)
+            return hs::host_fail(HS_UNSUPPORTED, "block " + std::to_string(i) +
+                                                     " is a mixed block (profile logs): its unfold needs the "
+                                                     "match model and the mixer of the caller");
+    if ((rc = hs_batch_set_overlap(batch, c.overlap))) return rc;
+    auto corrupt = [](uint32_t i, const std::string& why) {
+        return hs::host_fail(HS_CORRUPT, "block " + std::to_string(i) + " is corrupt: " + why);
+    };
+    // Raw and zstd blocks on the host; the coded ones collected for the GPU.
+    std::vector<uint32_t> coded;
+    for (uint32_t i = 0; i < c.count; i++) {
+        const size_t o = (size_t)i * c.block_size;
+        const size_t olen = (size_t)std::min<uint64_t>(c.block_size, c.original_len - o);
+        if (c.kinds[i] == KIND_RAW) memcpy(out + o, container + c.at[i], olen);
+        else if (c.kinds[i] == KIND_ZSTD && !decompress_zstd(container + c.at[i], c.stored[i], out + o, olen))
+            return corrupt(i, "the zstd frame does not give the block");
+        else if (c.kinds[i] == KIND_CODED) coded.push_back(i);
+    }
+    // The coded blocks: the varint token count (1 .. the block length), then the coder bytes,
+    // decoded on the device in rounds of up to min(slots, max_rows) blocks (codec.rs:370-520
+    // BlockDecoder, with the decoder of hs_batch_decode_blocks), then the tokens' bytes.
+    const size_t per = std::max<size_t>(1, std::min(hs::batch_slots(batch), hs::batch_max_rows(batch)));
+    for (size_t r0 = 0; r0 < coded.size(); r0 += per) {
+        const size_t r1 = std::min(coded.size(), r0 + per), m = r1 - r0;
+        std::vector<uint32_t> slots(m), counts(m), status(m);
+        std::vector<uint64_t> offs(m), lens(m), toff(m);
+        uint64_t total = 0;
+        for (size_t j = 0; j < m; j++) {
+            const uint32_t i = coded[r0 + j];
+            const uint8_t* p = container + c.at[i];
+            const size_t sl = c.stored[i];
+            uint64_t count = 0;
+            size_t k = 0;
+            for (int shift = 0;; shift += 7, k++) {
+                if (k >= sl || shift > 63) return corrupt(i, "the token count is not valid");
+                count |= (uint64_t)(p[k] & 0x7F) << shift;
+                if (!(p[k] & 0x80)) break;
+            }
+            k++;
+            const size_t olen = (size_t)std::min<uint64_t>(c.block_size, c.original_len - (uint64_t)i * c.block_size);
+            if (count == 0 || count > olen) return corrupt(i, "the token count does not agree with the block length");
+            slots[j] = (uint32_t)j;
+            counts[j] = (uint32_t)count;
+            offs[j] = c.at[i] + k;
+            lens[j] = sl - k;
+            toff[j] = total;
+            total += count;
+        }
+        std::vector<uint32_t> toks(std::max<uint64_t>(total, 1));
+        if ((rc = hs_batch_decode_blocks(batch, (uint32_t)m, slots.data(), container, len, offs.data(), lens.data(),
+                                         counts.data(), FREQ_BITS, toks.data(), total, toff.data(), status.data())))
+            return rc;
+        for (size_t j = 0; j < m; j++) {
+            const uint32_t i = coded[r0 + j];
+            if (status[j]) return corrupt(i, "an interval does not hold its target");
+            const size_t o = (size_t)i * c.block_size;
+            const size_t olen = (size_t)std::min<uint64_t>(c.block_size, c.original_len - o);
+            size_t at = 0;
+            for (uint32_t t = 0; t < counts[j]; t++) {
+                size_t nb;
+                const uint32_t id = toks[toff[j] + t];
+                const uint8_t* b = hs::token_bytes(tok, id, &nb);
+                if (id == info.eot_token || nb == 0 || nb > olen - at)
+                    return corrupt(i, "the tokens do not give the block length");
+                memcpy(out + o + at, b, nb);
+                at += nb;
+            }
+            if (at != olen) return corrupt(i, "the tokens do not give the block length");
+        }
+    }
+    uint8_t sum[32];
+    hs::sha256(out, (size_t)c.original_len, sum);
+    if (memcmp(sum, c.checksum, 32) != 0)
+        return hs::host_fail(HS_CORRUPT, "the restored bytes do not have the container's SHA-256");
+    return HS_OK;
+}
 
 }  // extern "C"

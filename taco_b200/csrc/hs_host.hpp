@@ -23,6 +23,10 @@ namespace hs {
 // The model of a batch, and its slot count.
 hs_model* batch_model(hs_batch* b);
 uint32_t batch_slots(const hs_batch* b);
+uint32_t batch_max_rows(const hs_batch* b);
+
+// The bytes of token `id` (empty for an id out of range).
+const uint8_t* token_bytes(const hs_tokenizer* t, uint32_t id, size_t* n);
 
 // Tokenizer::encode, and the check of crates/taco/src/codec.rs:55 tokens_restore: the bytes of
 // `tokens` (none of them EOT or empty) join to data[0 .. len).

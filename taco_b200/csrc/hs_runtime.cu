@@ -1661,3 +1661,4 @@ int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, co
 
 hs_model* hs::batch_model(hs_batch* b) { return b->model; }
 uint32_t hs::batch_slots(const hs_batch* b) { return (uint32_t)b->slots; }
+uint32_t hs::batch_max_rows(const hs_batch* b) { return (uint32_t)b->max_rows; }

@@ -297,6 +297,16 @@ void tokenize(const hs_tokenizer* t, const uint8_t* data, size_t len, std::vecto
     t->encode(data, len, out);
 }
 
+const uint8_t* token_bytes(const hs_tokenizer* t, uint32_t id, size_t* n) {
+    if (id >= t->vocab) {
+        *n = 0;
+        return nullptr;
+    }
+    const size_t a = id ? t->ends[id - 1] : 0;
+    *n = t->ends[id] - a;
+    return t->bytes.data() + a;
+}
+
 bool tokens_restore(const hs_tokenizer* t, const uint32_t* tokens, size_t n, const uint8_t* data, size_t len) {
     size_t at = 0;
     for (size_t i = 0; i < n; i++) {

@@ -99,3 +99,52 @@ def test_a_larger_input_folds_and_every_block_decodes(setup):
             assert stats["coded_blocks"] > 0
         out = b"".join(_decode(om, c, b) for b in c.blocks)
         assert out == data
+
+
+@pytest.mark.parametrize("name", TEXT_VECTORS)
+def test_unfold_gives_the_published_inputs(setup, name):
+    batch, tok = setup
+    want = (GOLDEN / (name + ".in")).read_bytes()
+    assert B.unfold(batch, tok, (GOLDEN / (name + ".taco")).read_bytes()) == want
+
+
+def test_fold_then_unfold_round_trips(setup):
+    batch, tok = setup
+    rng = np.random.default_rng(12)
+    pred = (GOLDEN / "predicted_text_k32.in").read_bytes()
+    data = pred * 3 + rng.integers(0, 256, 333, dtype=np.uint8).tobytes() + pred
+    for bs, k in [(300, 32), (64, 0), (5000, 7)]:
+        got, stats = B.fold(batch, tok, data, bs, k)
+        assert B.unfold(batch, tok, got) == data
+
+
+def test_unfold_refuses_bad_containers(setup):
+    batch, tok = setup
+    good = (GOLDEN / "all_kinds_text.taco").read_bytes()
+
+    def code(blob):
+        with pytest.raises(B.HardShellError) as e:
+            B.unfold(batch, tok, blob, original_len=1 << 16)
+        return e.value.code
+
+    assert code(b"TACX" + good[4:]) == B.HS_FORMAT
+    assert code(good[:-1]) == B.HS_FORMAT
+    assert code(good + b"\0") == B.HS_FORMAT
+    c = C.parse(good)
+    other = bytearray(good)
+    other[8] ^= 1  # another model's hash
+    assert code(bytes(other)) == B.HS_MODEL_MISMATCH
+    wrong_sum = bytearray(good)
+    wrong_sum[48] ^= 1
+    assert code(bytes(wrong_sum)) == B.HS_CORRUPT
+    # A damaged coded block: its tokens no longer give its bytes (or an interval misses).
+    coded = next(b for b in c.blocks if b.kind == C.KIND_CODED)
+    c2 = C.parse(good)
+    blk = c2.blocks[coded.index]
+    blk.stored = blk.stored[:2] + bytes(x ^ 0x5A for x in blk.stored[2:])
+    assert code(C.build(c2)) == B.HS_CORRUPT
+    # A mixed block (profile logs) needs the caller's mixer.
+    c3 = C.parse(good)
+    c3.profile, c3.mixer_rule = C.PROFILE_LOGS, 1
+    c3.blocks[coded.index].kind = C.KIND_MIXED
+    assert code(C.build(c3)) == B.HS_UNSUPPORTED
