@@ -21,8 +21,9 @@ roofline = the kernel with the largest share of the pass time: algorithmic int8 
 cpu_baseline = the CPU oracle's fast path (a C++ restatement of the reference CPU engine) on a
          bounded sample of the same windows, all host threads, rank 0 at N = 1.
 Extra fields: the GEMM microbench, the unfold decode step, the unfold of
-coded blocks with the range decoder on the device, and the encoder op of the profile logs
-(run_coded_dual). `--only fold_dual` runs the last alone on --windows windows (a profiling case).
+coded blocks with the range decoder on the device, the encoder op of the profile logs
+(run_coded_dual), and the fold and unfold of the host library end to end (hs_fold, hs_unfold).
+`--only fold_dual|fold_glue` runs one of the last two alone (profiling cases).
 """
 
 from __future__ import annotations
@@ -61,7 +62,8 @@ def parse_args():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-peak", action="store_true", help="skip the int8 peak measurement (profiling runs)")
-    ap.add_argument("--only", default="", choices=["", "fold_dual"], help="run one extra alone (profiling runs)")
+    ap.add_argument("--only", default="", choices=["", "fold_dual", "fold_glue"],
+                    help="run one extra alone (profiling runs)")
     return ap.parse_args()
 
 
@@ -299,10 +301,13 @@ def main():
     slots, inputs, coded = window_rows(windows, eot)
     kinds = np.zeros(slots.size, np.uint32)
     step_bytes = int(lens[coded.astype(np.int64)].sum())
-    if args.only == "fold_dual":
+    if args.only:
         dev = B.CudaDevice(local)
         model = B.CudaModel(dev, model_bytes)
-        print(json.dumps({"fold_dual": fold_dual(B, model, windows, lens, eot, sample=args.windows)}))
+        if args.only == "fold_dual":
+            print(json.dumps({"fold_dual": fold_dual(B, model, windows, lens, eot, sample=args.windows)}))
+        else:
+            print(json.dumps({"fold_glue": fold_glue(B, model, model_bytes, vocab)}))
         model.close()
         dev.close()
         return 0
@@ -407,6 +412,7 @@ def main():
         result["unfold"] = unfold_step(B, model, lens, eot, clock_note=None)
         result["unfold_blocks"] = unfold_blocks(B, model)
         result["fold_dual"] = fold_dual(B, model, windows, lens, eot)
+        result["fold_glue"] = fold_glue(B, model, model_bytes, vocab)
     if rank == 0:
         if world == 1 and not args.no_cpu:
             threads = args.cpu_threads or os.cpu_count() or 1
@@ -557,6 +563,48 @@ def fold_dual(B, model, windows, lens, eot, sample: int = 64) -> dict:
                      "coder_launches": prof["coder"]["launches"]}
     batch.close()
     return out
+
+
+def fold_glue(B, model, model_bytes, vocab, mb: int = 2) -> dict:
+    """The fold and the unfold of the profile text end to end through the host library (hs_fold,
+    hs_unfold: tokenizer, zstd level 19, the coder op on the GPU, range encoder, container) on `mb`
+    MiB of seeded Zipf text (the bytes of the synthetic vocabulary's word tokens), default block
+    size 16 KiB, one slot per block. The synthetic vocabulary has no merges, so the tokenizer gives
+    one token per byte (about 4.6 times the rows of the bench's token windows per byte). Timed by
+    the wall clock (the better of two); the device time of the fold's passes from a third,
+    profiled call. A random-initialised model rarely beats zstd, so the unfold mostly decodes zstd
+    frames: it measures the glue, not the coder."""
+    from taco_b200 import synth
+
+    w = synth.zipf_windows(256, 1024, seed=4242)
+    text = b"".join(vocab[t] for t in w.reshape(-1).tolist())[: mb << 20]
+    tok = B.Tokenizer(model_bytes)
+    batch = B.CudaBatch(model, 256, 16384)
+    B.fold(batch, tok, text[:20000])  # warm-up
+    wall = float("inf")
+    for _ in range(2):
+        t0 = time.perf_counter()
+        got, stats = B.fold(batch, tok, text)
+        wall = min(wall, time.perf_counter() - t0)
+    batch.set_profiling(True)
+    B.fold(batch, tok, text)
+    prof = batch.profile()
+    batch.set_profiling(False)
+    uwall = float("inf")
+    for _ in range(2):
+        t0 = time.perf_counter()
+        back = B.unfold(batch, tok, got)
+        uwall = min(uwall, time.perf_counter() - t0)
+    if back != text:
+        raise SystemExit("the unfold did not give the input back")
+    batch.close()
+    tok.close()
+    return {"input_bytes": len(text), "blocks": stats["blocks"], "tokens": stats["tokens"],
+            "coded_blocks": stats["coded_blocks"], "zstd_blocks": stats["zstd_blocks"],
+            "container_bytes": stats["container_len"],
+            "fold_e2e_MB_per_s": len(text) / wall / 1e6, "fold_device_ms": round(prof["pass"]["ms"], 3),
+            "fold_wall_ms": round(wall * 1e3, 3), "fold_device_share": round(prof["pass"]["ms"] / (wall * 1e3), 3),
+            "unfold_e2e_MB_per_s": len(text) / uwall / 1e6}
 
 
 if __name__ == "__main__":

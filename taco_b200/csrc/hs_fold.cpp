@@ -279,41 +279,69 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
         return hs::host_fail(HS_MODEL, "the tokens of block " + std::to_string(bad_tokens.load()) +
                                            " do not give its bytes back (TokenizerRoundTrip)");
     if (bad_zstd >= 0) return hs::host_fail(HS_CUDA, "zstd failed on block " + std::to_string(bad_zstd.load()));
-    // 3. The intervals on the GPU: rounds of up to `slots` blocks, slot-major rows. A block whose
-    // payload prefix already reaches its bound needs none.
+    // 3. The intervals on the GPU. A block's inputs are x_0 = EOT, x_j = t_(j-1) (input j codes
+    // t_j). In one slot its context restarts after every n_ctx positions with EOT and the last K
+    // inputs (crates/hardshell/src/gpt2/context.rs), so the block divides into context windows:
+    // window 0 is inputs 0 .. n_ctx - 1, each later window the next n_ctx - K - 1 inputs. A window
+    // runs in a fresh slot of its own as EOT, its K overlap inputs (whose answers are not used)
+    // and its inputs, the same rows as the restart (crates/taco/src/gpu_fold.rs Window::rows), so
+    // the windows of all blocks run side by side in full passes. A block whose payload prefix
+    // already reaches its bound needs none.
     const uint32_t slots = hs::batch_slots(batch);
+    const size_t n_ctx = info.n_ctx, K = std::min<size_t>(opt->overlap, n_ctx - 2);
     auto stop_of = [&](const FoldBlock& b) { return std::min(b.len, b.zstd.size()); };
+    struct Window {
+        size_t block, start, count;
+    };
+    std::vector<Window> windows;
+    for (size_t i = 0; i < nblocks; i++) {
+        FoldBlock& b = blocks[i];
+        if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
+        b.intervals.resize(b.tokens.size());
+        for (size_t s0 = 0; s0 < b.tokens.size();) {
+            const size_t c = std::min(b.tokens.size() - s0, s0 == 0 ? n_ctx : n_ctx - K - 1);
+            windows.push_back({i, s0, c});
+            s0 += c;
+        }
+    }
     std::vector<uint32_t> s_slot, s_tok, s_kind;
     std::vector<uint64_t> s_val;
     std::vector<hs_interval> ivs;
-    for (size_t r0 = 0; r0 < nblocks; r0 += slots) {
-        const size_t r1 = std::min(nblocks, r0 + slots);
+    std::vector<size_t> first;
+    for (size_t w0 = 0; w0 < windows.size(); w0 += slots) {
+        const size_t w1 = std::min(windows.size(), w0 + slots);
         s_slot.clear();
         s_tok.clear();
         s_val.clear();
-        std::vector<size_t> first(r1 - r0);
-        for (size_t i = r0; i < r1; i++) {
-            const FoldBlock& b = blocks[i];
-            const uint32_t s = (uint32_t)(i - r0);
-            first[i - r0] = s_slot.size();
-            if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
-            if ((rc = hs_batch_reset(batch, s))) return rc;
-            for (size_t j = 0; j < b.tokens.size(); j++) {
-                s_slot.push_back(s);
-                s_tok.push_back(j ? b.tokens[j - 1] : info.eot_token);
-                s_val.push_back(b.tokens[j]);
+        first.assign(w1 - w0, 0);
+        for (size_t w = w0; w < w1; w++) {
+            const Window& win = windows[w];
+            const std::vector<uint32_t>& t = blocks[win.block].tokens;
+            const uint32_t slot = (uint32_t)(w - w0);
+            if ((rc = hs_batch_reset(batch, slot))) return rc;
+            auto row = [&](size_t j) {  // input j of the block, coding t_j
+                s_slot.push_back(slot);
+                s_tok.push_back(j ? t[j - 1] : info.eot_token);
+                s_val.push_back(t[j]);
+            };
+            if (win.start > 0) {
+                s_slot.push_back(slot);  // the restart's EOT row
+                s_tok.push_back(info.eot_token);
+                s_val.push_back(0);
+                for (size_t j = win.start - K; j < win.start; j++) row(j);
             }
+            first[w - w0] = s_slot.size();
+            for (size_t j = win.start; j < win.start + win.count; j++) row(j);
         }
         s_kind.assign(s_slot.size(), 0);
         ivs.resize(s_slot.size());
-        if (!s_slot.empty() &&
-            (rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
+        if ((rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
                                      (uint32_t)s_slot.size(), FREQ_BITS, ivs.data())))
             return rc;
-        for (size_t i = r0; i < r1; i++) {
-            FoldBlock& b = blocks[i];
-            if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
-            b.intervals.assign(ivs.begin() + first[i - r0], ivs.begin() + first[i - r0] + b.tokens.size());
+        for (size_t w = w0; w < w1; w++) {
+            const Window& win = windows[w];
+            std::copy(ivs.begin() + first[w - w0], ivs.begin() + first[w - w0] + win.count,
+                      blocks[win.block].intervals.begin() + win.start);
         }
     }
     // 4.-5. The range encoder with the stop rule, then the smallest form.
