@@ -1220,11 +1220,19 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder_mix(const uint16_t* d16
     W = block_sum64(W, redu) + wpm;
     const bool all_zero = W == 0;  // a plain row whose weights are all 0: every weight counts 1
     const uint64_t Wo = has_o ? g(lo) : 0;
-    int32_t gh = -1;
-    if (has_o)
-        for (int j = lo + threadIdx.x; j <= last; j += CODER_THREADS)
-            if (g(j) == Wo) gh = j > gh ? j : gh;
-    gh = (int32_t)block_max64(gh, red);
+    // gh: g does not increase, so g(d) == g(lo) exactly on [lo, gh]; a binary search.
+    __shared__ int32_t s_gh;
+    if (threadIdx.x == 0) {
+        int32_t a = lo, b = last;
+        while (has_o && a < b) {
+            const int32_t mid = a + (b - a + 1) / 2;
+            if (g(mid) == Wo) a = mid;
+            else b = mid - 1;
+        }
+        s_gh = has_o ? a : -1;
+    }
+    __syncthreads();
+    const int32_t gh = s_gh;
     const uint64_t Wmax = Wo > wpm ? Wo : wpm;
     const bool cand_p = has_p && wpm == Wmax;
     const bool cand_o = has_o && Wo == Wmax;
