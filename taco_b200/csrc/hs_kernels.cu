@@ -248,7 +248,7 @@ __device__ __noinline__ int64_t ln_exact(int64_t cg, i128 u, int s, int32_t b, i
 // 4-byte word), and the row width is a compile-time constant, so the divisions by it become
 // multiplications.
 template <int NV>
-__global__ void __launch_bounds__(256, 3) k_resid_ln_v(int32_t* x, const int32_t* delta, int R, LnDev ln, int ln_k,
+__global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t* delta, int R, LnDev ln, int ln_k,
                                                        int ln_j, uint64_t eps, int8_t* out, int ldo, int8_t* out_lo) {
     constexpr int D = 128 * NV;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
