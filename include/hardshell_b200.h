@@ -227,8 +227,8 @@ uint64_t hs_fold_bound(uint64_t len, uint32_t block_size);
  * the tokenizer, zstd and the range encoder run on host threads. zstd comes from the system
  * library (libzstd.so.1, hs_zstd_version); the reference pins zstd 1.5.7, and a zstd frame of
  * another version can differ in its bytes (it decodes to the same block). *out_len = the container
- * length; HS_BAD_ARGUMENT if it is more than cap (see hs_fold_bound). The slots of the batch are
- * left with the last blocks' contexts. */
+ * length; HS_BAD_ARGUMENT if it is more than cap (see hs_fold_bound). The batch keeps the fold's
+ * overlap, and its slots the contexts of the last windows. */
 int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input, size_t len,
             const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats);
 

@@ -259,6 +259,7 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
     if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
     if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
     const size_t nblocks = (size_t)((len + bs - 1) / bs);
+    if (nblocks > 0xFFFFFFFFull) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
     const uint64_t need = HEADER_LEN + 5 * (uint64_t)nblocks + len;
     const unsigned threads = opt->threads ? opt->threads : std::max(1u, std::thread::hardware_concurrency());
     std::vector<FoldBlock> blocks(nblocks);
