@@ -95,7 +95,7 @@ int utf8_char(const uint8_t* p, const uint8_t* end, uint32_t* cp) {
 }
 
 struct Char {
-    uint32_t off;  // byte offset of the character in the input
+    size_t off;  // byte offset of the character in the input
     uint32_t cp;
     CharClass cls;
 };
@@ -202,13 +202,13 @@ struct hs_tokenizer {
             uint32_t cp;
             int nb;
             while (i < len && (nb = utf8_char(data + i, data + len, &cp)) > 0) {
-                ch.push_back({(uint32_t)i, cp, class_of(cp)});
+                ch.push_back({i, cp, class_of(cp)});
                 i += (size_t)nb;
             }
             const size_t run_end = i;
             for (size_t c = 0; c < ch.size();) {
                 const size_t e = piece_end(ch, c);
-                on_piece((size_t)ch[c].off, e < ch.size() ? (size_t)ch[e].off : run_end, true);
+                on_piece(ch[c].off, e < ch.size() ? ch[e].off : run_end, true);
                 c = e;
             }
             if (i < len) {
