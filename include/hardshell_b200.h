@@ -232,6 +232,16 @@ uint64_t hs_fold_bound(uint64_t len, uint32_t block_size);
 int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input, size_t len,
             const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats);
 
+/* hs_fold on several GPUs of this host (crates/taco/src/gpu_fold.rs:128-186): one host thread
+ * per GPU opens device ordinals[g], loads the model file (the tokenizer must be of that model),
+ * makes a batch of `slots` slots and passes of `max_rows` rows, and runs the context windows
+ * dealt to it round-robin; the host stages are shared. The container is the bytes hs_fold gives
+ * on one GPU. An error of a GPU thread comes back with its status and message. */
+int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                  uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* input,
+                  size_t len, const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len,
+                  hs_fold_stats* stats);
+
 /* taco::unfold on the CUDA engine (crates/taco/src/unfold.rs, profile text): the original bytes of
  * a .taco container (version 1 or 2) into out[0 .. *out_len). The header and the block table are
  * checked as crates/taco-format/src/reader.rs checks them (HS_FORMAT); a container that names a

@@ -130,6 +130,9 @@ def lib() -> ctypes.CDLL:
     L.hs_fold_bound.restype = u64
     L.hs_fold.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(FoldOptions), vp, ctypes.c_size_t,
                           ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(FoldStats)]
+    L.hs_fold_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, ctypes.c_char_p,
+                                ctypes.c_size_t, ctypes.POINTER(FoldOptions), vp, ctypes.c_size_t,
+                                ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(FoldStats)]
     L.hs_unfold.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t,
                             ctypes.POINTER(ctypes.c_size_t)]
     L.hs_zstd_version.argtypes = []
@@ -205,6 +208,21 @@ def fold(batch, tokenizer, data: bytes, block_size: int = 0, overlap: int = 0, s
     st = FoldStats()
     _check(lib().hs_fold(batch.h, tokenizer.h, data, len(data), ctypes.byref(opt), _p(out), out.size,
                          ctypes.byref(n), ctypes.byref(st)))
+    stats = {name: getattr(st, name) for name, _ in FoldStats._fields_ if name != "reserved"}
+    return out[:n.value].tobytes(), stats
+
+
+def fold_multi(ordinals, model_file: bytes, tokenizer, data: bytes, block_size: int = 0, overlap: int = 0,
+               slots: int = 256, max_rows: int = 16384, spread: bool = False, threads: int = 0):
+    """hs_fold_multi: the fold of `data` on the GPUs `ordinals`, one host thread each."""
+    ords = np.ascontiguousarray(ordinals, dtype=np.int32)
+    opt = FoldOptions(block_size, overlap, int(spread), threads)
+    cap = int(lib().hs_fold_bound(len(data), block_size))
+    out = np.zeros(max(cap, 1), dtype=np.uint8)
+    n = ctypes.c_size_t()
+    st = FoldStats()
+    _check(lib().hs_fold_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows, tokenizer.h, data,
+                               len(data), ctypes.byref(opt), _p(out), out.size, ctypes.byref(n), ctypes.byref(st)))
     stats = {name: getattr(st, name) for name, _ in FoldStats._fields_ if name != "reserved"}
     return out[:n.value].tobytes(), stats
 

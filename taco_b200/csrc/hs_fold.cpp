@@ -19,6 +19,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <functional>
 #include <atomic>
 #include <cstdint>
 #include <cstring>
@@ -239,14 +240,76 @@ uint64_t hs_fold_bound(uint64_t len, uint32_t block_size) {
     return HEADER_LEN + 5 * ((len + bs - 1) / bs) + len;
 }
 
-int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt,
-            uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
-    if (!batch || !tok || !opt || !out_len || (len && !input)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+}  // extern "C"
+
+namespace {
+
+// A context window of a block: inputs start .. start + count - 1 of the block's token stream.
+struct Window {
+    size_t block, start, count;
+};
+
+// The GPU stage for the windows `mine` (indices into `windows`) on one batch whose overlap is
+// K: rounds of up to `slots` windows, one fresh slot each, slot-major rows. A window runs as EOT,
+// its K overlap inputs (answers not used) and its own inputs, the rows of the context restart
+// (crates/taco/src/gpu_fold.rs Window::rows); the answers of its own inputs go to their block.
+int run_windows(hs_batch* batch, uint32_t eot, size_t K, const std::vector<Window>& windows,
+                const std::vector<size_t>& mine, std::vector<FoldBlock>& blocks) {
+    const uint32_t slots = hs::batch_slots(batch);
+    std::vector<uint32_t> s_slot, s_tok, s_kind;
+    std::vector<uint64_t> s_val;
+    std::vector<hs_interval> ivs;
+    std::vector<size_t> first;
+    int rc;
+    for (size_t m0 = 0; m0 < mine.size(); m0 += slots) {
+        const size_t m1 = std::min(mine.size(), m0 + slots);
+        s_slot.clear();
+        s_tok.clear();
+        s_val.clear();
+        first.assign(m1 - m0, 0);
+        for (size_t m = m0; m < m1; m++) {
+            const Window& win = windows[mine[m]];
+            const std::vector<uint32_t>& t = blocks[win.block].tokens;
+            const uint32_t slot = (uint32_t)(m - m0);
+            if ((rc = hs_batch_reset(batch, slot))) return rc;
+            auto row = [&](size_t j) {  // input j of the block, coding t_j
+                s_slot.push_back(slot);
+                s_tok.push_back(j ? t[j - 1] : eot);
+                s_val.push_back(t[j]);
+            };
+            if (win.start > 0) {
+                s_slot.push_back(slot);  // the restart's EOT row
+                s_tok.push_back(eot);
+                s_val.push_back(0);
+                for (size_t j = win.start - K; j < win.start; j++) row(j);
+            }
+            first[m - m0] = s_slot.size();
+            for (size_t j = win.start; j < win.start + win.count; j++) row(j);
+        }
+        s_kind.assign(s_slot.size(), 0);
+        ivs.resize(s_slot.size());
+        if ((rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
+                                     (uint32_t)s_slot.size(), FREQ_BITS, ivs.data())))
+            return rc;
+        for (size_t m = m0; m < m1; m++) {
+            const Window& win = windows[mine[m]];
+            std::copy(ivs.begin() + first[m - m0], ivs.begin() + first[m - m0] + win.count,
+                      blocks[win.block].intervals.begin() + win.start);
+        }
+    }
+    return HS_OK;
+}
+
+// The GPU stage of a fold: fills the intervals of every window (the blocks' interval arrays are
+// sized; the windows of one block never overlap, so GPUs may fill them side by side).
+using GpuStage = std::function<int(const std::vector<Window>&, std::vector<FoldBlock>&)>;
+
+// The fold of fold_with (steps 1, 2, 4, 5 and the container) around a GPU stage, for a model
+// with this hash, EOT token and context length.
+int fold_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, const GpuStage& gpu,
+              const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt, uint8_t* out,
+              size_t cap, size_t* out_len, hs_fold_stats* stats) {
     if (!zstd().ok) return hs::host_fail(HS_UNSUPPORTED, "the zstd library (libzstd.so.1) is not available");
-    hs_model* model = hs::batch_model(batch);
-    hs_model_info info;
-    int rc = hs_model_get_info(model, &info);
-    if (rc) return rc;
     // FoldOptions::block_size_for (fold.rs:159-170): a set size, or 16 KiB; with `spread`, the
     // power of two that makes about 64 blocks, within 4 KiB .. 16 KiB.
     uint64_t bs = opt->block_size ? opt->block_size : DEFAULT_BLOCK_SIZE;
@@ -256,8 +319,6 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
         bs = std::min<uint64_t>(std::max<uint64_t>(p2, SPREAD_MIN_BLOCK), DEFAULT_BLOCK_SIZE);
     }
     if (bs == 0 || bs > MAX_BLOCK_SIZE) return hs::host_fail(HS_UNSUPPORTED, "the block size is out of range");
-    if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
-    if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
     const size_t nblocks = (size_t)((len + bs - 1) / bs);
     if (nblocks > 0xFFFFFFFFull) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
     const uint64_t need = HEADER_LEN + 5 * (uint64_t)nblocks + len;
@@ -267,6 +328,7 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
         blocks[i].off = i * bs;
         blocks[i].len = std::min<size_t>(bs, len - i * bs);
     }
+    int rc;
     // 2. Tokens and zstd frames on the host threads.
     std::atomic<int> bad_tokens{-1}, bad_zstd{-1};
     parallel_for(nblocks, threads, [&](size_t i) {
@@ -283,68 +345,23 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
     // 3. The intervals on the GPU. A block's inputs are x_0 = EOT, x_j = t_(j-1) (input j codes
     // t_j). In one slot its context restarts after every n_ctx positions with EOT and the last K
     // inputs (crates/hardshell/src/gpt2/context.rs), so the block divides into context windows:
-    // window 0 is inputs 0 .. n_ctx - 1, each later window the next n_ctx - K - 1 inputs. A window
-    // runs in a fresh slot of its own as EOT, its K overlap inputs (whose answers are not used)
-    // and its inputs, the same rows as the restart (crates/taco/src/gpu_fold.rs Window::rows), so
-    // the windows of all blocks run side by side in full passes. A block whose payload prefix
-    // already reaches its bound needs none.
-    const uint32_t slots = hs::batch_slots(batch);
-    const size_t n_ctx = info.n_ctx, K = std::min<size_t>(opt->overlap, n_ctx - 2);
+    // window 0 is inputs 0 .. n_ctx - 1, each later window the next n_ctx - K - 1 inputs. Each
+    // window runs in a fresh slot of its own (run_windows), so the windows of all blocks run side
+    // by side in full passes. A block whose payload prefix already reaches its bound needs none.
+    const size_t K = std::min<size_t>(opt->overlap, n_ctx - 2);
     auto stop_of = [&](const FoldBlock& b) { return std::min(b.len, b.zstd.size()); };
-    struct Window {
-        size_t block, start, count;
-    };
     std::vector<Window> windows;
     for (size_t i = 0; i < nblocks; i++) {
         FoldBlock& b = blocks[i];
         if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
         b.intervals.resize(b.tokens.size());
         for (size_t s0 = 0; s0 < b.tokens.size();) {
-            const size_t c = std::min(b.tokens.size() - s0, s0 == 0 ? n_ctx : n_ctx - K - 1);
+            const size_t c = std::min(b.tokens.size() - s0, s0 == 0 ? (size_t)n_ctx : n_ctx - K - 1);
             windows.push_back({i, s0, c});
             s0 += c;
         }
     }
-    std::vector<uint32_t> s_slot, s_tok, s_kind;
-    std::vector<uint64_t> s_val;
-    std::vector<hs_interval> ivs;
-    std::vector<size_t> first;
-    for (size_t w0 = 0; w0 < windows.size(); w0 += slots) {
-        const size_t w1 = std::min(windows.size(), w0 + slots);
-        s_slot.clear();
-        s_tok.clear();
-        s_val.clear();
-        first.assign(w1 - w0, 0);
-        for (size_t w = w0; w < w1; w++) {
-            const Window& win = windows[w];
-            const std::vector<uint32_t>& t = blocks[win.block].tokens;
-            const uint32_t slot = (uint32_t)(w - w0);
-            if ((rc = hs_batch_reset(batch, slot))) return rc;
-            auto row = [&](size_t j) {  // input j of the block, coding t_j
-                s_slot.push_back(slot);
-                s_tok.push_back(j ? t[j - 1] : info.eot_token);
-                s_val.push_back(t[j]);
-            };
-            if (win.start > 0) {
-                s_slot.push_back(slot);  // the restart's EOT row
-                s_tok.push_back(info.eot_token);
-                s_val.push_back(0);
-                for (size_t j = win.start - K; j < win.start; j++) row(j);
-            }
-            first[w - w0] = s_slot.size();
-            for (size_t j = win.start; j < win.start + win.count; j++) row(j);
-        }
-        s_kind.assign(s_slot.size(), 0);
-        ivs.resize(s_slot.size());
-        if ((rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
-                                     (uint32_t)s_slot.size(), FREQ_BITS, ivs.data())))
-            return rc;
-        for (size_t w = w0; w < w1; w++) {
-            const Window& win = windows[w];
-            std::copy(ivs.begin() + first[w - w0], ivs.begin() + first[w - w0] + win.count,
-                      blocks[win.block].intervals.begin() + win.start);
-        }
-    }
+    if (!windows.empty() && (rc = gpu(windows, blocks))) return rc;
     // 4.-5. The range encoder with the stop rule, then the smallest form.
     parallel_for(nblocks, threads, [&](size_t i) {
         FoldBlock& b = blocks[i];
@@ -410,7 +427,7 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
     put("TACO", 4);
     put16(2);  // version
     put16(0);  // flags
-    put(info.hash, 32);
+    put(model_hash, 32);
     put64(len);
     uint8_t sum[32];
     hs::sha256(input, len, sum);
@@ -434,6 +451,92 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
         else put(b.stored.data(), b.stored.size());
     }
     return HS_OK;
+}
+
+// FoldPlan::new (fold.rs:388-395): the tokenizer must have the model's vocabulary.
+int check_tokenizer(const hs_tokenizer* tok, uint32_t vocab) {
+    uint32_t tv, te, tc;
+    hs::tokenizer_info(tok, &tv, &te, &tc);
+    if (tv != vocab)
+        return hs::host_fail(HS_MODEL, "the tokenizer has " + std::to_string(tv) + " tokens, the model " +
+                                           std::to_string(vocab) + " (TokenizerMismatch)");
+    return HS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt,
+            uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
+    if (!batch || !tok || !opt || !out_len || (len && !input)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    hs_model_info info;
+    int rc = hs_model_get_info(hs::batch_model(batch), &info);
+    if (rc || (rc = check_tokenizer(tok, info.vocab))) return rc;
+    if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
+    if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
+    const size_t K = std::min<size_t>(opt->overlap, info.n_ctx - 2);
+    GpuStage gpu = [&](const std::vector<Window>& windows, std::vector<FoldBlock>& blocks) {
+        std::vector<size_t> all(windows.size());
+        for (size_t w = 0; w < all.size(); w++) all[w] = w;
+        return run_windows(batch, info.eot_token, K, windows, all, blocks);
+    };
+    return fold_impl(info.hash, info.eot_token, info.n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
+}
+
+int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                  uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, const uint8_t* input, size_t len,
+                  const hs_fold_options* opt, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !opt || !out_len || (len && !input))
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    uint32_t vocab, eot, n_ctx;
+    hs::tokenizer_info(tok, &vocab, &eot, &n_ctx);
+    if (opt->overlap > 0xFFFF || (n_ctx >= 2 && opt->overlap > n_ctx - 2))
+        return hs::host_fail(HS_INVALID_OVERLAP, "the overlap must be at most n_ctx - 2");
+    uint8_t hash[32];
+    hs::sha256(model_file, model_len, hash);  // the model hash of the container (model.rs:359)
+    const size_t K = opt->overlap;
+    // One host thread per GPU: it opens the device (a device handle belongs to its thread), loads
+    // the model, and runs the windows dealt to it round-robin (crates/taco/src/gpu_fold.rs:128-186).
+    // A thread's error message is thread-local; it comes back with its status.
+    GpuStage gpu = [&](const std::vector<Window>& windows, std::vector<FoldBlock>& blocks) {
+        std::vector<int> rcs(n_gpus, HS_OK);
+        std::vector<std::string> msgs(n_gpus);
+        auto worker = [&](uint32_t g) {
+            hs_dev* dev = nullptr;
+            hs_model* model = nullptr;
+            hs_batch* batch = nullptr;
+            int rc = hs_open(ordinals[g], &dev);
+            if (!rc) rc = hs_model_load(dev, model_file, model_len, &model);
+            hs_model_info mi;
+            if (!rc && !(rc = hs_model_get_info(model, &mi)) && memcmp(mi.hash, hash, 32) != 0)
+                rc = hs::host_fail(HS_MODEL, "the model hash differs");
+            if (!rc && mi.vocab != vocab) rc = check_tokenizer(tok, mi.vocab);
+            if (!rc) rc = hs_batch_new(model, slots, max_rows, &batch);
+            if (!rc) rc = hs_batch_set_overlap(batch, (uint16_t)K);
+            if (!rc) {
+                std::vector<size_t> mine;
+                for (size_t w = g; w < windows.size(); w += n_gpus) mine.push_back(w);
+                rc = run_windows(batch, eot, K, windows, mine, blocks);
+            }
+            if (rc) {
+                char buf[1024];
+                hs_last_error(buf, sizeof buf);
+                msgs[g] = buf;
+            }
+            rcs[g] = rc;
+            if (batch) hs_batch_free(batch);
+            if (model) hs_model_free(model);
+            if (dev) hs_dev_free(dev);
+        };
+        std::vector<std::thread> pool;
+        for (uint32_t g = 0; g < n_gpus; g++) pool.emplace_back(worker, g);
+        for (auto& t : pool) t.join();
+        for (uint32_t g = 0; g < n_gpus; g++)
+            if (rcs[g]) return hs::host_fail(rcs[g], "GPU " + std::to_string(ordinals[g]) + ": " + msgs[g]);
+        return (int)HS_OK;
+    };
+    return fold_impl(hash, eot, n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
 }
 
 uint32_t hs_zstd_version(void) { return zstd().ok ? zstd().version() : 0; }

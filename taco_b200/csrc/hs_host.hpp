@@ -25,6 +25,9 @@ hs_model* batch_model(hs_batch* b);
 uint32_t batch_slots(const hs_batch* b);
 uint32_t batch_max_rows(const hs_batch* b);
 
+// The vocabulary size, EOT token and context length of the tokenizer's model.
+void tokenizer_info(const hs_tokenizer* t, uint32_t* vocab, uint32_t* eot, uint32_t* n_ctx);
+
 // The bytes of token `id` (empty for an id out of range).
 const uint8_t* token_bytes(const hs_tokenizer* t, uint32_t id, size_t* n);
 

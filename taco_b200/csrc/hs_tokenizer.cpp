@@ -139,7 +139,7 @@ uint64_t pair_key(uint32_t a, uint32_t b) { return (uint64_t)a << 32 | b; }
 struct hs_tokenizer {
     uint32_t byte_tokens[256];
     std::unordered_map<uint64_t, Merge> merges;
-    uint32_t vocab = 0, eot = 0;
+    uint32_t vocab = 0, eot = 0, n_ctx = 0;
     std::vector<uint8_t> bytes;  // the bytes of every token, joined
     std::vector<size_t> ends;    // the end of token i in `bytes`
 
@@ -240,6 +240,7 @@ int make_tokenizer(const hsm::Model& M, hs_tokenizer* t) {
     const size_t V = M.vocab_ends.size();
     t->vocab = (uint32_t)V;
     t->eot = M.eot;
+    t->n_ctx = (uint32_t)M.n_ctx;
     t->bytes = M.vocab_bytes;
     t->ends = M.vocab_ends;
     auto token = [&](size_t i) {
@@ -295,6 +296,12 @@ int tokenizer_from_model(const hsm::Model& M, hs_tokenizer** out) {
 
 void tokenize(const hs_tokenizer* t, const uint8_t* data, size_t len, std::vector<uint32_t>& out) {
     t->encode(data, len, out);
+}
+
+void tokenizer_info(const hs_tokenizer* t, uint32_t* vocab, uint32_t* eot, uint32_t* n_ctx) {
+    *vocab = t->vocab;
+    *eot = t->eot;
+    *n_ctx = t->n_ctx;
 }
 
 const uint8_t* token_bytes(const hs_tokenizer* t, uint32_t id, size_t* n) {

@@ -148,3 +148,19 @@ def test_unfold_refuses_bad_containers(setup):
     c3.profile, c3.mixer_rule = C.PROFILE_LOGS, 1
     c3.blocks[coded.index].kind = C.KIND_MIXED
     assert code(C.build(c3)) == B.HS_UNSUPPORTED
+
+
+def test_fold_on_several_gpu_threads_equals_one_gpu(setup):
+    """hs_fold_multi deals the windows to one host thread per GPU; the container is hs_fold's. On
+    a box with one GPU both threads use device 0 (two handles, two batches)."""
+    batch, tok = setup
+    import torch
+
+    ords = [0, 1] if torch.cuda.device_count() >= 2 else [0, 0]
+    pred = (GOLDEN / "predicted_text_k32.in").read_bytes()
+    data = pred * 4 + (GOLDEN / "all_kinds_text.in").read_bytes()
+    for bs, k in [(300, 32), (2000, 5)]:
+        want, _ = B.fold(batch, tok, data, bs, k)
+        got, stats = B.fold_multi(ords, tiny_bytes(), tok, data, bs, k, slots=8, max_rows=4096)
+        assert got == want
+        assert stats["coded_blocks"] > 0 or bs == 2000
