@@ -64,7 +64,9 @@ typedef struct hs_model_info {
 } hs_model_info;
 
 /* CudaDevice::open (crates/hardshell-cuda/src/device.rs:29). HS_NO_DEVICE without a device,
- * HS_UNSUPPORTED below compute capability 10.0 (the kernels are sm_100a). */
+ * HS_UNSUPPORTED below compute capability 10.0 (the kernels are sm_100a). For tests of the
+ * callers' fallback, the environment variable HS_FAIL_OPEN (a comma-separated list of ordinals)
+ * makes the open of those ordinals fail with HS_NO_DEVICE before any CUDA call. */
 int hs_open(int ordinal, hs_dev** out);
 void hs_dev_free(hs_dev* dev);
 /* CudaDevice::memory (device.rs:58): free and total bytes. */
@@ -214,7 +216,8 @@ typedef struct hs_fold_options {
 /* FoldStats (fold.rs): the counts of one fold. */
 typedef struct hs_fold_stats {
     uint64_t original_len, container_len, blocks, coded_blocks, zstd_blocks, tokens;
-    uint32_t block_size, reserved;
+    uint32_t block_size;
+    uint32_t gpus_failed; /* hs_fold_multi: the GPUs that did not open and gave their windows away */
 } hs_fold_stats;
 
 /* The largest container of a fold of `len` bytes with this block size (0 = the default). */
@@ -233,10 +236,14 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input
             const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats);
 
 /* hs_fold on several GPUs of this host (crates/taco/src/gpu_fold.rs:128-186): one host thread
- * per GPU opens device ordinals[g], loads the model file (the tokenizer must be of that model),
- * makes a batch of `slots` slots and passes of `max_rows` rows, and runs the context windows
- * dealt to it round-robin; the host stages are shared. The container is the bytes hs_fold gives
- * on one GPU. An error of a GPU thread comes back with its status and message. */
+ * per GPU opens device ordinals[g], loads the model file, makes a batch of `slots` slots and
+ * passes of `max_rows` rows, and runs the context windows dealt to it round-robin; the host
+ * stages are shared. The windows follow the model file's context length and EOT token; the
+ * tokenizer must have the model's vocabulary (HS_MODEL). A GPU that cannot be opened, load the
+ * model or hold the batch gives its windows to the GPUs that can (stats->gpus_failed counts it),
+ * as the reference falls back from a device that fails (crates/taco/src/backend.rs:288-342); with
+ * no GPU left the call fails with the first GPU's error. An error while windows run fails the
+ * call with that GPU's status and message. The container is the bytes hs_fold gives on one GPU. */
 int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
                   uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* input,
                   size_t len, const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len,
@@ -298,8 +305,10 @@ int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, co
  * padded operands, parameters and result are staged in one static __device__ array of
  * HS_STATIC_SCRATCH_BYTES per GPU (held until exit); shapes that need more are refused with
  * HS_UNSUPPORTED. It calls no cudaMalloc or cudaFree. The first call on a device resolves the
- * array's address (cudaGetSymbolAddress): make it before any stream capture. Calls share the
- * array, so calls that overlap on one GPU race: serialise them. */
+ * array's address (cudaGetSymbolAddress) and creates the library's non-blocking stream for that
+ * device, on which every call runs (not the legacy default stream): make that first call before
+ * any stream capture. Calls share the array, so calls that overlap on one GPU race: serialise
+ * them. */
 #define HS_STATIC_SCRATCH_BYTES (32u << 20)
 int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, const int8_t* W, const int32_t* bias,
                              const int32_t* mult, uint32_t shift, uint32_t M, uint32_t N, uint32_t K, int8_t* out8,

@@ -70,7 +70,7 @@ class FoldOptions(ctypes.Structure):
 class FoldStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("original_len", "container_len", "blocks", "coded_blocks",
                                                "zstd_blocks", "tokens")] + \
-               [("block_size", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+               [("block_size", ctypes.c_uint32), ("gpus_failed", ctypes.c_uint32)]
 
 
 MIXER_FN = ctypes.CFUNCTYPE(ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(MixStats))
@@ -208,7 +208,7 @@ def fold(batch, tokenizer, data: bytes, block_size: int = 0, overlap: int = 0, s
     st = FoldStats()
     _check(lib().hs_fold(batch.h, tokenizer.h, data, len(data), ctypes.byref(opt), _p(out), out.size,
                          ctypes.byref(n), ctypes.byref(st)))
-    stats = {name: getattr(st, name) for name, _ in FoldStats._fields_ if name != "reserved"}
+    stats = {name: getattr(st, name) for name, _ in FoldStats._fields_}
     return out[:n.value].tobytes(), stats
 
 
@@ -223,7 +223,7 @@ def fold_multi(ordinals, model_file: bytes, tokenizer, data: bytes, block_size: 
     st = FoldStats()
     _check(lib().hs_fold_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows, tokenizer.h, data,
                                len(data), ctypes.byref(opt), _p(out), out.size, ctypes.byref(n), ctypes.byref(st)))
-    stats = {name: getattr(st, name) for name, _ in FoldStats._fields_ if name != "reserved"}
+    stats = {name: getattr(st, name) for name, _ in FoldStats._fields_}
     return out[:n.value].tobytes(), stats
 
 

@@ -4,6 +4,11 @@
 
 #include <cstdint>
 
+// The device error word (one int per device, 0 = no error): a bounded wait that gives up writes
+// its wait's code (below 40); the coder op writes ERR_CODER_DIVISION when its frequency division
+// is not exact after its correction steps. The first code written stays.
+constexpr int ERR_CODER_DIVISION = 40;
+
 namespace hs {
 
 // Rows of the GEMM operand tiles and the padding of every K and N dimension.

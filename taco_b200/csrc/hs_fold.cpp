@@ -21,6 +21,8 @@
 #include <algorithm>
 #include <functional>
 #include <atomic>
+#include <condition_variable>
+#include <mutex>
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -489,19 +491,44 @@ int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_fil
                   const hs_fold_options* opt, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
     if (!ordinals || !n_gpus || !model_file || !tok || !opt || !out_len || (len && !input))
         return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    // The windows are cut with the model's context length and EOT token, as hs_fold cuts them
+    // with those of its batch's model (gpu_fold.rs windows_of, Window::rows); the tokenizer only
+    // has to share the model's vocabulary (FoldPlan::new, fold.rs:388-395).
     uint32_t vocab, eot, n_ctx;
-    hs::tokenizer_info(tok, &vocab, &eot, &n_ctx);
-    if (opt->overlap > 0xFFFF || (n_ctx >= 2 && opt->overlap > n_ctx - 2))
+    {
+        std::string err;
+        if (!hs::model_file_info(model_file, model_len, &vocab, &eot, &n_ctx, err))
+            return hs::host_fail(HS_MODEL, "the model file is not valid: " + err);
+    }
+    int rc0 = check_tokenizer(tok, vocab);
+    if (rc0) return rc0;
+    if (opt->overlap > 0xFFFF || opt->overlap > n_ctx - 2)
         return hs::host_fail(HS_INVALID_OVERLAP, "the overlap must be at most n_ctx - 2");
     uint8_t hash[32];
     hs::sha256(model_file, model_len, hash);  // the model hash of the container (model.rs:359)
     const size_t K = opt->overlap;
+    uint32_t gpus_failed = 0;
     // One host thread per GPU: it opens the device (a device handle belongs to its thread), loads
-    // the model, and runs the windows dealt to it round-robin (crates/taco/src/gpu_fold.rs:128-186).
-    // A thread's error message is thread-local; it comes back with its status.
+    // the model and makes its batch (crates/taco/src/gpu_fold.rs:128-186). When every thread has
+    // tried, the windows are dealt round-robin to the GPUs that opened: a GPU that cannot be
+    // opened, load the model or hold the batch gives its share to the others, as the reference's
+    // backend choice falls back from a device that fails to open (crates/taco/src/backend.rs:
+    // 288-342). An error while windows run fails the fold. A thread's error message is
+    // thread-local; it comes back with its status.
     GpuStage gpu = [&](const std::vector<Window>& windows, std::vector<FoldBlock>& blocks) {
         std::vector<int> rcs(n_gpus, HS_OK);
         std::vector<std::string> msgs(n_gpus);
+        std::vector<uint32_t> live;
+        std::mutex mu;
+        std::condition_variable cv;
+        uint32_t tried = 0;
+        bool go = false;
+        auto note = [&](uint32_t g, int rc) {
+            char buf[1024];
+            hs_last_error(buf, sizeof buf);
+            msgs[g] = buf;
+            rcs[g] = rc;
+        };
         auto worker = [&](uint32_t g) {
             hs_dev* dev = nullptr;
             hs_model* model = nullptr;
@@ -509,34 +536,51 @@ int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_fil
             int rc = hs_open(ordinals[g], &dev);
             if (!rc) rc = hs_model_load(dev, model_file, model_len, &model);
             hs_model_info mi;
-            if (!rc && !(rc = hs_model_get_info(model, &mi)) && memcmp(mi.hash, hash, 32) != 0)
-                rc = hs::host_fail(HS_MODEL, "the model hash differs");
-            if (!rc && mi.vocab != vocab) rc = check_tokenizer(tok, mi.vocab);
+            if (!rc && !(rc = hs_model_get_info(model, &mi))) {
+                if (memcmp(mi.hash, hash, 32) != 0 || mi.n_ctx != n_ctx || mi.eot_token != eot || mi.vocab != vocab)
+                    rc = hs::host_fail(HS_MODEL, "the loaded model is not the model file");
+            }
             if (!rc) rc = hs_batch_new(model, slots, max_rows, &batch);
             if (!rc) rc = hs_batch_set_overlap(batch, (uint16_t)K);
+            {
+                std::unique_lock<std::mutex> lk(mu);
+                if (rc) note(g, rc);
+                tried++;
+                cv.notify_all();
+                cv.wait(lk, [&] { return go; });
+            }
             if (!rc) {
+                const size_t n = live.size(), k = (size_t)(std::find(live.begin(), live.end(), g) - live.begin());
                 std::vector<size_t> mine;
-                for (size_t w = g; w < windows.size(); w += n_gpus) mine.push_back(w);
+                for (size_t w = k; w < windows.size(); w += n) mine.push_back(w);
                 rc = run_windows(batch, eot, K, windows, mine, blocks);
+                if (rc) note(g, rc);
             }
-            if (rc) {
-                char buf[1024];
-                hs_last_error(buf, sizeof buf);
-                msgs[g] = buf;
-            }
-            rcs[g] = rc;
             if (batch) hs_batch_free(batch);
             if (model) hs_model_free(model);
             if (dev) hs_dev_free(dev);
         };
         std::vector<std::thread> pool;
         for (uint32_t g = 0; g < n_gpus; g++) pool.emplace_back(worker, g);
+        {
+            std::unique_lock<std::mutex> lk(mu);
+            cv.wait(lk, [&] { return tried == n_gpus; });
+            for (uint32_t g = 0; g < n_gpus; g++)
+                if (rcs[g] == HS_OK) live.push_back(g);
+            gpus_failed = n_gpus - (uint32_t)live.size();
+            go = true;
+            cv.notify_all();
+        }
         for (auto& t : pool) t.join();
-        for (uint32_t g = 0; g < n_gpus; g++)
+        if (live.empty()) return hs::host_fail(rcs[0], "no GPU of the fold opened; GPU " + std::to_string(ordinals[0]) +
+                                                           ": " + msgs[0]);
+        for (uint32_t g : live)
             if (rcs[g]) return hs::host_fail(rcs[g], "GPU " + std::to_string(ordinals[g]) + ": " + msgs[g]);
         return (int)HS_OK;
     };
-    return fold_impl(hash, eot, n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
+    const int rc = fold_impl(hash, eot, n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
+    if (!rc && stats) stats->gpus_failed = gpus_failed;
+    return rc;
 }
 
 uint32_t hs_zstd_version(void) { return zstd().ok ? zstd().version() : 0; }

@@ -25,6 +25,11 @@ hs_model* batch_model(hs_batch* b);
 uint32_t batch_slots(const hs_batch* b);
 uint32_t batch_max_rows(const hs_batch* b);
 
+// The vocabulary size, EOT token and context length of a model file (false with a message if the
+// file is not a valid model).
+bool model_file_info(const uint8_t* file, size_t len, uint32_t* vocab, uint32_t* eot, uint32_t* n_ctx,
+                     std::string& err);
+
 // The vocabulary size, EOT token and context length of the tokenizer's model.
 void tokenizer_info(const hs_tokenizer* t, uint32_t* vocab, uint32_t* eot, uint32_t* n_ctx);
 

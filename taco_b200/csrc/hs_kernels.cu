@@ -720,7 +720,8 @@ constexpr int CODER_MAX_STEPS = 32;  // steps of 256 symbols per warp: V <= 8 * 
 // groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step).
 __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
                                                          int tsh, int R, int V, const uint64_t* table, int tlen,
-                                                         int head, uint32_t bits, const RowInfo* rows, uint64_t* out) {
+                                                         int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
+                                                         int* err) {
     extern __shared__ __align__(16) uint32_t F[];  // counts, then 1 + floor(table[j] * spare / W), j <= dmax
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
@@ -850,6 +851,9 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
                 q += 1;
                 rm -= (int64_t)W;
             }
+            // The error bound above makes one step enough; a remainder still out of [0, W) means
+            // the bound failed for this table, and the call fails instead of coding a wrong q.
+            if (rm < 0 || rm >= (int64_t)W) atomicCAS(err, 0, ERR_CODER_DIVISION);
             return q;
         };
         for (int j = threadIdx.x; j <= dmax; j += CODER_THREADS) {
@@ -1041,12 +1045,15 @@ __global__ void k_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int
 
 // floor(t * spare / W) for 0 < t <= W (so the quotient is at most spare < 2^32): the double
 // estimate is within one or two of it, and exact 128-bit products put it right.
-__device__ __forceinline__ uint64_t mix_fdiv(uint64_t t, uint64_t spare, uint64_t W, double ratio) {
+// A q that the 8 steps do not put right sets the error word (the call fails, nothing is coded
+// with it).
+__device__ __forceinline__ uint64_t mix_fdiv(uint64_t t, uint64_t spare, uint64_t W, double ratio, int* err) {
     uint64_t q = (uint64_t)((double)t * ratio);
     q = q < spare ? q : spare;
     const u128 x = (u128)t * spare;
     for (int k = 0; k < 8 && (u128)q * W > x; k++) q--;
     for (int k = 0; k < 8 && (u128)(q + 1) * W <= x; k++) q++;
+    if ((u128)q * W > x || (u128)(q + 1) * W <= x) atomicCAS(err, 0, ERR_CODER_DIVISION);
     return q;
 }
 
@@ -1068,7 +1075,8 @@ __device__ __forceinline__ uint64_t mix_fdiv(uint64_t t, uint64_t spare, uint64_
 __global__ void __launch_bounds__(CODER_THREADS) k_coder_mix(const uint16_t* d16, int ldd, const int64_t* tmax,
                                                              int ldt, int tsh, int R, int V, const uint64_t* table,
                                                              int tlen, int head, uint32_t bits, const RowInfo* rows,
-                                                             const MixRow* mix, int phase, uint64_t* out) {
+                                                             const MixRow* mix, int phase, uint64_t* out,
+                                                             int* err) {
     extern __shared__ __align__(16) uint32_t F[];  // counts, then F[d] of the distances that occur
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
@@ -1247,14 +1255,14 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder_mix(const uint16_t* d16
             for (int j = lo + threadIdx.x; j <= hi; j += CODER_THREADS) {
                 const uint32_t c = F[j];
                 if (c) {
-                    const uint32_t f = (uint32_t)(1 + mix_fdiv(g(j), spare, W, ratio));
+                    const uint32_t f = (uint32_t)(1 + mix_fdiv(g(j), spare, W, ratio, err));
                     F[j] = f;
                     sum_f += (uint64_t)c * f;
                 }
             }
         sum_f = block_sum64(sum_f, redu);  // (its barriers also publish F)
         if (has_p) {
-            f_p = 1 + mix_fdiv(wpm, spare, W, ratio);
+            f_p = 1 + mix_fdiv(wpm, spare, W, ratio, err);
             sum_f += f_p;
         }
     }
@@ -1548,18 +1556,18 @@ void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, con
 
 void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                   const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
-                  cudaStream_t st) {
+                  int* err, cudaStream_t st) {
     if (R <= 0) return;
     k_coder<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, tsh, R, V, table, tlen, head, bits,
-                                                         rows, out);
+                                                         rows, out, err);
 }
 
 void launch_coder_mix(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                       const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows,
-                      const MixRow* mix, int phase, uint64_t* out, cudaStream_t st) {
+                      const MixRow* mix, int phase, uint64_t* out, int* err, cudaStream_t st) {
     if (R <= 0) return;
     k_coder_mix<<<R, CODER_THREADS, (size_t)tlen * 4, st>>>(d16, ldd, tmax, ldt, tsh, R, V, table, tlen, head, bits,
-                                                             rows, mix, phase, out);
+                                                             rows, mix, phase, out, err);
 }
 
 void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,

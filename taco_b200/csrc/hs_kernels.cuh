@@ -109,7 +109,7 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
 // is the last index j with table[j] == table[0] (the table is not increasing).
 void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                   const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
-                  cudaStream_t st);
+                  int* err, cudaStream_t st);
 
 // The mixed coder op of the profile logs, in two phases around a host step. Phase 0 (the stats
 // kernel): out = {W, w[p], top} of the GPT-2 weights of each row, p = mix[r].p. Phase 1: the
@@ -117,7 +117,7 @@ void launch_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, in
 // mix[r] describes. One block per row, as launch_coder.
 void launch_coder_mix(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,
                       const uint64_t* table, int tlen, int head, uint32_t bits, const RowInfo* rows,
-                      const MixRow* mix, int phase, uint64_t* out, cudaStream_t st);
+                      const MixRow* mix, int phase, uint64_t* out, int* err, cudaStream_t st);
 
 // The full weights of each row (run_weights): w[r, v] = table[min(max - logit, last)].
 void launch_weights(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt, int tsh, int R, int V,

@@ -12,11 +12,15 @@
 // holds until the process exits. It calls no cudaMalloc, cudaFree or other allocating routine.
 //
 // Set-up: the first call on a device (with that device current) resolves the array's address
-// with cudaGetSymbolAddress, which loads the module on that device; make that first call before
-// any stream capture begins. Every call shares the one array and it keeps the last call's
-// contents, so each call first clears the padding that the GEMM reads as zeros. Calls that
-// overlap on the GPU (from several host threads on one device) race on the array; serialise
-// them. Shapes whose staging needs more than the array holds are refused with HS_UNSUPPORTED.
+// with cudaGetSymbolAddress, which loads the module on that device, and creates the library's
+// own non-blocking stream for that device; make that first call before any stream capture
+// begins. Every call then runs on that stream (asynchronous memset and copies, the launch, one
+// stream synchronisation), never on the legacy default stream, so it does not wait on the
+// caller's other blocking streams and they do not wait on it. Every call shares the one array
+// and it keeps the last call's contents, so each call first clears the padding that the GEMM
+// reads as zeros. Calls that overlap on the GPU (from several host threads on one device) race on
+// the array; serialise them. Shapes whose staging needs more than the array holds are refused
+// with HS_UNSUPPORTED.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -42,11 +46,13 @@ namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mu;
 uint8_t* g_scratch_ptr[kMaxDevices] = {};
+cudaStream_t g_stream[kMaxDevices] = {};
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
-// The array's device address on the current device, resolved once per device.
-int scratch_of_current_device(uint8_t** out) {
+// The array's device address on the current device and the library's stream there, both made
+// once per device.
+int scratch_of_current_device(uint8_t** out, cudaStream_t* stream) {
     int ord = 0;
     cudaError_t e = cudaGetDevice(&ord);
     if (e != cudaSuccess) return hs_internal_fail(HS_CUDA, cudaGetErrorString(e));
@@ -57,9 +63,15 @@ int scratch_of_current_device(uint8_t** out) {
         e = cudaGetSymbolAddress(&p, g_static_scratch);
         if (e != cudaSuccess)
             return hs_internal_fail(HS_CUDA, (std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e)).c_str());
+        cudaStream_t st = nullptr;
+        e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+        if (e != cudaSuccess)
+            return hs_internal_fail(HS_CUDA, (std::string("cudaStreamCreateWithFlags: ") + cudaGetErrorString(e)).c_str());
+        g_stream[ord] = st;
         g_scratch_ptr[ord] = static_cast<uint8_t*>(p);
     }
     *out = g_scratch_ptr[ord];
+    *stream = g_stream[ord];
     return HS_OK;
 }
 
@@ -98,7 +110,8 @@ extern "C" int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, 
     int rc = hs_internal_dev_info(dev, &num_sms, &unused_err);  // makes the device current
     if (rc) return rc;
     uint8_t* base = nullptr;
-    if ((rc = scratch_of_current_device(&base))) return rc;
+    cudaStream_t st = nullptr;
+    if ((rc = scratch_of_current_device(&base, &st))) return rc;
     int* d_err = reinterpret_cast<int*>(base);
     int8_t* da = reinterpret_cast<int8_t*>(base + off_a);
     int8_t* dw = reinterpret_cast<int8_t*>(base + off_w);
@@ -106,12 +119,12 @@ extern "C" int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, 
     int32_t* dm = reinterpret_cast<int32_t*>(base + off_m);
 
     // The GEMM reads the padding of A, W, bias and mult, which hold the previous call's data.
-    NA_CK(cudaMemset(base, 0, off_o));
-    NA_CK(cudaMemcpy2D(da, Kp, A, K, K, M, cudaMemcpyHostToDevice));
-    NA_CK(cudaMemcpy2D(dw, Kp, W, K, K, N, cudaMemcpyHostToDevice));
+    NA_CK(cudaMemsetAsync(base, 0, off_o, st));
+    NA_CK(cudaMemcpy2DAsync(da, Kp, A, K, K, M, cudaMemcpyHostToDevice, st));
+    NA_CK(cudaMemcpy2DAsync(dw, Kp, W, K, K, N, cudaMemcpyHostToDevice, st));
     if (!raw32) {
-        NA_CK(cudaMemcpy(db, bias, 4 * (size_t)N, cudaMemcpyHostToDevice));
-        NA_CK(cudaMemcpy(dm, mult, 4 * (size_t)N, cudaMemcpyHostToDevice));
+        NA_CK(cudaMemcpyAsync(db, bias, 4 * (size_t)N, cudaMemcpyHostToDevice, st));
+        NA_CK(cudaMemcpyAsync(dm, mult, 4 * (size_t)N, cudaMemcpyHostToDevice, st));
     }
     LinearDev L{dw, (int)N, (int)K, (int)Np, (int)Kp, db, dm, (int)shift};
     EpiArgs e{};
@@ -124,7 +137,6 @@ extern "C" int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, 
     if (raw32) e.out32 = reinterpret_cast<int32_t*>(base + off_o);
     else e.out8 = reinterpret_cast<int8_t*>(base + off_o);
     const int mode = raw32 ? EPI_RAW : EPI_ACT;
-    cudaStream_t st = 0;
     if (path == 0) {
         alignas(128) CUtensorMap ta, tb;
         if ((rc = hs_internal_tmap(dev, &ta, da, Mp, Kp, TILE_M)) || (rc = hs_internal_tmap(dev, &tb, dw, Np, Kp, TILE_N)))
@@ -136,9 +148,11 @@ extern "C" int hs_op_linear_act_noalloc(hs_dev* dev, int path, const int8_t* A, 
     NA_CK(cudaGetLastError());
     NA_CK(cudaStreamSynchronize(st));
     int herr = 0;
-    NA_CK(cudaMemcpy(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    NA_CK(cudaMemcpyAsync(&herr, d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    NA_CK(cudaStreamSynchronize(st));
     if (herr) return hs_internal_fail(HS_CUDA, ("a kernel wait timed out (code " + std::to_string(herr) + ")").c_str());
-    if (raw32) NA_CK(cudaMemcpy(raw32, base + off_o, 4 * (size_t)M * N, cudaMemcpyDeviceToHost));
-    else NA_CK(cudaMemcpy(out8, base + off_o, (size_t)M * N, cudaMemcpyDeviceToHost));
+    if (raw32) NA_CK(cudaMemcpyAsync(raw32, base + off_o, 4 * (size_t)M * N, cudaMemcpyDeviceToHost, st));
+    else NA_CK(cudaMemcpyAsync(out8, base + off_o, (size_t)M * N, cudaMemcpyDeviceToHost, st));
+    NA_CK(cudaStreamSynchronize(st));
     return HS_OK;
 }

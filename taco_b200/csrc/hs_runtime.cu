@@ -544,6 +544,8 @@ int check_device_error(hs_batch* b) {
     CK(cudaMemcpy(&herr, dev->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (herr != 0) {
         cudaMemset(dev->d_err, 0, sizeof(int));
+        if (herr == ERR_CODER_DIVISION)
+            return fail(HS_CUDA, "the coder op's frequency division did not converge (code " + std::to_string(herr) + ")");
         return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
     }
     return HS_OK;
@@ -814,9 +816,10 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             ProfScope p(b, OP_CODER, 0);
             if (mix->plain)
                 launch_coder(b->mx_d16[h], c.Vp, b->mx_tmax[h], c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
-                             m->logits_head, bits, b->mx_rows[h], b->d_plain, b->stream);
+                             m->logits_head, bits, b->mx_rows[h], b->d_plain, m->dev->d_err, b->stream);
             launch_coder_mix(b->mx_d16[h], c.Vp, b->mx_tmax[h], c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
-                             m->logits_head, bits, b->mx_rows[h], b->d_mix, 1, b->intervals, b->stream);
+                             m->logits_head, bits, b->mx_rows[h], b->d_mix, 1, b->intervals, m->dev->d_err,
+                             b->stream);
         }
         if (mix->plain)
             CK(cudaMemcpyAsync(b->h_plain + h * 3 * Rc, b->d_plain, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
@@ -868,7 +871,8 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             {
                 ProfScope p(b, OP_CODER, 0);
                 launch_coder_mix(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len,
-                                 m->logits_head, bits, b->d_rows, b->d_mix, 0, b->d_stats, b->stream);
+                                 m->logits_head, bits, b->d_rows, b->d_mix, 0, b->d_stats, m->dev->d_err,
+                                 b->stream);
             }
             pass_scope.reset();
             CK(cudaMemcpyAsync(b->h_stats + (k & 1) * 3 * (size_t)b->Rcap, b->d_stats, sizeof(uint64_t) * 3 * R,
@@ -879,7 +883,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             {
                 ProfScope p(b, OP_CODER, 0);
                 launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len, m->logits_head, bits, b->d_rows,
-                             b->intervals, b->stream);
+                             b->intervals, m->dev->d_err, b->stream);
             }
             pass_scope.reset();
             CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
@@ -1062,7 +1066,7 @@ int decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t*
                 if (rc) return rc;
                 ProfScope p(b, OP_CODER, 0);
                 launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, (int)L, c.V, m->logits_exp, m->logits_len,
-                             m->logits_head, bits, b->d_rows, b->intervals, st);
+                             m->logits_head, bits, b->d_rows, b->intervals, m->dev->d_err, st);
             }
             {
                 ProfScope p(b, OP_DECODER, 0);
@@ -1215,9 +1219,27 @@ int hs_last_error(char* buf, size_t cap) {
     return HS_OK;
 }
 
+// HS_FAIL_OPEN: a comma-separated list of ordinals whose open fails on the host, before any CUDA
+// call (a test of the callers' fallback without a fault of any GPU).
+static bool open_fails_by_request(int ordinal) {
+    const char* v = getenv("HS_FAIL_OPEN");
+    if (!v) return false;
+    for (const char* p = v; *p;) {
+        char* end = nullptr;
+        const long o = strtol(p, &end, 10);
+        if (end == p) break;
+        if (o == ordinal) return true;
+        p = *end == ',' ? end + 1 : end;
+        if (*end != ',') break;
+    }
+    return false;
+}
+
 int hs_open(int ordinal, hs_dev** out) {
     if (!out) return fail(HS_BAD_ARGUMENT, "null output");
     *out = nullptr;
+    if (open_fails_by_request(ordinal))
+        return fail(HS_NO_DEVICE, "device " + std::to_string(ordinal) + " refused by HS_FAIL_OPEN");
     int count = 0;
     cudaError_t e = cudaGetDeviceCount(&count);
     if (e != cudaSuccess || count == 0)
@@ -1650,6 +1672,8 @@ int hs_op_linear_act(hs_dev* dev, int path, const int8_t* A, const int8_t* W, co
     CK(cudaMemcpy(&herr, dev->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (herr) {
         cudaMemset(dev->d_err, 0, sizeof(int));
+        if (herr == ERR_CODER_DIVISION)
+            return fail(HS_CUDA, "the coder op's frequency division did not converge (code " + std::to_string(herr) + ")");
         return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
     }
     if (raw32) CK(cudaMemcpy(raw32, d32, sizeof(int32_t) * M * N, cudaMemcpyDeviceToHost));

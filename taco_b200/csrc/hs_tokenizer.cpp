@@ -298,6 +298,16 @@ void tokenize(const hs_tokenizer* t, const uint8_t* data, size_t len, std::vecto
     t->encode(data, len, out);
 }
 
+bool model_file_info(const uint8_t* file, size_t len, uint32_t* vocab, uint32_t* eot, uint32_t* n_ctx,
+                     std::string& err) {
+    hsm::Model M;
+    if (!file || !hsm::load_model(file, len, M, err)) return false;
+    *vocab = (uint32_t)M.vocab;
+    *eot = M.eot;
+    *n_ctx = (uint32_t)M.n_ctx;
+    return true;
+}
+
 void tokenizer_info(const hs_tokenizer* t, uint32_t* vocab, uint32_t* eot, uint32_t* n_ctx) {
     *vocab = t->vocab;
     *eot = t->eot;

@@ -164,3 +164,21 @@ def test_fold_on_several_gpu_threads_equals_one_gpu(setup):
         got, stats = B.fold_multi(ords, tiny_bytes(), tok, data, bs, k, slots=8, max_rows=4096)
         assert got == want
         assert stats["coded_blocks"] > 0 or bs == 2000
+    assert stats["gpus_failed"] == 0
+
+
+def test_fold_moves_the_windows_of_a_gpu_that_fails_to_open(setup, monkeypatch):
+    """A GPU whose open fails (HS_FAIL_OPEN refuses it on the host, no GPU fault) gives its windows
+    to the others: the container is still hs_fold's, and the stats count the failed GPU. With every
+    GPU refused, the fold fails with the open's error."""
+    batch, tok = setup
+    data = (GOLDEN / "predicted_text_k32.in").read_bytes() * 3
+    want, _ = B.fold(batch, tok, data, 300, 32)
+    monkeypatch.setenv("HS_FAIL_OPEN", "7")
+    got, stats = B.fold_multi([0, 7, 0], tiny_bytes(), tok, data, 300, 32, slots=8, max_rows=4096)
+    assert got == want
+    assert stats["gpus_failed"] == 1
+    monkeypatch.setenv("HS_FAIL_OPEN", "0,7")
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_multi([0, 7], tiny_bytes(), tok, data, 300, 32, slots=8, max_rows=4096)
+    assert e.value.code == B.HS_NO_DEVICE

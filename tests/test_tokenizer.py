@@ -86,3 +86,100 @@ def test_a_bad_model_file_is_refused():
     with pytest.raises(B.HardShellError) as e:
         B.Tokenizer(b"not a model")
     assert e.value.code == B.HS_MODEL
+
+
+# ---- the Unicode classes: the reference's own tables ----
+
+# The counts of the three tables of the reference's crates/taco/src/tokenizer/unicode_tables.rs
+# (LETTER :12-15, NUMBER :168-171, WHITESPACE :207-210), and the SHA-256 of their ranges written
+# as "LO-HI;" in hex, in order (the digest gen_unicode_classes.py records).
+REFERENCE_TABLES = {
+    "kLetter": (694, 158172, "7e16409502d0aeccb1c6e18a1f43d85b4afca5c041901f5c0b9d3ff31cb8ad43"),
+    "kNumber": (148, 2247, "63534d2a58d9ce4ddafb45b3819baa5c05459365d2a5d070277ea389d4d15c1c"),
+    "kWhiteSpace": (10, 25, "263aa7d5325ac8ea2f2b9627c44ce959bc2af786386e205068c76ccbe65f16f3"),
+}
+
+
+def _inc_tables() -> dict[str, list[tuple[int, int]]]:
+    import re
+    from pathlib import Path
+
+    text = (Path(B.__file__).resolve().parent / "csrc" / "hs_unicode.inc").read_text()
+    out = {}
+    for m in re.finditer(r"static const CodeRange (\w+)\[\] = \{(.*?)\};", text, re.S):
+        out[m.group(1)] = [(int(a, 16), int(b, 16)) for a, b in re.findall(r"\{0x([0-9A-F]+), 0x([0-9A-F]+)\}",
+                                                                           m.group(2))]
+    return out
+
+
+def test_unicode_tables_are_the_reference_tables():
+    import hashlib
+
+    tables = _inc_tables()
+    for name, (n_ranges, n_points, sha) in REFERENCE_TABLES.items():
+        rs = tables[name]
+        assert len(rs) == n_ranges, name
+        assert sum(b - a + 1 for a, b in rs) == n_points, name
+        assert hashlib.sha256("".join(f"{a:X}-{b:X};" for a, b in rs).encode()).hexdigest() == sha, name
+
+
+def test_pieces_follow_the_reference_classes_where_this_image_differs(tok):
+    """Every code point that the reference's tables and this image's `regex` module classify
+    differently: the pieces around it follow the reference's class (a letter joins letters, a
+    number joins numbers, any other non-space joins punctuation, and none of them joins another
+    class), as pretokenize.rs does with those tables."""
+    regex = pytest.importorskip("regex")
+    tables = _inc_tables()
+
+    def member(rs, c):
+        import bisect
+        i = bisect.bisect_right(rs, (c, 0x110000)) - 1
+        return i >= 0 and rs[i][0] <= c <= rs[i][1]
+
+    rx_l, rx_n = regex.compile(r"\p{L}"), regex.compile(r"\p{N}")
+    rep = {"L": "a", "N": "1", "O": "!"}
+    differ = 0
+    for c in range(0x80, 0x110000):
+        if 0xD800 <= c <= 0xDFFF or member(tables["kWhiteSpace"], c):
+            continue
+        ref = "L" if member(tables["kLetter"], c) else "N" if member(tables["kNumber"], c) else "O"
+        ch = chr(c)
+        img = "L" if rx_l.match(ch) else "N" if rx_n.match(ch) else "O"
+        if ref == img:
+            continue
+        differ += 1
+        same = (rep[ref] + ch + rep[ref]).encode()
+        assert tok.pieces(same) == [same], hex(c)
+        for other in "LNO":
+            if other != ref:
+                text = (rep[other] + ch).encode()
+                assert tok.pieces(text) == [rep[other].encode(), ch.encode()], (hex(c), other)
+    # This image's regex 2026.3.32 knows an older Unicode than the reference's tables: 12,500
+    # letters and 323 numbers are new there. A newer regex would leave fewer to check.
+    print(f"{differ} code points classified by the reference's tables, not this image's regex")
+
+
+# ---- the refusals of the fold on several GPUs, decided on the host before any GPU call ----
+
+def test_fold_multi_refuses_a_bad_model_file(tok):
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_multi([0], b"not a model", tok, b"some text", 300, 0, slots=2, max_rows=64)
+    assert e.value.code == B.HS_MODEL
+
+
+def test_fold_multi_refuses_a_tokenizer_of_another_vocabulary(tok):
+    from taco_b200 import synth
+
+    other = synth.gpt2_hsm(7, shape=synth.MINI)  # 1,000 tokens; the tiny model has 300
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_multi([0], other, tok, b"some text", 300, 0, slots=2, max_rows=64)
+    assert e.value.code == B.HS_MODEL
+    assert "TokenizerMismatch" in str(e.value)
+
+
+def test_fold_multi_with_no_gpu_that_opens_fails_with_the_open_error(tok, monkeypatch):
+    monkeypatch.setenv("HS_FAIL_OPEN", "0,1")
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_multi([0, 1], tiny_bytes(), tok, b"some text " * 100, 300, 0, slots=2, max_rows=64)
+    assert e.value.code == B.HS_NO_DEVICE
+    assert "no GPU of the fold opened" in str(e.value)
