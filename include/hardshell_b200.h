@@ -218,6 +218,7 @@ typedef struct hs_fold_stats {
     uint64_t original_len, container_len, blocks, coded_blocks, zstd_blocks, tokens;
     uint32_t block_size;
     uint32_t gpus_failed; /* hs_fold_multi: the GPUs that did not open and gave their windows away */
+    uint64_t gpu_rows;    /* the rows that ran on the GPUs (windows of stopped blocks never start) */
 } hs_fold_stats;
 
 /* The largest container of a fold of `len` bytes with this block size (0 = the default). */
@@ -226,8 +227,10 @@ uint64_t hs_fold_bound(uint64_t len, uint32_t block_size);
 /* taco::fold_with on the CUDA engine (fold.rs:334-360), profile text: the .taco container
  * (version 2) of input[0 .. len) with the model of `batch`. Each block is stored raw, as a zstd
  * frame or coded by the model, whichever is smallest (writer.rs:89). The coder intervals come from
- * hs_batch_run_coded (the slots of the batch take the blocks in rounds; their contexts are reset);
- * the tokenizer, zstd and the range encoder run on host threads. zstd comes from the system
+ * hs_batch_run_coded: each block's context windows run in fresh slots, in waves (window 0 of every
+ * block, then window 1, ...), and each block's range encoder takes its windows' intervals as they
+ * complete; the later windows of a block whose encoder stopped do not run (gpu_fold.rs:200-204).
+ * The tokenizer, zstd and the range encoder run on host threads. zstd comes from the system
  * library (libzstd.so.1, hs_zstd_version); the reference pins zstd 1.5.7, and a zstd frame of
  * another version can differ in its bytes (it decodes to the same block). *out_len = the container
  * length; HS_BAD_ARGUMENT if it is more than cap (see hs_fold_bound). The batch keeps the fold's
@@ -238,7 +241,8 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input
 /* hs_fold on several GPUs of this host (crates/taco/src/gpu_fold.rs:128-186): one host thread
  * per GPU opens device ordinals[g], loads the model file, makes a batch of `slots` slots and
  * passes of `max_rows` rows, and runs the context windows dealt to it round-robin; the host
- * stages are shared. The windows follow the model file's context length and EOT token; the
+ * stages are shared; the GPUs take rounds of windows from one queue. The windows follow the
+ * model file's context length and EOT token; the
  * tokenizer must have the model's vocabulary (HS_MODEL). A GPU that cannot be opened, load the
  * model or hold the batch gives its windows to the GPUs that can (stats->gpus_failed counts it),
  * as the reference falls back from a device that fails (crates/taco/src/backend.rs:288-342); with

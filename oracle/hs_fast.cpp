@@ -16,6 +16,7 @@ namespace hso {
 namespace {
 
 const int CHUNK = 32;  // crates/taco/src/fold.rs:24 FOLD_CHUNK
+const size_t MIN_LANES = 4, MAX_LANES = 8;  // crates/taco/src/unfold.rs:249-256
 const int32_t RES = (1 << 30) - 1;
 const int64_t SCORE_LIMIT = 1LL << 40;
 
@@ -80,6 +81,7 @@ struct Row {
     int pos;
     uint32_t tok;
     long input;  // -1 for a restart row
+    int slot;
 };
 
 struct Work {
@@ -102,8 +104,12 @@ FastBatch::FastBatch(const Model* m, int s, uint16_t k) : M(m), slots(s), overla
     vt.assign(per * s, 0);
 }
 
-static void run_chunk(const Model& M, int8_t* kc, int8_t* vt, const Row* rows, int c, Work& w, uint32_t bits,
-                      const uint32_t* kind, const uint64_t* value, uint64_t* answers, uint64_t* weights, int* err) {
+// The rows of a chunk: up to CHUNK rows of one slot at consecutive positions (prefill), or one row
+// of each of up to MAX_LANES slots (lockstep lanes). Row r reads and writes the KV cache of its
+// slot, at kc_all / vt_all + per * rows[r].slot.
+static void run_chunk(const Model& M, int8_t* kc_all, int8_t* vt_all, size_t per, const Row* rows, int c, Work& w,
+                      uint32_t bits, const uint32_t* kind, const uint64_t* value, uint64_t* answers,
+                      uint64_t* weights, int* err) {
     const int d = M.d_model, f = M.d_ff, H = M.n_head, hd = M.head_dim, C = M.n_ctx, V = M.vocab;
     // ops.rs:52 embed
     for (int r = 0; r < c; r++) {
@@ -128,6 +134,8 @@ static void run_chunk(const Model& M, int8_t* kc, int8_t* vt, const Row* rows, i
         // attention.rs:138 write the keys and values of all rows of the chunk.
         for (int r = 0; r < c; r++) {
             int p = rows[r].pos;
+            int8_t* kc = kc_all + per * rows[r].slot;
+            int8_t* vt = vt_all + per * rows[r].slot;
             for (int h = 0; h < H; h++) {
                 const int8_t* kk = &w.qkv[(size_t)r * 3 * d + d + h * hd];
                 const int8_t* vv = &w.qkv[(size_t)r * 3 * d + 2 * d + h * hd];
@@ -137,6 +145,8 @@ static void run_chunk(const Model& M, int8_t* kc, int8_t* vt, const Row* rows, i
         }
         for (int r = 0; r < c; r++) {
             int n = rows[r].pos + 1;
+            const int8_t* kc = kc_all + per * rows[r].slot;
+            const int8_t* vt = vt_all + per * rows[r].slot;
             for (int h = 0; h < H; h++) {
                 const int8_t* q = &w.qkv[(size_t)r * 3 * d + h * hd];
                 const int8_t* keys = kc + lbase + (size_t)h * C * hd;
@@ -247,7 +257,7 @@ static void run_chunk(const Model& M, int8_t* kc, int8_t* vt, const Row* rows, i
 }
 
 int FastBatch::run(const uint32_t* slot, const uint32_t* token, size_t n, const uint32_t* kind, const uint64_t* value,
-                   uint32_t bits, uint64_t* answers, uint64_t* weights, int threads) {
+                   uint32_t bits, uint64_t* answers, uint64_t* weights, int threads, bool lanes) {
     const Model& m = *M;
     const int C = m.n_ctx;
     if (answers) {
@@ -272,16 +282,34 @@ int FastBatch::run(const uint32_t* slot, const uint32_t* token, size_t n, const 
         if (at >= C) {
             memmove(h + 1, h + (C - k), sizeof(uint32_t) * k);
             h[0] = m.eot;
-            for (int q = 0; q <= k; q++) rows[s].push_back({q, h[q], -1});
+            for (int q = 0; q <= k; q++) rows[s].push_back({q, h[q], -1, s});
             at = k + 1;
         }
         h[at] = token[i];
-        rows[s].push_back({at, token[i], (long)i});
+        rows[s].push_back({at, token[i], (long)i, s});
         pos[s] = at + 1;
     }
     std::vector<int> active;
+    bool single = true;  // every active slot has one row: the step of a lockstep decode
     for (int s = 0; s < slots; s++)
-        if (!rows[s].empty()) active.push_back(s);
+        if (!rows[s].empty()) {
+            active.push_back(s);
+            single = single && rows[s].size() == 1;
+        }
+    // Lockstep lanes (crates/taco/src/unfold.rs:215-246 decode_blocks on the CPU): the slots go in
+    // groups of ceil(slots / threads) clamped to [min(MIN_LANES, slots), MAX_LANES], and one thread
+    // runs a group's rows as one chunk, so each weight row is read once for the group. Without
+    // lanes (or with more than one row in a slot: a prefill), each slot is one task.
+    std::vector<std::vector<Row>> groups;
+    if (lanes && single && !active.empty()) {
+        const size_t nt = (size_t)std::max(1, threads);
+        const size_t fill = std::min<size_t>(active.size(), MIN_LANES);
+        const size_t gs = std::min<size_t>(std::max((active.size() + nt - 1) / nt, fill), MAX_LANES);
+        for (size_t g = 0; g < active.size(); g += gs) {
+            groups.emplace_back();
+            for (size_t k2 = g; k2 < std::min(active.size(), g + gs); k2++) groups.back().push_back(rows[active[k2]][0]);
+        }
+    }
     std::atomic<size_t> next(0);
     auto worker = [&]() {
         const int d = m.d_model, f = m.d_ff;
@@ -303,6 +331,12 @@ int FastBatch::run(const uint32_t* slot, const uint32_t* token, size_t n, const 
         w.starts.assign(m.vocab, 0);
         size_t per = (size_t)m.n_layer * C * d;
         int err = 0;
+        if (!groups.empty()) {
+            for (size_t idx; (idx = next.fetch_add(1)) < groups.size();)
+                run_chunk(m, kc.data(), vt.data(), per, groups[idx].data(), (int)groups[idx].size(), w, bits, kind,
+                          value, answers, weights, &err);
+            return;
+        }
         while (true) {
             size_t idx = next.fetch_add(1);
             if (idx >= active.size()) break;
@@ -313,13 +347,13 @@ int FastBatch::run(const uint32_t* slot, const uint32_t* token, size_t n, const 
                 // A chunk: at most CHUNK rows at consecutive positions (a restart starts a new one).
                 size_t j = i + 1;
                 while (j < rs.size() && (int)(j - i) < CHUNK && rs[j].pos == rs[j - 1].pos + 1) j++;
-                run_chunk(m, &kc[per * s], &vt[per * s], &rs[i], (int)(j - i), w, bits, kind, value, answers,
+                run_chunk(m, kc.data(), vt.data(), per, &rs[i], (int)(j - i), w, bits, kind, value, answers,
                           weights, &err);
                 i = j;
             }
         }
     };
-    int nt = std::max(1, std::min<int>(threads, (int)active.size()));
+    int nt = std::max(1, std::min<int>(threads, (int)(groups.empty() ? active.size() : groups.size())));
     std::vector<std::thread> pool;
     for (int t = 1; t < nt; t++) pool.emplace_back(worker);
     worker();
@@ -339,7 +373,12 @@ void hso_fast_reset(void* b, int slot) { ((hso::FastBatch*)b)->pos[slot] = 0; }
 int hso_fast_position(void* b, int slot) { return ((hso::FastBatch*)b)->pos[slot]; }
 int hso_fast_run(void* b, const uint32_t* slot, const uint32_t* token, size_t n, const uint32_t* kind,
                  const uint64_t* value, uint32_t bits, uint64_t* answers, uint64_t* weights, int threads) {
-    return ((hso::FastBatch*)b)->run(slot, token, n, kind, value, bits, answers, weights, threads);
+    return ((hso::FastBatch*)b)->run(slot, token, n, kind, value, bits, answers, weights, threads, false);
+}
+// The same with lockstep lanes for decode steps (one row per slot).
+int hso_fast_run_lanes(void* b, const uint32_t* slot, const uint32_t* token, size_t n, const uint32_t* kind,
+                       const uint64_t* value, uint32_t bits, uint64_t* answers, uint64_t* weights, int threads) {
+    return ((hso::FastBatch*)b)->run(slot, token, n, kind, value, bits, answers, weights, threads, true);
 }
 
 }  // extern "C"

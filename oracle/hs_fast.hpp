@@ -30,10 +30,12 @@ struct FastBatch {
     // The inputs (slot[i], token[i]) in order; the rows of one slot run at consecutive positions,
     // with the context restart of gpt2/context.rs. For each input i: with `weights`, its vocab
     // weights at weights[i * vocab]; with `answers`, the coder answer {symbol, start, freq} of
-    // query (kind[i], value[i]) at answers[3 * i]. `threads` workers take whole slots.
+    // query (kind[i], value[i]) at answers[3 * i]. `threads` workers take whole slots; with
+    // `lanes` and one row per slot (a decode step), they take groups of up to 8 slots in lockstep
+    // (the CPU unfold of crates/taco/src/unfold.rs:215-246). The answers do not depend on it.
     // Returns 0, or 1 (bad slot), 2 (token out of range), 4 (bad query), 5 (bad freq_bits).
     int run(const uint32_t* slot, const uint32_t* token, size_t n, const uint32_t* kind, const uint64_t* value,
-            uint32_t bits, uint64_t* answers, uint64_t* weights, int threads);
+            uint32_t bits, uint64_t* answers, uint64_t* weights, int threads, bool lanes);
 };
 
 }  // namespace hso

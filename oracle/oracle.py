@@ -83,6 +83,8 @@ def lib() -> ctypes.CDLL:
     L.hso_fast_position.argtypes = [vp, ctypes.c_int]
     L.hso_fast_run.argtypes = [vp, ctypes.c_void_p, ctypes.c_void_p, sz, ctypes.c_void_p, ctypes.c_void_p,
                                ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    L.hso_fast_run_lanes.argtypes = [vp, ctypes.c_void_p, ctypes.c_void_p, sz, ctypes.c_void_p, ctypes.c_void_p,
+                                     ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
     _lib = L
     return L
 
@@ -315,14 +317,18 @@ class FastBatch:
     def position(self, slot: int) -> int:
         return lib().hso_fast_position(self.h, slot)
 
-    def run_coded(self, slots, tokens, kinds, values, bits: int = 32, threads: int | None = None) -> np.ndarray:
+    def run_coded(self, slots, tokens, kinds, values, bits: int = 32, threads: int | None = None,
+                  lanes: bool = False) -> np.ndarray:
+        """{symbol, start, freq} per input. `lanes`: a decode step (one row per slot) runs in lockstep
+        groups of up to 8 slots per thread, as the reference's CPU unfold (unfold.rs:215-246)."""
         s = np.ascontiguousarray(slots, dtype=np.uint32)
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         k = np.ascontiguousarray(kinds, dtype=np.uint32)
         v = np.ascontiguousarray(values, dtype=np.uint64)
         out = np.zeros((s.size, 3), dtype=np.uint64)
-        rc = lib().hso_fast_run(self.h, _ptr(s), _ptr(t), s.size, _ptr(k), _ptr(v), bits, _ptr(out), None,
-                                threads or os.cpu_count() or 1)
+        fn = lib().hso_fast_run_lanes if lanes else lib().hso_fast_run
+        rc = fn(self.h, _ptr(s), _ptr(t), s.size, _ptr(k), _ptr(v), bits, _ptr(out), None,
+                threads or os.cpu_count() or 1)
         if rc:
             raise OracleError(f"fast run failed: {rc}")
         return out

@@ -70,7 +70,7 @@ class FoldOptions(ctypes.Structure):
 class FoldStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("original_len", "container_len", "blocks", "coded_blocks",
                                                "zstd_blocks", "tokens")] + \
-               [("block_size", ctypes.c_uint32), ("gpus_failed", ctypes.c_uint32)]
+               [("block_size", ctypes.c_uint32), ("gpus_failed", ctypes.c_uint32), ("gpu_rows", ctypes.c_uint64)]
 
 
 MIXER_FN = ctypes.CFUNCTYPE(ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(MixStats))

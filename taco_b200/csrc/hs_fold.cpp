@@ -214,7 +214,6 @@ struct FoldBlock {
     std::vector<uint32_t> tokens;
     std::vector<uint8_t> zstd;
     bool zstd_ok = false;
-    std::vector<hs_interval> intervals;
     uint8_t kind = KIND_RAW;
     std::vector<uint8_t> stored;  // the stored bytes of a zstd or coded block
 };
@@ -251,28 +250,139 @@ struct Window {
     size_t block, start, count;
 };
 
-// The GPU stage for the windows `mine` (indices into `windows`) on one batch whose overlap is
-// K: rounds of up to `slots` windows, one fresh slot each, slot-major rows. A window runs as EOT,
-// its K overlap inputs (answers not used) and its own inputs, the rows of the context restart
-// (crates/taco/src/gpu_fold.rs Window::rows); the answers of its own inputs go to their block.
-int run_windows(hs_batch* batch, uint32_t eot, size_t K, const std::vector<Window>& windows,
-                const std::vector<size_t>& mine, std::vector<FoldBlock>& blocks) {
+// The windows of a fold and the range encoders of its blocks, shared by the GPU threads.
+//
+// The windows are dealt in waves: window 0 of every block, then window 1 of every block, and so
+// on. After each round of a GPU, the encoder of each block takes the intervals of its windows in
+// order as they complete (codec.rs BlockEncoder::push_interval), and a block whose encoder stopped
+// (its payload reached min(block length, zstd length): codec.rs:70-131, ADR 0007 section 5.2) has
+// no later window started, as the reference's GPU fold leaves them in its queue
+// (crates/taco/src/gpu_fold.rs:200-204). The container does not depend on that order: a stopped
+// block is stored raw or as zstd whatever ran after its stop.
+class WindowFeed {
+  public:
+    WindowFeed(std::vector<Window> windows, std::vector<FoldBlock>& blocks, size_t n_blocks)
+        : windows_(std::move(windows)), blocks_(blocks), iv_(windows_.size()), done_(windows_.size(), 0),
+          st_(n_blocks), locks_(n_blocks) {
+        for (size_t w = 0; w < windows_.size(); w++) {
+            BlockState& bs = st_[windows_[w].block];
+            if (bs.windows.empty()) {
+                const FoldBlock& fb = blocks_[windows_[w].block];
+                bs.prefix = varint_len(fb.tokens.size());
+                bs.stop = std::min(fb.len, fb.zstd.size());
+            }
+            bs.windows.push_back(w);
+        }
+    }
+
+    const std::vector<Window>& windows() const { return windows_; }
+    std::vector<hs_interval>& intervals(size_t w) { return iv_[w]; }
+
+    // Up to n windows of blocks whose encoders have not stopped, in wave order.
+    void take(size_t n, std::vector<size_t>& out) {
+        out.clear();
+        std::lock_guard<std::mutex> lk(mu_);
+        while (out.size() < n && next_ < order_.size()) {
+            const size_t w = order_[next_++];
+            if (!st_[windows_[w].block].stopped.load(std::memory_order_relaxed)) out.push_back(w);
+        }
+    }
+
+    // The windows `ws` completed (their intervals are in intervals(w)): each block's encoder takes
+    // the intervals of its next windows in order; a window whose block stopped is dropped.
+    void complete(const std::vector<size_t>& ws) {
+        for (size_t w : ws) {
+            const size_t b = windows_[w].block;
+            std::lock_guard<std::mutex> lk(locks_[b]);
+            BlockState& bs = st_[b];
+            done_[w] = 1;
+            while (!bs.stopped && bs.taken < bs.windows.size() && done_[bs.windows[bs.taken]]) {
+                const size_t v = bs.windows[bs.taken++];
+                for (const hs_interval& iv : iv_[v]) {
+                    bs.enc.encode(iv.start, iv.freq, iv.is_last != 0, FREQ_BITS);
+                    if (bs.prefix + bs.enc.nonzero_len >= bs.stop) {
+                        bs.stopped = true;
+                        break;
+                    }
+                }
+                std::vector<hs_interval>().swap(iv_[v]);
+            }
+            if (bs.stopped) std::vector<hs_interval>().swap(iv_[w]);
+        }
+    }
+
+    // The wave order of the windows (set once, before the GPU stage).
+    void order_by_waves() {
+        order_.clear();
+        for (size_t k = 0;; k++) {
+            bool any = false;
+            for (const BlockState& bs : st_)
+                if (k < bs.windows.size()) {
+                    order_.push_back(bs.windows[k]);
+                    any = true;
+                }
+            if (!any) break;
+        }
+        next_ = 0;
+    }
+
+    // After the GPU stage: the payload of block b (the varint count, then the coder bytes), or
+    // false if its encoder stopped. Every window of a live block has been taken.
+    bool finish(size_t b, std::vector<uint8_t>& coded) {
+        BlockState& bs = st_[b];
+        if (bs.windows.empty() || bs.stopped || bs.taken != bs.windows.size()) return false;
+        write_varint(blocks_[b].tokens.size(), coded);
+        const std::vector<uint8_t> tail = bs.enc.finish();
+        coded.insert(coded.end(), tail.begin(), tail.end());
+        return true;
+    }
+
+    size_t rows_run() const { return rows_run_.load(); }
+    void add_rows(size_t n) { rows_run_ += n; }
+
+  private:
+    struct BlockState {
+        std::vector<size_t> windows;  // this block's windows, in order
+        size_t taken = 0;             // windows whose intervals the encoder took
+        size_t prefix = 0, stop = 0;
+        RangeEncoder enc;
+        std::atomic<bool> stopped{false};
+    };
+    std::vector<Window> windows_;
+    std::vector<FoldBlock>& blocks_;
+    std::vector<std::vector<hs_interval>> iv_;
+    std::vector<uint8_t> done_;
+    std::vector<BlockState> st_;
+    std::vector<std::mutex> locks_;
+    std::vector<size_t> order_;
+    size_t next_ = 0;
+    std::mutex mu_;
+    std::atomic<size_t> rows_run_{0};
+};
+
+// The GPU stage on one batch whose overlap is K: rounds of up to `slots` windows from the feed,
+// one fresh slot each, slot-major rows. A window runs as EOT, its K overlap inputs (answers not
+// used) and its own inputs, the rows of the context restart (crates/taco/src/gpu_fold.rs
+// Window::rows); the answers of its own inputs go to the feed's encoders.
+int run_windows(hs_batch* batch, uint32_t eot, size_t K, WindowFeed& feed, const std::vector<FoldBlock>& blocks) {
     const uint32_t slots = hs::batch_slots(batch);
+    const std::vector<Window>& windows = feed.windows();
     std::vector<uint32_t> s_slot, s_tok, s_kind;
     std::vector<uint64_t> s_val;
     std::vector<hs_interval> ivs;
-    std::vector<size_t> first;
+    std::vector<size_t> first, mine;
     int rc;
-    for (size_t m0 = 0; m0 < mine.size(); m0 += slots) {
-        const size_t m1 = std::min(mine.size(), m0 + slots);
+    for (;;) {
+        feed.take(slots, mine);
+        if (mine.empty()) return HS_OK;
         s_slot.clear();
         s_tok.clear();
         s_val.clear();
-        first.assign(m1 - m0, 0);
-        for (size_t m = m0; m < m1; m++) {
+        first.assign(mine.size(), 0);
+        for (size_t m = 0; m < mine.size(); m++) {
             const Window& win = windows[mine[m]];
             const std::vector<uint32_t>& t = blocks[win.block].tokens;
-            const uint32_t slot = (uint32_t)(m - m0);
+            const uint32_t slot = (uint32_t)m;
             if ((rc = hs_batch_reset(batch, slot))) return rc;
             auto row = [&](size_t j) {  // input j of the block, coding t_j
                 s_slot.push_back(slot);
@@ -285,7 +395,7 @@ int run_windows(hs_batch* batch, uint32_t eot, size_t K, const std::vector<Windo
                 s_val.push_back(0);
                 for (size_t j = win.start - K; j < win.start; j++) row(j);
             }
-            first[m - m0] = s_slot.size();
+            first[m] = s_slot.size();
             for (size_t j = win.start; j < win.start + win.count; j++) row(j);
         }
         s_kind.assign(s_slot.size(), 0);
@@ -293,18 +403,17 @@ int run_windows(hs_batch* batch, uint32_t eot, size_t K, const std::vector<Windo
         if ((rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
                                      (uint32_t)s_slot.size(), FREQ_BITS, ivs.data())))
             return rc;
-        for (size_t m = m0; m < m1; m++) {
+        feed.add_rows(s_slot.size());
+        for (size_t m = 0; m < mine.size(); m++) {
             const Window& win = windows[mine[m]];
-            std::copy(ivs.begin() + first[m - m0], ivs.begin() + first[m - m0] + win.count,
-                      blocks[win.block].intervals.begin() + win.start);
+            feed.intervals(mine[m]).assign(ivs.begin() + first[m], ivs.begin() + first[m] + win.count);
         }
+        feed.complete(mine);
     }
-    return HS_OK;
 }
 
-// The GPU stage of a fold: fills the intervals of every window (the blocks' interval arrays are
-// sized; the windows of one block never overlap, so GPUs may fill them side by side).
-using GpuStage = std::function<int(const std::vector<Window>&, std::vector<FoldBlock>&)>;
+// The GPU stage of a fold: runs windows from the feed until it is empty.
+using GpuStage = std::function<int(WindowFeed&, const std::vector<FoldBlock>&)>;
 
 // The fold of fold_with (steps 1, 2, 4, 5 and the container) around a GPU stage, for a model
 // with this hash, EOT token and context length.
@@ -344,47 +453,32 @@ int fold_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, const 
         return hs::host_fail(HS_MODEL, "the tokens of block " + std::to_string(bad_tokens.load()) +
                                            " do not give its bytes back (TokenizerRoundTrip)");
     if (bad_zstd >= 0) return hs::host_fail(HS_CUDA, "zstd failed on block " + std::to_string(bad_zstd.load()));
-    // 3. The intervals on the GPU. A block's inputs are x_0 = EOT, x_j = t_(j-1) (input j codes
-    // t_j). In one slot its context restarts after every n_ctx positions with EOT and the last K
-    // inputs (crates/hardshell/src/gpt2/context.rs), so the block divides into context windows:
-    // window 0 is inputs 0 .. n_ctx - 1, each later window the next n_ctx - K - 1 inputs. Each
-    // window runs in a fresh slot of its own (run_windows), so the windows of all blocks run side
-    // by side in full passes. A block whose payload prefix already reaches its bound needs none.
+    // 3. The intervals on the GPU, coded as they come. A block's inputs are x_0 = EOT,
+    // x_j = t_(j-1) (input j codes t_j). In one slot its context restarts after every n_ctx
+    // positions with EOT and the last K inputs (crates/hardshell/src/gpt2/context.rs), so the
+    // block divides into context windows: window 0 is inputs 0 .. n_ctx - 1, each later window the
+    // next n_ctx - K - 1 inputs (gpu_fold.rs windows_of). Each window runs in a fresh slot of its
+    // own (run_windows), so the windows of all blocks run side by side in full passes. A block
+    // whose payload prefix already reaches its bound needs none (BlockEncoder::stopped).
     const size_t K = std::min<size_t>(opt->overlap, n_ctx - 2);
-    auto stop_of = [&](const FoldBlock& b) { return std::min(b.len, b.zstd.size()); };
     std::vector<Window> windows;
     for (size_t i = 0; i < nblocks; i++) {
         FoldBlock& b = blocks[i];
-        if (varint_len(b.tokens.size()) >= stop_of(b)) continue;
-        b.intervals.resize(b.tokens.size());
+        if (b.tokens.empty() || varint_len(b.tokens.size()) >= std::min(b.len, b.zstd.size())) continue;
         for (size_t s0 = 0; s0 < b.tokens.size();) {
             const size_t c = std::min(b.tokens.size() - s0, s0 == 0 ? (size_t)n_ctx : n_ctx - K - 1);
             windows.push_back({i, s0, c});
             s0 += c;
         }
     }
-    if (!windows.empty() && (rc = gpu(windows, blocks))) return rc;
-    // 4.-5. The range encoder with the stop rule, then the smallest form.
+    WindowFeed feed(std::move(windows), blocks, nblocks);
+    feed.order_by_waves();
+    if (!feed.windows().empty() && (rc = gpu(feed, blocks))) return rc;
+    // 4.-5. The payloads of the blocks whose encoders did not stop, then the smallest form.
     parallel_for(nblocks, threads, [&](size_t i) {
         FoldBlock& b = blocks[i];
-        const size_t stop = stop_of(b), prefix = varint_len(b.tokens.size());
         std::vector<uint8_t> coded;
-        bool live = prefix < stop;
-        if (live) {
-            RangeEncoder enc;
-            for (const hs_interval& iv : b.intervals) {
-                enc.encode(iv.start, iv.freq, iv.is_last != 0, FREQ_BITS);
-                if (prefix + enc.nonzero_len >= stop) {
-                    live = false;
-                    break;
-                }
-            }
-            if (live) {
-                write_varint(b.tokens.size(), coded);
-                const std::vector<uint8_t> tail = enc.finish();
-                coded.insert(coded.end(), tail.begin(), tail.end());
-            }
-        }
+        const bool live = feed.finish(i, coded);
         size_t best = b.len;
         if (b.zstd.size() < best) {
             best = b.zstd.size();
@@ -395,8 +489,6 @@ int fold_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, const 
             b.kind = KIND_CODED;
             b.stored = std::move(coded);
         }
-        b.intervals.clear();
-        b.intervals.shrink_to_fit();
     });
     // The container (writer.rs:245-300; the header of header.rs, version 2, profile text).
     uint64_t total = HEADER_LEN + 5 * (uint64_t)nblocks;
@@ -413,6 +505,7 @@ int fold_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, const 
             stats->coded_blocks += b.kind == KIND_CODED;
             stats->zstd_blocks += b.kind == KIND_ZSTD;
         }
+        stats->gpu_rows = feed.rows_run();
     }
     if (cap < total || !out)
         return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
@@ -478,10 +571,8 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size
     if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
     if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
     const size_t K = std::min<size_t>(opt->overlap, info.n_ctx - 2);
-    GpuStage gpu = [&](const std::vector<Window>& windows, std::vector<FoldBlock>& blocks) {
-        std::vector<size_t> all(windows.size());
-        for (size_t w = 0; w < all.size(); w++) all[w] = w;
-        return run_windows(batch, info.eot_token, K, windows, all, blocks);
+    GpuStage gpu = [&](WindowFeed& feed, const std::vector<FoldBlock>& blocks) {
+        return run_windows(batch, info.eot_token, K, feed, blocks);
     };
     return fold_impl(info.hash, info.eot_token, info.n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
 }
@@ -510,12 +601,13 @@ int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_fil
     uint32_t gpus_failed = 0;
     // One host thread per GPU: it opens the device (a device handle belongs to its thread), loads
     // the model and makes its batch (crates/taco/src/gpu_fold.rs:128-186). When every thread has
-    // tried, the windows are dealt round-robin to the GPUs that opened: a GPU that cannot be
+    // tried, the windows go to the GPUs that opened: a GPU that cannot be
     // opened, load the model or hold the batch gives its share to the others, as the reference's
     // backend choice falls back from a device that fails to open (crates/taco/src/backend.rs:
-    // 288-342). An error while windows run fails the fold. A thread's error message is
-    // thread-local; it comes back with its status.
-    GpuStage gpu = [&](const std::vector<Window>& windows, std::vector<FoldBlock>& blocks) {
+    // 288-342). The GPUs take their rounds of windows from one shared feed, so a faster GPU takes
+    // more. An error while windows run fails the fold. A thread's error message is thread-local;
+    // it comes back with its status.
+    GpuStage gpu = [&](WindowFeed& feed, const std::vector<FoldBlock>& blocks) {
         std::vector<int> rcs(n_gpus, HS_OK);
         std::vector<std::string> msgs(n_gpus);
         std::vector<uint32_t> live;
@@ -550,10 +642,7 @@ int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_fil
                 cv.wait(lk, [&] { return go; });
             }
             if (!rc) {
-                const size_t n = live.size(), k = (size_t)(std::find(live.begin(), live.end(), g) - live.begin());
-                std::vector<size_t> mine;
-                for (size_t w = k; w < windows.size(); w += n) mine.push_back(w);
-                rc = run_windows(batch, eot, K, windows, mine, blocks);
+                rc = run_windows(batch, eot, K, feed, blocks);
                 if (rc) note(g, rc);
             }
             if (batch) hs_batch_free(batch);

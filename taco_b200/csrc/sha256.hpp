@@ -1,5 +1,6 @@
 // SHA-256 (FIPS 180-4) of a byte string: the model hash of a .hsm file
-// (crates/hardshell/src/hsm/reader.rs:443, the hash that the .taco header stores).
+// (crates/hardshell/src/hsm/reader.rs:443, the hash that the .taco header stores), and the
+// checksum of a container's original bytes, which a stream fold or unfold takes segment by segment.
 #pragma once
 
 #include <cstddef>
@@ -8,35 +9,78 @@
 
 namespace hs {
 
-inline void sha256(const uint8_t* data, size_t len, uint8_t out[32]) {
-    static const uint32_t K[64] = {
-        0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5,
-        0xd807aa98, 0x12835b01, 0x243185be, 0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174,
-        0xe49b69c1, 0xefbe4786, 0x0fc19dc6, 0x240ca1cc, 0x2de92c6f, 0x4a7484aa, 0x5cb0a9dc, 0x76f988da,
-        0x983e5152, 0xa831c66d, 0xb00327c8, 0xbf597fc7, 0xc6e00bf3, 0xd5a79147, 0x06ca6351, 0x14292967,
-        0x27b70a85, 0x2e1b2138, 0x4d2c6dfc, 0x53380d13, 0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85,
-        0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3, 0xd192e819, 0xd6990624, 0xf40e3585, 0x106aa070,
-        0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3,
-        0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
-    uint32_t h[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
-    auto rotr = [](uint32_t x, int n) { return (x >> n) | (x << (32 - n)); };
-    auto block = [&](const uint8_t* p) {
+// Incremental: update() with the bytes in order, then final().
+class Sha256 {
+  public:
+    void update(const uint8_t* data, size_t len) {
+        total_ += len;
+        if (fill_) {
+            const size_t take = len < 64 - fill_ ? len : 64 - fill_;
+            memcpy(buf_ + fill_, data, take);
+            fill_ += take;
+            data += take;
+            len -= take;
+            if (fill_ < 64) return;
+            block(buf_);
+            fill_ = 0;
+        }
+        for (; len >= 64; data += 64, len -= 64) block(data);
+        memcpy(buf_, data, len);
+        fill_ = len;
+    }
+
+    void final(uint8_t out[32]) {
+        uint8_t tail[128];
+        memcpy(tail, buf_, fill_);
+        tail[fill_] = 0x80;
+        const size_t tl = fill_ + 1 + 8 <= 64 ? 64 : 128;
+        memset(tail + fill_ + 1, 0, tl - fill_ - 1);
+        const uint64_t bits = total_ * 8;
+        for (int i = 0; i < 8; i++) tail[tl - 1 - i] = (uint8_t)(bits >> (8 * i));
+        block(tail);
+        if (tl == 128) block(tail + 64);
+        for (int i = 0; i < 8; i++) {
+            out[4 * i] = (uint8_t)(h_[i] >> 24);
+            out[4 * i + 1] = (uint8_t)(h_[i] >> 16);
+            out[4 * i + 2] = (uint8_t)(h_[i] >> 8);
+            out[4 * i + 3] = (uint8_t)h_[i];
+        }
+    }
+
+  private:
+    uint32_t h_[8] = {0x6a09e667, 0xbb67ae85, 0x3c6ef372, 0xa54ff53a, 0x510e527f, 0x9b05688c, 0x1f83d9ab, 0x5be0cd19};
+    uint8_t buf_[64];
+    size_t fill_ = 0;
+    uint64_t total_ = 0;
+
+    static uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+
+    void block(const uint8_t* p) {
+        static const uint32_t K[64] = {
+            0x428a2f98, 0x71374491, 0xb5c0fbcf, 0xe9b5dba5, 0x3956c25b, 0x59f111f1, 0x923f82a4, 0xab1c5ed5,
+            0xd807aa98, 0x12835b01, 0x243185be, 0x550c7dc3, 0x72be5d74, 0x80deb1fe, 0x9bdc06a7, 0xc19bf174,
+            0xe49b69c1, 0xefbe4786, 0x0fc19dc6, 0x240ca1cc, 0x2de92c6f, 0x4a7484aa, 0x5cb0a9dc, 0x76f988da,
+            0x983e5152, 0xa831c66d, 0xb00327c8, 0xbf597fc7, 0xc6e00bf3, 0xd5a79147, 0x06ca6351, 0x14292967,
+            0x27b70a85, 0x2e1b2138, 0x4d2c6dfc, 0x53380d13, 0x650a7354, 0x766a0abb, 0x81c2c92e, 0x92722c85,
+            0xa2bfe8a1, 0xa81a664b, 0xc24b8b70, 0xc76c51a3, 0xd192e819, 0xd6990624, 0xf40e3585, 0x106aa070,
+            0x19a4c116, 0x1e376c08, 0x2748774c, 0x34b0bcb5, 0x391c0cb3, 0x4ed8aa4a, 0x5b9cca4f, 0x682e6ff3,
+            0x748f82ee, 0x78a5636f, 0x84c87814, 0x8cc70208, 0x90befffa, 0xa4506ceb, 0xbef9a3f7, 0xc67178f2};
         uint32_t w[64];
         for (int i = 0; i < 16; i++)
             w[i] = (uint32_t)p[4 * i] << 24 | (uint32_t)p[4 * i + 1] << 16 | (uint32_t)p[4 * i + 2] << 8 | p[4 * i + 3];
         for (int i = 16; i < 64; i++) {
-            uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
-            uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
+            const uint32_t s0 = rotr(w[i - 15], 7) ^ rotr(w[i - 15], 18) ^ (w[i - 15] >> 3);
+            const uint32_t s1 = rotr(w[i - 2], 17) ^ rotr(w[i - 2], 19) ^ (w[i - 2] >> 10);
             w[i] = w[i - 16] + s0 + w[i - 7] + s1;
         }
-        uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+        uint32_t a = h_[0], b = h_[1], c = h_[2], d = h_[3], e = h_[4], f = h_[5], g = h_[6], hh = h_[7];
         for (int i = 0; i < 64; i++) {
-            uint32_t S1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
-            uint32_t ch = (e & f) ^ (~e & g);
-            uint32_t t1 = hh + S1 + ch + K[i] + w[i];
-            uint32_t S0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
-            uint32_t mj = (a & b) ^ (a & c) ^ (b & c);
-            uint32_t t2 = S0 + mj;
+            const uint32_t S1 = rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25);
+            const uint32_t ch = (e & f) ^ (~e & g);
+            const uint32_t t1 = hh + S1 + ch + K[i] + w[i];
+            const uint32_t S0 = rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22);
+            const uint32_t mj = (a & b) ^ (a & c) ^ (b & c);
+            const uint32_t t2 = S0 + mj;
             hh = g;
             g = f;
             f = e;
@@ -46,33 +90,21 @@ inline void sha256(const uint8_t* data, size_t len, uint8_t out[32]) {
             b = a;
             a = t1 + t2;
         }
-        h[0] += a;
-        h[1] += b;
-        h[2] += c;
-        h[3] += d;
-        h[4] += e;
-        h[5] += f;
-        h[6] += g;
-        h[7] += hh;
-    };
-    size_t full = len / 64;
-    for (size_t i = 0; i < full; i++) block(data + 64 * i);
-    uint8_t tail[128];
-    size_t rest = len - 64 * full;
-    memcpy(tail, data + 64 * full, rest);
-    tail[rest] = 0x80;
-    size_t tl = rest + 1 + 8 <= 64 ? 64 : 128;
-    memset(tail + rest + 1, 0, tl - rest - 1);
-    uint64_t bits = (uint64_t)len * 8;
-    for (int i = 0; i < 8; i++) tail[tl - 1 - i] = (uint8_t)(bits >> (8 * i));
-    block(tail);
-    if (tl == 128) block(tail + 64);
-    for (int i = 0; i < 8; i++) {
-        out[4 * i] = (uint8_t)(h[i] >> 24);
-        out[4 * i + 1] = (uint8_t)(h[i] >> 16);
-        out[4 * i + 2] = (uint8_t)(h[i] >> 8);
-        out[4 * i + 3] = (uint8_t)h[i];
+        h_[0] += a;
+        h_[1] += b;
+        h_[2] += c;
+        h_[3] += d;
+        h_[4] += e;
+        h_[5] += f;
+        h_[6] += g;
+        h_[7] += hh;
     }
+};
+
+inline void sha256(const uint8_t* data, size_t len, uint8_t out[32]) {
+    Sha256 s;
+    s.update(data, len);
+    s.final(out);
 }
 
 }  // namespace hs

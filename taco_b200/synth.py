@@ -9,9 +9,21 @@
   GELU tables. The reference converter needs the published GPT-2 files and exact rationals; this
   stand-in uses float64 numpy for the same rules, so its bytes are its own (the HardShell engine
   only needs a valid file).
-- `zipf_windows(...)`: token windows of seeded Zipf(s=1.1) text over a 5,000-word random
-  lowercase vocabulary, space and newline separated. The synthetic vocabulary has one token per
-  word (with its leading space or newline), so the text is exactly the bytes of its tokens.
+- `zipf_text(...)`: seeded Zipf(s=1.1) text over a 5,000-word random lowercase vocabulary, space
+  and newline separated (one line in about 12 words); `mixed_stream(...)` the large input of
+  configs[4] (Zipf text, JSON-shaped key/number records and uniform random bytes in 64 KiB
+  pieces).
+- The synthetic vocabulary of GPT-2's size is byte-level BPE with merges, as the reference
+  converter writes GPT-2's (crates/hardshell/src/hsm/merges.rs:1-20, the optional merges
+  section): the 256 single bytes, every prefix of " w" and of "w" for the text words w, and the
+  " w" prefixes of other words up to 50,256 tokens, then <|endoftext|>. Each multi-byte token t
+  has the merge (t[:-1], t[-1]); the merges of the " w" tokens rank before those of the bare
+  ones, so the tokenizer turns every " w" piece of the text into its one word token, and a bare
+  word after a newline into one or a few tokens. `tokenize_text(...)` restates that BPE in Python
+  for text of this alphabet only (a check of the product tokenizer, and the windows of the
+  reference arm of the benchmark, which must not run this repository's engine).
+- `text_windows(...)`: the token windows of the benchmark: consecutive n-token runs of the
+  tokens of seeded Zipf text, so the bytes a window codes are bytes the fold would tokenize.
 """
 
 from __future__ import annotations
@@ -48,55 +60,198 @@ N_WORDS = 5000
 CACHE = Path(__file__).resolve().parent / "_cache"
 
 
-# ---- the synthetic vocabulary ----
+# ---- the synthetic vocabulary, its merges and the text ----
 
-def vocabulary(seed: int = 0x7AC0, vocab: int = VOCAB) -> list[bytes]:
-    """256 single bytes, word tokens (for GPT-2's 50,257: 25,000 " w" and 25,000 "\\nw" tokens; for a
-    smaller vocabulary: " w" tokens only), and <|endoftext|> last."""
+EOT_BYTES = b"<|endoftext|>"
+
+
+def _words(seed: int, n: int) -> list[bytes]:
+    """n distinct random lowercase words of 2 to 5 letters (the first N_WORDS are the text's)."""
     rng = np.random.default_rng(seed)
-    if vocab != VOCAB:
-        letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz", dtype=np.uint8)
-        words, seen = [], set()
-        while len(words) < vocab - 257:
-            w = letters[rng.integers(0, 26, int(rng.integers(2, 6)))].tobytes()
-            if w not in seen:
-                seen.add(w)
-                words.append(b" " + w)
-        return [bytes([b]) for b in range(256)] + words + [b"<|endoftext|>"]
     letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz", dtype=np.uint8)
     words: list[bytes] = []
     seen = set()
-    while len(words) < 25_000:
-        n = int(rng.integers(2, 6))
-        w = letters[rng.integers(0, 26, n)].tobytes()
+    while len(words) < n:
+        w = letters[rng.integers(0, 26, int(rng.integers(2, 6)))].tobytes()
         if w not in seen:
             seen.add(w)
             words.append(w)
+    return words
+
+
+def vocabulary(seed: int = 0x7AC0, vocab: int = VOCAB) -> list[bytes]:
+    """The token bytes, by id. For GPT-2's 50,257: 256 single bytes; the prefixes of " w" (length
+    >= 2) and of "w" (length >= 2) of the N_WORDS text words; the " w" prefixes of further words
+    until 50,256 tokens; <|endoftext|> last. Every token's bytes minus its last byte are a token,
+    so each has a merge. For a smaller vocabulary: single bytes, " w" word tokens (no merges)."""
+    if vocab != VOCAB:
+        words = _words(seed, vocab - 257)
+        return [bytes([b]) for b in range(256)] + [b" " + w for w in words] + [EOT_BYTES]
+    words = _words(seed, 40_000)
     toks = [bytes([b]) for b in range(256)]
-    toks += [b" " + w for w in words]
-    toks += [b"\n" + w for w in words]
-    toks.append(b"<|endoftext|>")
-    assert len(toks) == VOCAB
+    seen = set(toks)
+
+    def add(t: bytes):
+        if t not in seen and len(toks) < VOCAB - 1:
+            seen.add(t)
+            toks.append(t)
+
+    for w in words[:N_WORDS]:
+        for i in range(1, len(w) + 1):
+            add(b" " + w[:i])
+    for w in words[:N_WORDS]:
+        for i in range(2, len(w) + 1):
+            add(w[:i])
+    for w in words[N_WORDS:]:
+        for i in range(1, len(w) + 1):
+            add(b" " + w[:i])
+    assert len(toks) == VOCAB - 1
+    toks.append(EOT_BYTES)
     return toks
 
 
-def text_word_tokens() -> tuple[np.ndarray, np.ndarray]:
-    """The token ids of the 5,000 text words with a leading space and with a leading newline."""
-    space = 256 + np.arange(N_WORDS)
-    newline = 256 + 25_000 + np.arange(N_WORDS)
-    return space, newline
+def merges(vocab: list[bytes]) -> list[tuple[int, int]]:
+    """The BPE merges in rank order: (id of t[:-1], id of t[-1:]) for each multi-byte token t but
+    <|endoftext|>; the tokens that start with a space first, then the others, each group in id
+    order (a prefix before its extensions). Empty for a vocabulary whose tokens are not closed
+    under dropping the last byte (the small test vocabularies)."""
+    ids = {t: i for i, t in enumerate(vocab)}
+    out_sp, out_bare = [], []
+    for i, t in enumerate(vocab):
+        if len(t) < 2 or t == EOT_BYTES:
+            continue
+        left = ids.get(t[:-1])
+        if left is None:
+            return []
+        (out_sp if t[:1] == b" " else out_bare).append((left, ids[t[-1:]]))
+    return out_sp + out_bare
 
 
-def zipf_windows(n_windows: int, window: int, seed: int) -> np.ndarray:
-    """[n_windows, window] token ids of seeded Zipf(1.1) text; one line in ~12 words."""
+def text_word_ids(vocab: list[bytes]) -> np.ndarray:
+    """The ids of the " w" tokens of the N_WORDS text words, in Zipf rank order."""
+    ids = {t: i for i, t in enumerate(vocab)}
+    return np.array([ids[b" " + w] for w in _words(0x7AC0, N_WORDS)], dtype=np.uint32)
+
+
+def zipf_text(n_bytes: int, seed: int) -> bytes:
+    """About n_bytes (at least) of seeded Zipf(1.1) text over the N_WORDS text words, each word
+    after a space, or after a newline with probability 1/12; the text starts with a word."""
     rng = np.random.default_rng(seed)
+    words = _words(0x7AC0, N_WORDS)
     ranks = np.arange(1, N_WORDS + 1, dtype=np.float64)
     p = ranks ** -1.1
     p /= p.sum()
-    idx = rng.choice(N_WORDS, size=(n_windows, window), p=p)
-    space, newline = text_word_tokens()
-    nl = rng.random((n_windows, window)) < 1.0 / 12
-    return np.where(nl, newline[idx], space[idx]).astype(np.uint32)
+    out, total = [], 0
+    while total < n_bytes:
+        n = max(1024, (n_bytes - total) // 4 + 16)
+        idx = rng.choice(N_WORDS, size=n, p=p)
+        nl = rng.random(n) < 1.0 / 12
+        chunk = b"".join((b"\n" if f else b" ") + words[i] for i, f in zip(idx.tolist(), nl.tolist()))
+        out.append(chunk)
+        total += len(chunk)
+    return b"".join(out)[1:]
+
+
+def json_records(n_bytes: int, seed: int) -> bytes:
+    """About n_bytes (at least) of JSON-shaped records, one per line: 1 to 6 "key": number pairs,
+    keys from the text words (Zipf), numbers uniform integers in [-10^6, 10^6]."""
+    rng = np.random.default_rng(seed)
+    words = _words(0x7AC0, N_WORDS)
+    ranks = np.arange(1, N_WORDS + 1, dtype=np.float64)
+    p = ranks ** -1.1
+    p /= p.sum()
+    out, total = [], 0
+    while total < n_bytes:
+        n = 4096
+        pairs = rng.integers(1, 7, n)
+        keys = rng.choice(N_WORDS, size=int(pairs.sum()), p=p).tolist()
+        nums = rng.integers(-10**6, 10**6 + 1, int(pairs.sum())).tolist()
+        k = 0
+        lines = []
+        for c in pairs.tolist():
+            lines.append(b"{" + b", ".join(b'"%s": %d' % (words[keys[k + j]], nums[k + j]) for j in range(c)) + b"}\n")
+            k += c
+        chunk = b"".join(lines)
+        out.append(chunk)
+        total += len(chunk)
+    return b"".join(out)
+
+
+def mixed_stream(n_bytes: int = 256 << 20, seed: int = 4, piece: int = 64 << 10) -> bytes:
+    """n_bytes of seeded input in pieces of `piece` bytes, 70 % Zipf text, 20 %
+    JSON-shaped key/number records and 10 % uniform random bytes (exact counts of pieces, in a
+    seeded order)."""
+    n = n_bytes // piece
+    rng = np.random.default_rng(seed)
+    kinds = np.array([0] * (n * 7 // 10) + [1] * (n * 2 // 10), dtype=np.int8)
+    kinds = np.concatenate([kinds, np.full(n - kinds.size, 2, np.int8)])
+    rng.shuffle(kinds)
+    counts = np.bincount(kinds, minlength=3)
+    text = zipf_text(int(counts[0]) * piece, seed + 1)
+    js = json_records(int(counts[1]) * piece, seed + 2)
+    rnd = rng.integers(0, 256, int(counts[2]) * piece, dtype=np.uint8).tobytes()
+    src = [text, js, rnd]
+    at = [0, 0, 0]
+    out = bytearray()
+    for k in kinds.tolist():
+        out += src[k][at[k]:at[k] + piece]
+        at[k] += piece
+    return bytes(out)
+
+
+def tokenize_text(text: bytes, vocab: list[bytes], merge_list: list[tuple[int, int]]) -> np.ndarray:
+    """Byte-level BPE of text made of lowercase words, spaces and newlines only (zipf_text): the
+    GPT-2 pattern cuts it into " w", "w" and newline pieces (crates/taco/src/tokenizer/
+    pretokenize.rs), and each piece merges the adjacent pair of lowest rank first, every place of
+    that pair from the left, until no pair has a rank (bpe.rs). Each distinct piece is merged
+    once."""
+    import re
+
+    ids = {t: i for i, t in enumerate(vocab)}
+    rank = {pair: r for r, pair in enumerate(merge_list)}
+    joined = {(a, b): ids[vocab[a] + vocab[b]] for a, b in merge_list}
+    memo: dict[bytes, list[int]] = {}
+
+    def bpe(piece: bytes) -> list[int]:
+        t = [ids[piece[i:i + 1]] for i in range(len(piece))]
+        while len(t) > 1:
+            best = min(((rank.get((t[i], t[i + 1]), 1 << 62), i) for i in range(len(t) - 1)))[0]
+            if best == 1 << 62:
+                break
+            pair = merge_list[best]
+            out, i = [], 0
+            while i < len(t):
+                if i + 1 < len(t) and (t[i], t[i + 1]) == pair:
+                    out.append(joined[pair])
+                    i += 2
+                else:
+                    out.append(t[i])
+                    i += 1
+            t = out
+        return t
+
+    pieces = re.findall(rb"\n+| ?[a-z]+| +", text)
+    assert sum(len(x) for x in pieces) == len(text), "text outside the alphabet of zipf_text"
+    out: list[int] = []
+    for pc in pieces:
+        got = memo.get(pc)
+        if got is None:
+            got = memo[pc] = bpe(pc)
+        out.extend(got)
+    return np.array(out, dtype=np.uint32)
+
+
+def text_windows(n_windows: int, window: int, seed: int) -> np.ndarray:
+    """[n_windows, window] token ids: consecutive runs of the tokens of seeded Zipf text
+    (zipf_text, tokenize_text with the GPT-2-sized synthetic vocabulary and its merges)."""
+    vocab = vocabulary()
+    need = n_windows * window
+    text = zipf_text(int(need * 4.7) + 4096, seed)
+    toks = tokenize_text(text, vocab, merges(vocab))
+    while toks.size < need:
+        text += b" " + zipf_text(int((need - toks.size) * 5) + 4096, seed + toks.size)
+        toks = tokenize_text(text, vocab, merges(vocab))
+    return toks[:need].reshape(n_windows, window)
 
 
 def token_lengths(vocab: list[bytes]) -> np.ndarray:
@@ -298,8 +453,11 @@ def build_tensors(fm: dict, rg: dict, wide: bool = False) -> list[tuple[str, str
 
 def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2, wide: bool = False) -> bytes:
     """The .hsm layout (crates/hardshell/src/hsm/mod.rs:1-120): preamble, compact JSON header,
-    vocabulary and tensors at 64-byte boundaries with zero padding."""
+    vocabulary, the merges section when the vocabulary has merges (two u32 ids per merge in rank
+    order, at the 64-byte boundary after the vocabulary: hsm/merges.rs:1-20), and tensors at
+    64-byte boundaries with zero padding."""
     vocab_sec = b"".join(struct.pack("<H", len(t)) + t for t in vocab)
+    merge_sec = b"".join(struct.pack("<II", a, b) for a, b in merges(vocab))
     dt = {"i8": np.int8, "i16": np.int16, "i32": np.int32, "u64": np.uint64}
     blobs = [(n, d, np.ascontiguousarray(v, dtype=dt[d]).astype(np.dtype(dt[d]).newbyteorder("<")), s)
              for n, d, v, s in tensors]
@@ -309,6 +467,9 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2, wide: boo
         cursor = align(16 + hlen)
         voff = cursor
         cursor = voff + len(vocab_sec)
+        moff = align(cursor)
+        if merge_sec:
+            cursor = moff + len(merge_sec)
         entries = []
         for n, d, v, s in blobs:
             off = align(cursor)
@@ -323,6 +484,7 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2, wide: boo
                       "constants": dict({"ln_k": LN_K, "ln_j": LN_J, "ln_eps": eps, "softmax_p": SOFTMAX_P},
                                         **({"ln_f_bits": 16, "ln_beta_frac": BETA_FRAC} if wide else {}))},
             "vocabulary": {"offset": voff, "length": len(vocab_sec)},
+            **({"merges": {"offset": moff, "length": len(merge_sec)}} if merge_sec else {}),
             "tensors": entries,
         }
         text = json.dumps(header, separators=(",", ":")).encode()
@@ -333,6 +495,9 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2, wide: boo
     out = bytearray(b"HSHLMDL\0" + struct.pack("<II", 2 if wide else 1, hlen) + text)
     out += bytes(align(len(out)) - len(out))
     out += vocab_sec
+    if merge_sec:
+        out += bytes(moff - len(out))
+        out += merge_sec
     for (n, d, v, s), e in zip(blobs, entries):
         out += bytes(e["offset"] - len(out))
         out += v.tobytes()
@@ -342,7 +507,7 @@ def write_hsm(tensors, vocab: list[bytes], eps: int, sh: Shape = GPT2, wide: boo
 def gpt2_hsm(seed: int = 124, cache: bool = True, shape: Shape = GPT2, wide: bool = False) -> bytes:
     """The synthetic GPT-2 model file for `seed` and `shape` (GPT-2 124M by default; cached under
     taco_b200/_cache). `wide`: a version 2 file (16-bit ln_f and GELU, fractional betas)."""
-    tag = "gpt2_124m" if shape == GPT2 else "gpt2_{}l{}h{}d{}f{}v{}c".format(*vars(shape).values())
+    tag = "gpt2_124m_bpe" if shape == GPT2 else "gpt2_{}l{}h{}d{}f{}v{}c".format(*vars(shape).values())
     tag += "_v2" if wide else ""
     path = CACHE / f"{tag}_seed{seed}.hsm"
     if cache and path.exists():

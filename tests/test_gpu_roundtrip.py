@@ -125,9 +125,7 @@ def _check(gpt2, data):
 
 
 def test_zipf_text_gives_the_oracles_container(gpt2):
-    vocab = synth.vocabulary()
-    toks = synth.zipf_windows(1, 2000, seed=3672)[0]
-    data = b"".join(vocab[t] for t in toks.tolist()).lstrip()[:3672]
+    data = synth.zipf_text(3672, seed=3672)[:3672]
     assert len(data) == 3672
     _check(gpt2, data)
 

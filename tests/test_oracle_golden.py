@@ -237,3 +237,26 @@ def test_fast_path_equals_the_reference_session_on_a_version_2_model():
     w = fast.run_weights([s for s, _ in seq], [t for _, t in seq])
     for i, (s, t) in enumerate(seq):
         assert np.array_equal(w[i], refs[s].step(t)), i
+
+
+def test_fast_path_lockstep_lanes_give_the_same_answers():
+    """The oracle's lockstep lanes (one decode row for each of up to 8 slots per thread, the CPU
+    unfold of crates/taco/src/unfold.rs:215-246) answer as the per-slot path does."""
+    om = O.Model(tiny_bytes())
+    rng = np.random.default_rng(5)
+    slots = 13
+    a, b = O.FastBatch(om, slots, 3), O.FastBatch(om, slots, 3)
+    pre = rng.integers(0, om.vocab - 1, (slots, 9)).astype(np.uint32)
+    sl = np.repeat(np.arange(slots, dtype=np.uint32), 9)
+    k0 = np.zeros(sl.size, np.uint32)
+    v0 = pre.reshape(-1).astype(np.uint64)
+    assert np.array_equal(a.run_coded(sl, pre.reshape(-1), k0, v0, 32, threads=3),
+                          b.run_coded(sl, pre.reshape(-1), k0, v0, 32, threads=3))
+    one = np.arange(slots, dtype=np.uint32)
+    for step in range(4):
+        toks = rng.integers(0, om.vocab - 1, slots).astype(np.uint32)
+        kinds = np.ones(slots, np.uint32)
+        targets = rng.integers(0, 1 << 32, slots, dtype=np.uint64)
+        got = a.run_coded(one, toks, kinds, targets, 32, threads=3, lanes=True)
+        want = b.run_coded(one, toks, kinds, targets, 32, threads=3)
+        assert np.array_equal(got, want), step

@@ -183,3 +183,29 @@ def test_fold_multi_with_no_gpu_that_opens_fails_with_the_open_error(tok, monkey
         B.fold_multi([0, 1], tiny_bytes(), tok, b"some text " * 100, 300, 0, slots=2, max_rows=64)
     assert e.value.code == B.HS_NO_DEVICE
     assert "no GPU of the fold opened" in str(e.value)
+
+
+# ---- the synthetic GPT-2 vocabulary of the benchmark: byte-level BPE with merges ----
+
+def test_synthetic_vocabulary_tokenizes_the_zipf_text_as_the_python_bpe():
+    """The product tokenizer, on the merges section of the synthetic GPT-2 model, gives the tokens
+    of the Python restatement of the BPE (taco_b200/synth.py tokenize_text) for Zipf text, and
+    every " w" word of the text is one token."""
+    from taco_b200 import synth
+
+    model = synth.gpt2_hsm(124)
+    t = B.Tokenizer(model)
+    try:
+        vocab = synth.vocabulary()
+        merge_list = synth.merges(vocab)
+        assert len(merge_list) == len(vocab) - 257
+        text = synth.zipf_text(300_000, seed=11)
+        got = t.encode(text)
+        want = synth.tokenize_text(text, vocab, merge_list)
+        assert np.array_equal(got, want)
+        words = set(synth.text_word_ids(vocab).tolist())
+        n_space_words = text.count(b" ")
+        assert sum(1 for x in got.tolist() if x in words) == n_space_words
+        assert b"".join(vocab[x] for x in got.tolist()) == text
+    finally:
+        t.close()
