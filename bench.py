@@ -3,27 +3,35 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 Workload ("fold throughput"): the synthetic GPT-2 124M .hsm
-(taco_b200/synth.py), 512 independent 1024-token windows of seeded Zipf text per GPU, all
-positions of every window scored in one forward pass of its slot, each row answered by the coder
-op (the interval of the coded token in FreqTable::from_weights(weights, 32)). One step = one
-run_coded call over the 512 windows (passes of --max-rows rows). Windows are dealt to GPUs
-(weak scaling: 512 per GPU, no collective on the data path; torch.distributed only for the
-barrier and the max over ranks of the timings).
+(taco_b200/synth.py) and 512 independent 1024-token windows per GPU: consecutive runs of the tokens
+of seeded Zipf text (the synthetic vocabulary is byte-level BPE with merges, so the tokens are what
+the fold's tokenizer makes of the text, and the bytes a window codes are text bytes). All positions
+of every window are scored in one forward pass of its slot, each row answered by the coder op (the
+interval of the coded token in FreqTable::from_weights(weights, 32)). One step = one run_coded call
+over the 512 windows (passes of --max-rows rows). Windows are dealt to GPUs (weak scaling: 512 per
+GPU, no collective on the data path; torch.distributed only for barriers and the max over ranks of
+the timings).
 
 value  = input bytes of all ranks / max over ranks of the device time of the K steps (CUDA
          events around every pass on the batch stream, the token rows already on the device);
 e2e    = the same bytes / wall time of K more C-ABI calls with host buffers, without the
          profiling events (row upload, planning, interval read back inside);
+parity = rank 0 compares the intervals (symbol, start, freq) of the first windows of the timed
+         shape (512 slots, 16,384-row passes) with the CPU oracle's, field by field; a mismatch
+         fails the run;
 roofline = the kernel with the largest share of the pass time: algorithmic int8 ops (tensor-bound
          kernels) or algorithmic bytes (HBM-bound kernels) per launch / its mean CUDA-event launch
          time, against the int8 tensor peak measured in this run (torch._int_mm, cuBLASLt) or the
          measured HBM copy bandwidth (MEASURED_PEAKS.json); `rooflines` has every kernel class;
-cpu_baseline = the CPU oracle's fast path (a C++ restatement of the reference CPU engine) on a
-         bounded sample of the same windows, all host threads, rank 0 at N = 1.
-Extra fields: the GEMM microbench, the unfold decode step, the unfold of
-coded blocks with the range decoder on the device, the encoder op of the profile logs
-(run_coded_dual), and the fold and unfold of the host library end to end (hs_fold, hs_unfold).
-`--only fold_dual|fold_glue` runs one of the last two alone (profiling cases).
+cpu_baseline = the CPU oracle's fast path (a C++ restatement of the reference CPU engine) on the
+         parity windows, one window per host thread, rank 0 at N = 1.
+Extra fields: the GEMM microbench (configs[1], M = 1024, 8192, 65536, each shape checked exactly
+once), the unfold decode step over contexts 1 to 1024, the unfold of coded blocks with
+the range decoder on the device on every rank (unfold at N GPUs) next to the CPU unfold (the
+oracle's lockstep lanes), the encoder op of the profile logs (run_coded_dual), the fold and unfold
+of the host library end to end (hs_fold, hs_unfold), and the 256 MiB mixed input of configs[4]
+folded by hs_fold_multi on all N GPUs (`large_input`, with its SHA-256).
+`--only fold_dual|fold_glue|large_input` runs one of those alone (profiling cases).
 """
 
 from __future__ import annotations
@@ -47,6 +55,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "fold/unfold input MB/s at 1/2/4/8 B200 (bit-exact); int8 GEMM % of peak"
 WINDOWS, WINDOW = 512, 1024
+PARITY_WINDOWS = 16
 NOMINAL_INT8_TOPS = 4500.0
 
 
@@ -62,8 +71,9 @@ def parse_args():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-peak", action="store_true", help="skip the int8 peak measurement (profiling runs)")
-    ap.add_argument("--only", default="", choices=["", "fold_dual", "fold_glue"],
+    ap.add_argument("--only", default="", choices=["", "fold_dual", "fold_glue", "large_input"],
                     help="run one extra alone (profiling runs)")
+    ap.add_argument("--large-mb", type=int, default=256, help="configs[4] input size in MiB (0 = skip)")
     return ap.parse_args()
 
 
@@ -205,45 +215,48 @@ def rooflines(prof: dict, info, peak_tops: float | None, hbm_gbs: float | None, 
     return out
 
 
-def cpu_baseline(model_bytes: bytes, windows: np.ndarray, eot: int, lens: np.ndarray, threads: int,
-                 n_tokens: int) -> dict:
-    """The CPU oracle's fast path on `threads` windows of `n_tokens` tokens (one window per thread)."""
+def oracle_windows(model_bytes: bytes, windows: np.ndarray, eot: int, lens: np.ndarray, threads: int) -> dict:
+    """The CPU oracle's fast path on `windows` (one window per host thread at a time): its
+    answers {symbol, start, freq} per row, and its speed (the bench's cpu_baseline)."""
     from oracle import oracle as O
 
     om = O.Model(model_bytes)
-    sample = windows[:threads, :n_tokens]
-    fb = O.FastBatch(om, sample.shape[0], 0)
-    slots, inputs, coded = window_rows(sample, eot)
+    fb = O.FastBatch(om, windows.shape[0], 0)
+    slots, inputs, coded = window_rows(windows, eot)
     t0 = time.perf_counter()
-    fb.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32, threads=threads)
+    ans = fb.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32, threads=threads)
     dt = time.perf_counter() - t0
     nbytes = int(lens[coded.astype(np.int64)].sum())
-    return {"value": nbytes / dt / 1e6, "unit": "MB/s", "cores": threads, "kind": "port",
+    return {"answers": ans, "value": nbytes / dt / 1e6, "unit": "MB/s", "cores": threads, "kind": "port",
             "tokens_per_s": slots.size / dt,
-            "sample": f"{sample.shape[0]} windows x {n_tokens} tokens (positions 0..{n_tokens - 1}), "
+            "sample": f"{windows.shape[0]} windows x {windows.shape[1]} tokens (positions 0..{windows.shape[1] - 1}), "
                       f"{nbytes} input bytes, {dt:.1f} s, one window per thread"}
 
 
 def run_reference(args, world, rank):
-    """--impl reference: the CPU oracle port of the reference CPU engine, timed on the host cores."""
+    """--impl reference: the CPU oracle port of the reference CPU engine, timed on the host cores,
+    on the bench's own configuration: the same text windows of 1024 tokens, all positions scored.
+    A step is one window per host thread (the smallest sample that keeps every thread busy); the
+    warm-up steps run one window of 64 tokens each. The windows are tokenized by the Python
+    restatement of the BPE (taco_b200/synth.py tokenize_text), not this repository's engine."""
     if rank != 0:
         return 0
+    from oracle import oracle as O
     from taco_b200 import synth
 
     model = synth.gpt2_hsm(124)
     vocab = synth.vocabulary()
     lens = synth.token_lengths(vocab)
+    eot = synth.VOCAB - 1
     threads = args.cpu_threads or os.cpu_count() or 1
-    n_tok = 256
-    wins = synth.zipf_windows(threads, n_tok, seed=1000)
-    from oracle import oracle as O
-
+    wins = synth.text_windows(threads, WINDOW, seed=1000)
     om = O.Model(model)
-    slots, inputs, coded = window_rows(wins, synth.VOCAB - 1)
+    slots, inputs, coded = window_rows(wins, eot)
     nbytes = int(lens[coded.astype(np.int64)].sum())
+    ws, wi, wc = window_rows(wins[:1, :64], eot)
     for _ in range(args.warmup):
-        fb = O.FastBatch(om, threads, 0)
-        fb.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32, threads=threads)
+        fb = O.FastBatch(om, 1, 0)
+        fb.run_coded(ws, wi, np.zeros(ws.size, np.uint32), wc, 32, threads=1)
     times = []
     for _ in range(args.steps):
         fb = O.FastBatch(om, threads, 0)
@@ -252,13 +265,17 @@ def run_reference(args, world, rank):
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = nbytes * args.steps / total / 1e6
-    sample = f"{threads} windows x {n_tok} tokens per step ({nbytes} input bytes), one window per thread"
+    sample = (f"{threads} windows x {WINDOW} tokens per step ({nbytes} input bytes), one window per thread; "
+              "warm-up steps: one window of 64 tokens")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "MB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32/int64",
-        "data": "synthetic", "config": {"workload": "fold throughput (configs[2]) sample on host cores",
-                                         "model": "GPT-2 124M synthetic .hsm", "window": n_tok},
+        "data": "synthetic",
+        "config": {"workload": "fold throughput (BASELINE configs[2]): 1024-token windows of Zipf text, all "
+                               "positions scored, coder interval per row; a step holds one window per host thread",
+                   "model": "GPT-2 124M .hsm from seeded N(0,0.02) (taco_b200/synth.py)",
+                   "window_tokens": WINDOW, "windows_per_step": threads, "same_config": True},
         "cpu_baseline": {"value": value, "unit": "MB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "MB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "tokens_per_s": slots.size * args.steps / total,
@@ -296,18 +313,21 @@ def main():
     # The job: windows x world windows of seeded text, dealt round-robin to the GPUs (weak scaling:
     # each GPU gets `windows`); no collective touches them.
     n_total = args.windows * world
-    all_windows = synth.zipf_windows(n_total, WINDOW, seed=1000)
+    all_windows = synth.text_windows(n_total, WINDOW, seed=1000)
     windows = all_windows[shard.deal(n_total, world, rank)]
     slots, inputs, coded = window_rows(windows, eot)
     kinds = np.zeros(slots.size, np.uint32)
     step_bytes = int(lens[coded.astype(np.int64)].sum())
     if args.only:
+        if args.only == "large_input":
+            print(json.dumps({"large_input": large_input(B, model_bytes, args.large_mb, [local])}))
+            return 0
         dev = B.CudaDevice(local)
         model = B.CudaModel(dev, model_bytes)
         if args.only == "fold_dual":
             print(json.dumps({"fold_dual": fold_dual(B, model, windows, lens, eot, sample=args.windows)}))
         else:
-            print(json.dumps({"fold_glue": fold_glue(B, model, model_bytes, vocab)}))
+            print(json.dumps({"fold_glue": fold_glue(B, model, model_bytes)}))
         model.close()
         dev.close()
         return 0
@@ -322,7 +342,8 @@ def main():
             batch.reset(s)
         return batch.run_coded(slots, inputs, kinds, coded, 32)
 
-    # Warm-up; the first answers are checked for their symbols (the coded tokens).
+    # Warm-up; the answers of the last one are checked: the symbols here, the intervals of the
+    # first windows against the oracle below.
     for i in range(args.warmup):
         ans = step()
     if not np.array_equal(ans["symbol"].astype(np.uint64), coded):
@@ -360,10 +381,20 @@ def main():
 
     gemm_ops = sum(prof[k]["ops"] for k in prof if k.startswith("gemm"))
     gemm_ms = sum(prof[k]["ms"] for k in prof if k.startswith("gemm"))
-    gemm_launches = sum(prof[k]["launches"] for k in prof if k.startswith("gemm"))
     achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else 0.0
 
+    # The unfold on every GPU at once (configs[3] at N GPUs): each rank decodes its own coded
+    # blocks with the device range decoder, timed between barriers, the max over ranks.
+    ub = unfold_blocks(B, model, lens)
+    barrier()
+    t0 = time.perf_counter()
+    ub_timed = unfold_blocks(B, model, lens, timed_only=True)
+    ub_wall = time.perf_counter() - t0
+    barrier()
+    (ub_max,) = shard.max_over_ranks([ub_wall], device=f"cuda:{local}")
+
     result = None
+    failed = False
     if rank == 0:
         kernels = {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
                        "share": round(v["ms"] / prof["pass"]["ms"], 4) if prof["pass"]["ms"] else None}
@@ -381,10 +412,13 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dev_s / args.steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic",
-            "config": {"workload": "fold throughput (BASELINE configs[2]): 512 windows x 1024 tokens per GPU, "
-                                   "all positions in one forward pass per window, coder interval per row",
-                       "model": "GPT-2 124M .hsm from seeded N(0,0.02) (taco_b200/synth.py)",
+            "config": {"workload": "fold throughput (BASELINE configs[2]): 512 windows x 1024 tokens per GPU of "
+                                   "tokenized Zipf text, all positions in one forward pass per window, coder "
+                                   "interval per row",
+                       "model": "GPT-2 124M .hsm from seeded N(0,0.02) with a byte-level BPE vocabulary and merges "
+                                "(taco_b200/synth.py)",
                        "windows_per_gpu": args.windows, "window_tokens": WINDOW, "max_rows_per_pass": args.max_rows,
+                       "bytes_per_token": round(step_bytes / slots.size, 3),
                        "parallelism": f"{n_total} windows dealt round-robin to {world} GPU(s), no collective",
                        "l2": "inputs larger than L2: each step streams 124 MB of weights per pass and "
                              "9.7 GB of KV cache"},
@@ -397,85 +431,163 @@ def main():
             "clocks": clk,
             "gpu_launches": launches,
             "kernels": kernels,
+            "unfold_gpus": {"n_gpus": world, "streams_per_gpu": ub_timed["streams"],
+                            "tokens_per_block": ub_timed["tokens_per_block"],
+                            "e2e_tokens_per_s": world * ub_timed["tokens"] / ub_max,
+                            "e2e_MB_per_s": world * ub_timed["bytes"] / ub_max / 1e6,
+                            "timing": "wall clock of one hs_batch_decode_blocks call per rank between barriers, "
+                                      "max over ranks"},
         }
-
-    # Extras: the GEMM microbench and one unfold decode step.
-    if rank == 0 and not args.no_extras:
-        micro = {}
-        for (K, N) in [(768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 50257)]:
-            n16 = (N + 15) // 16 * 16
-            us = dev.linear_bench(8192, n16, K, seed=7, warmup=3, iters=20)
-            tops = 2.0 * 8192 * N * K / (us * 1e-6) / 1e12
-            micro[f"M8192_K{K}_N{N}"] = {"us": round(us, 2), "tops": round(tops, 1),
-                                        "frac": round(tops / peak["tops"], 3) if peak else None}
-        result["gemm_microbench"] = micro
-        result["unfold"] = unfold_step(B, model, lens, eot, clock_note=None)
-        result["unfold_blocks"] = unfold_blocks(B, model)
-        result["fold_dual"] = fold_dual(B, model, windows, lens, eot)
-        result["fold_glue"] = fold_glue(B, model, model_bytes, vocab)
-    if rank == 0:
+        # Parity on the bench's own shape: the intervals of the first windows of the last warm-up
+        # step (512 slots, passes of max_rows rows) against the oracle's, field by field.
+        threads = args.cpu_threads or os.cpu_count() or 1
+        n_par = max(PARITY_WINDOWS, threads) if world == 1 else PARITY_WINDOWS
+        n_par = min(n_par, args.windows)
+        ora = oracle_windows(model_bytes, windows[:n_par], eot, lens, threads)
+        got = np.stack([ans["symbol"], ans["start"], ans["freq"]], 1).astype(np.uint64)[:n_par * WINDOW]
+        bad = np.any(got != ora["answers"], axis=1)
+        result["parity"] = {"windows": int(n_par), "rows": int(n_par * WINDOW), "pass_rows": args.max_rows,
+                            "slots": args.windows, "fields": ["symbol", "start", "freq"],
+                            "mismatches": int(bad.sum()),
+                            "against": "CPU oracle fast path (oracle/), the same windows"}
+        failed = bool(bad.any())
         if world == 1 and not args.no_cpu:
-            threads = args.cpu_threads or os.cpu_count() or 1
-            result["cpu_baseline"] = cpu_baseline(model_bytes, windows, eot, lens, threads, 1024)
-        print(json.dumps(result))
+            result["cpu_baseline"] = {k: v for k, v in ora.items() if k != "answers"}
+        result["unfold_gpus"]["per_rank_first_call"] = {k: ub[k] for k in ("e2e_tokens_per_s", "device_tokens_per_s")}
+
+    # Extras: the GEMM microbench, the unfold sweep and the CPU unfold.
+    if rank == 0 and not args.no_extras:
+        result["gemm_microbench"] = gemm_microbench(dev, peak)
+        result["unfold"] = unfold_sweep(B, model, lens, eot)
+        result["unfold_blocks"] = ub
+        threads = args.cpu_threads or os.cpu_count() or 1
+        cpu_u = unfold_cpu(model_bytes, eot, threads)
+        result["unfold_cpu_baseline"] = cpu_u
+        result["unfold_ratio"] = {
+            "e2e_device_decoder_vs_cpu": ub["e2e_tokens_per_s"] / cpu_u["tokens_per_s"],
+            f"gpus_{world}_vs_cpu": result["unfold_gpus"]["e2e_tokens_per_s"] / cpu_u["tokens_per_s"],
+            "note": "tokens/s of the device decoder (1,024 blocks x 256 tokens from position 0, wall clock) over the "
+                    "CPU oracle's lockstep-lane decode from position 0 on all host threads"}
+        result["fold_dual"] = fold_dual(B, model, windows, lens, eot)
+        result["fold_glue"] = fold_glue(B, model, model_bytes)
     batch.close()
     model.close()
     dev.close()
+    # the large mixed input through hs_fold_multi on every GPU of the job, from rank 0
+    # after every rank has freed its handles.
+    if args.large_mb and not args.no_extras:
+        if pg:
+            torch.distributed.barrier()
+        if rank == 0:
+            result["large_input"] = large_input(B, model_bytes, args.large_mb, list(range(world)))
+        if pg:
+            torch.distributed.barrier()
+    if rank == 0:
+        print(json.dumps(result))
     if pg:
         torch.distributed.destroy_process_group()
+    if failed:
+        print("parity: the GPU intervals differ from the oracle's", file=sys.stderr)
+        return 1
     return 0
 
 
-def unfold_step(B, model, lens, eot, clock_note=None, streams: int = 1024, context: int = 512, steps: int = 16) -> dict:
-    """1024 streams decoded token by token. The streams are filled to `context`
-    positions (prefill, not timed), then `steps` decode steps (one row per stream, the coder
-    op answering a decode query for each row: the symbol whose interval holds a seeded 32-bit
-    target) are timed with the wall clock around the C-ABI calls (end to end, no profiling), and
-    the next `steps` steps on the device (per-op CUDA events). The next input of a stream is the
-    text's own next token, so the rows are those of a real unfold."""
+def gemm_microbench(dev, peak) -> dict:
+    """the linear op on device-resident int8 operands (hs_op_linear_bench, CUDA events
+    over 20 launches after 3) at M = 1024, 8192 and 65536 for the five GPT-2 shapes (N rounded up
+    to 16). Each shape is also checked exactly once at M = 1024 through the host-buffer op: the
+    int32 accumulators against A . W^T (float64 BLAS, exact below 2^53) and the requantised int8
+    against the rule of ops.rs:434 (LinearOut::Act)."""
+    micro = {}
+    rng = np.random.default_rng(12)
+    for (K, N) in [(768, 2304), (768, 768), (768, 3072), (3072, 768), (768, 50257)]:
+        n16 = (N + 15) // 16 * 16
+        for M in (1024, 8192, 65536):
+            us = dev.linear_bench(M, n16, K, seed=7, warmup=3, iters=20)
+            tops = 2.0 * M * N * K / (us * 1e-6) / 1e12
+            micro[f"M{M}_K{K}_N{N}"] = {"us": round(us, 2), "tops": round(tops, 1),
+                                        "frac": round(tops / peak["tops"], 3) if peak else None}
+        A = rng.integers(-127, 128, (1024, K), dtype=np.int8)
+        W = rng.integers(-127, 128, (n16, K), dtype=np.int8)
+        b = rng.integers(-2**20, 2**20, n16).astype(np.int32)
+        m = rng.integers(1 << 30, 1 << 31, n16).astype(np.int32)
+        sh = 38
+        raw = dev.matmul_raw(A, W)
+        want = A.astype(np.float64) @ W.astype(np.float64).T
+        exact_raw = bool(np.array_equal(raw.astype(np.float64), want))
+        y = dev.linear_act(A, W, b, m, sh)
+        p = (want.astype(np.int64) + b.astype(np.int64)) * m.astype(np.int64)
+        yw = np.clip((p >> sh) + ((p >> (sh - 1)) & 1), -127, 127).astype(np.int8)
+        micro[f"exact_K{K}_N{N}"] = {"M": 1024, "int32": exact_raw, "requant_int8": bool(np.array_equal(y, yw))}
+        if not (exact_raw and np.array_equal(y, yw)):
+            raise SystemExit(f"the GEMM microbench shape K={K} N={N} is not exact")
+    return micro
+
+
+def unfold_sweep(B, model, lens, eot, streams: int = 1024, steps: int = 8,
+                 points=(0, 128, 256, 384, 512, 640, 768, 896, 1008)) -> dict:
+    """1024 streams decoded token by token with the context growing from 1 to 1024.
+    The streams are filled (prefill, not timed) to each point p, then `steps` decode steps (one row
+    per stream, a decode query with a seeded 32-bit target each) are timed end to end (the wall
+    clock around the C-ABI calls), and the next `steps` on the device (per-op CUDA events). Each
+    stream's next input is its text's own next token, so the rows are those of a real unfold.
+    The KV cache read per step is streams x 2 x L x d bytes per context position."""
     from taco_b200 import synth
 
-    toks = synth.zipf_windows(streams, context + 2 * steps, seed=77)
+    toks = synth.text_windows(streams, 1024, seed=77)
+    info = model.info
     batch = B.CudaBatch(model, streams, 16384)
-    slots, inputs, coded = window_rows(toks[:, :context], eot)
-    batch.run_coded(slots, inputs, np.zeros(slots.size, np.uint32), coded, 32)
     sl = np.arange(streams, dtype=np.uint32)
     kinds = np.ones(streams, np.uint32)
-    targets = np.random.default_rng(78).integers(0, 1 << 32, (2 * steps, streams), dtype=np.uint64)
-    t0 = time.perf_counter()
-    for i in range(steps):
-        batch.run_coded(sl, toks[:, context + i - 1], kinds, targets[i], 32)
-    wall = time.perf_counter() - t0
-    batch.set_profiling(True)
-    for i in range(steps, 2 * steps):
-        batch.run_coded(sl, toks[:, context + i - 1], kinds, targets[i], 32)
-    prof = batch.profile()
+    rng = np.random.default_rng(78)
+    pos, out = 0, []
+
+    def inputs_at(j):
+        return np.full(streams, eot, np.uint32) if j == 0 else toks[:, j - 1]
+
+    for p in points:
+        if p > pos:  # prefill rows pos .. p - 1 of every stream, slot-major
+            cols = np.arange(pos, p)
+            inp = np.stack([inputs_at(j) for j in cols], 1).reshape(-1)
+            s = np.repeat(sl, cols.size)
+            batch.run_coded(s, inp, np.zeros(s.size, np.uint32), toks[:, pos:p].reshape(-1).astype(np.uint64), 32)
+        t0 = time.perf_counter()
+        for j in range(p, p + steps):
+            batch.run_coded(sl, inputs_at(j), kinds, rng.integers(0, 1 << 32, streams, dtype=np.uint64), 32)
+        wall = time.perf_counter() - t0
+        batch.set_profiling(True)
+        for j in range(p + steps, p + 2 * steps):
+            batch.run_coded(sl, inputs_at(j), kinds, rng.integers(0, 1 << 32, streams, dtype=np.uint64), 32)
+        prof = batch.profile()
+        batch.set_profiling(False)
+        pos = p + 2 * steps
+        dev_s = prof["pass"]["ms"] / 1e3
+        kv = streams * steps * 2 * info.n_layer * info.d_model * (p + steps + (steps + 1) / 2)
+        out.append({"context": f"{p + steps + 1}..{p + 2 * steps}", "tokens_per_s": streams * steps / dev_s,
+                    "e2e_tokens_per_s": streams * steps / wall, "kv_GB_per_s": kv / dev_s / 1e9,
+                    "ms_per_step": round(1000 * dev_s / steps, 3),
+                    "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3)})
     batch.close()
-    dev_s = prof["pass"]["ms"] / 1e3
-    nbytes = int(lens[toks[:, context + steps:context + 2 * steps].astype(np.int64)].sum())
-    kv_read = streams * steps * 2 * 12 * 768 * (context + 1.5 * steps)
-    return {"streams": streams, "positions": f"{context}..{context + steps - 1} (end to end), "
-            f"{context + steps}..{context + 2 * steps - 1} (device)", "steps": steps,
-            "tokens_per_s": streams * steps / dev_s, "MB_per_s": nbytes / dev_s / 1e6,
-            "e2e_tokens_per_s": streams * steps / wall,
-            "kv_GB_per_s": kv_read / dev_s / 1e9,
-            "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3),
-            "kernels_ms_per_step": {k: round(v["ms"] / steps, 3) for k, v in prof.items() if v["launches"]}}
+    return {"streams": streams, "steps_per_point": steps, "points": out}
 
 
-def unfold_blocks(B, model, streams: int = 1024, tokens: int = 256) -> dict:
+def unfold_blocks(B, model, lens, streams: int = 1024, tokens: int = 256, timed_only: bool = False) -> dict:
     """configs[3] with the range decoder on the device: `streams` coded blocks of `tokens` tokens,
-    unfolded from position 0 by one hs_batch_decode_blocks call (no host round trip per token),
-    against the same rows driven step by step through run_coded with decode queries (one host
-    round trip per step, the structure of the reference's unfold loop; its targets here are
-    seeded, as a host decoder's would be). The payloads are seeded random bytes: the decoder turns
-    any input into symbols, and the work of a step does not depend on the bytes. Both arms are
-    timed by the wall clock around the C-ABI calls, the better of two runs each; the device time
-    of the decoder arm comes from a third, profiled call."""
+    unfolded from position 0 by one hs_batch_decode_blocks call (no host round trip per token).
+    The payloads are seeded random bytes: the decoder turns any input into symbols, and the work of
+    a step does not depend on the bytes. Timed by the wall clock around the C-ABI call, the better
+    of two, with the device time from a third, profiled call; then the same rows driven step by
+    step through run_coded with decode queries (one host round trip per step, the structure of the
+    reference's GPU unfold loop). `timed_only`: one call, its symbols and bytes, nothing else."""
     rng = np.random.default_rng(79)
     payloads = [rng.integers(0, 256, 4 * tokens, dtype=np.uint8).tobytes() for _ in range(streams)]
     sl = np.arange(streams, dtype=np.uint32)
     batch = B.CudaBatch(model, streams, 4096)
+    if timed_only:
+        toks, status = batch.decode_blocks(sl, payloads, [tokens] * streams, 32)
+        batch.close()
+        return {"streams": streams, "tokens_per_block": tokens, "tokens": streams * tokens,
+                "bytes": int(lens[np.concatenate(toks).astype(np.int64)].sum())}
     batch.decode_blocks(sl[:8], payloads[:8], [4] * 8, 32)  # warm-up
     wall = float("inf")
     for _ in range(2):  # the better of two calls, for each arm
@@ -487,7 +599,6 @@ def unfold_blocks(B, model, streams: int = 1024, tokens: int = 256) -> dict:
     prof = batch.profile()
     batch.set_profiling(False)
     dev_ms = prof["pass"]["ms"] + prof.get("decoder", {"ms": 0.0})["ms"]
-    # The host loop over run_coded, from position 0 as well.
     targets = rng.integers(0, 1 << 32, (tokens, streams), dtype=np.uint64)
     kinds = np.ones(streams, np.uint32)
     wall_host = float("inf")
@@ -502,10 +613,36 @@ def unfold_blocks(B, model, streams: int = 1024, tokens: int = 256) -> dict:
         wall_host = min(wall_host, time.perf_counter() - t0)
     batch.close()
     n = streams * tokens
+    nbytes = int(lens[np.concatenate(toks).astype(np.int64)].sum())
     return {"streams": streams, "tokens_per_block": tokens, "positions": f"0..{tokens - 1}",
             "e2e_tokens_per_s": n / wall, "device_tokens_per_s": n / (dev_ms / 1e3),
+            "e2e_MB_per_s": nbytes / wall / 1e6,
             "host_loop_e2e_tokens_per_s": n / wall_host, "failed_blocks": int(status.sum()),
             "decoder_ms": round(prof.get("decoder", {"ms": 0.0})["ms"], 3)}
+
+
+def unfold_cpu(model_bytes: bytes, eot: int, threads: int, steps: int = 24) -> dict:
+    """The CPU unfold of the reference (crates/taco/src/unfold.rs:215-246): blocks decode in
+    lockstep lanes of up to 8 per thread, every thread busy: 8 x threads streams decoded from
+    position 0 for `steps` steps (one row per stream and step, a decode query with a seeded target
+    each) by the CPU oracle's fast path with lanes, timed by the wall clock."""
+    from oracle import oracle as O
+
+    om = O.Model(model_bytes)
+    streams = 8 * threads
+    fb = O.FastBatch(om, streams, 0)
+    rng = np.random.default_rng(80)
+    sl = np.arange(streams, dtype=np.uint32)
+    kinds = np.ones(streams, np.uint32)
+    inp = np.full(streams, eot, np.uint32)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ans = fb.run_coded(sl, inp, kinds, rng.integers(0, 1 << 32, streams, dtype=np.uint64), 32, threads=threads,
+                           lanes=True)
+        inp = ans[:, 0].astype(np.uint32)
+    dt = time.perf_counter() - t0
+    return {"tokens_per_s": streams * steps / dt, "cores": threads, "kind": "port",
+            "sample": f"{streams} streams (8 lanes per thread) x {steps} decode steps from position 0, {dt:.1f} s"}
 
 
 def fold_dual(B, model, windows, lens, eot, sample: int = 64) -> dict:
@@ -565,21 +702,18 @@ def fold_dual(B, model, windows, lens, eot, sample: int = 64) -> dict:
     return out
 
 
-def fold_glue(B, model, model_bytes, vocab, mb: int = 2) -> dict:
+def fold_glue(B, model, model_bytes, mb: int = 2) -> dict:
     """The fold and the unfold of the profile text end to end through the host library (hs_fold,
     hs_unfold: tokenizer, zstd level 19, the coder op on the GPU, range encoder, container) on `mb`
-    MiB of seeded Zipf text (the bytes of the synthetic vocabulary's word tokens), default block
-    size 16 KiB, one slot per block. The synthetic vocabulary has no merges, so the tokenizer gives
-    one token per byte (about 4.6 times the rows of the bench's token windows per byte). Timed by
-    the wall clock (the better of two); the device time of the fold's passes from a third,
-    profiled call. A random-initialised model rarely beats zstd, so the unfold mostly decodes zstd
-    frames: it measures the glue, not the coder."""
+    MiB of seeded Zipf text, default block size 16 KiB. Timed by the wall clock (the better of
+    two); the device time of the fold's passes from a third, profiled call. A random-initialised
+    model rarely beats zstd, so the encoders of most blocks stop before their last windows (which
+    then never run) and the unfold mostly decodes zstd frames."""
     from taco_b200 import synth
 
-    w = synth.zipf_windows(256, 1024, seed=4242)
-    text = b"".join(vocab[t] for t in w.reshape(-1).tolist())[: mb << 20]
+    text = synth.zipf_text(mb << 20, seed=4242)[: mb << 20]
     tok = B.Tokenizer(model_bytes)
-    batch = B.CudaBatch(model, 256, 16384)
+    batch = B.CudaBatch(model, 512, 16384)
     B.fold(batch, tok, text[:20000])  # warm-up
     wall = float("inf")
     for _ in range(2):
@@ -600,11 +734,51 @@ def fold_glue(B, model, model_bytes, vocab, mb: int = 2) -> dict:
     batch.close()
     tok.close()
     return {"input_bytes": len(text), "blocks": stats["blocks"], "tokens": stats["tokens"],
-            "coded_blocks": stats["coded_blocks"], "zstd_blocks": stats["zstd_blocks"],
+            "gpu_rows": stats["gpu_rows"], "coded_blocks": stats["coded_blocks"], "zstd_blocks": stats["zstd_blocks"],
             "container_bytes": stats["container_len"],
             "fold_e2e_MB_per_s": len(text) / wall / 1e6, "fold_device_ms": round(prof["pass"]["ms"], 3),
             "fold_wall_ms": round(wall * 1e3, 3), "fold_device_share": round(prof["pass"]["ms"] / (wall * 1e3), 3),
+            "stages_ms": {k: round(stats[k], 1) for k in ("prep_ms", "gpu_ms", "finish_ms")},
             "unfold_e2e_MB_per_s": len(text) / uwall / 1e6}
+
+
+def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int]) -> dict:
+    """`mb` MiB of the seeded mixed stream (70 % Zipf text, 20 % JSON key/number
+    records, 10 % uniform random bytes, in 64 KiB pieces; synth.mixed_stream) folded by
+    hs_fold_multi on the GPUs `ordinals` (one host thread each; 512 slots, 16,384-row passes) and
+    unfolded by hs_unfold on the first; wall clock, the container's SHA-256, the stage times of the
+    fold. The same bytes on every GPU count (tests/test_gpu_fold.py, tests/test_gpu_large_input.py
+    check the equality with one GPU and with the CPU path on samples)."""
+    import hashlib
+
+    from taco_b200 import synth
+
+    data = synth.mixed_stream(mb << 20)
+    tok = B.Tokenizer(model_bytes)
+    t0 = time.perf_counter()
+    got, stats = B.fold_multi(ordinals, model_bytes, tok, data, slots=512, max_rows=16384)
+    fold_s = time.perf_counter() - t0
+    dev = B.CudaDevice(ordinals[0])
+    model = B.CudaModel(dev, model_bytes)
+    batch = B.CudaBatch(model, 256, 16384)
+    t0 = time.perf_counter()
+    back = B.unfold(batch, tok, got)
+    unfold_s = time.perf_counter() - t0
+    ok = back == data
+    batch.close()
+    model.close()
+    dev.close()
+    tok.close()
+    if not ok:
+        raise SystemExit("the large input did not unfold to itself")
+    return {"input_MiB": mb, "gpus": len(ordinals), "blocks": stats["blocks"], "tokens": stats["tokens"],
+            "gpu_rows": stats["gpu_rows"], "coded_blocks": stats["coded_blocks"], "zstd_blocks": stats["zstd_blocks"],
+            "raw_blocks": stats["blocks"] - stats["coded_blocks"] - stats["zstd_blocks"],
+            "container_bytes": stats["container_len"], "sha256": hashlib.sha256(got).hexdigest(),
+            "fold_wall_s": round(fold_s, 3), "fold_MB_per_s": len(data) / fold_s / 1e6,
+            "fold_stages_ms": {k: round(stats[k], 1) for k in ("prep_ms", "gpu_ms", "finish_ms")},
+            "unfold_wall_s": round(unfold_s, 3), "unfold_MB_per_s": len(data) / unfold_s / 1e6,
+            "gpus_failed": stats["gpus_failed"]}
 
 
 if __name__ == "__main__":

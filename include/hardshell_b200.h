@@ -37,7 +37,9 @@ enum hs_status {
     HS_BAD_ARGUMENT = 9,    /* a null pointer or a size out of range */
     HS_FORMAT = 10,         /* TacoError::Format: the container breaks a rule of the format */
     HS_CORRUPT = 11,        /* TacoError::CorruptBlock / ChecksumMismatch: a block or the output is wrong */
-    HS_MODEL_MISMATCH = 12  /* TacoError::ModelHashMismatch: the container names another model */
+    HS_MODEL_MISMATCH = 12, /* TacoError::ModelHashMismatch: the container names another model */
+    HS_IO = 13              /* TacoError::Io / StreamError: a source, sink or writer of the caller failed,
+                               or the input is shorter or longer than its length */
 };
 
 typedef struct hs_dev hs_dev;
@@ -219,6 +221,10 @@ typedef struct hs_fold_stats {
     uint32_t block_size;
     uint32_t gpus_failed; /* hs_fold_multi: the GPUs that did not open and gave their windows away */
     uint64_t gpu_rows;    /* the rows that ran on the GPUs (windows of stopped blocks never start) */
+    /* Wall time of the stages, summed over the segments: the host threads' tokens and zstd frames
+     * (overlapped with the GPU stage of the previous segment), the GPU stage (passes and the range
+     * encoders), and the payloads, the stored forms and the writes. */
+    double prep_ms, gpu_ms, finish_ms;
 } hs_fold_stats;
 
 /* The largest container of a fold of `len` bytes with this block size (0 = the default). */
@@ -252,6 +258,45 @@ int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_fil
                   uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* input,
                   size_t len, const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len,
                   hs_fold_stats* stats);
+
+/* ---- streams: inputs of any size with bounded memory (crates/taco/src/stream.rs) ----
+ *
+ * The bytes are those of hs_fold and hs_unfold; the work moves in segments of blocks (at most 64
+ * MiB of input and 4,096 blocks each), and a fold or unfold holds about two segments: the one on
+ * the GPUs and the next one on the host threads. The callbacks are called on the caller's thread
+ * only, in order. */
+
+/* The input of a fold: fills buf with up to cap bytes and gives their count; 0 only at the end
+ * of the input; < 0 on an error (the call fails with HS_IO). */
+typedef int64_t (*hs_source_fn)(void* user, uint8_t* buf, size_t cap);
+/* The output of a fold, seekable: writes buf[0 .. n) at offset `at`; 0, or non-zero on an error. */
+typedef int (*hs_sink_fn)(void* user, uint64_t at, const uint8_t* buf, size_t n);
+/* The container of an unfold: reads n bytes at offset `at` into buf; 0, or non-zero on an error. */
+typedef int (*hs_read_at_fn)(void* user, uint64_t at, uint8_t* buf, size_t n);
+/* The output of an unfold, in order: takes buf[0 .. n); 0, or non-zero on an error. */
+typedef int (*hs_write_fn)(void* user, const uint8_t* buf, size_t n);
+
+/* StreamFold::to_seekable (stream.rs:419-428): the fold of hs_fold of the `len` bytes that
+ * `source` gives, into `sink`. The sink receives the block table and the stored blocks of each
+ * segment as it ends, and the header (which holds the input's SHA-256) last; *out_len = the
+ * container length. HS_IO if the source gives fewer or more than `len` bytes or a callback fails. */
+int hs_fold_stream(hs_batch* batch, const hs_tokenizer* tokenizer, uint64_t len, hs_source_fn source,
+                   void* source_user, hs_sink_fn sink, void* sink_user, const hs_fold_options* options,
+                   uint64_t* out_len, hs_fold_stats* stats);
+
+/* hs_fold_stream on several GPUs of this host, as hs_fold_multi. */
+int hs_fold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                         uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, uint64_t len,
+                         hs_source_fn source, void* source_user, hs_sink_fn sink, void* sink_user,
+                         const hs_fold_options* options, uint64_t* out_len, hs_fold_stats* stats);
+
+/* StreamUnfold::from_seekable (stream.rs): the unfold of hs_unfold of the `len`-byte container
+ * that `read_at` reads, into `write`. The header, the whole block table and the container length
+ * are checked before any output; then each segment's bytes go to `write` in order. *out_len = the
+ * original length (from the header). The SHA-256 is checked at the end: HS_CORRUPT then means
+ * that the bytes already written are wrong. */
+int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tokenizer, uint64_t len, hs_read_at_fn read_at,
+                     void* read_user, hs_write_fn write, void* write_user, uint64_t* out_len);
 
 /* taco::unfold on the CUDA engine (crates/taco/src/unfold.rs, profile text): the original bytes of
  * a .taco container (version 1 or 2) into out[0 .. *out_len). The header and the block table are

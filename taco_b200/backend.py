@@ -18,12 +18,12 @@ LIB_PATH = Path(__file__).resolve().parent / "libhardshell_b200.so"
 
 HS_OK, HS_NO_DEVICE, HS_CUDA, HS_UNSUPPORTED, HS_MODEL = 0, 1, 2, 3, 4
 HS_BAD_SLOT, HS_LENGTH_MISMATCH, HS_TOKEN_RANGE, HS_INVALID_OVERLAP, HS_BAD_ARGUMENT = 5, 6, 7, 8, 9
-HS_FORMAT, HS_CORRUPT, HS_MODEL_MISMATCH = 10, 11, 12
+HS_FORMAT, HS_CORRUPT, HS_MODEL_MISMATCH, HS_IO = 10, 11, 12, 13
 _NAMES = {
     HS_NO_DEVICE: "NoDevice", HS_CUDA: "Cuda", HS_UNSUPPORTED: "Unsupported", HS_MODEL: "Model",
     HS_BAD_SLOT: "BadSlot", HS_LENGTH_MISMATCH: "LengthMismatch", HS_TOKEN_RANGE: "TokenOutOfRange",
     HS_INVALID_OVERLAP: "InvalidOverlap", HS_BAD_ARGUMENT: "BadArgument", HS_FORMAT: "Format",
-    HS_CORRUPT: "CorruptBlock", HS_MODEL_MISMATCH: "ModelHashMismatch",
+    HS_CORRUPT: "CorruptBlock", HS_MODEL_MISMATCH: "ModelHashMismatch", HS_IO: "Io",
 }
 
 ENCODE, DECODE = 0, 1
@@ -70,8 +70,16 @@ class FoldOptions(ctypes.Structure):
 class FoldStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in ("original_len", "container_len", "blocks", "coded_blocks",
                                                "zstd_blocks", "tokens")] + \
-               [("block_size", ctypes.c_uint32), ("gpus_failed", ctypes.c_uint32), ("gpu_rows", ctypes.c_uint64)]
+               [("block_size", ctypes.c_uint32), ("gpus_failed", ctypes.c_uint32), ("gpu_rows", ctypes.c_uint64),
+                ("prep_ms", ctypes.c_double), ("gpu_ms", ctypes.c_double), ("finish_ms", ctypes.c_double)]
 
+
+SOURCE_FN = ctypes.CFUNCTYPE(ctypes.c_int64, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint8), ctypes.c_size_t)
+SINK_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint8),
+                           ctypes.c_size_t)
+READ_AT_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint8),
+                              ctypes.c_size_t)
+WRITE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint8), ctypes.c_size_t)
 
 MIXER_FN = ctypes.CFUNCTYPE(ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(MixStats))
 MIX_NONE = 0xFFFFFFFF   # a mixed table without a prediction: the weights max(1, w)
@@ -135,6 +143,12 @@ def lib() -> ctypes.CDLL:
                                 ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(FoldStats)]
     L.hs_unfold.argtypes = [vp, vp, ctypes.c_char_p, ctypes.c_size_t, vp, ctypes.c_size_t,
                             ctypes.POINTER(ctypes.c_size_t)]
+    L.hs_fold_stream.argtypes = [vp, vp, u64, SOURCE_FN, vp, SINK_FN, vp, ctypes.POINTER(FoldOptions),
+                                 ctypes.POINTER(u64), ctypes.POINTER(FoldStats)]
+    L.hs_fold_stream_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, u64, SOURCE_FN, vp,
+                                       SINK_FN, vp, ctypes.POINTER(FoldOptions), ctypes.POINTER(u64),
+                                       ctypes.POINTER(FoldStats)]
+    L.hs_unfold_stream.argtypes = [vp, vp, u64, READ_AT_FN, vp, WRITE_FN, vp, ctypes.POINTER(u64)]
     L.hs_zstd_version.argtypes = []
     L.hs_zstd_version.restype = u32
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
@@ -225,6 +239,83 @@ def fold_multi(ordinals, model_file: bytes, tokenizer, data: bytes, block_size: 
                                len(data), ctypes.byref(opt), _p(out), out.size, ctypes.byref(n), ctypes.byref(st)))
     stats = {name: getattr(st, name) for name, _ in FoldStats._fields_}
     return out[:n.value].tobytes(), stats
+
+
+def _stream_callbacks(read, write):
+    """ctypes callbacks over Python file-like callables: read(n) -> bytes (the source),
+    write(at, data) (the seekable sink). An exception in either fails the call with HS_IO."""
+
+    def source(_user, buf, cap):
+        try:
+            data = read(cap)
+        except Exception:  # noqa: BLE001 - any failure of the caller's source is an I/O error
+            return -1
+        ctypes.memmove(buf, data, len(data))
+        return len(data)
+
+    def sink(_user, at, buf, n):
+        try:
+            write(at, ctypes.string_at(buf, n))
+        except Exception:  # noqa: BLE001
+            return 1
+        return 0
+
+    return SOURCE_FN(source), SINK_FN(sink)
+
+
+def fold_stream(batch, tokenizer, length: int, read, write, block_size: int = 0, overlap: int = 0,
+                spread: bool = False, threads: int = 0):
+    """hs_fold_stream: the fold of the `length` bytes that read(n) gives, into the seekable sink
+    write(at, data); returns (container length, stats)."""
+    opt = FoldOptions(block_size, overlap, int(spread), threads)
+    src, snk = _stream_callbacks(read, write)
+    n = ctypes.c_uint64()
+    st = FoldStats()
+    _check(lib().hs_fold_stream(batch.h, tokenizer.h, length, src, None, snk, None, ctypes.byref(opt), ctypes.byref(n),
+                                ctypes.byref(st)))
+    return n.value, {name: getattr(st, name) for name, _ in FoldStats._fields_}
+
+
+def fold_stream_multi(ordinals, model_file: bytes, tokenizer, length: int, read, write, block_size: int = 0,
+                      overlap: int = 0, slots: int = 256, max_rows: int = 16384, spread: bool = False,
+                      threads: int = 0):
+    """hs_fold_stream_multi: fold_stream on the GPUs `ordinals`, one host thread each."""
+    ords = np.ascontiguousarray(ordinals, dtype=np.int32)
+    opt = FoldOptions(block_size, overlap, int(spread), threads)
+    src, snk = _stream_callbacks(read, write)
+    n = ctypes.c_uint64()
+    st = FoldStats()
+    _check(lib().hs_fold_stream_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows, tokenizer.h,
+                                      length, src, None, snk, None, ctypes.byref(opt), ctypes.byref(n),
+                                      ctypes.byref(st)))
+    return n.value, {name: getattr(st, name) for name, _ in FoldStats._fields_}
+
+
+def unfold_stream(batch, tokenizer, length: int, read_at, write) -> int:
+    """hs_unfold_stream: the unfold of the `length`-byte container that read_at(at, n) -> bytes
+    reads, into write(data); returns the original length."""
+
+    def ra(_user, at, buf, n):
+        try:
+            data = read_at(at, n)
+        except Exception:  # noqa: BLE001
+            return 1
+        if len(data) != n:
+            return 1
+        ctypes.memmove(buf, data, n)
+        return 0
+
+    def wr(_user, buf, n):
+        try:
+            write(ctypes.string_at(buf, n))
+        except Exception:  # noqa: BLE001
+            return 1
+        return 0
+
+    cb_ra, cb_wr = READ_AT_FN(ra), WRITE_FN(wr)
+    n = ctypes.c_uint64()
+    _check(lib().hs_unfold_stream(batch.h, tokenizer.h, length, cb_ra, None, cb_wr, None, ctypes.byref(n)))
+    return n.value
 
 
 def unfold(batch, tokenizer, container: bytes, original_len: int | None = None) -> bytes:

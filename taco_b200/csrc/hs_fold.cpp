@@ -20,7 +20,9 @@
 
 #include <algorithm>
 #include <functional>
+#include <memory>
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <mutex>
 #include <cstdint>
@@ -412,14 +414,275 @@ int run_windows(hs_batch* batch, uint32_t eot, size_t K, WindowFeed& feed, const
     }
 }
 
-// The GPU stage of a fold: runs windows from the feed until it is empty.
-using GpuStage = std::function<int(WindowFeed&, const std::vector<FoldBlock>&)>;
+// ---- the GPU side of a fold: the caller's batch, or one host thread per GPU ----
 
-// The fold of fold_with (steps 1, 2, 4, 5 and the container) around a GPU stage, for a model
-// with this hash, EOT token and context length.
-int fold_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, const GpuStage& gpu,
-              const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt, uint8_t* out,
-              size_t cap, size_t* out_len, hs_fold_stats* stats) {
+class GpuRunner {
+  public:
+    virtual ~GpuRunner() = default;
+    // Runs the windows of the feed until it is empty (every window taken has completed).
+    virtual int run(WindowFeed& feed, const std::vector<FoldBlock>& blocks) = 0;
+};
+
+// The batch of hs_fold, on the caller's thread (its device handle belongs to that thread).
+class OneGpu : public GpuRunner {
+  public:
+    OneGpu(hs_batch* batch, uint32_t eot, size_t K) : batch_(batch), eot_(eot), K_(K) {}
+    int run(WindowFeed& feed, const std::vector<FoldBlock>& blocks) override {
+        return run_windows(batch_, eot_, K_, feed, blocks);
+    }
+
+  private:
+    hs_batch* batch_;
+    uint32_t eot_;
+    size_t K_;
+};
+
+// hs_fold_multi: one host thread per GPU for the whole fold (crates/taco/src/gpu_fold.rs:128-186).
+// Each thread opens its device (a device handle belongs to its thread), loads the model and makes
+// its batch once; then it runs the windows of each segment's feed with the others, all taking
+// rounds from the one feed, so a faster GPU takes more. A GPU that cannot be opened, load the
+// model or hold the batch gives its share to the others, as the reference's backend choice falls
+// back from a device that fails (crates/taco/src/backend.rs:288-342). An error while windows run
+// fails the fold (the windows it had taken never complete). A thread's error message is
+// thread-local; it comes back with its status.
+class MultiGpu : public GpuRunner {
+  public:
+    struct Config {
+        const int* ordinals;
+        uint32_t n;
+        const uint8_t* model_file;
+        size_t model_len;
+        const uint8_t* hash;
+        uint32_t vocab, eot, n_ctx, slots, max_rows;
+        size_t K;
+    };
+
+    explicit MultiGpu(const Config& c) : c_(c), rcs_(c.n, HS_OK), msgs_(c.n), live_(c.n, 0) {}
+
+    ~MultiGpu() override {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            quit_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : threads_) t.join();
+    }
+
+    // Starts the threads and waits until every GPU tried to open. HS_OK if one or more did.
+    int start() {
+        for (uint32_t g = 0; g < c_.n; g++) threads_.emplace_back([this, g] { worker(g); });
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return tried_ == c_.n; });
+        uint32_t ok = 0;
+        for (uint32_t g = 0; g < c_.n; g++) ok += live_[g];
+        failed_ = c_.n - ok;
+        if (ok == 0)
+            return hs::host_fail(rcs_[0], "no GPU of the fold opened; GPU " + std::to_string(c_.ordinals[0]) + ": " +
+                                              msgs_[0]);
+        return HS_OK;
+    }
+
+    uint32_t failed() const { return failed_; }
+
+    int run(WindowFeed& feed, const std::vector<FoldBlock>& blocks) override {
+        std::unique_lock<std::mutex> lk(mu_);
+        feed_ = &feed;
+        blocks_ = &blocks;
+        busy_ = c_.n - failed_;
+        gen_++;
+        cv_.notify_all();
+        cv_.wait(lk, [&] { return busy_ == 0; });
+        for (uint32_t g = 0; g < c_.n; g++)
+            if (live_[g] && rcs_[g])
+                return hs::host_fail(rcs_[g], "GPU " + std::to_string(c_.ordinals[g]) + ": " + msgs_[g]);
+        return HS_OK;
+    }
+
+  private:
+    void note(uint32_t g, int rc) {  // under mu_
+        char buf[1024];
+        hs_last_error(buf, sizeof buf);
+        msgs_[g] = buf;
+        rcs_[g] = rc;
+    }
+
+    void worker(uint32_t g) {
+        hs_dev* dev = nullptr;
+        hs_model* model = nullptr;
+        hs_batch* batch = nullptr;
+        int rc = hs_open(c_.ordinals[g], &dev);
+        if (!rc) rc = hs_model_load(dev, c_.model_file, c_.model_len, &model);
+        hs_model_info mi;
+        if (!rc && !(rc = hs_model_get_info(model, &mi))) {
+            if (memcmp(mi.hash, c_.hash, 32) != 0 || mi.n_ctx != c_.n_ctx || mi.eot_token != c_.eot ||
+                mi.vocab != c_.vocab)
+                rc = hs::host_fail(HS_MODEL, "the loaded model is not the model file");
+        }
+        if (!rc) rc = hs_batch_new(model, c_.slots, c_.max_rows, &batch);
+        if (!rc) rc = hs_batch_set_overlap(batch, (uint16_t)c_.K);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            if (rc) note(g, rc);
+            live_[g] = rc == HS_OK;
+            tried_++;
+        }
+        cv_.notify_all();
+        uint64_t seen = 0;
+        while (!rc) {
+            WindowFeed* feed;
+            const std::vector<FoldBlock>* blocks;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return quit_ || gen_ != seen; });
+                if (quit_) break;
+                seen = gen_;
+                feed = feed_;
+                blocks = blocks_;
+            }
+            const int r = run_windows(batch, c_.eot, c_.K, *feed, *blocks);
+            {
+                std::lock_guard<std::mutex> lk(mu_);
+                if (r) note(g, r);
+                busy_--;
+            }
+            cv_.notify_all();
+            rc = r;
+        }
+        if (batch) hs_batch_free(batch);
+        if (model) hs_model_free(model);
+        if (dev) hs_dev_free(dev);
+    }
+
+    Config c_;
+    std::vector<int> rcs_;
+    std::vector<std::string> msgs_;
+    std::vector<char> live_;
+    std::vector<std::thread> threads_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    uint32_t tried_ = 0, failed_ = 0, busy_ = 0;
+    uint64_t gen_ = 0;
+    bool quit_ = false;
+    WindowFeed* feed_ = nullptr;
+    const std::vector<FoldBlock>* blocks_ = nullptr;
+};
+
+// ---- the input and the output of a fold ----
+
+// The input bytes in order: read() gives up to cap bytes, 0 only at the end, < 0 on an error.
+struct Source {
+    virtual ~Source() = default;
+    virtual int64_t read(uint8_t* buf, size_t cap) = 0;
+};
+
+// A seekable output: write() puts n bytes at offset `at`; 0, or non-zero on an error.
+struct Sink {
+    virtual ~Sink() = default;
+    virtual int write(uint64_t at, const uint8_t* p, size_t n) = 0;
+};
+
+struct MemSource : Source {
+    const uint8_t* p;
+    size_t left;
+    MemSource(const uint8_t* d, size_t n) : p(d), left(n) {}
+    int64_t read(uint8_t* buf, size_t cap) override {
+        const size_t n = std::min(cap, left);
+        if (n) memcpy(buf, p, n);
+        p += n;
+        left -= n;
+        return (int64_t)n;
+    }
+};
+
+// The caller's buffer; writes past its end are dropped and remembered (the caller gets the
+// length it needs).
+struct MemSink : Sink {
+    uint8_t* out;
+    size_t cap;
+    bool overflow = false;
+    MemSink(uint8_t* o, size_t c) : out(o), cap(c) {}
+    int write(uint64_t at, const uint8_t* p, size_t n) override {
+        if (!out || at > cap || n > cap - at) overflow = true;
+        else if (n) memcpy(out + at, p, n);
+        return 0;
+    }
+};
+
+struct CallbackSource : Source {
+    hs_source_fn fn;
+    void* user;
+    int64_t read(uint8_t* buf, size_t cap) override { return fn(user, buf, cap); }
+    CallbackSource(hs_source_fn f, void* u) : fn(f), user(u) {}
+};
+
+struct CallbackSink : Sink {
+    hs_sink_fn fn;
+    void* user;
+    int write(uint64_t at, const uint8_t* p, size_t n) override { return fn(user, at, p, n); }
+    CallbackSink(hs_sink_fn f, void* u) : fn(f), user(u) {}
+};
+
+// The blocks of one segment and their input bytes. A fold holds two segments at a time: the
+// one on the GPUs and the next one, which the host threads tokenize and compress meanwhile.
+struct Segment {
+    uint64_t first = 0;  // index of the segment's first block
+    std::vector<uint8_t> data;
+    std::vector<FoldBlock> blocks;  // off is relative to data
+    int rc = HS_OK;
+    std::string msg;
+    double ms = 0;
+};
+
+// The largest input of one segment, and its most blocks (crates/taco/src/stream.rs:56-63 has 64
+// MiB and 256 blocks). The bytes do not depend on the segment size (stream.rs:19-20). Here a
+// segment holds up to 4,096 blocks, so that 8 GPUs of 512 slots have windows enough to fill their
+// passes; the memory stays bounded by the 64 MiB of input per segment (its tokens, zstd frames
+// and payloads), two segments at a time.
+constexpr uint64_t SEGMENT_BYTES = 64ull << 20;
+constexpr uint64_t SEGMENT_BLOCKS = 4096;
+
+double ms_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// Tokens and zstd frames of a segment's blocks on the host threads.
+void prep_segment(Segment& seg, const hs_tokenizer* tok, unsigned threads) {
+    const auto t0 = std::chrono::steady_clock::now();
+    std::atomic<int64_t> bad_tokens{-1}, bad_zstd{-1};
+    parallel_for(seg.blocks.size(), threads, [&](size_t i) {
+        FoldBlock& b = seg.blocks[i];
+        const uint8_t* in = seg.data.data() + b.off;
+        hs::tokenize(tok, in, b.len, b.tokens);
+        if (!hs::tokens_restore(tok, b.tokens.data(), b.tokens.size(), in, b.len)) bad_tokens = (int64_t)i;
+        b.zstd_ok = compress_zstd(in, b.len, b.zstd);
+        if (!b.zstd_ok) bad_zstd = (int64_t)i;
+    });
+    if (bad_tokens >= 0) {
+        seg.rc = HS_MODEL;
+        seg.msg = "the tokens of block " + std::to_string(seg.first + bad_tokens.load()) +
+                  " do not give its bytes back (TokenizerRoundTrip)";
+    } else if (bad_zstd >= 0) {
+        seg.rc = HS_CUDA;
+        seg.msg = "zstd failed on block " + std::to_string(seg.first + bad_zstd.load());
+    }
+    seg.ms = ms_since(t0);
+}
+
+struct FoldStatsAcc {
+    uint64_t tokens = 0, coded = 0, zstd = 0, rows = 0;
+    double prep_ms = 0, gpu_ms = 0, finish_ms = 0;
+};
+
+// The fold of fold_with, segment by segment (crates/taco/src/fold.rs code_segment over the
+// segments of stream.rs StreamFold::to_seekable): the block table and the stored blocks go to the
+// sink as each segment ends, the header (with the input's SHA-256) last. Per segment:
+// 2. tokens and zstd frames on the host threads (for the next segment while the GPUs run this one);
+// 3. the context windows on the GPUs, each block's range encoder taking its intervals as they
+//    complete (WindowFeed);
+// 4.-5. each block's payload if its encoder did not stop, and its smallest stored form.
+int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, GpuRunner& gpu,
+                     const hs_tokenizer* tok, Source& src, uint64_t len, Sink& sink, const hs_fold_options* opt,
+                     uint64_t* out_len, hs_fold_stats* stats) {
     if (!zstd().ok) return hs::host_fail(HS_UNSUPPORTED, "the zstd library (libzstd.so.1) is not available");
     // FoldOptions::block_size_for (fold.rs:159-170): a set size, or 16 KiB; with `spread`, the
     // power of two that makes about 64 blocks, within 4 KiB .. 16 KiB.
@@ -430,120 +693,163 @@ int fold_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, const 
         bs = std::min<uint64_t>(std::max<uint64_t>(p2, SPREAD_MIN_BLOCK), DEFAULT_BLOCK_SIZE);
     }
     if (bs == 0 || bs > MAX_BLOCK_SIZE) return hs::host_fail(HS_UNSUPPORTED, "the block size is out of range");
-    const size_t nblocks = (size_t)((len + bs - 1) / bs);
+    const uint64_t nblocks = (len + bs - 1) / bs;
     if (nblocks > 0xFFFFFFFFull) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
-    const uint64_t need = HEADER_LEN + 5 * (uint64_t)nblocks + len;
     const unsigned threads = opt->threads ? opt->threads : std::max(1u, std::thread::hardware_concurrency());
-    std::vector<FoldBlock> blocks(nblocks);
-    for (size_t i = 0; i < nblocks; i++) {
-        blocks[i].off = i * bs;
-        blocks[i].len = std::min<size_t>(bs, len - i * bs);
-    }
-    int rc;
-    // 2. Tokens and zstd frames on the host threads.
-    std::atomic<int> bad_tokens{-1}, bad_zstd{-1};
-    parallel_for(nblocks, threads, [&](size_t i) {
-        FoldBlock& b = blocks[i];
-        hs::tokenize(tok, input + b.off, b.len, b.tokens);
-        if (!hs::tokens_restore(tok, b.tokens.data(), b.tokens.size(), input + b.off, b.len)) bad_tokens = (int)i;
-        b.zstd_ok = compress_zstd(input + b.off, b.len, b.zstd);
-        if (!b.zstd_ok) bad_zstd = (int)i;
-    });
-    if (bad_tokens >= 0)
-        return hs::host_fail(HS_MODEL, "the tokens of block " + std::to_string(bad_tokens.load()) +
-                                           " do not give its bytes back (TokenizerRoundTrip)");
-    if (bad_zstd >= 0) return hs::host_fail(HS_CUDA, "zstd failed on block " + std::to_string(bad_zstd.load()));
-    // 3. The intervals on the GPU, coded as they come. A block's inputs are x_0 = EOT,
-    // x_j = t_(j-1) (input j codes t_j). In one slot its context restarts after every n_ctx
-    // positions with EOT and the last K inputs (crates/hardshell/src/gpt2/context.rs), so the
-    // block divides into context windows: window 0 is inputs 0 .. n_ctx - 1, each later window the
-    // next n_ctx - K - 1 inputs (gpu_fold.rs windows_of). Each window runs in a fresh slot of its
-    // own (run_windows), so the windows of all blocks run side by side in full passes. A block
-    // whose payload prefix already reaches its bound needs none (BlockEncoder::stopped).
     const size_t K = std::min<size_t>(opt->overlap, n_ctx - 2);
-    std::vector<Window> windows;
-    for (size_t i = 0; i < nblocks; i++) {
-        FoldBlock& b = blocks[i];
-        if (b.tokens.empty() || varint_len(b.tokens.size()) >= std::min(b.len, b.zstd.size())) continue;
-        for (size_t s0 = 0; s0 < b.tokens.size();) {
-            const size_t c = std::min(b.tokens.size() - s0, s0 == 0 ? (size_t)n_ctx : n_ctx - K - 1);
-            windows.push_back({i, s0, c});
-            s0 += c;
+    const uint64_t seg_blocks = std::min<uint64_t>(std::max<uint64_t>(SEGMENT_BYTES / bs, 1), SEGMENT_BLOCKS);
+    const uint64_t data_off = HEADER_LEN + 5 * nblocks;
+    hs::Sha256 sum;
+    FoldStatsAcc acc;
+    uint64_t write_at = data_off;
+    int rc;
+    auto io = [](const std::string& what) { return hs::host_fail(HS_IO, what); };
+    // Reads the input bytes of the segment that starts at block `first`.
+    auto read_segment = [&](uint64_t first, Segment& seg) -> int {
+        seg.first = first;
+        const uint64_t nb = std::min(seg_blocks, nblocks - first);
+        const uint64_t off = first * bs, n = std::min<uint64_t>(nb * bs, len - off);
+        seg.data.resize((size_t)n);
+        for (uint64_t got = 0; got < n;) {
+            const int64_t r = src.read(seg.data.data() + got, (size_t)(n - got));
+            if (r < 0) return io("the input source failed");
+            if (r == 0) return io("the input is shorter than its length");
+            got += (uint64_t)r;
+        }
+        sum.update(seg.data.data(), (size_t)n);
+        seg.blocks.assign((size_t)nb, FoldBlock());
+        for (uint64_t i = 0; i < nb; i++) {
+            seg.blocks[i].off = (size_t)(i * bs);
+            seg.blocks[i].len = (size_t)std::min<uint64_t>(bs, n - i * bs);
+        }
+        seg.rc = HS_OK;
+        seg.msg.clear();
+        return HS_OK;
+    };
+    auto cur = std::make_unique<Segment>(), next = std::make_unique<Segment>();
+    if (nblocks) {
+        if ((rc = read_segment(0, *cur))) return rc;
+        prep_segment(*cur, tok, threads);
+        acc.prep_ms += cur->ms;
+    }
+    std::vector<uint8_t> table;
+    for (uint64_t first = 0; first < nblocks; first += seg_blocks) {
+        if (cur->rc) return hs::host_fail(cur->rc, cur->msg);
+        // The next segment: read here (the source is called on the caller's thread only), then
+        // tokenized and compressed on the host threads while the GPUs run this one.
+        std::thread helper;
+        const bool more = first + seg_blocks < nblocks;
+        if (more) {
+            if ((rc = read_segment(first + seg_blocks, *next))) return rc;
+            helper = std::thread([&] { prep_segment(*next, tok, threads); });
+        }
+        struct Join {
+            std::thread& t;
+            ~Join() {
+                if (t.joinable()) t.join();
+            }
+        } join{helper};
+        // 3. The windows (gpu_fold.rs windows_of). A block's inputs are x_0 = EOT, x_j = t_(j-1)
+        // (input j codes t_j). In one slot its context restarts after every n_ctx positions with
+        // EOT and the last K inputs (crates/hardshell/src/gpt2/context.rs), so the block divides
+        // into context windows: window 0 is inputs 0 .. n_ctx - 1, each later window the next
+        // n_ctx - K - 1 inputs. Each window runs in a fresh slot of its own (run_windows), so the
+        // windows of all blocks run side by side in full passes. A block whose payload prefix
+        // already reaches its bound needs none (BlockEncoder::stopped).
+        std::vector<FoldBlock>& blocks = cur->blocks;
+        std::vector<Window> windows;
+        for (size_t i = 0; i < blocks.size(); i++) {
+            const FoldBlock& b = blocks[i];
+            if (b.tokens.empty() || varint_len(b.tokens.size()) >= std::min(b.len, b.zstd.size())) continue;
+            for (size_t s0 = 0; s0 < b.tokens.size();) {
+                const size_t c = std::min(b.tokens.size() - s0, s0 == 0 ? (size_t)n_ctx : n_ctx - K - 1);
+                windows.push_back({i, s0, c});
+                s0 += c;
+            }
+        }
+        WindowFeed feed(std::move(windows), blocks, blocks.size());
+        feed.order_by_waves();
+        auto t0 = std::chrono::steady_clock::now();
+        if (!feed.windows().empty() && (rc = gpu.run(feed, blocks))) return rc;
+        acc.gpu_ms += ms_since(t0);
+        // 4.-5. The payloads of the blocks whose encoders did not stop, then the smallest form.
+        t0 = std::chrono::steady_clock::now();
+        parallel_for(blocks.size(), threads, [&](size_t i) {
+            FoldBlock& b = blocks[i];
+            std::vector<uint8_t> coded;
+            const bool live = feed.finish(i, coded);
+            size_t best = b.len;
+            if (b.zstd.size() < best) {
+                best = b.zstd.size();
+                b.kind = KIND_ZSTD;
+                b.stored = std::move(b.zstd);
+            }
+            if (live && coded.size() < best) {
+                b.kind = KIND_CODED;
+                b.stored = std::move(coded);
+            }
+        });
+        acc.rows += feed.rows_run();
+        // The segment's table entries and stored blocks (writer.rs:245-300).
+        table.clear();
+        for (const FoldBlock& b : blocks) {
+            const uint32_t sl = (uint32_t)(b.kind == KIND_RAW ? b.len : b.stored.size());
+            table.push_back(b.kind);
+            for (int k = 0; k < 4; k++) table.push_back((uint8_t)(sl >> (8 * k)));
+            if (sink.write(write_at, b.kind == KIND_RAW ? cur->data.data() + b.off : b.stored.data(), sl))
+                return io("the output sink failed");
+            write_at += sl;
+            acc.tokens += b.tokens.size();
+            acc.coded += b.kind == KIND_CODED;
+            acc.zstd += b.kind == KIND_ZSTD;
+        }
+        if (sink.write(HEADER_LEN + 5 * first, table.data(), table.size())) return io("the output sink failed");
+        acc.finish_ms += ms_since(t0);
+        if (more) {
+            helper.join();
+            acc.prep_ms += next->ms;
+            std::swap(cur, next);
         }
     }
-    WindowFeed feed(std::move(windows), blocks, nblocks);
-    feed.order_by_waves();
-    if (!feed.windows().empty() && (rc = gpu(feed, blocks))) return rc;
-    // 4.-5. The payloads of the blocks whose encoders did not stop, then the smallest form.
-    parallel_for(nblocks, threads, [&](size_t i) {
-        FoldBlock& b = blocks[i];
-        std::vector<uint8_t> coded;
-        const bool live = feed.finish(i, coded);
-        size_t best = b.len;
-        if (b.zstd.size() < best) {
-            best = b.zstd.size();
-            b.kind = KIND_ZSTD;
-            b.stored = std::move(b.zstd);
-        }
-        if (live && coded.size() < best) {
-            b.kind = KIND_CODED;
-            b.stored = std::move(coded);
-        }
-    });
-    // The container (writer.rs:245-300; the header of header.rs, version 2, profile text).
-    uint64_t total = HEADER_LEN + 5 * (uint64_t)nblocks;
-    for (const FoldBlock& b : blocks) total += b.kind == KIND_RAW ? b.len : b.stored.size();
-    *out_len = (size_t)total;
+    {
+        uint8_t extra;
+        const int64_t r = src.read(&extra, 1);
+        if (r < 0) return io("the input source failed");
+        if (r > 0) return io("the input is longer than its length");
+    }
+    // The header (header.rs, version 2, profile text).
+    uint8_t h[HEADER_LEN] = {0};
+    auto put16 = [&](size_t o, uint16_t v) { memcpy(h + o, &v, 2); };
+    auto put32 = [&](size_t o, uint32_t v) { memcpy(h + o, &v, 4); };
+    auto put64 = [&](size_t o, uint64_t v) { memcpy(h + o, &v, 8); };
+    memcpy(h, "TACO", 4);
+    put16(4, 2);  // version
+    put16(6, 0);  // flags
+    memcpy(h + 8, model_hash, 32);
+    put64(40, len);
+    sum.final(h + 48);
+    put32(80, (uint32_t)bs);
+    put32(84, (uint32_t)nblocks);
+    const uint16_t k = (uint16_t)opt->overlap;
+    h[88] = 0;                 // profile text
+    h[89] = 0;                 // reserved
+    put16(90, k ? 2 : 0);      // coding parts: bit 1 = the overlap
+    memcpy(h + 92 + 2, &k, 2);  // coding parameters: the overlap
+    if (sink.write(0, h, HEADER_LEN)) return io("the output sink failed");
+    *out_len = write_at;
     if (stats) {
         memset(stats, 0, sizeof(*stats));
         stats->original_len = len;
-        stats->container_len = total;
+        stats->container_len = write_at;
         stats->blocks = nblocks;
         stats->block_size = (uint32_t)bs;
-        for (const FoldBlock& b : blocks) {
-            stats->tokens += b.tokens.size();
-            stats->coded_blocks += b.kind == KIND_CODED;
-            stats->zstd_blocks += b.kind == KIND_ZSTD;
-        }
-        stats->gpu_rows = feed.rows_run();
-    }
-    if (cap < total || !out)
-        return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
-                                                  std::to_string(total) + " needed (hs_fold_bound: " +
-                                                  std::to_string(need) + ")");
-    uint8_t* p = out;
-    auto put = [&](const void* src, size_t n) {
-        memcpy(p, src, n);
-        p += n;
-    };
-    auto put16 = [&](uint16_t v) { put(&v, 2); };
-    auto put32 = [&](uint32_t v) { put(&v, 4); };
-    auto put64 = [&](uint64_t v) { put(&v, 8); };
-    put("TACO", 4);
-    put16(2);  // version
-    put16(0);  // flags
-    put(model_hash, 32);
-    put64(len);
-    uint8_t sum[32];
-    hs::sha256(input, len, sum);
-    put(sum, 32);
-    put32((uint32_t)bs);
-    put32((uint32_t)nblocks);
-    const uint16_t k = (uint16_t)opt->overlap;
-    const uint8_t profile = 0, reserved = 0;
-    put(&profile, 1);
-    put(&reserved, 1);
-    put16(k ? 2 : 0);  // coding parts: bit 1 = the overlap
-    uint8_t params[12] = {0};
-    memcpy(params + 2, &k, 2);
-    put(params, 12);
-    for (const FoldBlock& b : blocks) {
-        put(&b.kind, 1);
-        put32((uint32_t)(b.kind == KIND_RAW ? b.len : b.stored.size()));
-    }
-    for (const FoldBlock& b : blocks) {
-        if (b.kind == KIND_RAW) put(input + b.off, b.len);
-        else put(b.stored.data(), b.stored.size());
+        stats->tokens = acc.tokens;
+        stats->coded_blocks = acc.coded;
+        stats->zstd_blocks = acc.zstd;
+        stats->gpu_rows = acc.rows;
+        stats->prep_ms = acc.prep_ms;
+        stats->gpu_ms = acc.gpu_ms;
+        stats->finish_ms = acc.finish_ms;
     }
     return HS_OK;
 }
@@ -558,30 +864,22 @@ int check_tokenizer(const hs_tokenizer* tok, uint32_t vocab) {
     return HS_OK;
 }
 
-}  // namespace
-
-extern "C" {
-
-int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt,
-            uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
-    if (!batch || !tok || !opt || !out_len || (len && !input)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+// The one-GPU fold of a batch (hs_fold, hs_fold_stream).
+int fold_one(hs_batch* batch, const hs_tokenizer* tok, Source& src, uint64_t len, Sink& sink,
+             const hs_fold_options* opt, uint64_t* out_len, hs_fold_stats* stats) {
     hs_model_info info;
     int rc = hs_model_get_info(hs::batch_model(batch), &info);
     if (rc || (rc = check_tokenizer(tok, info.vocab))) return rc;
     if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
     if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
-    const size_t K = std::min<size_t>(opt->overlap, info.n_ctx - 2);
-    GpuStage gpu = [&](WindowFeed& feed, const std::vector<FoldBlock>& blocks) {
-        return run_windows(batch, info.eot_token, K, feed, blocks);
-    };
-    return fold_impl(info.hash, info.eot_token, info.n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
+    OneGpu gpu(batch, info.eot_token, std::min<size_t>(opt->overlap, info.n_ctx - 2));
+    return fold_stream_impl(info.hash, info.eot_token, info.n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
 }
 
-int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
-                  uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, const uint8_t* input, size_t len,
-                  const hs_fold_options* opt, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
-    if (!ordinals || !n_gpus || !model_file || !tok || !opt || !out_len || (len && !input))
-        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+// The fold on several GPUs (hs_fold_multi, hs_fold_stream_multi).
+int fold_many(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len, uint32_t slots,
+              uint32_t max_rows, const hs_tokenizer* tok, Source& src, uint64_t len, Sink& sink,
+              const hs_fold_options* opt, uint64_t* out_len, hs_fold_stats* stats) {
     // The windows are cut with the model's context length and EOT token, as hs_fold cuts them
     // with those of its batch's model (gpu_fold.rs windows_of, Window::rows); the tokenizer only
     // has to share the model's vocabulary (FoldPlan::new, fold.rs:388-395).
@@ -591,264 +889,380 @@ int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_fil
         if (!hs::model_file_info(model_file, model_len, &vocab, &eot, &n_ctx, err))
             return hs::host_fail(HS_MODEL, "the model file is not valid: " + err);
     }
-    int rc0 = check_tokenizer(tok, vocab);
-    if (rc0) return rc0;
+    int rc = check_tokenizer(tok, vocab);
+    if (rc) return rc;
     if (opt->overlap > 0xFFFF || opt->overlap > n_ctx - 2)
         return hs::host_fail(HS_INVALID_OVERLAP, "the overlap must be at most n_ctx - 2");
     uint8_t hash[32];
     hs::sha256(model_file, model_len, hash);  // the model hash of the container (model.rs:359)
-    const size_t K = opt->overlap;
-    uint32_t gpus_failed = 0;
-    // One host thread per GPU: it opens the device (a device handle belongs to its thread), loads
-    // the model and makes its batch (crates/taco/src/gpu_fold.rs:128-186). When every thread has
-    // tried, the windows go to the GPUs that opened: a GPU that cannot be
-    // opened, load the model or hold the batch gives its share to the others, as the reference's
-    // backend choice falls back from a device that fails to open (crates/taco/src/backend.rs:
-    // 288-342). The GPUs take their rounds of windows from one shared feed, so a faster GPU takes
-    // more. An error while windows run fails the fold. A thread's error message is thread-local;
-    // it comes back with its status.
-    GpuStage gpu = [&](WindowFeed& feed, const std::vector<FoldBlock>& blocks) {
-        std::vector<int> rcs(n_gpus, HS_OK);
-        std::vector<std::string> msgs(n_gpus);
-        std::vector<uint32_t> live;
-        std::mutex mu;
-        std::condition_variable cv;
-        uint32_t tried = 0;
-        bool go = false;
-        auto note = [&](uint32_t g, int rc) {
-            char buf[1024];
-            hs_last_error(buf, sizeof buf);
-            msgs[g] = buf;
-            rcs[g] = rc;
-        };
-        auto worker = [&](uint32_t g) {
-            hs_dev* dev = nullptr;
-            hs_model* model = nullptr;
-            hs_batch* batch = nullptr;
-            int rc = hs_open(ordinals[g], &dev);
-            if (!rc) rc = hs_model_load(dev, model_file, model_len, &model);
-            hs_model_info mi;
-            if (!rc && !(rc = hs_model_get_info(model, &mi))) {
-                if (memcmp(mi.hash, hash, 32) != 0 || mi.n_ctx != n_ctx || mi.eot_token != eot || mi.vocab != vocab)
-                    rc = hs::host_fail(HS_MODEL, "the loaded model is not the model file");
-            }
-            if (!rc) rc = hs_batch_new(model, slots, max_rows, &batch);
-            if (!rc) rc = hs_batch_set_overlap(batch, (uint16_t)K);
-            {
-                std::unique_lock<std::mutex> lk(mu);
-                if (rc) note(g, rc);
-                tried++;
-                cv.notify_all();
-                cv.wait(lk, [&] { return go; });
-            }
-            if (!rc) {
-                rc = run_windows(batch, eot, K, feed, blocks);
-                if (rc) note(g, rc);
-            }
-            if (batch) hs_batch_free(batch);
-            if (model) hs_model_free(model);
-            if (dev) hs_dev_free(dev);
-        };
-        std::vector<std::thread> pool;
-        for (uint32_t g = 0; g < n_gpus; g++) pool.emplace_back(worker, g);
-        {
-            std::unique_lock<std::mutex> lk(mu);
-            cv.wait(lk, [&] { return tried == n_gpus; });
-            for (uint32_t g = 0; g < n_gpus; g++)
-                if (rcs[g] == HS_OK) live.push_back(g);
-            gpus_failed = n_gpus - (uint32_t)live.size();
-            go = true;
-            cv.notify_all();
-        }
-        for (auto& t : pool) t.join();
-        if (live.empty()) return hs::host_fail(rcs[0], "no GPU of the fold opened; GPU " + std::to_string(ordinals[0]) +
-                                                           ": " + msgs[0]);
-        for (uint32_t g : live)
-            if (rcs[g]) return hs::host_fail(rcs[g], "GPU " + std::to_string(ordinals[g]) + ": " + msgs[g]);
-        return (int)HS_OK;
-    };
-    const int rc = fold_impl(hash, eot, n_ctx, gpu, tok, input, len, opt, out, cap, out_len, stats);
-    if (!rc && stats) stats->gpus_failed = gpus_failed;
+    MultiGpu gpu({ordinals, n_gpus, model_file, model_len, hash, vocab, eot, n_ctx, slots, max_rows, opt->overlap});
+    if ((rc = gpu.start())) return rc;
+    rc = fold_stream_impl(hash, eot, n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
+    if (!rc && stats) stats->gpus_failed = gpu.failed();
     return rc;
+}
+
+int mem_result(const MemSink& sink, uint64_t total, size_t cap, size_t* out_len) {
+    *out_len = (size_t)total;
+    if (sink.overflow)
+        return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
+                                                  std::to_string(total) + " needed (hs_fold_bound)");
+    return HS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hs_fold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* input, size_t len, const hs_fold_options* opt,
+            uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
+    if (!batch || !tok || !opt || !out_len || (len && !input)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    MemSource src(input, len);
+    MemSink sink(out, cap);
+    uint64_t total = 0;
+    const int rc = fold_one(batch, tok, src, len, sink, opt, &total, stats);
+    return rc ? rc : mem_result(sink, total, cap, out_len);
+}
+
+int hs_fold_stream(hs_batch* batch, const hs_tokenizer* tok, uint64_t len, hs_source_fn source, void* source_user,
+                   hs_sink_fn sink, void* sink_user, const hs_fold_options* opt, uint64_t* out_len,
+                   hs_fold_stats* stats) {
+    if (!batch || !tok || !opt || !out_len || !source || !sink) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    CallbackSource src(source, source_user);
+    CallbackSink snk(sink, sink_user);
+    return fold_one(batch, tok, src, len, snk, opt, out_len, stats);
+}
+
+int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                  uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, const uint8_t* input, size_t len,
+                  const hs_fold_options* opt, uint8_t* out, size_t cap, size_t* out_len, hs_fold_stats* stats) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !opt || !out_len || (len && !input))
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    MemSource src(input, len);
+    MemSink sink(out, cap);
+    uint64_t total = 0;
+    const int rc =
+        fold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, src, len, sink, opt, &total, stats);
+    return rc ? rc : mem_result(sink, total, cap, out_len);
+}
+
+int hs_fold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                         uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, uint64_t len,
+                         hs_source_fn source, void* source_user, hs_sink_fn sink, void* sink_user,
+                         const hs_fold_options* opt, uint64_t* out_len, hs_fold_stats* stats) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !opt || !out_len || !source || !sink)
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    CallbackSource src(source, source_user);
+    CallbackSink snk(sink, sink_user);
+    return fold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, src, len, snk, opt, out_len,
+                     stats);
 }
 
 uint32_t hs_zstd_version(void) { return zstd().ok ? zstd().version() : 0; }
 
-// The header and the block table of a container (crates/taco-format/src/header.rs:220-330 and
-// reader.rs), checked: versions 1 and 2, the layout rules, and the lengths.
-struct Parsed {
+}  // extern "C"
+
+// ---- unfold ----
+
+namespace {
+
+// Positional reads of a container: read() fills n bytes from offset `at`; 0, or non-zero on an
+// error.
+struct ReadAt {
+    virtual ~ReadAt() = default;
+    virtual int read(uint64_t at, uint8_t* p, size_t n) = 0;
+};
+
+// The original bytes in order: write() takes n bytes; 0, or non-zero on an error.
+struct Writer {
+    virtual ~Writer() = default;
+    virtual int write(const uint8_t* p, size_t n) = 0;
+};
+
+struct MemReadAt : ReadAt {
+    const uint8_t* d;
+    uint64_t n;
+    MemReadAt(const uint8_t* p, uint64_t len) : d(p), n(len) {}
+    int read(uint64_t at, uint8_t* p, size_t k) override {
+        if (at > n || k > n - at) return 1;
+        if (k) memcpy(p, d + at, k);
+        return 0;
+    }
+};
+
+struct MemWriter : Writer {
+    uint8_t* out;
+    size_t at = 0, cap;
+    MemWriter(uint8_t* o, size_t c) : out(o), cap(c) {}
+    int write(const uint8_t* p, size_t n) override {
+        if (n > cap - at) return 1;
+        if (n) memcpy(out + at, p, n);
+        at += n;
+        return 0;
+    }
+};
+
+struct CallbackReadAt : ReadAt {
+    hs_read_at_fn fn;
+    void* user;
+    CallbackReadAt(hs_read_at_fn f, void* u) : fn(f), user(u) {}
+    int read(uint64_t at, uint8_t* p, size_t n) override { return fn(user, at, p, n); }
+};
+
+struct CallbackWriter : Writer {
+    hs_write_fn fn;
+    void* user;
+    CallbackWriter(hs_write_fn f, void* u) : fn(f), user(u) {}
+    int write(const uint8_t* p, size_t n) override { return fn(user, p, n); }
+};
+
+// The header of a container (crates/taco-format/src/header.rs:220-330), checked.
+struct Header {
     uint16_t version = 0;
+    size_t hlen = 0;
     uint8_t model_hash[32];
     uint64_t original_len = 0;
     uint8_t checksum[32];
     uint32_t block_size = 0, count = 0;
     uint8_t profile = 0, mixer_rule = 0;
     uint16_t overlap = 0;
-    std::vector<uint8_t> kinds;
-    std::vector<uint32_t> stored;
-    std::vector<size_t> at;  // offset of each block's stored bytes
+    bool needs_model = false;
 };
 
-static int parse_container(const uint8_t* d, size_t n, Parsed& c) {
-    auto bad = [](const std::string& why) { return hs::host_fail(HS_FORMAT, "the container is not valid: " + why); };
+int bad_container(const std::string& why) { return hs::host_fail(HS_FORMAT, "the container is not valid: " + why); }
+
+int parse_header(ReadAt& in, uint64_t n, Header& c) {
+    uint8_t d[HEADER_LEN];
+    if (n < 6 || in.read(0, d, 6)) return bad_container("truncated header");
     auto rd16 = [&](size_t o) { uint16_t v; memcpy(&v, d + o, 2); return v; };
     auto rd32 = [&](size_t o) { uint32_t v; memcpy(&v, d + o, 4); return v; };
     auto rd64 = [&](size_t o) { uint64_t v; memcpy(&v, d + o, 8); return v; };
-    if (n < 6) return bad("truncated header");
-    if (memcmp(d, "TACO", 4) != 0) return bad("bad magic");
+    if (memcmp(d, "TACO", 4) != 0) return bad_container("bad magic");
     c.version = rd16(4);
-    if (c.version != 1 && c.version != 2) return bad("unsupported version " + std::to_string(c.version));
-    const size_t hlen = c.version == 1 ? 88 : HEADER_LEN;
-    if (n < hlen) return bad("truncated header");
-    if (rd16(6) != 0) return bad("unknown flags");
+    if (c.version != 1 && c.version != 2) return bad_container("unsupported version " + std::to_string(c.version));
+    c.hlen = c.version == 1 ? 88 : HEADER_LEN;
+    if (n < c.hlen || in.read(0, d, c.hlen)) return bad_container("truncated header");
+    if (rd16(6) != 0) return bad_container("unknown flags");
     memcpy(c.model_hash, d + 8, 32);
     c.original_len = rd64(40);
     memcpy(c.checksum, d + 48, 32);
     c.block_size = rd32(80);
     c.count = rd32(84);
-    if (c.block_size == 0 || c.block_size > MAX_BLOCK_SIZE) return bad("block size out of range");
-    if ((uint64_t)c.count != (c.original_len + c.block_size - 1) / c.block_size) return bad("wrong block count");
+    if (c.block_size == 0 || c.block_size > MAX_BLOCK_SIZE) return bad_container("block size out of range");
+    if ((uint64_t)c.count != (c.original_len + c.block_size - 1) / c.block_size) return bad_container("wrong block count");
     if (c.version == 2) {
         c.profile = d[88];
         const uint8_t reserved = d[89];
         const uint16_t bits = rd16(90);
         const uint8_t* params = d + 92;
-        if (c.profile > 1 || reserved != 0 || (bits & ~3u)) return bad("bad version 2 fields");
-        if (c.profile == 0 && (bits & 1)) return bad("the text profile has no mixer");
+        if (c.profile > 1 || reserved != 0 || (bits & ~3u)) return bad_container("bad version 2 fields");
+        if (c.profile == 0 && (bits & 1)) return bad_container("the text profile has no mixer");
         if (bits & 1) {
-            if (params[0] != 1 && params[0] != 2) return bad("unknown mixer rule");
+            if (params[0] != 1 && params[0] != 2) return bad_container("unknown mixer rule");
             c.mixer_rule = params[0];
         } else if (params[0] != 0) {
-            return bad("mixer rule without the mixer bit");
+            return bad_container("mixer rule without the mixer bit");
         }
         uint16_t k;
         memcpy(&k, params + 2, 2);
-        if ((bits & 2) && k == 0) return bad("overlap bit with K = 0");
-        if (!(bits & 2) && k != 0) return bad("overlap without the overlap bit");
+        if ((bits & 2) && k == 0) return bad_container("overlap bit with K = 0");
+        if (!(bits & 2) && k != 0) return bad_container("overlap without the overlap bit");
         c.overlap = k;
-        if (params[1] != 0) return bad("non-zero coding parameters");
+        if (params[1] != 0) return bad_container("non-zero coding parameters");
         for (int i = 4; i < 12; i++)
-            if (params[i] != 0) return bad("non-zero coding parameters");
+            if (params[i] != 0) return bad_container("non-zero coding parameters");
     }
-    const bool needs_model = std::any_of(c.model_hash, c.model_hash + 32, [](uint8_t b) { return b != 0; });
-    const uint64_t table_end = hlen + 5 * (uint64_t)c.count;
-    if (n < table_end) return bad("truncated block table");
-    uint64_t off = table_end, remaining = c.original_len;
-    c.kinds.resize(c.count);
-    c.stored.resize(c.count);
-    c.at.resize(c.count);
-    for (uint32_t i = 0; i < c.count; i++) {
-        const uint8_t kind = d[hlen + 5 * (size_t)i];
-        const uint32_t sl = rd32(hlen + 5 * (size_t)i + 1);
-        const uint64_t olen = std::min<uint64_t>(c.block_size, remaining);
-        remaining -= olen;
-        if (kind > 3 || (c.version == 1 && kind > 1)) return bad("unknown block kind");
-        if (kind == KIND_RAW && sl != olen) return bad("a raw block stores its original bytes");
-        if (kind != KIND_RAW && sl >= olen) return bad("a coded, mixed or zstd block is not smaller than its bytes");
-        if ((kind == KIND_CODED || kind == 3) && !needs_model) return bad("a coded block needs a model");
-        if (kind == 3 && c.mixer_rule == 0) return bad("a mixed block needs the mixer bit");
-        if (off + sl > n) return bad("truncated block");
-        c.kinds[i] = kind;
-        c.stored[i] = sl;
-        c.at[i] = (size_t)off;
-        off += sl;
-    }
-    if (off != n) return bad("extra bytes after the last block");
+    c.needs_model = std::any_of(c.model_hash, c.model_hash + 32, [](uint8_t b) { return b != 0; });
     return HS_OK;
 }
+
+constexpr uint32_t TABLE_GROUP = 4096;  // table entries read at a time (stream.rs:66)
+
+// Reads the table entries [first, first + n) into kinds / stored, and checks each entry's rules
+// (reader.rs): the kind, a raw block stores its original length, any other kind is smaller, a
+// coded or mixed block needs a model, a mixed block needs the mixer bit.
+int read_table(ReadAt& in, const Header& c, uint32_t first, uint32_t n, std::vector<uint8_t>& kinds,
+               std::vector<uint32_t>& stored) {
+    std::vector<uint8_t> raw((size_t)n * 5);
+    if (n && in.read(c.hlen + 5 * (uint64_t)first, raw.data(), raw.size())) return bad_container("truncated block table");
+    kinds.resize(n);
+    stored.resize(n);
+    for (uint32_t j = 0; j < n; j++) {
+        const uint32_t i = first + j;
+        const uint8_t kind = raw[5 * (size_t)j];
+        uint32_t sl;
+        memcpy(&sl, &raw[5 * (size_t)j + 1], 4);
+        const uint64_t olen = std::min<uint64_t>(c.block_size, c.original_len - (uint64_t)i * c.block_size);
+        if (kind > 3 || (c.version == 1 && kind > 1)) return bad_container("unknown block kind");
+        if (kind == KIND_RAW && sl != olen) return bad_container("a raw block stores its original bytes");
+        if (kind != KIND_RAW && sl >= olen) return bad_container("a coded, mixed or zstd block is not smaller than its bytes");
+        if ((kind == KIND_CODED || kind == 3) && !c.needs_model) return bad_container("a coded block needs a model");
+        if (kind == 3 && c.mixer_rule == 0) return bad_container("a mixed block needs the mixer bit");
+        kinds[j] = kind;
+        stored[j] = sl;
+    }
+    return HS_OK;
+}
+
+// taco::unfold segment by segment (crates/taco/src/stream.rs StreamUnfold::from_seekable): the
+// whole table and the container length are checked before any output; then each segment's stored
+// bytes are read, its raw blocks copied, its zstd blocks decoded on the host, its coded blocks on
+// the GPU, and its bytes written out; the SHA-256 of all of them is checked at the end.
+int unfold_stream_impl(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uint64_t n, Writer& out) {
+    Header c;
+    int rc = parse_header(in, n, c);
+    if (rc) return rc;
+    hs_model_info info;
+    if ((rc = hs_model_get_info(hs::batch_model(batch), &info))) return rc;
+    // unfold.rs:157-180 checked_model: a container that names a model needs that model.
+    if (c.needs_model && memcmp(c.model_hash, info.hash, 32) != 0)
+        return hs::host_fail(HS_MODEL_MISMATCH, "the container was folded with another model");
+    std::vector<uint8_t> kinds;
+    std::vector<uint32_t> stored;
+    const uint64_t table_end = c.hlen + 5 * (uint64_t)c.count;
+    if (n < table_end) return bad_container("truncated block table");
+    uint64_t total = table_end;
+    for (uint32_t g = 0; g < c.count; g += TABLE_GROUP) {
+        const uint32_t m = std::min<uint32_t>(TABLE_GROUP, c.count - g);
+        if ((rc = read_table(in, c, g, m, kinds, stored))) return rc;
+        for (uint32_t j = 0; j < m; j++) {
+            if (kinds[j] == 3)
+                return hs::host_fail(HS_UNSUPPORTED, "block " + std::to_string(g + j) +
+                                                         " is a mixed block (profile logs): its unfold needs the "
+                                                         "match model and the mixer of the caller");
+            total += stored[j];
+        }
+    }
+    if (total > n) return bad_container("truncated block");
+    if (total < n) return bad_container("extra bytes after the last block");
+    if ((rc = hs_batch_set_overlap(batch, c.overlap))) return rc;
+    auto corrupt = [](uint64_t i, const std::string& why) {
+        return hs::host_fail(HS_CORRUPT, "block " + std::to_string(i) + " is corrupt: " + why);
+    };
+    const uint64_t seg_blocks = std::min<uint64_t>(std::max<uint64_t>(SEGMENT_BYTES / c.block_size, 1), SEGMENT_BLOCKS);
+    const size_t per = std::max<size_t>(1, std::min(hs::batch_slots(batch), hs::batch_max_rows(batch)));
+    hs::Sha256 sum;
+    std::vector<uint8_t> data, restored;
+    std::vector<uint64_t> at;
+    uint64_t pos = table_end;
+    for (uint64_t first = 0; first < c.count; first += seg_blocks) {
+        const uint32_t m = (uint32_t)std::min<uint64_t>(seg_blocks, c.count - first);
+        if ((rc = read_table(in, c, (uint32_t)first, m, kinds, stored))) return rc;
+        at.resize(m);
+        uint64_t seg_stored = 0;
+        for (uint32_t j = 0; j < m; j++) {
+            at[j] = seg_stored;
+            seg_stored += stored[j];
+        }
+        data.resize((size_t)seg_stored);
+        if (seg_stored && in.read(pos, data.data(), data.size())) return bad_container("truncated block");
+        pos += seg_stored;
+        const uint64_t o0 = first * c.block_size;
+        const uint64_t seg_len = std::min<uint64_t>((uint64_t)m * c.block_size, c.original_len - o0);
+        restored.resize((size_t)seg_len);
+        // Raw and zstd blocks on the host; the coded ones collected for the GPU.
+        std::vector<uint32_t> coded;
+        for (uint32_t j = 0; j < m; j++) {
+            const size_t o = (size_t)j * c.block_size;
+            const size_t olen = (size_t)std::min<uint64_t>(c.block_size, seg_len - o);
+            if (kinds[j] == KIND_RAW) memcpy(restored.data() + o, data.data() + at[j], olen);
+            else if (kinds[j] == KIND_ZSTD &&
+                     !decompress_zstd(data.data() + at[j], stored[j], restored.data() + o, olen))
+                return corrupt(first + j, "the zstd frame does not give the block");
+            else if (kinds[j] == KIND_CODED) coded.push_back(j);
+        }
+        // The coded blocks: the varint token count (1 .. the block length), then the coder bytes,
+        // decoded on the device in rounds of up to min(slots, max_rows) blocks (codec.rs:370-520
+        // BlockDecoder, with the decoder of hs_batch_decode_blocks), then the tokens' bytes.
+        for (size_t r0 = 0; r0 < coded.size(); r0 += per) {
+            const size_t r1 = std::min(coded.size(), r0 + per), mm = r1 - r0;
+            std::vector<uint32_t> slots(mm), counts(mm), status(mm);
+            std::vector<uint64_t> offs(mm), lens(mm), toff(mm);
+            uint64_t ntok = 0;
+            for (size_t q = 0; q < mm; q++) {
+                const uint32_t j = coded[r0 + q];
+                const uint8_t* p = data.data() + at[j];
+                const size_t sl = stored[j];
+                uint64_t count = 0;
+                size_t k = 0;
+                for (int shift = 0;; shift += 7, k++) {
+                    if (k >= sl || shift > 63) return corrupt(first + j, "the token count is not valid");
+                    count |= (uint64_t)(p[k] & 0x7F) << shift;
+                    if (!(p[k] & 0x80)) break;
+                }
+                k++;
+                const size_t olen = (size_t)std::min<uint64_t>(c.block_size, seg_len - (uint64_t)j * c.block_size);
+                if (count == 0 || count > olen)
+                    return corrupt(first + j, "the token count does not agree with the block length");
+                slots[q] = (uint32_t)q;
+                counts[q] = (uint32_t)count;
+                offs[q] = at[j] + k;
+                lens[q] = sl - k;
+                toff[q] = ntok;
+                ntok += count;
+            }
+            std::vector<uint32_t> toks(std::max<uint64_t>(ntok, 1));
+            if ((rc = hs_batch_decode_blocks(batch, (uint32_t)mm, slots.data(), data.data(), data.size(), offs.data(),
+                                             lens.data(), counts.data(), FREQ_BITS, toks.data(), ntok, toff.data(),
+                                             status.data())))
+                return rc;
+            for (size_t q = 0; q < mm; q++) {
+                const uint32_t j = coded[r0 + q];
+                if (status[q]) return corrupt(first + j, "an interval does not hold its target");
+                const size_t o = (size_t)j * c.block_size;
+                const size_t olen = (size_t)std::min<uint64_t>(c.block_size, seg_len - o);
+                size_t w = 0;
+                for (uint32_t t = 0; t < counts[q]; t++) {
+                    size_t nb;
+                    const uint32_t id = toks[toff[q] + t];
+                    const uint8_t* b = hs::token_bytes(tok, id, &nb);
+                    if (id == info.eot_token || nb == 0 || nb > olen - w)
+                        return corrupt(first + j, "the tokens do not give the block length");
+                    memcpy(restored.data() + o + w, b, nb);
+                    w += nb;
+                }
+                if (w != olen) return corrupt(first + j, "the tokens do not give the block length");
+            }
+        }
+        sum.update(restored.data(), restored.size());
+        if (out.write(restored.data(), restored.size())) return hs::host_fail(HS_IO, "the output writer failed");
+    }
+    uint8_t got[32];
+    sum.final(got);
+    if (memcmp(got, c.checksum, 32) != 0)
+        return hs::host_fail(HS_CORRUPT, "the restored bytes do not have the container's SHA-256");
+    return HS_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 int hs_unfold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* container, size_t len, uint8_t* out,
               size_t cap, size_t* out_len) {
     if (!batch || !tok || !out_len || (len && !container)) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
-    Parsed c;
-    int rc = parse_container(container, len, c);
+    MemReadAt in(container, len);
+    Header c;
+    int rc = parse_header(in, len, c);
     if (rc) return rc;
     *out_len = (size_t)c.original_len;
     if (cap < c.original_len || (!out && c.original_len))
         return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
                                                   std::to_string(c.original_len) + " needed");
-    hs_model_info info;
-    if ((rc = hs_model_get_info(hs::batch_model(batch), &info))) return rc;
-    // unfold.rs:157-180 checked_model: a container that names a model needs that model.
-    if (std::any_of(c.model_hash, c.model_hash + 32, [](uint8_t b) { return b != 0; }) &&
-        memcmp(c.model_hash, info.hash, 32) != 0)
-        return hs::host_fail(HS_MODEL_MISMATCH, "the container was folded with another model");
-    for (uint32_t i = 0; i < c.count; i++)
-        if (c.kinds[i] == 3)
-            return hs::host_fail(HS_UNSUPPORTED, "block " + std::to_string(i) +
-                                                     " is a mixed block (profile logs): its unfold needs the "
-                                                     "match model and the mixer of the caller");
-    if ((rc = hs_batch_set_overlap(batch, c.overlap))) return rc;
-    auto corrupt = [](uint32_t i, const std::string& why) {
-        return hs::host_fail(HS_CORRUPT, "block " + std::to_string(i) + " is corrupt: " + why);
-    };
-    // Raw and zstd blocks on the host; the coded ones collected for the GPU.
-    std::vector<uint32_t> coded;
-    for (uint32_t i = 0; i < c.count; i++) {
-        const size_t o = (size_t)i * c.block_size;
-        const size_t olen = (size_t)std::min<uint64_t>(c.block_size, c.original_len - o);
-        if (c.kinds[i] == KIND_RAW) memcpy(out + o, container + c.at[i], olen);
-        else if (c.kinds[i] == KIND_ZSTD && !decompress_zstd(container + c.at[i], c.stored[i], out + o, olen))
-            return corrupt(i, "the zstd frame does not give the block");
-        else if (c.kinds[i] == KIND_CODED) coded.push_back(i);
-    }
-    // The coded blocks: the varint token count (1 .. the block length), then the coder bytes,
-    // decoded on the device in rounds of up to min(slots, max_rows) blocks (codec.rs:370-520
-    // BlockDecoder, with the decoder of hs_batch_decode_blocks), then the tokens' bytes.
-    const size_t per = std::max<size_t>(1, std::min(hs::batch_slots(batch), hs::batch_max_rows(batch)));
-    for (size_t r0 = 0; r0 < coded.size(); r0 += per) {
-        const size_t r1 = std::min(coded.size(), r0 + per), m = r1 - r0;
-        std::vector<uint32_t> slots(m), counts(m), status(m);
-        std::vector<uint64_t> offs(m), lens(m), toff(m);
-        uint64_t total = 0;
-        for (size_t j = 0; j < m; j++) {
-            const uint32_t i = coded[r0 + j];
-            const uint8_t* p = container + c.at[i];
-            const size_t sl = c.stored[i];
-            uint64_t count = 0;
-            size_t k = 0;
-            for (int shift = 0;; shift += 7, k++) {
-                if (k >= sl || shift > 63) return corrupt(i, "the token count is not valid");
-                count |= (uint64_t)(p[k] & 0x7F) << shift;
-                if (!(p[k] & 0x80)) break;
-            }
-            k++;
-            const size_t olen = (size_t)std::min<uint64_t>(c.block_size, c.original_len - (uint64_t)i * c.block_size);
-            if (count == 0 || count > olen) return corrupt(i, "the token count does not agree with the block length");
-            slots[j] = (uint32_t)j;
-            counts[j] = (uint32_t)count;
-            offs[j] = c.at[i] + k;
-            lens[j] = sl - k;
-            toff[j] = total;
-            total += count;
-        }
-        std::vector<uint32_t> toks(std::max<uint64_t>(total, 1));
-        if ((rc = hs_batch_decode_blocks(batch, (uint32_t)m, slots.data(), container, len, offs.data(), lens.data(),
-                                         counts.data(), FREQ_BITS, toks.data(), total, toff.data(), status.data())))
-            return rc;
-        for (size_t j = 0; j < m; j++) {
-            const uint32_t i = coded[r0 + j];
-            if (status[j]) return corrupt(i, "an interval does not hold its target");
-            const size_t o = (size_t)i * c.block_size;
-            const size_t olen = (size_t)std::min<uint64_t>(c.block_size, c.original_len - o);
-            size_t at = 0;
-            for (uint32_t t = 0; t < counts[j]; t++) {
-                size_t nb;
-                const uint32_t id = toks[toff[j] + t];
-                const uint8_t* b = hs::token_bytes(tok, id, &nb);
-                if (id == info.eot_token || nb == 0 || nb > olen - at)
-                    return corrupt(i, "the tokens do not give the block length");
-                memcpy(out + o + at, b, nb);
-                at += nb;
-            }
-            if (at != olen) return corrupt(i, "the tokens do not give the block length");
-        }
-    }
-    uint8_t sum[32];
-    hs::sha256(out, (size_t)c.original_len, sum);
-    if (memcmp(sum, c.checksum, 32) != 0)
-        return hs::host_fail(HS_CORRUPT, "the restored bytes do not have the container's SHA-256");
-    return HS_OK;
+    MemWriter w(out, cap);
+    return unfold_stream_impl(batch, tok, in, len, w);
+}
+
+int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tok, uint64_t len, hs_read_at_fn read_at, void* read_user,
+                     hs_write_fn write, void* write_user, uint64_t* out_len) {
+    if (!batch || !tok || !read_at || !write || !out_len) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    CallbackReadAt in(read_at, read_user);
+    Header c;
+    int rc = parse_header(in, len, c);
+    if (rc) return rc;
+    *out_len = c.original_len;
+    CallbackWriter w(write, write_user);
+    return unfold_stream_impl(batch, tok, in, len, w);
 }
 
 }  // extern "C"

@@ -133,59 +133,112 @@ def text_word_ids(vocab: list[bytes]) -> np.ndarray:
     return np.array([ids[b" " + w] for w in _words(0x7AC0, N_WORDS)], dtype=np.uint32)
 
 
+def _zipf_draw(rng, n: int) -> np.ndarray:
+    """n word indices of the Zipf(1.1) law over N_WORDS (inverse CDF of one uniform draw each)."""
+    p = np.arange(1, N_WORDS + 1, dtype=np.float64) ** -1.1
+    cdf = np.cumsum(p / p.sum())
+    return np.minimum(np.searchsorted(cdf, rng.random(n), side="right"), N_WORDS - 1)
+
+
 def zipf_text(n_bytes: int, seed: int) -> bytes:
     """About n_bytes (at least) of seeded Zipf(1.1) text over the N_WORDS text words, each word
     after a space, or after a newline with probability 1/12; the text starts with a word."""
     rng = np.random.default_rng(seed)
     words = _words(0x7AC0, N_WORDS)
-    ranks = np.arange(1, N_WORDS + 1, dtype=np.float64)
-    p = ranks ** -1.1
-    p /= p.sum()
+    lens = np.array([len(w) for w in words], dtype=np.int64)
+    letters = np.zeros((N_WORDS, 5), dtype=np.uint8)
+    for i, w in enumerate(words):
+        letters[i, :len(w)] = np.frombuffer(w, dtype=np.uint8)
     out, total = [], 0
     while total < n_bytes:
-        n = max(1024, (n_bytes - total) // 4 + 16)
-        idx = rng.choice(N_WORDS, size=n, p=p)
+        n = min(1 << 20, max(1024, (n_bytes - total) // 4 + 16))
+        idx = _zipf_draw(rng, n)
         nl = rng.random(n) < 1.0 / 12
-        chunk = b"".join((b"\n" if f else b" ") + words[i] for i, f in zip(idx.tolist(), nl.tolist()))
-        out.append(chunk)
-        total += len(chunk)
+        wl = lens[idx] + 1  # the separator, then the word
+        starts = np.concatenate([[0], np.cumsum(wl)[:-1]])
+        chunk = np.empty(int(wl.sum()), dtype=np.uint8)
+        chunk[starts] = np.where(nl, ord("\n"), ord(" "))
+        for k in range(5):
+            m = lens[idx] > k
+            chunk[starts[m] + 1 + k] = letters[idx[m], k]
+        out.append(chunk.tobytes())
+        total += chunk.size
     return b"".join(out)[1:]
 
 
 def json_records(n_bytes: int, seed: int) -> bytes:
     """About n_bytes (at least) of JSON-shaped records, one per line: 1 to 6 "key": number pairs,
-    keys from the text words (Zipf), numbers uniform integers in [-10^6, 10^6]."""
+    keys from the text words (Zipf), numbers uniform integers in [-10^6, 10^6]; e.g.
+    {"abc": -12, "qz": 40571}."""
     rng = np.random.default_rng(seed)
     words = _words(0x7AC0, N_WORDS)
-    ranks = np.arange(1, N_WORDS + 1, dtype=np.float64)
-    p = ranks ** -1.1
-    p /= p.sum()
+    # Each key as the bytes '"word": ' (at most 9 bytes).
+    keys = [b'"' + w + b'": ' for w in words]
+    klen = np.array([len(k) for k in keys], dtype=np.int64)
+    kbytes = np.zeros((N_WORDS, 9), dtype=np.uint8)
+    for i, k in enumerate(keys):
+        kbytes[i, :len(k)] = np.frombuffer(k, dtype=np.uint8)
     out, total = [], 0
     while total < n_bytes:
-        n = 4096
-        pairs = rng.integers(1, 7, n)
-        keys = rng.choice(N_WORDS, size=int(pairs.sum()), p=p).tolist()
-        nums = rng.integers(-10**6, 10**6 + 1, int(pairs.sum())).tolist()
-        k = 0
-        lines = []
-        for c in pairs.tolist():
-            lines.append(b"{" + b", ".join(b'"%s": %d' % (words[keys[k + j]], nums[k + j]) for j in range(c)) + b"}\n")
-            k += c
-        chunk = b"".join(lines)
-        out.append(chunk)
-        total += len(chunk)
+        n = max(256, (n_bytes - total) // 40 + 16)  # records
+        c = rng.integers(1, 7, n)
+        P = int(c.sum())
+        kid = _zipf_draw(rng, P)
+        num = rng.integers(-10**6, 10**6 + 1, P)
+        mag = np.abs(num)
+        ndig = np.ones(P, dtype=np.int64)
+        for t in range(1, 7):
+            ndig += mag >= 10 ** t
+        neg = (num < 0).astype(np.int64)
+        first = np.zeros(P, dtype=bool)
+        first[np.concatenate([[0], np.cumsum(c)[:-1]])] = True
+        last = np.zeros(P, dtype=bool)
+        last[np.cumsum(c) - 1] = True
+        # A pair: "{" if first, else ", "; the key; "-" if negative; the digits; "}\n" if last.
+        pre = np.where(first, 1, 2)
+        plen = pre + klen[kid] + neg + ndig + np.where(last, 2, 0)
+        start = np.concatenate([[0], np.cumsum(plen)[:-1]])
+        buf = np.empty(int(plen.sum()), dtype=np.uint8)
+        buf[start[first]] = ord("{")
+        nf = ~first
+        buf[start[nf]] = ord(",")
+        buf[start[nf] + 1] = ord(" ")
+        at = start + pre
+        for k in range(9):
+            m = klen[kid] > k
+            buf[at[m] + k] = kbytes[kid[m], k]
+        at = at + klen[kid]
+        buf[at[neg == 1]] = ord("-")
+        at = at + neg
+        for k in range(7):  # digit k from the left
+            m = ndig > k
+            e = ndig[m] - 1 - k
+            buf[at[m] + k] = ord("0") + (mag[m] // (10 ** e)) % 10
+        at = at + ndig
+        buf[at[last]] = ord("}")
+        buf[at[last] + 1] = ord("\n")
+        out.append(buf.tobytes())
+        total += buf.size
     return b"".join(out)
+
+
+def mixed_kinds(n: int, seed: int = 4) -> np.ndarray:
+    """The kinds of the n pieces of mixed_stream: 0 Zipf text (70 %), 1 JSON records (20 %),
+    2 uniform random bytes (the rest), in a seeded order."""
+    rng = np.random.default_rng(seed)
+    kinds = np.array([0] * (n * 7 // 10) + [1] * (n * 2 // 10), dtype=np.int8)
+    kinds = np.concatenate([kinds, np.full(n - kinds.size, 2, np.int8)])
+    rng.shuffle(kinds)
+    return kinds
 
 
 def mixed_stream(n_bytes: int = 256 << 20, seed: int = 4, piece: int = 64 << 10) -> bytes:
     """n_bytes of seeded input in pieces of `piece` bytes, 70 % Zipf text, 20 %
     JSON-shaped key/number records and 10 % uniform random bytes (exact counts of pieces, in a
-    seeded order)."""
+    seeded order: mixed_kinds)."""
     n = n_bytes // piece
-    rng = np.random.default_rng(seed)
-    kinds = np.array([0] * (n * 7 // 10) + [1] * (n * 2 // 10), dtype=np.int8)
-    kinds = np.concatenate([kinds, np.full(n - kinds.size, 2, np.int8)])
-    rng.shuffle(kinds)
+    kinds = mixed_kinds(n, seed)
+    rng = np.random.default_rng(seed + 3)
     counts = np.bincount(kinds, minlength=3)
     text = zipf_text(int(counts[0]) * piece, seed + 1)
     js = json_records(int(counts[1]) * piece, seed + 2)

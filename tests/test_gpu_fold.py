@@ -182,3 +182,92 @@ def test_fold_moves_the_windows_of_a_gpu_that_fails_to_open(setup, monkeypatch):
     with pytest.raises(B.HardShellError) as e:
         B.fold_multi([0, 7], tiny_bytes(), tok, data, 300, 32, slots=8, max_rows=4096)
     assert e.value.code == B.HS_NO_DEVICE
+
+
+# ---- streams: the same bytes segment by segment, bounded memory (crates/taco/src/stream.rs) ----
+
+def _reader(data: bytes):
+    pos = [0]
+
+    def read(n):
+        out = data[pos[0]:pos[0] + n]
+        pos[0] += len(out)
+        return out
+
+    return read
+
+
+def _seekable():
+    buf = bytearray()
+
+    def write(at, chunk):
+        if len(buf) < at + len(chunk):
+            buf.extend(bytes(at + len(chunk) - len(buf)))
+        buf[at:at + len(chunk)] = chunk
+
+    return buf, write
+
+
+def _many_blocks():
+    """More than one segment (4,096 blocks) of 256-byte blocks: coded, zstd and raw blocks."""
+    pred = (GOLDEN / "predicted_text_k32.in").read_bytes()
+    rng = np.random.default_rng(17)
+    parts = [pred, rng.integers(0, 256, 40_000, dtype=np.uint8).tobytes(), (GOLDEN / "all_kinds_text.in").read_bytes()]
+    data = b""
+    while len(data) < 4100 * 256 + 77:
+        data += parts[len(data) % 3]
+    return data[:4100 * 256 + 77]
+
+
+@pytest.mark.parametrize("case", ["vector", "segments"])
+def test_fold_stream_gives_the_bytes_of_fold(setup, case):
+    batch, tok = setup
+    if case == "vector":
+        data, bs, k = (GOLDEN / "predicted_text_k32.in").read_bytes() * 2, 300, 32
+    else:
+        data, bs, k = _many_blocks(), 256, 5
+    want, wstats = B.fold(batch, tok, data, bs, k)
+    buf, write = _seekable()
+    n, stats = B.fold_stream(batch, tok, len(data), _reader(data), write, bs, k)
+    assert n == len(want) and bytes(buf) == want
+    for key in ("blocks", "coded_blocks", "zstd_blocks", "tokens", "container_len"):
+        assert stats[key] == wstats[key]
+    assert stats["coded_blocks"] > 0
+    # The unfold stream gives the input back.
+    out = bytearray()
+    got_len = B.unfold_stream(batch, tok, len(want), lambda at, m: want[at:at + m], out.extend)
+    assert got_len == len(data) and bytes(out) == data
+    if case == "segments":
+        ords = [0, 1] if __import__("torch").cuda.device_count() >= 2 else [0, 0]
+        buf2, write2 = _seekable()
+        n2, _ = B.fold_stream_multi(ords, tiny_bytes(), tok, len(data), _reader(data), write2, bs, k, slots=8,
+                                    max_rows=4096)
+        assert bytes(buf2) == want
+
+
+def test_fold_stream_refuses_a_short_or_long_source_and_a_failing_sink(setup):
+    batch, tok = setup
+    data = (GOLDEN / "predicted_text_k32.in").read_bytes()
+    for length in (len(data) + 1, len(data) - 1):
+        _, write = _seekable()
+        with pytest.raises(B.HardShellError) as e:
+            B.fold_stream(batch, tok, length, _reader(data), write, 300, 0)
+        assert e.value.code == B.HS_IO
+
+    def bad_write(at, chunk):
+        raise OSError("disk full")
+
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_stream(batch, tok, len(data), _reader(data), bad_write, 300, 0)
+    assert e.value.code == B.HS_IO
+
+
+def test_unfold_stream_refuses_a_damaged_table_before_any_output(setup):
+    batch, tok = setup
+    good = (GOLDEN / "predicted_text_k32.taco").read_bytes()
+    for bad in (good[:-1], good + b"\0", good[:150]):
+        out = []
+        with pytest.raises(B.HardShellError) as e:
+            B.unfold_stream(batch, tok, len(bad), lambda at, m, d=bad: d[at:at + m], out.append)
+        assert e.value.code == B.HS_FORMAT
+        assert out == []
