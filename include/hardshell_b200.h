@@ -81,6 +81,11 @@ int hs_dev_name(hs_dev* dev, char* buf, size_t cap);
  * weights. The bytes are copied. HS_MODEL for an invalid file, HS_UNSUPPORTED for a valid model
  * this backend does not run (see the message). */
 int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out);
+/* hardshell::gpt2::Model::load (crates/hardshell/src/gpt2/model.rs:292) on the host alone: the
+ * checks of hs_model_load without a device or an upload. HS_MODEL for an invalid file; else the
+ * dimensions, version, cache bytes per slot and SHA-256 (weight_bytes is 0: it depends on the
+ * device layout). */
+int hs_model_check(const uint8_t* file, size_t len, hs_model_info* out);
 void hs_model_free(hs_model* model);
 int hs_model_get_info(hs_model* model, hs_model_info* out);
 

@@ -106,6 +106,7 @@ def lib() -> ctypes.CDLL:
     L.hs_mem_info.argtypes = [vp, ctypes.POINTER(u64), ctypes.POINTER(u64)]
     L.hs_dev_name.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t]
     L.hs_model_load.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(vp)]
+    L.hs_model_check.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ModelInfo)]
     L.hs_model_free.argtypes = [vp]
     L.hs_model_free.restype = None
     L.hs_model_get_info.argtypes = [vp, ctypes.POINTER(ModelInfo)]
@@ -210,6 +211,16 @@ class Tokenizer:
             out.append(data[a:e])
             a = e
         return out
+
+
+def check_model(data: bytes) -> dict:
+    """hs_model_check: the host-side validation of a .hsm file (Model::load without a device); its
+    dimensions and SHA-256, or HardShellError(HS_MODEL)."""
+    info = ModelInfo()
+    _check(lib().hs_model_check(data, len(data), ctypes.byref(info)))
+    out = {name: getattr(info, name) for name, _ in ModelInfo._fields_ if name != "hash"}
+    out["hash"] = bytes(info.hash)
+    return out
 
 
 def fold(batch, tokenizer, data: bytes, block_size: int = 0, overlap: int = 0, spread: bool = False,

@@ -141,6 +141,9 @@ struct EpiArgs {
     // (vt_run) goes here, row-major with stride ldv, for launch_v_scatter to place in vc.
     int8_t* vstage;
     int ldv;
+    // The first row of A that this launch reads (row tile mt reads A rows a_row0 + 128 mt ...);
+    // the outputs are written from row 0. The LM head runs in row chunks with it.
+    int a_row0;
 };
 
 // The 32 rows r0 .. r0 + 31 of a pass are one slot at 32 consecutive positions starting at a

@@ -208,10 +208,10 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                     }
                     uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
                     mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, &bars->full[stage], kb * BK, mt * BM);
+                    tma_load_2d(sa, &tmA, &bars->full[stage], kb * BK, e.a_row0 + mt * BM);
                     if (WIDE) {
                         // [A hi | A lo | B (128 rows)]: 16 + 16 + 16 KB.
-                        tma_load_2d(sa + A_BYTES, &tmA2, &bars->full[stage], kb * BK, mt * BM);
+                        tma_load_2d(sa + A_BYTES, &tmA2, &bars->full[stage], kb * BK, e.a_row0 + mt * BM);
                         tma_load_2d(sa + 2 * A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * TN);
                     } else {
                         tma_load_2d(sa + A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * BN);

@@ -218,8 +218,15 @@ struct hs_batch {
     int8_t* a_lo = nullptr;
     int8_t* g_lo = nullptr;
     int32_t* dbuf = nullptr;  // the residual delta of the last proj/mlp GEMM
+    // The logits of the mixed coder op (a whole pass; made on the first mixed call).
     uint16_t* d16 = nullptr;
     int64_t* tmax = nullptr;
+    // The logits of the other paths: the LM head and the coder run in chunks of `lchunk` rows,
+    // so the distances of a chunk (lchunk x 50,432 x 2 bytes) stay in L2 between the GEMM that
+    // writes them and the coder that reads them.
+    uint16_t* d16c = nullptr;
+    int64_t* tmaxc = nullptr;
+    int lchunk = 0;
     uint64_t* intervals = nullptr;
     uint64_t* weights = nullptr;
     // The host copies of a pass (pinned, two halves: run() prepares the next pass in one half
@@ -271,7 +278,8 @@ struct hs_batch {
     alignas(128) CUtensorMap tm_v;   // the transposed values cache
     alignas(128) CUtensorMap ts_delta;  // epilogue stores: the residual delta (i32)
     alignas(128) CUtensorMap ts_g;      // the GELU output (i8)
-    alignas(128) CUtensorMap ts_d16;    // the logit distances (u16)
+    alignas(128) CUtensorMap ts_d16;    // the logit distances (u16) of the mixed op
+    alignas(128) CUtensorMap ts_d16c;   // the logit distances (u16) of a chunk
     alignas(128) CUtensorMap tm_a_lo;   // version 2: the lo plane of the ln_f output
     alignas(128) CUtensorMap tm_g_lo;   // version 2: the lo plane of the GELU output
 
@@ -393,7 +401,8 @@ int upload_ln(hs_model* m, const hsm::LayerNormP& L, LnDev& D) {
     return HS_OK;
 }
 
-// The forward pass of R rows (the rows are in b->d_rows): the layers, then the logits GEMM.
+// The forward pass of R rows (the rows are in b->d_rows): the layers and ln_f into b->a; the
+// LM head is logits() (run_logits_chunks or the mixed pass).
 int forward(hs_batch* b, int R) {
     hs_model* m = b->model;
     const ModelConsts& c = m->c;
@@ -521,19 +530,45 @@ int forward(hs_batch* b, int R) {
         launch_resid_layernorm(b->x, b->dbuf, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st,
                                c.lnf_wide ? b->a_lo : nullptr);
     }
+    return HS_OK;
+}
+
+// The LM head of rows r0 .. r0 + n - 1 of the pass (ln_f output in b->a): the logit distances
+// and tile maxima of those rows into rows 0 .. n - 1 of d16 / tmax (store map ts).
+void logits(hs_batch* b, int r0, int n, uint16_t* d16, int64_t* tmax, const CUtensorMap* ts) {
+    hs_model* m = b->model;
+    const ModelConsts& c = m->c;
     const DevLinear& lmh = *m->lins[4 * c.L];
+    ProfScope p(b, OP_GEMM_LOGITS, 2ULL * n * lmh.ld.N * lmh.ld.K);
     EpiArgs e{};
-    e.R = R;
+    e.R = n;
     e.N = c.V;
     e.m = lmh.ld.m;
     e.s = lmh.ld.s;
-    e.d16 = b->d16;
+    e.d16 = d16;
     e.ldd = c.Vp;
-    e.tmax = b->tmax;
+    e.tmax = tmax;
     e.ldt = c.VT;
     e.last = m->logits_len - 1;
-    gemm(OP_GEMM_LOGITS, EPI_LOGITS, b->a, c.Dp, &b->tm_a, lmh, e, &b->ts_d16, c.lnf_wide ? &b->tm_a_lo : nullptr);
-    return HS_OK;
+    e.small = lmh.small ? 1 : 0;
+    e.wsum = lmh.wsum;
+    e.a_row0 = r0;
+    if (m->use_tc)
+        launch_gemm_tc(EPI_LOGITS, &b->tm_a, c.lnf_wide ? &lmh.tm128 : &lmh.tm, ts, n, lmh.ld.Np, lmh.ld.Kp, e,
+                       m->dev->num_sms, m->dev->d_err, b->stream, c.lnf_wide ? &b->tm_a_lo : nullptr);
+    else
+        launch_gemm_simple(EPI_LOGITS, b->a + (size_t)r0 * c.Dp, c.Dp, n, lmh.ld, e, b->stream);
+}
+
+// The LM head and the op on its logits, chunk by chunk (lchunk rows): op(r0, n) runs on the
+// chunk's d16c / tmaxc right after its GEMM, while they are in L2.
+template <class Op>
+void run_logits_chunks(hs_batch* b, int R, Op op) {
+    for (int r0 = 0; r0 < R; r0 += b->lchunk) {
+        const int n = std::min(b->lchunk, R - r0);
+        logits(b, r0, n, b->d16c, b->tmaxc, &b->ts_d16c);
+        op(r0, n);
+    }
 }
 
 int check_device_error(hs_batch* b) {
@@ -699,6 +734,11 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         // The buffers of the mixed coder op, made on the first mixed call: the second half of the
         // row table and of the logits (with its store map), the mix records, the statistics.
         const size_t Rc = (size_t)b->Rcap;
+        if ((rc = dalloc(&b->d16, Rc * c.Vp, b->owned)) || (rc = dalloc(&b->tmax, Rc * c.VT, b->owned)) ||
+            (rc = make_store_tmap(m->dev, &b->ts_d16, b->d16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (int)Rc, c.V, c.Vp,
+                                  128)))
+            return rc;
+        b->bytes += Rc * (2 * (size_t)c.Vp + 8 * (size_t)c.VT);
         b->mx_rows[0] = b->d_rows;
         b->mx_d16[0] = b->d16;
         b->mx_tmax[0] = b->tmax;
@@ -860,6 +900,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         rc = forward(b, R);
         if (rc) return rc;
         if (out && mix) {
+            logits(b, 0, R, b->d16, b->tmax, &b->ts_d16);
             // The first half of a mixed pass: the statistics of its rows, read back into half k & 1;
             // then the second half of the previous pass.
             MixRow* pw = b->h_mix + (k & 1) * (size_t)b->Rcap;
@@ -880,21 +921,22 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
             CK(cudaEventRecord(b->stats_done[k & 1], b->stream));
             if (k >= 1 && (rc = finish(k - 1))) return rc;
         } else if (out) {
-            {
+            run_logits_chunks(b, R, [&](int r0, int nr) {
                 ProfScope p(b, OP_CODER, 0);
-                launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len, m->logits_head, bits, b->d_rows,
-                             b->intervals, m->dev->d_err, b->stream);
-            }
+                launch_coder(b->d16c, c.Vp, b->tmaxc, c.VT, c.tsh, nr, c.V, m->logits_exp, m->logits_len,
+                             m->logits_head, bits, b->d_rows + r0, b->intervals + 3 * (size_t)r0, m->dev->d_err,
+                             b->stream);
+            });
             pass_scope.reset();
             CK(cudaMemcpyAsync(b->h_intervals, b->intervals, sizeof(uint64_t) * 3 * R, cudaMemcpyDeviceToHost,
                                b->stream));
             CK(cudaEventRecord(b->pass_done[k & 1], b->stream));
         } else {
-            {
+            run_logits_chunks(b, R, [&](int r0, int nr) {
                 ProfScope p(b, OP_CODER, 0);
-                launch_weights(b->d16, c.Vp, b->tmax, c.VT, c.tsh, R, c.V, m->logits_exp, m->logits_len, b->weights,
-                               b->stream);
-            }
+                launch_weights(b->d16c, c.Vp, b->tmaxc, c.VT, c.tsh, nr, c.V, m->logits_exp, m->logits_len,
+                               b->weights + (size_t)r0 * c.V, b->stream);
+            });
             pass_scope.reset();
             // The weights of this pass leave before the next pass overwrites them.
             rc = check_device_error(b);
@@ -1064,9 +1106,12 @@ int decode_blocks(hs_batch* b, uint32_t n, const uint32_t* slots, const uint8_t*
                 std::unique_ptr<ProfScope> pass_scope(new ProfScope(b, OP_PASS, (uint64_t)L));
                 rc = forward(b, (int)L);
                 if (rc) return rc;
-                ProfScope p(b, OP_CODER, 0);
-                launch_coder(b->d16, c.Vp, b->tmax, c.VT, c.tsh, (int)L, c.V, m->logits_exp, m->logits_len,
-                             m->logits_head, bits, b->d_rows, b->intervals, m->dev->d_err, st);
+                run_logits_chunks(b, (int)L, [&](int r0, int nr) {
+                    ProfScope p(b, OP_CODER, 0);
+                    launch_coder(b->d16c, c.Vp, b->tmaxc, c.VT, c.tsh, nr, c.V, m->logits_exp, m->logits_len,
+                                 m->logits_head, bits, b->d_rows + r0, b->intervals + 3 * (size_t)r0, m->dev->d_err,
+                                 st);
+                });
             }
             {
                 ProfScope p(b, OP_DECODER, 0);
@@ -1294,6 +1339,25 @@ int hs_dev_name(hs_dev* d, char* buf, size_t cap) {
     return HS_OK;
 }
 
+int hs_model_check(const uint8_t* file, size_t len, hs_model_info* out) {
+    if (!file || !out) return fail(HS_BAD_ARGUMENT, "null argument");
+    hsm::Model M;
+    std::string err;
+    if (!hsm::load_model(file, len, M, err)) return fail(HS_MODEL, "the model file is not valid: " + err);
+    memset(out, 0, sizeof(*out));
+    out->n_layer = (uint32_t)M.n_layer;
+    out->n_head = (uint32_t)M.n_head;
+    out->d_model = (uint32_t)M.d_model;
+    out->d_ff = (uint32_t)M.d_ff;
+    out->vocab = (uint32_t)M.vocab;
+    out->n_ctx = (uint32_t)M.n_ctx;
+    out->eot_token = M.eot;
+    out->version = M.version;
+    out->cache_bytes_per_slot = 2ULL * M.n_layer * M.n_ctx * M.d_model;
+    sha256(file, len, out->hash);
+    return HS_OK;
+}
+
 int hs_model_load(hs_dev* dev, const uint8_t* file, size_t len, hs_model** out) {
     if (!dev || !file || !out) return fail(HS_BAD_ARGUMENT, "null argument");
     *out = nullptr;
@@ -1449,9 +1513,18 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         (rc = dalloc(&b->a, R * c.Dp, b->owned)) || (rc = dalloc(&b->qkv, R * c.QKVp, b->owned)) ||
         (rc = dalloc(&b->att, R * c.Dp, b->owned)) || (rc = dalloc(&b->g, R * c.Fp, b->owned)) ||
         (rc = dalloc(&b->dbuf, R * c.d, b->owned)) ||
-        (rc = dalloc(&b->d16, R * c.Vp, b->owned)) || (rc = dalloc(&b->tmax, R * c.VT, b->owned)) ||
         (rc = dalloc(&b->intervals, 3 * R, b->owned)))
         return rc;
+    // The chunk of the LM head: HS_LOGIT_CHUNK rows (a multiple of 128; 768 by default: 6 x 197
+    // GEMM tiles are 8 full waves on 148 SMs, and the 78 MB of distances stay in the 126 MB L2
+    // with the 39 MB of wte), at most the pass.
+    {
+        int ch = 768;
+        if (const char* v = getenv("HS_LOGIT_CHUNK")) ch = std::max(128, atoi(v) / 128 * 128);
+        b->lchunk = (int)std::min<size_t>(R, (size_t)ch);
+    }
+    const size_t LC = (size_t)b->lchunk;
+    if ((rc = dalloc(&b->d16c, LC * c.Vp, b->owned)) || (rc = dalloc(&b->tmaxc, LC * c.VT, b->owned))) return rc;
     if ((rc = dalloc(&b->d_groups, R, b->owned)) || (rc = dalloc(&b->d_rowlist, R, b->owned))) return rc;
     bool gelu_wide = false;
     for (const LayerDev& Ld : m->layers) gelu_wide |= Ld.gelu16 != nullptr;
@@ -1472,11 +1545,13 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
     b->h_rowlist = b->h_rowlist_base;
     b->h_rows = b->h_rows_base;
     b->h_intervals = b->h_intervals_base;
-    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 2 * c.Vp + 8 * c.VT + 24 +
-                                (c.lnf_wide ? c.Dp : 0) + (gelu_wide ? c.Fp : 0));
+    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 24 + (c.lnf_wide ? c.Dp : 0) +
+                                (gelu_wide ? c.Fp : 0)) +
+               LC * (2 * c.Vp + 8 * c.VT);
     if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d, 128)) ||
         (rc = make_store_tmap(m->dev, &b->ts_g, b->g, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, c.f, c.Fp, 32)) ||
-        (rc = make_store_tmap(m->dev, &b->ts_d16, b->d16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, R, c.V, c.Vp, 128)))
+        (rc = make_store_tmap(m->dev, &b->ts_d16c, b->d16c, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (int)LC, c.V, c.Vp,
+                              128)))
         return rc;
     if ((rc = make_tmap(m->dev, &b->tm_a, b->a, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_att, b->att, R, c.Dp, TILE_M)) ||
