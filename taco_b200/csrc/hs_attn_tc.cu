@@ -245,25 +245,19 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         const int32_t last = tl - 1;
         // The last position of this warp's 32 rows: a key slice past it is masked for every lane.
         const int wlast = (int)grp.pos0 + g * 32 + 31;
-        // The table index min(M - score(dot), last). NARROW: with the row constant
-        // Kr = M 2^ss + 2^ss - 1 - h, M - floor((dot sm + h) / 2^ss) = floor((Kr - dot sm) / 2^ss),
-        // one wide multiply-add and one shift (of the high word when ss >= 32, a funnel shift
-        // below). |score| < 2^(52 - ss), so M 2^ss and Kr - dot sm fit in 63 bits and the index,
-        // never negative, in 31.
-        auto dist = [&](int64_t Kr, int64_t M, int32_t dot) -> int32_t {
+        // The table index min(M - score(dot), last); NARROW: the score is the low word of the
+        // 64-bit shift (one shift of the high word when ss >= 32, a funnel shift below).
+        auto dist = [&](int64_t M, int32_t dot) -> int32_t {
             if constexpr (NARROW) {
-                const int64_t t = Kr - (int64_t)dot * (int64_t)sm;
-                int32_t dd;
-                if constexpr (SSHI) dd = (int32_t)(t >> 32) >> (ss - 32);
-                else dd = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+                const int64_t t = (int64_t)dot * (int64_t)sm + hround;
+                int32_t score;
+                if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
+                else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+                const int32_t dd = (int32_t)M - score;
                 return (uint32_t)dd < (uint32_t)last ? dd : last;
             } else {
                 return dist_of<false>(M, dot, sm, ss, fast, hround, last);
             }
-        };
-        auto row_const = [&](int64_t M) -> int64_t {
-            if (!NARROW || M == INT64_MIN) return 0;  // a row without keys: its indices are never used
-            return (int64_t)((uint64_t)M << ss) + ((int64_t)1 << ss) - 1 - hround;
         };
         int it = 0;
         // Pass 1: the max and min dot over the row's causal keys.
@@ -321,7 +315,6 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
             M = s1 > s2 ? s1 : s2;
         }
-        const int64_t Kr = row_const(M);
         // Pass 2: the row sum of e.
         mbar_wait(&bars->t_full, 0, err, 26);
         uint64_t sum = 0;
@@ -339,18 +332,15 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             if (j0 > wlast) {
                 // masked for every lane
             } else if (j0 + 31 <= rpos) {
-                // Four partial sums: independent chains for the look-ups and adds. The entries
-                // are in [0, 2^31) (the loader checks it), so a pair adds in 32 bits.
+                // Four partial sums: independent chains for the look-ups and adds.
                 uint64_t ps[4] = {0, 0, 0, 0};
 #pragma unroll
-                for (int q = 0; q < 32; q += 2)
-                    ps[(q >> 1) & 3] += (uint32_t)sT[dist(Kr, M, (int32_t)v[q])] +
-                                        (uint32_t)sT[dist(Kr, M, (int32_t)v[q + 1])];
+                for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[dist(M, (int32_t)v[q])];
                 sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             } else {
 #pragma unroll
                 for (int q = 0; q < 32; q++)
-                    if (j0 + q <= rpos) sum += (uint32_t)sT[dist(Kr, M, (int32_t)v[q])];
+                    if (j0 + q <= rpos) sum += (uint32_t)sT[dist(M, (int32_t)v[q])];
             }
         }
         named_bar(1, ETH);  // everyone has read sX (pass 1) before it is reused
@@ -384,7 +374,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             mbar_arrive(&bars->s_empty[sb]);
             const int j0 = c * KC + qt * 32;
             auto prob = [&](int32_t dot) -> uint32_t {
-                const uint32_t e = (uint32_t)sT[dist(Kr, M, dot)];
+                const uint32_t e = (uint32_t)sT[dist(M, dot)];
                 const uint64_t t = (uint64_t)e * ml;
                 const uint64_t u = (uint64_t)e * mh + (t >> 32);
                 return (uint32_t)(u >> psh);
@@ -573,14 +563,13 @@ __global__ void __launch_bounds__(32 * DEC_WARPS, 5) k_attention_dec(const RowIn
     const int32_t last = (tlen < TABLE_MAX ? tlen : TABLE_MAX) - 1;
     const int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
     const int64_t M = s1 > s2 ? s1 : s2;
-    // The row constant of k_attention_tc: M - score(dot) = (Kr - dot sm) >> ss (NARROW).
-    const int64_t Kr = NARROW ? (int64_t)((uint64_t)M << ss) + ((int64_t)1 << ss) - 1 - hround : 0;
     auto dist = [&](int32_t dot) -> int32_t {
         if constexpr (NARROW) {
-            const int64_t t = Kr - (int64_t)dot * (int64_t)sm;
-            int32_t dd;
-            if constexpr (SSHI) dd = (int32_t)(t >> 32) >> (ss - 32);
-            else dd = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+            const int64_t t = (int64_t)dot * (int64_t)sm + hround;
+            int32_t score;
+            if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
+            else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+            const int32_t dd = (int32_t)M - score;
             return (uint32_t)dd < (uint32_t)last ? dd : last;
         } else {
             return dist_of<false>(M, dot, sm, ss, fast, hround, last);

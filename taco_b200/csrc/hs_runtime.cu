@@ -1515,11 +1515,12 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         (rc = dalloc(&b->dbuf, R * c.d, b->owned)) ||
         (rc = dalloc(&b->intervals, 3 * R, b->owned)))
         return rc;
-    // The chunk of the LM head: HS_LOGIT_CHUNK rows (a multiple of 128; 768 by default: 6 x 197
-    // GEMM tiles are 8 full waves on 148 SMs, and the 78 MB of distances stay in the 126 MB L2
-    // with the 39 MB of wte), at most the pass.
+    // The chunk of the LM head: the whole pass by default. Chunks small enough for their
+    // distances to stay in L2 (HS_LOGIT_CHUNK rows, a multiple of 128) were measured slower on a
+    // B200: at 512, 768 and 1024 rows the fold ran at 6.8, 7.0 and 7.3 MB/s against 8.1 MB/s
+    // unchunked, the logits GEMM and the coder paying their start-up and last wave per chunk.
     {
-        int ch = 768;
+        int ch = (int)R;
         if (const char* v = getenv("HS_LOGIT_CHUNK")) ch = std::max(128, atoi(v) / 128 * 128);
         b->lchunk = (int)std::min<size_t>(R, (size_t)ch);
     }
