@@ -26,6 +26,7 @@
 #include <condition_variable>
 #include <mutex>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -895,10 +896,18 @@ int fold_many(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, s
         return hs::host_fail(HS_INVALID_OVERLAP, "the overlap must be at most n_ctx - 2");
     uint8_t hash[32];
     hs::sha256(model_file, model_len, hash);  // the model hash of the container (model.rs:359)
-    MultiGpu gpu({ordinals, n_gpus, model_file, model_len, hash, vocab, eot, n_ctx, slots, max_rows, opt->overlap});
+    // HS_FOLD_WORKERS_PER_GPU (default 1): host threads per GPU, each with its own batch, so that
+    // one thread's host work between its rounds (rows, planning, range coding) overlaps another
+    // thread's passes on the same GPU.
+    uint32_t per = 1;
+    if (const char* v = getenv("HS_FOLD_WORKERS_PER_GPU")) per = (uint32_t)std::min(8, std::max(1, atoi(v)));
+    std::vector<int> ords;
+    for (uint32_t k = 0; k < per; k++) ords.insert(ords.end(), ordinals, ordinals + n_gpus);
+    MultiGpu gpu({ords.data(), (uint32_t)ords.size(), model_file, model_len, hash, vocab, eot, n_ctx, slots,
+                  max_rows, opt->overlap});
     if ((rc = gpu.start())) return rc;
     rc = fold_stream_impl(hash, eot, n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
-    if (!rc && stats) stats->gpus_failed = gpu.failed();
+    if (!rc && stats) stats->gpus_failed = gpu.failed() / per;  // a GPU's workers fail together
     return rc;
 }
 
