@@ -204,9 +204,9 @@ def rooflines(prof: dict, info, peak_tops: float | None, hbm_gbs: float | None, 
     gemm_keys = [k for k in prof if k.startswith("gemm")]
     add("gemm", gemm_keys, "tensor", sum(prof[k]["ops"] for k in gemm_keys), "TOP/s")
     add("attention", ["attention"], "tensor", prof["attention"]["ops"], "TOP/s")
-    # LayerNorm: each of the 2L + 1 reads x and writes a (5d bytes per row); the residual adds
-    # are in the proj and mlp GEMM epilogues.
-    add("layernorm", ["layernorm"], "hbm", rows * d * 5 * (2 * L + 1), "GB/s")
+    # LayerNorm: layer 0's first one reads x and writes a (5d bytes per row); the other 2L ones
+    # also read the residual delta and write x back (13d bytes per row).
+    add("layernorm", ["layernorm"], "hbm", rows * d * (5 + 13 * 2 * L), "GB/s")
     # The coder op: the row's logit distances (2V bytes) and tile maxima (8 per 128 symbols) in,
     # one interval (24 bytes) out.
     add("coder", ["coder"], "hbm", rows * (2 * V + 8 * vt + 24), "GB/s")
@@ -783,7 +783,7 @@ def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int]) -> dict:
             "fold_stages_ms": {k: round(stats[k], 1) for k in ("prep_ms", "gpu_ms", "finish_ms")},
             "unfold_wall_s": round(unfold_s, 3), "unfold_MB_per_s": len(data) / unfold_s / 1e6,
             "gpus_failed": stats["gpus_failed"], "host_cores": os.cpu_count(),
-            "workers_per_gpu": int(os.environ.get("HS_FOLD_WORKERS_PER_GPU", "1"))}
+            "workers_per_gpu": int(os.environ.get("HS_FOLD_WORKERS_PER_GPU", "2"))}
 
 
 if __name__ == "__main__":

@@ -449,12 +449,6 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                             o[q] = (int32_t)clamp128(rescale128(value(vh[q], vl[q], c0 + q) + pc[c0 + q], pm[c0 + q],
                                                                 (uint32_t)s),
                                                      INT32_MIN, INT32_MAX);
-                        if (e.x) {  // the residual add, as in the 8-bit path
-                            const int32_t* xr = e.x + (size_t)row * e.ldx + colb;
-#pragma unroll
-                            for (int q = 0; q < 32; q++)
-                                o[q] = (int32_t)clamp64((int64_t)xr[q] + o[q], -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-                        }
                         uint4 blk[8];
 #pragma unroll
                         for (int j = 0; j < 8; j++) blk[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
@@ -731,36 +725,10 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                         }
                     } else if (MODE == EPI_DELTA) {
                         int32_t o[32];
-                        if (e.x) {
-                            // The residual add of the next LayerNorm, done here: x = clamp(x + y,
-                            // +-RESIDUAL_LIMIT) (gpt2/ops.rs residual; the oracle's c_proj / mlp
-                            // step). Rows past R read and write the buffer's padding rows.
-                            const int4* xr = reinterpret_cast<const int4*>(e.x + (size_t)row * e.ldx + colb);
-                            int32_t xv[32];
 #pragma unroll
-                            for (int j = 0; j < 8; j++) {
-                                const int4 t4 = xr[j];
-                                xv[4 * j] = t4.x;
-                                xv[4 * j + 1] = t4.y;
-                                xv[4 * j + 2] = t4.z;
-                                xv[4 * j + 3] = t4.w;
-                            }
-#pragma unroll
-                            for (int q = 0; q < 32; q++) {
-                                if constexpr (S32) {
-                                    const int32_t t = xv[q] + y32[q];  // |x| < 2^30, |y| < 2^30
-                                    o[q] = min(max(t, -RESIDUAL_LIMIT), RESIDUAL_LIMIT);
-                                } else {
-                                    o[q] = (int32_t)clamp64((int64_t)xv[q] + clamp64(Y(q), INT32_MIN, INT32_MAX),
-                                                            -RESIDUAL_LIMIT, RESIDUAL_LIMIT);
-                                }
-                            }
-                        } else {
-#pragma unroll
-                            for (int q = 0; q < 32; q++) {
-                                if constexpr (S32) o[q] = y32[q];
-                                else o[q] = (int32_t)clamp64(Y(q), INT32_MIN, INT32_MAX);
-                            }
+                        for (int q = 0; q < 32; q++) {
+                            if constexpr (S32) o[q] = y32[q];
+                            else o[q] = (int32_t)clamp64(Y(q), INT32_MIN, INT32_MAX);
                         }
                         uint4 blk[8];
 #pragma unroll

@@ -217,6 +217,7 @@ struct hs_batch {
     // Version 2: the lo planes of the i16 ln_f output and of the i16 GELU outputs.
     int8_t* a_lo = nullptr;
     int8_t* g_lo = nullptr;
+    int32_t* dbuf = nullptr;  // the residual delta of the last proj/mlp GEMM
     // The logits of the mixed coder op (a whole pass; made on the first mixed call).
     uint16_t* d16 = nullptr;
     int64_t* tmax = nullptr;
@@ -275,7 +276,7 @@ struct hs_batch {
     alignas(128) CUtensorMap tm_q;   // qkv rows, 64-byte boxes (attention Q)
     alignas(128) CUtensorMap tm_k;   // the keys cache
     alignas(128) CUtensorMap tm_v;   // the transposed values cache
-    alignas(128) CUtensorMap ts_x;      // epilogue stores: the residual stream x (i32)
+    alignas(128) CUtensorMap ts_delta;  // epilogue stores: the residual delta (i32)
     alignas(128) CUtensorMap ts_g;      // the GELU output (i8)
     alignas(128) CUtensorMap ts_d16;    // the logit distances (u16) of the mixed op
     alignas(128) CUtensorMap ts_d16c;   // the logit distances (u16) of a chunk
@@ -423,7 +424,7 @@ int forward(hs_batch* b, int R) {
             launch_gemm_tc(mode, tmA, tmA2 ? &W.tm128 : &W.tm, tmC, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms,
                            m->dev->d_err, st, tmA2);
         else
-            launch_gemm_simple(mode == EPI_DELTA && e.x ? EPI_RESID : mode, A, lda, R, W.ld, e, st);
+            launch_gemm_simple(mode, A, lda, R, W.ld, e, st);
     };
     for (int l = 0; l < c.L; l++) {
         const LayerDev& Ld = m->layers[l];
@@ -432,9 +433,10 @@ int forward(hs_batch* b, int R) {
         const DevLinear& fc = *m->lins[4 * l + 2];
         const DevLinear& mlp = *m->lins[4 * l + 3];
         {
-            // The residual of the previous layer's MLP is already in x (its GEMM epilogue adds it).
+            // The residual of the previous layer's MLP joins x here (none before layer 0).
             ProfScope p(b, OP_LN, 0);
-            launch_resid_layernorm(b->x, nullptr, R, c.d, Ld.ln1, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+            launch_resid_layernorm(b->x, l == 0 ? nullptr : b->dbuf, R, c.d, Ld.ln1, c.ln_k, c.ln_j, c.ln_eps, b->a,
+                                   c.Dp, st);
         }
         EpiArgs e{};
         e.R = R;
@@ -488,15 +490,12 @@ int forward(hs_batch* b, int R) {
         e.b = proj.ld.b;
         e.m = proj.ld.m;
         e.s = proj.ld.s;
-        // The residual add joins the epilogue: x += rescale(att . W^T) (saturating), stored back.
-        e.x = b->x;
-        e.ldx = c.d;
-        e.out32 = b->x;
+        e.out32 = b->dbuf;
         e.ldo = c.d;
-        gemm(OP_GEMM_PROJ, EPI_DELTA, b->att, c.Dp, &b->tm_att, proj, e, &b->ts_x);
+        gemm(OP_GEMM_PROJ, EPI_DELTA, b->att, c.Dp, &b->tm_att, proj, e, &b->ts_delta);
         {
             ProfScope p(b, OP_LN, 0);
-            launch_resid_layernorm(b->x, nullptr, R, c.d, Ld.ln2, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
+            launch_resid_layernorm(b->x, b->dbuf, R, c.d, Ld.ln2, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st);
         }
         e = EpiArgs{};
         e.R = R;
@@ -522,15 +521,13 @@ int forward(hs_batch* b, int R) {
         e.b = mlp.ld.b;
         e.m = mlp.ld.m;
         e.s = mlp.ld.s;
-        e.x = b->x;
-        e.ldx = c.d;
-        e.out32 = b->x;
+        e.out32 = b->dbuf;
         e.ldo = c.d;
-        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e, &b->ts_x, gwide ? &b->tm_g_lo : nullptr);
+        gemm(OP_GEMM_MLP, EPI_DELTA, b->g, c.Fp, &b->tm_g, mlp, e, &b->ts_delta, gwide ? &b->tm_g_lo : nullptr);
     }
     {
         ProfScope p(b, OP_LN, 0);
-        launch_resid_layernorm(b->x, nullptr, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st,
+        launch_resid_layernorm(b->x, b->dbuf, R, c.d, m->lnf, c.ln_k, c.ln_j, c.ln_eps, b->a, c.Dp, st,
                                c.lnf_wide ? b->a_lo : nullptr);
     }
     return HS_OK;
@@ -1515,6 +1512,7 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         (rc = dalloc(&b->d_rows, R, b->owned)) || (rc = dalloc(&b->x, R * c.d, b->owned)) ||
         (rc = dalloc(&b->a, R * c.Dp, b->owned)) || (rc = dalloc(&b->qkv, R * c.QKVp, b->owned)) ||
         (rc = dalloc(&b->att, R * c.Dp, b->owned)) || (rc = dalloc(&b->g, R * c.Fp, b->owned)) ||
+        (rc = dalloc(&b->dbuf, R * c.d, b->owned)) ||
         (rc = dalloc(&b->intervals, 3 * R, b->owned)))
         return rc;
     // The chunk of the LM head: the whole pass by default. Chunks small enough for their
@@ -1548,10 +1546,10 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
     b->h_rowlist = b->h_rowlist_base;
     b->h_rows = b->h_rows_base;
     b->h_intervals = b->h_intervals_base;
-    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 4 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 24 + (c.lnf_wide ? c.Dp : 0) +
+    b->bytes = 2 * cache + R * (sizeof(RowInfo) + 8 * c.d + 2 * c.Dp + c.QKVp + c.Fp + 24 + (c.lnf_wide ? c.Dp : 0) +
                                 (gelu_wide ? c.Fp : 0)) +
                LC * (2 * c.Vp + 8 * c.VT);
-    if ((rc = make_store_tmap(m->dev, &b->ts_x, b->x, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d, 128)) ||
+    if ((rc = make_store_tmap(m->dev, &b->ts_delta, b->dbuf, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, R, c.d, c.d, 128)) ||
         (rc = make_store_tmap(m->dev, &b->ts_g, b->g, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, c.f, c.Fp, 32)) ||
         (rc = make_store_tmap(m->dev, &b->ts_d16c, b->d16c, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (int)LC, c.V, c.Vp,
                               128)))
