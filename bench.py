@@ -385,16 +385,18 @@ def main():
 
     # The unfold on every GPU at once (configs[3] at N GPUs): each rank decodes its own coded
     # blocks with the device range decoder, timed between barriers, the max over ranks.
-    ub = unfold_blocks(B, model, lens)
-    ub_batch = B.CudaBatch(model, 1024, 4096)
-    unfold_blocks(B, model, lens, timed_only=True, batch=ub_batch)  # warm
-    barrier()
-    t0 = time.perf_counter()
-    ub_timed = unfold_blocks(B, model, lens, timed_only=True, batch=ub_batch)
-    ub_wall = time.perf_counter() - t0
-    barrier()
-    ub_batch.close()
-    (ub_max,) = shard.max_over_ranks([ub_wall], device=f"cuda:{local}")
+    ub = ub_timed = None
+    if not args.no_extras:
+        ub = unfold_blocks(B, model, lens)
+        ub_batch = B.CudaBatch(model, 1024, 4096)
+        unfold_blocks(B, model, lens, timed_only=True, batch=ub_batch)  # warm
+        barrier()
+        t0 = time.perf_counter()
+        ub_timed = unfold_blocks(B, model, lens, timed_only=True, batch=ub_batch)
+        ub_wall = time.perf_counter() - t0
+        barrier()
+        ub_batch.close()
+        (ub_max,) = shard.max_over_ranks([ub_wall], device=f"cuda:{local}")
 
     result = None
     failed = False
@@ -434,13 +436,15 @@ def main():
             "clocks": clk,
             "gpu_launches": launches,
             "kernels": kernels,
-            "unfold_gpus": {"n_gpus": world, "streams_per_gpu": ub_timed["streams"],
-                            "tokens_per_block": ub_timed["tokens_per_block"],
-                            "e2e_tokens_per_s": world * ub_timed["tokens"] / ub_max,
-                            "e2e_MB_per_s": world * ub_timed["bytes"] / ub_max / 1e6,
-                            "timing": "wall clock of one hs_batch_decode_blocks call per rank between barriers, "
-                                      "max over ranks"},
         }
+        if ub_timed:
+            result["unfold_gpus"] = {
+                "n_gpus": world, "streams_per_gpu": ub_timed["streams"], "tokens_per_block": ub_timed["tokens_per_block"],
+                "e2e_tokens_per_s": world * ub_timed["tokens"] / ub_max,
+                "e2e_MB_per_s": world * ub_timed["bytes"] / ub_max / 1e6,
+                "timing": "wall clock of one hs_batch_decode_blocks call per rank (its batch made beforehand) between "
+                          "barriers, max over ranks",
+                "per_rank_first_call": {k: ub[k] for k in ("e2e_tokens_per_s", "device_tokens_per_s")}}
         # Parity on the bench's own shape: the intervals of the first windows of the last warm-up
         # step (512 slots, passes of max_rows rows) against the oracle's, field by field.
         threads = args.cpu_threads or os.cpu_count() or 1
@@ -456,7 +460,6 @@ def main():
         failed = bool(bad.any())
         if world == 1 and not args.no_cpu:
             result["cpu_baseline"] = {k: v for k, v in ora.items() if k != "answers"}
-        result["unfold_gpus"]["per_rank_first_call"] = {k: ub[k] for k in ("e2e_tokens_per_s", "device_tokens_per_s")}
 
     # Extras: the GEMM microbench, the unfold sweep and the CPU unfold.
     if rank == 0 and not args.no_extras:
