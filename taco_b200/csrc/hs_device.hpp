@@ -141,6 +141,9 @@ struct EpiArgs {
     // (vt_run) goes here, row-major with stride ldv, for launch_v_scatter to place in vc.
     int8_t* vstage;
     int ldv;
+    // EPI_QKV: whole 32 x 32-byte pieces of q, and of k and v for 32-row prefill runs, leave
+    // through the TMA store maps that the launch passes (the batch made them).
+    int kv_tma;
     // The first row of A that this launch reads (row tile mt reads A rows a_row0 + 128 mt ...);
     // the outputs are written from row 0. The LM head runs in row chunks with it.
     int a_row0;

@@ -55,9 +55,10 @@ struct Cfg {
     static constexpr int EPI_WARPS = MODE == EPI_QKV ? 12 : 8;
     static constexpr int EPI_THREADS = 32 * EPI_WARPS;
     static constexpr int THREADS = 64 + EPI_THREADS;
-    static constexpr int STAGES = (MODE == EPI_GELU || MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 3 : 4;
+    static constexpr int STAGES = (MODE == EPI_GELU || MODE == EPI_DELTA || MODE == EPI_LOGITS || MODE == EPI_QKV) ? 3 : 4;
     static constexpr int EXTRA = MODE == EPI_GELU ? GELU_SMEM : (MODE == EPI_QKV ? EPI_WARPS * VT_TILE : 0);
-    static constexpr int STORE_WARP = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 8192 : (MODE == EPI_GELU ? 1024 : 0);
+    static constexpr int STORE_WARP =
+        (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 8192 : (MODE == EPI_GELU ? 1024 : (MODE == EPI_QKV ? 2048 : 0));
     static constexpr int WSUM = (MODE == EPI_DELTA || MODE == EPI_LOGITS) ? 2 * BN * 8 : 0;  // s_w (WIDE)
     static constexpr size_t SMEM =
         (size_t)STAGES * STAGE_BYTES + EXTRA + EPI_WARPS * STORE_WARP + 2 * BN * 12 + WSUM + 256 + 1024;
@@ -144,7 +145,8 @@ __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowIn
 template <int MODE, bool S32, bool WIDE>
 __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
-              const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC, int MT, int NT,
+              const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
+              const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, int MT, int NT,
               int KB, EpiArgs e, int* err) {
     constexpr int STAGES = Cfg<MODE>::STAGES;
     constexpr int EPI_WARPS = Cfg<MODE>::EPI_WARPS;
@@ -168,6 +170,11 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
         prefetch_tmap(&tmA);
         if (WIDE) prefetch_tmap(&tmA2);
         prefetch_tmap(&tmB);
+        if (MODE == EPI_QKV && e.kv_tma) {
+            prefetch_tmap(&tmC);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+        }
         for (int s = 0; s < STAGES; s++) {
             mbar_init(&bars->full[s], 1);
             mbar_init(&bars->empty[s], 1);
@@ -294,6 +301,24 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                 tma_store_2d(&tmC, my_store, x, y);
                 bulk_commit();
             }
+        };
+        // EPI_QKV: one 32-row x 32-byte piece through the TMA store map `map` (the 32-byte swizzle),
+        // alternating between two 1 KB buffers. Warp-collective.
+        uint32_t qpieces = 0;
+        auto store_piece2 = [&](const CUtensorMap* map, const uint32_t (&pk)[8], int x, int y) {
+            uint8_t* buf = my_store + (qpieces & 1) * 1024;
+            if (lane == 0) bulk_wait_read1();  // the store that last used this buffer has read it
+            __syncwarp();
+            const uint32_t sw = (uint32_t)((lane >> 2) & 1);
+            *reinterpret_cast<uint4*>(buf + lane * 32 + (sw << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            *reinterpret_cast<uint4*>(buf + lane * 32 + ((sw ^ 1) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(map, buf, x, y);
+                bulk_commit();
+            }
+            qpieces++;
         };
         // One 32-row x 128-byte block (this lane's row: 8 x 16 bytes) through TMA at element column
         // x and row y (the 128-byte swizzle), alternating between two buffers. Warp-collective.
@@ -586,7 +611,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                     if (colb >= e.N) continue;
                     // GELU and DELTA store through TMA (warp-collective): rows past R land in the
                     // padding rows of the output, which nothing reads.
-                    if (MODE != EPI_GELU && MODE != EPI_DELTA && !row_ok) continue;
+                    // EPI_QKV: the TMA stores are warp-collective too; its other stores check row_ok.
+                    if (MODE != EPI_GELU && MODE != EPI_DELTA && MODE != EPI_QKV && !row_ok) continue;
                     const bool full = colb + 32 <= e.N;
                     // The rescaled values: 32-bit on the S32 path, computed for the whole chunk.
                     int32_t y32[32];
@@ -599,11 +625,51 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                         else return rescale_fast(v[q], pm[c0 + q], pc[c0 + q], s, fast);
                     };
                     if (MODE == EPI_QKV) {
-                        const RowInfo ri = e.rows[row];
+                        const RowInfo ri = e.rows[row];  // rows past R read stale entries of the table
                         int8_t o[32];
 #pragma unroll
                         for (int q = 0; q < 32; q++)
                             o[q] = (int8_t)clamp_e(Y(q), -127, 127);
+                        uint32_t pk[8];
+#pragma unroll
+                        for (int q = 0; q < 8; q++)
+                            pk[q] = (uint32_t)(uint8_t)o[4 * q] | (uint32_t)(uint8_t)o[4 * q + 1] << 8 |
+                                    (uint32_t)(uint8_t)o[4 * q + 2] << 16 | (uint32_t)(uint8_t)o[4 * q + 3] << 24;
+                        // The 32 x 32-byte pieces of whole runs leave by TMA (kv_tma): q rows to the qkv
+                        // buffer (rows past R land in its padding rows), and, for a warp whose 32 rows
+                        // are 32 consecutive positions of one slot, key rows and the transposed value
+                        // rows straight into the caches.
+                        if (e.kv_tma && full && colb + 32 <= e.d) {
+                            store_piece2(&tmC, pk, colb, mt * BM + g * 32);
+                            continue;
+                        }
+                        if (e.kv_tma && full && vt_ok && colb >= e.d && colb < 2 * e.d) {
+                            const int j = colb - e.d, h = j / e.hd, c = j - h * e.hd;
+                            const size_t head = ((size_t)vt_slot * e.L + e.layer) * e.H + h;
+                            store_piece2(&tmK, pk, c, (int)(head * e.n_ctx + vt_pos0));
+                            continue;
+                        }
+                        if (e.kv_tma && full && vt_ok && colb >= 2 * e.d) {
+                            // The 32 x 32 transpose through shared memory; lane l then holds the 32
+                            // positions of channel colb - 2d + l, which leave as one TMA piece.
+                            uint8_t* tile = reinterpret_cast<uint8_t*>(s_gelu) + (warp - 2) * VT_TILE;
+#pragma unroll
+                            for (int q = 0; q < 8; q++) *reinterpret_cast<uint32_t*>(tile + lane * VT_STRIDE + 4 * q) = pk[q];
+                            __syncwarp();
+                            uint32_t tk[8];
+#pragma unroll
+                            for (int q = 0; q < 8; q++)
+                                tk[q] = (uint32_t)tile[(4 * q) * VT_STRIDE + lane] |
+                                        (uint32_t)tile[(4 * q + 1) * VT_STRIDE + lane] << 8 |
+                                        (uint32_t)tile[(4 * q + 2) * VT_STRIDE + lane] << 16 |
+                                        (uint32_t)tile[(4 * q + 3) * VT_STRIDE + lane] << 24;
+                            __syncwarp();
+                            const int j = colb - 2 * e.d, h = j / e.hd, c = j - h * e.hd;
+                            const size_t head = ((size_t)vt_slot * e.L + e.layer) * e.H + h;
+                            store_piece2(&tmV, tk, (int)vt_pos0, (int)(head * e.hd + c));
+                            continue;
+                        }
+                        if (!row_ok) continue;
                         if (full && colb + 32 <= e.d && (e.ldo & 15) == 0) {
                             // A whole 32-byte run of q.
                             uint32_t pk[8];
@@ -757,22 +823,24 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
 }
 
 template <int MODE>
-void launch_mode(const void* tmA, const void* tmA2, const void* tmB, const void* tmC, int MT, int NT, int KB,
-                 const EpiArgs& e, int grid, int* err, cudaStream_t st) {
+void launch_mode(const void* tmA, const void* tmA2, const void* tmB, const void* tmC, const void* tmK,
+                 const void* tmV, int MT, int NT, int KB, const EpiArgs& e, int grid, int* err, cudaStream_t st) {
     const CUtensorMap& a = *reinterpret_cast<const CUtensorMap*>(tmA);
     const CUtensorMap& b = *reinterpret_cast<const CUtensorMap*>(tmB);
     const CUtensorMap& c = *reinterpret_cast<const CUtensorMap*>(tmC ? tmC : tmB);
+    const CUtensorMap& k = *reinterpret_cast<const CUtensorMap*>(tmK ? tmK : tmB);
+    const CUtensorMap& v = *reinterpret_cast<const CUtensorMap*>(tmV ? tmV : tmB);
     if constexpr (MODE == EPI_DELTA || MODE == EPI_LOGITS) {
         if (tmA2) {
             const CUtensorMap& a2 = *reinterpret_cast<const CUtensorMap*>(tmA2);
-            k_gemm_tc<MODE, false, true><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a2, b, c, MT, NT, KB, e, err);
+            k_gemm_tc<MODE, false, true><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a2, b, c, k, v, MT, NT, KB, e, err);
             return;
         }
     }
     if (MODE != EPI_RAW && e.small && e.s >= 0 && e.s <= 62)
-        k_gemm_tc<MODE, true, false><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, true, false><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, k, v, MT, NT, KB, e, err);
     else
-        k_gemm_tc<MODE, false, false><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, MT, NT, KB, e, err);
+        k_gemm_tc<MODE, false, false><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, k, v, MT, NT, KB, e, err);
 }
 
 template <int MODE>
@@ -803,19 +871,20 @@ cudaError_t configure_tc_kernels() {
 }
 
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
-                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2) {
+                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2, const void* tmK,
+                    const void* tmV) {
     if (R <= 0) return;
     int MT = (R + BM - 1) / BM, NT = Np / (tmA2 ? 128 : BN), KB = Kp / BK;
     int tiles = MT * NT;
     int grid = tiles < num_sms ? tiles : num_sms;
     switch (mode) {
-        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
-        case EPI_GELU16: launch_mode<EPI_GELU16>(tmA, tmA2, tmB, tmC, MT, NT, KB, e, grid, err, st); break;
+        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_GELU16: launch_mode<EPI_GELU16>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
         default: break;
     }
 }

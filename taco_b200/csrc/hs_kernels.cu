@@ -54,8 +54,8 @@ __device__ uint64_t block_sum64(uint64_t v, uint64_t* sh) {
 
 __global__ void k_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const int32_t* em, int es,
                         const int8_t* wpe, const int32_t* pm, int ps, int d, int32_t* x) {
-    int r = blockIdx.y;
-    int j = blockIdx.x * blockDim.x + threadIdx.x;
+    int r = blockIdx.x;  // rows in x: a pass can have more than 65,535 of them
+    int j = blockIdx.y * blockDim.x + threadIdx.x;
     if (r >= R || j >= d) return;
     uint32_t tok = rows[r].token, pos = rows[r].pos;
     int64_t a = rescale64(wte[(size_t)tok * ldw + j], em[tok], es);
@@ -422,8 +422,8 @@ __global__ void __launch_bounds__(256) k_gemm_simple(int mode, const int8_t* A, 
                                                      EpiArgs e) {
     __shared__ int4 sa[SG_ROWS][8];  // 8 rows x 128 bytes of K
     __shared__ int64_t red[SG_ROWS][8];
-    int n = blockIdx.x * 256 + threadIdx.x;
-    int r0 = blockIdx.y * SG_ROWS;
+    int n = blockIdx.y * 256 + threadIdx.x;
+    int r0 = blockIdx.x * SG_ROWS;  // row groups in x: up to 2^20 rows
     int32_t acc[SG_ROWS];
 #pragma unroll
     for (int i = 0; i < SG_ROWS; i++) acc[i] = 0;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const RowInfo* rows, 
     __shared__ uint64_t redu[32];
     __shared__ int8_t q[1024];
     __shared__ int64_t part[ATT_THREADS];
-    int h = blockIdx.x, r = rowlist ? rowlist[blockIdx.y] : (int)blockIdx.y;
+    int h = blockIdx.y, r = rowlist ? rowlist[blockIdx.x] : (int)blockIdx.x;
     if (r >= R) return;
     uint32_t slot = rows[r].slot;
     int n = (int)rows[r].pos + 1;
@@ -615,7 +615,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention_vec(const RowInfo* ro
     int4* s_dig = reinterpret_cast<int4*>(smem_att + 8 * (size_t)n_ctx);  // n_ctx / 4 quads x 4 planes
     __shared__ int64_t red[32];
     __shared__ uint64_t redu[32];
-    const int h = blockIdx.x, r = rowlist ? rowlist[blockIdx.y] : (int)blockIdx.y;
+    const int h = blockIdx.y, r = rowlist ? rowlist[blockIdx.x] : (int)blockIdx.x;
     if (r >= R) return;
     const uint32_t slot = rows[r].slot;
     const int n = (int)rows[r].pos + 1;
@@ -1486,7 +1486,7 @@ cudaError_t configure_core_kernels() {
 void launch_embed(const RowInfo* rows, int R, const int8_t* wte, int ldw, const int32_t* em, int es,
                   const int8_t* wpe, const int32_t* pm, int ps, int d, int32_t* x, cudaStream_t st) {
     if (R <= 0) return;
-    dim3 grid((d + 255) / 256, R);
+    dim3 grid(R, (d + 255) / 256);
     k_embed<<<grid, 256, 0, st>>>(rows, R, wte, ldw, em, es, wpe, pm, ps, d, x);
 }
 
@@ -1519,7 +1519,7 @@ void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, cons
 void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearDev& W, const EpiArgs& e,
                         cudaStream_t st) {
     if (R <= 0) return;
-    dim3 grid(W.Np / 256, (R + SG_ROWS - 1) / SG_ROWS);
+    dim3 grid((R + SG_ROWS - 1) / SG_ROWS, W.Np / 256);
     k_gemm_simple<<<grid, 256, 0, st>>>(mode, A, lda, R, W, e);
 }
 
@@ -1535,7 +1535,7 @@ void launch_attention(const RowInfo* rows, int R, const int* rowlist, int n, con
                       int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att,
                       int lda, cudaStream_t st) {
     if (R <= 0 || n <= 0) return;
-    dim3 grid(H, n);
+    dim3 grid(n, H);  // rows in x (a pass can have more than 65,535), heads in y
     // The vector kernel needs 16-byte aligned q rows and 4-byte aligned value rows.
     bool vec_ok = (n_ctx % 4) == 0 && (ldq % 16) == 0;
     size_t vsmem = 8 * (size_t)n_ctx + 16 * (size_t)(n_ctx / 4 + 1);

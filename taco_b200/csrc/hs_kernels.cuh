@@ -48,8 +48,12 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
 // the other modes take nullptr.
 // tmA2 != nullptr (EPI_DELTA and EPI_LOGITS of version 2 models): tmA and tmA2 are the hi and lo
 // planes of i16 activations, tmB has 128-row boxes and the tiles are 128 x 128.
+// EPI_QKV with e.kv_tma: tmC, tmK and tmV are the 32-row x 32-byte store maps (32-byte swizzle) of
+// the qkv buffer, the keys cache [heads * n_ctx, hd] and the transposed values cache
+// [heads * hd, n_ctx].
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
-                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2 = nullptr);
+                    const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2 = nullptr,
+                    const void* tmK = nullptr, const void* tmV = nullptr);
 
 #ifdef __CUDACC__
 // vt_run_host for the warp whose lane l holds row r0 + l (warp-uniform result).

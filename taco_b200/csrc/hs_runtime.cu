@@ -278,6 +278,10 @@ struct hs_batch {
     alignas(128) CUtensorMap tm_v;   // the transposed values cache
     alignas(128) CUtensorMap ts_delta;  // epilogue stores: the residual delta (i32)
     alignas(128) CUtensorMap ts_g;      // the GELU output (i8)
+    // The QKV epilogue's stores (32 x 32-byte boxes): q into the qkv buffer, keys and transposed
+    // values into the caches; kv_tma when they exist (the cache layouts allow them).
+    alignas(128) CUtensorMap ts_q, ts_kc, ts_vt;
+    bool kv_tma = false;
     alignas(128) CUtensorMap ts_d16;    // the logit distances (u16) of the mixed op
     alignas(128) CUtensorMap ts_d16c;   // the logit distances (u16) of a chunk
     alignas(128) CUtensorMap tm_a_lo;   // version 2: the lo plane of the ln_f output
@@ -420,9 +424,12 @@ int forward(hs_batch* b, int R) {
         ProfScope p(b, op, 2ULL * R * W.ld.N * W.ld.K);
         e.small = W.small ? 1 : 0;
         e.wsum = W.wsum;
+        const bool qkv_tma = mode == EPI_QKV && b->kv_tma;
+        e.kv_tma = qkv_tma ? 1 : 0;
         if (m->use_tc)
-            launch_gemm_tc(mode, tmA, tmA2 ? &W.tm128 : &W.tm, tmC, R, W.ld.Np, W.ld.Kp, e, m->dev->num_sms,
-                           m->dev->d_err, st, tmA2);
+            launch_gemm_tc(mode, tmA, tmA2 ? &W.tm128 : &W.tm, qkv_tma ? &b->ts_q : tmC, R, W.ld.Np, W.ld.Kp, e,
+                           m->dev->num_sms, m->dev->d_err, st, tmA2, qkv_tma ? &b->ts_kc : nullptr,
+                           qkv_tma ? &b->ts_vt : nullptr);
         else
             launch_gemm_simple(mode, A, lda, R, W.ld, e, st);
     };
@@ -1558,6 +1565,16 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         (rc = make_tmap(m->dev, &b->tm_att, b->att, R, c.Dp, TILE_M)) ||
         (rc = make_tmap(m->dev, &b->tm_g, b->g, R, c.Fp, TILE_M)))
         return rc;
+    if (m->use_tc && (c.n_ctx % 16) == 0 && (c.hd % 32) == 0 && (c.d % 32) == 0 && (c.QKVp % 16) == 0) {
+        const uint64_t heads = (uint64_t)slots * c.L * c.H;
+        if ((rc = make_store_tmap(m->dev, &b->ts_q, b->qkv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, R, 3 * c.d, c.QKVp, 32)) ||
+            (rc = make_store_tmap(m->dev, &b->ts_kc, b->kc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, heads * c.n_ctx, c.hd,
+                                  c.hd, 32)) ||
+            (rc = make_store_tmap(m->dev, &b->ts_vt, b->vc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, heads * c.hd, c.n_ctx,
+                                  c.n_ctx, 32)))
+            return rc;
+        b->kv_tma = getenv("HS_QKV_TMA") == nullptr || atoi(getenv("HS_QKV_TMA")) != 0;
+    }
     if (m->attn_tc) {
         uint64_t heads = (uint64_t)slots * c.L * c.H;
         if ((rc = make_tmap(m->dev, &b->tm_q, b->qkv, R, c.QKVp, 128, 64)) ||

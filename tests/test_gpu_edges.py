@@ -109,3 +109,25 @@ def test_coder_queries_at_the_ends_of_their_ranges(dev, mini, bits):
     assert np.array_equal(got["is_last"] != 0, want[:, 0] == om.vocab - 1)
     batch.close()
     model.close()
+
+
+def test_one_pass_of_more_than_65535_rows(dev):
+    """A pass of 70,400 rows (1,100 slots x 64 positions of the tiny model, max_rows 70,400): the
+    kernels index rows in the first grid dimension, so a pass may hold up to max_rows (2^20)
+    rows. Every coder answer equals the oracle's."""
+    slots, n = 1100, 64
+    rng = np.random.default_rng(65536)
+    toks = rng.integers(0, 299, (slots, n)).astype(np.uint32)
+    sl = np.repeat(np.arange(slots, dtype=np.uint32), n)
+    inputs = np.concatenate([np.full((slots, 1), 299, np.uint32), toks[:, :-1]], axis=1).reshape(-1)
+    coded = toks.reshape(-1).astype(np.uint64)
+    model = B.CudaModel(dev, tiny_bytes())
+    batch = B.CudaBatch(model, slots, slots * n)
+    try:
+        got = batch.run_coded(sl, inputs, np.zeros(sl.size, np.uint32), coded, 32)
+    finally:
+        batch.close()
+        model.close()
+    fb = O.FastBatch(O.Model(tiny_bytes()), slots, 0)
+    want = fb.run_coded(sl, inputs, np.zeros(sl.size, np.uint32), coded, 32)
+    _same(np.stack([got["symbol"], got["start"], got["freq"]], 1).astype(np.uint64), want)
