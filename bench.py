@@ -320,14 +320,14 @@ def main():
     step_bytes = int(lens[coded.astype(np.int64)].sum())
     if args.only:
         if args.only == "large_input":
-            print(json.dumps({"large_input": large_input(B, model_bytes, args.large_mb, [local])}))
+            print(json.dumps({"large_input": large_input(B, model_bytes, args.large_mb, [local], args.max_rows)}))
             return 0
         dev = B.CudaDevice(local)
         model = B.CudaModel(dev, model_bytes)
         if args.only == "fold_dual":
             print(json.dumps({"fold_dual": fold_dual(B, model, windows, lens, eot, sample=args.windows)}))
         else:
-            print(json.dumps({"fold_glue": fold_glue(B, model, model_bytes)}))
+            print(json.dumps({"fold_glue": fold_glue(B, model, model_bytes, args.max_rows)}))
         model.close()
         dev.close()
         return 0
@@ -475,7 +475,7 @@ def main():
             "note": "tokens/s of the device decoder (1,024 blocks x 256 tokens from position 0, wall clock) over the "
                     "CPU oracle's lockstep-lane decode from position 0 on all host threads"}
         result["fold_dual"] = fold_dual(B, model, windows, lens, eot)
-        result["fold_glue"] = fold_glue(B, model, model_bytes)
+        result["fold_glue"] = fold_glue(B, model, model_bytes, args.max_rows)
     batch.close()
     model.close()
     dev.close()
@@ -485,7 +485,7 @@ def main():
         if pg:
             torch.distributed.barrier()
         if rank == 0:
-            result["large_input"] = large_input(B, model_bytes, args.large_mb, list(range(world)))
+            result["large_input"] = large_input(B, model_bytes, args.large_mb, list(range(world)), args.max_rows)
         if pg:
             torch.distributed.barrier()
     if rank == 0:
@@ -709,7 +709,7 @@ def fold_dual(B, model, windows, lens, eot, sample: int = 64) -> dict:
     return out
 
 
-def fold_glue(B, model, model_bytes, mb: int = 2) -> dict:
+def fold_glue(B, model, model_bytes, max_rows: int, mb: int = 2) -> dict:
     """The fold and the unfold of the profile text end to end through the host library (hs_fold,
     hs_unfold: tokenizer, zstd level 19, the coder op on the GPU, range encoder, container) on `mb`
     MiB of seeded Zipf text, default block size 16 KiB. Timed by the wall clock (the better of
@@ -720,7 +720,7 @@ def fold_glue(B, model, model_bytes, mb: int = 2) -> dict:
 
     text = synth.zipf_text(mb << 20, seed=4242)[: mb << 20]
     tok = B.Tokenizer(model_bytes)
-    batch = B.CudaBatch(model, 512, 16384)
+    batch = B.CudaBatch(model, 512, max_rows)
     B.fold(batch, tok, text[:20000])  # warm-up
     wall = float("inf")
     for _ in range(2):
@@ -749,10 +749,10 @@ def fold_glue(B, model, model_bytes, mb: int = 2) -> dict:
             "unfold_e2e_MB_per_s": len(text) / uwall / 1e6}
 
 
-def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int]) -> dict:
+def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int], max_rows: int) -> dict:
     """`mb` MiB of the seeded mixed stream (70 % Zipf text, 20 % JSON key/number
     records, 10 % uniform random bytes, in 64 KiB pieces; synth.mixed_stream) folded by
-    hs_fold_multi on the GPUs `ordinals` (one host thread each; 512 slots, 16,384-row passes) and
+    hs_fold_multi on the GPUs `ordinals` (two host threads each; 512 slots, passes of max_rows) and
     unfolded by hs_unfold on the first; wall clock, the container's SHA-256, the stage times of the
     fold. The same bytes on every GPU count (tests/test_gpu_fold.py, tests/test_gpu_large_input.py
     check the equality with one GPU and with the CPU path on samples)."""
@@ -763,11 +763,11 @@ def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int]) -> dict:
     data = synth.mixed_stream(mb << 20)
     tok = B.Tokenizer(model_bytes)
     t0 = time.perf_counter()
-    got, stats = B.fold_multi(ordinals, model_bytes, tok, data, slots=512, max_rows=16384)
+    got, stats = B.fold_multi(ordinals, model_bytes, tok, data, slots=512, max_rows=max_rows)
     fold_s = time.perf_counter() - t0
     dev = B.CudaDevice(ordinals[0])
     model = B.CudaModel(dev, model_bytes)
-    batch = B.CudaBatch(model, 256, 16384)
+    batch = B.CudaBatch(model, 256, max_rows)
     t0 = time.perf_counter()
     back = B.unfold(batch, tok, got)
     unfold_s = time.perf_counter() - t0

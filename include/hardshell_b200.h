@@ -316,6 +316,15 @@ int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tokenizer, uint64_t le
 int hs_unfold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* container, size_t len, uint8_t* out,
               size_t cap, size_t* out_len);
 
+/* hs_unfold on several GPUs of this host: worker threads (two per GPU of `ordinals`, each with its
+ * device, the model file loaded and a batch of `slots` slots and `max_rows` rows) take rounds of
+ * each segment's coded blocks, as the reference deals the blocks of an unfold job to its lanes
+ * (crates/taco/src/gpu_unfold.rs:74-200); raw and zstd blocks stay on the host. The output and the
+ * errors are those of hs_unfold (several corrupt blocks report the lowest index). */
+int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                    uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* container,
+                    size_t len, uint8_t* out, size_t cap, size_t* out_len);
+
 /* The version of the zstd library that hs_fold uses (major * 10000 + minor * 100 + patch), or 0
  * if it is not available. */
 uint32_t hs_zstd_version(void);

@@ -149,6 +149,8 @@ def lib() -> ctypes.CDLL:
     L.hs_fold_stream_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, u64, SOURCE_FN, vp,
                                        SINK_FN, vp, ctypes.POINTER(FoldOptions), ctypes.POINTER(u64),
                                        ctypes.POINTER(FoldStats)]
+    L.hs_unfold_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, ctypes.c_char_p,
+                                  ctypes.c_size_t, vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]
     L.hs_unfold_stream.argtypes = [vp, vp, u64, READ_AT_FN, vp, WRITE_FN, vp, ctypes.POINTER(u64)]
     L.hs_zstd_version.argtypes = []
     L.hs_zstd_version.restype = u32
@@ -327,6 +329,19 @@ def unfold_stream(batch, tokenizer, length: int, read_at, write) -> int:
     n = ctypes.c_uint64()
     _check(lib().hs_unfold_stream(batch.h, tokenizer.h, length, cb_ra, None, cb_wr, None, ctypes.byref(n)))
     return n.value
+
+
+def unfold_multi(ordinals, model_file: bytes, tokenizer, container: bytes, slots: int = 256,
+                 max_rows: int = 16384) -> bytes:
+    """hs_unfold_multi: the unfold of a .taco container with its coded blocks dealt to worker
+    threads on the GPUs `ordinals`."""
+    ords = np.ascontiguousarray(ordinals, dtype=np.int32)
+    original_len = int.from_bytes(container[40:48], "little") if len(container) >= 48 else 0
+    out = np.zeros(max(original_len, 1), dtype=np.uint8)
+    n = ctypes.c_size_t()
+    _check(lib().hs_unfold_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows, tokenizer.h,
+                                 container, len(container), _p(out), out.size, ctypes.byref(n)))
+    return out[:n.value].tobytes()
 
 
 def unfold(batch, tokenizer, container: bytes, original_len: int | None = None) -> bytes:

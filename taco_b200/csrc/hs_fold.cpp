@@ -1114,18 +1114,266 @@ int read_table(ReadAt& in, const Header& c, uint32_t first, uint32_t n, std::vec
     return HS_OK;
 }
 
+// The coded blocks of one unfold segment, for the GPU side: the segment's stored bytes, its
+// blocks' offsets and lengths, the indices (in the segment) of its coded blocks, and the buffer of
+// the restored bytes.
+struct CodedJob {
+    const Header* c;
+    const hs_tokenizer* tok;
+    uint32_t eot;
+    const uint8_t* data;
+    size_t data_len;
+    const std::vector<uint64_t>* at;
+    const std::vector<uint32_t>* stored;
+    const std::vector<uint32_t>* coded;
+    uint64_t first, seg_len;
+    uint8_t* restored;
+};
+
+// Decodes the coded blocks coded[r0 .. r1) of the job on `batch` (slots 0 .. r1 - r0 - 1): the
+// varint token count (1 .. the block length), then the coder bytes on the device
+// (hs_batch_decode_blocks: codec.rs:370-520 BlockDecoder), then the tokens' bytes. A corrupt
+// block gives HS_CORRUPT with its index in *bad and the reason in *why (no error is recorded, so
+// several threads can each report theirs); another failure returns its status with the thread's
+// last error set.
+int decode_round(hs_batch* batch, const CodedJob& J, size_t r0, size_t r1, uint64_t* bad, std::string* why) {
+    const Header& c = *J.c;
+    const size_t mm = r1 - r0;
+    std::vector<uint32_t> slots(mm), counts(mm), status(mm);
+    std::vector<uint64_t> offs(mm), lens(mm), toff(mm);
+    auto corrupt = [&](uint32_t j, const char* reason) {
+        *bad = J.first + j;
+        *why = reason;
+        return (int)HS_CORRUPT;
+    };
+    uint64_t ntok = 0;
+    for (size_t q = 0; q < mm; q++) {
+        const uint32_t j = (*J.coded)[r0 + q];
+        const uint8_t* p = J.data + (*J.at)[j];
+        const size_t sl = (*J.stored)[j];
+        uint64_t count = 0;
+        size_t k = 0;
+        for (int shift = 0;; shift += 7, k++) {
+            if (k >= sl || shift > 63) return corrupt(j, "the token count is not valid");
+            count |= (uint64_t)(p[k] & 0x7F) << shift;
+            if (!(p[k] & 0x80)) break;
+        }
+        k++;
+        const size_t olen = (size_t)std::min<uint64_t>(c.block_size, J.seg_len - (uint64_t)j * c.block_size);
+        if (count == 0 || count > olen) return corrupt(j, "the token count does not agree with the block length");
+        slots[q] = (uint32_t)q;
+        counts[q] = (uint32_t)count;
+        offs[q] = (*J.at)[j] + k;
+        lens[q] = sl - k;
+        toff[q] = ntok;
+        ntok += count;
+    }
+    std::vector<uint32_t> toks(std::max<uint64_t>(ntok, 1));
+    int rc = hs_batch_decode_blocks(batch, (uint32_t)mm, slots.data(), J.data, J.data_len, offs.data(), lens.data(),
+                                    counts.data(), FREQ_BITS, toks.data(), ntok, toff.data(), status.data());
+    if (rc) return rc;
+    for (size_t q = 0; q < mm; q++) {
+        const uint32_t j = (*J.coded)[r0 + q];
+        if (status[q]) return corrupt(j, "an interval does not hold its target");
+        const size_t o = (size_t)j * c.block_size;
+        const size_t olen = (size_t)std::min<uint64_t>(c.block_size, J.seg_len - o);
+        size_t w = 0;
+        for (uint32_t t = 0; t < counts[q]; t++) {
+            size_t nb;
+            const uint32_t id = toks[toff[q] + t];
+            const uint8_t* bytes = hs::token_bytes(J.tok, id, &nb);
+            if (id == J.eot || nb == 0 || nb > olen - w) return corrupt(j, "the tokens do not give the block length");
+            memcpy(J.restored + o + w, bytes, nb);
+            w += nb;
+        }
+        if (w != olen) return corrupt(j, "the tokens do not give the block length");
+    }
+    return HS_OK;
+}
+
+int corrupt_block(uint64_t i, const std::string& why) {
+    return hs::host_fail(HS_CORRUPT, "block " + std::to_string(i) + " is corrupt: " + why);
+}
+
+// The GPU side of an unfold: decodes every coded block of a job.
+class UnfoldGpu {
+  public:
+    virtual ~UnfoldGpu() = default;
+    virtual int set_overlap(uint16_t k) = 0;
+    virtual int run(const CodedJob& J) = 0;
+};
+
+// hs_unfold: the caller's batch, rounds of up to min(slots, max_rows) blocks in order.
+class OneDecoder : public UnfoldGpu {
+  public:
+    explicit OneDecoder(hs_batch* b) : b_(b) {}
+    int set_overlap(uint16_t k) override { return hs_batch_set_overlap(b_, k); }
+    int run(const CodedJob& J) override {
+        const size_t per = std::max<size_t>(1, std::min(hs::batch_slots(b_), hs::batch_max_rows(b_)));
+        for (size_t r0 = 0; r0 < J.coded->size(); r0 += per) {
+            uint64_t bad = 0;
+            std::string why;
+            const int rc = decode_round(b_, J, r0, std::min(J.coded->size(), r0 + per), &bad, &why);
+            if (rc == HS_CORRUPT) return corrupt_block(bad, why);
+            if (rc) return rc;
+        }
+        return HS_OK;
+    }
+
+  private:
+    hs_batch* b_;
+};
+
+// hs_unfold_multi: worker threads (each with its device, model and batch, made once) take rounds of
+// the job's coded blocks from one counter, as the GPU fold's threads take windows
+// (crates/taco/src/gpu_unfold.rs:74-200 deals the blocks of a job to the lanes). Several corrupt
+// blocks report the one with the lowest index, so the error does not depend on the dealing
+// (unfold.rs decode_group). Workers that cannot open give their share to the others.
+class MultiDecoder : public UnfoldGpu {
+  public:
+    MultiDecoder(const std::vector<int>& ords, const uint8_t* model_file, size_t model_len, const uint8_t* hash,
+                 uint32_t slots, uint32_t max_rows)
+        : ords_(ords), file_(model_file), len_(model_len), hash_(hash), slots_(slots), rows_(max_rows),
+          rcs_(ords.size(), HS_OK), msgs_(ords.size()), live_(ords.size(), 0) {}
+
+    ~MultiDecoder() override {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            quit_ = true;
+        }
+        cv_.notify_all();
+        for (auto& t : threads_) t.join();
+    }
+
+    int start() {
+        for (size_t g = 0; g < ords_.size(); g++) threads_.emplace_back([this, g] { worker(g); });
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return tried_ == ords_.size(); });
+        size_t ok = 0;
+        for (char l : live_) ok += l;
+        if (!ok) return hs::host_fail(rcs_[0], "no GPU of the unfold opened: " + msgs_[0]);
+        n_live_ = ok;
+        return HS_OK;
+    }
+
+    int set_overlap(uint16_t k) override {
+        overlap_ = k;
+        return HS_OK;
+    }
+
+    int run(const CodedJob& J) override {
+        std::unique_lock<std::mutex> lk(mu_);
+        job_ = &J;
+        next_ = 0;
+        bad_ = UINT64_MAX;
+        busy_ = n_live_;
+        gen_++;
+        cv_.notify_all();
+        cv_.wait(lk, [&] { return busy_ == 0; });
+        for (size_t g = 0; g < ords_.size(); g++)
+            if (live_[g] && rcs_[g]) return hs::host_fail(rcs_[g], "GPU " + std::to_string(ords_[g]) + ": " + msgs_[g]);
+        if (bad_ != UINT64_MAX) return corrupt_block(bad_, bad_why_);
+        return HS_OK;
+    }
+
+  private:
+    void note(size_t g, int rc) {  // under mu_
+        char buf[1024];
+        hs_last_error(buf, sizeof buf);
+        msgs_[g] = buf;
+        rcs_[g] = rc;
+    }
+
+    void worker(size_t g) {
+        hs_dev* dev = nullptr;
+        hs_model* model = nullptr;
+        hs_batch* batch = nullptr;
+        int rc = hs_open(ords_[g], &dev);
+        if (!rc) rc = hs_model_load(dev, file_, len_, &model);
+        hs_model_info mi;
+        if (!rc && !(rc = hs_model_get_info(model, &mi)) && memcmp(mi.hash, hash_, 32) != 0)
+            rc = hs::host_fail(HS_MODEL, "the loaded model is not the model file");
+        if (!rc) rc = hs_batch_new(model, slots_, rows_, &batch);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            if (rc) note(g, rc);
+            live_[g] = rc == HS_OK;
+            tried_++;
+        }
+        cv_.notify_all();
+        uint64_t seen = 0;
+        while (!rc) {
+            const CodedJob* J;
+            {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return quit_ || gen_ != seen; });
+                if (quit_) break;
+                seen = gen_;
+                J = job_;
+            }
+            int r = hs_batch_set_overlap(batch, overlap_);
+            const size_t per = std::max<size_t>(1, std::min<size_t>(slots_, rows_));
+            uint64_t my_bad = UINT64_MAX;
+            std::string my_why;
+            while (!r) {
+                const size_t r0 = next_.fetch_add(per);
+                if (r0 >= J->coded->size()) break;
+                uint64_t bad = 0;
+                std::string why;
+                const int d = decode_round(batch, *J, r0, std::min(J->coded->size(), r0 + per), &bad, &why);
+                if (d == HS_CORRUPT) {
+                    if (bad < my_bad) my_bad = bad, my_why = why;
+                } else {
+                    r = d;
+                }
+            }
+            {
+                std::lock_guard<std::mutex> lk(mu_);
+                if (r) note(g, r);
+                if (my_bad < bad_) bad_ = my_bad, bad_why_ = my_why;
+                busy_--;
+            }
+            cv_.notify_all();
+            rc = r;
+        }
+        if (batch) hs_batch_free(batch);
+        if (model) hs_model_free(model);
+        if (dev) hs_dev_free(dev);
+    }
+
+    std::vector<int> ords_;
+    const uint8_t* file_;
+    size_t len_;
+    const uint8_t* hash_;
+    uint32_t slots_, rows_;
+    std::vector<int> rcs_;
+    std::vector<std::string> msgs_;
+    std::vector<char> live_;
+    std::vector<std::thread> threads_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    size_t tried_ = 0, n_live_ = 0, busy_ = 0;
+    uint64_t gen_ = 0;
+    bool quit_ = false;
+    uint16_t overlap_ = 0;
+    const CodedJob* job_ = nullptr;
+    std::atomic<size_t> next_{0};
+    uint64_t bad_ = UINT64_MAX;
+    std::string bad_why_;
+};
+
 // taco::unfold segment by segment (crates/taco/src/stream.rs StreamUnfold::from_seekable): the
 // whole table and the container length are checked before any output; then each segment's stored
 // bytes are read, its raw blocks copied, its zstd blocks decoded on the host, its coded blocks on
-// the GPU, and its bytes written out; the SHA-256 of all of them is checked at the end.
-int unfold_stream_impl(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uint64_t n, Writer& out) {
+// the GPUs, and its bytes written out; the SHA-256 of all of them is checked at the end. `hash`
+// and `eot` are those of the model (the container must name it, if it names one).
+int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const hs_tokenizer* tok, ReadAt& in,
+                       uint64_t n, Writer& out) {
     Header c;
     int rc = parse_header(in, n, c);
     if (rc) return rc;
-    hs_model_info info;
-    if ((rc = hs_model_get_info(hs::batch_model(batch), &info))) return rc;
     // unfold.rs:157-180 checked_model: a container that names a model needs that model.
-    if (c.needs_model && memcmp(c.model_hash, info.hash, 32) != 0)
+    if (c.needs_model && memcmp(c.model_hash, hash, 32) != 0)
         return hs::host_fail(HS_MODEL_MISMATCH, "the container was folded with another model");
     std::vector<uint8_t> kinds;
     std::vector<uint32_t> stored;
@@ -1145,12 +1393,8 @@ int unfold_stream_impl(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uin
     }
     if (total > n) return bad_container("truncated block");
     if (total < n) return bad_container("extra bytes after the last block");
-    if ((rc = hs_batch_set_overlap(batch, c.overlap))) return rc;
-    auto corrupt = [](uint64_t i, const std::string& why) {
-        return hs::host_fail(HS_CORRUPT, "block " + std::to_string(i) + " is corrupt: " + why);
-    };
+    if ((rc = gpu.set_overlap(c.overlap))) return rc;
     const uint64_t seg_blocks = std::min<uint64_t>(std::max<uint64_t>(SEGMENT_BYTES / c.block_size, 1), SEGMENT_BLOCKS);
-    const size_t per = std::max<size_t>(1, std::min(hs::batch_slots(batch), hs::batch_max_rows(batch)));
     hs::Sha256 sum;
     std::vector<uint8_t> data, restored;
     std::vector<uint64_t> at;
@@ -1170,7 +1414,7 @@ int unfold_stream_impl(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uin
         const uint64_t o0 = first * c.block_size;
         const uint64_t seg_len = std::min<uint64_t>((uint64_t)m * c.block_size, c.original_len - o0);
         restored.resize((size_t)seg_len);
-        // Raw and zstd blocks on the host; the coded ones collected for the GPU.
+        // Raw and zstd blocks on the host; the coded ones collected for the GPUs.
         std::vector<uint32_t> coded;
         for (uint32_t j = 0; j < m; j++) {
             const size_t o = (size_t)j * c.block_size;
@@ -1178,61 +1422,13 @@ int unfold_stream_impl(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uin
             if (kinds[j] == KIND_RAW) memcpy(restored.data() + o, data.data() + at[j], olen);
             else if (kinds[j] == KIND_ZSTD &&
                      !decompress_zstd(data.data() + at[j], stored[j], restored.data() + o, olen))
-                return corrupt(first + j, "the zstd frame does not give the block");
+                return corrupt_block(first + j, "the zstd frame does not give the block");
             else if (kinds[j] == KIND_CODED) coded.push_back(j);
         }
-        // The coded blocks: the varint token count (1 .. the block length), then the coder bytes,
-        // decoded on the device in rounds of up to min(slots, max_rows) blocks (codec.rs:370-520
-        // BlockDecoder, with the decoder of hs_batch_decode_blocks), then the tokens' bytes.
-        for (size_t r0 = 0; r0 < coded.size(); r0 += per) {
-            const size_t r1 = std::min(coded.size(), r0 + per), mm = r1 - r0;
-            std::vector<uint32_t> slots(mm), counts(mm), status(mm);
-            std::vector<uint64_t> offs(mm), lens(mm), toff(mm);
-            uint64_t ntok = 0;
-            for (size_t q = 0; q < mm; q++) {
-                const uint32_t j = coded[r0 + q];
-                const uint8_t* p = data.data() + at[j];
-                const size_t sl = stored[j];
-                uint64_t count = 0;
-                size_t k = 0;
-                for (int shift = 0;; shift += 7, k++) {
-                    if (k >= sl || shift > 63) return corrupt(first + j, "the token count is not valid");
-                    count |= (uint64_t)(p[k] & 0x7F) << shift;
-                    if (!(p[k] & 0x80)) break;
-                }
-                k++;
-                const size_t olen = (size_t)std::min<uint64_t>(c.block_size, seg_len - (uint64_t)j * c.block_size);
-                if (count == 0 || count > olen)
-                    return corrupt(first + j, "the token count does not agree with the block length");
-                slots[q] = (uint32_t)q;
-                counts[q] = (uint32_t)count;
-                offs[q] = at[j] + k;
-                lens[q] = sl - k;
-                toff[q] = ntok;
-                ntok += count;
-            }
-            std::vector<uint32_t> toks(std::max<uint64_t>(ntok, 1));
-            if ((rc = hs_batch_decode_blocks(batch, (uint32_t)mm, slots.data(), data.data(), data.size(), offs.data(),
-                                             lens.data(), counts.data(), FREQ_BITS, toks.data(), ntok, toff.data(),
-                                             status.data())))
-                return rc;
-            for (size_t q = 0; q < mm; q++) {
-                const uint32_t j = coded[r0 + q];
-                if (status[q]) return corrupt(first + j, "an interval does not hold its target");
-                const size_t o = (size_t)j * c.block_size;
-                const size_t olen = (size_t)std::min<uint64_t>(c.block_size, seg_len - o);
-                size_t w = 0;
-                for (uint32_t t = 0; t < counts[q]; t++) {
-                    size_t nb;
-                    const uint32_t id = toks[toff[q] + t];
-                    const uint8_t* b = hs::token_bytes(tok, id, &nb);
-                    if (id == info.eot_token || nb == 0 || nb > olen - w)
-                        return corrupt(first + j, "the tokens do not give the block length");
-                    memcpy(restored.data() + o + w, b, nb);
-                    w += nb;
-                }
-                if (w != olen) return corrupt(first + j, "the tokens do not give the block length");
-            }
+        if (!coded.empty()) {
+            const CodedJob J{&c, tok, eot, data.data(), data.size(), &at, &stored, &coded, first, seg_len,
+                             restored.data()};
+            if ((rc = gpu.run(J))) return rc;
         }
         sum.update(restored.data(), restored.size());
         if (out.write(restored.data(), restored.size())) return hs::host_fail(HS_IO, "the output writer failed");
@@ -1242,6 +1438,15 @@ int unfold_stream_impl(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uin
     if (memcmp(got, c.checksum, 32) != 0)
         return hs::host_fail(HS_CORRUPT, "the restored bytes do not have the container's SHA-256");
     return HS_OK;
+}
+
+// hs_unfold and hs_unfold_stream on the caller's batch.
+int unfold_one(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uint64_t n, Writer& out) {
+    hs_model_info info;
+    int rc = hs_model_get_info(hs::batch_model(batch), &info);
+    if (rc) return rc;
+    OneDecoder gpu(batch);
+    return unfold_stream_impl(gpu, info.hash, info.eot_token, tok, in, n, out);
 }
 
 }  // namespace
@@ -1260,7 +1465,7 @@ int hs_unfold(hs_batch* batch, const hs_tokenizer* tok, const uint8_t* container
         return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
                                                   std::to_string(c.original_len) + " needed");
     MemWriter w(out, cap);
-    return unfold_stream_impl(batch, tok, in, len, w);
+    return unfold_one(batch, tok, in, len, w);
 }
 
 int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tok, uint64_t len, hs_read_at_fn read_at, void* read_user,
@@ -1272,7 +1477,40 @@ int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tok, uint64_t len, hs_
     if (rc) return rc;
     *out_len = c.original_len;
     CallbackWriter w(write, write_user);
-    return unfold_stream_impl(batch, tok, in, len, w);
+    return unfold_one(batch, tok, in, len, w);
+}
+
+int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len, uint32_t slots,
+                    uint32_t max_rows, const hs_tokenizer* tok, const uint8_t* container, size_t len, uint8_t* out,
+                    size_t cap, size_t* out_len) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !out_len || (len && !container))
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    uint32_t vocab, eot, n_ctx;
+    {
+        std::string err;
+        if (!hs::model_file_info(model_file, model_len, &vocab, &eot, &n_ctx, err))
+            return hs::host_fail(HS_MODEL, "the model file is not valid: " + err);
+    }
+    int rc = check_tokenizer(tok, vocab);
+    if (rc) return rc;
+    MemReadAt in(container, len);
+    Header c;
+    if ((rc = parse_header(in, len, c))) return rc;
+    *out_len = (size_t)c.original_len;
+    if (cap < c.original_len || (!out && c.original_len))
+        return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
+                                                  std::to_string(c.original_len) + " needed");
+    uint8_t hash[32];
+    hs::sha256(model_file, model_len, hash);
+    // Two worker threads per GPU, as the fold (HS_FOLD_WORKERS_PER_GPU).
+    uint32_t per = 2;
+    if (const char* v = getenv("HS_FOLD_WORKERS_PER_GPU")) per = (uint32_t)std::min(8, std::max(1, atoi(v)));
+    std::vector<int> ords;
+    for (uint32_t k = 0; k < per; k++) ords.insert(ords.end(), ordinals, ordinals + n_gpus);
+    MultiDecoder gpu(ords, model_file, model_len, hash, slots, max_rows);
+    if ((rc = gpu.start())) return rc;
+    MemWriter w(out, cap);
+    return unfold_stream_impl(gpu, hash, eot, tok, in, len, w);
 }
 
 }  // extern "C"

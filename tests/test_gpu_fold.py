@@ -271,3 +271,28 @@ def test_unfold_stream_refuses_a_damaged_table_before_any_output(setup):
             B.unfold_stream(batch, tok, len(bad), lambda at, m, d=bad: d[at:at + m], out.append)
         assert e.value.code == B.HS_FORMAT
         assert out == []
+
+
+def test_unfold_on_several_gpu_threads_equals_one_gpu(setup):
+    """hs_unfold_multi deals each segment's coded blocks to worker threads (two per GPU); the
+    output is hs_unfold's, and a damaged coded block is reported as by hs_unfold."""
+    batch, tok = setup
+    import torch
+
+    ords = [0, 1] if torch.cuda.device_count() >= 2 else [0]
+    for name in ["predicted_text_k0", "predicted_text_k32", "all_kinds_text"]:
+        c = (GOLDEN / (name + ".taco")).read_bytes()
+        want = (GOLDEN / (name + ".in")).read_bytes()
+        assert B.unfold_multi(ords, tiny_bytes(), tok, c, slots=8, max_rows=4096) == want
+    # Many coded blocks in many rounds: a fold of the predicted text in 300-byte blocks.
+    data = (GOLDEN / "predicted_text_k32.in").read_bytes() * 6
+    folded, stats = B.fold(batch, tok, data, 300, 32)
+    assert stats["coded_blocks"] > 8
+    assert B.unfold_multi(ords, tiny_bytes(), tok, folded, slots=4, max_rows=4096) == data
+    cont = C.parse(folded)
+    coded = [b for b in cont.blocks if b.kind == C.KIND_CODED]
+    blk = cont.blocks[coded[3].index]
+    blk.stored = blk.stored[:2] + bytes(x ^ 0x5A for x in blk.stored[2:])
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_multi(ords, tiny_bytes(), tok, C.build(cont), slots=4, max_rows=4096)
+    assert e.value.code == B.HS_CORRUPT

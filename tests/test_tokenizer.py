@@ -209,3 +209,14 @@ def test_synthetic_vocabulary_tokenizes_the_zipf_text_as_the_python_bpe():
         assert b"".join(vocab[x] for x in got.tolist()) == text
     finally:
         t.close()
+
+
+def test_unfold_multi_refusals_before_any_gpu(tok, monkeypatch):
+    good = (GOLDEN / "predicted_text_k32.taco").read_bytes()
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_multi([0], b"not a model", tok, good)
+    assert e.value.code == B.HS_MODEL
+    monkeypatch.setenv("HS_FAIL_OPEN", "0")
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_multi([0], tiny_bytes(), tok, good)
+    assert e.value.code == B.HS_NO_DEVICE
