@@ -16,9 +16,10 @@ value  = input bytes of all ranks / max over ranks of the device time of the K s
          events around every pass on the batch stream, the token rows already on the device);
 e2e    = the same bytes / wall time of K more C-ABI calls with host buffers, without the
          profiling events (row upload, planning, interval read back inside);
-parity = rank 0 compares the intervals (symbol, start, freq) of the first windows of the timed
-         shape (512 slots, 16,384-row passes) with the CPU oracle's, field by field; a mismatch
-         fails the run;
+parity = rank 0 compares the intervals (symbol, start, freq) of windows spread evenly over the
+         timed step (512 slots, passes of --max-rows rows; the first and the last window of the
+         step among them, so the rows at both ends of a pass are checked) with the CPU oracle's,
+         field by field; a mismatch fails the run;
 roofline = the kernel with the largest share of the pass time: algorithmic int8 ops (tensor-bound
          kernels) or algorithmic bytes (HBM-bound kernels) per launch / its mean CUDA-event launch
          time, against the int8 tensor peak measured in this run (torch._int_mm, cuBLASLt) or the
@@ -66,7 +67,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--windows", type=int, default=WINDOWS)
-    ap.add_argument("--max-rows", type=int, default=16384)
+    ap.add_argument("--max-rows", type=int, default=65536)
     ap.add_argument("--no-extras", action="store_true", help="skip the GEMM microbench and the unfold step")
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
@@ -445,15 +446,20 @@ def main():
                 "timing": "wall clock of one hs_batch_decode_blocks call per rank (its batch made beforehand) between "
                           "barriers, max over ranks",
                 "per_rank_first_call": {k: ub[k] for k in ("e2e_tokens_per_s", "device_tokens_per_s")}}
-        # Parity on the bench's own shape: the intervals of the first windows of the last warm-up
-        # step (512 slots, passes of max_rows rows) against the oracle's, field by field.
+        # Parity on the bench's own shape: the intervals of windows spread evenly over the last
+        # warm-up step (512 slots, passes of max_rows rows; the first and the last window among
+        # them) against the oracle's, field by field.
         threads = args.cpu_threads or os.cpu_count() or 1
         n_par = max(PARITY_WINDOWS, threads) if world == 1 else PARITY_WINDOWS
         n_par = min(n_par, args.windows)
-        ora = oracle_windows(model_bytes, windows[:n_par], eot, lens, threads)
-        got = np.stack([ans["symbol"], ans["start"], ans["freq"]], 1).astype(np.uint64)[:n_par * WINDOW]
+        pick = np.unique(np.linspace(0, args.windows - 1, n_par).round().astype(np.int64))
+        n_par = pick.size
+        ora = oracle_windows(model_bytes, windows[pick], eot, lens, threads)
+        got = np.stack([ans["symbol"], ans["start"], ans["freq"]], 1).astype(np.uint64)
+        got = got.reshape(args.windows, WINDOW, 3)[pick].reshape(-1, 3)
         bad = np.any(got != ora["answers"], axis=1)
         result["parity"] = {"windows": int(n_par), "rows": int(n_par * WINDOW), "pass_rows": args.max_rows,
+                            "window_indices": [int(w) for w in pick],
                             "slots": args.windows, "fields": ["symbol", "start", "freq"],
                             "mismatches": int(bad.sum()),
                             "against": "CPU oracle fast path (oracle/), the same windows"}
@@ -753,7 +759,8 @@ def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int], max_rows: i
     """`mb` MiB of the seeded mixed stream (70 % Zipf text, 20 % JSON key/number
     records, 10 % uniform random bytes, in 64 KiB pieces; synth.mixed_stream) folded by
     hs_fold_multi on the GPUs `ordinals` (two host threads each; 512 slots, passes of max_rows) and
-    unfolded by hs_unfold on the first; wall clock, the container's SHA-256, the stage times of the
+    unfolded by hs_unfold_multi on the same GPUs (each worker opens its device and loads the model
+    inside the timed call, as the fold's do); wall clock, the container's SHA-256, the stage times of the
     fold. The same bytes on every GPU count (tests/test_gpu_fold.py, tests/test_gpu_large_input.py
     check the equality with one GPU and with the CPU path on samples)."""
     import hashlib
@@ -765,16 +772,10 @@ def large_input(B, model_bytes: bytes, mb: int, ordinals: list[int], max_rows: i
     t0 = time.perf_counter()
     got, stats = B.fold_multi(ordinals, model_bytes, tok, data, slots=512, max_rows=max_rows)
     fold_s = time.perf_counter() - t0
-    dev = B.CudaDevice(ordinals[0])
-    model = B.CudaModel(dev, model_bytes)
-    batch = B.CudaBatch(model, 256, max_rows)
     t0 = time.perf_counter()
-    back = B.unfold(batch, tok, got)
+    back = B.unfold_multi(ordinals, model_bytes, tok, got, slots=256, max_rows=max_rows)
     unfold_s = time.perf_counter() - t0
     ok = back == data
-    batch.close()
-    model.close()
-    dev.close()
     tok.close()
     if not ok:
         raise SystemExit("the large input did not unfold to itself")

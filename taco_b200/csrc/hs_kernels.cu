@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(256) k_gemm_simple(int mode, const int8_t* A, 
     }
     __syncthreads();
     const int hq = w >> 2;  // which 128 columns
-    const int tile = blockIdx.x * 2 + hq;
+    const int tile = blockIdx.y * 2 + hq;  // column groups of 256 in y
 #pragma unroll
     for (int i = 0; i < SG_ROWS; i++) {
         int64_t tm = red[i][4 * hq];
