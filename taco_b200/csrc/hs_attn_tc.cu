@@ -101,7 +101,9 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                    int n_ctx, int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P,
                    int8_t* att, int lda, int* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // Aligned to 1,024 bytes by an offset from the __shared__ array itself (not through an
+    // integer cast), so every access below stays a shared-memory access with 32-bit addresses.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sQ = smem;
     uint8_t* sK = sQ + Q_BYTES;                 // 2 x 8 KB
     uint8_t* sV = sK + 2 * K_BYTES;             // 2 x 8 KB

@@ -157,7 +157,9 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     static_assert(!WIDE || EPI_WARPS == 8, "the version 2 epilogues take 8 warps");
     static_assert(MODE != EPI_LOGITS || EPI_WARPS == 8, "the logits epilogue takes 8 warps");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // Aligned to 1,024 bytes by an offset from the __shared__ array itself (not through an
+    // integer cast), so every access below stays a shared-memory access with 32-bit addresses.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     int8_t* s_gelu = reinterpret_cast<int8_t*>(smem + (size_t)STAGES * STAGE_BYTES);
     uint8_t* s_store = smem + (size_t)STAGES * STAGE_BYTES + Cfg<MODE>::EXTRA;  // [EPI_WARPS][STORE_WARP]
     int64_t* s_c = reinterpret_cast<int64_t*>(s_store + EPI_WARPS * Cfg<MODE>::STORE_WARP);  // [2][BN]
