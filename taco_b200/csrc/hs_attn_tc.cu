@@ -4,18 +4,23 @@
 // pos0 .. pos0 + count - 1, attending causally to the keys 0 .. pos0 + count - 1 of its slot.
 // The integer softmax of crates/hardshell/src/softmax.rs:78 needs the exact row max before any
 // weight and the exact row sum before any probability, so the scores S = Q K^T are computed
-// three times per 128-key chunk on the tensor cores (cheap: K = 64):
+// twice per 128-key chunk on the tensor cores (cheap: K = 64):
 //   pass 1: S -> the max and min dot of each row (score() is monotone in the dot, so the max
 //           score is max(score(maxdot), score(mindot)), as in the reference GPU kernel);
-//   pass 2: S -> e = attn_exp[min(max - score, len - 1)] -> the row sum;
-//   pass 3: S -> p = floor(e * 2^P / sum) (a 64-bit reciprocal and one exact correction), split
-//           into four unsigned bytes p = p0 + 2^8 p1 + 2^16 p2 + 2^24 p3, written to shared
-//           memory as four u8 A operands; O_k += P_k V (u8 x s8) accumulates in TMEM.
+//   pass 2: S -> the table index d = min(max - score, len - 1) -> e = attn_exp[d] -> the row sum;
+//           each key's d (u16) goes to this SM's slot of a scratch buffer in global memory;
+//   pass 3: d back from the scratch (no third S) -> p = floor(e * 2^P / sum) (an exact
+//           multiply-shift), split into four unsigned bytes p = p0 + 2^8 p1 + 2^16 p2 + 2^24 p3,
+//           written to shared memory as four u8 A operands; O_k += P_k V (u8 x s8) in TMEM.
+// The scratch slot is picked by %smid: a CTA needs more than half of an SM's shared memory, so at
+// most one runs on an SM at a time, and the slots of all SMs (n_ctx u16 per row, 256 KB at
+// n_ctx = 1024) stay in L2 between the two passes.
 // Then acc = sum_k 2^(8k) O_k (exact: each O_k has at most n_ctx terms below 2^15) and
 // att = clamp(rescale(acc, out_m, out_s), -127, 127) (crates/hardshell/src/gpt2/reference.rs:252-284).
 //
 // Operands come in by TMA (no multicast): Q [128 x 64] and K chunks [128 x 64] with the 64-byte
 // swizzle, V^T chunks [64 x 128] with the 128-byte swizzle from the transposed values cache.
+// (A fold pass runs this kernel on 96 % of its rows, so one S pass less is most of a pass.)
 // Warps 0..15 do the softmax: TMEM lane group warp % 4 (32 rows) and key quarter warp / 4 (32
 // of the 128 keys of a chunk). Warp 16 is the TMA producer, warp 17 owns TMEM and issues the
 // MMAs: S of chunk i + 1 is issued before P V of chunk i, and P is double-buffered, so the
@@ -43,6 +48,9 @@ constexpr int K_BYTES = KC * HDIM;        // 8 KB
 constexpr int V_BYTES = HDIM * KC;        // 8 KB
 constexpr int P_BYTES = 4 * GM * KC;      // 64 KB (four planes), double-buffered
 constexpr int TABLE_MAX = 8192;           // attn_exp entries kept in shared memory
+// The scratch slot of one SM: per 128-key chunk, key quarter, 16-byte word (8 keys) and row, the
+// u16 table indices of 8 keys, so that a warp's 32 rows store and load 512 contiguous bytes.
+constexpr size_t SCR_CHUNK_BYTES = 4 * 4 * GM * 16;  // 32 KB per chunk of 128 keys
 constexpr size_t ASMEM =
     (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 4 * TABLE_MAX + 8 * GM * 8 + 512 + 1024;
 
@@ -99,8 +107,14 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnGroup* groups, int L, int layer, int H,
                    int n_ctx, int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P,
-                   int8_t* att, int lda, int* err) {
+                   int8_t* att, int lda, uint8_t* scratch, int scr_slots, int* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint32_t smid;
+    asm("mov.u32 %0, %%smid;" : "=r"(smid));
+    if (smid >= (uint32_t)scr_slots) {  // the same for every thread of the CTA: nothing started yet
+        if (threadIdx.x == 0) atomicCAS(err, 0, ERR_ATTN_SCRATCH);
+        return;
+    }
     // Aligned to 1,024 bytes by an offset from the __shared__ array itself (not through an
     // integer cast), so every access below stays a shared-memory access with 32-bit addresses.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -161,7 +175,19 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             int ks = 0, vs = 0;
             uint32_t kph = 0, vph = 0;
             bool ok = true;
-            for (int it = 0; it < 3 * nch && ok; it++) {
+            // V^T chunk c of pass 3 (both buffers are free at the start: chunks 0 and 1 load first).
+            auto load_v = [&](int c) -> bool {
+                if (!mbar_wait(&bars->v_empty[vs], vph ^ 1, err, 12)) return false;
+                mbar_arrive_expect_tx(&bars->v_full[vs], V_BYTES);
+                tma_load_2d(sV + vs * V_BYTES, &tmV, &bars->v_full[vs], c * KC, (int)(head * HDIM));
+                if (++vs == 2) {
+                    vs = 0;
+                    vph ^= 1;
+                }
+                return true;
+            };
+            for (int c = 0; c < nch && c < 2 && ok; c++) ok = load_v(c);
+            for (int it = 0; it < 2 * nch && ok; it++) {
                 int c = it % nch;
                 if (!mbar_wait(&bars->k_empty[ks], kph ^ 1, err, 11)) break;
                 mbar_arrive_expect_tx(&bars->k_full[ks], K_BYTES);
@@ -170,20 +196,12 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     ks = 0;
                     kph ^= 1;
                 }
-                if (it >= 2 * nch) {
-                    if (!mbar_wait(&bars->v_empty[vs], vph ^ 1, err, 12)) break;
-                    mbar_arrive_expect_tx(&bars->v_full[vs], V_BYTES);
-                    tma_load_2d(sV + vs * V_BYTES, &tmV, &bars->v_full[vs], c * KC, (int)(head * HDIM));
-                    if (++vs == 2) {
-                        vs = 0;
-                        vph ^= 1;
-                    }
-                }
             }
+            for (int c = 2; c < nch && ok; c++) ok = load_v(c);
         }
     } else if (warp == EW + 1) {
-        // MMA issuer: S of chunk `it`, then (pass 3) the P V of the chunk before it, so the softmax
-        // warps always have the next S while the tensor core multiplies the previous P.
+        // MMA issuer: S of every chunk of passes 1 and 2, then the P V of each chunk of pass 3 as
+        // its planes are written (P is double-buffered).
         if (lane == 0) {
             const uint32_t id_s = idesc_i8(GM, KC, true, true);
             const uint32_t id_pv = idesc_i8(GM, HDIM, false, true);
@@ -214,7 +232,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                 }
                 return true;
             };
-            for (int it = 0; it < 3 * nch && ok; it++) {
+            for (int it = 0; it < 2 * nch && ok; it++) {
                 const int sb = it & 1;
                 const uint32_t sph = (it >> 1) & 1;
                 if (!mbar_wait(&bars->s_empty[sb], sph ^ 1, err, 14)) break;
@@ -231,9 +249,8 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     ks = 0;
                     kph ^= 1;
                 }
-                if (it > 2 * nch && !do_pv(it - 2 * nch - 1)) ok = false;
             }
-            if (ok) do_pv(nch - 1);
+            for (int c = 0; c < nch && ok; c++) ok = do_pv(c);
             mma_commit(&bars->o_full);
         }
     } else {
@@ -247,6 +264,10 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         const int32_t last = tl - 1;
         // The last position of this warp's 32 rows: a key slice past it is masked for every lane.
         const int wlast = (int)grp.pos0 + g * 32 + 31;
+        // The first: a key slice at or below it is whole for every lane. The choice between the
+        // whole and the masked path is the warp's, so the diagonal slice takes the masked path
+        // once instead of both paths diverged.
+        const int wfirst = (int)grp.pos0 + g * 32;
         // The table index min(M - score(dot), last); NARROW: the score is the low word of the
         // 64-bit shift (one shift of the high word when ss >= 32, a funnel shift below).
         auto dist = [&](int64_t M, int32_t dot) -> int32_t {
@@ -277,7 +298,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             const int j0 = c * KC + qt * 32;
             if (j0 > wlast) {
                 // every key of this slice is masked for this warp's rows
-            } else if (j0 + 31 <= rpos) {
+            } else if (j0 + 31 <= wfirst) {
                 // A max/min tree instead of one dependent chain of 32 steps.
                 int32_t mx[8], mn[8];
 #pragma unroll
@@ -317,7 +338,11 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
             M = s1 > s2 ? s1 : s2;
         }
-        // Pass 2: the row sum of e.
+        // Pass 2: the row sum of e, and each key's table index into this SM's scratch slot (the
+        // thread's 32 keys of a chunk as four 16-byte words, word k of the warp's 32 rows at 512
+        // contiguous bytes). The same thread reads them back in pass 3.
+        const size_t slot_bytes = (size_t)((n_ctx + KC - 1) / KC) * SCR_CHUNK_BYTES;  // the same for every CTA
+        uint4* scr = reinterpret_cast<uint4*>(scratch + (size_t)smid * slot_bytes) + qt * 4 * GM + row;
         mbar_wait(&bars->t_full, 0, err, 26);
         uint64_t sum = 0;
         for (int c = 0; c < nch; c++, it++) {
@@ -331,20 +356,38 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             tc_fence_before();
             mbar_arrive(&bars->s_empty[sb]);
             const int j0 = c * KC + qt * 32;
-            if (j0 > wlast) {
-                // masked for every lane
-            } else if (j0 + 31 <= rpos) {
+            if (j0 > wlast) continue;  // masked for every lane: nothing stored, nothing read back
+            uint32_t dk[16];
+#pragma unroll
+            for (int q = 0; q < 32; q += 2) {
+                const uint32_t d0 = (uint32_t)dist(M, (int32_t)v[q]), d1 = (uint32_t)dist(M, (int32_t)v[q + 1]);
+                dk[q >> 1] = d0 | (d1 << 16);
+            }
+            uint4* w = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
+#pragma unroll
+            for (int k = 0; k < 4; k++) __stcg(w + k * GM, make_uint4(dk[4 * k], dk[4 * k + 1], dk[4 * k + 2], dk[4 * k + 3]));
+            if (j0 + 31 <= wfirst) {
                 // Four partial sums: independent chains for the look-ups and adds.
                 uint64_t ps[4] = {0, 0, 0, 0};
 #pragma unroll
-                for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[dist(M, (int32_t)v[q])];
+                for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
                 sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
             } else {
 #pragma unroll
                 for (int q = 0; q < 32; q++)
-                    if (j0 + q <= rpos) sum += (uint32_t)sT[dist(M, (int32_t)v[q])];
+                    if (j0 + q <= rpos) sum += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
             }
         }
+        // Pass 3's first table indices are on their way while the sums are exchanged.
+        auto load_idx = [&](int c, uint4* dst) {
+            if (c < nch && c * KC + qt * 32 <= wlast) {
+                const uint4* r = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
+#pragma unroll
+                for (int k = 0; k < 4; k++) dst[k] = __ldcg(r + k * GM);
+            }
+        };
+        uint4 nxt[4] = {};
+        load_idx(0, nxt);
         named_bar(1, ETH);  // everyone has read sX (pass 1) before it is reused
         sX[qt * GM + row] = (int64_t)sum;
         named_bar(1, ETH);
@@ -359,24 +402,26 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         // p = u >> (l - 1): two 32x32 multiplies per key.
         int l = 64 - __clzll((long long)(sum - 1));
         if (l < 1) l = 1;
-        const uint64_t mg = (uint64_t)((((u128)1 << (31 + P + l)) + (sum - 1)) / sum);
+        const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
         const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
         const int psh = l - 1;
-        // Pass 3: p, its four byte planes into shared memory (128-byte swizzle, K-major), P V.
+        // Pass 3: the table indices back from the scratch (the next chunk's loads in flight while
+        // this one is used), p, its four byte planes into shared memory (128-byte swizzle,
+        // K-major), P V.
         const uint32_t rsw = (uint32_t)(row & 7);
-        for (int c = 0; c < nch; c++, it++) {
-            const int sb = it & 1;
-            mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 23);
-            __syncwarp();
-            tc_fence_after();
-            uint32_t v[32];
-            tmem_ld32(tbase + sb * KC, v);
-            tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(&bars->s_empty[sb]);
+        for (int c = 0; c < nch; c++) {
             const int j0 = c * KC + qt * 32;
-            auto prob = [&](int32_t dot) -> uint32_t {
-                const uint32_t e = (uint32_t)sT[dist(M, dot)];
+            uint32_t dk[16];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                dk[4 * k] = nxt[k].x;
+                dk[4 * k + 1] = nxt[k].y;
+                dk[4 * k + 2] = nxt[k].z;
+                dk[4 * k + 3] = nxt[k].w;
+            }
+            load_idx(c + 1, nxt);
+            auto prob = [&](int q) -> uint32_t {
+                const uint32_t e = (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
                 const uint64_t t = (uint64_t)e * ml;
                 const uint64_t u = (uint64_t)e * mh + (t >> 32);
                 return (uint32_t)(u >> psh);
@@ -385,12 +430,12 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             if (j0 > wlast) {
 #pragma unroll
                 for (int q = 0; q < 32; q++) pv[q] = 0u;
-            } else if (j0 + 31 <= rpos) {
+            } else if (j0 + 31 <= wfirst) {
 #pragma unroll
-                for (int q = 0; q < 32; q++) pv[q] = prob((int32_t)v[q]);
+                for (int q = 0; q < 32; q++) pv[q] = prob(q);
             } else {
 #pragma unroll
-                for (int q = 0; q < 32; q++) pv[q] = j0 + q <= rpos ? prob((int32_t)v[q]) : 0u;
+                for (int q = 0; q < 32; q++) pv[q] = j0 + q <= rpos ? prob(q) : 0u;
             }
             // The four byte planes of each 4-key word: a 4x4 byte transpose with byte permutes.
             uint32_t pw[4][8];  // [plane][4-key word] of this thread's 32 keys
@@ -589,7 +634,7 @@ __global__ void __launch_bounds__(32 * DEC_WARPS, 5) k_attention_dec(const RowIn
     if (sum == 0) sum = 1;
     int l = 64 - __clzll((long long)(sum - 1));
     if (l < 1) l = 1;
-    const uint64_t mg = (uint64_t)((((u128)1 << (31 + P + l)) + (sum - 1)) / sum);
+    const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
     const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
     const int psh = l - 1;
     __syncwarp();
@@ -713,9 +758,33 @@ bool attention_tc_supported(int hd, int n_ctx, int tlen) {
     return hd == HDIM && n_ctx % 16 == 0 && n_ctx <= 8192 && tlen <= TABLE_MAX;
 }
 
+// %nsmid: SM ids run from 0 to this bound minus one (not necessarily every id in between).
+__global__ void k_sm_id_bound(int* out) {
+    uint32_t n;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(n));
+    *out = (int)n;
+}
+
+cudaError_t attn_scratch_slots(int* slots, cudaStream_t st) {
+    int* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, sizeof(int));
+    if (e != cudaSuccess) return e;
+    k_sm_id_bound<<<1, 1, 0, st>>>(d);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(slots, d, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaError_t f = cudaFree(d);
+    return e != cudaSuccess ? e : f;
+}
+
+size_t attn_scratch_bytes(int slots, int n_ctx) {
+    return (size_t)slots * (size_t)((n_ctx + KC - 1) / KC) * SCR_CHUNK_BYTES;
+}
+
 void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, const AttnGroup* groups, int n_groups,
                          int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,
-                         const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st) {
+                         const int32_t* table, int tlen, int P, int8_t* att, int lda, uint8_t* scratch, int scr_slots,
+                         int* err, cudaStream_t st) {
     if (n_groups <= 0) return;
     dim3 grid(n_groups, H);
     const CUtensorMap& q = *reinterpret_cast<const CUtensorMap*>(tmQ);
@@ -723,13 +792,13 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
     const CUtensorMap& v = *reinterpret_cast<const CUtensorMap*>(tmV);
     if (ss >= 32 && ss <= 62)
         k_attention_tc<true, true><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os,
-                                                                 table, tlen, P, att, lda, err);
+                                                                 table, tlen, P, att, lda, scratch, scr_slots, err);
     else if (ss >= 21 && ss < 32)
         k_attention_tc<true, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os,
-                                                                  table, tlen, P, att, lda, err);
+                                                                  table, tlen, P, att, lda, scratch, scr_slots, err);
     else
         k_attention_tc<false, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om,
-                                                                   os, table, tlen, P, att, lda, err);
+                                                                   os, table, tlen, P, att, lda, scratch, scr_slots, err);
 }
 
 }  // namespace hs

@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstring>
 #include <cuda_runtime.h>
 
 #define HS_HD __host__ __device__ __forceinline__
@@ -115,6 +116,29 @@ __device__ __forceinline__ uint64_t udiv128_small(u128 x, uint64_t d) {
         qw += d;
     }
     return q;
+}
+
+// 2^k as a double, exact for 0 <= k <= 1023.
+HS_HD double pow2_double(int k) {
+    const uint64_t bits = (uint64_t)(1023 + k) << 52;
+    double d;
+    memcpy(&d, &bits, sizeof d);
+    return d;
+}
+
+// ceil(2^sh / s) for 1 <= s < 2^44, sh <= 108, when the quotient is at most 2^62. The double
+// estimate x of 2^sh / s has a relative error below 2^-52, so x is within 2^11 of the quotient and
+// the residual R = 2^sh - x s is below 2^56 in magnitude: the low word of its 128-bit two's
+// complement is its value. One signed 64-bit division brings |R| below s, and one unit step makes
+// x the least value with x s >= 2^sh. No loop, on the device and the host alike.
+HS_HD uint64_t ceil_pow2_div(int sh, uint64_t s) {
+    uint64_t x = (uint64_t)((1.0 / (double)s) * pow2_double(sh));
+    int64_t R = (int64_t)(uint64_t)(((u128)1 << sh) - (u128)x * s);
+    const int64_t d = R / (int64_t)s;
+    x += (uint64_t)d;
+    R -= d * (int64_t)s;
+    if (R > 0) x += 1;
+    return x;
 }
 
 // floor(x / d) for a 128-bit x and a 32-bit d >= 1, with three 64-bit divisions.

@@ -104,9 +104,14 @@ void launch_attention_dec(const RowInfo* rows, const int* rowlist, int nrows, co
                           int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att, int lda,
                           cudaStream_t st);
 
+// The prefill attention's scratch: one slot per SM id (attn_scratch_slots reads the bound of the
+// device's SM ids), attn_scratch_bytes(slots, n_ctx) bytes in all.
+cudaError_t attn_scratch_slots(int* slots, cudaStream_t st);
+size_t attn_scratch_bytes(int slots, int n_ctx);
 void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, const AttnGroup* groups, int n_groups,
                          int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,
-                         const int32_t* table, int tlen, int P, int8_t* att, int lda, int* err, cudaStream_t st);
+                         const int32_t* table, int tlen, int P, int8_t* att, int lda, uint8_t* scratch, int scr_slots,
+                         int* err, cudaStream_t st);
 
 // The coder op: from the d16/tmax output of the logits GEMM, the interval of each row's query
 // in the table of taco_coder::FreqTable::from_weights(weights, bits). out: 3 u64 per row. `head`

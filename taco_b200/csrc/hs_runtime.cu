@@ -242,6 +242,8 @@ struct hs_batch {
     int* h_rowlist = nullptr;
     cudaEvent_t pass_done[2] = {nullptr, nullptr};  // recorded after a pass's read back, per half
     AttnGroup* d_groups = nullptr;   // the prefill groups of the pass
+    uint8_t* attn_scr = nullptr;     // the prefill attention's scratch, attn_scr_slots SM slots
+    int attn_scr_slots = 0;
     int* d_rowlist = nullptr;        // the other rows of the pass
     int n_groups = 0, n_rowlist = 0;
     bool v_scatter = false;  // some 32-row group of the pass is not a transposed v run
@@ -479,7 +481,7 @@ int forward(hs_batch* b, int R) {
             ProfScope p(b, OP_ATTN, attn_ops);
             launch_attention_tc(&b->tm_q, &b->tm_k, &b->tm_v, b->d_groups, b->n_groups, c.L, l, c.H, c.n_ctx,
                                 Ld.score_m, Ld.score_s, Ld.out_m, Ld.out_s, m->attn_exp, m->attn_len, c.softmax_p,
-                                b->att, c.Dp, m->dev->d_err, st);
+                                b->att, c.Dp, b->attn_scr, b->attn_scr_slots, m->dev->d_err, st);
             const int* rl = b->n_groups ? b->d_rowlist : nullptr;
             const int nr = b->n_groups ? b->n_rowlist : R;
             if (m->attn_dec)
@@ -588,6 +590,9 @@ int check_device_error(hs_batch* b) {
         cudaMemset(dev->d_err, 0, sizeof(int));
         if (herr == ERR_CODER_DIVISION)
             return fail(HS_CUDA, "the coder op's frequency division did not converge (code " + std::to_string(herr) + ")");
+        if (herr == ERR_ATTN_SCRATCH)
+            return fail(HS_CUDA, "the prefill attention ran on an SM without a scratch slot (code " +
+                                     std::to_string(herr) + ")");
         return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
     }
     return HS_OK;
@@ -1576,6 +1581,12 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
         b->kv_tma = getenv("HS_QKV_TMA") == nullptr || atoi(getenv("HS_QKV_TMA")) != 0;
     }
     if (m->attn_tc) {
+        // The prefill attention's scratch (the exp-table index of every key of the rows of one
+        // CTA, one slot per SM id): 256 KB per SM at n_ctx = 1024.
+        CK(attn_scratch_slots(&b->attn_scr_slots, b->stream));
+        const size_t scr = attn_scratch_bytes(b->attn_scr_slots, c.n_ctx);
+        if ((rc = dalloc(&b->attn_scr, scr, b->owned))) return rc;
+        b->bytes += scr;
         uint64_t heads = (uint64_t)slots * c.L * c.H;
         if ((rc = make_tmap(m->dev, &b->tm_q, b->qkv, R, c.QKVp, 128, 64)) ||
             (rc = make_tmap(m->dev, &b->tm_k, b->kc, heads * c.n_ctx, c.hd, 128, 64)) ||
