@@ -1,30 +1,38 @@
 // Prefill attention of the B200 HardShell backend on the tensor cores (tcgen05).
 //
-// One CTA per (group, head): a group is up to 128 rows of one slot at consecutive positions
-// pos0 .. pos0 + count - 1, attending causally to the keys 0 .. pos0 + count - 1 of its slot.
+// The unit of work is a tile: one (group, head). A group is up to 128 rows of one slot at
+// consecutive positions pos0 .. pos0 + count - 1, attending causally to the keys
+// 0 .. pos0 + count - 1 of its slot. The kernel is persistent: one CTA per SM takes the tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... in the host's order (groups longest first, the
+// heads of a group consecutive).
 // The integer softmax of crates/hardshell/src/softmax.rs:78 needs the exact row max before any
-// weight and the exact row sum before any probability, so the scores S = Q K^T are computed
-// twice per 128-key chunk on the tensor cores (cheap: K = 64):
+// weight and the exact row sum before any probability, so a tile runs three passes over its
+// 128-key chunks, with S = Q K^T computed twice on the tensor cores (cheap: K = 64):
 //   pass 1: S -> the max and min dot of each row (score() is monotone in the dot, so the max
 //           score is max(score(maxdot), score(mindot)), as in the reference GPU kernel);
 //   pass 2: S -> the table index d = min(max - score, len - 1) -> e = attn_exp[d] -> the row sum;
-//           each key's d (u16) goes to this SM's slot of a scratch buffer in global memory;
+//           each key's d (u16) goes to this CTA's slot of a scratch buffer in global memory;
 //   pass 3: d back from the scratch (no third S) -> p = floor(e * 2^P / sum) (an exact
 //           multiply-shift), split into four unsigned bytes p = p0 + 2^8 p1 + 2^16 p2 + 2^24 p3,
 //           written to shared memory as four u8 A operands; O_k += P_k V (u8 x s8) in TMEM.
-// The scratch slot is picked by %smid: a CTA needs more than half of an SM's shared memory, so at
-// most one runs on an SM at a time, and the slots of all SMs (n_ctx u16 per row, 256 KB at
-// n_ctx = 1024) stay in L2 between the two passes.
 // Then acc = sum_k 2^(8k) O_k (exact: each O_k has at most n_ctx terms below 2^15) and
 // att = clamp(rescale(acc, out_m, out_s), -127, 127) (crates/hardshell/src/gpt2/reference.rs:252-284).
 //
-// Operands come in by TMA (no multicast): Q [128 x 64] and K chunks [128 x 64] with the 64-byte
-// swizzle, V^T chunks [64 x 128] with the 128-byte swizzle from the transposed values cache.
-// (A fold pass runs this kernel on 96 % of its rows, so one S pass less is most of a pass.)
-// Warps 0..15 do the softmax: TMEM lane group warp % 4 (32 rows) and key quarter warp / 4 (32
-// of the 128 keys of a chunk). Warp 16 is the TMA producer, warp 17 owns TMEM and issues the
-// MMAs: S of chunk i + 1 is issued before P V of chunk i, and P is double-buffered, so the
-// softmax warps always have work while the tensor core runs. Every wait is bounded.
+// Tiles overlap. Pass 3 reads no S, so the first two S of the next tile are computed while the
+// softmax warps run pass 3; and a tile's output (its epilogue) is read from TMEM after the pass 1
+// of the next tile, when its last P V products are done. The softmax warps run, per tile t:
+// pass 1 (t), epilogue (t - 1), pass 2 (t), pass 3 (t). The P V of tile t + 1 starts only after
+// every softmax thread has written its first P planes, so after its epilogue of tile t.
+//
+// Operands come in by TMA (no multicast): Q [128 x 64] (double-buffered) and K chunks [128 x 64]
+// with the 64-byte swizzle, V^T chunks [64 x 128] with the 128-byte swizzle from the transposed
+// values cache. Warps 0..15 do the softmax: TMEM lane group warp % 4 (32 rows) and key quarter
+// warp / 4 (32 of the 128 keys of a chunk). Warp 16 loads Q and K, warp 17 owns TMEM and issues
+// the MMAs (S two items ahead of the softmax, across tiles), warp 18 loads V: a producer waiting
+// for a K buffer never holds up a V load that the softmax needs first. The scratch slot of a CTA
+// is 32 KB per 128-key chunk of n_ctx (256 KB at n_ctx = 1024); a thread reads back only what it
+// wrote itself, and the slots of the resident CTAs stay in L2 between the passes. Every wait is
+// bounded.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -42,20 +50,27 @@ constexpr int KC = 128;        // keys per chunk
 constexpr int HDIM = 64;       // head width of this kernel
 constexpr int EW = 16;         // softmax warps
 constexpr int ETH = 32 * EW;   // softmax threads
-constexpr int ATHREADS = ETH + 64;
-constexpr int Q_BYTES = GM * HDIM;        // 8 KB
+constexpr int W_QK = EW;       // the Q and K producer warp
+constexpr int W_MMA = EW + 1;  // the TMEM owner and MMA issuer
+constexpr int W_V = EW + 2;    // the V producer warp
+constexpr int ATHREADS = ETH + 96;
+constexpr int Q_BYTES = GM * HDIM;        // 8 KB, double-buffered
 constexpr int K_BYTES = KC * HDIM;        // 8 KB
 constexpr int V_BYTES = HDIM * KC;        // 8 KB
 constexpr int P_BYTES = 4 * GM * KC;      // 64 KB (four planes), double-buffered
 constexpr int TABLE_MAX = 8192;           // attn_exp entries kept in shared memory
-// The scratch slot of one SM: per 128-key chunk, key quarter, 16-byte word (8 keys) and row, the
+// The row exchange: max and min dots (regions 0..7) and the sums (regions 8..11) apart, so that a
+// warp's pass 1 of the next tile never writes where a slower warp still reads this tile's sums.
+constexpr int XREGIONS = 12;
+// The scratch slot of one CTA: per 128-key chunk, key quarter, 16-byte word (8 keys) and row, the
 // u16 table indices of 8 keys, so that a warp's 32 rows store and load 512 contiguous bytes.
 constexpr size_t SCR_CHUNK_BYTES = 4 * 4 * GM * 16;  // 32 KB per chunk of 128 keys
-constexpr size_t ASMEM =
-    (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 4 * TABLE_MAX + 8 * GM * 8 + 512 + 1024;
+constexpr size_t ASMEM = 2 * (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 4 * TABLE_MAX +
+                         XREGIONS * GM * 8 + 512 + 1024;
+static_assert(ASMEM <= 232448, "the attention CTA's shared memory exceeds the 227 KB per block");
 
 struct __align__(8) ABars {
-    uint64_t q_full;
+    uint64_t q_full[2], q_empty[2];
     uint64_t k_full[2], k_empty[2];
     uint64_t v_full[2], v_empty[2];
     uint64_t s_full[2], s_empty[2];
@@ -64,6 +79,10 @@ struct __align__(8) ABars {
     uint64_t t_full;  // the exp table in shared memory
     uint32_t tmem_base;
 };
+static_assert(sizeof(ABars) <= 512, "the barriers exceed their shared-memory slot");
+
+__device__ __forceinline__ int tile_chunks(const AttnGroup& g) { return ((int)g.pos0 + (int)g.count + KC - 1) / KC; }
+
 
 // The shared-memory descriptor of a K-major tile with the 64-byte swizzle (rows of 64 bytes,
 // 8-row groups 512 bytes apart), descriptor version 1, layout type 4 = SWIZZLE_64B.
@@ -102,47 +121,49 @@ __device__ __forceinline__ int32_t dist_of(int64_t M, int32_t dot, int32_t sm, i
     }
 }
 
+
+// 32 lanes x 32 bits, 8 columns: thread t of the warp gets columns c..c+7 of lane (base + t).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
 template <bool NARROW, bool SSHI>
 __global__ void __launch_bounds__(ATHREADS, 1)
     k_attention_tc(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const AttnGroup* groups, int L, int layer, int H,
+                   const __grid_constant__ CUtensorMap tmV, const AttnGroup* groups, int T, int L, int layer, int H,
                    int n_ctx, int32_t sm, int ss, int32_t om, int os, const int32_t* table, int tlen, int P,
                    int8_t* att, int lda, uint8_t* scratch, int scr_slots, int* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint32_t smid;
-    asm("mov.u32 %0, %%smid;" : "=r"(smid));
-    if (smid >= (uint32_t)scr_slots) {  // the same for every thread of the CTA: nothing started yet
+    if (blockIdx.x >= (uint32_t)scr_slots) {  // the same for every thread of the CTA: nothing started yet
         if (threadIdx.x == 0) atomicCAS(err, 0, ERR_ATTN_SCRATCH);
         return;
     }
     // Aligned to 1,024 bytes by an offset from the __shared__ array itself (not through an
     // integer cast), so every access below stays a shared-memory access with 32-bit addresses.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint8_t* sQ = smem;
-    uint8_t* sK = sQ + Q_BYTES;                 // 2 x 8 KB
+    uint8_t* sQ = smem;                         // 2 x 8 KB
+    uint8_t* sK = sQ + 2 * Q_BYTES;             // 2 x 8 KB
     uint8_t* sV = sK + 2 * K_BYTES;             // 2 x 8 KB
     uint8_t* sP = sV + 2 * V_BYTES;             // 2 x 4 planes x 16 KB
     int32_t* sT = reinterpret_cast<int32_t*>(sP + 2 * P_BYTES);
-    int64_t* sX = reinterpret_cast<int64_t*>(sT + TABLE_MAX);  // [2][4][GM] row exchange
-    ABars* bars = reinterpret_cast<ABars*>(sX + 8 * GM);
+    int64_t* sX = reinterpret_cast<int64_t*>(sT + TABLE_MAX);  // [XREGIONS][GM] row exchange
+    ABars* bars = reinterpret_cast<ABars*>(sX + XREGIONS * GM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const AttnGroup grp = groups[blockIdx.x];
-    const int h = blockIdx.y;
-    const int n_keys = (int)grp.pos0 + (int)grp.count;
-    const int nch = (n_keys + KC - 1) / KC;
-    const size_t head = ((size_t)grp.slot * L + layer) * H + h;
+    const int t0 = (int)blockIdx.x, tstep = (int)gridDim.x;
+    const int n_mine = t0 < T ? (T - t0 + tstep - 1) / tstep : 0;  // this CTA's tiles
 
     if (threadIdx.x == 0) {
-        mbar_init(&bars->q_full, 1);
         for (int i = 0; i < 2; i++) {
+            mbar_init(&bars->q_full[i], 1);
+            mbar_init(&bars->q_empty[i], 1);
             mbar_init(&bars->k_full[i], 1);
             mbar_init(&bars->k_empty[i], 1);
             mbar_init(&bars->v_full[i], 1);
             mbar_init(&bars->v_empty[i], 1);
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->s_empty[i], ETH);
-        }
-        for (int i = 0; i < 2; i++) {
             mbar_init(&bars->p_full[i], ETH);
             mbar_init(&bars->p_empty[i], 1);
         }
@@ -150,7 +171,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         mbar_init(&bars->t_full, 1);
         fence_barrier_init();
     }
-    if (warp == EW + 1) {
+    if (warp == W_MMA) {
         tmem_alloc(&bars->tmem_base, 512);
         tmem_relinquish();
         tc_fence_before();
@@ -160,84 +181,89 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
 
-    if (warp == EW) {
-        // TMA producer: Q, then K chunks for the three passes, with the V^T chunks in pass 3.
+    if (warp == W_QK) {
+        // Q of each tile (buffer seq & 1, free once the tile before the last has its S), then the
+        // K chunks of its passes 1 and 2, in the order the MMA issuer uses them.
         if (lane == 0) {
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
-            prefetch_tmap(&tmV);
             // The exp table (its buffer is padded to 16 bytes), needed from pass 2 on.
             const uint32_t tbytes = (uint32_t)((tl * 4 + 15) & ~15);
             mbar_arrive_expect_tx(&bars->t_full, tbytes);
             bulk_load(sT, table, tbytes, &bars->t_full);
-            mbar_arrive_expect_tx(&bars->q_full, Q_BYTES);
-            tma_load_2d(sQ, &tmQ, &bars->q_full, h * HDIM, (int)grp.first_row);
-            int ks = 0, vs = 0;
-            uint32_t kph = 0, vph = 0;
+            int ks = 0;
+            uint32_t kph = 0;
             bool ok = true;
-            // V^T chunk c of pass 3 (both buffers are free at the start: chunks 0 and 1 load first).
-            auto load_v = [&](int c) -> bool {
-                if (!mbar_wait(&bars->v_empty[vs], vph ^ 1, err, 12)) return false;
-                mbar_arrive_expect_tx(&bars->v_full[vs], V_BYTES);
-                tma_load_2d(sV + vs * V_BYTES, &tmV, &bars->v_full[vs], c * KC, (int)(head * HDIM));
-                if (++vs == 2) {
-                    vs = 0;
-                    vph ^= 1;
-                }
-                return true;
-            };
-            for (int c = 0; c < nch && c < 2 && ok; c++) ok = load_v(c);
-            for (int it = 0; it < 2 * nch && ok; it++) {
-                int c = it % nch;
-                if (!mbar_wait(&bars->k_empty[ks], kph ^ 1, err, 11)) break;
-                mbar_arrive_expect_tx(&bars->k_full[ks], K_BYTES);
-                tma_load_2d(sK + ks * K_BYTES, &tmK, &bars->k_full[ks], 0, (int)(head * n_ctx) + c * KC);
-                if (++ks == 2) {
-                    ks = 0;
-                    kph ^= 1;
+            for (int seq = 0; seq < n_mine && ok; seq++) {
+                const int t = t0 + seq * tstep;
+                const AttnGroup grp = groups[t / H];
+                const int h = t % H, nch = tile_chunks(grp);
+                const size_t head = ((size_t)grp.slot * L + layer) * H + h;
+                const int qb = seq & 1;
+                if (!mbar_wait(&bars->q_empty[qb], ((seq >> 1) & 1) ^ 1, err, 10)) break;
+                mbar_arrive_expect_tx(&bars->q_full[qb], Q_BYTES);
+                tma_load_2d(sQ + qb * Q_BYTES, &tmQ, &bars->q_full[qb], h * HDIM, (int)grp.first_row);
+                for (int it = 0; it < 2 * nch; it++) {
+                    const int c = it < nch ? it : it - nch;
+                    if (!mbar_wait(&bars->k_empty[ks], kph ^ 1, err, 11)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&bars->k_full[ks], K_BYTES);
+                    tma_load_2d(sK + ks * K_BYTES, &tmK, &bars->k_full[ks], 0, (int)(head * n_ctx) + c * KC);
+                    if (++ks == 2) {
+                        ks = 0;
+                        kph ^= 1;
+                    }
                 }
             }
-            for (int c = 2; c < nch && ok; c++) ok = load_v(c);
         }
-    } else if (warp == EW + 1) {
-        // MMA issuer: S of every chunk of passes 1 and 2, then the P V of each chunk of pass 3 as
-        // its planes are written (P is double-buffered).
+    } else if (warp == W_V) {
+        // The V^T chunks of each tile's pass 3.
+        if (lane == 0) {
+            prefetch_tmap(&tmV);
+            int vs = 0;
+            uint32_t vph = 0;
+            bool ok = true;
+            for (int seq = 0; seq < n_mine && ok; seq++) {
+                const int t = t0 + seq * tstep;
+                const AttnGroup grp = groups[t / H];
+                const int h = t % H, nch = tile_chunks(grp);
+                const size_t head = ((size_t)grp.slot * L + layer) * H + h;
+                for (int c = 0; c < nch; c++) {
+                    if (!mbar_wait(&bars->v_empty[vs], vph ^ 1, err, 12)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&bars->v_full[vs], V_BYTES);
+                    tma_load_2d(sV + vs * V_BYTES, &tmV, &bars->v_full[vs], c * KC, (int)(head * HDIM));
+                    if (++vs == 2) {
+                        vs = 0;
+                        vph ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == W_MMA) {
+        // MMA issuer. The S items (pass 1 then pass 2 of each tile, nch chunks each) run two ahead
+        // of the softmax warps' use, across tiles: each S item the softmax warps take frees the
+        // S buffer of the item two later. After the S items of tile t's passes (which include the
+        // first two of tile t + 1), the P V of tile t as its planes are written, then o_full.
         if (lane == 0) {
             const uint32_t id_s = idesc_i8(GM, KC, true, true);
             const uint32_t id_pv = idesc_i8(GM, HDIM, false, true);
-            bool ok = mbar_wait(&bars->q_full, 0, err, 13);
-            tc_fence_after();
-            const uint32_t qa = smem_u32(sQ);
-            int ks = 0, vs = 0;
-            uint32_t kph = 0, vph = 0;
-            auto do_pv = [&](int c) -> bool {
-                const int pb = c & 1;
-                if (!mbar_wait(&bars->p_full[pb], (c >> 1) & 1, err, 16)) return false;
-                if (!mbar_wait(&bars->v_full[vs], vph, err, 17)) return false;
+            // The S stream: tile s_seq, item s_j of its 2 s_nch.
+            int s_seq = 0, s_j = 0, s_nch = n_mine > 0 ? tile_chunks(groups[t0 / H]) : 0;
+            int ks = 0, sit = 0;
+            uint32_t kph = 0;
+            auto issue_s = [&]() -> bool {
+                if (s_seq >= n_mine) return true;  // no S item left
+                const int sb = sit & 1, qb = s_seq & 1;
+                if (s_j == 0 && !mbar_wait(&bars->q_full[qb], (s_seq >> 1) & 1, err, 13)) return false;
+                if (!mbar_wait(&bars->s_empty[sb], ((sit >> 1) & 1) ^ 1, err, 14)) return false;
+                if (!mbar_wait(&bars->k_full[ks], kph, err, 15)) return false;
                 tc_fence_after();
-                const uint32_t vb = smem_u32(sV + vs * V_BYTES);
-#pragma unroll
-                for (int pl = 0; pl < 4; pl++) {
-                    const uint32_t pa = smem_u32(sP + pb * P_BYTES + pl * (GM * KC));
-                    const uint32_t o = tmem + 2 * KC + pl * HDIM;
-#pragma unroll
-                    for (int k = 0; k < KC / 32; k++)
-                        mma_i8(o, sdesc_sw128(pa + 32 * k), sdesc_sw128(vb + 32 * k), id_pv, (c > 0 || k > 0) ? 1u : 0u);
-                }
-                mma_commit(&bars->v_empty[vs]);
-                mma_commit(&bars->p_empty[pb]);
-                if (++vs == 2) {
-                    vs = 0;
-                    vph ^= 1;
-                }
-                return true;
-            };
-            for (int it = 0; it < 2 * nch && ok; it++) {
-                const int sb = it & 1;
-                const uint32_t sph = (it >> 1) & 1;
-                if (!mbar_wait(&bars->s_empty[sb], sph ^ 1, err, 14)) break;
-                if (!mbar_wait(&bars->k_full[ks], kph, err, 15)) break;
-                tc_fence_after();
+                const uint32_t qa = smem_u32(sQ + qb * Q_BYTES);
                 const uint32_t kb = smem_u32(sK + ks * K_BYTES);
                 const uint32_t d = tmem + sb * KC;
 #pragma unroll
@@ -249,25 +275,58 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     ks = 0;
                     kph ^= 1;
                 }
+                sit++;
+                if (++s_j == 2 * s_nch) {
+                    mma_commit(&bars->q_empty[qb]);  // Q of this tile is read
+                    s_j = 0;
+                    if (++s_seq < n_mine) s_nch = tile_chunks(groups[(t0 + s_seq * tstep) / H]);
+                }
+                return true;
+            };
+            bool ok = issue_s() && issue_s();
+            int vs = 0, pit = 0;
+            uint32_t vph = 0;
+            for (int seq = 0; seq < n_mine && ok; seq++) {
+                const int nch = tile_chunks(groups[(t0 + seq * tstep) / H]);
+                for (int j = 0; j < 2 * nch && ok; j++) ok = issue_s();
+                for (int c = 0; c < nch && ok; c++, pit++) {
+                    const int pb = pit & 1;
+                    if (!mbar_wait(&bars->p_full[pb], (pit >> 1) & 1, err, 16)) ok = false;
+                    else if (!mbar_wait(&bars->v_full[vs], vph, err, 17)) ok = false;
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t vb = smem_u32(sV + vs * V_BYTES);
+#pragma unroll
+                    for (int pl = 0; pl < 4; pl++) {
+                        const uint32_t pa = smem_u32(sP + pb * P_BYTES + pl * (GM * KC));
+                        const uint32_t o = tmem + 2 * KC + pl * HDIM;
+#pragma unroll
+                        for (int k = 0; k < KC / 32; k++)
+                            mma_i8(o, sdesc_sw128(pa + 32 * k), sdesc_sw128(vb + 32 * k), id_pv,
+                                   (c > 0 || k > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&bars->v_empty[vs]);
+                    mma_commit(&bars->p_empty[pb]);
+                    if (++vs == 2) {
+                        vs = 0;
+                        vph ^= 1;
+                    }
+                }
+                if (ok) mma_commit(&bars->o_full);
             }
-            for (int c = 0; c < nch && ok; c++) ok = do_pv(c);
-            mma_commit(&bars->o_full);
         }
     } else {
         // Softmax warps: one row per thread, 32 keys of each chunk (quarter qt = warp / 4).
         const int g = warp & 3, qt = warp >> 2;
         const int row = g * 32 + lane;
-        const int rpos = (int)grp.pos0 + row;  // rows past the group compute harmless values
         const uint32_t tbase = tmem + ((uint32_t)(g * 32) << 16) + (uint32_t)(qt * 32);
         const bool fast = ss >= 0 && ss <= 62;
         const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
         const int32_t last = tl - 1;
-        // The last position of this warp's 32 rows: a key slice past it is masked for every lane.
-        const int wlast = (int)grp.pos0 + g * 32 + 31;
-        // The first: a key slice at or below it is whole for every lane. The choice between the
-        // whole and the masked path is the warp's, so the diagonal slice takes the masked path
-        // once instead of both paths diverged.
-        const int wfirst = (int)grp.pos0 + g * 32;
+        const double omsc = (double)om * exp2_neg(os);
+        // This thread's words of the CTA's scratch slot (the same size for every CTA).
+        const size_t slot_bytes = (size_t)((n_ctx + KC - 1) / KC) * SCR_CHUNK_BYTES;
+        uint4* scr = reinterpret_cast<uint4*>(scratch + (size_t)blockIdx.x * slot_bytes) + qt * 4 * GM + row;
         // The table index min(M - score(dot), last); NARROW: the score is the low word of the
         // 64-bit shift (one shift of the high word when ss >= 32, a funnel shift below).
         auto dist = [&](int64_t M, int32_t dot) -> int32_t {
@@ -282,239 +341,268 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                 return dist_of<false>(M, dot, sm, ss, fast, hround, last);
             }
         };
-        int it = 0;
-        // Pass 1: the max and min dot over the row's causal keys.
-        int32_t maxd = INT32_MIN, mind = INT32_MAX;
-        for (int c = 0; c < nch; c++, it++) {
-            const int sb = it & 1;
-            mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 21);
+        // The epilogue of a tile: acc = sum_k 2^(8k) O_k for this thread's 16 channels, then the
+        // output rescale. o_full completes once per tile, so the tile's sequence number gives the
+        // phase.
+        auto epilogue = [&](int eseq, uint32_t first_row, uint32_t count, int eh) {
+            mbar_wait(&bars->o_full, (uint32_t)(eseq & 1), err, 25);
             __syncwarp();
             tc_fence_after();
-            uint32_t v[32];
-            tmem_ld32(tbase + sb * KC, v);
-            tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(&bars->s_empty[sb]);
-            const int j0 = c * KC + qt * 32;
-            if (j0 > wlast) {
-                // every key of this slice is masked for this warp's rows
-            } else if (j0 + 31 <= wfirst) {
-                // A max/min tree instead of one dependent chain of 32 steps.
-                int32_t mx[8], mn[8];
+            // Two halves of 8 channels, so that the loads and the estimates of one half fit in the
+            // registers that the next tile's live values leave.
+            uint32_t packed[4];
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                uint32_t o[4][8];
+#pragma unroll
+                for (int pl = 0; pl < 4; pl++)
+                    tmem_ld8(tmem + ((uint32_t)(g * 32) << 16) + 2 * KC + pl * HDIM + qt * 16 + half * 8, o[pl]);
+                tmem_ld_wait();
+                // att = clamp(rescale(acc, om, os), -127, 127), |acc| <= 2^30 * 128 (rescale_clamp127):
+                // the double estimates of all 8 values first, branch-free, so their latencies overlap;
+                // the values too close to a rounding boundary take the exact rule afterwards.
+                int64_t accs[8];
+                int32_t ys[8];
+                uint32_t slow = os > 95 ? 0xFFu : 0u;
 #pragma unroll
                 for (int q = 0; q < 8; q++) {
-                    mx[q] = max(max((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), max((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
-                    mn[q] = min(min((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), min((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
+                    accs[q] = ((((int64_t)(int32_t)o[3][q] * 256 + (int32_t)o[2][q]) * 256 + (int32_t)o[1][q]) * 256) +
+                              (int32_t)o[0][q];
+                    const double z = fma((double)accs[q], omsc, 0.5);
+                    const double zc = fmin(fmax(z, -1024.0), 1024.0);
+                    const double fl = floor(zc);
+                    const double fr = zc - fl;
+                    ys[q] = min(max((int32_t)fl, -127), 127);
+                    const bool near =
+                        fabs(z) < 1024.0 && !(fr > 9.094947017729282e-13 && fr < 1.0 - 9.094947017729282e-13);
+                    slow |= (uint32_t)near << q;
+                }
+                if (slow) {
+#pragma unroll
+                    for (int q = 0; q < 8; q++)
+                        if ((slow >> q) & 1) ys[q] = (int32_t)clamp128(rescale128(accs[q], om, (uint32_t)os), -127, 127);
                 }
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    mx[q] = max(mx[q], mx[q + 4]);
-                    mn[q] = min(mn[q], mn[q + 4]);
-                }
-                maxd = max(maxd, max(max(mx[0], mx[1]), max(mx[2], mx[3])));
-                mind = min(mind, min(min(mn[0], mn[1]), min(mn[2], mn[3])));
-            } else {
+                for (int w = 0; w < 2; w++)
+                    packed[2 * half + w] = __byte_perm(__byte_perm(ys[4 * w], ys[4 * w + 1], 0x0040),
+                                                       __byte_perm(ys[4 * w + 2], ys[4 * w + 3], 0x0040), 0x5410);
+            }
+            tc_fence_before();
+            if (row < (int)count)
+                *reinterpret_cast<uint4*>(att + (size_t)(first_row + row) * lda + eh * HDIM + qt * 16) =
+                    make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        };
+        int sit = 0, pit = 0;  // S items taken, P chunks written (across tiles)
+        uint32_t prev_first = 0, prev_count = 0;
+        int prev_h = 0;
+        for (int seq = 0; seq <= n_mine; seq++) {
+            if (seq == n_mine) {
+                if (seq > 0) epilogue(seq - 1, prev_first, prev_count, prev_h);
+                break;
+            }
+            const int t = t0 + seq * tstep;
+            const AttnGroup grp = groups[t / H];
+            const int h = t % H, nch = tile_chunks(grp);
+            const int rpos = (int)grp.pos0 + row;  // rows past the group compute harmless values
+            // The last position of this warp's 32 rows: a key slice past it is masked for every lane.
+            const int wlast = (int)grp.pos0 + g * 32 + 31;
+            // The first: a key slice at or below it is whole for every lane. The choice between the
+            // whole and the masked path is the warp's, so the diagonal slice takes the masked path
+            // once instead of both paths diverged.
+            const int wfirst = (int)grp.pos0 + g * 32;
+            // Pass 1: the max and min dot over the row's causal keys.
+            int32_t maxd = INT32_MIN, mind = INT32_MAX;
+            for (int c = 0; c < nch; c++, sit++) {
+                const int sb = sit & 1;
+                mbar_wait(&bars->s_full[sb], (sit >> 1) & 1, err, 21);
+                __syncwarp();
+                tc_fence_after();
+                uint32_t v[32];
+                tmem_ld32(tbase + sb * KC, v);
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(&bars->s_empty[sb]);
+                const int j0 = c * KC + qt * 32;
+                if (j0 > wlast) {
+                    // every key of this slice is masked for this warp's rows
+                } else if (j0 + 31 <= wfirst) {
+                    // A max/min tree instead of one dependent chain of 32 steps.
+                    int32_t mx[8], mn[8];
 #pragma unroll
-                for (int q = 0; q < 32; q++) {
-                    if (j0 + q <= rpos) {
-                        int32_t dv = (int32_t)v[q];
-                        maxd = dv > maxd ? dv : maxd;
-                        mind = dv < mind ? dv : mind;
+                    for (int q = 0; q < 8; q++) {
+                        mx[q] = max(max((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), max((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
+                        mn[q] = min(min((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), min((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        mx[q] = max(mx[q], mx[q + 4]);
+                        mn[q] = min(mn[q], mn[q + 4]);
+                    }
+                    maxd = max(maxd, max(max(mx[0], mx[1]), max(mx[2], mx[3])));
+                    mind = min(mind, min(min(mn[0], mn[1]), min(mn[2], mn[3])));
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 32; q++) {
+                        if (j0 + q <= rpos) {
+                            int32_t dv = (int32_t)v[q];
+                            maxd = dv > maxd ? dv : maxd;
+                            mind = dv < mind ? dv : mind;
+                        }
                     }
                 }
             }
-        }
-        sX[(0 * 4 + qt) * GM + row] = maxd;
-        sX[(1 * 4 + qt) * GM + row] = mind;
-        named_bar(1, ETH);
+            sX[(0 * 4 + qt) * GM + row] = maxd;
+            sX[(1 * 4 + qt) * GM + row] = mind;
+            named_bar(1, ETH);
 #pragma unroll
-        for (int o = 0; o < 4; o++) {
-            int64_t a = sX[(0 * 4 + o) * GM + row], b = sX[(1 * 4 + o) * GM + row];
-            maxd = (int32_t)(a > maxd ? a : maxd);
-            mind = (int32_t)(b < mind ? b : mind);
-        }
-        int64_t M = INT64_MIN;
-        if (maxd >= mind) {
-            int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
-            M = s1 > s2 ? s1 : s2;
-        }
-        // Pass 2: the row sum of e, and each key's table index into this SM's scratch slot (the
-        // thread's 32 keys of a chunk as four 16-byte words, word k of the warp's 32 rows at 512
-        // contiguous bytes). The same thread reads them back in pass 3.
-        const size_t slot_bytes = (size_t)((n_ctx + KC - 1) / KC) * SCR_CHUNK_BYTES;  // the same for every CTA
-        uint4* scr = reinterpret_cast<uint4*>(scratch + (size_t)smid * slot_bytes) + qt * 4 * GM + row;
-        mbar_wait(&bars->t_full, 0, err, 26);
-        uint64_t sum = 0;
-        for (int c = 0; c < nch; c++, it++) {
-            const int sb = it & 1;
-            mbar_wait(&bars->s_full[sb], (it >> 1) & 1, err, 22);
-            __syncwarp();
-            tc_fence_after();
-            uint32_t v[32];
-            tmem_ld32(tbase + sb * KC, v);
-            tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(&bars->s_empty[sb]);
-            const int j0 = c * KC + qt * 32;
-            if (j0 > wlast) continue;  // masked for every lane: nothing stored, nothing read back
-            uint32_t dk[16];
-#pragma unroll
-            for (int q = 0; q < 32; q += 2) {
-                const uint32_t d0 = (uint32_t)dist(M, (int32_t)v[q]), d1 = (uint32_t)dist(M, (int32_t)v[q + 1]);
-                dk[q >> 1] = d0 | (d1 << 16);
+            for (int o = 0; o < 4; o++) {
+                int64_t a = sX[(0 * 4 + o) * GM + row], b = sX[(1 * 4 + o) * GM + row];
+                maxd = (int32_t)(a > maxd ? a : maxd);
+                mind = (int32_t)(b < mind ? b : mind);
             }
-            uint4* w = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
-#pragma unroll
-            for (int k = 0; k < 4; k++) __stcg(w + k * GM, make_uint4(dk[4 * k], dk[4 * k + 1], dk[4 * k + 2], dk[4 * k + 3]));
-            if (j0 + 31 <= wfirst) {
-                // Four partial sums: independent chains for the look-ups and adds.
-                uint64_t ps[4] = {0, 0, 0, 0};
-#pragma unroll
-                for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
-                sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-            } else {
-#pragma unroll
-                for (int q = 0; q < 32; q++)
-                    if (j0 + q <= rpos) sum += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
+            int64_t M = INT64_MIN;
+            if (maxd >= mind) {
+                int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
+                M = s1 > s2 ? s1 : s2;
             }
-        }
-        // Pass 3's first table indices are on their way while the sums are exchanged.
-        auto load_idx = [&](int c, uint4* dst) {
-            if (c < nch && c * KC + qt * 32 <= wlast) {
-                const uint4* r = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
+            // The tile before: its last P V products ran while this pass 1 did.
+            if (seq > 0) epilogue(seq - 1, prev_first, prev_count, prev_h);
+            prev_first = grp.first_row;
+            prev_count = grp.count;
+            prev_h = h;
+            // Pass 2: the row sum of e, and each key's table index into this CTA's scratch slot (the
+            // thread's 32 keys of a chunk as four 16-byte words, word k of the warp's 32 rows at 512
+            // contiguous bytes). The same thread reads them back in pass 3.
+            if (seq == 0) mbar_wait(&bars->t_full, 0, err, 26);
+            uint64_t sum = 0;
+            for (int c = 0; c < nch; c++, sit++) {
+                const int sb = sit & 1;
+                mbar_wait(&bars->s_full[sb], (sit >> 1) & 1, err, 22);
+                __syncwarp();
+                tc_fence_after();
+                uint32_t v[32];
+                tmem_ld32(tbase + sb * KC, v);
+                tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(&bars->s_empty[sb]);
+                const int j0 = c * KC + qt * 32;
+                if (j0 > wlast) continue;  // masked for every lane: nothing stored, nothing read back
+                uint32_t dk[16];
 #pragma unroll
-                for (int k = 0; k < 4; k++) dst[k] = __ldcg(r + k * GM);
-            }
-        };
-        uint4 nxt[4] = {};
-        load_idx(0, nxt);
-        named_bar(1, ETH);  // everyone has read sX (pass 1) before it is reused
-        sX[qt * GM + row] = (int64_t)sum;
-        named_bar(1, ETH);
-        sum = 0;
+                for (int q = 0; q < 32; q += 2) {
+                    const uint32_t d0 = (uint32_t)dist(M, (int32_t)v[q]), d1 = (uint32_t)dist(M, (int32_t)v[q + 1]);
+                    dk[q >> 1] = d0 | (d1 << 16);
+                }
+                uint4* w = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
 #pragma unroll
-        for (int o = 0; o < 4; o++) sum += (uint64_t)sX[o * GM + row];
-        if (sum == 0) sum = 1;
-        // p = floor(e * 2^P / sum) for every e < 2^31 as floor(e * mg / 2^(31 + l)): the numerators
-        // e * 2^P have N = 31 + P <= 61 bits, 2^l >= sum and mg = ceil(2^(N + l) / sum) <= 2^(N + 1),
-        // so the quotient is exact (Granlund and Montgomery, "Division by invariant integers using
-        // multiplication", 1994, Theorem 4.2). With mg = mh 2^32 + ml and u = e mh + (e ml >> 32),
-        // p = u >> (l - 1): two 32x32 multiplies per key.
-        int l = 64 - __clzll((long long)(sum - 1));
-        if (l < 1) l = 1;
-        const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
-        const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
-        const int psh = l - 1;
-        // Pass 3: the table indices back from the scratch (the next chunk's loads in flight while
-        // this one is used), p, its four byte planes into shared memory (128-byte swizzle,
-        // K-major), P V.
-        const uint32_t rsw = (uint32_t)(row & 7);
-        for (int c = 0; c < nch; c++) {
-            const int j0 = c * KC + qt * 32;
-            uint32_t dk[16];
+                for (int k = 0; k < 4; k++)
+                    __stcg(w + k * GM, make_uint4(dk[4 * k], dk[4 * k + 1], dk[4 * k + 2], dk[4 * k + 3]));
+                if (j0 + 31 <= wfirst) {
+                    // Four partial sums: independent chains for the look-ups and adds.
+                    uint64_t ps[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                dk[4 * k] = nxt[k].x;
-                dk[4 * k + 1] = nxt[k].y;
-                dk[4 * k + 2] = nxt[k].z;
-                dk[4 * k + 3] = nxt[k].w;
-            }
-            load_idx(c + 1, nxt);
-            auto prob = [&](int q) -> uint32_t {
-                const uint32_t e = (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
-                const uint64_t t = (uint64_t)e * ml;
-                const uint64_t u = (uint64_t)e * mh + (t >> 32);
-                return (uint32_t)(u >> psh);
-            };
-            uint32_t pv[32];
-            if (j0 > wlast) {
+                    for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
+                    sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+                } else {
 #pragma unroll
-                for (int q = 0; q < 32; q++) pv[q] = 0u;
-            } else if (j0 + 31 <= wfirst) {
-#pragma unroll
-                for (int q = 0; q < 32; q++) pv[q] = prob(q);
-            } else {
-#pragma unroll
-                for (int q = 0; q < 32; q++) pv[q] = j0 + q <= rpos ? prob(q) : 0u;
-            }
-            // The four byte planes of each 4-key word: a 4x4 byte transpose with byte permutes.
-            uint32_t pw[4][8];  // [plane][4-key word] of this thread's 32 keys
-#pragma unroll
-            for (int w = 0; w < 8; w++) {
-                const uint32_t a = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x5140);
-                const uint32_t b2 = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x7362);
-                const uint32_t c2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x5140);
-                const uint32_t d2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x7362);
-                pw[0][w] = __byte_perm(a, c2, 0x5410);
-                pw[1][w] = __byte_perm(a, c2, 0x7632);
-                pw[2][w] = __byte_perm(b2, d2, 0x5410);
-                pw[3][w] = __byte_perm(b2, d2, 0x7632);
-            }
-            // The P V of chunk c - 2 (the same buffer) must be done before its planes are overwritten.
-            const int pb = c & 1;
-            mbar_wait(&bars->p_empty[pb], ((c >> 1) & 1) ^ 1, err, 24);
-            __syncwarp();
-            uint8_t* prow = sP + pb * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-            for (int pl = 0; pl < 4; pl++) {
-                uint8_t* base = prow + pl * (GM * KC);
-#pragma unroll
-                for (int cc = 0; cc < 2; cc++) {
-                    const uint32_t chunk = (uint32_t)(qt * 2 + cc);  // 16-byte chunk of the 128-byte row
-                    *reinterpret_cast<uint4*>(base + ((chunk ^ rsw) << 4)) =
-                        make_uint4(pw[pl][4 * cc], pw[pl][4 * cc + 1], pw[pl][4 * cc + 2], pw[pl][4 * cc + 3]);
+                    for (int q = 0; q < 32; q++)
+                        if (j0 + q <= rpos) sum += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
                 }
             }
-            fence_proxy_async();
-            mbar_arrive(&bars->p_full[pb]);
-        }
-        // O: acc = sum_k 2^(8k) O_k for this thread's 16 channels, then the output rescale.
-        mbar_wait(&bars->o_full, 0, err, 25);
-        __syncwarp();
-        tc_fence_after();
-        const bool row_ok = row < (int)grp.count;
-        uint32_t o[4][16];
+            // Pass 3's first table indices are on their way while the sums are exchanged.
+            auto load_idx = [&](int c, uint4* dst) {
+                if (c < nch && c * KC + qt * 32 <= wlast) {
+                    const uint4* r = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
 #pragma unroll
-        for (int pl = 0; pl < 4; pl++)
-            tmem_ld16(tmem + ((uint32_t)(g * 32) << 16) + 2 * KC + pl * HDIM + qt * 16, o[pl]);
-        tmem_ld_wait();
-        if (row_ok) {
-            // att = clamp(rescale(acc, om, os), -127, 127), |acc| <= 2^30 * 128 (rescale_clamp127): the
-            // double estimates of all 16 values first, branch-free, so their latencies overlap; the
-            // values too close to a rounding boundary take the exact rule afterwards.
-            const double omsc = (double)om * exp2_neg(os);
-            int64_t accs[16];
-            int32_t ys[16];
-            uint32_t slow = os > 95 ? 0xFFFFu : 0u;
+                    for (int k = 0; k < 4; k++) dst[k] = __ldcg(r + k * GM);
+                }
+            };
+            uint4 nxt[4] = {};
+            load_idx(0, nxt);
+            sX[(8 + qt) * GM + row] = (int64_t)sum;
+            named_bar(1, ETH);
+            sum = 0;
 #pragma unroll
-            for (int q = 0; q < 16; q++) {
-                accs[q] = ((((int64_t)(int32_t)o[3][q] * 256 + (int32_t)o[2][q]) * 256 + (int32_t)o[1][q]) * 256) +
-                          (int32_t)o[0][q];
-                const double z = fma((double)accs[q], omsc, 0.5);
-                const double zc = fmin(fmax(z, -1024.0), 1024.0);
-                const double fl = floor(zc);
-                const double fr = zc - fl;
-                ys[q] = min(max((int32_t)fl, -127), 127);
-                const bool near = fabs(z) < 1024.0 && !(fr > 9.094947017729282e-13 && fr < 1.0 - 9.094947017729282e-13);
-                slow |= (uint32_t)near << q;
+            for (int o = 0; o < 4; o++) sum += (uint64_t)sX[(8 + o) * GM + row];
+            if (sum == 0) sum = 1;
+            // p = floor(e * 2^P / sum) for every e < 2^31 as floor(e * mg / 2^(31 + l)): the
+            // numerators e * 2^P have N = 31 + P <= 61 bits, 2^l >= sum and mg = ceil(2^(N + l) / sum)
+            // <= 2^(N + 1), so the quotient is exact (Granlund and Montgomery, "Division by invariant
+            // integers using multiplication", 1994, Theorem 4.2). With mg = mh 2^32 + ml and
+            // u = e mh + (e ml >> 32), p = u >> (l - 1): two 32x32 multiplies per key.
+            int l = 64 - __clzll((long long)(sum - 1));
+            if (l < 1) l = 1;
+            const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
+            const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
+            const int psh = l - 1;
+            // Pass 3: the table indices back from the scratch (the next chunk's loads in flight
+            // while this one is used), p, its four byte planes into shared memory (128-byte
+            // swizzle, K-major), P V.
+            const uint32_t rsw = (uint32_t)(row & 7);
+            for (int c = 0; c < nch; c++, pit++) {
+                const int j0 = c * KC + qt * 32;
+                uint32_t dk[16];
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    dk[4 * k] = nxt[k].x;
+                    dk[4 * k + 1] = nxt[k].y;
+                    dk[4 * k + 2] = nxt[k].z;
+                    dk[4 * k + 3] = nxt[k].w;
+                }
+                load_idx(c + 1, nxt);
+                auto prob = [&](int q) -> uint32_t {
+                    const uint32_t e = (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
+                    const uint64_t t = (uint64_t)e * ml;
+                    const uint64_t u = (uint64_t)e * mh + (t >> 32);
+                    return (uint32_t)(u >> psh);
+                };
+                uint32_t pv[32];
+                if (j0 > wlast) {
+#pragma unroll
+                    for (int q = 0; q < 32; q++) pv[q] = 0u;
+                } else if (j0 + 31 <= wfirst) {
+#pragma unroll
+                    for (int q = 0; q < 32; q++) pv[q] = prob(q);
+                } else {
+#pragma unroll
+                    for (int q = 0; q < 32; q++) pv[q] = j0 + q <= rpos ? prob(q) : 0u;
+                }
+                // The four byte planes of each 4-key word: a 4x4 byte transpose with byte permutes.
+                uint32_t pw[4][8];  // [plane][4-key word] of this thread's 32 keys
+#pragma unroll
+                for (int w = 0; w < 8; w++) {
+                    const uint32_t a = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x5140);
+                    const uint32_t b2 = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x7362);
+                    const uint32_t c2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x5140);
+                    const uint32_t d2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x7362);
+                    pw[0][w] = __byte_perm(a, c2, 0x5410);
+                    pw[1][w] = __byte_perm(a, c2, 0x7632);
+                    pw[2][w] = __byte_perm(b2, d2, 0x5410);
+                    pw[3][w] = __byte_perm(b2, d2, 0x7632);
+                }
+                // The P V of two chunks before (the same buffer) must be done before its planes are
+                // overwritten.
+                const int pb = pit & 1;
+                mbar_wait(&bars->p_empty[pb], ((pit >> 1) & 1) ^ 1, err, 24);
+                __syncwarp();
+                uint8_t* prow = sP + pb * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+                for (int pl = 0; pl < 4; pl++) {
+                    uint8_t* base = prow + pl * (GM * KC);
+#pragma unroll
+                    for (int cc = 0; cc < 2; cc++) {
+                        const uint32_t chunk = (uint32_t)(qt * 2 + cc);  // 16-byte chunk of the 128-byte row
+                        *reinterpret_cast<uint4*>(base + ((chunk ^ rsw) << 4)) =
+                            make_uint4(pw[pl][4 * cc], pw[pl][4 * cc + 1], pw[pl][4 * cc + 2], pw[pl][4 * cc + 3]);
+                    }
+                }
+                fence_proxy_async();
+                mbar_arrive(&bars->p_full[pb]);
             }
-            if (slow) {
-#pragma unroll
-                for (int q = 0; q < 16; q++)
-                    if ((slow >> q) & 1) ys[q] = (int32_t)clamp128(rescale128(accs[q], om, (uint32_t)os), -127, 127);
-            }
-            uint32_t packed[4];
-#pragma unroll
-            for (int w = 0; w < 4; w++)
-                packed[w] = __byte_perm(__byte_perm(ys[4 * w], ys[4 * w + 1], 0x0040),
-                                        __byte_perm(ys[4 * w + 2], ys[4 * w + 3], 0x0040), 0x5410);
-            *reinterpret_cast<uint4*>(att + (size_t)(grp.first_row + row) * lda + h * HDIM + qt * 16) =
-                make_uint4(packed[0], packed[1], packed[2], packed[3]);
         }
-        tc_fence_before();
     }
     __syncthreads();
-    if (warp == EW + 1) {
+    if (warp == W_MMA) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, 512);
@@ -758,25 +846,6 @@ bool attention_tc_supported(int hd, int n_ctx, int tlen) {
     return hd == HDIM && n_ctx % 16 == 0 && n_ctx <= 8192 && tlen <= TABLE_MAX;
 }
 
-// %nsmid: SM ids run from 0 to this bound minus one (not necessarily every id in between).
-__global__ void k_sm_id_bound(int* out) {
-    uint32_t n;
-    asm("mov.u32 %0, %%nsmid;" : "=r"(n));
-    *out = (int)n;
-}
-
-cudaError_t attn_scratch_slots(int* slots, cudaStream_t st) {
-    int* d = nullptr;
-    cudaError_t e = cudaMalloc(&d, sizeof(int));
-    if (e != cudaSuccess) return e;
-    k_sm_id_bound<<<1, 1, 0, st>>>(d);
-    e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaMemcpyAsync(slots, d, sizeof(int), cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    cudaError_t f = cudaFree(d);
-    return e != cudaSuccess ? e : f;
-}
-
 size_t attn_scratch_bytes(int slots, int n_ctx) {
     return (size_t)slots * (size_t)((n_ctx + KC - 1) / KC) * SCR_CHUNK_BYTES;
 }
@@ -785,20 +854,24 @@ void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, cons
                          int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,
                          const int32_t* table, int tlen, int P, int8_t* att, int lda, uint8_t* scratch, int scr_slots,
                          int* err, cudaStream_t st) {
-    if (n_groups <= 0) return;
-    dim3 grid(n_groups, H);
+    if (n_groups <= 0 || scr_slots <= 0) return;
+    // One persistent CTA per SM (a CTA takes more than half of an SM's shared memory), at most one
+    // per tile and per scratch slot.
+    const int T = n_groups * H;
+    const int grid = T < scr_slots ? T : scr_slots;
     const CUtensorMap& q = *reinterpret_cast<const CUtensorMap*>(tmQ);
     const CUtensorMap& k = *reinterpret_cast<const CUtensorMap*>(tmK);
     const CUtensorMap& v = *reinterpret_cast<const CUtensorMap*>(tmV);
     if (ss >= 32 && ss <= 62)
-        k_attention_tc<true, true><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os,
-                                                                 table, tlen, P, att, lda, scratch, scr_slots, err);
+        k_attention_tc<true, true><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, T, L, layer, H, n_ctx, sm, ss, om,
+                                                                 os, table, tlen, P, att, lda, scratch, scr_slots, err);
     else if (ss >= 21 && ss < 32)
-        k_attention_tc<true, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om, os,
-                                                                  table, tlen, P, att, lda, scratch, scr_slots, err);
+        k_attention_tc<true, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, T, L, layer, H, n_ctx, sm, ss, om,
+                                                                  os, table, tlen, P, att, lda, scratch, scr_slots, err);
     else
-        k_attention_tc<false, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, L, layer, H, n_ctx, sm, ss, om,
-                                                                   os, table, tlen, P, att, lda, scratch, scr_slots, err);
+        k_attention_tc<false, false><<<grid, ATHREADS, ASMEM, st>>>(q, k, v, groups, T, L, layer, H, n_ctx, sm, ss, om,
+                                                                   os, table, tlen, P, att, lda, scratch, scr_slots,
+                                                                   err);
 }
 
 }  // namespace hs

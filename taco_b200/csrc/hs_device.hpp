@@ -7,7 +7,7 @@
 // The device error word (one int per device, 0 = no error): a bounded wait that gives up writes
 // its wait's code (below 40); the coder op writes ERR_CODER_DIVISION when its frequency division
 // is not exact after its correction steps; the prefill attention writes ERR_ATTN_SCRATCH when it
-// runs on an SM whose id has no scratch slot. The first code written stays.
+// is launched with more CTAs than scratch slots. The first code written stays.
 constexpr int ERR_CODER_DIVISION = 40;
 constexpr int ERR_ATTN_SCRATCH = 41;
 

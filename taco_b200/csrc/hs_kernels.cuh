@@ -104,9 +104,8 @@ void launch_attention_dec(const RowInfo* rows, const int* rowlist, int nrows, co
                           int32_t om, int os, const int32_t* table, int tlen, int P, int8_t* att, int lda,
                           cudaStream_t st);
 
-// The prefill attention's scratch: one slot per SM id (attn_scratch_slots reads the bound of the
-// device's SM ids), attn_scratch_bytes(slots, n_ctx) bytes in all.
-cudaError_t attn_scratch_slots(int* slots, cudaStream_t st);
+// The prefill attention's scratch: one slot per persistent CTA (the launch uses at most
+// scr_slots CTAs; one per SM is the most that fit), attn_scratch_bytes(slots, n_ctx) bytes in all.
 size_t attn_scratch_bytes(int slots, int n_ctx);
 void launch_attention_tc(const void* tmQ, const void* tmK, const void* tmV, const AttnGroup* groups, int n_groups,
                          int L, int layer, int H, int n_ctx, int32_t sm, int ss, int32_t om, int os,

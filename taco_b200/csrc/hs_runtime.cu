@@ -242,7 +242,7 @@ struct hs_batch {
     int* h_rowlist = nullptr;
     cudaEvent_t pass_done[2] = {nullptr, nullptr};  // recorded after a pass's read back, per half
     AttnGroup* d_groups = nullptr;   // the prefill groups of the pass
-    uint8_t* attn_scr = nullptr;     // the prefill attention's scratch, attn_scr_slots SM slots
+    uint8_t* attn_scr = nullptr;     // the prefill attention's scratch, one slot per persistent CTA
     int attn_scr_slots = 0;
     int* d_rowlist = nullptr;        // the other rows of the pass
     int n_groups = 0, n_rowlist = 0;
@@ -591,7 +591,7 @@ int check_device_error(hs_batch* b) {
         if (herr == ERR_CODER_DIVISION)
             return fail(HS_CUDA, "the coder op's frequency division did not converge (code " + std::to_string(herr) + ")");
         if (herr == ERR_ATTN_SCRATCH)
-            return fail(HS_CUDA, "the prefill attention ran on an SM without a scratch slot (code " +
+            return fail(HS_CUDA, "the prefill attention ran a CTA without a scratch slot (code " +
                                      std::to_string(herr) + ")");
         return fail(HS_CUDA, "a kernel wait timed out (code " + std::to_string(herr) + ")");
     }
@@ -1582,8 +1582,14 @@ int hs_batch_new(hs_model* m, uint32_t slots, uint32_t max_rows, hs_batch** out)
     }
     if (m->attn_tc) {
         // The prefill attention's scratch (the exp-table index of every key of the rows of one
-        // CTA, one slot per SM id): 256 KB per SM at n_ctx = 1024.
-        CK(attn_scratch_slots(&b->attn_scr_slots, b->stream));
+        // tile, one slot per persistent CTA, one CTA per SM): 256 KB per SM at n_ctx = 1024.
+        b->attn_scr_slots = m->dev->num_sms;
+        // HS_ATTN_CTAS=<n> caps the persistent grid (a test hook: a few CTAs then run many tiles
+        // each, with every length of tile after every other).
+        if (const char* v = getenv("HS_ATTN_CTAS")) {
+            const int n = atoi(v);
+            if (n > 0 && n < b->attn_scr_slots) b->attn_scr_slots = n;
+        }
         const size_t scr = attn_scratch_bytes(b->attn_scr_slots, c.n_ctx);
         if ((rc = dalloc(&b->attn_scr, scr, b->owned))) return rc;
         b->bytes += scr;

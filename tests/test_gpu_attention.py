@@ -40,6 +40,17 @@ def _model(dev, data, attn):
         os.environ.pop("HS_ATTN", None)
 
 
+def _batch(model, slots, max_rows, ctas=None):
+    """A batch whose persistent attention grid is capped at `ctas` CTAs (HS_ATTN_CTAS), so that
+    each CTA runs several tiles of different lengths one after the other."""
+    if ctas is not None:
+        os.environ["HS_ATTN_CTAS"] = str(ctas)
+    try:
+        return B.CudaBatch(model, slots, max_rows)
+    finally:
+        os.environ.pop("HS_ATTN_CTAS", None)
+
+
 def _calls(rng, vocab):
     """Three calls: long prefill runs, a continuation past position 0 with decode rows mixed in,
     and runs that cross n_ctx = 512 (restarts)."""
@@ -57,12 +68,12 @@ def _calls(rng, vocab):
 
 
 @pytest.mark.parametrize("overlap", [0, 20])
-@pytest.mark.parametrize("attn", ["tc", "vec"])
-def test_prefill_attention_equals_the_oracle(dev, mini, attn, overlap):
+@pytest.mark.parametrize("attn,ctas", [("tc", None), ("tc", 1), ("tc", 3), ("vec", None)])
+def test_prefill_attention_equals_the_oracle(dev, mini, attn, ctas, overlap):
     om = O.Model(mini)
     model = _model(dev, mini, attn)
     slots = 3
-    batch = B.CudaBatch(model, slots, 1024)
+    batch = _batch(model, slots, 1024, ctas)
     batch.set_overlap(overlap)
     fast = O.FastBatch(om, slots, overlap)
     rng = np.random.default_rng(123 + overlap)
