@@ -24,7 +24,7 @@
 // pass 1 (t), epilogue (t - 1), pass 2 (t), pass 3 (t). The P V of tile t + 1 starts only after
 // every softmax thread has written its first P planes, so after its epilogue of tile t.
 //
-// Operands come in by TMA (no multicast): Q [128 x 64] (double-buffered) and K chunks [128 x 64]
+// Operands come in by TMA (no multicast): Q [128 x 64] (Q_STAGES buffers) and K chunks [128 x 64]
 // with the 64-byte swizzle, V^T chunks [64 x 128] with the 128-byte swizzle from the transposed
 // values cache. Warps 0..15 do the softmax: TMEM lane group warp % 4 (32 rows) and key quarter
 // warp / 4 (32 of the 128 keys of a chunk). Warp 16 loads Q and K, warp 17 owns TMEM and issues
@@ -54,24 +54,26 @@ constexpr int W_QK = EW;       // the Q and K producer warp
 constexpr int W_MMA = EW + 1;  // the TMEM owner and MMA issuer
 constexpr int W_V = EW + 2;    // the V producer warp
 constexpr int ATHREADS = ETH + 96;
-constexpr int Q_BYTES = GM * HDIM;        // 8 KB, double-buffered
+constexpr int Q_BYTES = GM * HDIM;        // 8 KB
 constexpr int K_BYTES = KC * HDIM;        // 8 KB
+constexpr int Q_STAGES = 2;               // Q of this tile and of the next
+constexpr int K_STAGES = 3;               // K chunks in flight: pass 1 is bound by their latency
 constexpr int V_BYTES = HDIM * KC;        // 8 KB
 constexpr int P_BYTES = 4 * GM * KC;      // 64 KB (four planes), double-buffered
 constexpr int TABLE_MAX = 8192;           // attn_exp entries kept in shared memory
-// The row exchange: max and min dots (regions 0..7) and the sums (regions 8..11) apart, so that a
+// The row exchange: max and min dots (i32 [8][GM]) and the sums (i64 [4][GM]) apart, so that a
 // warp's pass 1 of the next tile never writes where a slower warp still reads this tile's sums.
-constexpr int XREGIONS = 12;
-// The scratch slot of one CTA: per 128-key chunk, key quarter, 16-byte word (8 keys) and row, the
-// u16 table indices of 8 keys, so that a warp's 32 rows store and load 512 contiguous bytes.
-constexpr size_t SCR_CHUNK_BYTES = 4 * 4 * GM * 16;  // 32 KB per chunk of 128 keys
-constexpr size_t ASMEM = 2 * (size_t)Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + 4 * TABLE_MAX +
-                         XREGIONS * GM * 8 + 512 + 1024;
+constexpr int XBYTES = 8 * GM * 4 + 4 * GM * 8;
+// The scratch slot of one CTA: per 128-key chunk, key quarter, 16-byte word (4 keys) and row, the
+// u32 weights e of 4 keys, so that a warp's 32 rows store and load 512 contiguous bytes.
+constexpr size_t SCR_CHUNK_BYTES = 4 * 8 * GM * 16;  // 64 KB per chunk of 128 keys
+constexpr size_t ASMEM = (size_t)Q_STAGES * Q_BYTES + (size_t)K_STAGES * K_BYTES + 2 * V_BYTES + 2 * P_BYTES +
+                         4 * TABLE_MAX + XBYTES + 512 + 1024;
 static_assert(ASMEM <= 232448, "the attention CTA's shared memory exceeds the 227 KB per block");
 
 struct __align__(8) ABars {
-    uint64_t q_full[2], q_empty[2];
-    uint64_t k_full[2], k_empty[2];
+    uint64_t q_full[Q_STAGES], q_empty[Q_STAGES];
+    uint64_t k_full[K_STAGES], k_empty[K_STAGES];
     uint64_t v_full[2], v_empty[2];
     uint64_t s_full[2], s_empty[2];
     uint64_t p_full[2], p_empty[2];
@@ -144,22 +146,27 @@ __global__ void __launch_bounds__(ATHREADS, 1)
     // integer cast), so every access below stays a shared-memory access with 32-bit addresses.
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* sQ = smem;                         // 2 x 8 KB
-    uint8_t* sK = sQ + 2 * Q_BYTES;             // 2 x 8 KB
-    uint8_t* sV = sK + 2 * K_BYTES;             // 2 x 8 KB
+    uint8_t* sK = sQ + Q_STAGES * Q_BYTES;      // K_STAGES x 8 KB
+    uint8_t* sV = sK + K_STAGES * K_BYTES;      // 2 x 8 KB
     uint8_t* sP = sV + 2 * V_BYTES;             // 2 x 4 planes x 16 KB
     int32_t* sT = reinterpret_cast<int32_t*>(sP + 2 * P_BYTES);
-    int64_t* sX = reinterpret_cast<int64_t*>(sT + TABLE_MAX);  // [XREGIONS][GM] row exchange
-    ABars* bars = reinterpret_cast<ABars*>(sX + XREGIONS * GM);
+    int32_t* sXm = sT + TABLE_MAX;                                // [8][GM] max, min dots
+    int64_t* sXs = reinterpret_cast<int64_t*>(sXm + 8 * GM);      // [4][GM] sums
+    ABars* bars = reinterpret_cast<ABars*>(sXs + 4 * GM);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t0 = (int)blockIdx.x, tstep = (int)gridDim.x;
     const int n_mine = t0 < T ? (T - t0 + tstep - 1) / tstep : 0;  // this CTA's tiles
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < Q_STAGES; i++) {
             mbar_init(&bars->q_full[i], 1);
             mbar_init(&bars->q_empty[i], 1);
+        }
+        for (int i = 0; i < K_STAGES; i++) {
             mbar_init(&bars->k_full[i], 1);
             mbar_init(&bars->k_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
             mbar_init(&bars->v_full[i], 1);
             mbar_init(&bars->v_empty[i], 1);
             mbar_init(&bars->s_full[i], 1);
@@ -199,8 +206,8 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                 const AttnGroup grp = groups[t / H];
                 const int h = t % H, nch = tile_chunks(grp);
                 const size_t head = ((size_t)grp.slot * L + layer) * H + h;
-                const int qb = seq & 1;
-                if (!mbar_wait(&bars->q_empty[qb], ((seq >> 1) & 1) ^ 1, err, 10)) break;
+                const int qb = seq % Q_STAGES;
+                if (!mbar_wait(&bars->q_empty[qb], ((seq / Q_STAGES) & 1) ^ 1, err, 10)) break;
                 mbar_arrive_expect_tx(&bars->q_full[qb], Q_BYTES);
                 tma_load_2d(sQ + qb * Q_BYTES, &tmQ, &bars->q_full[qb], h * HDIM, (int)grp.first_row);
                 for (int it = 0; it < 2 * nch; it++) {
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     }
                     mbar_arrive_expect_tx(&bars->k_full[ks], K_BYTES);
                     tma_load_2d(sK + ks * K_BYTES, &tmK, &bars->k_full[ks], 0, (int)(head * n_ctx) + c * KC);
-                    if (++ks == 2) {
+                    if (++ks == K_STAGES) {
                         ks = 0;
                         kph ^= 1;
                     }
@@ -258,8 +265,8 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             uint32_t kph = 0;
             auto issue_s = [&]() -> bool {
                 if (s_seq >= n_mine) return true;  // no S item left
-                const int sb = sit & 1, qb = s_seq & 1;
-                if (s_j == 0 && !mbar_wait(&bars->q_full[qb], (s_seq >> 1) & 1, err, 13)) return false;
+                const int sb = sit & 1, qb = s_seq % Q_STAGES;
+                if (s_j == 0 && !mbar_wait(&bars->q_full[qb], (s_seq / Q_STAGES) & 1, err, 13)) return false;
                 if (!mbar_wait(&bars->s_empty[sb], ((sit >> 1) & 1) ^ 1, err, 14)) return false;
                 if (!mbar_wait(&bars->k_full[ks], kph, err, 15)) return false;
                 tc_fence_after();
@@ -271,7 +278,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     mma_i8(d, sdesc_sw64(qa + 32 * k), sdesc_sw64(kb + 32 * k), id_s, k != 0 ? 1u : 0u);
                 mma_commit(&bars->k_empty[ks]);
                 mma_commit(&bars->s_full[sb]);
-                if (++ks == 2) {
+                if (++ks == K_STAGES) {
                     ks = 0;
                     kph ^= 1;
                 }
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
         const double omsc = (double)om * exp2_neg(os);
         // This thread's words of the CTA's scratch slot (the same size for every CTA).
         const size_t slot_bytes = (size_t)((n_ctx + KC - 1) / KC) * SCR_CHUNK_BYTES;
-        uint4* scr = reinterpret_cast<uint4*>(scratch + (size_t)blockIdx.x * slot_bytes) + qt * 4 * GM + row;
+        uint4* scr = reinterpret_cast<uint4*>(scratch + (size_t)blockIdx.x * slot_bytes) + qt * 8 * GM + row;
         // The table index min(M - score(dot), last); NARROW: the score is the low word of the
         // 64-bit shift (one shift of the high word when ss >= 32, a funnel shift below).
         auto dist = [&](int64_t M, int32_t dot) -> int32_t {
@@ -451,14 +458,14 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                     }
                 }
             }
-            sX[(0 * 4 + qt) * GM + row] = maxd;
-            sX[(1 * 4 + qt) * GM + row] = mind;
+            sXm[(0 * 4 + qt) * GM + row] = maxd;
+            sXm[(1 * 4 + qt) * GM + row] = mind;
             named_bar(1, ETH);
 #pragma unroll
             for (int o = 0; o < 4; o++) {
-                int64_t a = sX[(0 * 4 + o) * GM + row], b = sX[(1 * 4 + o) * GM + row];
-                maxd = (int32_t)(a > maxd ? a : maxd);
-                mind = (int32_t)(b < mind ? b : mind);
+                const int32_t a = sXm[(0 * 4 + o) * GM + row], b = sXm[(1 * 4 + o) * GM + row];
+                maxd = a > maxd ? a : maxd;
+                mind = b < mind ? b : mind;
             }
             int64_t M = INT64_MIN;
             if (maxd >= mind) {
@@ -487,90 +494,90 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                 mbar_arrive(&bars->s_empty[sb]);
                 const int j0 = c * KC + qt * 32;
                 if (j0 > wlast) continue;  // masked for every lane: nothing stored, nothing read back
-                uint32_t dk[16];
+                uint32_t ev[32];
 #pragma unroll
-                for (int q = 0; q < 32; q += 2) {
-                    const uint32_t d0 = (uint32_t)dist(M, (int32_t)v[q]), d1 = (uint32_t)dist(M, (int32_t)v[q + 1]);
-                    dk[q >> 1] = d0 | (d1 << 16);
-                }
+                for (int q = 0; q < 32; q++) ev[q] = (uint32_t)sT[dist(M, (int32_t)v[q])];
                 uint4* w = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
 #pragma unroll
-                for (int k = 0; k < 4; k++)
-                    __stcg(w + k * GM, make_uint4(dk[4 * k], dk[4 * k + 1], dk[4 * k + 2], dk[4 * k + 3]));
+                for (int k = 0; k < 8; k++)
+                    __stcg(w + k * GM, make_uint4(ev[4 * k], ev[4 * k + 1], ev[4 * k + 2], ev[4 * k + 3]));
                 if (j0 + 31 <= wfirst) {
-                    // Four partial sums: independent chains for the look-ups and adds.
+                    // Four partial sums: independent chains for the adds.
                     uint64_t ps[4] = {0, 0, 0, 0};
 #pragma unroll
-                    for (int q = 0; q < 32; q++) ps[q & 3] += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
+                    for (int q = 0; q < 32; q++) ps[q & 3] += ev[q];
                     sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
                 } else {
 #pragma unroll
                     for (int q = 0; q < 32; q++)
-                        if (j0 + q <= rpos) sum += (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
+                        if (j0 + q <= rpos) sum += ev[q];
                 }
             }
-            // Pass 3's first table indices are on their way while the sums are exchanged.
-            auto load_idx = [&](int c, uint4* dst) {
+            // Pass 3's first weights are on their way while the sums are exchanged. Pass 3 goes by
+            // half slices of 16 keys (hc = 2 c + half): the 16 weights of one half come back from
+            // the scratch while the half before is used.
+            auto load_half = [&](int hc, uint4* dst) {
+                const int c = hc >> 1;
                 if (c < nch && c * KC + qt * 32 <= wlast) {
-                    const uint4* r = scr + (size_t)c * (SCR_CHUNK_BYTES / 16);
+                    const uint4* r = scr + (size_t)c * (SCR_CHUNK_BYTES / 16) + (size_t)(hc & 1) * 4 * GM;
 #pragma unroll
                     for (int k = 0; k < 4; k++) dst[k] = __ldcg(r + k * GM);
                 }
             };
             uint4 nxt[4] = {};
-            load_idx(0, nxt);
-            sX[(8 + qt) * GM + row] = (int64_t)sum;
+            load_half(0, nxt);
+            sXs[qt * GM + row] = (int64_t)sum;
             named_bar(1, ETH);
             sum = 0;
 #pragma unroll
-            for (int o = 0; o < 4; o++) sum += (uint64_t)sX[(8 + o) * GM + row];
+            for (int o = 0; o < 4; o++) sum += (uint64_t)sXs[o * GM + row];
             if (sum == 0) sum = 1;
             // p = floor(e * 2^P / sum) for every e < 2^31 as floor(e * mg / 2^(31 + l)): the
             // numerators e * 2^P have N = 31 + P <= 61 bits, 2^l >= sum and mg = ceil(2^(N + l) / sum)
             // <= 2^(N + 1), so the quotient is exact (Granlund and Montgomery, "Division by invariant
             // integers using multiplication", 1994, Theorem 4.2). With mg = mh 2^32 + ml and
-            // u = e mh + (e ml >> 32), p = u >> (l - 1): two 32x32 multiplies per key.
+            // u = e mh + (e ml >> 32), p = u >> (l - 1): one wide and one high-word multiply per key
+            // (the high word alone: 10 % off pass 3 against two wide products).
             int l = 64 - __clzll((long long)(sum - 1));
             if (l < 1) l = 1;
             const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
             const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
             const int psh = l - 1;
-            // Pass 3: the table indices back from the scratch (the next chunk's loads in flight
-            // while this one is used), p, its four byte planes into shared memory (128-byte
-            // swizzle, K-major), P V.
+            auto prob = [&](uint32_t e) -> uint32_t {
+                const uint64_t u = (uint64_t)e * mh + __umulhi(e, ml);  // the high word of e ml: 32 bits
+                return (uint32_t)(u >> psh);
+            };
+            // Pass 3: the weights back from the scratch, p, its four byte planes into shared memory
+            // (128-byte swizzle, K-major), P V.
             const uint32_t rsw = (uint32_t)(row & 7);
-            for (int c = 0; c < nch; c++, pit++) {
-                const int j0 = c * KC + qt * 32;
-                uint32_t dk[16];
+            uint8_t* prow0 = sP + (row >> 3) * 1024 + (row & 7) * 128;
+            for (int hc = 0; hc < 2 * nch; hc++) {
+                const int c = hc >> 1, half = hc & 1;
+                const int j0 = c * KC + qt * 32 + half * 16;  // the first key of this half slice
+                uint32_t ev[16];
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    dk[4 * k] = nxt[k].x;
-                    dk[4 * k + 1] = nxt[k].y;
-                    dk[4 * k + 2] = nxt[k].z;
-                    dk[4 * k + 3] = nxt[k].w;
+                    ev[4 * k] = nxt[k].x;
+                    ev[4 * k + 1] = nxt[k].y;
+                    ev[4 * k + 2] = nxt[k].z;
+                    ev[4 * k + 3] = nxt[k].w;
                 }
-                load_idx(c + 1, nxt);
-                auto prob = [&](int q) -> uint32_t {
-                    const uint32_t e = (uint32_t)sT[(dk[q >> 1] >> (16 * (q & 1))) & 0xFFFFu];
-                    const uint64_t t = (uint64_t)e * ml;
-                    const uint64_t u = (uint64_t)e * mh + (t >> 32);
-                    return (uint32_t)(u >> psh);
-                };
-                uint32_t pv[32];
+                load_half(hc + 1, nxt);
+                uint32_t pv[16];
                 if (j0 > wlast) {
 #pragma unroll
-                    for (int q = 0; q < 32; q++) pv[q] = 0u;
-                } else if (j0 + 31 <= wfirst) {
+                    for (int q = 0; q < 16; q++) pv[q] = 0u;
+                } else if (j0 + 15 <= wfirst) {
 #pragma unroll
-                    for (int q = 0; q < 32; q++) pv[q] = prob(q);
+                    for (int q = 0; q < 16; q++) pv[q] = prob(ev[q]);
                 } else {
 #pragma unroll
-                    for (int q = 0; q < 32; q++) pv[q] = j0 + q <= rpos ? prob(q) : 0u;
+                    for (int q = 0; q < 16; q++) pv[q] = j0 + q <= rpos ? prob(ev[q]) : 0u;
                 }
                 // The four byte planes of each 4-key word: a 4x4 byte transpose with byte permutes.
-                uint32_t pw[4][8];  // [plane][4-key word] of this thread's 32 keys
+                uint32_t pw[4][4];  // [plane][4-key word] of this half slice
 #pragma unroll
-                for (int w = 0; w < 8; w++) {
+                for (int w = 0; w < 4; w++) {
                     const uint32_t a = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x5140);
                     const uint32_t b2 = __byte_perm(pv[4 * w], pv[4 * w + 1], 0x7362);
                     const uint32_t c2 = __byte_perm(pv[4 * w + 2], pv[4 * w + 3], 0x5140);
@@ -583,21 +590,20 @@ __global__ void __launch_bounds__(ATHREADS, 1)
                 // The P V of two chunks before (the same buffer) must be done before its planes are
                 // overwritten.
                 const int pb = pit & 1;
-                mbar_wait(&bars->p_empty[pb], ((pit >> 1) & 1) ^ 1, err, 24);
-                __syncwarp();
-                uint8_t* prow = sP + pb * P_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll
-                for (int pl = 0; pl < 4; pl++) {
-                    uint8_t* base = prow + pl * (GM * KC);
-#pragma unroll
-                    for (int cc = 0; cc < 2; cc++) {
-                        const uint32_t chunk = (uint32_t)(qt * 2 + cc);  // 16-byte chunk of the 128-byte row
-                        *reinterpret_cast<uint4*>(base + ((chunk ^ rsw) << 4)) =
-                            make_uint4(pw[pl][4 * cc], pw[pl][4 * cc + 1], pw[pl][4 * cc + 2], pw[pl][4 * cc + 3]);
-                    }
+                if (half == 0) {
+                    mbar_wait(&bars->p_empty[pb], ((pit >> 1) & 1) ^ 1, err, 24);
+                    __syncwarp();
                 }
-                fence_proxy_async();
-                mbar_arrive(&bars->p_full[pb]);
+                const uint32_t chunk = (uint32_t)(qt * 2 + half);  // 16-byte chunk of the 128-byte row
+                uint8_t* prow = prow0 + pb * P_BYTES + ((chunk ^ rsw) << 4);
+#pragma unroll
+                for (int pl = 0; pl < 4; pl++)
+                    *reinterpret_cast<uint4*>(prow + pl * (GM * KC)) = make_uint4(pw[pl][0], pw[pl][1], pw[pl][2], pw[pl][3]);
+                if (half == 1) {
+                    fence_proxy_async();
+                    mbar_arrive(&bars->p_full[pb]);
+                    pit++;
+                }
             }
         }
     }
@@ -736,8 +742,7 @@ __global__ void __launch_bounds__(32 * DEC_WARPS, 5) k_attention_dec(const RowIn
             uint32_t p = 0;
             if (j < n) {
                 const uint32_t e = sb[j];
-                const uint64_t t = (uint64_t)e * ml;
-                const uint64_t u = (uint64_t)e * mh + (t >> 32);
+                const uint64_t u = (uint64_t)e * mh + __umulhi(e, ml);
                 p = (uint32_t)(u >> psh);
             }
             pv[k] = p;
