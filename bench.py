@@ -163,8 +163,8 @@ def measured_int8_peak_tops(device: int) -> dict:
 
 
 def read_traffic() -> dict:
-    """DRAM bytes (read + write) per launch of each kernel class, from the committed ncu summary of
-    one 16384-row fold pass (the same pass shape as every pass of this benchmark)."""
+    """DRAM bytes (read + write) per launch of each kernel class at this benchmark's 65,536-row
+    passes, from the committed ncu summary (a 16,384-row pass captured, scaled by the rows)."""
     p = ROOT / "profiles" / "fold_pass_traffic.md"
     if not p.exists():
         return {}
