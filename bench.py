@@ -72,7 +72,7 @@ def parse_args():
     ap.add_argument("--cpu-threads", type=int, default=0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--no-peak", action="store_true", help="skip the int8 peak measurement (profiling runs)")
-    ap.add_argument("--only", default="", choices=["", "fold_dual", "fold_glue", "large_input"],
+    ap.add_argument("--only", default="", choices=["", "fold_dual", "fold_glue", "large_input", "unfold"],
                     help="run one extra alone (profiling runs)")
     ap.add_argument("--large-mb", type=int, default=256, help="configs[4] input size in MiB (0 = skip)")
     return ap.parse_args()
@@ -327,6 +327,8 @@ def main():
         model = B.CudaModel(dev, model_bytes)
         if args.only == "fold_dual":
             print(json.dumps({"fold_dual": fold_dual(B, model, windows, lens, eot, sample=args.windows)}))
+        elif args.only == "unfold":
+            print(json.dumps({"unfold": unfold_sweep(B, model, lens, eot)}))
         else:
             print(json.dumps({"fold_glue": fold_glue(B, model, model_bytes, args.max_rows)}))
         model.close()
@@ -578,7 +580,9 @@ def unfold_sweep(B, model, lens, eot, streams: int = 1024, steps: int = 8,
         out.append({"context": f"{p + steps + 1}..{p + 2 * steps}", "tokens_per_s": streams * steps / dev_s,
                     "e2e_tokens_per_s": streams * steps / wall, "kv_GB_per_s": kv / dev_s / 1e9,
                     "ms_per_step": round(1000 * dev_s / steps, 3),
-                    "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3)})
+                    "attention_share": round(prof["attention"]["ms"] / prof["pass"]["ms"], 3),
+                    "ops_ms_per_step": {k: round(v["ms"] / steps, 4) for k, v in prof.items()
+                                        if k != "pass" and v["ms"] > 0}})
     batch.close()
     return {"streams": streams, "steps_per_point": steps, "points": out}
 

@@ -627,6 +627,7 @@ __global__ void __launch_bounds__(ATHREADS, 1)
 // lane 4c gathers the four planes of channel c. The dots pass keeps 2 keys per lane in flight,
 // so that 5 blocks fit on an SM. No block-wide synchronisation.
 constexpr int DEC_WARPS = 4;
+constexpr int DEC_SHORT = 64;  // the longest context of the lane-per-channel P V
 
 __device__ __forceinline__ int32_t dp4a_us(uint32_t a, uint32_t b, int32_t c) {
     int32_t d;
@@ -653,108 +654,151 @@ __global__ void __launch_bounds__(32 * DEC_WARPS, 5) k_attention_dec(const RowIn
     const size_t head = ((size_t)ri.slot * L + layer) * H + h;
     const int4* K = reinterpret_cast<const int4*>(kc + head * n_ctx * HDIM);
     const int8_t* Vt = vc + head * HDIM * n_ctx;
-    int32_t qw[16];
-    {
-        const int4* qp = reinterpret_cast<const int4*>(qkv + (size_t)r * ldq + h * HDIM);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int4 v = qp[i];
-            qw[4 * i] = v.x;
-            qw[4 * i + 1] = v.y;
-            qw[4 * i + 2] = v.z;
-            qw[4 * i + 3] = v.w;
-        }
-    }
-    // Pass 1: the dots (2 keys per lane in flight).
-    int32_t maxd = INT32_MIN, mind = INT32_MAX;
-    for (int j0 = 0; j0 < n; j0 += 64) {
-        int4 kv[2][4];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int j = j0 + 32 * u + lane;
-            if (j < n) {
-#pragma unroll
-                for (int i = 0; i < 4; i++) kv[u][i] = K[(size_t)j * 4 + i];
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int j = j0 + 32 * u + lane;
-            if (j < n) {
-                int32_t dot = 0;
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    dot = __dp4a(qw[4 * i], kv[u][i].x, dot);
-                    dot = __dp4a(qw[4 * i + 1], kv[u][i].y, dot);
-                    dot = __dp4a(qw[4 * i + 2], kv[u][i].z, dot);
-                    dot = __dp4a(qw[4 * i + 3], kv[u][i].w, dot);
-                }
-                sb[j] = (uint32_t)dot;
-                maxd = max(maxd, dot);
-                mind = min(mind, dot);
-            }
-        }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        maxd = max(maxd, __shfl_xor_sync(0xffffffffu, maxd, o));
-        mind = min(mind, __shfl_xor_sync(0xffffffffu, mind, o));
-    }
-    const bool fast = ss >= 0 && ss <= 62;
-    const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
-    const int32_t last = (tlen < TABLE_MAX ? tlen : TABLE_MAX) - 1;
-    const int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
-    const int64_t M = s1 > s2 ? s1 : s2;
-    auto dist = [&](int32_t dot) -> int32_t {
-        if constexpr (NARROW) {
-            const int64_t t = (int64_t)dot * (int64_t)sm + hround;
-            int32_t score;
-            if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
-            else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
-            const int32_t dd = (int32_t)M - score;
-            return (uint32_t)dd < (uint32_t)last ? dd : last;
-        } else {
-            return dist_of<false>(M, dot, sm, ss, fast, hround, last);
-        }
-    };
-    __syncwarp();
-    // Pass 2: e in place and the sum.
-    uint64_t sum = 0;
-    for (int j = lane; j < n; j += 32) {
-        const uint32_t e = (uint32_t)__ldg(table + dist((int32_t)sb[j]));
-        sb[j] = e;
-        sum += e;
-    }
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (sum == 0) sum = 1;
-    int l = 64 - __clzll((long long)(sum - 1));
-    if (l < 1) l = 1;
-    const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
-    const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
-    const int psh = l - 1;
-    __syncwarp();
-    // Pass 3: p as four byte planes of each quad of keys, in place (keys past n give 0).
     const int nq = (n + 15) >> 4 << 2;  // whole 16-key groups (n_ctx % 16 == 0), zeros past n
-    for (int qd = lane; qd < nq; qd += 32) {
-        uint32_t pv[4];
+    // The dots, the softmax and p as four byte planes in shared memory (passes 1 to 3).
+    auto planes = [&]() {
+        int32_t qw[16];
+        {
+            const int4* qp = reinterpret_cast<const int4*>(qkv + (size_t)r * ldq + h * HDIM);
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int j = 4 * qd + k;
-            uint32_t p = 0;
-            if (j < n) {
-                const uint32_t e = sb[j];
-                const uint64_t u = (uint64_t)e * mh + __umulhi(e, ml);
-                p = (uint32_t)(u >> psh);
+            for (int i = 0; i < 4; i++) {
+                const int4 v = qp[i];
+                qw[4 * i] = v.x;
+                qw[4 * i + 1] = v.y;
+                qw[4 * i + 2] = v.z;
+                qw[4 * i + 3] = v.w;
             }
-            pv[k] = p;
         }
-        const uint32_t a = __byte_perm(pv[0], pv[1], 0x5140), b2 = __byte_perm(pv[0], pv[1], 0x7362);
-        const uint32_t c2 = __byte_perm(pv[2], pv[3], 0x5140), d2 = __byte_perm(pv[2], pv[3], 0x7362);
-        *reinterpret_cast<uint4*>(sb + 4 * qd) = make_uint4(__byte_perm(a, c2, 0x5410), __byte_perm(a, c2, 0x7632),
-                                                            __byte_perm(b2, d2, 0x5410), __byte_perm(b2, d2, 0x7632));
-    }
-    __syncwarp();
-    // P V, 8 channels at a time.
+        // Pass 1: the dots (2 keys per lane in flight).
+        int32_t maxd = INT32_MIN, mind = INT32_MAX;
+        for (int j0 = 0; j0 < n; j0 += 64) {
+            int4 kv[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = j0 + 32 * u + lane;
+                if (j < n) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) kv[u][i] = K[(size_t)j * 4 + i];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = j0 + 32 * u + lane;
+                if (j < n) {
+                    int32_t dot = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        dot = __dp4a(qw[4 * i], kv[u][i].x, dot);
+                        dot = __dp4a(qw[4 * i + 1], kv[u][i].y, dot);
+                        dot = __dp4a(qw[4 * i + 2], kv[u][i].z, dot);
+                        dot = __dp4a(qw[4 * i + 3], kv[u][i].w, dot);
+                    }
+                    sb[j] = (uint32_t)dot;
+                    maxd = max(maxd, dot);
+                    mind = min(mind, dot);
+                }
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            maxd = max(maxd, __shfl_xor_sync(0xffffffffu, maxd, o));
+            mind = min(mind, __shfl_xor_sync(0xffffffffu, mind, o));
+        }
+        const bool fast = ss >= 0 && ss <= 62;
+        const int64_t hround = (fast && ss > 0) ? (1LL << (ss - 1)) : 0;
+        const int32_t last = (tlen < TABLE_MAX ? tlen : TABLE_MAX) - 1;
+        const int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
+        const int64_t M = s1 > s2 ? s1 : s2;
+        auto dist = [&](int32_t dot) -> int32_t {
+            if constexpr (NARROW) {
+                const int64_t t = (int64_t)dot * (int64_t)sm + hround;
+                int32_t score;
+                if constexpr (SSHI) score = (int32_t)(t >> 32) >> (ss - 32);
+                else score = (int32_t)__funnelshift_r((uint32_t)t, (uint32_t)((uint64_t)t >> 32), ss);
+                const int32_t dd = (int32_t)M - score;
+                return (uint32_t)dd < (uint32_t)last ? dd : last;
+            } else {
+                return dist_of<false>(M, dot, sm, ss, fast, hround, last);
+            }
+        };
+        __syncwarp();
+        // Pass 2: e in place and the sum.
+        uint64_t sum = 0;
+        for (int j = lane; j < n; j += 32) {
+            const uint32_t e = (uint32_t)__ldg(table + dist((int32_t)sb[j]));
+            sb[j] = e;
+            sum += e;
+        }
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (sum == 0) sum = 1;
+        int l = 64 - __clzll((long long)(sum - 1));
+        if (l < 1) l = 1;
+        const uint64_t mg = ceil_pow2_div(31 + P + l, sum);
+        const uint32_t mh = (uint32_t)(mg >> 32), ml = (uint32_t)mg;
+        const int psh = l - 1;
+        __syncwarp();
+        // Pass 3: p as four byte planes of each quad of keys, in place (keys past n give 0).
+        for (int qd = lane; qd < nq; qd += 32) {
+            uint32_t pv[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int j = 4 * qd + k;
+                uint32_t p = 0;
+                if (j < n) {
+                    const uint32_t e = sb[j];
+                    const uint64_t u = (uint64_t)e * mh + __umulhi(e, ml);
+                    p = (uint32_t)(u >> psh);
+                }
+                pv[k] = p;
+            }
+            const uint32_t a = __byte_perm(pv[0], pv[1], 0x5140), b2 = __byte_perm(pv[0], pv[1], 0x7362);
+            const uint32_t c2 = __byte_perm(pv[2], pv[3], 0x5140), d2 = __byte_perm(pv[2], pv[3], 0x7362);
+            *reinterpret_cast<uint4*>(sb + 4 * qd) = make_uint4(__byte_perm(a, c2, 0x5410), __byte_perm(a, c2, 0x7632),
+                                                                __byte_perm(b2, d2, 0x5410), __byte_perm(b2, d2, 0x7632));
+        }
+        __syncwarp();
+    };
     const double omsc = (double)om * exp2_neg(os);
+    // A short context (n <= DEC_SHORT): lane l takes channels 2l and 2l + 1 in P V, and their V^T
+    // rows (at most 4 x 16 bytes each) are loaded first, so that their latency overlaps the K
+    // loads and the softmax instead of following it. Bytes past n multiply p = 0.
+    if (n <= DEC_SHORT) {
+        uint4 vsh[2][4];
+        const int nv = (n + 15) >> 4;
+#pragma unroll
+        for (int ch = 0; ch < 2; ch++) {
+            const uint4* vr = reinterpret_cast<const uint4*>(Vt + (size_t)(2 * lane + ch) * n_ctx);
+#pragma unroll
+            for (int i = 0; i < 4; i++) vsh[ch][i] = i < nv ? __ldg(vr + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        planes();
+        // P V of channels 2 lane and 2 lane + 1: the p words of each quad of keys are the same for
+        // every lane (broadcast reads), so no reduction across lanes follows.
+        int32_t a[2][4] = {};
+#pragma unroll
+        for (int qd = 0; qd < DEC_SHORT / 4; qd++) {
+            if (qd < nq) {
+                const uint4 pw = *reinterpret_cast<const uint4*>(sb + 4 * qd);
+#pragma unroll
+                for (int ch = 0; ch < 2; ch++) {
+                    const uint4 vq = vsh[ch][qd >> 2];
+                    const uint32_t v = (qd & 3) == 0 ? vq.x : (qd & 3) == 1 ? vq.y : (qd & 3) == 2 ? vq.z : vq.w;
+                    a[ch][0] = dp4a_us(pw.x, v, a[ch][0]);
+                    a[ch][1] = dp4a_us(pw.y, v, a[ch][1]);
+                    a[ch][2] = dp4a_us(pw.z, v, a[ch][2]);
+                    a[ch][3] = dp4a_us(pw.w, v, a[ch][3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int ch = 0; ch < 2; ch++) {
+            // Each plane sum is at most n * 255 * 128 < 2^31 in magnitude.
+            const int64_t acc = ((((int64_t)a[ch][3] * 256 + a[ch][2]) * 256 + a[ch][1]) * 256) + a[ch][0];
+            att[(size_t)r * lda + h * HDIM + 2 * lane + ch] = (int8_t)rescale_clamp127(acc, om, os, omsc);
+        }
+        return;
+    }
+    planes();
+    // P V, 8 channels at a time.
 #pragma unroll 1
     for (int c0 = 0; c0 < HDIM; c0 += 8) {
         int32_t acc[32];  // [channel][plane]
