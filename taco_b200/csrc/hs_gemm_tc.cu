@@ -142,7 +142,9 @@ __device__ __forceinline__ void qkv_store(const EpiArgs& e, int row, const RowIn
 // are 128 x 128; each stage holds both A planes and a 128-row B tile (the same 48 KB), the MMA warp
 // accumulates hi and lo into two TMEM accumulators of 128 columns, and the epilogue recombines
 // v = 256 acc_hi + acc_lo + 128 sum_k W[n][k] exactly in i64 (hardshell.cu:798-830 wide_dot).
-template <int MODE, bool S32, bool WIDE>
+// NN: tiles of 64 columns (passes of few rows, so that the tiles fill the SMs); else 256 (128 for
+// WIDE).
+template <int MODE, bool S32, bool WIDE, bool NN = false>
 __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmC,
@@ -153,7 +155,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
     constexpr int EPI_THREADS = Cfg<MODE>::EPI_THREADS;
     constexpr int THREADS = Cfg<MODE>::THREADS;
     constexpr int NPART = EPI_WARPS / 4;  // epilogue warps per TMEM lane group
-    constexpr int TN = WIDE ? 128 : BN;  // columns of one tile
+    constexpr int TN = WIDE ? 128 : (NN ? 64 : BN);  // columns of one tile
+    static_assert(!(WIDE && NN), "the version 2 tiles are 128 columns");
     static_assert(!WIDE || EPI_WARPS == 8, "the version 2 epilogues take 8 warps");
     static_assert(MODE != EPI_LOGITS || EPI_WARPS == 8, "the logits epilogue takes 8 warps");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -216,14 +219,14 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                         break;
                     }
                     uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
-                    mbar_arrive_expect_tx(&bars->full[stage], STAGE_BYTES);
+                    mbar_arrive_expect_tx(&bars->full[stage], WIDE ? STAGE_BYTES : A_BYTES + TN * BK);
                     tma_load_2d(sa, &tmA, &bars->full[stage], kb * BK, e.a_row0 + mt * BM);
                     if (WIDE) {
                         // [A hi | A lo | B (128 rows)]: 16 + 16 + 16 KB.
                         tma_load_2d(sa + A_BYTES, &tmA2, &bars->full[stage], kb * BK, e.a_row0 + mt * BM);
                         tma_load_2d(sa + 2 * A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * TN);
                     } else {
-                        tma_load_2d(sa + A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * BN);
+                        tma_load_2d(sa + A_BYTES, &tmB, &bars->full[stage], kb * BK, nt * TN);
                     }
                     if (++stage == STAGES) {
                         stage = 0;
@@ -826,7 +829,8 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
 
 template <int MODE>
 void launch_mode(const void* tmA, const void* tmA2, const void* tmB, const void* tmC, const void* tmK,
-                 const void* tmV, int MT, int NT, int KB, const EpiArgs& e, int grid, int* err, cudaStream_t st) {
+                 const void* tmV, int MT, int NT, int KB, const EpiArgs& e, int grid, int* err, cudaStream_t st,
+                 bool narrow) {
     const CUtensorMap& a = *reinterpret_cast<const CUtensorMap*>(tmA);
     const CUtensorMap& b = *reinterpret_cast<const CUtensorMap*>(tmB);
     const CUtensorMap& c = *reinterpret_cast<const CUtensorMap*>(tmC ? tmC : tmB);
@@ -836,6 +840,17 @@ void launch_mode(const void* tmA, const void* tmA2, const void* tmB, const void*
         if (tmA2) {
             const CUtensorMap& a2 = *reinterpret_cast<const CUtensorMap*>(tmA2);
             k_gemm_tc<MODE, false, true><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a2, b, c, k, v, MT, NT, KB, e, err);
+            return;
+        }
+    }
+    if constexpr (MODE == EPI_ACT || MODE == EPI_GELU || MODE == EPI_DELTA || MODE == EPI_QKV) {
+        if (narrow) {
+            if (e.small && e.s >= 0 && e.s <= 62)
+                k_gemm_tc<MODE, true, false, true><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, k, v, MT,
+                                                                                                 NT, KB, e, err);
+            else
+                k_gemm_tc<MODE, false, false, true><<<grid, Cfg<MODE>::THREADS, Cfg<MODE>::SMEM, st>>>(a, a, b, c, k, v, MT,
+                                                                                                  NT, KB, e, err);
             return;
         }
     }
@@ -856,6 +871,14 @@ cudaError_t configure_mode() {
     if constexpr (MODE == EPI_DELTA || MODE == EPI_LOGITS)
         r = cudaFuncSetAttribute(k_gemm_tc<MODE, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)Cfg<MODE>::SMEM);
+    if (r != cudaSuccess) return r;
+    if constexpr (MODE == EPI_ACT || MODE == EPI_GELU || MODE == EPI_DELTA || MODE == EPI_QKV) {
+        r = cudaFuncSetAttribute(k_gemm_tc<MODE, true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)Cfg<MODE>::SMEM);
+        if (r != cudaSuccess) return r;
+        r = cudaFuncSetAttribute(k_gemm_tc<MODE, false, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)Cfg<MODE>::SMEM);
+    }
     return r;
 }
 
@@ -874,19 +897,28 @@ cudaError_t configure_tc_kernels() {
 
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
                     const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2, const void* tmK,
-                    const void* tmV) {
+                    const void* tmV, const void* tmB64) {
     if (R <= 0) return;
     int MT = (R + BM - 1) / BM, NT = Np / (tmA2 ? 128 : BN), KB = Kp / BK;
+    // 256-column tiles for at most half the SMs (a decode step): 64-column tiles, four times as many
+    // CTAs. (With 96 tiles on 148 SMs, the fc GEMM of a 1,024-row step, the narrow tiles were 12 %
+    // slower; with 24, proj and mlp, 17-19 % faster.)
+    const bool narrow = tmB64 != nullptr && !tmA2 && Np % 64 == 0 && 2 * MT * NT <= num_sms &&
+                        (mode == EPI_ACT || mode == EPI_GELU || mode == EPI_DELTA || mode == EPI_QKV);
+    if (narrow) {
+        NT = Np / 64;
+        tmB = tmB64;
+    }
     int tiles = MT * NT;
     int grid = tiles < num_sms ? tiles : num_sms;
     switch (mode) {
-        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
-        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
-        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
-        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
-        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
-        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
-        case EPI_GELU16: launch_mode<EPI_GELU16>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st); break;
+        case EPI_ACT: launch_mode<EPI_ACT>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, narrow); break;
+        case EPI_GELU: launch_mode<EPI_GELU>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, narrow); break;
+        case EPI_LOGITS: launch_mode<EPI_LOGITS>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, false); break;
+        case EPI_RAW: launch_mode<EPI_RAW>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, false); break;
+        case EPI_DELTA: launch_mode<EPI_DELTA>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, narrow); break;
+        case EPI_QKV: launch_mode<EPI_QKV>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, narrow); break;
+        case EPI_GELU16: launch_mode<EPI_GELU16>(tmA, tmA2, tmB, tmC, tmK, tmV, MT, NT, KB, e, grid, err, st, false); break;
         default: break;
     }
 }

@@ -243,26 +243,27 @@ __device__ __noinline__ int64_t ln_exact(int64_t cg, i128 u, int s, int32_t b, i
     return (int64_t)clamp128(y, -32767, 32767);
 }
 
-// The same fused step for rows of exactly 128 * NV values (GPT-2: NV = 6): each lane holds NV
-// groups of four consecutive values, so every load and store is a 16-byte vector (the output a
-// 4-byte word), and the row width is a compile-time constant, so the divisions by it become
-// multiplications.
-template <int NV>
-__global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t* delta, int R, LnDev ln, int ln_k,
-                                                       int ln_j, uint64_t eps, int8_t* out, int ldo, int8_t* out_lo) {
+// The same fused step for rows of exactly 128 * NV values (GPT-2: NV = 6): each lane holds groups
+// of four consecutive values, so every load and store is a 16-byte vector (the output a 4-byte
+// word), and the row width is a compile-time constant, so the divisions by it become
+// multiplications. A row is taken by WPR warps (warp w of the row: the groups w * NV / WPR ..),
+// whose sums meet in shared memory (s_red: WPR * 3 words) when WPR > 1.
+template <int NV, int WPR>
+__device__ __forceinline__ void resid_ln_row(int32_t* x, const int32_t* delta, int r, int w, int lane, const LnDev& ln,
+                                             int ln_k, int ln_j, uint64_t eps, int8_t* out, int ldo,
+                                             int8_t* out_lo, uint64_t* s_red) {
     constexpr int D = 128 * NV;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r = blockIdx.x * 8 + warp;
-    if (r >= R) return;
-    int4* xr = reinterpret_cast<int4*>(x + (size_t)r * D) + lane;
-    int4 v[NV];
+    constexpr int NW = NV / WPR;  // 16-byte groups per lane
+    static_assert(NV % WPR == 0, "the warps of a row take equal parts");
+    int4* xr = reinterpret_cast<int4*>(x + (size_t)r * D) + 32 * NW * w + lane;
+    int4 v[NW];
 #pragma unroll
-    for (int i = 0; i < NV; i++) v[i] = xr[32 * i];
+    for (int i = 0; i < NW; i++) v[i] = xr[32 * i];
     if (delta) {
-        const int4* dr = reinterpret_cast<const int4*>(delta + (size_t)r * D) + lane;
-        int4 dv[NV];
+        const int4* dr = reinterpret_cast<const int4*>(delta + (size_t)r * D) + 32 * NW * w + lane;
+        int4 dv[NW];
 #pragma unroll
-        for (int i = 0; i < NV; i++) dv[i] = __ldcs(dr + 32 * i);
+        for (int i = 0; i < NW; i++) dv[i] = __ldcs(dr + 32 * i);
         // clamp(x + delta, -R, R): |x| <= R < 2^31, so the saturating 32-bit sum clamped to
         // [-R, R] is exact.
         auto radd = [](int32_t a, int32_t b) {
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t
             return min(max(t, -RESIDUAL_LIMIT), RESIDUAL_LIMIT);
         };
 #pragma unroll
-        for (int i = 0; i < NV; i++) {
+        for (int i = 0; i < NW; i++) {
             v[i].x = radd(v[i].x, dv[i].x);
             v[i].y = radd(v[i].y, dv[i].y);
             v[i].z = radd(v[i].z, dv[i].z);
@@ -282,8 +283,15 @@ __global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t
     // Pairs of values (|x| <= R < 2^30) add in 32 bits without overflow.
     int64_t sum = 0;
 #pragma unroll
-    for (int i = 0; i < NV; i++) sum += (int64_t)(v[i].x + v[i].y) + (int64_t)(v[i].z + v[i].w);
+    for (int i = 0; i < NW; i++) sum += (int64_t)(v[i].x + v[i].y) + (int64_t)(v[i].z + v[i].w);
     sum = warp_sums64(sum);
+    if constexpr (WPR > 1) {
+        if (lane == 0) s_red[w] = (uint64_t)sum;
+        __syncthreads();
+        sum = 0;
+#pragma unroll
+        for (int k = 0; k < WPR; k++) sum += (int64_t)s_red[k];
+    }
     const int64_t mean = floor_div64(sum, D);
     // |x - mean| < 2^31, so (x - mean)^2 < 2^62 is one 32x32 -> 64 multiply, and three of them add in
     // 64 bits without overflow; the 128-bit total carries between the groups of three.
@@ -297,19 +305,19 @@ __global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t
         lo += t;
         hi += lo < t ? 1 : 0;
     };
-    int32_t xs_all[4 * NV];
+    int32_t xs_all[4 * NW];
 #pragma unroll
-    for (int i = 0; i < NV; i++) {
+    for (int i = 0; i < NW; i++) {
         xs_all[4 * i] = v[i].x;
         xs_all[4 * i + 1] = v[i].y;
         xs_all[4 * i + 2] = v[i].z;
         xs_all[4 * i + 3] = v[i].w;
     }
 #pragma unroll
-    for (int k = 0; k < 4 * NV; k += 3) {
+    for (int k = 0; k < 4 * NW; k += 3) {
         uint64_t t = sq(xs_all[k]);
-        if (k + 1 < 4 * NV) t += sq(xs_all[k + 1]);
-        if (k + 2 < 4 * NV) t += sq(xs_all[k + 2]);
+        if (k + 1 < 4 * NW) t += sq(xs_all[k + 1]);
+        if (k + 2 < 4 * NW) t += sq(xs_all[k + 2]);
         acc3(t);
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -317,6 +325,21 @@ __global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t
         uint64_t hi2 = __shfl_xor_sync(0xffffffffu, hi, o);
         lo += lo2;
         hi += hi2 + (lo < lo2 ? 1 : 0);
+    }
+    if constexpr (WPR > 1) {
+        if (lane == 0) {
+            s_red[WPR + 2 * w] = lo;
+            s_red[WPR + 2 * w + 1] = hi;
+        }
+        __syncthreads();
+        lo = 0;
+        hi = 0;
+#pragma unroll
+        for (int k = 0; k < WPR; k++) {
+            const uint64_t lo2 = s_red[WPR + 2 * k];
+            lo += lo2;
+            hi += s_red[WPR + 2 * k + 1] + (lo < lo2 ? 1 : 0);
+        }
     }
     const u128 sum_sq = ((u128)hi << 64) | lo;
     const u128 var = udiv128_u32(sum_sq, (uint32_t)D);
@@ -332,11 +355,11 @@ __global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t
     const int s = ln.s;
     const bool est_ok = ln.beta_frac == 0 && s <= 126;
     const double ud = u128_to_double_signed(u) * exp2_neg(s);
-    uint32_t* orow = reinterpret_cast<uint32_t*>(out + (size_t)r * ldo) + lane;
-    uint32_t* lrow = out_lo ? reinterpret_cast<uint32_t*>(out_lo + (size_t)r * ldo) + lane : nullptr;
+    uint32_t* orow = reinterpret_cast<uint32_t*>(out + (size_t)r * ldo) + 32 * NW * w + lane;
+    uint32_t* lrow = out_lo ? reinterpret_cast<uint32_t*>(out_lo + (size_t)r * ldo) + 32 * NW * w + lane : nullptr;
 #pragma unroll
-    for (int i = 0; i < NV; i++) {
-        const int j0 = 128 * i + 4 * lane;
+    for (int i = 0; i < NW; i++) {
+        const int j0 = 128 * (NW * w + i) + 4 * lane;
         const uint2 graw = *reinterpret_cast<const uint2*>(ln.g + j0);
         const int4 bv = *reinterpret_cast<const int4*>(ln.b + j0);
         const int32_t xs[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
@@ -373,6 +396,29 @@ __global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t
         orow[32 * i] = word;
         if (lrow) lrow[32 * i] = lword;
     }
+}
+
+
+// One warp per row, 8 rows per block (passes with many rows).
+template <int NV>
+__global__ void __launch_bounds__(256, 4) k_resid_ln_v(int32_t* x, const int32_t* delta, int R, LnDev ln, int ln_k,
+                                                       int ln_j, uint64_t eps, int8_t* out, int ldo, int8_t* out_lo) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;
+    if (r >= R) return;
+    resid_ln_row<NV, 1>(x, delta, r, 0, lane, ln, ln_k, ln_j, eps, out, ldo, out_lo, nullptr);
+}
+
+// WPR warps per row, one row per block (passes of few rows, such as a decode step: more warps in
+// flight and a shorter chain per warp).
+template <int NV, int WPR>
+__global__ void __launch_bounds__(32 * WPR) k_resid_ln_split(int32_t* x, const int32_t* delta, int R, LnDev ln,
+                                                             int ln_k, int ln_j, uint64_t eps, int8_t* out, int ldo,
+                                                             int8_t* out_lo) {
+    __shared__ uint64_t s_red[3 * WPR];
+    const int r = blockIdx.x;  // every thread of the block takes part in the barriers
+    resid_ln_row<NV, WPR>(x, delta, r, threadIdx.x >> 5, threadIdx.x & 31, ln, ln_k, ln_j, eps, out, ldo, out_lo,
+                          s_red);
 }
 
 __global__ void k_resid_add(int32_t* x, const int32_t* delta, size_t n) {
@@ -1496,11 +1542,16 @@ void launch_layernorm(const int32_t* x, int R, int d, const LnDev& ln, int ln_k,
     k_layernorm<<<R, 256, 0, st>>>(x, R, d, ln, ln_k, ln_j, eps, out, ldo, out_lo);
 }
 
+// Up to this many rows a LayerNorm row is split over three warps (the decode steps of an unfold).
+constexpr int LN_SPLIT_ROWS = 4096;
+
 void launch_resid_layernorm(int32_t* x, const int32_t* delta, int R, int d, const LnDev& ln, int ln_k, int ln_j,
                             uint64_t eps, int8_t* out, int ldo, cudaStream_t st, int8_t* out_lo) {
     if (R <= 0) return;
     int blocks = (R + 7) / 8;
-    if (d == 768 && ldo % 4 == 0) {
+    if (d == 768 && ldo % 4 == 0 && R <= LN_SPLIT_ROWS) {
+        k_resid_ln_split<6, 3><<<R, 96, 0, st>>>(x, delta, R, ln, ln_k, ln_j, eps, out, ldo, out_lo);
+    } else if (d == 768 && ldo % 4 == 0) {
         k_resid_ln_v<6><<<blocks, 256, 0, st>>>(x, delta, R, ln, ln_k, ln_j, eps, out, ldo, out_lo);
     } else if (d <= 32 * 24) {
         k_resid_ln<24><<<blocks, 256, 0, st>>>(x, delta, R, d, ln, ln_k, ln_j, eps, out, ldo, out_lo);

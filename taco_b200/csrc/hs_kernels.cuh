@@ -53,7 +53,7 @@ void launch_gemm_simple(int mode, const int8_t* A, int lda, int R, const LinearD
 // [heads * hd, n_ctx].
 void launch_gemm_tc(int mode, const void* tmA, const void* tmB, const void* tmC, int R, int Np, int Kp,
                     const EpiArgs& e, int num_sms, int* err, cudaStream_t st, const void* tmA2 = nullptr,
-                    const void* tmK = nullptr, const void* tmV = nullptr);
+                    const void* tmK = nullptr, const void* tmV = nullptr, const void* tmB64 = nullptr);
 
 #ifdef __CUDACC__
 // vt_run_host for the warp whose lane l holds row r0 + l (warp-uniform result).

@@ -150,6 +150,7 @@ struct DevLinear {
     int64_t* wsum = nullptr;
     alignas(128) CUtensorMap tm;
     alignas(128) CUtensorMap tm128;
+    alignas(128) CUtensorMap tm64;  // 64-row boxes: the 64-column tiles of passes of few rows
 };
 
 }  // namespace
@@ -394,6 +395,7 @@ int upload_linear(hs_model* m, const hsm::Linear& L, DevLinear& D, bool wide_in 
         if ((rc = upload(&D.wsum, ws.data(), ws.size(), m->owned))) return rc;
         if ((rc = make_tmap(m->dev, &D.tm128, dw, Np, Kp, 128))) return rc;
     }
+    if ((rc = make_tmap(m->dev, &D.tm64, dw, Np, Kp, 64))) return rc;
     return make_tmap(m->dev, &D.tm, dw, Np, Kp, TILE_N);
 }
 
@@ -431,7 +433,7 @@ int forward(hs_batch* b, int R) {
         if (m->use_tc)
             launch_gemm_tc(mode, tmA, tmA2 ? &W.tm128 : &W.tm, qkv_tma ? &b->ts_q : tmC, R, W.ld.Np, W.ld.Kp, e,
                            m->dev->num_sms, m->dev->d_err, st, tmA2, qkv_tma ? &b->ts_kc : nullptr,
-                           qkv_tma ? &b->ts_vt : nullptr);
+                           qkv_tma ? &b->ts_vt : nullptr, &W.tm64);
         else
             launch_gemm_simple(mode, A, lda, R, W.ld, e, st);
     };
