@@ -549,8 +549,10 @@ class CudaBatch:
         return {arr[i].name.decode(): {"ms": arr[i].ms, "launches": arr[i].launches, "ops": arr[i].ops}
                 for i in range(n)}
 
-    def run_coded(self, slots, tokens, kinds, values, freq_bits: int = 32) -> np.ndarray:
-        """The coder answers of the inputs: a structured array (symbol, is_last, start, freq)."""
+    def run_coded(self, slots, tokens, kinds, values, freq_bits: int = 32, out: np.ndarray | None = None) -> np.ndarray:
+        """The coder answers of the inputs: a structured array (symbol, is_last, start, freq).
+        `out`, if given, is a caller-owned INTERVAL_DTYPE array of the inputs' length that receives
+        the answers (a caller that codes many batches reuses one buffer)."""
         s = np.ascontiguousarray(slots, dtype=np.uint32)
         t = np.ascontiguousarray(tokens, dtype=np.uint32)
         k = np.ascontiguousarray(kinds, dtype=np.uint32)
@@ -558,7 +560,10 @@ class CudaBatch:
         n = s.size
         if not (t.size == k.size == v.size == n):
             raise HardShellError(HS_LENGTH_MISMATCH, "the inputs and the queries differ in length")
-        out = np.zeros(n, dtype=INTERVAL_DTYPE)
+        if out is None:
+            out = np.zeros(n, dtype=INTERVAL_DTYPE)
+        elif out.dtype != INTERVAL_DTYPE or out.size != n or not out.flags["C_CONTIGUOUS"] or not out.flags["WRITEABLE"]:
+            raise HardShellError(HS_LENGTH_MISMATCH, "out must be a writable contiguous interval array of the inputs' length")
         _check(lib().hs_batch_run_coded(self.h, _p(s), _p(t), _p(k), _p(v), n, freq_bits, _p(out)))
         return out
 

@@ -203,6 +203,7 @@ struct hs_batch {
     uint16_t overlap = 0;
     std::vector<int> pos;
     std::vector<uint32_t> hist;  // [slots, n_ctx]
+    std::vector<uint32_t> hist_work;  // the planning copy of hist during a call (swapped in on commit)
     std::vector<StreamSt> streams;              // per slot
     std::vector<std::vector<uint32_t>> prev;    // per slot: the full context before the last restart
     std::vector<void*> owned;
@@ -634,8 +635,10 @@ struct PlanRow {
 // positions and histories change in copies; the caller commits them after the passes ran.
 // The stream states and kept contexts of the slots that a call touches, committed with the
 // positions (batch/plan.rs:68-116).
+// The stream states of a call, committed only when every pass ran: a copy of each slot's state
+// (slot-indexed, so that an input costs no look-up) and the contexts saved by restarts.
 struct StreamPlan {
-    std::unordered_map<uint32_t, StreamSt> st;
+    std::vector<StreamSt> st;
     std::unordered_map<uint32_t, std::vector<uint32_t>> prev;
 };
 
@@ -646,12 +649,15 @@ void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* token
     const int k = std::min<int>(b->overlap, n_ctx - 2);
     const uint32_t eot = b->model->eot;
     pos = b->pos;
-    hist = b->hist;
+    hist.assign(b->hist.begin(), b->hist.end());  // into a buffer kept by the batch: no new pages
+    sp.st = b->streams;
     std::vector<char> in_pass(b->slots, 0);
     std::vector<PlanRow> cur;
+    cur.reserve(std::min<size_t>((size_t)b->max_rows, n + 64));
     auto flush = [&]() {
         if (!cur.empty()) passes.push_back(std::move(cur));
-        cur.clear();
+        cur = std::vector<PlanRow>();
+        cur.reserve(std::min<size_t>((size_t)b->max_rows, n + 64));
         std::fill(in_pass.begin(), in_pass.end(), 0);
     };
     auto push = [&](PlanRow r) {
@@ -663,7 +669,7 @@ void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* token
         uint32_t s = slots[i];
         uint32_t* h = &hist[(size_t)s * n_ctx];
         int at = pos[s];
-        StreamSt& ss = sp.st.try_emplace(s, b->streams[s]).first->second;
+        StreamSt& ss = sp.st[s];
         if (at >= n_ctx) {
             if (in_pass[s]) flush();
             // The full context before the restart, for a truncation (stream.rs restart).
@@ -795,7 +801,7 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     }
     std::vector<std::vector<PlanRow>> passes;
     std::vector<int> pos;
-    std::vector<uint32_t> hist;
+    std::vector<uint32_t>& hist = b->hist_work;
     StreamPlan sp;
     plan_passes(b, slots, tokens, n, passes, pos, hist, sp);
     // Coder answers: pass k uses half k & 1 of the host buffers, and the host prepares pass k + 1
@@ -975,8 +981,8 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
     }
     // Every pass ran: commit the positions and histories (batch/plan.rs:120 commit).
     b->pos = pos;
-    b->hist = hist;
-    for (auto& kv : sp.st) b->streams[kv.first] = kv.second;
+    b->hist.swap(b->hist_work);
+    b->streams.swap(sp.st);
     for (auto& kv : sp.prev) b->prev[kv.first] = std::move(kv.second);
     return HS_OK;
 }
