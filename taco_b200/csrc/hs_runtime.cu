@@ -17,6 +17,7 @@
 #include <memory>
 #include <string>
 #include <unordered_map>
+#include <deque>
 #include <vector>
 
 #include "../../include/hardshell_b200.h"
@@ -642,54 +643,83 @@ struct StreamPlan {
     std::unordered_map<uint32_t, std::vector<uint32_t>> prev;
 };
 
-void plan_passes(const hs_batch* b, const uint32_t* slots, const uint32_t* tokens, uint32_t n,
-                 std::vector<std::vector<PlanRow>>& passes, std::vector<int>& pos, std::vector<uint32_t>& hist,
-                 StreamPlan& sp) {
-    const int n_ctx = b->model->c.n_ctx;
-    const int k = std::min<int>(b->overlap, n_ctx - 2);
-    const uint32_t eot = b->model->eot;
-    pos = b->pos;
-    hist.assign(b->hist.begin(), b->hist.end());  // into a buffer kept by the batch: no new pages
-    sp.st = b->streams;
-    std::vector<char> in_pass(b->slots, 0);
+// The passes of a call (crates/hardshell-cuda/src/batch/plan.rs:60-120), made as the call runs
+// them: advance(want) takes inputs until `want` passes are complete or the inputs end, so the
+// host plans pass k + 1 while the GPU runs pass k. A pass is cut at max_rows rows and before a
+// context restart of a slot already in it. The positions, histories and stream states are
+// copies, committed only when every pass ran. The passes are a deque, so a pass stays where it
+// is while later ones are added.
+struct Planner {
+    const hs_batch* b;
+    const uint32_t* slots;
+    const uint32_t* tokens;
+    const uint32_t n;
+    uint32_t i = 0;
+    const int n_ctx, k;
+    const uint32_t eot;
+    std::deque<std::vector<PlanRow>> passes;
+    std::vector<int> pos;
+    std::vector<uint32_t>& hist;
+    StreamPlan sp;
+    std::vector<char> in_pass;
     std::vector<PlanRow> cur;
-    cur.reserve(std::min<size_t>((size_t)b->max_rows, n + 64));
-    auto flush = [&]() {
-        if (!cur.empty()) passes.push_back(std::move(cur));
-        cur = std::vector<PlanRow>();
-        cur.reserve(std::min<size_t>((size_t)b->max_rows, n + 64));
+    bool done = false;
+
+    Planner(const hs_batch* b_, const uint32_t* slots_, const uint32_t* tokens_, uint32_t n_,
+            std::vector<uint32_t>& hist_work)
+        : b(b_), slots(slots_), tokens(tokens_), n(n_), n_ctx(b_->model->c.n_ctx),
+          k(std::min<int>(b_->overlap, b_->model->c.n_ctx - 2)), eot(b_->model->eot), pos(b_->pos), hist(hist_work),
+          in_pass(b_->slots, 0) {
+        hist.assign(b->hist.begin(), b->hist.end());  // into a buffer kept by the batch: no new pages
+        sp.st = b->streams;
+        cur.reserve(row_reserve());
+    }
+    size_t row_reserve() const { return std::min<size_t>((size_t)b->max_rows, (size_t)n + 64); }
+    void flush() {
+        if (!cur.empty()) {
+            passes.push_back(std::move(cur));
+            cur = std::vector<PlanRow>();
+            cur.reserve(row_reserve());
+        }
         std::fill(in_pass.begin(), in_pass.end(), 0);
-    };
-    auto push = [&](PlanRow r) {
+    }
+    void push(PlanRow r) {
         if ((int)cur.size() >= b->max_rows) flush();
         in_pass[r.slot] = 1;
         cur.push_back(r);
-    };
-    for (uint32_t i = 0; i < n; i++) {
-        uint32_t s = slots[i];
-        uint32_t* h = &hist[(size_t)s * n_ctx];
-        int at = pos[s];
-        StreamSt& ss = sp.st[s];
-        if (at >= n_ctx) {
-            if (in_pass[s]) flush();
-            // The full context before the restart, for a truncation (stream.rs restart).
-            sp.prev[s].assign(h, h + n_ctx);
-            ss.prev_first = (int32_t)ss.first;
-            ss.first = (uint32_t)k + 1;
-            ss.written = (uint32_t)k + 1;
-            memmove(h + 1, h + (n_ctx - k), sizeof(uint32_t) * k);
-            h[0] = eot;
-            for (int q = 0; q <= k; q++) push({s, h[q], (uint32_t)q, -1});
-            at = k + 1;
-        }
-        h[at] = tokens[i];
-        push({s, tokens[i], (uint32_t)at, (long)i});
-        pos[s] = at + 1;
-        ss.len++;
-        ss.written = std::max(ss.written, (uint32_t)at + 1);
     }
-    flush();
-}
+    void advance(size_t want) {
+        while (!done && passes.size() < want) {
+            if (i == n) {
+                flush();
+                done = true;
+                break;
+            }
+            const uint32_t s = slots[i];
+            uint32_t* h = &hist[(size_t)s * n_ctx];
+            int at = pos[s];
+            StreamSt& ss = sp.st[s];
+            if (at >= n_ctx) {
+                if (in_pass[s]) flush();
+                // The full context before the restart, for a truncation (stream.rs restart).
+                sp.prev[s].assign(h, h + n_ctx);
+                ss.prev_first = (int32_t)ss.first;
+                ss.first = (uint32_t)k + 1;
+                ss.written = (uint32_t)k + 1;
+                memmove(h + 1, h + (n_ctx - k), sizeof(uint32_t) * k);
+                h[0] = eot;
+                for (int q = 0; q <= k; q++) push({s, h[q], (uint32_t)q, -1});
+                at = k + 1;
+            }
+            h[at] = tokens[i];
+            push({s, tokens[i], (uint32_t)at, (long)i});
+            pos[s] = at + 1;
+            ss.len++;
+            ss.written = std::max(ss.written, (uint32_t)at + 1);
+            i++;
+        }
+    }
+};
 
 // The host side of a mixed call (crates/hardshell-cuda/src/batch/mixed.rs:25-35 Mixing): the
 // table word of each input, the host mixer, and for run_coded_dual the intervals of GPT-2 alone.
@@ -799,11 +829,8 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         if ((rc = dalloc(&b->weights, (size_t)b->Rcap * c.V, b->owned))) return rc;
         b->bytes += (uint64_t)b->Rcap * c.V * 8;
     }
-    std::vector<std::vector<PlanRow>> passes;
-    std::vector<int> pos;
-    std::vector<uint32_t>& hist = b->hist_work;
-    StreamPlan sp;
-    plan_passes(b, slots, tokens, n, passes, pos, hist, sp);
+    Planner plan(b, slots, tokens, n, b->hist_work);
+    auto& passes = plan.passes;
     // Coder answers: pass k uses half k & 1 of the host buffers, and the host prepares pass k + 1
     // while the GPU runs pass k. Before a half is filled again (pass k + 2), the answers of the
     // pass that used it are copied out. The device buffers are reused in stream order.
@@ -889,7 +916,9 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         CK(cudaEventRecord(b->pass_done[h], b->stream));
         return HS_OK;
     };
-    for (size_t k = 0; k < passes.size(); k++) {
+    for (size_t k = 0;; k++) {
+        plan.advance(k + 1);  // pass k (planned while the GPU runs pass k - 1)
+        if (k >= passes.size()) break;
         const auto& pass = passes[k];
         if (out && !mix && k >= 2 && (rc = answers_out(k - 2))) return rc;
         use_half(k);
@@ -980,10 +1009,10 @@ int run(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32
         }
     }
     // Every pass ran: commit the positions and histories (batch/plan.rs:120 commit).
-    b->pos = pos;
+    b->pos = plan.pos;
     b->hist.swap(b->hist_work);
-    b->streams.swap(sp.st);
-    for (auto& kv : sp.prev) b->prev[kv.first] = std::move(kv.second);
+    b->streams.swap(plan.sp.st);
+    for (auto& kv : plan.sp.prev) b->prev[kv.first] = std::move(kv.second);
     return HS_OK;
 }
 
