@@ -320,7 +320,8 @@ int hs_unfold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* con
  * device, the model file loaded and a batch of `slots` slots and `max_rows` rows) take rounds of
  * each segment's coded blocks, as the reference deals the blocks of an unfold job to its lanes
  * (crates/taco/src/gpu_unfold.rs:74-200); raw and zstd blocks stay on the host. The output and the
- * errors are those of hs_unfold (several corrupt blocks report the lowest index). */
+ * errors are those of hs_unfold (several corrupt blocks report the lowest index). The workers
+ * start at the first segment with coded blocks, so a container without any opens no GPU. */
 int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
                     uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* container,
                     size_t len, uint8_t* out, size_t cap, size_t* out_len);

@@ -1228,7 +1228,8 @@ class OneDecoder : public UnfoldGpu {
 // the job's coded blocks from one counter, as the GPU fold's threads take windows
 // (crates/taco/src/gpu_unfold.rs:74-200 deals the blocks of a job to the lanes). Several corrupt
 // blocks report the one with the lowest index, so the error does not depend on the dealing
-// (unfold.rs decode_group). Workers that cannot open give their share to the others.
+// (unfold.rs decode_group). Workers that cannot open give their share to the others. The workers
+// start at the first segment with coded blocks: a container of raw and zstd blocks opens no GPU.
 class MultiDecoder : public UnfoldGpu {
   public:
     MultiDecoder(const std::vector<int>& ords, const uint8_t* model_file, size_t model_len, const uint8_t* hash,
@@ -1262,6 +1263,11 @@ class MultiDecoder : public UnfoldGpu {
     }
 
     int run(const CodedJob& J) override {
+        if (!started_) {
+            started_ = true;
+            if ((start_rc_ = start())) return start_rc_;
+        }
+        if (start_rc_) return start_rc_;
         std::unique_lock<std::mutex> lk(mu_);
         job_ = &J;
         next_ = 0;
@@ -1357,6 +1363,8 @@ class MultiDecoder : public UnfoldGpu {
     bool quit_ = false;
     uint16_t overlap_ = 0;
     const CodedJob* job_ = nullptr;
+    bool started_ = false;
+    int start_rc_ = HS_OK;
     std::atomic<size_t> next_{0};
     uint64_t bad_ = UINT64_MAX;
     std::string bad_why_;
@@ -1508,7 +1516,6 @@ int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_f
     std::vector<int> ords;
     for (uint32_t k = 0; k < per; k++) ords.insert(ords.end(), ordinals, ordinals + n_gpus);
     MultiDecoder gpu(ords, model_file, model_len, hash, slots, max_rows);
-    if ((rc = gpu.start())) return rc;
     MemWriter w(out, cap);
     return unfold_stream_impl(gpu, hash, eot, tok, in, len, w);
 }
