@@ -8,8 +8,9 @@
 // The integer softmax of crates/hardshell/src/softmax.rs:78 needs the exact row max before any
 // weight and the exact row sum before any probability, so a tile runs three passes over its
 // 128-key chunks, with S = Q K^T computed twice on the tensor cores (cheap: K = 64):
-//   pass 1: S -> the max and min dot of each row (score() is monotone in the dot, so the max
-//           score is max(score(maxdot), score(mindot)), as in the reference GPU kernel);
+//   pass 1: S -> the max dot of each row when the score multiplier is >= 0, else the min dot
+//           (score() is monotone in the dot, rising or falling with the multiplier's sign, so the
+//           max score is the score of that extreme);
 //   pass 2: S -> the table index d = min(max - score, len - 1) -> e = attn_exp[d] -> the row sum;
 //           each key's d (u16) goes to this CTA's slot of a scratch buffer in global memory;
 //   pass 3: d back from the scratch (no third S) -> p = floor(e * 2^P / sum) (an exact
@@ -417,61 +418,51 @@ __global__ void __launch_bounds__(ATHREADS, 1)
             // whole and the masked path is the warp's, so the diagonal slice takes the masked path
             // once instead of both paths diverged.
             const int wfirst = (int)grp.pos0 + g * 32;
-            // Pass 1: the max and min dot over the row's causal keys.
-            int32_t maxd = INT32_MIN, mind = INT32_MAX;
-            for (int c = 0; c < nch; c++, sit++) {
-                const int sb = sit & 1;
-                mbar_wait(&bars->s_full[sb], (sit >> 1) & 1, err, 21);
-                __syncwarp();
-                tc_fence_after();
-                uint32_t v[32];
-                tmem_ld32(tbase + sb * KC, v);
-                tmem_ld_wait();
-                tc_fence_before();
-                mbar_arrive(&bars->s_empty[sb]);
-                const int j0 = c * KC + qt * 32;
-                if (j0 > wlast) {
-                    // every key of this slice is masked for this warp's rows
-                } else if (j0 + 31 <= wfirst) {
-                    // A max/min tree instead of one dependent chain of 32 steps.
-                    int32_t mx[8], mn[8];
+            // Pass 1: the extreme dot over the row's causal keys. score() is monotone in the dot,
+            // rising with it when sm >= 0 and falling when sm < 0 (the same for every row), so the
+            // max score is score(max dot) or score(min dot): one of the two is tracked.
+            auto pass1 = [&](auto ext, const int32_t ident) -> int32_t {
+                int32_t xd = ident;
+                for (int c = 0; c < nch; c++, sit++) {
+                    const int sb = sit & 1;
+                    mbar_wait(&bars->s_full[sb], (sit >> 1) & 1, err, 21);
+                    __syncwarp();
+                    tc_fence_after();
+                    uint32_t v[32];
+                    tmem_ld32(tbase + sb * KC, v);
+                    tmem_ld_wait();
+                    tc_fence_before();
+                    mbar_arrive(&bars->s_empty[sb]);
+                    const int j0 = c * KC + qt * 32;
+                    if (j0 > wlast) {
+                        // every key of this slice is masked for this warp's rows
+                    } else if (j0 + 31 <= wfirst) {
+                        // A tree instead of one dependent chain of 32 steps.
+                        int32_t t[8];
 #pragma unroll
-                    for (int q = 0; q < 8; q++) {
-                        mx[q] = max(max((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), max((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
-                        mn[q] = min(min((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), min((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
-                    }
+                        for (int q = 0; q < 8; q++)
+                            t[q] = ext(ext((int32_t)v[4 * q], (int32_t)v[4 * q + 1]), ext((int32_t)v[4 * q + 2], (int32_t)v[4 * q + 3]));
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        mx[q] = max(mx[q], mx[q + 4]);
-                        mn[q] = min(mn[q], mn[q + 4]);
-                    }
-                    maxd = max(maxd, max(max(mx[0], mx[1]), max(mx[2], mx[3])));
-                    mind = min(mind, min(min(mn[0], mn[1]), min(mn[2], mn[3])));
-                } else {
+                        for (int q = 0; q < 4; q++) t[q] = ext(t[q], t[q + 4]);
+                        xd = ext(xd, ext(ext(t[0], t[1]), ext(t[2], t[3])));
+                    } else {
 #pragma unroll
-                    for (int q = 0; q < 32; q++) {
-                        if (j0 + q <= rpos) {
-                            int32_t dv = (int32_t)v[q];
-                            maxd = dv > maxd ? dv : maxd;
-                            mind = dv < mind ? dv : mind;
-                        }
+                        for (int q = 0; q < 32; q++)
+                            if (j0 + q <= rpos) xd = ext(xd, (int32_t)v[q]);
                     }
                 }
-            }
-            sXm[(0 * 4 + qt) * GM + row] = maxd;
-            sXm[(1 * 4 + qt) * GM + row] = mind;
-            named_bar(1, ETH);
+                sXm[qt * GM + row] = xd;
+                named_bar(1, ETH);
 #pragma unroll
-            for (int o = 0; o < 4; o++) {
-                const int32_t a = sXm[(0 * 4 + o) * GM + row], b = sXm[(1 * 4 + o) * GM + row];
-                maxd = a > maxd ? a : maxd;
-                mind = b < mind ? b : mind;
-            }
-            int64_t M = INT64_MIN;
-            if (maxd >= mind) {
-                int64_t s1 = score_of(maxd, sm, ss, fast, hround), s2 = score_of(mind, sm, ss, fast, hround);
-                M = s1 > s2 ? s1 : s2;
-            }
+                for (int o = 0; o < 4; o++) xd = ext(xd, sXm[o * GM + row]);
+                return xd;
+            };
+            const bool rising = sm >= 0;
+            const int32_t ident = rising ? INT32_MIN : INT32_MAX;
+            const int32_t xd = rising ? pass1([](int32_t a, int32_t b) { return max(a, b); }, INT32_MIN)
+                                      : pass1([](int32_t a, int32_t b) { return min(a, b); }, INT32_MAX);
+            // |dot| <= 2^20, so the identity means that the row has no key (a row past the group).
+            const int64_t M = xd != ident ? score_of(xd, sm, ss, fast, hround) : INT64_MIN;
             // The tile before: its last P V products ran while this pass 1 did.
             if (seq > 0) epilogue(seq - 1, prev_first, prev_count, prev_h);
             prev_first = grp.first_row;
