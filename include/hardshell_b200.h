@@ -257,8 +257,10 @@ int hs_fold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* input
  * tokenizer must have the model's vocabulary (HS_MODEL). A GPU that cannot be opened, load the
  * model or hold the batch gives its windows to the GPUs that can (stats->gpus_failed counts it),
  * as the reference falls back from a device that fails (crates/taco/src/backend.rs:288-342); with
- * no GPU left the call fails with the first GPU's error. An error while windows run fails the
- * call with that GPU's status and message. The container is the bytes hs_fold gives on one GPU. */
+ * no GPU left the call fails with the first GPU's error when the first windows are to run. The
+ * GPUs open while the host tokenizes and compresses the first segment. An error while windows run
+ * fails the call with that GPU's status and message. The container is the bytes hs_fold gives on
+ * one GPU. */
 int hs_fold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
                   uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* input,
                   size_t len, const hs_fold_options* options, uint8_t* out, size_t cap, size_t* out_len,
@@ -295,6 +297,34 @@ int hs_fold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* mo
                          hs_source_fn source, void* source_user, hs_sink_fn sink, void* sink_user,
                          const hs_fold_options* options, uint64_t* out_len, hs_fold_stats* stats);
 
+/* The length of a fold input that is not known before it ends (a pipe). */
+#define HS_LEN_UNKNOWN UINT64_MAX
+
+/* StreamFold::to_writer (stream.rs:430-452), the method "spool": the fold of hs_fold of the bytes
+ * that `source` gives, into `write`, an output that cannot seek (a pipe). The stored blocks and
+ * the table go to two temporary files in `spool_dir` (NULL: $TMPDIR, else /tmp), named
+ * .taco-spool-<pid>-blocks-XXXXXX and -table-XXXXXX and unlinked as soon as they are made, so
+ * they vanish when the call ends, after an error or a crash too; at the end the header, the
+ * table and the blocks go to `write` in that order. The spool holds about the container's size.
+ * `len` is the input length, or HS_LEN_UNKNOWN: then the source is read until it ends, and the
+ * block size is options->block_size or the default (`spread` needs the length and is ignored).
+ * HS_IO if the source gives fewer or more than a known `len` bytes, a temporary file cannot be
+ * made or written, or a callback fails; HS_UNSUPPORTED past 2^32 - 1 blocks. The container is
+ * the bytes of hs_fold_stream. hs_fold_stream refuses HS_LEN_UNKNOWN (HS_BAD_ARGUMENT): a
+ * seekable output needs the table's size before the first block. */
+int hs_fold_spool(hs_batch* batch, const hs_tokenizer* tokenizer, uint64_t len, hs_source_fn source,
+                  void* source_user, hs_write_fn write, void* write_user, const char* spool_dir,
+                  const hs_fold_options* options, uint64_t* out_len, hs_fold_stats* stats);
+
+/* hs_fold_spool on several GPUs of this host, as hs_fold_multi. The GPUs open while the host
+ * works on the first segment, and a fold whose blocks need no model window (blocks too short to
+ * code) runs on no GPU. */
+int hs_fold_spool_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                        uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, uint64_t len,
+                        hs_source_fn source, void* source_user, hs_write_fn write, void* write_user,
+                        const char* spool_dir, const hs_fold_options* options, uint64_t* out_len,
+                        hs_fold_stats* stats);
+
 /* StreamUnfold::from_seekable (stream.rs): the unfold of hs_unfold of the `len`-byte container
  * that `read_at` reads, into `write`. The header, the whole block table and the container length
  * are checked before any output; then each segment's bytes go to `write` in order. *out_len = the
@@ -302,6 +332,16 @@ int hs_fold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* mo
  * that the bytes already written are wrong. */
 int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tokenizer, uint64_t len, hs_read_at_fn read_at,
                      void* read_user, hs_write_fn write, void* write_user, uint64_t* out_len);
+
+/* StreamUnfold::from_reader (stream.rs:809-827): the unfold of hs_unfold of the container that
+ * `source` gives in one pass (a pipe), into `write`. The header and the whole block table are
+ * read and checked before any output (they stay in memory: 5 bytes per block); the stored blocks
+ * are then read in order. A missing byte is HS_FORMAT where the segment that needs it is read,
+ * a byte after the last block HS_FORMAT at the end, so `write` can have taken restored bytes
+ * before an error; the output is complete and correct only if the call returns HS_OK. HS_IO if
+ * the source fails. *out_len = the original length (from the header). */
+int hs_unfold_pipe(hs_batch* batch, const hs_tokenizer* tokenizer, hs_source_fn source, void* source_user,
+                   hs_write_fn write, void* write_user, uint64_t* out_len);
 
 /* taco::unfold on the CUDA engine (crates/taco/src/unfold.rs, profile text): the original bytes of
  * a .taco container (version 1 or 2) into out[0 .. *out_len). The header and the block table are
@@ -325,6 +365,11 @@ int hs_unfold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* con
 int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
                     uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, const uint8_t* container,
                     size_t len, uint8_t* out, size_t cap, size_t* out_len);
+
+/* hs_unfold_pipe with the worker threads of hs_unfold_multi. */
+int hs_unfold_pipe_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                         uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, hs_source_fn source,
+                         void* source_user, hs_write_fn write, void* write_user, uint64_t* out_len);
 
 /* The version of the zstd library that hs_fold uses (major * 10000 + minor * 100 + patch), or 0
  * if it is not available. */

@@ -8,6 +8,7 @@ There is no CPU fallback: if the library or a GPU is missing, every call raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import weakref
 from dataclasses import dataclass
 from pathlib import Path
@@ -152,6 +153,14 @@ def lib() -> ctypes.CDLL:
     L.hs_unfold_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, ctypes.c_char_p,
                                   ctypes.c_size_t, vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]
     L.hs_unfold_stream.argtypes = [vp, vp, u64, READ_AT_FN, vp, WRITE_FN, vp, ctypes.POINTER(u64)]
+    L.hs_fold_spool.argtypes = [vp, vp, u64, SOURCE_FN, vp, WRITE_FN, vp, ctypes.c_char_p,
+                                ctypes.POINTER(FoldOptions), ctypes.POINTER(u64), ctypes.POINTER(FoldStats)]
+    L.hs_fold_spool_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, u64, SOURCE_FN, vp,
+                                      WRITE_FN, vp, ctypes.c_char_p, ctypes.POINTER(FoldOptions),
+                                      ctypes.POINTER(u64), ctypes.POINTER(FoldStats)]
+    L.hs_unfold_pipe.argtypes = [vp, vp, SOURCE_FN, vp, WRITE_FN, vp, ctypes.POINTER(u64)]
+    L.hs_unfold_pipe_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, SOURCE_FN, vp,
+                                       WRITE_FN, vp, ctypes.POINTER(u64)]
     L.hs_zstd_version.argtypes = []
     L.hs_zstd_version.restype = u32
     L.hs_op_linear_act.argtypes = [vp, i32, vp, vp, vp, vp, u32, u32, u32, u32, vp, vp]
@@ -254,17 +263,39 @@ def fold_multi(ordinals, model_file: bytes, tokenizer, data: bytes, block_size: 
     return out[:n.value].tobytes(), stats
 
 
-def _stream_callbacks(read, write):
-    """ctypes callbacks over Python file-like callables: read(n) -> bytes (the source),
-    write(at, data) (the seekable sink). An exception in either fails the call with HS_IO."""
+def _source(read):
+    """A ctypes source over read(n) -> bytes (at most n; b"" at the end). An exception, or more
+    than n bytes, fails the call with HS_IO."""
 
     def source(_user, buf, cap):
         try:
             data = read(cap)
         except Exception:  # noqa: BLE001 - any failure of the caller's source is an I/O error
             return -1
+        if len(data) > cap:
+            return -1
         ctypes.memmove(buf, data, len(data))
         return len(data)
+
+    return SOURCE_FN(source)
+
+
+def _writer(write):
+    """A ctypes in-order writer over write(data). An exception fails the call with HS_IO."""
+
+    def wr(_user, buf, n):
+        try:
+            write(ctypes.string_at(buf, n))
+        except Exception:  # noqa: BLE001
+            return 1
+        return 0
+
+    return WRITE_FN(wr)
+
+
+def _stream_callbacks(read, write):
+    """ctypes callbacks over Python file-like callables: read(n) -> bytes (the source),
+    write(at, data) (the seekable sink). An exception in either fails the call with HS_IO."""
 
     def sink(_user, at, buf, n):
         try:
@@ -273,7 +304,7 @@ def _stream_callbacks(read, write):
             return 1
         return 0
 
-    return SOURCE_FN(source), SINK_FN(sink)
+    return _source(read), SINK_FN(sink)
 
 
 def fold_stream(batch, tokenizer, length: int, read, write, block_size: int = 0, overlap: int = 0,
@@ -302,6 +333,64 @@ def fold_stream_multi(ordinals, model_file: bytes, tokenizer, length: int, read,
                                       length, src, None, snk, None, ctypes.byref(opt), ctypes.byref(n),
                                       ctypes.byref(st)))
     return n.value, {name: getattr(st, name) for name, _ in FoldStats._fields_}
+
+
+LEN_UNKNOWN = 0xFFFFFFFFFFFFFFFF  # HS_LEN_UNKNOWN: a fold input whose length is known only at its end
+
+
+def _spool_dir(spool_dir) -> bytes | None:
+    return None if spool_dir is None else os.fsencode(spool_dir)
+
+
+def fold_spool(batch, tokenizer, read, write, length: int | None = None, spool_dir=None, block_size: int = 0,
+               overlap: int = 0, spread: bool = False, threads: int = 0):
+    """hs_fold_spool (StreamFold::to_writer): the fold of the bytes that read(n) gives (`length`
+    of them, or None if it is not known) into the in-order writer write(data), spooling the
+    blocks and the table in `spool_dir`; returns (container length, stats)."""
+    opt = FoldOptions(block_size, overlap, int(spread), threads)
+    src, wr = _source(read), _writer(write)
+    n = ctypes.c_uint64()
+    st = FoldStats()
+    _check(lib().hs_fold_spool(batch.h, tokenizer.h, LEN_UNKNOWN if length is None else length, src, None, wr, None,
+                               _spool_dir(spool_dir), ctypes.byref(opt), ctypes.byref(n), ctypes.byref(st)))
+    return n.value, {name: getattr(st, name) for name, _ in FoldStats._fields_}
+
+
+def fold_spool_multi(ordinals, model_file: bytes, tokenizer, read, write, length: int | None = None, spool_dir=None,
+                     block_size: int = 0, overlap: int = 0, slots: int = 256, max_rows: int = 16384,
+                     spread: bool = False, threads: int = 0):
+    """hs_fold_spool_multi: fold_spool on the GPUs `ordinals`, one host thread each (a fold whose
+    blocks need no model window opens no GPU)."""
+    ords = np.ascontiguousarray(ordinals, dtype=np.int32)
+    opt = FoldOptions(block_size, overlap, int(spread), threads)
+    src, wr = _source(read), _writer(write)
+    n = ctypes.c_uint64()
+    st = FoldStats()
+    _check(lib().hs_fold_spool_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows, tokenizer.h,
+                                     LEN_UNKNOWN if length is None else length, src, None, wr, None,
+                                     _spool_dir(spool_dir), ctypes.byref(opt), ctypes.byref(n), ctypes.byref(st)))
+    return n.value, {name: getattr(st, name) for name, _ in FoldStats._fields_}
+
+
+def unfold_pipe(batch, tokenizer, read, write) -> int:
+    """hs_unfold_pipe (StreamUnfold::from_reader): the unfold of the container that read(n)
+    gives in one pass, into write(data); returns the original length."""
+    src, wr = _source(read), _writer(write)
+    n = ctypes.c_uint64()
+    _check(lib().hs_unfold_pipe(batch.h, tokenizer.h, src, None, wr, None, ctypes.byref(n)))
+    return n.value
+
+
+def unfold_pipe_multi(ordinals, model_file: bytes, tokenizer, read, write, slots: int = 256,
+                      max_rows: int = 16384) -> int:
+    """hs_unfold_pipe_multi: unfold_pipe with the worker threads of unfold_multi (a container
+    without coded blocks opens no GPU); returns the original length."""
+    ords = np.ascontiguousarray(ordinals, dtype=np.int32)
+    src, wr = _source(read), _writer(write)
+    n = ctypes.c_uint64()
+    _check(lib().hs_unfold_pipe_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows, tokenizer.h,
+                                      src, None, wr, None, ctypes.byref(n)))
+    return n.value
 
 
 def unfold_stream(batch, tokenizer, length: int, read_at, write) -> int:

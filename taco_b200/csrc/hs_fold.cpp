@@ -17,6 +17,7 @@
 // 5. Each block is stored in its smallest form: raw, then zstd, then coded, ties to the earlier
 //    (writer.rs:89 choose_smallest), and the container is written (header version 2).
 #include <dlfcn.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <functional>
@@ -25,7 +26,9 @@
 #include <chrono>
 #include <condition_variable>
 #include <mutex>
+#include <cerrno>
 #include <cstdint>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -46,6 +49,8 @@ constexpr size_t HEADER_LEN = 104;                  // version 2 header
 constexpr uint32_t FREQ_BITS = 32;                  // codec.rs:35
 constexpr int ZSTD_LEVEL = 19;                      // crates/taco-format/src/zstd_block.rs:23
 constexpr uint8_t KIND_RAW = 0, KIND_CODED = 1, KIND_ZSTD = 2;
+constexpr uint64_t MAX_BLOCKS = 0xFFFFFFFFull;      // the block count is a u32 (header.rs)
+constexpr uint64_t LEN_UNKNOWN = HS_LEN_UNKNOWN;    // a fold input or an unfold container of unknown length
 
 // ---- zstd, from the system library (opened once) ----
 
@@ -469,24 +474,25 @@ class MultiGpu : public GpuRunner {
         for (auto& t : threads_) t.join();
     }
 
-    // Starts the threads and waits until every GPU tried to open. HS_OK if one or more did.
-    int start() {
+    // Starts the threads, each of which opens its GPU. The opening overlaps the host's work on
+    // the first segment; run() waits for it, so a fold that needs no window opens no GPU.
+    void start() {
         for (uint32_t g = 0; g < c_.n; g++) threads_.emplace_back([this, g] { worker(g); });
-        std::unique_lock<std::mutex> lk(mu_);
-        cv_.wait(lk, [&] { return tried_ == c_.n; });
-        uint32_t ok = 0;
-        for (uint32_t g = 0; g < c_.n; g++) ok += live_[g];
-        failed_ = c_.n - ok;
-        if (ok == 0)
-            return hs::host_fail(rcs_[0], "no GPU of the fold opened; GPU " + std::to_string(c_.ordinals[0]) + ": " +
-                                              msgs_[0]);
-        return HS_OK;
     }
 
-    uint32_t failed() const { return failed_; }
+    // The GPUs that did not open (after every GPU tried).
+    uint32_t failed() {
+        std::unique_lock<std::mutex> lk(mu_);
+        wait_tried(lk);
+        return failed_;
+    }
 
     int run(WindowFeed& feed, const std::vector<FoldBlock>& blocks) override {
         std::unique_lock<std::mutex> lk(mu_);
+        wait_tried(lk);
+        if (failed_ == c_.n)
+            return hs::host_fail(rcs_[0], "no GPU of the fold opened; GPU " + std::to_string(c_.ordinals[0]) + ": " +
+                                              msgs_[0]);
         feed_ = &feed;
         blocks_ = &blocks;
         busy_ = c_.n - failed_;
@@ -500,6 +506,13 @@ class MultiGpu : public GpuRunner {
     }
 
   private:
+    void wait_tried(std::unique_lock<std::mutex>& lk) {  // under mu_
+        cv_.wait(lk, [&] { return tried_ == c_.n; });
+        uint32_t ok = 0;
+        for (uint32_t g = 0; g < c_.n; g++) ok += live_[g];
+        failed_ = c_.n - ok;
+    }
+
     void note(uint32_t g, int rc) {  // under mu_
         char buf[1024];
         hs_last_error(buf, sizeof buf);
@@ -576,10 +589,41 @@ struct Source {
     virtual int64_t read(uint8_t* buf, size_t cap) = 0;
 };
 
-// A seekable output: write() puts n bytes at offset `at`; 0, or non-zero on an error.
+// Where the parts of the container go (stream.rs Layout): the stored blocks in order, the
+// table entries in order, and the header last, which completes the container. Each call gives 0,
+// or non-zero on an error. A sink that needs the input length before the first block (it puts
+// the blocks after a table whose size follows from the length) says so with needs_len() and
+// receives the offset of the first stored byte in begin().
 struct Sink {
     virtual ~Sink() = default;
+    virtual bool needs_len() const { return false; }
+    virtual int begin(uint64_t /*data_off*/) { return 0; }
+    virtual int block(const uint8_t* p, size_t n) = 0;
+    virtual int table(const uint8_t* p, size_t n) = 0;
+    virtual int header(const uint8_t* p, size_t n) = 0;
+    // What failed, after a call gave non-zero.
+    virtual std::string why() const { return "the output sink failed"; }
+};
+
+// A seekable output (stream.rs SeekLayout): write() puts n bytes at offset `at`. The header and
+// the table have their places at the start; the blocks follow the table.
+struct SeekSink : Sink {
+    uint64_t block_at = 0, table_at = HEADER_LEN;
     virtual int write(uint64_t at, const uint8_t* p, size_t n) = 0;
+    bool needs_len() const override { return true; }
+    int begin(uint64_t data_off) override {
+        block_at = data_off;
+        return 0;
+    }
+    int block(const uint8_t* p, size_t n) override {
+        block_at += n;
+        return write(block_at - n, p, n);
+    }
+    int table(const uint8_t* p, size_t n) override {
+        table_at += n;
+        return write(table_at - n, p, n);
+    }
+    int header(const uint8_t* p, size_t n) override { return write(0, p, n); }
 };
 
 struct MemSource : Source {
@@ -597,7 +641,7 @@ struct MemSource : Source {
 
 // The caller's buffer; writes past its end are dropped and remembered (the caller gets the
 // length it needs).
-struct MemSink : Sink {
+struct MemSink : SeekSink {
     uint8_t* out;
     size_t cap;
     bool overflow = false;
@@ -616,11 +660,86 @@ struct CallbackSource : Source {
     CallbackSource(hs_source_fn f, void* u) : fn(f), user(u) {}
 };
 
-struct CallbackSink : Sink {
+struct CallbackSink : SeekSink {
     hs_sink_fn fn;
     void* user;
     int write(uint64_t at, const uint8_t* p, size_t n) override { return fn(user, at, p, n); }
     CallbackSink(hs_sink_fn f, void* u) : fn(f), user(u) {}
+};
+
+// The method "spool" for an output that cannot seek (stream.rs SpoolLayout and TempFile): the
+// stored blocks and the table go to two temporary files in a directory of the caller; at the end
+// the header goes to the writer, then the table and the blocks are copied after it. Each file is
+// unlinked as soon as it is made (mkstemp, name .taco-spool-<pid>-<part>-XXXXXX), so it vanishes
+// when the fold ends, after an error or a crash too; the reference deletes its files when the
+// fold ends.
+class SpoolSink : public Sink {
+  public:
+    SpoolSink(hs_write_fn fn, void* user) : fn_(fn), user_(user) {}
+    ~SpoolSink() override {
+        if (blocks_) fclose(blocks_);
+        if (table_) fclose(table_);
+    }
+    // Makes the two files in `dir` (NULL: $TMPDIR, else /tmp). HS_IO if it cannot.
+    int open(const char* dir) {
+        std::string d = dir ? dir : "";
+        if (d.empty()) {
+            const char* t = getenv("TMPDIR");
+            d = t && *t ? t : "/tmp";
+        }
+        if (!make(d, "blocks", &blocks_) || !make(d, "table", &table_))
+            return hs::host_fail(HS_IO, "cannot make a temporary file in " + d + ": " + why_);
+        return HS_OK;
+    }
+    int block(const uint8_t* p, size_t n) override { return put(blocks_, p, n); }
+    int table(const uint8_t* p, size_t n) override { return put(table_, p, n); }
+    int header(const uint8_t* p, size_t n) override {
+        if (fn_(user_, p, n)) return fail("the output writer failed");
+        return copy(table_) || copy(blocks_);
+    }
+    std::string why() const override { return why_.empty() ? "the output writer failed" : why_; }
+
+  private:
+    bool make(const std::string& dir, const char* part, FILE** f) {
+        std::string path = dir + "/.taco-spool-" + std::to_string((long)getpid()) + "-" + part + "-XXXXXX";
+        const int fd = mkstemp(&path[0]);
+        if (fd < 0) {
+            why_ = strerror(errno);
+            return false;
+        }
+        unlink(path.c_str());
+        *f = fdopen(fd, "w+b");
+        if (!*f) {
+            why_ = strerror(errno);
+            ::close(fd);
+            return false;
+        }
+        setvbuf(*f, nullptr, _IOFBF, 1 << 20);
+        return true;
+    }
+    int fail(const std::string& w) {
+        why_ = w;
+        return 1;
+    }
+    int put(FILE* f, const uint8_t* p, size_t n) {
+        if (n && fwrite(p, 1, n, f) != n) return fail(std::string("a temporary file failed: ") + strerror(errno));
+        return 0;
+    }
+    int copy(FILE* f) {
+        if (fflush(f) || fseeko(f, 0, SEEK_SET)) return fail(std::string("a temporary file failed: ") + strerror(errno));
+        std::vector<uint8_t> buf(1 << 20);
+        for (;;) {
+            const size_t k = fread(buf.data(), 1, buf.size(), f);
+            if (k && fn_(user_, buf.data(), k)) return fail("the output writer failed");
+            if (k < buf.size()) return ferror(f) ? fail("a temporary file failed on reading") : 0;
+        }
+    }
+
+    hs_write_fn fn_;
+    void* user_;
+    FILE* blocks_ = nullptr;
+    FILE* table_ = nullptr;
+    std::string why_;
 };
 
 // The blocks of one segment and their input bytes. A fold holds two segments at a time: the
@@ -675,8 +794,11 @@ struct FoldStatsAcc {
 };
 
 // The fold of fold_with, segment by segment (crates/taco/src/fold.rs code_segment over the
-// segments of stream.rs StreamFold::to_seekable): the block table and the stored blocks go to the
-// sink as each segment ends, the header (with the input's SHA-256) last. Per segment:
+// segments of stream.rs StreamFold::run, for to_seekable and to_writer): the stored blocks and
+// the table entries go to the sink as each segment ends, the header (with the input's length,
+// block count and SHA-256) last. `len` may be LEN_UNKNOWN (to_writer with no input length): then
+// the segments are read until the input ends, and the block size is the set one or the default
+// (the spread rule needs the length). Per segment:
 // 2. tokens and zstd frames on the host threads (for the next segment while the GPUs run this one);
 // 3. the context windows on the GPUs, each block's range encoder taking its intervals as they
 //    complete (WindowFeed);
@@ -687,62 +809,82 @@ int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx,
     if (!zstd().ok) return hs::host_fail(HS_UNSUPPORTED, "the zstd library (libzstd.so.1) is not available");
     // FoldOptions::block_size_for (fold.rs:159-170): a set size, or 16 KiB; with `spread`, the
     // power of two that makes about 64 blocks, within 4 KiB .. 16 KiB.
+    const bool known = len != LEN_UNKNOWN;
     uint64_t bs = opt->block_size ? opt->block_size : DEFAULT_BLOCK_SIZE;
-    if (opt->spread && !opt->block_size) {
+    if (opt->spread && !opt->block_size && known) {
         uint64_t per = (len + SPREAD_BLOCKS - 1) / SPREAD_BLOCKS, p2 = 1;
         while (p2 < per) p2 <<= 1;
         bs = std::min<uint64_t>(std::max<uint64_t>(p2, SPREAD_MIN_BLOCK), DEFAULT_BLOCK_SIZE);
     }
     if (bs == 0 || bs > MAX_BLOCK_SIZE) return hs::host_fail(HS_UNSUPPORTED, "the block size is out of range");
-    const uint64_t nblocks = (len + bs - 1) / bs;
-    if (nblocks > 0xFFFFFFFFull) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
+    // The block count: from the length, or (length unknown) counted as the segments arrive.
+    const uint64_t nblocks = known ? (len + bs - 1) / bs : 0;
+    if (nblocks > MAX_BLOCKS) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
+    if (!known && sink.needs_len())
+        return hs::host_fail(HS_BAD_ARGUMENT, "a seekable output needs the input length");
     const unsigned threads = opt->threads ? opt->threads : std::max(1u, std::thread::hardware_concurrency());
     const size_t K = std::min<size_t>(opt->overlap, n_ctx - 2);
     const uint64_t seg_blocks = std::min<uint64_t>(std::max<uint64_t>(SEGMENT_BYTES / bs, 1), SEGMENT_BLOCKS);
-    const uint64_t data_off = HEADER_LEN + 5 * nblocks;
     hs::Sha256 sum;
     FoldStatsAcc acc;
-    uint64_t write_at = data_off;
+    uint64_t total_len = 0, total_blocks = 0, stored_total = 0;
     int rc;
     auto io = [](const std::string& what) { return hs::host_fail(HS_IO, what); };
-    // Reads the input bytes of the segment that starts at block `first`.
+    if (known && sink.begin(HEADER_LEN + 5 * nblocks)) return io(sink.why());
+    // Reads the input bytes of the segment that starts at block `first`: the segment's share of
+    // `len`, or (length unknown) up to a full segment, fewer only at the end of the input. The
+    // buffer grows with the bytes that arrive (stream.rs read_up_to).
     auto read_segment = [&](uint64_t first, Segment& seg) -> int {
         seg.first = first;
-        const uint64_t nb = std::min(seg_blocks, nblocks - first);
-        const uint64_t off = first * bs, n = std::min<uint64_t>(nb * bs, len - off);
-        seg.data.resize((size_t)n);
-        for (uint64_t got = 0; got < n;) {
-            const int64_t r = src.read(seg.data.data() + got, (size_t)(n - got));
+        const uint64_t want = known ? std::min<uint64_t>(seg_blocks * bs, len - first * bs) : seg_blocks * bs;
+        seg.data.clear();
+        if (known) seg.data.resize((size_t)want);
+        uint64_t got = 0;
+        while (got < want) {
+            if (seg.data.size() == got)
+                seg.data.resize((size_t)std::min<uint64_t>(want, std::max<uint64_t>(2 * got, 1u << 20)));
+            const int64_t r = src.read(seg.data.data() + got, (size_t)(seg.data.size() - got));
             if (r < 0) return io("the input source failed");
-            if (r == 0) return io("the input is shorter than its length");
+            if (r == 0) {
+                if (known) return io("the input is shorter than its length");
+                break;
+            }
             got += (uint64_t)r;
         }
-        sum.update(seg.data.data(), (size_t)n);
+        seg.data.resize((size_t)got);
+        const uint64_t nb = (got + bs - 1) / bs;
+        if (first + nb > MAX_BLOCKS) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
+        sum.update(seg.data.data(), (size_t)got);
+        total_len += got;
         seg.blocks.assign((size_t)nb, FoldBlock());
         for (uint64_t i = 0; i < nb; i++) {
             seg.blocks[i].off = (size_t)(i * bs);
-            seg.blocks[i].len = (size_t)std::min<uint64_t>(bs, n - i * bs);
+            seg.blocks[i].len = (size_t)std::min<uint64_t>(bs, got - i * bs);
         }
         seg.rc = HS_OK;
         seg.msg.clear();
         return HS_OK;
     };
     auto cur = std::make_unique<Segment>(), next = std::make_unique<Segment>();
-    if (nblocks) {
-        if ((rc = read_segment(0, *cur))) return rc;
+    if ((rc = read_segment(0, *cur))) return rc;
+    if (!cur->blocks.empty()) {
         prep_segment(*cur, tok, threads);
         acc.prep_ms += cur->ms;
     }
     std::vector<uint8_t> table;
-    for (uint64_t first = 0; first < nblocks; first += seg_blocks) {
+    while (!cur->blocks.empty()) {
         if (cur->rc) return hs::host_fail(cur->rc, cur->msg);
+        const uint64_t first = cur->first;
         // The next segment: read here (the source is called on the caller's thread only), then
-        // tokenized and compressed on the host threads while the GPUs run this one.
+        // tokenized and compressed on the host threads while the GPUs run this one. With the
+        // length unknown, a full segment may have one after it; a read that finds the end of the
+        // input gives an empty one.
         std::thread helper;
-        const bool more = first + seg_blocks < nblocks;
+        bool more = known ? first + seg_blocks < nblocks : cur->data.size() == seg_blocks * bs;
         if (more) {
             if ((rc = read_segment(first + seg_blocks, *next))) return rc;
-            helper = std::thread([&] { prep_segment(*next, tok, threads); });
+            more = !next->blocks.empty();
+            if (more) helper = std::thread([&] { prep_segment(*next, tok, threads); });
         }
         struct Join {
             std::thread& t;
@@ -797,22 +939,22 @@ int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx,
             const uint32_t sl = (uint32_t)(b.kind == KIND_RAW ? b.len : b.stored.size());
             table.push_back(b.kind);
             for (int k = 0; k < 4; k++) table.push_back((uint8_t)(sl >> (8 * k)));
-            if (sink.write(write_at, b.kind == KIND_RAW ? cur->data.data() + b.off : b.stored.data(), sl))
-                return io("the output sink failed");
-            write_at += sl;
+            if (sink.block(b.kind == KIND_RAW ? cur->data.data() + b.off : b.stored.data(), sl))
+                return io(sink.why());
+            stored_total += sl;
             acc.tokens += b.tokens.size();
             acc.coded += b.kind == KIND_CODED;
             acc.zstd += b.kind == KIND_ZSTD;
         }
-        if (sink.write(HEADER_LEN + 5 * first, table.data(), table.size())) return io("the output sink failed");
+        if (sink.table(table.data(), table.size())) return io(sink.why());
+        total_blocks += blocks.size();
         acc.finish_ms += ms_since(t0);
-        if (more) {
-            helper.join();
-            acc.prep_ms += next->ms;
-            std::swap(cur, next);
-        }
+        if (!more) break;
+        helper.join();
+        acc.prep_ms += next->ms;
+        std::swap(cur, next);
     }
-    {
+    if (known) {
         uint8_t extra;
         const int64_t r = src.read(&extra, 1);
         if (r < 0) return io("the input source failed");
@@ -827,22 +969,23 @@ int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx,
     put16(4, 2);  // version
     put16(6, 0);  // flags
     memcpy(h + 8, model_hash, 32);
-    put64(40, len);
+    put64(40, total_len);
     sum.final(h + 48);
     put32(80, (uint32_t)bs);
-    put32(84, (uint32_t)nblocks);
+    put32(84, (uint32_t)total_blocks);
     const uint16_t k = (uint16_t)opt->overlap;
     h[88] = 0;                 // profile text
     h[89] = 0;                 // reserved
     put16(90, k ? 2 : 0);      // coding parts: bit 1 = the overlap
     memcpy(h + 92 + 2, &k, 2);  // coding parameters: the overlap
-    if (sink.write(0, h, HEADER_LEN)) return io("the output sink failed");
-    *out_len = write_at;
+    if (sink.header(h, HEADER_LEN)) return io(sink.why());
+    const uint64_t container_len = HEADER_LEN + 5 * total_blocks + stored_total;
+    *out_len = container_len;
     if (stats) {
         memset(stats, 0, sizeof(*stats));
-        stats->original_len = len;
-        stats->container_len = write_at;
-        stats->blocks = nblocks;
+        stats->original_len = total_len;
+        stats->container_len = container_len;
+        stats->blocks = total_blocks;
         stats->block_size = (uint32_t)bs;
         stats->tokens = acc.tokens;
         stats->coded_blocks = acc.coded;
@@ -906,7 +1049,7 @@ int fold_many(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, s
     for (uint32_t k = 0; k < per; k++) ords.insert(ords.end(), ordinals, ordinals + n_gpus);
     MultiGpu gpu({ords.data(), (uint32_t)ords.size(), model_file, model_len, hash, vocab, eot, n_ctx, slots,
                   max_rows, opt->overlap});
-    if ((rc = gpu.start())) return rc;
+    gpu.start();
     rc = fold_stream_impl(hash, eot, n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
     if (!rc && stats) stats->gpus_failed = gpu.failed() / per;  // a GPU's workers fail together
     return rc;
@@ -967,6 +1110,29 @@ int hs_fold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* mo
     return fold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, src, len, snk, opt, out_len,
                      stats);
 }
+int hs_fold_spool(hs_batch* batch, const hs_tokenizer* tok, uint64_t len, hs_source_fn source, void* source_user,
+                  hs_write_fn write, void* write_user, const char* spool_dir, const hs_fold_options* opt,
+                  uint64_t* out_len, hs_fold_stats* stats) {
+    if (!batch || !tok || !opt || !out_len || !source || !write) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    CallbackSource src(source, source_user);
+    SpoolSink snk(write, write_user);
+    int rc = snk.open(spool_dir);
+    if (rc) return rc;
+    return fold_one(batch, tok, src, len, snk, opt, out_len, stats);
+}
+int hs_fold_spool_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                        uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, uint64_t len, hs_source_fn source,
+                        void* source_user, hs_write_fn write, void* write_user, const char* spool_dir,
+                        const hs_fold_options* opt, uint64_t* out_len, hs_fold_stats* stats) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !opt || !out_len || !source || !write)
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    CallbackSource src(source, source_user);
+    SpoolSink snk(write, write_user);
+    int rc = snk.open(spool_dir);
+    if (rc) return rc;
+    return fold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, src, len, snk, opt, out_len,
+                     stats);
+}
 
 uint32_t hs_zstd_version(void) { return zstd().ok ? zstd().version() : 0; }
 
@@ -981,6 +1147,10 @@ namespace {
 struct ReadAt {
     virtual ~ReadAt() = default;
     virtual int read(uint64_t at, uint8_t* p, size_t n) = 0;
+    // Whether a read failed in the caller's source (an I/O error, not a short container).
+    virtual bool failed() const { return false; }
+    // The bytes before `end` (the header and the table) will be read again; the later ones once.
+    virtual void keep(uint64_t /*end*/) {}
 };
 
 // The original bytes in order: write() takes n bytes; 0, or non-zero on an error.
@@ -1017,6 +1187,48 @@ struct CallbackReadAt : ReadAt {
     void* user;
     CallbackReadAt(hs_read_at_fn f, void* u) : fn(f), user(u) {}
     int read(uint64_t at, uint8_t* p, size_t n) override { return fn(user, at, p, n); }
+};
+
+// A container that arrives through a pipe (stream.rs PipeSource), read in one pass. The bytes
+// below keep_to (the header and the block table) are kept in memory as they arrive, so that they
+// can be read again by offset; the bytes after them (the stored blocks) are read in order, each
+// once. read() gives 0, 1 if the container ends first or the read would skip bytes or go back
+// before them, 2 if the source failed. The kept bytes grow only with the bytes that arrive, so a
+// false block count in a header costs no memory before its table exists (stream.rs:566-568).
+struct PipeReadAt : ReadAt {
+    hs_source_fn fn;
+    void* user;
+    std::vector<uint8_t> kept;
+    uint64_t pos = 0;  // the bytes taken from the source
+    uint64_t keep_to = UINT64_MAX;
+    bool bad = false;
+    PipeReadAt(hs_source_fn f, void* u) : fn(f), user(u) {}
+    bool failed() const override { return bad; }
+    void keep(uint64_t end) override { keep_to = end; }
+    int read(uint64_t at, uint8_t* p, size_t n) override {
+        size_t done = 0;
+        if (at < kept.size()) {
+            done = (size_t)std::min<uint64_t>(n, kept.size() - at);
+            memcpy(p, kept.data() + at, done);
+        }
+        if (done == n) return 0;
+        if (at + done != pos) return 1;
+        while (done < n) {
+            const int64_t r = fn(user, p + done, n - done);
+            if (r < 0 || (uint64_t)r > n - done) {
+                bad = true;
+                return 2;
+            }
+            if (r == 0) return 1;
+            if (pos < keep_to) {
+                const uint64_t k = std::min<uint64_t>((uint64_t)r, keep_to - pos);
+                kept.insert(kept.end(), p + done, p + done + k);
+            }
+            pos += (uint64_t)r;
+            done += (size_t)r;
+        }
+        return 0;
+    }
 };
 
 struct CallbackWriter : Writer {
@@ -1370,13 +1582,17 @@ class MultiDecoder : public UnfoldGpu {
     std::string bad_why_;
 };
 
-// taco::unfold segment by segment (crates/taco/src/stream.rs StreamUnfold::from_seekable): the
-// whole table and the container length are checked before any output; then each segment's stored
-// bytes are read, its raw blocks copied, its zstd blocks decoded on the host, its coded blocks on
-// the GPUs, and its bytes written out; the SHA-256 of all of them is checked at the end. `hash`
-// and `eot` are those of the model (the container must name it, if it names one).
+// taco::unfold segment by segment (crates/taco/src/stream.rs StreamUnfold::from_seekable and
+// from_reader): the whole table is checked before any output, and with a known length `n` the
+// container length too; then each segment's stored bytes are read, its raw blocks copied, its
+// zstd blocks decoded on the host, its coded blocks on the GPUs, and its bytes written out; the
+// SHA-256 of all of them is checked at the end. With n = LEN_UNKNOWN (a pipe) a missing byte is
+// an error where the segment that needs it is read, and a byte after the last block an error at
+// the end, so the output can hold restored bytes before the error. `hash` and `eot` are those of
+// the model (the container must name it, if it names one).
 int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const hs_tokenizer* tok, ReadAt& in,
                        uint64_t n, Writer& out) {
+    const bool known = n != LEN_UNKNOWN;
     Header c;
     int rc = parse_header(in, n, c);
     if (rc) return rc;
@@ -1387,6 +1603,7 @@ int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const 
     std::vector<uint32_t> stored;
     const uint64_t table_end = c.hlen + 5 * (uint64_t)c.count;
     if (n < table_end) return bad_container("truncated block table");
+    in.keep(table_end);
     uint64_t total = table_end;
     for (uint32_t g = 0; g < c.count; g += TABLE_GROUP) {
         const uint32_t m = std::min<uint32_t>(TABLE_GROUP, c.count - g);
@@ -1399,8 +1616,8 @@ int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const 
             total += stored[j];
         }
     }
-    if (total > n) return bad_container("truncated block");
-    if (total < n) return bad_container("extra bytes after the last block");
+    if (known && total > n) return bad_container("truncated block");
+    if (known && total < n) return bad_container("extra bytes after the last block");
     if ((rc = gpu.set_overlap(c.overlap))) return rc;
     const uint64_t seg_blocks = std::min<uint64_t>(std::max<uint64_t>(SEGMENT_BYTES / c.block_size, 1), SEGMENT_BLOCKS);
     hs::Sha256 sum;
@@ -1441,6 +1658,11 @@ int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const 
         sum.update(restored.data(), restored.size());
         if (out.write(restored.data(), restored.size())) return hs::host_fail(HS_IO, "the output writer failed");
     }
+    if (!known) {
+        uint8_t one;
+        if (in.read(pos, &one, 1) == 0) return bad_container("extra bytes after the last block");
+        if (in.failed()) return hs::host_fail(HS_IO, "the input source failed");
+    }
     uint8_t got[32];
     sum.final(got);
     if (memcmp(got, c.checksum, 32) != 0)
@@ -1448,13 +1670,40 @@ int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const 
     return HS_OK;
 }
 
-// hs_unfold and hs_unfold_stream on the caller's batch.
+// hs_unfold, hs_unfold_stream and hs_unfold_pipe on the caller's batch.
 int unfold_one(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uint64_t n, Writer& out) {
     hs_model_info info;
     int rc = hs_model_get_info(hs::batch_model(batch), &info);
     if (rc) return rc;
     OneDecoder gpu(batch);
-    return unfold_stream_impl(gpu, info.hash, info.eot_token, tok, in, n, out);
+    rc = unfold_stream_impl(gpu, info.hash, info.eot_token, tok, in, n, out);
+    if (rc && in.failed()) return hs::host_fail(HS_IO, "the input source failed");
+    return rc;
+}
+
+// hs_unfold_multi and hs_unfold_pipe_multi: worker threads on the GPUs of `ordinals`, which start
+// at the first segment with coded blocks.
+int unfold_many(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len, uint32_t slots,
+                uint32_t max_rows, const hs_tokenizer* tok, ReadAt& in, uint64_t n, Writer& out) {
+    uint32_t vocab, eot, n_ctx;
+    {
+        std::string err;
+        if (!hs::model_file_info(model_file, model_len, &vocab, &eot, &n_ctx, err))
+            return hs::host_fail(HS_MODEL, "the model file is not valid: " + err);
+    }
+    int rc = check_tokenizer(tok, vocab);
+    if (rc) return rc;
+    uint8_t hash[32];
+    hs::sha256(model_file, model_len, hash);
+    // Two worker threads per GPU, as the fold (HS_FOLD_WORKERS_PER_GPU).
+    uint32_t per = 2;
+    if (const char* v = getenv("HS_FOLD_WORKERS_PER_GPU")) per = (uint32_t)std::min(8, std::max(1, atoi(v)));
+    std::vector<int> ords;
+    for (uint32_t k = 0; k < per; k++) ords.insert(ords.end(), ordinals, ordinals + n_gpus);
+    MultiDecoder gpu(ords, model_file, model_len, hash, slots, max_rows);
+    rc = unfold_stream_impl(gpu, hash, eot, tok, in, n, out);
+    if (rc && in.failed()) return hs::host_fail(HS_IO, "the input source failed");
+    return rc;
 }
 
 }  // namespace
@@ -1493,31 +1742,42 @@ int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_f
                     size_t cap, size_t* out_len) {
     if (!ordinals || !n_gpus || !model_file || !tok || !out_len || (len && !container))
         return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
-    uint32_t vocab, eot, n_ctx;
-    {
-        std::string err;
-        if (!hs::model_file_info(model_file, model_len, &vocab, &eot, &n_ctx, err))
-            return hs::host_fail(HS_MODEL, "the model file is not valid: " + err);
-    }
-    int rc = check_tokenizer(tok, vocab);
-    if (rc) return rc;
     MemReadAt in(container, len);
     Header c;
-    if ((rc = parse_header(in, len, c))) return rc;
+    int rc = parse_header(in, len, c);
+    if (rc) return rc;
     *out_len = (size_t)c.original_len;
     if (cap < c.original_len || (!out && c.original_len))
         return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
                                                   std::to_string(c.original_len) + " needed");
-    uint8_t hash[32];
-    hs::sha256(model_file, model_len, hash);
-    // Two worker threads per GPU, as the fold (HS_FOLD_WORKERS_PER_GPU).
-    uint32_t per = 2;
-    if (const char* v = getenv("HS_FOLD_WORKERS_PER_GPU")) per = (uint32_t)std::min(8, std::max(1, atoi(v)));
-    std::vector<int> ords;
-    for (uint32_t k = 0; k < per; k++) ords.insert(ords.end(), ordinals, ordinals + n_gpus);
-    MultiDecoder gpu(ords, model_file, model_len, hash, slots, max_rows);
     MemWriter w(out, cap);
-    return unfold_stream_impl(gpu, hash, eot, tok, in, len, w);
+    return unfold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, in, len, w);
+}
+
+int hs_unfold_pipe(hs_batch* batch, const hs_tokenizer* tok, hs_source_fn source, void* source_user, hs_write_fn write,
+                   void* write_user, uint64_t* out_len) {
+    if (!batch || !tok || !source || !write || !out_len) return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    PipeReadAt in(source, source_user);
+    Header c;
+    int rc = parse_header(in, LEN_UNKNOWN, c);
+    if (rc) return in.failed() ? hs::host_fail(HS_IO, "the input source failed") : rc;
+    *out_len = c.original_len;
+    CallbackWriter w(write, write_user);
+    return unfold_one(batch, tok, in, LEN_UNKNOWN, w);
+}
+
+int hs_unfold_pipe_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                         uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, hs_source_fn source,
+                         void* source_user, hs_write_fn write, void* write_user, uint64_t* out_len) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !source || !write || !out_len)
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    PipeReadAt in(source, source_user);
+    Header c;
+    int rc = parse_header(in, LEN_UNKNOWN, c);
+    if (rc) return in.failed() ? hs::host_fail(HS_IO, "the input source failed") : rc;
+    *out_len = c.original_len;
+    CallbackWriter w(write, write_user);
+    return unfold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, in, LEN_UNKNOWN, w);
 }
 
 }  // extern "C"

@@ -245,6 +245,49 @@ def test_fold_stream_gives_the_bytes_of_fold(setup, case):
         assert bytes(buf2) == want
 
 
+@pytest.mark.parametrize("known", [True, False])
+def test_spool_fold_and_pipe_unfold_give_the_bytes_of_fold(setup, tmp_path, known):
+    """hs_fold_spool (StreamFold::to_writer) gives the container of hs_fold, with the input length
+    known or not, across segments with coded, zstd and raw blocks; hs_unfold_pipe
+    (StreamUnfold::from_reader) gives the input back from the container read in one pass."""
+    batch, tok = setup
+    data, bs, k = _many_blocks(), 256, 5
+    want, wstats = B.fold(batch, tok, data, bs, k)
+    out = bytearray()
+    n, stats = B.fold_spool(batch, tok, _reader(data), out.extend, len(data) if known else None, tmp_path, bs, k)
+    assert n == len(want) and bytes(out) == want
+    for key in ("blocks", "coded_blocks", "zstd_blocks", "tokens", "container_len", "original_len"):
+        assert stats[key] == wstats[key]
+    assert stats["coded_blocks"] > 0 and list(tmp_path.iterdir()) == []
+    restored = bytearray()
+    assert B.unfold_pipe(batch, tok, _reader(want), restored.extend) == len(data)
+    assert bytes(restored) == data
+    if not known:
+        ords = [0, 1] if __import__("torch").cuda.device_count() >= 2 else [0, 0]
+        out2 = bytearray()
+        B.fold_spool_multi(ords, tiny_bytes(), tok, _reader(data), out2.extend, None, tmp_path, bs, k, slots=8,
+                           max_rows=4096)
+        assert bytes(out2) == want
+        restored2 = bytearray()
+        B.unfold_pipe_multi(ords, tiny_bytes(), tok, _reader(want), restored2.extend, slots=8, max_rows=4096)
+        assert bytes(restored2) == data
+
+
+def test_pipe_unfold_gives_the_published_inputs(setup):
+    batch, tok = setup
+    for name in TEXT_VECTORS:
+        container = (GOLDEN / (name + ".taco")).read_bytes()
+        out = bytearray()
+        B.unfold_pipe(batch, tok, _reader(container), out.extend)
+        assert bytes(out) == (GOLDEN / (name + ".in")).read_bytes()
+    # A missing byte inside a coded block, and an extra byte after the last.
+    good = (GOLDEN / "predicted_text_k32.taco").read_bytes()
+    for bad, why in ((good[:-1], "truncated block"), (good + b"\0", "extra bytes")):
+        with pytest.raises(B.HardShellError) as e:
+            B.unfold_pipe(batch, tok, _reader(bad), lambda c: None)
+        assert e.value.code == B.HS_FORMAT and why in str(e.value)
+
+
 def test_fold_stream_refuses_a_short_or_long_source_and_a_failing_sink(setup):
     batch, tok = setup
     data = (GOLDEN / "predicted_text_k32.in").read_bytes()

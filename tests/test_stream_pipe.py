@@ -1,0 +1,245 @@
+"""The pipe forms of the stream fold and unfold (crates/taco/src/stream.rs StreamFold::to_writer,
+the method "spool", and StreamUnfold::from_reader), on the host, with no GPU.
+
+The multi-GPU entry points open their GPUs only when a model window or a coded block needs one,
+so two kinds of input run here with every GPU refused (HS_FAIL_OPEN, a host-side refusal):
+- a fold in blocks of one byte: a block whose token count already takes its whole length never
+  starts a model window (the stop rule, crates/taco/src/codec.rs:70-131), so every block is raw;
+- the unfold of the conformance containers whose blocks are raw or zstd.
+The spooled container must be the container that container.py builds from the same blocks, with
+the input length known or not, across several segments (4,096 blocks each), and its spool files
+must never be visible in the spool directory. The pipe unfold must give the published inputs, and
+report a missing byte where it is found and an extra byte at the end, as the reference does.
+"""
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+from taco_b200 import backend as B
+from taco_b200 import container as C
+
+from .common import GOLDEN, tiny_bytes
+
+NO_CODED = ["empty", "one_byte", "random_raw", "text_k0", "text_k20", "text_kinds"]
+
+
+@pytest.fixture(scope="module")
+def tok():
+    t = B.Tokenizer(tiny_bytes())
+    yield t
+    t.close()
+
+
+@pytest.fixture(autouse=True)
+def no_gpu(monkeypatch):
+    monkeypatch.setenv("HS_FAIL_OPEN", "0,1")
+
+
+def _reader(data: bytes, seed: int = 5):
+    """read(n) over `data` in pieces of random sizes (a pipe gives what it has)."""
+    rng = np.random.default_rng(seed)
+    pos = [0]
+
+    def read(n):
+        k = min(n, int(rng.integers(1, 5000)))
+        out = data[pos[0]:pos[0] + k]
+        pos[0] += len(out)
+        return out
+
+    return read
+
+
+def _raw_container(data: bytes) -> bytes:
+    """The container of `data` in raw blocks of one byte (the tiny model named, no overlap)."""
+    c = C.Container(2, hashlib.sha256(tiny_bytes()).digest(), len(data), hashlib.sha256(data).digest(), 1)
+    c.blocks = [C.Block(i, C.KIND_RAW, 1, data[i:i + 1]) for i in range(len(data))]
+    return C.build(c)
+
+
+def _spool(tok, data, length, spool_dir, **kw):
+    out = bytearray()
+    n, stats = B.fold_spool_multi([0, 1], tiny_bytes(), tok, _reader(data), out.extend, length=length,
+                                  spool_dir=spool_dir, block_size=1, **kw)
+    assert n == len(out)
+    return bytes(out), stats
+
+
+@pytest.mark.parametrize("size", [0, 1, 4096, 8192, 10_000])
+@pytest.mark.parametrize("known", [True, False])
+def test_spool_fold_gives_the_container_of_its_blocks(tok, tmp_path, size, known):
+    data = np.random.default_rng(size).integers(0, 256, size, dtype=np.uint8).tobytes()
+    got, stats = _spool(tok, data, len(data) if known else None, tmp_path)
+    assert got == _raw_container(data)
+    assert stats["original_len"] == size and stats["blocks"] == size and stats["block_size"] == 1
+    assert stats["coded_blocks"] == 0 and stats["gpu_rows"] == 0 and stats["gpus_failed"] == 2
+    assert list(tmp_path.iterdir()) == []
+    c = C.parse(got)
+    assert b"".join(b.stored for b in c.blocks) == data
+
+
+def test_spool_files_never_show_in_the_directory(tok, tmp_path):
+    """The spool files are unlinked as soon as they are made: the directory is empty while the
+    container goes out, and after."""
+    data = bytes(range(256)) * 40
+    seen = []
+
+    def write(chunk):
+        seen.append(sorted(p.name for p in tmp_path.iterdir()))
+
+    B.fold_spool_multi([0], tiny_bytes(), tok, _reader(data), write, spool_dir=tmp_path, block_size=1)
+    assert seen and all(s == [] for s in seen)
+
+
+def test_spool_fold_with_the_default_directory(tok, tmp_path, monkeypatch):
+    monkeypatch.setenv("TMPDIR", str(tmp_path))
+    data = b"pipe" * 3000
+    got, _ = _spool(tok, data, None, None)
+    assert got == _raw_container(data)
+
+
+def test_spool_fold_refusals(tok, tmp_path):
+    data = b"x" * 5000
+    # A known length that the source does not have: fewer or more bytes.
+    for length in (len(data) + 1, len(data) - 1):
+        with pytest.raises(B.HardShellError) as e:
+            _spool(tok, data, length, tmp_path)
+        assert e.value.code == B.HS_IO
+    # A source or a writer that fails.
+    def bad_read(n):
+        raise OSError("gone")
+
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_spool_multi([0], tiny_bytes(), tok, bad_read, lambda c: None, spool_dir=tmp_path, block_size=1)
+    assert e.value.code == B.HS_IO
+
+    def bad_write(chunk):
+        raise OSError("disk full")
+
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_spool_multi([0], tiny_bytes(), tok, _reader(data), bad_write, spool_dir=tmp_path, block_size=1)
+    assert e.value.code == B.HS_IO and "output writer" in str(e.value)
+    # A spool directory that does not exist.
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_spool_multi([0], tiny_bytes(), tok, _reader(data), lambda c: None,
+                           spool_dir=tmp_path / "missing", block_size=1)
+    assert e.value.code == B.HS_IO and "temporary file" in str(e.value)
+    assert list(tmp_path.iterdir()) == []
+    # A seekable output needs the length before the first block.
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_stream_multi([0], tiny_bytes(), tok, B.LEN_UNKNOWN, _reader(data), lambda at, c: None, 1, 0)
+    assert e.value.code == B.HS_BAD_ARGUMENT
+
+
+def test_spool_fold_that_needs_a_window_fails_with_no_gpu(tok, tmp_path):
+    """Blocks of 300 bytes of text need the model: with every GPU refused the fold fails with the
+    open error, and leaves no spool file."""
+    data = (GOLDEN / "text_kinds.in").read_bytes()
+    with pytest.raises(B.HardShellError) as e:
+        B.fold_spool_multi([0, 1], tiny_bytes(), tok, _reader(data), lambda c: None, spool_dir=tmp_path,
+                           block_size=300)
+    assert e.value.code == B.HS_NO_DEVICE and "no GPU of the fold opened" in str(e.value)
+    assert list(tmp_path.iterdir()) == []
+
+
+def _unpipe(tok, container: bytes, seed: int = 3):
+    out = bytearray()
+    n = B.unfold_pipe_multi([0, 1], tiny_bytes(), tok, _reader(container, seed), out.extend)
+    return n, bytes(out)
+
+
+@pytest.mark.parametrize("name", NO_CODED)
+def test_pipe_unfold_gives_the_published_input(tok, name):
+    container = (GOLDEN / (name + ".taco")).read_bytes()
+    want = (GOLDEN / (name + ".in")).read_bytes()
+    for seed in (1, 2):
+        n, got = _unpipe(tok, container, seed)
+        assert n == len(want) and got == want
+
+
+@pytest.mark.parametrize("known", [True, False])
+def test_spool_then_pipe_round_trips_across_segments(tok, tmp_path, known):
+    data = np.random.default_rng(9).integers(0, 256, 9_999, dtype=np.uint8).tobytes()
+    folded, _ = _spool(tok, data, len(data) if known else None, tmp_path)
+    n, got = _unpipe(tok, folded)
+    assert n == len(data) and got == data
+
+
+def test_pipe_unfold_finds_a_missing_byte_where_it_is_needed(tok, tmp_path):
+    """A container cut inside its third segment: the first two segments (8,192 bytes) are
+    restored before the error, as from_reader restores them."""
+    data = np.random.default_rng(4).integers(0, 256, 10_000, dtype=np.uint8).tobytes()
+    folded, _ = _spool(tok, data, None, tmp_path)
+    out = bytearray()
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(folded[:-100]), out.extend)
+    assert e.value.code == B.HS_FORMAT and "truncated block" in str(e.value)
+    assert bytes(out) == data[:8192]
+
+
+def test_pipe_unfold_finds_an_extra_byte_at_the_end(tok):
+    container = (GOLDEN / "text_kinds.taco").read_bytes()
+    want = (GOLDEN / "text_kinds.in").read_bytes()
+    out = bytearray()
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(container + b"\0"), out.extend)
+    assert e.value.code == B.HS_FORMAT and "extra bytes" in str(e.value)
+    assert bytes(out) == want
+
+
+def test_pipe_unfold_checks_the_whole_table_before_any_output(tok):
+    good = (GOLDEN / "text_kinds.taco").read_bytes()
+    cut = good[:C.HEADER_LEN + 5 * 10]  # inside the table
+    bad_kind = bytearray(good)
+    bad_kind[C.HEADER_LEN + 5 * 16] = 9  # the last entry's kind
+    for bad in (good[:50], cut, bytes(bad_kind)):
+        out = []
+        with pytest.raises(B.HardShellError) as e:
+            B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(bad), out.append)
+        assert e.value.code == B.HS_FORMAT
+        assert out == []
+
+
+def test_pipe_unfold_refusals(tok):
+    good = (GOLDEN / "text_kinds.taco").read_bytes()
+
+    def bad_read(n):
+        raise OSError("gone")
+
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, bad_read, lambda c: None)
+    assert e.value.code == B.HS_IO
+    # A source that fails after the table: the error is I/O, not a short container.
+    pos = [0]
+
+    def fails_late(n):
+        if pos[0] > C.HEADER_LEN + 5 * 17:
+            raise OSError("gone")
+        k = min(n, 7)
+        pos[0] += k
+        return good[pos[0] - k:pos[0]]
+
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, fails_late, lambda c: None)
+    assert e.value.code == B.HS_IO
+
+    def bad_write(chunk):
+        raise OSError("disk full")
+
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(good), bad_write)
+    assert e.value.code == B.HS_IO
+    # A damaged checksum: HS_CORRUPT after the output.
+    bad = bytearray(good)
+    bad[50] ^= 1
+    with pytest.raises(B.HardShellError) as e:
+        _unpipe(tok, bytes(bad))
+    assert e.value.code == B.HS_CORRUPT
+    # Coded blocks need a GPU: with every GPU refused, the open error.
+    coded = (GOLDEN / "predicted_text_k0.taco").read_bytes()
+    with pytest.raises(B.HardShellError) as e:
+        _unpipe(tok, coded)
+    assert e.value.code == B.HS_NO_DEVICE
+    assert os.environ["HS_FAIL_OPEN"] == "0,1"
