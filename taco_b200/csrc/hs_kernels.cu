@@ -764,7 +764,9 @@ constexpr int CODER_MAX_STEPS = 32;  // steps of 256 symbols per warp: V <= 8 * 
 // An encode query (kind 0) then sums f over the symbols below its token: one block reduction. A
 // decode query walks warp -> step -> lane -> symbol, each level a parallel scan: warp w owns the
 // groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step).
-__global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
+// Five blocks per SM (48 registers, no spills): the shared-memory atomics of the counts bound the
+// kernel, and more resident rows keep more of the row loads in flight around them.
+__global__ void __launch_bounds__(CODER_THREADS, 5) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
                                                          int tsh, int R, int V, const uint64_t* table, int tlen,
                                                          int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
                                                          int* err) {
@@ -783,7 +785,8 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     const uint64_t total = 1ULL << bits;
     const uint64_t spare = total - (uint64_t)V;
     const int ng = (V + 7) / 8, ng_full = V / 8;
-    for (int j = threadIdx.x; j < tlen; j += CODER_THREADS) F[j] = 0;
+    for (int j = threadIdx.x; j < tlen / 4; j += CODER_THREADS) reinterpret_cast<uint4*>(F)[j] = make_uint4(0, 0, 0, 0);
+    for (int j = 4 * (tlen / 4) + threadIdx.x; j < tlen; j += CODER_THREADS) F[j] = 0;
     // The row max.
     int64_t mx = INT64_MIN;
     for (int t = threadIdx.x; t < VT; t += CODER_THREADS) mx = tr[t] > mx ? tr[t] : mx;
@@ -801,12 +804,15 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
     int best = V;
     const uint32_t last2 = (uint32_t)last * 0x10001u;
     const uint32_t head2 = (uint32_t)(head < last ? head : last) * 0x10001u;
+    // The largest distance counted, two halfwords at a time (the highest bin that occurs).
+    uint32_t dm2 = 0;
     // Groups of 8 symbols, CODER_UNROLL groups per thread and round so that several 16-byte loads
     // are in flight before the counting.
     auto count_group = [&](int v0, uint4 raw, auto track) {
         const int32_t off = tile_off(v0);
         if (off == last) {
             atomicAdd(&F[last], 8u);
+            dm2 = last2;
             if constexpr (decltype(track)::value) best = head >= last && v0 < best ? v0 : best;
             return;
         }
@@ -818,6 +824,7 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
             const uint32_t p = __vminu2(__vaddus2(u[k], off2), last2);
             atomicAdd(&F[p & 0xFFFFu], 1u);
             atomicAdd(&F[p >> 16], 1u);
+            dm2 = __vmaxu2(dm2, p);
             if constexpr (decltype(track)::value) near[k] = __vcmpleu2(p, head2);
         }
         if constexpr (decltype(track)::value) {
@@ -855,15 +862,14 @@ __global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, in
             int32_t dd = off + (int32_t)dr[v];
             dd = dd < last ? dd : last;
             atomicAdd(&F[dd], 1u);
+            dm2 = (uint32_t)dd > (dm2 & 0xFFFFu) ? (dm2 & 0xFFFF0000u) | (uint32_t)dd : dm2;
             best = dd <= head && v < best ? v : best;
         }
     }
     __syncthreads();  // the counts are complete
     const uint64_t n_last = F[last];
     // The largest distance that occurs: the highest counted bin.
-    int32_t dmax = n_last ? last : 0;
-    for (int j = threadIdx.x; j < last; j += CODER_THREADS)
-        if (F[j]) dmax = j > dmax ? j : dmax;
+    int32_t dmax = (int32_t)max(dm2 & 0xFFFFu, dm2 >> 16);
     dmax = (int32_t)block_max64(dmax, red);
     const int largest_found = (int)-block_max64(-(int64_t)best, red);
     // W = sum over the distances of count * table (< 2^16 * 2^40: fits in 64 bits).
@@ -1525,6 +1531,9 @@ cudaError_t configure_core_kernels() {
     e = cudaFuncSetAttribute(k_attention_vec<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsmem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_coder_mix, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
+    if (e != cudaSuccess) return e;
+    // The largest shared-memory carveout, so that five blocks of the counts fit on an SM.
+    e = cudaFuncSetAttribute(k_coder, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_coder, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
 }
