@@ -411,6 +411,17 @@ int run_windows(hs_batch* batch, uint32_t eot, size_t K, WindowFeed& feed, const
         if ((rc = hs_batch_run_coded(batch, s_slot.data(), s_tok.data(), s_kind.data(), s_val.data(),
                                      (uint32_t)s_slot.size(), FREQ_BITS, ivs.data())))
             return rc;
+        // Every answer is checked as the reference checks the coder op's intervals on the host
+        // (crates/taco/src/lanes.rs:119-128, interval.rs CodeInterval::new): a frequency of 0, an
+        // interval past the total or a wrong last-symbol flag is a fault of the device, and fails
+        // the fold here instead of reaching the range encoder (whose range a zero frequency would
+        // leave at 0).
+        constexpr uint64_t TOTAL = 1ull << FREQ_BITS;
+        for (const hs_interval& iv : ivs)
+            if (iv.freq == 0 || iv.start > TOTAL || iv.freq > TOTAL - iv.start ||
+                (iv.is_last != 0) != (iv.start + iv.freq == TOTAL))
+                return hs::host_fail(HS_CUDA, "the coder op gave a bad interval (start " + std::to_string(iv.start) +
+                                                  ", freq " + std::to_string(iv.freq) + ")");
         feed.add_rows(s_slot.size());
         for (size_t m = 0; m < mine.size(); m++) {
             const Window& win = windows[mine[m]];

@@ -764,9 +764,7 @@ constexpr int CODER_MAX_STEPS = 32;  // steps of 256 symbols per warp: V <= 8 * 
 // An encode query (kind 0) then sums f over the symbols below its token: one block reduction. A
 // decode query walks warp -> step -> lane -> symbol, each level a parallel scan: warp w owns the
 // groups [w * gpw, (w + 1) * gpw), lane l the groups w * gpw + l + 32 k (k = the step).
-// Five blocks per SM (48 registers, no spills): the shared-memory atomics of the counts bound the
-// kernel, and more resident rows keep more of the row loads in flight around them.
-__global__ void __launch_bounds__(CODER_THREADS, 5) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
+__global__ void __launch_bounds__(CODER_THREADS) k_coder(const uint16_t* d16, int ldd, const int64_t* tmax, int ldt,
                                                          int tsh, int R, int V, const uint64_t* table, int tlen,
                                                          int head, uint32_t bits, const RowInfo* rows, uint64_t* out,
                                                          int* err) {
@@ -1531,9 +1529,6 @@ cudaError_t configure_core_kernels() {
     e = cudaFuncSetAttribute(k_attention_vec<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsmem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_coder_mix, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
-    if (e != cudaSuccess) return e;
-    // The largest shared-memory carveout, so that five blocks of the counts fit on an SM.
-    e = cudaFuncSetAttribute(k_coder, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_coder, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_LOGIT_TABLE * 4);
 }
