@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -320,15 +321,16 @@ enum Op { OP_EMBED, OP_LN, OP_GEMM_QKV, OP_KV, OP_ATTN, OP_GEMM_PROJ, OP_GEMM_FC
 const char* OP_NAMES[OP_COUNT] = {"embed", "layernorm", "gemm_qkv", "kv_store", "attention", "gemm_proj",
                                   "gemm_fc", "gemm_mlp", "gemm_logits", "coder", "decoder", "pass"};
 
-// Kernel launches of this process (the bench reports the launches of its timed region).
-unsigned long long g_launches = 0;
+// Kernel launches of this process (the bench reports the launches of its timed region). Several
+// host threads launch at once in the multi-GPU fold and unfold, so the count is atomic.
+std::atomic<unsigned long long> g_launches{0};
 
 struct ProfScope {
     hs_batch* b;
     int op;
     int idx = -1;
     ProfScope(hs_batch* b_, int op_, uint64_t flops) : b(b_), op(op_) {
-        if (op != OP_PASS) g_launches++;
+        if (op != OP_PASS) g_launches.fetch_add(1, std::memory_order_relaxed);
         if (!b->profiling) return;
         b->op_launches[op]++;
         b->op_flops[op] += flops;
@@ -1691,7 +1693,7 @@ int hs_batch_profile(hs_batch* b, hs_op_profile* out, int cap) {
     return n;
 }
 
-uint64_t hs_launch_count(void) { return g_launches; }
+uint64_t hs_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int hs_batch_run_coded(hs_batch* b, const uint32_t* slots, const uint32_t* tokens, const uint32_t* kinds,
                        const uint64_t* values, uint32_t n, uint32_t freq_bits, hs_interval* out) {
