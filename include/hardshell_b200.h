@@ -232,7 +232,8 @@ typedef struct hs_fold_stats {
     double prep_ms, gpu_ms, finish_ms;
 } hs_fold_stats;
 
-/* The largest container of a fold of `len` bytes with this block size (0 = the default). */
+/* The largest container of a fold of `len` bytes with this block size (0: the default or the
+ * `spread` size, whichever gives the larger bound). UINT64_MAX if it does not fit in 64 bits. */
 uint64_t hs_fold_bound(uint64_t len, uint32_t block_size);
 
 /* taco::fold_with on the CUDA engine (fold.rs:334-360), profile text: the .taco container

@@ -52,6 +52,10 @@ constexpr uint8_t KIND_RAW = 0, KIND_CODED = 1, KIND_ZSTD = 2;
 constexpr uint64_t MAX_BLOCKS = 0xFFFFFFFFull;      // the block count is a u32 (header.rs)
 constexpr uint64_t LEN_UNKNOWN = HS_LEN_UNKNOWN;    // a fold input or an unfold container of unknown length
 
+// The blocks of `len` bytes in blocks of `bs` (the last one shorter), with no overflow for any
+// length (the reference's block_count is checked arithmetic too).
+constexpr uint64_t blocks_of(uint64_t len, uint64_t bs) { return len / bs + (len % bs != 0); }
+
 // ---- zstd, from the system library (opened once) ----
 
 struct Zstd {
@@ -245,8 +249,12 @@ void parallel_for(size_t n, unsigned threads, F&& f) {
 extern "C" {
 
 uint64_t hs_fold_bound(uint64_t len, uint32_t block_size) {
-    const uint64_t bs = block_size ? block_size : DEFAULT_BLOCK_SIZE;
-    return HEADER_LEN + 5 * ((len + bs - 1) / bs) + len;
+    // Block size 0: the fold takes the default or, with `spread`, a size down to 4 KiB; the
+    // smallest gives the most table entries.
+    const uint64_t bs = block_size ? block_size : SPREAD_MIN_BLOCK;
+    const uint64_t nb = blocks_of(len, bs);
+    if (len > UINT64_MAX - HEADER_LEN || nb > (UINT64_MAX - HEADER_LEN - len) / 5) return UINT64_MAX;
+    return HEADER_LEN + 5 * nb + len;
 }
 
 }  // extern "C"
@@ -829,7 +837,7 @@ int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx,
     }
     if (bs == 0 || bs > MAX_BLOCK_SIZE) return hs::host_fail(HS_UNSUPPORTED, "the block size is out of range");
     // The block count: from the length, or (length unknown) counted as the segments arrive.
-    const uint64_t nblocks = known ? (len + bs - 1) / bs : 0;
+    const uint64_t nblocks = known ? blocks_of(len, bs) : 0;
     if (nblocks > MAX_BLOCKS) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
     if (!known && sink.needs_len())
         return hs::host_fail(HS_BAD_ARGUMENT, "a seekable output needs the input length");
@@ -863,7 +871,7 @@ int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx,
             got += (uint64_t)r;
         }
         seg.data.resize((size_t)got);
-        const uint64_t nb = (got + bs - 1) / bs;
+        const uint64_t nb = blocks_of(got, bs);
         if (first + nb > MAX_BLOCKS) return hs::host_fail(HS_UNSUPPORTED, "more than 2^32 - 1 blocks");
         sum.update(seg.data.data(), (size_t)got);
         total_len += got;
@@ -1282,7 +1290,7 @@ int parse_header(ReadAt& in, uint64_t n, Header& c) {
     c.block_size = rd32(80);
     c.count = rd32(84);
     if (c.block_size == 0 || c.block_size > MAX_BLOCK_SIZE) return bad_container("block size out of range");
-    if ((uint64_t)c.count != (c.original_len + c.block_size - 1) / c.block_size) return bad_container("wrong block count");
+    if ((uint64_t)c.count != blocks_of(c.original_len, c.block_size)) return bad_container("wrong block count");
     if (c.version == 2) {
         c.profile = d[88];
         const uint8_t reserved = d[89];

@@ -243,3 +243,24 @@ def test_pipe_unfold_refusals(tok):
         _unpipe(tok, coded)
     assert e.value.code == B.HS_NO_DEVICE
     assert os.environ["HS_FAIL_OPEN"] == "0,1"
+
+
+def test_a_length_that_wraps_the_block_count_is_refused(tok):
+    """A header whose length needs more blocks than 2^64 bytes can count (2^64 - 1 bytes in blocks
+    of 2, block count 0) is a wrong block count, not an empty container of that length."""
+    c = C.Container(2, hashlib.sha256(tiny_bytes()).digest(), 2**64 - 1, hashlib.sha256(b"").digest(), 2)
+    out = []
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(C.build(c)), out.append)
+    assert e.value.code == B.HS_FORMAT and "block count" in str(e.value)
+    assert out == []
+
+
+def test_fold_bound():
+    L = B.lib()
+    assert L.hs_fold_bound(0, 0) == C.HEADER_LEN
+    assert L.hs_fold_bound(1, 0) == C.HEADER_LEN + 5 + 1
+    # Block size 0 bounds the spread sizes too: 16 KiB is four blocks of 4 KiB.
+    assert L.hs_fold_bound(16384, 0) == C.HEADER_LEN + 5 * 4 + 16384
+    assert L.hs_fold_bound(16384, 16384) == C.HEADER_LEN + 5 + 16384
+    assert L.hs_fold_bound(2**64 - 1, 1) == 2**64 - 1  # does not fit: saturates
