@@ -5,8 +5,9 @@ Run once in a container that has the reference checkout (its path is the first a
     python tests/golden/make_fixtures.py <reference checkout>
 
 The files are the reference's own golden data (conformance/README.md of the reference):
-the tiny model `tiny.hsm` and the version 2 container vectors of the `text` profile, with
-`vectors.tsv`. The profile `logs` and `auto` vectors (mixed blocks) are not copied: the mixer
+the tiny model `tiny.hsm`, the version 2 container vectors of the `text` profile, with
+`vectors.tsv`, and the version 1 container `taco-v1-tiny.taco` (folded with another tiny model,
+the one of the reference's Rust test builder: it pins the reading of a version 1 header). The profile `logs` and `auto` vectors (mixed blocks) are not copied: the mixer
 is outside the path this backend serves. The script writes MANIFEST.tsv with the SHA-256 of
 every copied file, so a test can check that the fixtures are the published bytes.
 """
@@ -26,7 +27,8 @@ TEXT_VECTORS = [
 def main() -> int:
     ref = Path(sys.argv[1])
     conf = ref / "conformance"
-    files = [("tiny.hsm", conf / "tiny.hsm"), ("vectors.tsv", conf / "v2" / "vectors.tsv")]
+    files = [("tiny.hsm", conf / "tiny.hsm"), ("vectors.tsv", conf / "v2" / "vectors.tsv"),
+             ("taco_v1_tiny.taco", conf / "taco-v1-tiny.taco")]
     for name in TEXT_VECTORS:
         for ext in (".in", ".taco"):
             files.append((name + ext, conf / "v2" / (name + ext)))

@@ -264,3 +264,57 @@ def test_fold_bound():
     assert L.hs_fold_bound(16384, 0) == C.HEADER_LEN + 5 * 4 + 16384
     assert L.hs_fold_bound(16384, 16384) == C.HEADER_LEN + 5 + 16384
     assert L.hs_fold_bound(2**64 - 1, 1) == 2**64 - 1  # does not fit: saturates
+
+
+def test_a_version_1_container_reads_as_version_1(tok):
+    """conformance/taco-v1-tiny.taco (container version 1, 88-byte header, 5 blocks of 512 bytes)
+    was folded with the tiny model of the reference's Rust test builder, not tiny.hsm
+    (conformance/README.md). Its header and table read as version 1, so unfolding it with tiny.hsm
+    stops at the model check, before any output, as crates/taco/src/unfold.rs checked_model does:
+    through a pipe and from memory. A zstd kind in its table (version 2 only) is a format error."""
+    data = (GOLDEN / "taco_v1_tiny.taco").read_bytes()
+    c = C.parse(data)
+    assert c.version == 1 and c.block_size == 512 and c.original_len == 2202
+    assert [b.kind for b in c.blocks] == [C.KIND_CODED, C.KIND_CODED, C.KIND_RAW, C.KIND_RAW, C.KIND_CODED]
+    out = []
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(data), out.append)
+    assert e.value.code == B.HS_MODEL_MISMATCH and out == []
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_multi([0], tiny_bytes(), tok, data)
+    assert e.value.code == B.HS_MODEL_MISMATCH
+    # The third entry (a raw block of 512 bytes) as a zstd block of 10: no such kind in version 1.
+    bad = bytearray(data)
+    bad[C.HEADER_LEN_V1 + 5 * 2:C.HEADER_LEN_V1 + 5 * 3] = bytes([C.KIND_ZSTD]) + (10).to_bytes(4, "little")
+    bad[8:40] = hashlib.sha256(tiny_bytes()).digest()  # past the model check
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(bytes(bad)), out.append)
+    assert e.value.code == B.HS_FORMAT and "kind" in str(e.value) and out == []
+
+
+def test_headers_the_reference_refuses(tok):
+    """crates/taco-cli/tests/stream.rs damaged_input_is_an_error...: a header that claims 2^32 - 1
+    blocks of 1 byte that the input does not hold is a truncated table (and costs no memory for
+    the claimed table), and headers cut at 0, 3, 5, 50 and 103 bytes are format errors."""
+    good = (GOLDEN / "text_kinds.taco").read_bytes()
+    claims = bytearray(good)
+    claims[40:48] = (2**32 - 1).to_bytes(8, "little")
+    claims[80:84] = (1).to_bytes(4, "little")
+    claims[84:88] = (2**32 - 1).to_bytes(4, "little")
+    for data in (bytes(claims), *(good[:n] for n in (0, 3, 5, 50, 103))):
+        out = []
+        with pytest.raises(B.HardShellError) as e:
+            B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(data), out.append)
+        assert e.value.code == B.HS_FORMAT and out == [], len(data)
+        assert "truncated" in str(e.value), str(e.value)
+
+
+def test_an_empty_container_that_names_no_model_unfolds(tok):
+    """crates/taco-cli/tests/stream.rs a_raw_only_container_unfolds_without_a_model: the empty
+    version 2 container with a zero model hash (block size 65,536) unfolds to nothing, whatever
+    the model."""
+    c = C.Container(2, bytes(32), 0, hashlib.sha256(b"").digest(), 65536)
+    out = bytearray()
+    assert B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(C.build(c)), out.extend) == 0
+    assert out == b""
+    assert B.unfold_multi([0], tiny_bytes(), tok, C.build(c)) == b""
