@@ -351,7 +351,8 @@ int hs_unfold_pipe(hs_batch* batch, const hs_tokenizer* tokenizer, hs_source_fn 
  * decoded (one frame, content size = the block length, window <= 8 MiB), coded blocks decoded on
  * the GPU by hs_batch_decode_blocks in rounds of min(slots, max_rows) blocks and turned into
  * bytes with the tokenizer's vocabulary; a block whose decoding fails or whose tokens do not give
- * its length, or output whose SHA-256 is not the header's, is HS_CORRUPT. Mixed blocks (profile
+ * its length, or output whose SHA-256 is not the header's, is HS_CORRUPT; a zstd frame that does
+ * not give exactly its block is HS_FORMAT (FormatError::CorruptZstdBlock). Mixed blocks (profile
  * logs) are HS_UNSUPPORTED: their unfold needs the caller's match model and mixer. *out_len = the
  * original length; HS_BAD_ARGUMENT if it is more than cap. */
 int hs_unfold(hs_batch* batch, const hs_tokenizer* tokenizer, const uint8_t* container, size_t len, uint8_t* out,

@@ -1666,7 +1666,10 @@ int unfold_stream_impl(UnfoldGpu& gpu, const uint8_t* hash, uint32_t eot, const 
             if (kinds[j] == KIND_RAW) memcpy(restored.data() + o, data.data() + at[j], olen);
             else if (kinds[j] == KIND_ZSTD &&
                      !decompress_zstd(data.data() + at[j], stored[j], restored.data() + o, olen))
-                return corrupt_block(first + j, "the zstd frame does not give the block");
+                // A format error in the reference (unfold.rs:93, FormatError::CorruptZstdBlock),
+                // not a corrupt coded block.
+                return bad_container("the zstd frame of block " + std::to_string(first + j) +
+                                     " does not give the block (CorruptZstdBlock)");
             else if (kinds[j] == KIND_CODED) coded.push_back(j);
         }
         if (!coded.empty()) {

@@ -318,3 +318,35 @@ def test_an_empty_container_that_names_no_model_unfolds(tok):
     assert B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(C.build(c)), out.extend) == 0
     assert out == b""
     assert B.unfold_multi([0], tiny_bytes(), tok, C.build(c)) == b""
+
+
+def _rle_frame(content: int, byte: int) -> bytes:
+    """A zstd frame of RLE blocks (RFC 8878 3.1.1.2): a 4-byte content size, then one 4-byte
+    block of `byte` for each 128 KiB."""
+    f = bytearray([0x28, 0xB5, 0x2F, 0xFD, 0x80, 10 << 3]) + content.to_bytes(4, "little")
+    left = content
+    while left > 0:
+        n = min(left, 128 * 1024)
+        left -= n
+        f += ((1 if left == 0 else 0) | (1 << 1) | (n << 3)).to_bytes(4, "little")[:3] + bytes([byte])
+    return bytes(f)
+
+
+@pytest.mark.parametrize("content", [4096, 3900])
+def test_a_zstd_frame_that_does_not_give_its_block_is_a_format_error(tok, content):
+    """crates/taco/tests/security_unfold.rs zstd_frame_longer_than_its_block_is_refused: a block
+    of 4,000 bytes whose frame states another length is FormatError::CorruptZstdBlock, in memory
+    and through a pipe."""
+    c = C.Container(2, bytes(32), 4000, hashlib.sha256(b"A" * 4000).digest(), 4000)
+    c.blocks = [C.Block(0, C.KIND_ZSTD, 4000, _rle_frame(content, ord("A")))]
+    data = C.build(c)
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_multi([0], tiny_bytes(), tok, data)
+    assert e.value.code == B.HS_FORMAT and "CorruptZstdBlock" in str(e.value)
+    out = []
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_pipe_multi([0], tiny_bytes(), tok, _reader(data), out.append)
+    assert e.value.code == B.HS_FORMAT and out == []
+    # The frame of the right length gives the block.
+    c.blocks = [C.Block(0, C.KIND_ZSTD, 4000, _rle_frame(4000, ord("A")))]
+    assert B.unfold_multi([0], tiny_bytes(), tok, C.build(c)) == b"A" * 4000
