@@ -334,6 +334,12 @@ int hs_fold_spool_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* mod
 int hs_unfold_stream(hs_batch* batch, const hs_tokenizer* tokenizer, uint64_t len, hs_read_at_fn read_at,
                      void* read_user, hs_write_fn write, void* write_user, uint64_t* out_len);
 
+/* hs_unfold_stream with the worker threads of hs_unfold_multi. */
+int hs_unfold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                           uint32_t slots, uint32_t max_rows, const hs_tokenizer* tokenizer, uint64_t len,
+                           hs_read_at_fn read_at, void* read_user, hs_write_fn write, void* write_user,
+                           uint64_t* out_len);
+
 /* StreamUnfold::from_reader (stream.rs:809-827): the unfold of hs_unfold of the container that
  * `source` gives in one pass (a pipe), into `write`. The header and the whole block table are
  * read and checked before any output (they stay in memory: 5 bytes per block); the stored blocks

@@ -158,6 +158,8 @@ def lib() -> ctypes.CDLL:
     L.hs_fold_spool_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, u64, SOURCE_FN, vp,
                                       WRITE_FN, vp, ctypes.c_char_p, ctypes.POINTER(FoldOptions),
                                       ctypes.POINTER(u64), ctypes.POINTER(FoldStats)]
+    L.hs_unfold_stream_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, u64, READ_AT_FN,
+                                         vp, WRITE_FN, vp, ctypes.POINTER(u64)]
     L.hs_unfold_pipe.argtypes = [vp, vp, SOURCE_FN, vp, WRITE_FN, vp, ctypes.POINTER(u64)]
     L.hs_unfold_pipe_multi.argtypes = [vp, u32, ctypes.c_char_p, ctypes.c_size_t, u32, u32, vp, SOURCE_FN, vp,
                                        WRITE_FN, vp, ctypes.POINTER(u64)]
@@ -393,9 +395,9 @@ def unfold_pipe_multi(ordinals, model_file: bytes, tokenizer, read, write, slots
     return n.value
 
 
-def unfold_stream(batch, tokenizer, length: int, read_at, write) -> int:
-    """hs_unfold_stream: the unfold of the `length`-byte container that read_at(at, n) -> bytes
-    reads, into write(data); returns the original length."""
+def _read_at(read_at):
+    """A ctypes positional reader over read_at(at, n) -> bytes (exactly n). An exception or a
+    short read fails the read."""
 
     def ra(_user, at, buf, n):
         try:
@@ -407,16 +409,27 @@ def unfold_stream(batch, tokenizer, length: int, read_at, write) -> int:
         ctypes.memmove(buf, data, n)
         return 0
 
-    def wr(_user, buf, n):
-        try:
-            write(ctypes.string_at(buf, n))
-        except Exception:  # noqa: BLE001
-            return 1
-        return 0
+    return READ_AT_FN(ra)
 
-    cb_ra, cb_wr = READ_AT_FN(ra), WRITE_FN(wr)
+
+def unfold_stream(batch, tokenizer, length: int, read_at, write) -> int:
+    """hs_unfold_stream: the unfold of the `length`-byte container that read_at(at, n) -> bytes
+    reads, into write(data); returns the original length."""
+    cb_ra, cb_wr = _read_at(read_at), _writer(write)
     n = ctypes.c_uint64()
     _check(lib().hs_unfold_stream(batch.h, tokenizer.h, length, cb_ra, None, cb_wr, None, ctypes.byref(n)))
+    return n.value
+
+
+def unfold_stream_multi(ordinals, model_file: bytes, tokenizer, length: int, read_at, write, slots: int = 256,
+                        max_rows: int = 16384) -> int:
+    """hs_unfold_stream_multi: unfold_stream with the worker threads of unfold_multi (a container
+    without coded blocks opens no GPU); returns the original length."""
+    ords = np.ascontiguousarray(ordinals, dtype=np.int32)
+    cb_ra, cb_wr = _read_at(read_at), _writer(write)
+    n = ctypes.c_uint64()
+    _check(lib().hs_unfold_stream_multi(_p(ords), ords.size, model_file, len(model_file), slots, max_rows,
+                                        tokenizer.h, length, cb_ra, None, cb_wr, None, ctypes.byref(n)))
     return n.value
 
 

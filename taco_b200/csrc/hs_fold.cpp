@@ -1703,8 +1703,8 @@ int unfold_one(hs_batch* batch, const hs_tokenizer* tok, ReadAt& in, uint64_t n,
     return rc;
 }
 
-// hs_unfold_multi and hs_unfold_pipe_multi: worker threads on the GPUs of `ordinals`, which start
-// at the first segment with coded blocks.
+// hs_unfold_multi, hs_unfold_stream_multi and hs_unfold_pipe_multi: worker threads on the GPUs of
+// `ordinals`, which start at the first segment with coded blocks.
 int unfold_many(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len, uint32_t slots,
                 uint32_t max_rows, const hs_tokenizer* tok, ReadAt& in, uint64_t n, Writer& out) {
     uint32_t vocab, eot, n_ctx;
@@ -1773,6 +1773,21 @@ int hs_unfold_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_f
         return hs::host_fail(HS_BAD_ARGUMENT, "the output holds " + std::to_string(cap) + " bytes, " +
                                                   std::to_string(c.original_len) + " needed");
     MemWriter w(out, cap);
+    return unfold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, in, len, w);
+}
+
+int hs_unfold_stream_multi(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, size_t model_len,
+                           uint32_t slots, uint32_t max_rows, const hs_tokenizer* tok, uint64_t len,
+                           hs_read_at_fn read_at, void* read_user, hs_write_fn write, void* write_user,
+                           uint64_t* out_len) {
+    if (!ordinals || !n_gpus || !model_file || !tok || !read_at || !write || !out_len)
+        return hs::host_fail(HS_BAD_ARGUMENT, "null argument");
+    CallbackReadAt in(read_at, read_user);
+    Header c;
+    int rc = parse_header(in, len, c);
+    if (rc) return rc;
+    *out_len = c.original_len;
+    CallbackWriter w(write, write_user);
     return unfold_many(ordinals, n_gpus, model_file, model_len, slots, max_rows, tok, in, len, w);
 }
 

@@ -350,3 +350,42 @@ def test_a_zstd_frame_that_does_not_give_its_block_is_a_format_error(tok, conten
     # The frame of the right length gives the block.
     c.blocks = [C.Block(0, C.KIND_ZSTD, 4000, _rle_frame(4000, ord("A")))]
     assert B.unfold_multi([0], tiny_bytes(), tok, C.build(c)) == b"A" * 4000
+
+
+@pytest.mark.parametrize("name", NO_CODED)
+def test_seekable_unfold_on_worker_threads_gives_the_published_input(tok, name):
+    """hs_unfold_stream_multi: the containers without coded blocks, read by offset."""
+    container = (GOLDEN / (name + ".taco")).read_bytes()
+    out = bytearray()
+    n = B.unfold_stream_multi([0], tiny_bytes(), tok, len(container), lambda at, k: container[at:at + k], out.extend)
+    assert n == len(out) and bytes(out) == (GOLDEN / (name + ".in")).read_bytes()
+    # A container one byte short: refused before any output (the length is checked first).
+    out2 = []
+    with pytest.raises(B.HardShellError) as e:
+        B.unfold_stream_multi([0], tiny_bytes(), tok, len(container) - 1, lambda at, k: container[at:at + k],
+                              out2.append)
+    assert e.value.code == B.HS_FORMAT and out2 == []
+
+
+def test_one_batch_wrappers_reach_the_library(tok):
+    """The Python wrappers of the one-batch entry points run only on a GPU otherwise. With a null
+    batch handle each must reach its C function with the right arguments and come back with the
+    library's refusal of the null argument."""
+    import types
+
+    nobatch = types.SimpleNamespace(h=None)
+    data = b"some text"
+    container = (GOLDEN / "one_byte.taco").read_bytes()
+    calls = [
+        lambda: B.fold(nobatch, tok, data),
+        lambda: B.fold_stream(nobatch, tok, len(data), _reader(data), lambda at, c: None),
+        lambda: B.fold_spool(nobatch, tok, _reader(data), lambda c: None),
+        lambda: B.fold_spool(nobatch, tok, _reader(data), lambda c: None, length=len(data)),
+        lambda: B.unfold(nobatch, tok, container),
+        lambda: B.unfold_stream(nobatch, tok, len(container), lambda at, k: container[at:at + k], lambda c: None),
+        lambda: B.unfold_pipe(nobatch, tok, _reader(container), lambda c: None),
+    ]
+    for i, call in enumerate(calls):
+        with pytest.raises(B.HardShellError) as e:
+            call()
+        assert e.value.code == B.HS_BAD_ARGUMENT and "null" in str(e.value), (i, e.value)
