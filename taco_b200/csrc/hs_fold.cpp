@@ -822,7 +822,7 @@ struct FoldStatsAcc {
 // 3. the context windows on the GPUs, each block's range encoder taking its intervals as they
 //    complete (WindowFeed);
 // 4.-5. each block's payload if its encoder did not stop, and its smallest stored form.
-int fold_stream_impl(const uint8_t model_hash[32], uint32_t eot, uint32_t n_ctx, GpuRunner& gpu,
+int fold_stream_impl(const uint8_t model_hash[32], uint32_t n_ctx, GpuRunner& gpu,
                      const hs_tokenizer* tok, Source& src, uint64_t len, Sink& sink, const hs_fold_options* opt,
                      uint64_t* out_len, hs_fold_stats* stats) {
     if (!zstd().ok) return hs::host_fail(HS_UNSUPPORTED, "the zstd library (libzstd.so.1) is not available");
@@ -1036,7 +1036,7 @@ int fold_one(hs_batch* batch, const hs_tokenizer* tok, Source& src, uint64_t len
     if (opt->overlap > 0xFFFF) return hs::host_fail(HS_INVALID_OVERLAP, "the overlap is out of range");
     if ((rc = hs_batch_set_overlap(batch, (uint16_t)opt->overlap))) return rc;
     OneGpu gpu(batch, info.eot_token, std::min<size_t>(opt->overlap, info.n_ctx - 2));
-    return fold_stream_impl(info.hash, info.eot_token, info.n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
+    return fold_stream_impl(info.hash, info.n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
 }
 
 // The fold on several GPUs (hs_fold_multi, hs_fold_stream_multi).
@@ -1069,7 +1069,7 @@ int fold_many(const int* ordinals, uint32_t n_gpus, const uint8_t* model_file, s
     MultiGpu gpu({ords.data(), (uint32_t)ords.size(), model_file, model_len, hash, vocab, eot, n_ctx, slots,
                   max_rows, opt->overlap});
     gpu.start();
-    rc = fold_stream_impl(hash, eot, n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
+    rc = fold_stream_impl(hash, n_ctx, gpu, tok, src, len, sink, opt, out_len, stats);
     if (!rc && stats) stats->gpus_failed = gpu.failed() / per;  // a GPU's workers fail together
     return rc;
 }

@@ -602,7 +602,6 @@ __global__ void __launch_bounds__(Cfg<MODE>::THREADS, 1)
                 }
                 continue;
             } else {
-#pragma unroll 1
                 // This warp's chunks of 32 columns: a contiguous range (4 of the 8 with 8 warps;
                 // 3, 3 and 2 with 12).
                 constexpr int CPP = (TN / 32 + NPART - 1) / NPART;
