@@ -12,6 +12,7 @@ must never be visible in the spool directory. The pipe unfold must give the publ
 report a missing byte where it is found and an extra byte at the end, as the reference does.
 """
 
+import ctypes
 import hashlib
 import os
 
@@ -389,3 +390,31 @@ def test_one_batch_wrappers_reach_the_library(tok):
         with pytest.raises(B.HardShellError) as e:
             call()
         assert e.value.code == B.HS_BAD_ARGUMENT and "null" in str(e.value), (i, e.value)
+
+
+@pytest.mark.parametrize("size", [0, 1, 4097, 9000])
+def test_seekable_outputs_place_blocks_table_and_header(tok, size):
+    """The seekable layouts (stream.rs SeekLayout): hs_fold_multi into memory and
+    hs_fold_stream_multi into a callback at offsets give the container of the spool method, with
+    the header at 0, the table after it and the blocks after the table, across segments."""
+    data = np.random.default_rng(size + 1).integers(0, 256, size, dtype=np.uint8).tobytes()
+    want = _raw_container(data)
+    got, stats = B.fold_multi([0], tiny_bytes(), tok, data, block_size=1)
+    assert got == want and stats["blocks"] == size
+    buf = bytearray()
+
+    def write_at(at, chunk):
+        if len(buf) < at + len(chunk):
+            buf.extend(bytes(at + len(chunk) - len(buf)))
+        buf[at:at + len(chunk)] = chunk
+
+    n, _ = B.fold_stream_multi([0], tiny_bytes(), tok, size, _reader(data), write_at, 1, 0)
+    assert n == len(want) and bytes(buf) == want
+    # An output one byte too small for hs_fold_multi: refused with the length it needs.
+    cap = np.zeros(max(len(want) - 1, 1), np.uint8)
+    m = ctypes.c_size_t()
+    opt = B.FoldOptions(1, 0, 0, 0)
+    ords = np.zeros(1, np.int32)
+    rc = B.lib().hs_fold_multi(ords.ctypes.data, 1, tiny_bytes(), len(tiny_bytes()), 256, 16384, tok.h, data,
+                               len(data), ctypes.byref(opt), cap.ctypes.data, len(want) - 1, ctypes.byref(m), None)
+    assert rc == B.HS_BAD_ARGUMENT and m.value == len(want)
