@@ -1,5 +1,6 @@
-"""The pipe forms of the stream fold and unfold (crates/taco/src/stream.rs StreamFold::to_writer,
-the method "spool", and StreamUnfold::from_reader), on the host, with no GPU.
+"""The stream forms of the fold and unfold (crates/taco/src/stream.rs: StreamFold::to_seekable
+and to_writer, the method "spool"; StreamUnfold::from_seekable and from_reader) and the container
+checks of the unfold, on the host, with no GPU.
 
 The multi-GPU entry points open their GPUs only when a model window or a coded block needs one,
 so two kinds of input run here with every GPU refused (HS_FAIL_OPEN, a host-side refusal):
@@ -8,8 +9,12 @@ so two kinds of input run here with every GPU refused (HS_FAIL_OPEN, a host-side
 - the unfold of the conformance containers whose blocks are raw or zstd.
 The spooled container must be the container that container.py builds from the same blocks, with
 the input length known or not, across several segments (4,096 blocks each), and its spool files
-must never be visible in the spool directory. The pipe unfold must give the published inputs, and
-report a missing byte where it is found and an extra byte at the end, as the reference does.
+must never be visible in the spool directory; the seekable outputs must give the same bytes. The
+pipe unfold must give the published inputs, and report a missing byte where it is found and an
+extra byte at the end, as the reference does. The damaged headers, the version 1 container and
+the zstd frame cases follow the reference's stream and security tests
+(crates/taco-cli/tests/stream.rs, crates/taco/tests/security_unfold.rs). The one-batch wrappers,
+which otherwise run only on a GPU, are checked to reach the library.
 """
 
 import ctypes
